@@ -1,0 +1,406 @@
+"""Sampler benchmark: sampled rows/s and logits GB/s (fraction of HBM peak).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: 4096 rows x 151,936 f32 logits (Qwen2.5-0.5B vocab), distribution of
+workload 5 (N(0, 2.5^2) + row offset + 8 peaks), temp 0.7, top-k 50, top-p 0.9,
+one xorshift64* draw per row.  Synthetic data: no model or dataset exists here.
+
+One step = one zs_sample call over the rank's 4096 rows (one kernel launch).
+With N GPUs (torchrun, one process per GPU) every rank samples its own 4096
+rows (row split, no communication): weak scaling, value = N*4096 rows / max
+over ranks of the step time.  For N > 1 the vocab-sharded mode (partials ->
+NCCL all-gather -> merge) over the same 4096 rows is reported beside it.
+
+Inputs (2.49 GB per rank) are larger than L2 (126 MB), so every step reads HBM.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+V = 151936
+ROWS = 4096
+WORKLOAD = 5
+ROW_BYTES = V * 4
+METRIC = "sampled rows/sec & logits GB/s (% of HBM peak) at batch 1/256/4096, 1-8 B200"
+UNIT = "rows/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def hbm_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def committed_traffic():
+    """dram bytes per launch of zs_select_kernel on this workload, from the
+    committed ncu summary (profiles/), scaled to 4096 rows; None if absent."""
+    path = os.path.join(ROOT, "profiles", "zs_select_kernel_workload5.md")
+    try:
+        txt = open(path).read()
+    except OSError:
+        return None
+    m = re.search(r"traffic_bytes_per_row:\s*([0-9.eE+]+)", txt)
+    return float(m.group(1)) * ROWS if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        out = {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        if self.proc is None:
+            return out
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        try:
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+            os.unlink(self.path)
+        except OSError:
+            pass
+        if sm:
+            out = {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
+                   "reasons": sorted(reasons), "samples": len(sm)}
+        return out
+
+
+def cpu_reference_rate(x_rows, params, seeds, budget_s=8.0, nthreads=None):
+    """The reference's own sampler (oracle/_ref, src/sample.cpp compiled unchanged)
+    on the host cores: rows/s over a bounded sample of the workload rows."""
+    import oracle
+    nthreads = nthreads or (os.cpu_count() or 1)
+    probe = min(len(x_rows), max(64, nthreads * 4))
+    t0 = time.perf_counter()
+    oracle.reference_sample(x_rows[:probe], params, seeds[:probe], nthreads=nthreads)
+    dt = time.perf_counter() - t0
+    rate = probe / max(dt, 1e-9)
+    rows = int(min(len(x_rows), max(probe, rate * budget_s)))
+    t0 = time.perf_counter()
+    oracle.reference_sample(x_rows[:rows], params, seeds[:rows], nthreads=nthreads)
+    dt = time.perf_counter() - t0
+    return rows / dt, rows, dt, nthreads
+
+
+def run_reference_arm(args, rank, world):
+    """--impl reference: zeninfer's CPU sampler on the host cores, same workload."""
+    if rank != 0:
+        return
+    import numpy as np
+    import oracle
+    from zeninfer_b200 import workloads as W
+    if not oracle.have_reference():
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "oracle/_ref/libzen_ref.so not built (needs the reference sources)"}))
+        return
+    wl = W.WORKLOADS[WORKLOAD]
+    nthreads = os.cpu_count() or 1
+    x = W.generate(WORKLOAD, ROWS)
+    seeds = wl.row_seeds(0, ROWS)
+    # Calibrate one step to a bounded sample (a few seconds of host work).
+    t0 = time.perf_counter()
+    probe = min(ROWS, max(64, 4 * nthreads))
+    oracle.reference_sample(x[:probe], wl.params, seeds[:probe], nthreads=nthreads)
+    rate = probe / max(time.perf_counter() - t0, 1e-9)
+    step_rows = int(min(ROWS, max(probe, rate * 3.0)))
+    for _ in range(args.warmup):
+        oracle.reference_sample(x[:step_rows], wl.params, seeds[:step_rows], nthreads=nthreads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        oracle.reference_sample(x[:step_rows], wl.params, seeds[:step_rows], nthreads=nthreads)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = step_rows * len(times) / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / len(times),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32/f64",
+        "data": "synthetic",
+        "config": {"workload": "4096 x 151936 f32 logits, temp 0.7, top-k 50, top-p 0.9",
+                   "rows_per_step": step_rows},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": nthreads, "kind": "reference",
+                         "sample": f"{step_rows} of the 4096 rows per step, zen::sample_token "
+                                   f"per row on {nthreads} host threads"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def time_device_steps(fn, steps, stream):
+    import torch
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+
+    world = env_int("WORLD_SIZE", 1)
+    rank = env_int("RANK", 0)
+    local_rank = env_int("LOCAL_RANK", 0)
+
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        return
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from zeninfer_b200 import Sampler, states_to_tensor
+    from zeninfer_b200 import workloads as W
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    wl = W.WORKLOADS[WORKLOAD]
+    params = wl.params
+    stream = torch.cuda.current_stream()
+
+    # Host copy of this rank's rows (distinct rows per rank), pinned for the e2e leg.
+    row0 = rank * ROWS
+    x_host = torch.empty((ROWS, V), dtype=torch.float32).pin_memory()
+    W.generate(WORKLOAD, ROWS, row0=row0, out=x_host.numpy())
+    x_dev = x_host.to(dev)
+    states0 = wl.row_states(row0, ROWS)
+    st = states_to_tensor(states0, dev)
+    out = torch.empty(ROWS, dtype=torch.int32, device=dev)
+    s = Sampler(local_rank)
+
+    def step():
+        s.sample(x_dev, params, st, out=out, stream=stream)
+
+    for _ in range(args.warmup):
+        step()
+    s.check_device_status(stream)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    ms_total = time_device_steps(step, args.steps, stream)
+    clk = clocks.stop()
+    torch.cuda.synchronize()
+    barrier()
+    s.check_device_status(stream)
+    ms_step = max_over_ranks(ms_total / args.steps)
+    value = world * ROWS / (ms_step / 1e3)
+
+    # Roofline of the dominant (only) kernel: one launch per step.
+    peak, peak_kind = hbm_peak()
+    alg_bytes = ROWS * ROW_BYTES + ROWS * 4
+    achieved = alg_bytes / (ms_step / 1e3) / 1e9
+    traffic = committed_traffic()
+
+    # Batch 1 and 256 on the same device (latency-bound and mid-size shapes).
+    by_batch = {}
+    for b, cfgw in ((1, 1), (256, 2)):
+        wlb = W.WORKLOADS[cfgw]
+        xb = torch.from_numpy(W.generate(cfgw, b, row0=row0)).to(dev)
+        stb = states_to_tensor(wlb.row_states(row0, b), dev)
+        ob = torch.empty(b, dtype=torch.int32, device=dev)
+        fnb = (lambda xb=xb, stb=stb, ob=ob, p=wlb.params:
+               s.sample(xb, p, stb, out=ob, stream=stream))
+        for _ in range(5):
+            fnb()
+        torch.cuda.synchronize()
+        reps = 200 if b == 1 else 50
+        msb = time_device_steps(fnb, reps, stream) / reps
+        by_batch[str(b)] = {"rows_per_s": b / (msb / 1e3), "us_per_call": msb * 1e3,
+                            "logits_gbs": b * ROW_BYTES / (msb / 1e3) / 1e9,
+                            "hbm_frac": b * ROW_BYTES / (msb / 1e3) / 1e9 / peak,
+                            "params": "temp 0.7, top-k 40" + (", top-p 0.9" if b == 256 else "")}
+        del xb
+    by_batch[str(ROWS)] = {"rows_per_s": ROWS / (ms_step / 1e3), "us_per_call": ms_step * 1e3,
+                           "logits_gbs": achieved, "hbm_frac": achieved / peak,
+                           "params": "temp 0.7, top-k 50, top-p 0.9"}
+
+    # End to end through the public API with host buffers: H2D of the step's
+    # logits from pinned memory, the sampler, D2H of the ids, every step.
+    e2e = None
+    if not args.no_e2e:
+        out_host = torch.empty(ROWS, dtype=torch.int32).pin_memory()
+        x_e2e = torch.empty_like(x_dev)
+
+        def e2e_step():
+            x_e2e.copy_(x_host, non_blocking=True)
+            s.sample(x_e2e, params, st, out=out, stream=stream)
+            out_host.copy_(out, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        k = max(3, min(args.steps, 5))
+        t0 = time.perf_counter()
+        for _ in range(k):
+            e2e_step()
+            torch.cuda.current_stream().synchronize()
+            _ = int(out_host[0])
+        e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3 / k)
+        e2e = {"value": world * ROWS / (e2e_ms / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": ROWS * ROW_BYTES, "d2h_bytes_per_step": ROWS * 4,
+               "ms_per_step": e2e_ms}
+        del x_e2e
+
+    # Vocab-sharded mode over the same rows (N > 1): partials -> all-gather -> merge.
+    sharded = None
+    if world > 1:
+        per = V // world
+        lo = rank * per
+        hi = V if rank == world - 1 else lo + per
+        x_loc = x_dev[:, lo:hi]
+        nbytes = Sampler.shard_partial_bytes(ROWS, V, world, params)
+        send = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        recv = torch.empty(world * nbytes, dtype=torch.uint8, device=dev)
+        st2 = states_to_tensor(states0, dev)
+        out2 = torch.empty(ROWS, dtype=torch.int32, device=dev)
+
+        def shard_step():
+            s.shard_partials(x_loc, lo, V, world, params, send, stream=stream)
+            dist.all_gather_into_tensor(recv, send)
+            s.shard_merge(recv, world, ROWS, V, params, st2, out=out2, stream=stream)
+
+        for _ in range(args.warmup):
+            shard_step()
+        torch.cuda.synchronize()
+        barrier()
+        ms_sh = time_device_steps(shard_step, args.steps, stream) / args.steps
+        torch.cuda.synchronize()
+        barrier()
+        ms_sh = max_over_ranks(ms_sh)
+        sharded = {"rows_per_s": ROWS / (ms_sh / 1e3), "ms_per_step": ms_sh,
+                   "allgather_bytes_per_rank": nbytes, "scaling": "strong"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        try:
+            import oracle
+            if oracle.have_reference():
+                rate, rows, dt, nth = cpu_reference_rate(x_host.numpy(), params,
+                                                         wl.row_seeds(row0, ROWS))
+                cpu = {"value": rate, "unit": UNIT, "cores": nth, "kind": "reference",
+                       "sample": f"{rows} of the 4096 rows ({dt:.1f} s), zen::sample_token "
+                                 f"(src/sample.cpp compiled unchanged) on {nth} threads"}
+        except Exception as e:  # reported, never fatal
+            cpu = {"value": None, "unit": UNIT, "cores": None, "kind": "reference",
+                   "sample": f"failed: {e}"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 (f64 shortlist softmax)", "data": "synthetic",
+            "config": {"workload": "4096 x 151936 f32 logits per GPU (workload 5: N(0,2.5^2)"
+                                   " + offset + 8 peaks), temp 0.7, top-k 50, top-p 0.9",
+                       "rows_per_gpu": ROWS, "vocab": V, "parallelism": f"row-split x{world}",
+                       "l2": "inputs (2.49 GB per GPU) larger than L2"},
+            "logits_gbs": achieved, "hbm_frac": achieved / peak,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "peak_source": f"{peak_kind} hbm_gbs",
+                         "kernel": "zs_select_kernel", "algorithmic_bytes_per_launch": alg_bytes},
+            "by_batch": by_batch,
+            "clocks": clk,
+            "e2e": e2e,
+            "gpu_launches": args.steps,
+            "cpu_baseline": cpu,
+        }
+        if sharded:
+            line["vocab_sharded"] = sharded
+        print(json.dumps(line), flush=True)
+
+    s.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

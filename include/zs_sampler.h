@@ -1,0 +1,174 @@
+/*
+ * zs_sampler.h -- C ABI of the B200 token sampler (libzs_sampler.so).
+ *
+ * This is the boundary a host program binds.  It replaces the two entry points
+ * of zeninfer's sampler, namespace zen in src/sample.h:
+ *
+ *   int32_t argmax_token(const float* logits, int n);              src/sample.h:28
+ *   int32_t sample_token(const float* logits, int n,
+ *                        const SamplingParams& p,
+ *                        const std::vector<int32_t>& history,
+ *                        Rng& rng);                                src/sample.h:36-37
+ *
+ * with batched, stream-ordered device entry points.  The C++ API of sample.h
+ * itself (host pointers, one row per call) is served on top of this ABI by
+ * include/zen/sample.h + libzen_sample.so.
+ *
+ * Semantics per row are those of sample_token (src/sample.cpp:32-102):
+ * repetition penalty over the last repeat_last_n history ids (compounding on
+ * duplicates) -> greedy argmax when temp <= 0 -> top-k shortlist (k = top_k, or
+ * 256 when top_k == 0) -> f64 softmax over the shortlist -> nucleus prefix
+ * (top_p < 1) -> inverse-CDF draw from the row's xorshift64* state, one draw per
+ * non-greedy row.  The shortlist order is value descending, then token id
+ * ascending (the reference leaves equal values in libstdc++'s introselect order).
+ *
+ * Conventions: every pointer argument documented "device" is CUDA device memory
+ * of the handle's device; "host" is ordinary host memory.  `stream` is a
+ * cudaStream_t (NULL = legacy default stream).  All entry points return a
+ * zs_status; nothing throws across the ABI.  Calls are asynchronous with
+ * respect to the host unless documented otherwise; errors detected on the
+ * device (a wait that ran out) are reported by zs_check_device_status().
+ */
+#ifndef ZS_SAMPLER_H_
+#define ZS_SAMPLER_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ZS_ABI_VERSION 1
+
+typedef enum zs_status {
+    ZS_OK = 0,
+    ZS_ERR_INVALID_ARGUMENT = 1, /* bad size, null pointer, misaligned logits */
+    ZS_ERR_CUDA = 2,             /* a CUDA runtime call failed; see zs_last_error() */
+    ZS_ERR_NO_DEVICE = 3,        /* no CUDA device, or not an sm_100 device */
+    ZS_ERR_DEVICE_TIMEOUT = 4,   /* a kernel's bounded wait ran out; the results are invalid */
+    ZS_ERR_NCCL = 5,             /* NCCL missing or a NCCL call failed */
+    ZS_ERR_OUT_OF_MEMORY = 6
+} zs_status;
+
+/* Same field order, types and meaning as zen::SamplingParams (src/sample.h:9-15). */
+typedef struct zs_params {
+    float temp;            /* <= 0 means greedy argmax */
+    int32_t top_k;         /* 0 = disabled: shortlist of 256 */
+    float top_p;           /* 1.0 = disabled (nucleus over the shortlist) */
+    float repeat_penalty;  /* 1.0 = disabled */
+    int32_t repeat_last_n; /* penalty window over the tail of the history */
+} zs_params;
+
+/* Optional per-row diagnostics (48 bytes). */
+typedef struct zs_row_info {
+    float max_logit; /* max_l of sample_token: f32 max over the penalised row (NaN if
+                        logits[0] is NaN); for greedy rows the chosen logit */
+    int32_t k;       /* shortlist size (0 for greedy rows) */
+    int32_t m;       /* nucleus size */
+    int32_t pos;     /* shortlist position of the drawn token (-1 for greedy rows) */
+    double r;        /* the uniform draw */
+    double sum;      /* sum of exp((x_i - max_l) * inv_temp) over the shortlist */
+    double boundary; /* |r - nearest CDF boundary| */
+    double log_z;    /* log sum_{all V} exp((x - max_l) * inv_temp) when requested
+                        (inv_temp = 1 for greedy rows), NaN otherwise */
+} zs_row_info;
+
+/* Optional outputs of zs_sample; any member may be NULL / 0. */
+typedef struct zs_extras {
+    zs_row_info* row_info; /* device [batch] */
+    int32_t* cand_ids;     /* device [batch][cand_ld]: sorted shortlist ids */
+    double* cand_probs;    /* device [batch][cand_ld]: shortlist softmax before the nucleus rescale */
+    int32_t cand_ld;       /* row stride of cand_ids / cand_probs; entries >= k are untouched */
+    int32_t want_log_z;    /* nonzero: fill row_info->log_z (costs one exp per logit) */
+} zs_extras;
+
+typedef struct zs_context* zs_handle;
+
+/* One handle per device; it owns the scratch and the kernel configuration.
+ * The handle is not thread-safe: use one per host thread, or serialise. */
+zs_status zs_create(int device, zs_handle* out);
+zs_status zs_destroy(zs_handle h);
+
+/* Message of the last failing call on this host thread ("" if none). */
+const char* zs_last_error(void);
+const char* zs_status_string(zs_status s);
+int zs_abi_version(void);
+
+/* zen::Rng(seed): the xorshift64* state a seed maps to (0 -> 0x9E3779B97F4A7C15). */
+uint64_t zs_rng_seed(uint64_t seed);
+
+/*
+ * Batched sample_token (src/sample.cpp:32-102) for `batch` rows of n_vocab f32
+ * logits, row r at logits + r * ld (device, 4-byte aligned, never modified).
+ *
+ *   params          host; 1 struct shared by every row, or `batch` structs when
+ *                   params_per_row != 0
+ *   history         device [batch][history_ld] token ids; row r's history is its
+ *                   first history_len[r] entries (history_len: device [batch]).
+ *                   Both may be NULL when no row has repeat_penalty != 1.
+ *   rng_state       device [batch] xorshift64* states, advanced in place by one
+ *                   draw for every non-greedy row (zen::Rng& semantics)
+ *   out_ids         device [batch]
+ *   extras          host pointer to optional outputs, or NULL
+ *
+ * n_vocab <= 0 writes 0 to every out_ids entry and draws nothing (sample.cpp:34).
+ */
+zs_status zs_sample(zs_handle h, const float* logits, int64_t ld, int32_t batch, int32_t n_vocab,
+                    const zs_params* params, int32_t params_per_row, const int32_t* history,
+                    int64_t history_ld, const int32_t* history_len, uint64_t* rng_state,
+                    int32_t* out_ids, const zs_extras* extras, void* stream);
+
+/* Batched argmax_token (src/sample.cpp:24-30): first index of the maximum; a NaN at
+ * index 0 yields 0.  No penalty, no draw. */
+zs_status zs_argmax(zs_handle h, const float* logits, int64_t ld, int32_t batch, int32_t n_vocab,
+                    int32_t* out_ids, void* stream);
+
+/* Waits for `stream` and reports ZS_ERR_DEVICE_TIMEOUT if any kernel of this handle
+ * gave up on a bounded wait since the last check (the flag is then cleared). */
+zs_status zs_check_device_status(zs_handle h, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * Vocab-sharded sampling (tensor-parallel lm_head layout).  Rank g of n_ranks
+ * holds columns [vocab_offset, vocab_offset + n_local) of every row.  Each rank
+ *   1. zs_shard_partials: selects its local candidates -> a partial block
+ *      (per row: local top-k keys, local max, local sum-exp, flags);
+ *   2. all-gathers the partial blocks (any transport: NCCL, torch.distributed);
+ *   3. zs_shard_merge: merges the n_ranks blocks per row and draws.
+ * Every rank ends with identical ids and rng states.  zs_sample_sharded does the
+ * three steps with NCCL itself.  All ranks must pass the same batch, n_vocab_total,
+ * n_ranks and params.
+ * --------------------------------------------------------------------------------- */
+
+/* Bytes of one rank's partial block (the all-gather send size), for this batch. */
+zs_status zs_shard_partial_bytes(int32_t batch, int32_t n_vocab_total, int32_t n_ranks,
+                                 const zs_params* params, int32_t params_per_row,
+                                 int64_t* out_bytes);
+
+zs_status zs_shard_partials(zs_handle h, const float* logits_local, int64_t ld, int32_t batch,
+                            int32_t n_local, int32_t vocab_offset, int32_t n_vocab_total,
+                            int32_t n_ranks, const zs_params* params, int32_t params_per_row,
+                            const int32_t* history, int64_t history_ld,
+                            const int32_t* history_len, void* partial_out, int32_t want_log_z,
+                            void* stream);
+
+/* gathered: device, n_ranks partial blocks back to back (rank order). */
+zs_status zs_shard_merge(zs_handle h, const void* gathered, int32_t n_ranks, int32_t batch,
+                         int32_t n_vocab_total, const zs_params* params, int32_t params_per_row,
+                         uint64_t* rng_state, int32_t* out_ids, const zs_extras* extras,
+                         void* stream);
+
+/* Steps 1-3 with an ncclComm_t (passed as void*) created by the caller against the
+ * NCCL that this process has loaded (libnccl.so.2 is resolved at run time). */
+zs_status zs_sample_sharded(zs_handle h, const float* logits_local, int64_t ld, int32_t batch,
+                            int32_t n_local, int32_t vocab_offset, int32_t n_vocab_total,
+                            int32_t n_ranks, const zs_params* params, int32_t params_per_row,
+                            const int32_t* history, int64_t history_ld,
+                            const int32_t* history_len, uint64_t* rng_state, int32_t* out_ids,
+                            const zs_extras* extras, void* nccl_comm, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ZS_SAMPLER_H_ */

@@ -1,0 +1,177 @@
+"""Checkers for the B200 sampler -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg import
+this package.  The product (zeninfer_b200/) never does.
+
+    restatement   liboracle.so        C restatement of src/sample.cpp with a total
+                                      shortlist order (value desc, id asc); exposes
+                                      the shortlist, p_i, m, r, boundary distance
+    reference     _ref/libzen_ref.so  the reference's src/sample.cpp compiled
+                                      unchanged, with a row-loop harness
+
+Both are built by oracle/Makefile (`make -C oracle`).
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libzen_ref.so")
+
+ROW_INFO_DTYPE = np.dtype([("max_logit", "<f4"), ("k", "<i4"), ("m", "<i4"), ("pos", "<i4"),
+                           ("r", "<f8"), ("sum", "<f8"), ("boundary", "<f8"), ("log_z", "<f8")])
+
+PARAMS_DTYPE = np.dtype([("temp", "<f4"), ("top_k", "<i4"), ("top_p", "<f4"),
+                         ("repeat_penalty", "<f4"), ("repeat_last_n", "<i4")])
+
+
+def params_array(params, batch=None) -> np.ndarray:
+    """SamplingParams-like object(s) -> PARAMS_DTYPE array."""
+    if not isinstance(params, (list, tuple)):
+        params = [params]
+    arr = np.zeros(len(params), dtype=PARAMS_DTYPE)
+    for i, p in enumerate(params):
+        arr[i] = (p.temp, p.top_k, p.top_p, p.repeat_penalty, p.repeat_last_n)
+    return arr
+
+
+_olib = None
+_rlib = None
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data
+
+
+def olib():
+    global _olib
+    if _olib is None:
+        if not os.path.exists(ORACLE_SO):
+            raise RuntimeError(f"{ORACLE_SO} missing; run make -C oracle")
+        L = C.CDLL(ORACLE_SO)
+        vp = C.c_void_p
+        L.zo_sample_rows.argtypes = [vp, C.c_int64, C.c_int, C.c_int, vp, C.c_int, vp, C.c_int64,
+                                     vp, vp, vp, vp, vp, vp, C.c_int, vp, C.c_int, C.c_int]
+        L.zo_sample_rows.restype = C.c_int
+        L.zo_argmax.argtypes = [vp, C.c_int]
+        L.zo_argmax.restype = C.c_int32
+        L.zo_rng_seed.argtypes = [C.c_uint64]
+        L.zo_rng_seed.restype = C.c_uint64
+        L.zo_rng_uniform.argtypes = [C.POINTER(C.c_uint64)]
+        L.zo_rng_uniform.restype = C.c_double
+        _olib = L
+    return _olib
+
+
+def rlib():
+    global _rlib
+    if _rlib is None:
+        if not os.path.exists(REF_SO):
+            raise RuntimeError(f"{REF_SO} missing; run make -C oracle ref (needs the reference)")
+        L = C.CDLL(REF_SO)
+        vp = C.c_void_p
+        L.zref_sample_rows.argtypes = [vp, C.c_int64, C.c_int, C.c_int, vp, C.c_int, vp, C.c_int64,
+                                       vp, vp, vp, vp, C.c_int]
+        L.zref_sample_rows.restype = C.c_int
+        L.zref_argmax.argtypes = [vp, C.c_int]
+        L.zref_argmax.restype = C.c_int32
+        L.zref_rng_stream.argtypes = [C.c_uint64, C.c_int, vp, vp]
+        L.zref_rng_stream.restype = None
+        _rlib = L
+    return _rlib
+
+
+def have_reference() -> bool:
+    return os.path.exists(REF_SO)
+
+
+def oracle_sample(logits: np.ndarray, params, states: np.ndarray, history=None, history_len=None,
+                  cand_ld: int = 0, full_z: bool = False, nthreads: int | None = None):
+    """Restatement over rows of `logits` [B, ld] (first n = logits.shape[1] columns
+    unless `n` differs).  states: uint64 [B] xorshift64* states, advanced in place.
+    Returns (ids int32[B], infos ROW_INFO_DTYPE[B], cand_ids, cand_vals, cand_probs)."""
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    B, n = logits.shape
+    par = params_array(params)
+    per_row = 1 if len(par) > 1 else 0
+    if per_row and len(par) != B:
+        raise ValueError("need one params entry per row")
+    ids = np.zeros(B, dtype=np.int32)
+    infos = np.zeros(B, dtype=ROW_INFO_DTYPE)
+    cid = cv = cp = None
+    if cand_ld > 0:
+        cid = np.full((B, cand_ld), -1, dtype=np.int32)
+        cv = np.zeros((B, cand_ld), dtype=np.float32)
+        cp = np.zeros((B, cand_ld), dtype=np.float64)
+    h = hl = None
+    hld = 0
+    if history is not None:
+        h = np.ascontiguousarray(history, dtype=np.int32)
+        hl = np.ascontiguousarray(history_len, dtype=np.int32)
+        hld = h.shape[1]
+    assert states.dtype == np.uint64 and states.flags["C_CONTIGUOUS"]
+    nthreads = nthreads or min(64, os.cpu_count() or 1)
+    olib().zo_sample_rows(logits.ctypes.data, n, B, n, par.ctypes.data, per_row, _ptr(h), hld,
+                          _ptr(hl), states.ctypes.data, ids.ctypes.data, _ptr(cid), _ptr(cv),
+                          _ptr(cp), cand_ld, infos.ctypes.data, 1 if full_z else 0, nthreads)
+    return ids, infos, cid, cv, cp
+
+
+def reference_sample(logits: np.ndarray, params, seeds: np.ndarray, history=None,
+                     history_len=None, nthreads: int | None = None, ld: int | None = None,
+                     n: int | None = None):
+    """The unchanged reference, one zen::Rng(seeds[r]) per row.
+    Returns (ids int32[B], next_after uint64[B]) -- the Rng's next() after the call."""
+    B = logits.shape[0]
+    ld = logits.shape[1] if ld is None else ld
+    n = logits.shape[1] if n is None else n
+    par = params_array(params)
+    per_row = 1 if len(par) > 1 else 0
+    ids = np.zeros(B, dtype=np.int32)
+    nxt = np.zeros(B, dtype=np.uint64)
+    seeds = np.ascontiguousarray(seeds, dtype=np.uint64)
+    h = hl = None
+    hld = 0
+    if history is not None:
+        h = np.ascontiguousarray(history, dtype=np.int32)
+        hl = np.ascontiguousarray(history_len, dtype=np.int32)
+        hld = h.shape[1]
+    nthreads = nthreads or min(64, os.cpu_count() or 1)
+    rlib().zref_sample_rows(logits.ctypes.data, ld, B, n, par.ctypes.data, per_row, _ptr(h), hld,
+                            _ptr(hl), seeds.ctypes.data, ids.ctypes.data, nxt.ctypes.data,
+                            nthreads)
+    return ids, nxt
+
+
+def reference_argmax(row: np.ndarray, n: int | None = None) -> int:
+    row = np.ascontiguousarray(row, dtype=np.float32)
+    return int(rlib().zref_argmax(row.ctypes.data, row.size if n is None else n))
+
+
+def oracle_argmax(row: np.ndarray, n: int | None = None) -> int:
+    row = np.ascontiguousarray(row, dtype=np.float32)
+    return int(olib().zo_argmax(row.ctypes.data, row.size if n is None else n))
+
+
+def reference_rng_stream(seed: int, count: int):
+    out = np.zeros(count, dtype=np.uint64)
+    u = C.c_double()
+    rlib().zref_rng_stream(seed, count, out.ctypes.data, C.addressof(u))
+    return out, u.value
+
+
+def build(with_reference: bool | None = None) -> None:
+    """make -C oracle (the reference part only where its sources exist)."""
+    import subprocess
+    targets = ["oracle"]
+    ref_src = os.environ.get("REF_SRC", "/root/reference/src")
+    if with_reference or (with_reference is None and os.path.exists(os.path.join(ref_src, "sample.cpp"))):
+        targets.append("ref")
+    r = subprocess.run(["make", "-s", "-C", HERE, *targets], capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError("oracle build failed:\n" + r.stdout + r.stderr)

@@ -1,0 +1,338 @@
+/*
+ * sampler_oracle.c -- CPU restatement of zeninfer's token sampler.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the checker for the CUDA sampler in
+ * zeninfer_b200/csrc; nothing in the product links, loads or calls it.  Only
+ * tests/, __graft_entry__.smoke() and bench.py's cpu_baseline leg use it.
+ *
+ * It restates src/sample.cpp of the reference step by step (same f32 / f64
+ * expressions, same summation order) with one deliberate change: the shortlist
+ * order is total -- value descending, then token id ascending -- where the
+ * reference's std::nth_element / std::sort (src/sample.cpp:101-106) order equal
+ * values in whatever way libstdc++'s introselect leaves them.  NaN logits rank
+ * below every number (the reference's comparator is not a strict weak order
+ * with NaNs, so its output there is unspecified).  On rows without ties at the
+ * shortlist boundary it must agree bit for bit with the reference compiled
+ * unchanged (oracle/_ref); tests/test_oracle.py checks exactly that.
+ *
+ * Besides the sampled id it exposes what the reference keeps internal: the
+ * sorted shortlist (ids, values), the shortlist softmax p_i, the nucleus size m,
+ * the uniform draw r and the distance of r to the nearest CDF boundary.
+ */
+#include <math.h>
+#include <pthread.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* Same field order and meaning as zen::SamplingParams (src/sample.h:9-15). */
+typedef struct zo_params {
+    float temp;
+    int32_t top_k;
+    float top_p;
+    float repeat_penalty;
+    int32_t repeat_last_n;
+} zo_params;
+
+/* Per-row diagnostics; same layout as zs_row_info in include/zs_sampler.h. */
+typedef struct zo_row_info {
+    float max_logit;
+    int32_t k;
+    int32_t m;
+    int32_t pos;
+    double r;
+    double sum;
+    double boundary;
+    double log_z;
+} zo_row_info;
+
+#define ZO_TOPP_SHORTLIST 256 /* kTopPShortlist, src/sample.cpp:12 */
+
+/* xorshift64*  (src/sample.h:18-26, src/sample.cpp:15-22). */
+uint64_t zo_rng_seed(uint64_t seed) { return seed ? seed : 0x9E3779B97F4A7C15ull; }
+
+uint64_t zo_rng_next(uint64_t* s) {
+    uint64_t x = *s;
+    x ^= x >> 12;
+    x ^= x << 25;
+    x ^= x >> 27;
+    *s = x;
+    return x * 2685821657736338717ull;
+}
+
+double zo_rng_uniform(uint64_t* s) {
+    return (double)(zo_rng_next(s) >> 11) * (1.0 / 9007199254740992.0);
+}
+
+/* argmax_token, src/sample.cpp:24-30: strict '>' so the first maximum wins. */
+int32_t zo_argmax(const float* x, int n) {
+    int32_t best = 0;
+    for (int i = 1; i < n; ++i)
+        if (x[i] > x[best]) best = i;
+    return best;
+}
+
+/* Total order key: value descending (NaN lowest, -0 == +0), then id ascending. */
+static inline uint32_t ord_of(float v) {
+    if (v != v) return 0u;
+    if (v == 0.0f) v = 0.0f;
+    uint32_t u;
+    memcpy(&u, &v, 4);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+static inline uint64_t key_of(float v, int32_t id) {
+    return ((uint64_t)ord_of(v) << 32) | (uint64_t)(uint32_t)(~(uint32_t)id);
+}
+
+static inline int32_t id_of(uint64_t key) { return (int32_t)(~(uint32_t)(key & 0xffffffffu)); }
+
+/* Rearranges a[0..n) so that a[0..k) hold the k largest keys (keys are unique). */
+static void select_largest(uint64_t* a, size_t n, size_t k) {
+    size_t lo = 0, hi = n;
+    if (k == 0 || k >= n) return;
+    while (hi - lo > 1) {
+        size_t mid = lo + (hi - lo) / 2;
+        uint64_t x = a[lo], y = a[mid], z = a[hi - 1];
+        size_t pidx;
+        if ((x < y) == (y < z)) pidx = mid;
+        else if ((y < x) == (x < z)) pidx = lo;
+        else pidx = hi - 1;
+        uint64_t piv = a[pidx];
+        a[pidx] = a[hi - 1];
+        a[hi - 1] = piv;
+        size_t store = lo;
+        for (size_t i = lo; i < hi - 1; ++i) {
+            if (a[i] > piv) {
+                uint64_t t = a[i];
+                a[i] = a[store];
+                a[store] = t;
+                ++store;
+            }
+        }
+        a[hi - 1] = a[store];
+        a[store] = piv;
+        if (store == k || store + 1 == k) return;
+        if (store > k) hi = store;
+        else lo = store + 1;
+    }
+}
+
+static int cmp_desc(const void* pa, const void* pb) {
+    uint64_t a = *(const uint64_t*)pa, b = *(const uint64_t*)pb;
+    return (a < b) - (a > b);
+}
+
+/* Applies the repetition penalty in place (src/sample.cpp:40-50): compounds per
+ * history entry, skips out-of-range ids, only over the last repeat_last_n. */
+static void apply_penalty(float* x, int n, const zo_params* p, const int32_t* hist, int hist_len) {
+    if (!(p->repeat_penalty != 1.0f) || hist_len <= 0 || hist == NULL) return;
+    size_t keep = (size_t)(p->repeat_last_n > 0 ? p->repeat_last_n : 0);
+    size_t len = (size_t)hist_len;
+    size_t begin = len > keep ? len - keep : 0;
+    for (size_t i = begin; i < len; ++i) {
+        int32_t id = hist[i];
+        if (id < 0 || id >= n) continue;
+        float v = x[id];
+        x[id] = (v > 0.0f) ? v / p->repeat_penalty : v * p->repeat_penalty;
+    }
+}
+
+/*
+ * One row, following sample_token (src/sample.cpp:32-102).
+ *   work: n floats + n uint64 of scratch, or NULL to allocate.
+ *   cand_ids/cand_vals/cand_probs (nullable, capacity cand_cap): sorted shortlist
+ *   and its softmax p_i (before the nucleus rescale).
+ *   full_z: when nonzero, info->log_z = log(sum_i exp((x_i - max_l) * inv_t)) over
+ *   the whole penalised row in f64 (inv_t = 1 for greedy rows).
+ */
+int32_t zo_sample_row(const float* logits, int n, const zo_params* p, const int32_t* hist,
+                      int hist_len, uint64_t* state, int32_t* cand_ids, float* cand_vals,
+                      double* cand_probs, int cand_cap, zo_row_info* info, int full_z,
+                      void* work) {
+    zo_row_info local;
+    if (info == NULL) info = &local;
+    info->max_logit = 0.0f;
+    info->k = 0;
+    info->m = 0;
+    info->pos = -1;
+    info->r = 0.0;
+    info->sum = 0.0;
+    info->boundary = 0.0;
+    info->log_z = NAN;
+    if (n <= 0) return 0;
+
+    int own = (work == NULL);
+    if (own) work = malloc((size_t)n * (sizeof(float) + sizeof(uint64_t)));
+    uint64_t* keys = (uint64_t*)work;
+    float* x = (float*)(keys + n);
+    memcpy(x, logits, (size_t)n * sizeof(float));
+    apply_penalty(x, n, p, hist, hist_len);
+
+    if (full_z) {
+        float inv_t = (p->temp > 0.0f) ? 1.0f / p->temp : 1.0f;
+        float mx = x[0];
+        for (int i = 1; i < n; ++i) mx = (mx < x[i]) ? x[i] : mx;
+        double z = 0.0;
+        for (int i = 0; i < n; ++i) z += exp(((double)x[i] - (double)mx) * (double)inv_t);
+        info->log_z = log(z);
+    }
+
+    if (p->temp <= 0.0f) {
+        int32_t id = zo_argmax(x, n);
+        info->max_logit = x[id];
+        if (own) free(work);
+        return id;
+    }
+
+    const float inv_temp = 1.0f / p->temp;
+    float max_l = x[0];
+    for (int i = 1; i < n; ++i) max_l = (max_l < x[i]) ? x[i] : max_l; /* std::max */
+    info->max_logit = max_l;
+
+    int k = (p->top_k > 0) ? (p->top_k < n ? p->top_k : n)
+                           : (ZO_TOPP_SHORTLIST < n ? ZO_TOPP_SHORTLIST : n);
+    for (int i = 0; i < n; ++i) keys[i] = key_of(x[i], i);
+    select_largest(keys, (size_t)n, (size_t)k);
+    qsort(keys, (size_t)k, sizeof(uint64_t), cmp_desc);
+
+    double* prob = (double*)malloc((size_t)k * sizeof(double));
+    double sum = 0.0;
+    for (int i = 0; i < k; ++i) {
+        const double e = exp(((double)x[id_of(keys[i])] - (double)max_l) * (double)inv_temp);
+        prob[i] = e;
+        sum += e;
+    }
+    for (int i = 0; i < k; ++i) prob[i] /= sum;
+    for (int i = 0; i < k && i < cand_cap; ++i) {
+        int32_t id = id_of(keys[i]);
+        if (cand_ids) cand_ids[i] = id;
+        if (cand_vals) cand_vals[i] = x[id];
+        if (cand_probs) cand_probs[i] = prob[i];
+    }
+
+    int m = k;
+    if (p->top_p < 1.0f) {
+        double acc = 0.0;
+        m = 0;
+        while (m < k && acc < (double)p->top_p) {
+            acc += prob[m];
+            ++m;
+        }
+        if (m == 0) m = 1;
+        double rescale = 0.0;
+        for (int i = 0; i < m; ++i) rescale += prob[i];
+        for (int i = 0; i < m; ++i) prob[i] /= rescale;
+    }
+
+    const double r = zo_rng_uniform(state);
+    double acc = 0.0, prev = 0.0;
+    int pos = m - 1;
+    int hit = 0;
+    for (int i = 0; i < m; ++i) {
+        prev = acc;
+        acc += prob[i];
+        if (r < acc) {
+            pos = i;
+            hit = 1;
+            break;
+        }
+    }
+    double d;
+    if (hit) {
+        double a = r - prev, b = acc - r;
+        d = a < b ? a : b;
+    } else {
+        d = r - acc;
+    }
+    int32_t out = id_of(keys[pos]);
+    info->k = k;
+    info->m = m;
+    info->pos = pos;
+    info->r = r;
+    info->sum = sum;
+    info->boundary = d;
+    free(prob);
+    if (own) free(work);
+    return out;
+}
+
+/* ---- batched, multithreaded driver (rows are independent) ---- */
+
+typedef struct {
+    const float* logits;
+    int64_t ld;
+    int B, n;
+    const zo_params* params;
+    int params_per_row;
+    const int32_t* hist;
+    int64_t hist_ld;
+    const int32_t* hist_len;
+    uint64_t* states;
+    int32_t* out_ids;
+    int32_t* cand_ids;
+    float* cand_vals;
+    double* cand_probs;
+    int cand_ld;
+    zo_row_info* infos;
+    int full_z;
+    int next_row;
+    pthread_mutex_t mu;
+} zo_batch;
+
+static void* zo_worker(void* arg) {
+    zo_batch* b = (zo_batch*)arg;
+    void* work = malloc((size_t)b->n * (sizeof(float) + sizeof(uint64_t)) + 64);
+    for (;;) {
+        pthread_mutex_lock(&b->mu);
+        int r = b->next_row++;
+        pthread_mutex_unlock(&b->mu);
+        if (r >= b->B) break;
+        const zo_params* p = b->params + (b->params_per_row ? r : 0);
+        const int32_t* h = b->hist ? b->hist + (int64_t)r * b->hist_ld : NULL;
+        int hl = b->hist_len ? b->hist_len[r] : 0;
+        size_t co = (size_t)r * (size_t)(b->cand_ld > 0 ? b->cand_ld : 0);
+        b->out_ids[r] = zo_sample_row(b->logits + (int64_t)r * b->ld, b->n, p, h, hl,
+                                      &b->states[r], b->cand_ids ? b->cand_ids + co : NULL,
+                                      b->cand_vals ? b->cand_vals + co : NULL,
+                                      b->cand_probs ? b->cand_probs + co : NULL, b->cand_ld,
+                                      b->infos ? &b->infos[r] : NULL, b->full_z, work);
+    }
+    free(work);
+    return NULL;
+}
+
+int zo_sample_rows(const float* logits, int64_t ld, int B, int n, const zo_params* params,
+                   int params_per_row, const int32_t* hist, int64_t hist_ld,
+                   const int32_t* hist_len, uint64_t* states, int32_t* out_ids, int32_t* cand_ids,
+                   float* cand_vals, double* cand_probs, int cand_ld, zo_row_info* infos,
+                   int full_z, int nthreads) {
+    zo_batch b;
+    b.logits = logits;
+    b.ld = ld;
+    b.B = B;
+    b.n = n;
+    b.params = params;
+    b.params_per_row = params_per_row;
+    b.hist = hist;
+    b.hist_ld = hist_ld;
+    b.hist_len = hist_len;
+    b.states = states;
+    b.out_ids = out_ids;
+    b.cand_ids = cand_ids;
+    b.cand_vals = cand_vals;
+    b.cand_probs = cand_probs;
+    b.cand_ld = cand_ld;
+    b.infos = infos;
+    b.full_z = full_z;
+    b.next_row = 0;
+    pthread_mutex_init(&b.mu, NULL);
+    if (nthreads < 1) nthreads = 1;
+    if (nthreads > 256) nthreads = 256;
+    pthread_t th[256];
+    for (int t = 1; t < nthreads; ++t) pthread_create(&th[t], NULL, zo_worker, &b);
+    zo_worker(&b);
+    for (int t = 1; t < nthreads; ++t) pthread_join(th[t], NULL);
+    pthread_mutex_destroy(&b.mu);
+    return 0;
+}

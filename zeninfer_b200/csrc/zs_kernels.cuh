@@ -1,0 +1,1193 @@
+// zs_kernels.cuh -- the sampler's device code.
+//
+// One launch of zs_select_kernel streams every logits row once from HBM and
+// produces, per row, the sampled id (or a partial candidate block for the
+// vocab-sharded mode).  Semantics follow sample_token, src/sample.cpp:32-102.
+//
+// Work unit = (row, vocab slice).  Large batches use one slice per row; small
+// batches cut rows into slices so every SM has work, and the CTA that finishes
+// a row's last slice merges the slices' partial blocks.
+//
+// Per CTA: one producer warp issues 1-D bulk copies (cp.async.bulk, no tensor
+// map, no multicast) of 8 KB tiles into an 8-stage shared-memory ring,
+// completion tracked by mbarrier transaction counts.  Eight consumer warps
+// filter each tile against the current threshold key: a float4 whose max is
+// below the threshold value costs four FMNMX and one vote; survivors are
+// appended with warp ballots to a shared candidate buffer.  When the buffer
+// fills, an exact radix select (8-bit digits over the 64-bit key) keeps the
+// K_eff best and raises the threshold.  At the end of a unit the survivors are
+// sorted (bitonic), the repetition penalty is patched in, and the f64 tail of
+// the reference (softmax over the shortlist, nucleus, inverse CDF) runs in
+// the reference's summation order.
+#pragma once
+
+#include <math.h>
+
+#include "zs_device.cuh"
+
+namespace zs {
+
+constexpr int kConsumerWarps = 8;
+constexpr int kNC = kConsumerWarps * 32;  // consumer threads
+constexpr int kThreads = kNC + 32;        // + one producer warp
+constexpr int kTileElems = 2048;          // floats per ring stage (8 KB)
+constexpr int kStages = 8;
+constexpr int kKeffFastMax = 2048;        // top-k + penalty window handled in shared memory
+constexpr int kWinFastMax = 512;          // penalty window handled in shared memory
+constexpr int kCandMargin = 16;           // head/tail elements appended outside the tile check
+constexpr int kSlackKeep = 64;            // a compaction may keep up to this many extra keys
+constexpr int kCompactMinGrowth = 512;    // compact once the buffer grew by max(K_eff, this)
+constexpr int kCandCap = 4224;            // >= kKeffFastMax + kSlackKeep + kTileElems + kCandMargin
+constexpr int kCandRegs = (kCandCap + kNC - 1) / kNC;
+constexpr int kSortMax = 4096;            // bitonic size bound (kKeffFastMax + kWinFastMax -> 4096)
+constexpr int kProbOffset = 2048;         // f64 probabilities alias cand[2048..4096)
+constexpr int kShortlistDefault = 256;    // kTopPShortlist, src/sample.cpp:12
+
+static_assert(kCandCap >= kKeffFastMax + kSlackKeep + kTileElems + kCandMargin,
+              "candidate buffer too small");
+static_assert(kSortMax <= kCandCap, "sort region exceeds the candidate buffer");
+static_assert(kProbOffset + kKeffFastMax / 1 * 1 <= kCandCap, "probability region");
+
+struct Params {  // zen::SamplingParams layout
+    float temp;
+    int32_t top_k;
+    float top_p;
+    float repeat_penalty;
+    int32_t repeat_last_n;
+};
+
+struct RowInfo {  // zs_row_info layout
+    float max_logit;
+    int32_t k;
+    int32_t m;
+    int32_t pos;
+    double r;
+    double sum;
+    double boundary;
+    double log_z;
+};
+
+// Partial block of one (row, slice): header then `count` keys sorted descending.
+struct PartialHeader {
+    uint32_t count;
+    uint32_t flags;
+    float lse_m;
+    float lse_s;
+};
+constexpr uint32_t kPartHasId0 = 1u;
+constexpr uint32_t kPartX0Nan = 2u;
+constexpr int kPartialHeaderBytes = 16;
+
+struct StageMeta {
+    int32_t unit;
+    int32_t start;
+    int32_t n;
+    int32_t flags;
+};
+constexpr int kMetaFirst = 1, kMetaLast = 2, kMetaDone = 4;
+
+constexpr int kStatusTimeout = 4;  // ZS_ERR_DEVICE_TIMEOUT
+
+struct Args {
+    const float* logits;
+    int64_t ld;
+    int32_t B;
+    int32_t V;          // columns held here
+    int32_t id_offset;  // global id of local column 0 (vocab shard)
+    int32_t V_total;    // vocabulary size n of sample_token
+    Params shared;
+    const Params* row_params;  // device [B] or null
+    const int32_t* hist;
+    int64_t hist_ld;
+    const int32_t* hist_len;
+    uint64_t* rng;
+    int32_t* out_ids;
+    RowInfo* info;
+    int32_t* cand_ids;
+    double* cand_probs;
+    int32_t cand_ld;
+    int32_t S;      // slices per row
+    int32_t slice;  // columns per slice (multiple of 4)
+    int32_t n_units;
+    int32_t mode;   // 0: draw here; 1: write partial blocks only (vocab shard)
+    uint8_t* part;  // partial blocks [B][S]
+    int64_t part_stride;
+    unsigned* row_cnt;  // [B] arrival counters, zero between launches
+    int* status;
+    // large-k path workspace
+    uint8_t* large_ws;
+    int64_t large_ws_per_cta;
+};
+
+struct MergeArgs {
+    const uint8_t* gathered;
+    int64_t rank_stride;
+    int32_t G;
+    int32_t S;
+    int64_t part_stride;
+    int32_t B;
+    int32_t V_total;
+    Params shared;
+    const Params* row_params;
+    uint64_t* rng;
+    int32_t* out_ids;
+    RowInfo* info;
+    int32_t* cand_ids;
+    double* cand_probs;
+    int32_t cand_ld;
+    int* status;
+};
+
+struct RowPlan {
+    Params p;
+    int32_t ksel;  // shortlist size (1 for greedy)
+    int32_t win;   // penalty window length
+    int32_t keff;  // ksel + win
+    int32_t hist_len;
+    bool greedy;
+    bool penal;
+    bool fast;
+};
+
+__device__ __forceinline__ Params load_params(const Params* rp, const Params& shared, int row) {
+    return rp ? rp[row] : shared;
+}
+
+__device__ __forceinline__ RowPlan plan_row(const Params& p, int V_total, const int32_t* hist,
+                                            const int32_t* hist_len, int64_t hist_ld, int row) {
+    RowPlan r;
+    r.p = p;
+    r.greedy = (p.temp <= 0.0f);
+    if (r.greedy) r.ksel = 1;
+    else if (p.top_k > 0) r.ksel = p.top_k < V_total ? p.top_k : V_total;
+    else r.ksel = kShortlistDefault < V_total ? kShortlistDefault : V_total;
+    r.hist_len = 0;
+    r.win = 0;
+    if (p.repeat_penalty != 1.0f && hist != nullptr && hist_len != nullptr) {
+        int len = hist_len[row];
+        if ((int64_t)len > hist_ld) len = (int)hist_ld;  // never read past the row
+        const int keep = p.repeat_last_n > 0 ? p.repeat_last_n : 0;
+        r.hist_len = len;
+        r.win = len > 0 ? (len < keep ? len : keep) : 0;
+    }
+    r.penal = r.win > 0;
+    r.keff = r.ksel + r.win;
+    r.fast = (r.keff <= kKeffFastMax) && (r.win <= kWinFastMax);
+    return r;
+}
+
+struct UnitGeom {
+    int32_t row, s;
+    int32_t v0, v1;  // columns of the unit
+    int32_t e0, e1;  // 16-byte aligned sub-range moved by bulk copies
+};
+
+__device__ __forceinline__ UnitGeom unit_geom(const Args& a, int u) {
+    UnitGeom g;
+    g.row = u / a.S;
+    g.s = u - g.row * a.S;
+    const int64_t v0 = (int64_t)g.s * a.slice;
+    g.v0 = (int32_t)(v0 < a.V ? v0 : a.V);
+    g.v1 = (int32_t)((int64_t)g.v0 + a.slice < a.V ? g.v0 + a.slice : a.V);
+    const uintptr_t p0 = (uintptr_t)(a.logits + (int64_t)g.row * a.ld + g.v0);
+    const int pad = (int)(((16u - (unsigned)(p0 & 15u)) & 15u) >> 2);
+    int e0 = g.v0 + pad;
+    if (e0 >= g.v1) {
+        g.e0 = g.e1 = g.v1;
+    } else {
+        g.e0 = e0;
+        g.e1 = e0 + ((g.v1 - e0) & ~3);
+    }
+    return g;
+}
+
+// ---------------------------------------------------------------------------
+// Shared state of the consumer warps
+// ---------------------------------------------------------------------------
+struct CandState {
+    uint64_t cand[kCandCap];
+    uint32_t hist[256];
+    uint32_t scan[kConsumerWarps + 1];
+    uint64_t red64[kConsumerWarps];
+    uint64_t red64b[kConsumerWarps];
+    float redf[2 * kConsumerWarps];
+    int32_t win[kWinFastMax];
+    uint64_t thr;
+    uint64_t thr2;
+    double d_sum;
+    double d_rescale;
+    double lse_delta;
+    uint32_t count;
+    uint32_t removed;
+    uint32_t sel_digit, sel_above, sel_cnt;
+    int32_t abort;
+    int32_t is_last;
+    int32_t x0_nan;
+    int32_t m;
+    float lse_m, lse_s;
+};
+
+struct FastSmem {
+    float ring[kStages][kTileElems];
+    uint64_t full[kStages];
+    uint64_t empty[kStages];
+    StageMeta meta[kStages];
+    CandState st;
+};
+
+// ---- block primitives over the kNC consumer threads ----
+
+__device__ __forceinline__ void csync() { consumer_sync<kNC>(); }
+
+// Inclusive scan across the consumer threads; ends synchronised.
+__device__ __forceinline__ uint32_t block_incl_scan(uint32_t v, uint32_t* s_scan, int ctid,
+                                                    uint32_t& total) {
+    const int lane = ctid & 31, warp = ctid >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(kFull, v, o);
+        if (lane >= o) v += t;
+    }
+    if (lane == 31) s_scan[warp] = v;
+    csync();
+    if (warp == 0) {
+        uint32_t w = lane < kConsumerWarps ? s_scan[lane] : 0u;
+#pragma unroll
+        for (int o = 1; o < kConsumerWarps; o <<= 1) {
+            const uint32_t t = __shfl_up_sync(kFull, w, o);
+            if (lane >= o) w += t;
+        }
+        if (lane < kConsumerWarps) s_scan[lane] = w;
+    }
+    csync();
+    const uint32_t pre = warp ? s_scan[warp - 1] : 0u;
+    total = s_scan[kConsumerWarps - 1];
+    csync();
+    return v + pre;
+}
+
+__device__ __forceinline__ uint64_t warp_min_u64(uint64_t v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const uint64_t t = __shfl_xor_sync(kFull, v, o);
+        v = t < v ? t : v;
+    }
+    return v;
+}
+
+__device__ __forceinline__ uint64_t warp_max_u64(uint64_t v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const uint64_t t = __shfl_xor_sync(kFull, v, o);
+        v = t > v ? t : v;
+    }
+    return v;
+}
+
+// Appends key k (if pred) with one atomic per warp.  All 32 lanes must call.
+__device__ __forceinline__ void warp_append(CandState& st, bool pred, uint64_t k, int lane) {
+    const unsigned m = __ballot_sync(kFull, pred);
+    if (m) {
+        const int leader = __ffs(m) - 1;
+        uint32_t base = 0;
+        if (lane == leader) base = atomicAdd(&st.count, (uint32_t)__popc(m));
+        base = __shfl_sync(kFull, base, leader);
+        if (pred) st.cand[base + __popc(m & lanemask_lt())] = k;
+    }
+}
+
+// Appends the components of v (ids id..id+3) whose keys beat tau: one warp
+// scan and one shared atomic per warp.  All 32 lanes must call.
+__device__ __forceinline__ void append4(CandState& st, bool hit, const float4& v, int32_t id,
+                                        uint64_t tau, int lane) {
+    const uint64_t k0 = make_key(v.x, id), k1 = make_key(v.y, id + 1);
+    const uint64_t k2 = make_key(v.z, id + 2), k3 = make_key(v.w, id + 3);
+    const bool a0 = hit && k0 > tau, a1 = hit && k1 > tau, a2 = hit && k2 > tau, a3 = hit && k3 > tau;
+    const uint32_t c = (uint32_t)a0 + (uint32_t)a1 + (uint32_t)a2 + (uint32_t)a3;
+    uint32_t incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += t;
+    }
+    const uint32_t total = __shfl_sync(kFull, incl, 31);
+    if (total == 0) return;
+    uint32_t base = 0;
+    if (lane == 31) base = atomicAdd(&st.count, total);
+    base = __shfl_sync(kFull, base, 31);
+    uint32_t pos = base + incl - c;
+    if (a0) st.cand[pos++] = k0;
+    if (a1) st.cand[pos++] = k1;
+    if (a2) st.cand[pos++] = k2;
+    if (a3) st.cand[pos] = k3;
+}
+
+// Appends one element without warp cooperation (head/tail columns).
+__device__ __forceinline__ void single_append(CandState& st, float x, int32_t id,
+                                              uint64_t tau_key) {
+    const uint64_t k = make_key(x, id);
+    if (k > tau_key) st.cand[atomicAdd(&st.count, 1u)] = k;
+}
+
+// Online log-sum-exp in base 2: s = sum 2^((x - m) * c).
+__device__ __forceinline__ void lse_add4(float& m, float& s, const float4& v, float vm, float c) {
+    const float mn = fmaxf(m, vm);
+    if (mn > m) {
+        s *= fast_exp2((m - mn) * c);
+        m = mn;
+    }
+    if (m > -INFINITY) {
+        s += fast_exp2((v.x - m) * c) + fast_exp2((v.y - m) * c) + fast_exp2((v.z - m) * c) +
+             fast_exp2((v.w - m) * c);
+    }
+}
+
+__device__ __forceinline__ void lse_add1(float& m, float& s, float x, float c) {
+    const float mn = fmaxf(m, x);
+    if (mn > m) {
+        s *= fast_exp2((m - mn) * c);
+        m = mn;
+    }
+    if (m > -INFINITY) s += fast_exp2((x - m) * c);
+}
+
+__device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2, float c) {
+    const float M = fmaxf(m, m2);
+    if (!(M > -INFINITY)) {
+        m = M;
+        s = 0.0f;
+        return;
+    }
+    const float a = (m > -INFINITY) ? s * fast_exp2((m - M) * c) : 0.0f;
+    const float b = (m2 > -INFINITY) ? s2 * fast_exp2((m2 - M) * c) : 0.0f;
+    m = M;
+    s = a + b;
+}
+
+// Reduces the per-thread (m, s) pairs into st.lse_m / st.lse_s.
+__device__ __forceinline__ void block_lse(CandState& st, float m, float s, float c, int ctid) {
+    const int lane = ctid & 31, warp = ctid >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float m2 = __shfl_xor_sync(kFull, m, o);
+        const float s2 = __shfl_xor_sync(kFull, s, o);
+        lse_merge(m, s, m2, s2, c);
+    }
+    if (lane == 0) {
+        st.redf[2 * warp] = m;
+        st.redf[2 * warp + 1] = s;
+    }
+    csync();
+    if (ctid == 0) {
+        float M = st.redf[0], Sx = st.redf[1];
+        for (int w = 1; w < kConsumerWarps; ++w) lse_merge(M, Sx, st.redf[2 * w], st.redf[2 * w + 1], c);
+        st.lse_m = M;
+        st.lse_s = Sx;
+    }
+    csync();
+}
+
+// Threshold fast-test value for a threshold key.
+__device__ __forceinline__ float tau_value(uint64_t tau_key) {
+    if (tau_key == 0ull) return -INFINITY;
+    const uint32_t o = (uint32_t)(tau_key >> 32);
+    return o == 0u ? -INFINITY : value_of_ord(o);
+}
+
+// Keeps the kk largest of the n > kk keys in cand[0..) -- plus at most `slack`
+// more, when a whole radix bucket is cheaper to keep than to split -- and
+// returns the smallest kept key, the new filter threshold.  Radix select on
+// the 64-bit key with 8-bit digits, starting below the keys' common prefix;
+// histogram increments are aggregated per warp with match.any.
+__device__ uint64_t compact_top(CandState& st, uint32_t n, uint32_t kk, uint32_t slack,
+                                int ctid) {
+    const int lane = ctid & 31, warp = ctid >> 5;
+    uint64_t lo = ~0ull, hi = 0ull;
+    for (uint32_t i = ctid; i < n; i += kNC) {
+        const uint64_t k = st.cand[i];
+        lo = k < lo ? k : lo;
+        hi = k > hi ? k : hi;
+    }
+    lo = warp_min_u64(lo);
+    hi = warp_max_u64(hi);
+    if (lane == 0) {
+        st.red64[warp] = lo;
+        st.red64b[warp] = hi;
+    }
+    csync();
+    if (ctid == 0) {
+        uint64_t a = st.red64[0], b = st.red64b[0];
+        for (int w = 1; w < kConsumerWarps; ++w) {
+            a = st.red64[w] < a ? st.red64[w] : a;
+            b = st.red64b[w] > b ? st.red64b[w] : b;
+        }
+        st.thr = a;
+        st.thr2 = b;
+    }
+    csync();
+    const uint64_t diff = st.thr ^ st.thr2;  // n >= 2 unique keys: nonzero
+    int shift = diff ? ((63 - __clzll((long long)diff)) >> 3) << 3 : 0;
+    uint64_t mask = shift >= 56 ? 0ull : (~0ull << (shift + 8));
+    uint64_t prefix = st.thr & mask;
+    uint32_t need = kk;
+    for (; shift >= 0; shift -= 8) {
+        st.hist[ctid] = 0u;
+        csync();
+        for (uint32_t b0 = (uint32_t)warp * 32; b0 < n; b0 += kNC) {
+            const uint32_t i = b0 + lane;
+            const uint64_t k = i < n ? st.cand[i] : 0ull;
+            const bool in = i < n && (k & mask) == prefix;
+            const uint32_t d = in ? ((uint32_t)(k >> shift) & 255u) : 256u + lane;
+            const unsigned peers = __match_any_sync(kFull, d);
+            if (in && (__ffs(peers) - 1) == lane) atomicAdd(&st.hist[d], (uint32_t)__popc(peers));
+        }
+        csync();
+        const uint32_t h = st.hist[255 - ctid];
+        uint32_t tot;
+        const uint32_t cum = block_incl_scan(h, st.scan, ctid, tot);
+        if (cum >= need && cum - h < need) {
+            st.sel_digit = 255u - (uint32_t)ctid;
+            st.sel_above = cum - h;
+            st.sel_cnt = h;
+        }
+        csync();
+        const uint32_t digit = st.sel_digit, above = st.sel_above, cnt = st.sel_cnt;
+        prefix |= (uint64_t)digit << shift;
+        mask |= 0xffull << shift;
+        need -= above;
+        csync();
+        if (cnt <= need + slack) break;  // keeping the whole bucket is exact or close enough
+    }
+    // Threshold = smallest key of the selected bucket (all of it is kept).
+    uint64_t mn = ~0ull;
+    for (uint32_t i = ctid; i < n; i += kNC) {
+        const uint64_t k = st.cand[i];
+        if ((k & mask) == prefix && k < mn) mn = k;
+    }
+    mn = warp_min_u64(mn);
+    if (lane == 0) st.red64[warp] = mn;
+    csync();
+    if (ctid == 0) {
+        uint64_t t = st.red64[0];
+        for (int w = 1; w < kConsumerWarps; ++w) t = st.red64[w] < t ? st.red64[w] : t;
+        st.thr = t;
+    }
+    csync();
+    const uint64_t T = st.thr;
+    uint64_t loc[kCandRegs];
+    uint32_t c = 0;
+#pragma unroll
+    for (int j = 0; j < kCandRegs; ++j) {
+        const uint32_t i = ctid + j * kNC;
+        const uint64_t k = (i < n) ? st.cand[i] : 0ull;
+        loc[j] = k;
+        c += (k >= T) ? 1u : 0u;
+    }
+    uint32_t tot;
+    uint32_t o = block_incl_scan(c, st.scan, ctid, tot) - c;
+#pragma unroll
+    for (int j = 0; j < kCandRegs; ++j)
+        if (loc[j] >= T) st.cand[o++] = loc[j];
+    if (ctid == 0) st.count = tot;
+    csync();
+    return T;
+}
+
+// Sorts cand[0..n) descending (bitonic over the next power of two, 0-padded).
+__device__ void sort_desc(CandState& st, uint32_t n, int ctid) {
+    if (n <= 1) return;
+    uint32_t N = 2;
+    while (N < n) N <<= 1;
+    for (uint32_t i = n + ctid; i < N; i += kNC) st.cand[i] = 0ull;
+    csync();
+    for (uint32_t k = 2; k <= N; k <<= 1) {
+        for (uint32_t j = k >> 1; j > 0; j >>= 1) {
+            for (uint32_t i = ctid; i < (N >> 1); i += kNC) {
+                const uint32_t lo = ((i & ~(j - 1)) << 1) | (i & (j - 1));
+                const uint32_t hi = lo | j;
+                const uint64_t x = st.cand[lo], y = st.cand[hi];
+                const bool desc = (lo & k) == 0;
+                if (desc ? (x < y) : (x > y)) {
+                    st.cand[lo] = y;
+                    st.cand[hi] = x;
+                }
+            }
+            csync();
+        }
+    }
+}
+
+// Repetition penalty (src/sample.cpp:40-50) for the ids of this unit: drop the
+// raw keys of penalised ids from cand[0..n) (they become 0) and append the
+// penalised values, compounding once per occurrence in the window.
+//
+// When have_lse, the unit's sum-exp (relative to lse_m, base-2 scale lse_c) was
+// accumulated over raw values; st.lse_delta receives the change that replacing
+// each penalised id's raw value by its penalised value makes to it.
+__device__ void penalty_fixup(CandState& st, const float* row_logits, const int32_t* window,
+                              int W, float pen, int32_t id_offset, int32_t v0, int32_t v1,
+                              int32_t V_total, uint32_t n, bool have_lse, float lse_m,
+                              float lse_c, int ctid) {
+    for (int i = ctid; i < W; i += kNC) st.win[i] = window[i];
+    if (ctid == 0) {
+        st.removed = 0u;
+        st.lse_delta = 0.0;
+    }
+    csync();
+    for (uint32_t i = ctid; i < n; i += kNC) {
+        const int32_t gid = key_id(st.cand[i]);
+        for (int j = 0; j < W; ++j) {
+            if (st.win[j] == gid) {
+                st.cand[i] = 0ull;
+                atomicAdd(&st.removed, 1u);
+                break;
+            }
+        }
+    }
+    csync();
+    const int32_t lo = id_offset + v0, hi = id_offset + v1;
+    for (int j = ctid; j < W; j += kNC) {
+        const int32_t gid = st.win[j];
+        if (gid < 0 || gid >= V_total || gid < lo || gid >= hi) continue;
+        bool first = true;
+        for (int q = 0; q < j; ++q)
+            if (st.win[q] == gid) {
+                first = false;
+                break;
+            }
+        if (!first) continue;
+        int mult = 1;
+        for (int q = j + 1; q < W; ++q) mult += (st.win[q] == gid) ? 1 : 0;
+        const float raw = row_logits[gid - id_offset];
+        float v = raw;
+        for (int c = 0; c < mult; ++c) v = (v > 0.0f) ? v / pen : v * pen;
+        st.cand[atomicAdd(&st.count, 1u)] = make_key(v, gid);
+        if (gid == 0) st.x0_nan = (v != v) ? 1 : 0;
+        if (have_lse && lse_m > -INFINITY) {
+            const double d = exp2(((double)v - (double)lse_m) * (double)lse_c) -
+                             exp2(((double)raw - (double)lse_m) * (double)lse_c);
+            atomicAdd(&st.lse_delta, d);
+        }
+    }
+    csync();
+}
+
+// f64 tail of sample_token (src/sample.cpp:52-101) over the sorted shortlist
+// cand[0..kk): softmax in shortlist order, nucleus prefix, inverse-CDF draw.
+// `prob` holds kk doubles of scratch.  Generic pointers: shared or global.
+__device__ void finalize_row(CandState& st, const uint64_t* cand, double* prob, uint32_t kk,
+                             const RowPlan& rp, bool x0_nan, bool have_lse, float lse_m,
+                             float lse_s, int row, uint64_t* rng, int32_t* out_ids,
+                             RowInfo* info, int32_t* cand_ids, double* cand_probs,
+                             int32_t cand_ld, int ctid) {
+    const Params& p = rp.p;
+    const float inv_t_lse = rp.greedy ? 1.0f : 1.0f / p.temp;
+    if (rp.greedy) {
+        if (ctid == 0) {
+            const int32_t id = (x0_nan || kk == 0) ? 0 : key_id(cand[0]);
+            if (out_ids) out_ids[row] = id;
+            if (info) {
+                RowInfo ri;
+                ri.max_logit = x0_nan ? __int_as_float(0x7fc00000) : (kk ? key_value(cand[0]) : 0.0f);
+                ri.k = 0;
+                ri.m = 0;
+                ri.pos = -1;
+                ri.r = 0.0;
+                ri.sum = 0.0;
+                ri.boundary = 0.0;
+                // relative to the row's f32 max, which is the greedy pick
+                ri.log_z = (have_lse && !x0_nan)
+                               ? log((double)lse_s) + ((double)lse_m - (double)ri.max_logit) * (double)inv_t_lse
+                               : __longlong_as_double(0x7ff8000000000000ll);
+                info[row] = ri;
+            }
+        }
+        csync();
+        return;
+    }
+    const float inv_temp = 1.0f / p.temp;
+    const float max_l = (x0_nan || kk == 0) ? __int_as_float(0x7fc00000) : key_value(cand[0]);
+    for (uint32_t i = ctid; i < kk; i += kNC)
+        prob[i] = exp(((double)key_value(cand[i]) - (double)max_l) * (double)inv_temp);
+    csync();
+    if (ctid == 0) {
+        double sum = 0.0;
+        for (uint32_t i = 0; i < kk; ++i) sum += prob[i];
+        st.d_sum = sum;
+    }
+    csync();
+    const double sum = st.d_sum;
+    for (uint32_t i = ctid; i < kk; i += kNC) {
+        const double pi = prob[i] / sum;
+        prob[i] = pi;
+        if ((int32_t)i < cand_ld) {
+            if (cand_ids) cand_ids[(int64_t)row * cand_ld + i] = key_id(cand[i]);
+            if (cand_probs) cand_probs[(int64_t)row * cand_ld + i] = pi;
+        }
+    }
+    csync();
+    const bool nucleus = p.top_p < 1.0f;
+    if (ctid == 0) {
+        int m = (int)kk;
+        double rescale = 1.0;
+        if (nucleus) {
+            double acc = 0.0;
+            m = 0;
+            while (m < (int)kk && acc < (double)p.top_p) {
+                acc += prob[m];
+                ++m;
+            }
+            if (m == 0) m = 1;
+            rescale = 0.0;
+            for (int i = 0; i < m; ++i) rescale += prob[i];
+        }
+        st.m = m;
+        st.d_rescale = rescale;
+    }
+    csync();
+    const int m = st.m;
+    if (nucleus) {
+        const double rs = st.d_rescale;
+        for (int i = ctid; i < m; i += kNC) prob[i] /= rs;
+        csync();
+    }
+    if (ctid == 0) {
+        uint64_t s = rng[row];
+        const double r = rng_uniform(s);
+        rng[row] = s;
+        double acc = 0.0, prev = 0.0;
+        int pos = m - 1;
+        bool hit = false;
+        for (int i = 0; i < m; ++i) {
+            prev = acc;
+            acc += prob[i];
+            if (r < acc) {
+                pos = i;
+                hit = true;
+                break;
+            }
+        }
+        double d;
+        if (hit) {
+            const double da = r - prev, db = acc - r;
+            d = da < db ? da : db;
+        } else {
+            d = r - acc;
+        }
+        if (out_ids) out_ids[row] = (kk == 0) ? 0 : key_id(cand[pos < 0 ? 0 : pos]);
+        if (info) {
+            RowInfo ri;
+            ri.max_logit = max_l;
+            ri.k = (int32_t)kk;
+            ri.m = m;
+            ri.pos = pos;
+            ri.r = r;
+            ri.sum = sum;
+            ri.boundary = d;
+            ri.log_z = (have_lse && !x0_nan)
+                           ? log((double)lse_s) + ((double)lse_m - (double)max_l) * (double)inv_temp
+                           : __longlong_as_double(0x7ff8000000000000ll);
+            info[row] = ri;
+        }
+    }
+    csync();
+}
+
+// Streams the keys of partial blocks through the threshold filter and leaves
+// the exact top-ksel, sorted, in st.cand[0..kk).  Also merges the partials'
+// sum-exp scalars and id-0 flags.  Returns kk.
+__device__ uint32_t merge_partials(CandState& st, const uint8_t* base, int64_t rank_stride,
+                                   int G, int S, int64_t part_stride, int row, uint32_t ksel,
+                                   float lse_c, bool& x0_nan, float& lse_m, float& lse_s,
+                                   int ctid) {
+    const int lane = ctid & 31;
+    if (ctid == 0) st.count = 0u;
+    csync();
+    uint64_t tau = 0ull;
+    float M = -INFINITY, Sx = 0.0f;
+    bool nan0 = false;
+    for (int g = 0; g < G; ++g) {
+        for (int s = 0; s < S; ++s) {
+            const uint8_t* pp = base + (int64_t)g * rank_stride + ((int64_t)row * S + s) * part_stride;
+            const uint4 hv = __ldcg(reinterpret_cast<const uint4*>(pp));
+            const uint32_t cnt = hv.x, flags = hv.y;
+            lse_merge(M, Sx, __uint_as_float(hv.z), __uint_as_float(hv.w), lse_c);
+            if ((flags & kPartHasId0) && (flags & kPartX0Nan)) nan0 = true;
+            const unsigned long long* keys =
+                reinterpret_cast<const unsigned long long*>(pp + kPartialHeaderBytes);
+            for (uint32_t b = 0; b < cnt; b += kNC) {
+                // Partial keys are sorted: stop at the first chunk that cannot pass.
+                if (__ldcg(keys + b) <= tau) break;
+                if (st.count + kNC + kCandMargin > (uint32_t)kCandCap) {
+                    tau = compact_top(st, st.count, ksel, kSlackKeep, ctid);
+                }
+                const uint32_t i = b + ctid;
+                const uint64_t k = (i < cnt) ? __ldcg(keys + i) : 0ull;
+                warp_append(st, k > tau, k, lane);
+                csync();
+            }
+        }
+    }
+    uint32_t n = st.count;
+    if (n > ksel) {
+        compact_top(st, n, ksel, kSlackKeep, ctid);
+        n = st.count;
+    }
+    sort_desc(st, n, ctid);
+    x0_nan = nan0;
+    lse_m = M;
+    lse_s = Sx;
+    return n < ksel ? n : ksel;
+}
+
+// ---------------------------------------------------------------------------
+// The streaming kernel
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ void set_status(int* status, int code) {
+    if (status) atomicExch(status, code);
+}
+
+__device__ void producer_loop(FastSmem& sm, const Args& a) {
+    const uint64_t pol = l2_evict_first_policy();
+    int stage = 0;
+    uint32_t eparity = 1u;  // fresh barriers: the phase "before" completes immediately
+    uint32_t pending = 0u;  // stages with a copy issued whose completion we have not seen
+    uint32_t pend_parity = 0u;
+    bool ok = true;
+    for (int u = blockIdx.x; u < a.n_units && ok; u += gridDim.x) {
+        const int row = u / a.S;
+        const RowPlan rp = plan_row(load_params(a.row_params, a.shared, row), a.V_total, a.hist,
+                                    a.hist_len, a.hist_ld, row);
+        if (!rp.fast) continue;
+        const UnitGeom g = unit_geom(a, u);
+        const int span = g.e1 - g.e0;
+        const int ntiles = span > 0 ? (span + kTileElems - 1) / kTileElems : 0;
+        const float* src_row = a.logits + (int64_t)row * a.ld;
+        int t = 0;
+        do {
+            if (!mbar_wait_bounded(&sm.empty[stage], eparity)) {
+                ok = false;
+                break;
+            }
+            const int start = g.e0 + t * kTileElems;
+            const int n = ntiles ? min(kTileElems, g.e1 - start) : 0;
+            StageMeta md;
+            md.unit = u;
+            md.start = start;
+            md.n = n;
+            md.flags = (t == 0 ? kMetaFirst : 0) | (t >= ntiles - 1 ? kMetaLast : 0);
+            sm.meta[stage] = md;
+            if (n > 0) {
+                mbar_arrive_expect_tx(&sm.full[stage], (uint32_t)n * 4u);
+                bulk_load(sm.ring[stage], src_row + start, (uint32_t)n * 4u, &sm.full[stage], pol);
+                pending |= 1u << stage;
+                // this use of the stage completes full-barrier phase parity (eparity ^ 1)
+                if (eparity) pend_parity &= ~(1u << stage);
+                else pend_parity |= 1u << stage;
+            } else {
+                pending &= ~(1u << stage);
+                mbar_arrive(&sm.full[stage]);
+            }
+            if (++stage == kStages) {
+                stage = 0;
+                eparity ^= 1u;
+            }
+        } while (++t < ntiles);
+    }
+    if (ok && mbar_wait_bounded(&sm.empty[stage], eparity)) {
+        StageMeta md;
+        md.unit = -1;
+        md.start = 0;
+        md.n = 0;
+        md.flags = kMetaDone;
+        sm.meta[stage] = md;
+        // The copy this stage held before was consumed (its empty phase completed).
+        pending &= ~(1u << stage);
+        mbar_arrive(&sm.full[stage]);
+    } else {
+        // The consumers notice on their own: their next bounded wait runs out.
+        set_status(a.status, kStatusTimeout);
+    }
+    // Leave no bulk copy in flight behind us.
+    for (int s = 0; s < kStages; ++s)
+        if (pending & (1u << s)) mbar_wait_bounded(&sm.full[s], (pend_parity >> s) & 1u);
+}
+
+template <bool LSE>
+__device__ void end_unit(FastSmem& sm, const Args& a, const RowPlan& rp, const UnitGeom& g,
+                         float lm, float ls, float lc, int ctid) {
+    CandState& st = sm.st;
+    uint32_t n = st.count;
+    if (n > (uint32_t)rp.keff) {
+        compact_top(st, n, (uint32_t)rp.keff, kSlackKeep, ctid);
+        n = st.count;
+    }
+    const float* row_logits = a.logits + (int64_t)g.row * a.ld;
+    float M = -INFINITY, Sx = 0.0f;
+    if (LSE) {
+        block_lse(st, lm, ls, lc, ctid);
+        M = st.lse_m;
+        Sx = st.lse_s;
+    }
+    uint32_t removed = 0;
+    if (rp.penal) {
+        const int32_t* window = a.hist + (int64_t)g.row * a.hist_ld + (rp.hist_len - rp.win);
+        penalty_fixup(st, row_logits, window, rp.win, rp.p.repeat_penalty, a.id_offset, g.v0,
+                      g.v1, a.V_total, n, LSE, M, lc, ctid);
+        n = st.count;
+        removed = st.removed;
+        if (LSE) Sx = (float)((double)Sx + st.lse_delta);
+    }
+    sort_desc(st, n, ctid);
+    const uint32_t valid = n - removed;
+    const uint32_t kk = valid < (uint32_t)rp.ksel ? valid : (uint32_t)rp.ksel;
+    const bool x0n = st.x0_nan != 0;
+    if (a.mode == 0 && a.S == 1) {
+        finalize_row(st, st.cand, reinterpret_cast<double*>(st.cand + kProbOffset), kk, rp, x0n,
+                     LSE, M, Sx, g.row, a.rng, a.out_ids, a.info, a.cand_ids, a.cand_probs,
+                     a.cand_ld, ctid);
+    } else {
+        uint8_t* pp = a.part + ((int64_t)g.row * a.S + g.s) * a.part_stride;
+        uint64_t* keys = reinterpret_cast<uint64_t*>(pp + kPartialHeaderBytes);
+        for (uint32_t i = ctid; i < kk; i += kNC) keys[i] = st.cand[i];
+        if (ctid == 0) {
+            const bool has0 = (a.id_offset + g.v0 == 0) && (g.v1 > g.v0);
+            uint4 hv;
+            hv.x = kk;
+            hv.y = (has0 ? kPartHasId0 : 0u) | ((has0 && x0n) ? kPartX0Nan : 0u);
+            hv.z = __float_as_uint(M);
+            hv.w = __float_as_uint(Sx);
+            *reinterpret_cast<uint4*>(pp) = hv;
+        }
+        if (a.mode == 0) {
+            __threadfence();
+            csync();
+            if (ctid == 0) st.is_last = (atomicAdd(&a.row_cnt[g.row], 1u) == (unsigned)(a.S - 1)) ? 1 : 0;
+            csync();
+            if (st.is_last) {
+                __threadfence();
+                bool x0m;
+                float mm, ss;
+                const uint32_t kf = merge_partials(st, a.part, 0, 1, a.S, a.part_stride, g.row,
+                                                   (uint32_t)rp.ksel, lc, x0m, mm, ss, ctid);
+                finalize_row(st, st.cand, reinterpret_cast<double*>(st.cand + kProbOffset), kf,
+                             rp, x0m, LSE, mm, ss, g.row, a.rng, a.out_ids, a.info, a.cand_ids,
+                             a.cand_probs, a.cand_ld, ctid);
+                if (ctid == 0) a.row_cnt[g.row] = 0u;
+            }
+        }
+    }
+    csync();
+    if (ctid == 0) {
+        st.count = 0u;
+        st.x0_nan = 0;
+    }
+}
+
+template <bool LSE>
+__device__ void consumer_loop(FastSmem& sm, const Args& a, int ctid) {
+    CandState& st = sm.st;
+    const int lane = ctid & 31, warp = ctid >> 5;
+    int stage = 0;
+    uint32_t fparity = 0u;
+    uint64_t tau_key = 0ull;
+    float tau_f = -INFINITY;
+    float lm = -INFINITY, ls = 0.0f, lc = 1.4426950408889634f;
+    uint32_t compact_at = (uint32_t)(kCandCap - kTileElems - kCandMargin);
+    RowPlan rp;
+    UnitGeom g;
+    rp.fast = false;
+    g.row = 0;
+    if (!mbar_wait_bounded(&sm.full[stage], fparity)) *(volatile int32_t*)&st.abort = 1;
+    csync();
+    for (;;) {
+        if (*(volatile int32_t*)&st.abort) break;
+        mbar_try_wait(&sm.full[stage], fparity);  // acquire for this thread (phase is complete)
+        const StageMeta md = sm.meta[stage];
+        if (md.flags & kMetaDone) break;
+        const float* row_logits;
+        if (md.flags & kMetaFirst) {
+            g = unit_geom(a, md.unit);
+            rp = plan_row(load_params(a.row_params, a.shared, g.row), a.V_total, a.hist,
+                          a.hist_len, a.hist_ld, g.row);
+            tau_key = 0ull;
+            tau_f = -INFINITY;
+            lm = -INFINITY;
+            ls = 0.0f;
+            lc = (rp.greedy ? 1.0f : 1.0f / rp.p.temp) * 1.4426950408889634f;
+            compact_at = min((uint32_t)(kCandCap - kTileElems - kCandMargin),
+                             (uint32_t)(rp.keff + max(rp.keff, kCompactMinGrowth)));
+            row_logits = a.logits + (int64_t)g.row * a.ld;
+            for (int i = g.v0 + ctid; i < g.e0; i += kNC) {
+                const float x = row_logits[i];
+                if (LSE) lse_add1(lm, ls, x, lc);
+                single_append(st, x, a.id_offset + i, tau_key);
+            }
+            if (ctid == 0 && a.id_offset + g.v0 == 0 && g.v1 > g.v0) {
+                const float x0 = row_logits[0];
+                st.x0_nan = (x0 != x0) ? 1 : 0;
+            }
+        }
+        row_logits = a.logits + (int64_t)g.row * a.ld;
+        {
+            const float4* t4 = reinterpret_cast<const float4*>(sm.ring[stage]);
+            const int n4 = md.n >> 2;
+            const int gid0 = a.id_offset + md.start;
+            for (int base = warp * 32; base < n4; base += kNC) {
+                const int j = base + lane;
+                const bool valid = j < n4;
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (valid) v = t4[j];
+                const float vm = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
+                const bool hit = valid && !(vm < tau_f);
+                if (LSE && valid) lse_add4(lm, ls, v, vm, lc);
+                if (__any_sync(kFull, hit)) append4(st, hit, v, gid0 + 4 * j, tau_key, lane);
+            }
+        }
+        const bool last = (md.flags & kMetaLast) != 0;
+        if (last) {
+            for (int i = g.e1 + ctid; i < g.v1; i += kNC) {
+                const float x = row_logits[i];
+                if (LSE) lse_add1(lm, ls, x, lc);
+                single_append(st, x, a.id_offset + i, tau_key);
+            }
+        }
+        const int prev = stage;
+        if (++stage == kStages) {
+            stage = 0;
+            fparity ^= 1u;
+        }
+        csync();  // every consumer is done with ring[prev]; all appends are visible
+        if (ctid == 0) mbar_arrive(&sm.empty[prev]);
+        if (last) {
+            end_unit<LSE>(sm, a, rp, g, lm, ls, lc, ctid);
+            tau_key = 0ull;
+            tau_f = -INFINITY;
+        } else if (st.count >= compact_at) {
+            tau_key = compact_top(st, st.count, (uint32_t)rp.keff, kSlackKeep, ctid);
+            tau_f = tau_value(tau_key);
+        }
+        if (!mbar_wait_bounded(&sm.full[stage], fparity)) {
+            *(volatile int32_t*)&st.abort = 1;
+            set_status(a.status, kStatusTimeout);
+        }
+        csync();
+    }
+}
+
+template <bool LSE>
+__global__ void __launch_bounds__(kThreads, 2) zs_select_kernel(const Args a) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    FastSmem& sm = *reinterpret_cast<FastSmem*>(smem_raw);
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&sm.full[s], 1);
+            mbar_init(&sm.empty[s], 1);
+        }
+        mbar_fence_init();
+        sm.st.count = 0u;
+        sm.st.abort = 0;
+        sm.st.x0_nan = 0;
+    }
+    __syncthreads();
+    if (tid >= kNC) {
+        if (tid == kNC) producer_loop(sm, a);
+        return;
+    }
+    consumer_loop<LSE>(sm, a, tid);
+}
+
+// Merge of gathered partial blocks (vocab shard): one CTA per row at a time.
+template <bool LSE>
+__global__ void __launch_bounds__(kNC) zs_merge_kernel(const MergeArgs a) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    CandState& st = *reinterpret_cast<CandState*>(smem_raw);
+    const int ctid = threadIdx.x;
+    for (int row = blockIdx.x; row < a.B; row += gridDim.x) {
+        const RowPlan rp = plan_row(load_params(a.row_params, a.shared, row), a.V_total, nullptr,
+                                    nullptr, 0, row);
+        const float lc = (rp.greedy ? 1.0f : 1.0f / rp.p.temp) * 1.4426950408889634f;
+        bool x0n;
+        float mm, ss;
+        const uint32_t kk = merge_partials(st, a.gathered, a.rank_stride, a.G, a.S, a.part_stride,
+                                           row, (uint32_t)rp.ksel, lc, x0n, mm, ss, ctid);
+        finalize_row(st, st.cand, reinterpret_cast<double*>(st.cand + kProbOffset), kk, rp, x0n,
+                     LSE, mm, ss, row, a.rng, a.out_ids, a.info, a.cand_ids, a.cand_probs,
+                     a.cand_ld, ctid);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Large-shortlist path: rows whose top-k + penalty window exceeds the shared
+// candidate buffer (top_k > 2048, or very long penalty windows).  One CTA per
+// row at a time with global scratch per CTA: keys[V], tmp[V] (u64) and
+// prob[V] (f64).  Exact: penalised keys -> radix-select threshold -> ordered
+// compaction -> stable LSD radix sort (8-bit digits, descending) -> f64 tail.
+// ---------------------------------------------------------------------------
+
+// k-th largest of src[0..n) (n > kk >= 1), radix select over 8-bit digits.
+__device__ uint64_t select_threshold_global(CandState& st, const uint64_t* src, uint32_t n,
+                                            uint32_t kk, int ctid) {
+    uint64_t prefix = 0, mask = 0;
+    uint32_t need = kk;
+    for (int shift = 56; shift >= 0; shift -= 8) {
+        st.hist[ctid] = 0u;
+        csync();
+        for (uint32_t i = ctid; i < n; i += kNC) {
+            const uint64_t k = src[i];
+            if ((k & mask) == prefix) atomicAdd(&st.hist[(uint32_t)(k >> shift) & 255u], 1u);
+        }
+        csync();
+        const uint32_t h = st.hist[255 - ctid];
+        uint32_t tot;
+        const uint32_t cum = block_incl_scan(h, st.scan, ctid, tot);
+        if (cum >= need && cum - h < need) {
+            st.sel_digit = 255u - (uint32_t)ctid;
+            st.sel_above = cum - h;
+            st.sel_cnt = h;
+        }
+        csync();
+        const uint32_t digit = st.sel_digit, above = st.sel_above, cnt = st.sel_cnt;
+        prefix |= (uint64_t)digit << shift;
+        mask |= 0xffull << shift;
+        need -= above;
+        csync();
+        if (cnt == need) break;
+    }
+    uint64_t mn = ~0ull;
+    for (uint32_t i = ctid; i < n; i += kNC) {
+        const uint64_t k = src[i];
+        if ((k & mask) == prefix && k < mn) mn = k;
+    }
+    mn = warp_min_u64(mn);
+    if ((ctid & 31) == 0) st.red64[ctid >> 5] = mn;
+    csync();
+    if (ctid == 0) {
+        uint64_t t = st.red64[0];
+        for (int w = 1; w < kConsumerWarps; ++w) t = st.red64[w] < t ? st.red64[w] : t;
+        st.thr = t;
+    }
+    csync();
+    return st.thr;
+}
+
+// Stable LSD radix sort of a[0..n) descending; b is scratch of n keys.  Eight
+// passes, so the result ends in a.  Per-warp digit counters live in wcnt.
+__device__ void radix_sort_desc_global(CandState& st, uint32_t* wcnt, uint64_t* a, uint64_t* b,
+                                       uint32_t n, int ctid) {
+    const int lane = ctid & 31, warp = ctid >> 5;
+    const uint32_t seg = ((n + kConsumerWarps - 1) / kConsumerWarps + 31) & ~31u;
+    const uint32_t w0 = min(n, (uint32_t)warp * seg), w1 = min(n, w0 + seg);
+    uint64_t* src = a;
+    uint64_t* dst = b;
+    for (int pass = 0; pass < 8; ++pass) {
+        const int shift = 8 * pass;
+        for (int i = ctid; i < kConsumerWarps * 256; i += kNC) wcnt[i] = 0u;
+        csync();
+        for (uint32_t i = w0 + lane; i < w1; i += 32) {
+            const uint32_t d = 255u - ((uint32_t)(src[i] >> shift) & 255u);
+            atomicAdd(&wcnt[warp * 256 + d], 1u);
+        }
+        csync();
+        uint32_t tot_d = 0;
+        for (int w = 0; w < kConsumerWarps; ++w) tot_d += wcnt[w * 256 + ctid];
+        uint32_t all;
+        uint32_t base = block_incl_scan(tot_d, st.scan, ctid, all) - tot_d;
+        for (int w = 0; w < kConsumerWarps; ++w) {
+            const uint32_t c = wcnt[w * 256 + ctid];
+            wcnt[w * 256 + ctid] = base;
+            base += c;
+        }
+        csync();
+        for (uint32_t c0 = w0; c0 < w1; c0 += 32) {
+            const uint32_t i = c0 + lane;
+            const bool valid = i < w1;
+            const uint64_t k = valid ? src[i] : 0ull;
+            const uint32_t d = valid ? 255u - ((uint32_t)(k >> shift) & 255u) : 256u + lane;
+            const unsigned peers = __match_any_sync(kFull, d);
+            const uint32_t rank = __popc(peers & lanemask_lt());
+            if (valid) dst[wcnt[warp * 256 + d] + rank] = k;
+            __syncwarp();
+            if (valid && rank == 0) wcnt[warp * 256 + d] += __popc(peers);
+            __syncwarp();
+        }
+        csync();
+        uint64_t* t = src;
+        src = dst;
+        dst = t;
+    }
+}
+
+template <bool LSE>
+__global__ void __launch_bounds__(kNC) zs_large_kernel(const Args a) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    CandState& st = *reinterpret_cast<CandState*>(smem_raw);
+    uint32_t* wcnt = reinterpret_cast<uint32_t*>(st.cand);  // 8 KB, cand is unused here
+    const int ctid = threadIdx.x;
+    uint8_t* ws = a.large_ws + (int64_t)blockIdx.x * a.large_ws_per_cta;
+    uint64_t* keys = reinterpret_cast<uint64_t*>(ws);
+    uint64_t* tmp = keys + a.V;
+    double* prob = reinterpret_cast<double*>(tmp + a.V);
+    for (int row = blockIdx.x; row < a.B; row += gridDim.x) {
+        const RowPlan rp = plan_row(load_params(a.row_params, a.shared, row), a.V_total, a.hist,
+                                    a.hist_len, a.hist_ld, row);
+        if (rp.fast) continue;
+        const float* x = a.logits + (int64_t)row * a.ld;
+        for (int i = ctid; i < a.V; i += kNC) keys[i] = make_key(x[i], a.id_offset + i);
+        __threadfence_block();
+        csync();
+        if (rp.penal && ctid == 0) {
+            // Sequential, in window order, exactly as src/sample.cpp:43-49.
+            const int32_t* w = a.hist + (int64_t)row * a.hist_ld + (rp.hist_len - rp.win);
+            const float pen = rp.p.repeat_penalty;
+            for (int j = 0; j < rp.win; ++j) {
+                const int32_t gid = w[j];
+                if (gid < 0 || gid >= a.V_total) continue;
+                const int32_t li = gid - a.id_offset;
+                if (li < 0 || li >= a.V) continue;
+                float v = key_value(keys[li]);
+                v = (v > 0.0f) ? v / pen : v * pen;
+                keys[li] = make_key(v, gid);
+            }
+        }
+        __threadfence_block();
+        csync();
+        const bool x0n = (a.id_offset == 0 && a.V > 0) ? ((uint32_t)(keys[0] >> 32) == 0u) : false;
+        const float lc = (rp.greedy ? 1.0f : 1.0f / rp.p.temp) * 1.4426950408889634f;
+        float M = -INFINITY, Sx = 0.0f;
+        if (LSE) {
+            float lm = -INFINITY, ls = 0.0f;
+            for (int i = ctid; i < a.V; i += kNC) lse_add1(lm, ls, key_value(keys[i]), lc);
+            block_lse(st, lm, ls, lc, ctid);
+            M = st.lse_m;
+            Sx = st.lse_s;
+        }
+        const uint32_t n = (uint32_t)a.V;
+        const uint32_t kk = (uint32_t)rp.ksel < n ? (uint32_t)rp.ksel : n;
+        uint64_t T = 0ull;
+        if (kk < n) T = select_threshold_global(st, keys, n, kk, ctid);
+        uint32_t base = 0;
+        for (uint32_t c0 = 0; c0 < n; c0 += kNC) {
+            const uint32_t i = c0 + ctid;
+            const uint64_t k = i < n ? keys[i] : 0ull;
+            const uint32_t f = (i < n && k >= T) ? 1u : 0u;
+            uint32_t tot;
+            const uint32_t incl = block_incl_scan(f, st.scan, ctid, tot);
+            if (f) tmp[base + incl - 1] = k;
+            base += tot;
+        }
+        __threadfence_block();
+        csync();
+        radix_sort_desc_global(st, wcnt, tmp, keys, kk, ctid);
+        __threadfence_block();
+        csync();
+        finalize_row(st, tmp, prob, kk, rp, x0n, LSE, M, Sx, row, a.rng, a.out_ids, a.info,
+                     a.cand_ids, a.cand_probs, a.cand_ld, ctid);
+        __threadfence_block();
+        csync();
+    }
+}
+
+}  // namespace zs

@@ -1,0 +1,566 @@
+// zs_sampler.cu -- host side of the C ABI in include/zs_sampler.h.
+//
+// Plans a batch (slices per row, scratch sizes, which rows need the large
+// shortlist path), owns the per-device scratch, and launches:
+//   zs_select_kernel  every row whose top-k + penalty window fits the shared
+//                     candidate buffer (all the reference's default shapes)
+//   zs_large_kernel   the remaining rows (top_k > 2048, long penalty windows)
+//   zs_merge_kernel   the vocab-sharded merge after the all-gather
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "zs_kernels.cuh"
+#include "zs_sampler.h"
+
+static_assert(sizeof(zs_params) == sizeof(zs::Params), "zs_params layout");
+static_assert(sizeof(zs_row_info) == sizeof(zs::RowInfo), "zs_row_info layout");
+static_assert(sizeof(zs_row_info) == 48, "zs_row_info size");
+
+namespace {
+
+thread_local std::string g_last_error;
+
+zs_status fail(zs_status s, const std::string& msg) {
+    g_last_error = msg;
+    return s;
+}
+
+zs_status cuda_fail(cudaError_t e, const char* what) {
+    g_last_error = std::string(what) + ": " + cudaGetErrorString(e);
+    return e == cudaErrorMemoryAllocation ? ZS_ERR_OUT_OF_MEMORY : ZS_ERR_CUDA;
+}
+
+#define ZS_CUDA(call)                                        \
+    do {                                                     \
+        cudaError_t e_ = (call);                             \
+        if (e_ != cudaSuccess) return cuda_fail(e_, #call);  \
+    } while (0)
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = false;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) == cudaSuccess && cudaSetDevice(dev) == cudaSuccess) ok = true;
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+constexpr int kShardLayoutCtas = 296;  // fixed, so every rank derives the same block layout
+
+struct Plan {
+    int S = 1;
+    int slice = 0;
+    int max_ksel = 1;
+    bool any_large = false;
+    bool any_penal = false;
+    int64_t part_stride = 0;
+};
+
+int ksel_of(const zs_params& p, int V_total) {
+    if (p.temp <= 0.0f) return 1;
+    if (p.top_k > 0) return std::min(p.top_k, V_total);
+    return std::min(zs::kShortlistDefault, V_total);
+}
+
+int win_bound_of(const zs_params& p) {
+    if (!(p.repeat_penalty != 1.0f)) return 0;
+    return std::max(0, p.repeat_last_n);
+}
+
+int choose_slices(int B, int V, int ctas) {
+    if (B <= 0 || V <= 0) return 1;
+    const int smax = std::max(1, V / (2 * zs::kTileElems));
+    const long want = (8L * ctas + B - 1) / B;
+    return (int)std::max(1L, std::min((long)smax, want));
+}
+
+Plan make_plan(int B, int V_cols, int V_total, const zs_params* params, int per_row, int ctas,
+               bool have_history) {
+    Plan pl;
+    const int np = per_row ? B : 1;
+    for (int i = 0; i < np; ++i) {
+        const zs_params& p = params[i];
+        const int ks = ksel_of(p, V_total);
+        const int wb = have_history ? win_bound_of(p) : 0;
+        pl.max_ksel = std::max(pl.max_ksel, ks);
+        if (wb > 0) pl.any_penal = true;
+        if ((long)ks + wb > zs::kKeffFastMax || wb > zs::kWinFastMax) pl.any_large = true;
+    }
+    pl.S = choose_slices(B, V_cols, ctas);
+    const int per = (V_cols + pl.S - 1) / pl.S;
+    pl.slice = std::max(4, (per + 3) & ~3);
+    pl.S = std::max(1, (V_cols + pl.slice - 1) / pl.slice);
+    pl.part_stride = ((int64_t)zs::kPartialHeaderBytes + 8LL * std::min(pl.max_ksel, zs::kKeffFastMax) + 15) & ~15LL;
+    return pl;
+}
+
+// ---- NCCL, resolved at run time from the libnccl.so.2 this process uses ----
+struct NcclApi {
+    typedef int (*AllGatherFn)(const void*, void*, size_t, int, void*, cudaStream_t);
+    typedef const char* (*ErrStrFn)(int);
+    AllGatherFn all_gather = nullptr;
+    ErrStrFn err_str = nullptr;
+    bool tried = false;
+};
+NcclApi g_nccl;
+std::mutex g_nccl_mu;
+
+bool load_nccl() {
+    std::lock_guard<std::mutex> lk(g_nccl_mu);
+    if (g_nccl.tried) return g_nccl.all_gather != nullptr;
+    g_nccl.tried = true;
+    void* lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!lib) lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!lib) return false;
+    g_nccl.all_gather = (NcclApi::AllGatherFn)dlsym(lib, "ncclAllGather");
+    g_nccl.err_str = (NcclApi::ErrStrFn)dlsym(lib, "ncclGetErrorString");
+    return g_nccl.all_gather != nullptr;
+}
+
+}  // namespace
+
+struct zs_context {
+    int device = 0;
+    int num_sms = 0;
+    int select_ctas_per_sm = 0;
+    int select_ctas = 0;
+    size_t select_smem = 0;
+    size_t merge_smem = 0;
+    // scratch, grown on demand (never shrinks)
+    uint8_t* part = nullptr;
+    size_t part_bytes = 0;
+    unsigned* row_cnt = nullptr;  // zeroed at allocation; kernels leave it zero
+    size_t row_cnt_n = 0;
+    int* status = nullptr;
+    zs::Params* params = nullptr;
+    size_t params_n = 0;
+    uint8_t* large = nullptr;
+    size_t large_bytes = 0;
+    uint8_t* gather = nullptr;  // zs_sample_sharded send + receive blocks
+    size_t gather_bytes = 0;
+};
+
+namespace {
+
+zs_status grow(void** p, size_t* have, size_t want) {
+    if (want <= *have) return ZS_OK;
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    *have = 0;
+    const size_t sz = std::max(want, (size_t)4096);
+    ZS_CUDA(cudaMalloc(p, sz));
+    *have = sz;
+    return ZS_OK;
+}
+
+zs_status ensure_row_cnt(zs_context* h, size_t n) {
+    if (n <= h->row_cnt_n) return ZS_OK;
+    if (h->row_cnt) cudaFree(h->row_cnt);
+    h->row_cnt = nullptr;
+    h->row_cnt_n = 0;
+    const size_t sz = std::max(n, (size_t)1024);
+    ZS_CUDA(cudaMalloc((void**)&h->row_cnt, sz * sizeof(unsigned)));
+    ZS_CUDA(cudaMemset(h->row_cnt, 0, sz * sizeof(unsigned)));
+    h->row_cnt_n = sz;
+    return ZS_OK;
+}
+
+zs_status validate_common(zs_handle h, const float* logits, int64_t ld, int32_t batch,
+                          int32_t n_vocab, const zs_params* params) {
+    if (!h) return fail(ZS_ERR_INVALID_ARGUMENT, "null handle");
+    if (batch < 0) return fail(ZS_ERR_INVALID_ARGUMENT, "batch < 0");
+    if (!params) return fail(ZS_ERR_INVALID_ARGUMENT, "params is null");
+    if (batch > 0 && n_vocab > 0) {
+        if (!logits) return fail(ZS_ERR_INVALID_ARGUMENT, "logits is null");
+        if (((uintptr_t)logits & 3u) != 0) return fail(ZS_ERR_INVALID_ARGUMENT, "logits not 4-byte aligned");
+        if (ld < n_vocab) return fail(ZS_ERR_INVALID_ARGUMENT, "ld < n_vocab");
+        if (batch > 1 && ld > (int64_t)1 << 40) return fail(ZS_ERR_INVALID_ARGUMENT, "ld too large");
+    }
+    return ZS_OK;
+}
+
+bool needs_rng(const zs_params* params, int per_row, int batch) {
+    const int np = per_row ? batch : 1;
+    for (int i = 0; i < np; ++i)
+        if (!(params[i].temp <= 0.0f)) return true;
+    return false;
+}
+
+zs_status upload_params(zs_context* h, const zs_params* params, int32_t per_row, int32_t batch,
+                        cudaStream_t st, const zs::Params** dev) {
+    *dev = nullptr;
+    if (!per_row) return ZS_OK;
+    if ((size_t)batch > h->params_n) {
+        if (h->params) cudaFree(h->params);
+        h->params = nullptr;
+        h->params_n = 0;
+        const size_t n = std::max((size_t)batch, (size_t)1024);
+        ZS_CUDA(cudaMalloc((void**)&h->params, n * sizeof(zs::Params)));
+        h->params_n = n;
+    }
+    ZS_CUDA(cudaMemcpyAsync(h->params, params, (size_t)batch * sizeof(zs::Params),
+                            cudaMemcpyHostToDevice, st));
+    *dev = h->params;
+    return ZS_OK;
+}
+
+zs::Params to_dev(const zs_params& p) {
+    zs::Params d;
+    std::memcpy(&d, &p, sizeof(d));
+    return d;
+}
+
+// Launches the select (and, when needed, large-path) kernels for one batch.
+zs_status launch_select(zs_context* h, const zs::Args& base, const Plan& pl, bool want_lse,
+                        cudaStream_t st) {
+    zs::Args a = base;
+    a.S = pl.S;
+    a.slice = pl.slice;
+    a.n_units = (int32_t)std::min<int64_t>((int64_t)a.B * pl.S, INT32_MAX);
+    a.part_stride = pl.part_stride;
+    a.status = h->status;
+    if (a.mode == 0 && pl.S > 1) {
+        zs_status s = grow((void**)&h->part, &h->part_bytes, (size_t)a.B * pl.S * pl.part_stride);
+        if (s != ZS_OK) return s;
+        s = ensure_row_cnt(h, (size_t)a.B);
+        if (s != ZS_OK) return s;
+        a.part = h->part;
+        a.row_cnt = h->row_cnt;
+    }
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(a.n_units, h->select_ctas));
+    if (want_lse)
+        zs::zs_select_kernel<true><<<grid, zs::kThreads, h->select_smem, st>>>(a);
+    else
+        zs::zs_select_kernel<false><<<grid, zs::kThreads, h->select_smem, st>>>(a);
+    ZS_CUDA(cudaGetLastError());
+    if (pl.any_large) {
+        if (a.mode != 0)
+            return fail(ZS_ERR_INVALID_ARGUMENT,
+                        "vocab-sharded sampling needs top_k + repeat window <= 2048");
+        const int lgrid = std::max(1, std::min(a.B, h->num_sms));
+        const int64_t per_cta = ((int64_t)a.V * 24 + 255) & ~255LL;
+        zs_status s = grow((void**)&h->large, &h->large_bytes, (size_t)per_cta * lgrid);
+        if (s != ZS_OK) return s;
+        a.large_ws = h->large;
+        a.large_ws_per_cta = per_cta;
+        if (want_lse)
+            zs::zs_large_kernel<true><<<lgrid, zs::kNC, h->merge_smem, st>>>(a);
+        else
+            zs::zs_large_kernel<false><<<lgrid, zs::kNC, h->merge_smem, st>>>(a);
+        ZS_CUDA(cudaGetLastError());
+    }
+    return ZS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int zs_abi_version(void) { return ZS_ABI_VERSION; }
+
+const char* zs_last_error(void) { return g_last_error.c_str(); }
+
+const char* zs_status_string(zs_status s) {
+    switch (s) {
+        case ZS_OK: return "ok";
+        case ZS_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case ZS_ERR_CUDA: return "CUDA error";
+        case ZS_ERR_NO_DEVICE: return "no sm_100 device";
+        case ZS_ERR_DEVICE_TIMEOUT: return "device wait timed out";
+        case ZS_ERR_NCCL: return "NCCL error";
+        case ZS_ERR_OUT_OF_MEMORY: return "out of device memory";
+    }
+    return "unknown status";
+}
+
+uint64_t zs_rng_seed(uint64_t seed) { return seed ? seed : 0x9E3779B97F4A7C15ull; }
+
+zs_status zs_create(int device, zs_handle* out) {
+    if (!out) return fail(ZS_ERR_INVALID_ARGUMENT, "out is null");
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0)
+        return fail(ZS_ERR_NO_DEVICE, "no CUDA device visible");
+    if (device < 0 || device >= n) return fail(ZS_ERR_INVALID_ARGUMENT, "device out of range");
+    cudaDeviceProp prop;
+    ZS_CUDA(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10) return fail(ZS_ERR_NO_DEVICE, std::string("not an sm_100 device: ") + prop.name);
+    DeviceGuard g(device);
+    if (!g.ok) return fail(ZS_ERR_CUDA, "cudaSetDevice failed");
+    zs_context* h = new zs_context();
+    h->device = device;
+    h->num_sms = prop.multiProcessorCount;
+    h->select_smem = sizeof(zs::FastSmem);
+    h->merge_smem = sizeof(zs::CandState);
+    auto cleanup = [&](zs_status s) {
+        delete h;
+        return s;
+    };
+    cudaError_t e;
+    if ((e = cudaFuncSetAttribute(zs::zs_select_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->select_smem)) != cudaSuccess ||
+        (e = cudaFuncSetAttribute(zs::zs_select_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->select_smem)) != cudaSuccess ||
+        (e = cudaFuncSetAttribute(zs::zs_merge_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->merge_smem)) != cudaSuccess ||
+        (e = cudaFuncSetAttribute(zs::zs_merge_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->merge_smem)) != cudaSuccess ||
+        (e = cudaFuncSetAttribute(zs::zs_large_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->merge_smem)) != cudaSuccess ||
+        (e = cudaFuncSetAttribute(zs::zs_large_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->merge_smem)) != cudaSuccess)
+        return cleanup(cuda_fail(e, "cudaFuncSetAttribute"));
+    int per_sm = 0;
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, zs::zs_select_kernel<false>, zs::kThreads, h->select_smem)) != cudaSuccess)
+        return cleanup(cuda_fail(e, "occupancy query"));
+    h->select_ctas_per_sm = std::max(1, per_sm);
+    h->select_ctas = h->select_ctas_per_sm * h->num_sms;
+    if ((e = cudaMalloc((void**)&h->status, sizeof(int))) != cudaSuccess) return cleanup(cuda_fail(e, "cudaMalloc status"));
+    if ((e = cudaMemset(h->status, 0, sizeof(int))) != cudaSuccess) return cleanup(cuda_fail(e, "cudaMemset status"));
+    *out = h;
+    return ZS_OK;
+}
+
+zs_status zs_destroy(zs_handle h) {
+    if (!h) return ZS_OK;
+    DeviceGuard g(h->device);
+    cudaFree(h->part);
+    cudaFree(h->row_cnt);
+    cudaFree(h->status);
+    cudaFree(h->params);
+    cudaFree(h->large);
+    cudaFree(h->gather);
+    delete h;
+    return ZS_OK;
+}
+
+zs_status zs_sample(zs_handle h, const float* logits, int64_t ld, int32_t batch, int32_t n_vocab,
+                    const zs_params* params, int32_t params_per_row, const int32_t* history,
+                    int64_t history_ld, const int32_t* history_len, uint64_t* rng_state,
+                    int32_t* out_ids, const zs_extras* extras, void* stream) {
+    zs_status s = validate_common(h, logits, ld, batch, n_vocab, params);
+    if (s != ZS_OK) return s;
+    if (batch == 0) return ZS_OK;
+    if (!out_ids) return fail(ZS_ERR_INVALID_ARGUMENT, "out_ids is null");
+    cudaStream_t st = (cudaStream_t)stream;
+    DeviceGuard g(h->device);
+    if (!g.ok) return fail(ZS_ERR_CUDA, "cudaSetDevice failed");
+    if (n_vocab <= 0) {  // sample.cpp:34 -- returns 0 before touching the Rng
+        ZS_CUDA(cudaMemsetAsync(out_ids, 0, (size_t)batch * sizeof(int32_t), st));
+        return ZS_OK;
+    }
+    if (!rng_state && needs_rng(params, params_per_row, batch))
+        return fail(ZS_ERR_INVALID_ARGUMENT, "rng_state is null");
+    const bool have_hist = history && history_len;
+    if (have_hist && history_ld < 0) return fail(ZS_ERR_INVALID_ARGUMENT, "history_ld < 0");
+    const zs::Params* dparams = nullptr;
+    s = upload_params(h, params, params_per_row, batch, st, &dparams);
+    if (s != ZS_OK) return s;
+    const Plan pl = make_plan(batch, n_vocab, n_vocab, params, params_per_row, h->select_ctas, have_hist);
+    zs::Args a;
+    std::memset(&a, 0, sizeof(a));
+    a.logits = logits;
+    a.ld = ld;
+    a.B = batch;
+    a.V = n_vocab;
+    a.id_offset = 0;
+    a.V_total = n_vocab;
+    a.shared = to_dev(params[0]);
+    a.row_params = dparams;
+    a.hist = have_hist ? history : nullptr;
+    a.hist_ld = history_ld;
+    a.hist_len = have_hist ? history_len : nullptr;
+    a.rng = rng_state;
+    a.out_ids = out_ids;
+    bool want_lse = false;
+    if (extras) {
+        a.info = reinterpret_cast<zs::RowInfo*>(extras->row_info);
+        a.cand_ids = extras->cand_ids;
+        a.cand_probs = extras->cand_probs;
+        a.cand_ld = (extras->cand_ids || extras->cand_probs) ? extras->cand_ld : 0;
+        if (a.cand_ld < 0) return fail(ZS_ERR_INVALID_ARGUMENT, "cand_ld < 0");
+        want_lse = extras->want_log_z && extras->row_info;
+    }
+    a.mode = 0;
+    return launch_select(h, a, pl, want_lse, st);
+}
+
+zs_status zs_argmax(zs_handle h, const float* logits, int64_t ld, int32_t batch, int32_t n_vocab,
+                    int32_t* out_ids, void* stream) {
+    zs_params p;
+    p.temp = 0.0f;
+    p.top_k = 0;
+    p.top_p = 1.0f;
+    p.repeat_penalty = 1.0f;
+    p.repeat_last_n = 64;
+    return zs_sample(h, logits, ld, batch, n_vocab, &p, 0, nullptr, 0, nullptr, nullptr, out_ids,
+                     nullptr, stream);
+}
+
+zs_status zs_check_device_status(zs_handle h, void* stream) {
+    if (!h) return fail(ZS_ERR_INVALID_ARGUMENT, "null handle");
+    DeviceGuard g(h->device);
+    int v = 0;
+    ZS_CUDA(cudaMemcpyAsync(&v, h->status, sizeof(int), cudaMemcpyDeviceToHost, (cudaStream_t)stream));
+    ZS_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+    if (v != 0) {
+        ZS_CUDA(cudaMemset(h->status, 0, sizeof(int)));
+        // An abandoned split-row merge can leave arrival counters behind.
+        if (h->row_cnt) ZS_CUDA(cudaMemset(h->row_cnt, 0, h->row_cnt_n * sizeof(unsigned)));
+        return fail(ZS_ERR_DEVICE_TIMEOUT, "a sampler kernel gave up on a bounded wait");
+    }
+    return ZS_OK;
+}
+
+zs_status zs_shard_partial_bytes(int32_t batch, int32_t n_vocab_total, int32_t n_ranks,
+                                 const zs_params* params, int32_t params_per_row,
+                                 int64_t* out_bytes) {
+    if (!out_bytes || !params || batch < 0 || n_vocab_total <= 0 || n_ranks <= 0)
+        return fail(ZS_ERR_INVALID_ARGUMENT, "bad shard layout arguments");
+    const int per_rank = (n_vocab_total + n_ranks - 1) / n_ranks;
+    const Plan pl = make_plan(batch, per_rank, n_vocab_total, params, params_per_row,
+                              kShardLayoutCtas, false);
+    *out_bytes = (int64_t)batch * pl.S * pl.part_stride;
+    return ZS_OK;
+}
+
+zs_status zs_shard_partials(zs_handle h, const float* logits_local, int64_t ld, int32_t batch,
+                            int32_t n_local, int32_t vocab_offset, int32_t n_vocab_total,
+                            int32_t n_ranks, const zs_params* params, int32_t params_per_row,
+                            const int32_t* history, int64_t history_ld,
+                            const int32_t* history_len, void* partial_out, int32_t want_log_z,
+                            void* stream) {
+    zs_status s = validate_common(h, logits_local, ld, batch, n_local, params);
+    if (s != ZS_OK) return s;
+    if (n_vocab_total <= 0 || n_ranks <= 0 || n_local < 0 || vocab_offset < 0 ||
+        (int64_t)vocab_offset + n_local > n_vocab_total)
+        return fail(ZS_ERR_INVALID_ARGUMENT, "bad shard geometry");
+    if (batch == 0) return ZS_OK;
+    if (!partial_out || ((uintptr_t)partial_out & 15u))
+        return fail(ZS_ERR_INVALID_ARGUMENT, "partial_out null or not 16-byte aligned");
+    cudaStream_t st = (cudaStream_t)stream;
+    DeviceGuard g(h->device);
+    if (!g.ok) return fail(ZS_ERR_CUDA, "cudaSetDevice failed");
+    const bool have_hist = history && history_len;
+    const zs::Params* dparams = nullptr;
+    s = upload_params(h, params, params_per_row, batch, st, &dparams);
+    if (s != ZS_OK) return s;
+    const int per_rank = (n_vocab_total + n_ranks - 1) / n_ranks;
+    Plan pl = make_plan(batch, per_rank, n_vocab_total, params, params_per_row, kShardLayoutCtas,
+                        have_hist);
+    if (pl.any_large)
+        return fail(ZS_ERR_INVALID_ARGUMENT, "vocab-sharded sampling needs top_k + repeat window <= 2048");
+    // Same S on every rank; this rank's slice length covers its own columns.
+    const int per = (std::max(n_local, 1) + pl.S - 1) / pl.S;
+    pl.slice = std::max(4, (per + 3) & ~3);
+    zs::Args a;
+    std::memset(&a, 0, sizeof(a));
+    a.logits = logits_local;
+    a.ld = ld;
+    a.B = batch;
+    a.V = std::max(n_local, 0);
+    a.id_offset = vocab_offset;
+    a.V_total = n_vocab_total;
+    a.shared = to_dev(params[0]);
+    a.row_params = dparams;
+    a.hist = have_hist ? history : nullptr;
+    a.hist_ld = history_ld;
+    a.hist_len = have_hist ? history_len : nullptr;
+    a.mode = 1;
+    a.part = (uint8_t*)partial_out;
+    // unit_geom needs a valid base address even for an empty shard
+    if (n_local <= 0) a.logits = (const float*)partial_out;
+    return launch_select(h, a, pl, want_log_z != 0, st);
+}
+
+zs_status zs_shard_merge(zs_handle h, const void* gathered, int32_t n_ranks, int32_t batch,
+                         int32_t n_vocab_total, const zs_params* params, int32_t params_per_row,
+                         uint64_t* rng_state, int32_t* out_ids, const zs_extras* extras,
+                         void* stream) {
+    if (!h || !params || n_ranks <= 0 || batch < 0 || n_vocab_total <= 0)
+        return fail(ZS_ERR_INVALID_ARGUMENT, "bad merge arguments");
+    if (batch == 0) return ZS_OK;
+    if (!gathered || !out_ids) return fail(ZS_ERR_INVALID_ARGUMENT, "null buffer");
+    if (!rng_state && needs_rng(params, params_per_row, batch))
+        return fail(ZS_ERR_INVALID_ARGUMENT, "rng_state is null");
+    cudaStream_t st = (cudaStream_t)stream;
+    DeviceGuard g(h->device);
+    if (!g.ok) return fail(ZS_ERR_CUDA, "cudaSetDevice failed");
+    const zs::Params* dparams = nullptr;
+    zs_status s = upload_params(h, params, params_per_row, batch, st, &dparams);
+    if (s != ZS_OK) return s;
+    const int per_rank = (n_vocab_total + n_ranks - 1) / n_ranks;
+    const Plan pl = make_plan(batch, per_rank, n_vocab_total, params, params_per_row,
+                              kShardLayoutCtas, false);
+    zs::MergeArgs m;
+    std::memset(&m, 0, sizeof(m));
+    m.gathered = (const uint8_t*)gathered;
+    m.rank_stride = (int64_t)batch * pl.S * pl.part_stride;
+    m.G = n_ranks;
+    m.S = pl.S;
+    m.part_stride = pl.part_stride;
+    m.B = batch;
+    m.V_total = n_vocab_total;
+    m.shared = to_dev(params[0]);
+    m.row_params = dparams;
+    m.rng = rng_state;
+    m.out_ids = out_ids;
+    m.status = h->status;
+    bool want_lse = false;
+    if (extras) {
+        m.info = reinterpret_cast<zs::RowInfo*>(extras->row_info);
+        m.cand_ids = extras->cand_ids;
+        m.cand_probs = extras->cand_probs;
+        m.cand_ld = (extras->cand_ids || extras->cand_probs) ? extras->cand_ld : 0;
+        want_lse = extras->want_log_z && extras->row_info;
+    }
+    const int grid = std::max(1, std::min(batch, 4 * h->num_sms));
+    if (want_lse)
+        zs::zs_merge_kernel<true><<<grid, zs::kNC, h->merge_smem, st>>>(m);
+    else
+        zs::zs_merge_kernel<false><<<grid, zs::kNC, h->merge_smem, st>>>(m);
+    ZS_CUDA(cudaGetLastError());
+    return ZS_OK;
+}
+
+zs_status zs_sample_sharded(zs_handle h, const float* logits_local, int64_t ld, int32_t batch,
+                            int32_t n_local, int32_t vocab_offset, int32_t n_vocab_total,
+                            int32_t n_ranks, const zs_params* params, int32_t params_per_row,
+                            const int32_t* history, int64_t history_ld,
+                            const int32_t* history_len, uint64_t* rng_state, int32_t* out_ids,
+                            const zs_extras* extras, void* nccl_comm, void* stream) {
+    if (!h || !nccl_comm) return fail(ZS_ERR_INVALID_ARGUMENT, "null handle or communicator");
+    if (!load_nccl()) return fail(ZS_ERR_NCCL, "libnccl.so.2 not loadable");
+    int64_t bytes = 0;
+    zs_status s = zs_shard_partial_bytes(batch, n_vocab_total, n_ranks, params, params_per_row, &bytes);
+    if (s != ZS_OK) return s;
+    if (batch == 0) return ZS_OK;
+    {
+        DeviceGuard g(h->device);
+        s = grow((void**)&h->gather, &h->gather_bytes, (size_t)bytes * (n_ranks + 1));
+        if (s != ZS_OK) return s;
+    }
+    uint8_t* send = h->gather;
+    uint8_t* recv = h->gather + bytes;
+    const bool want_lse = extras && extras->want_log_z && extras->row_info;
+    s = zs_shard_partials(h, logits_local, ld, batch, n_local, vocab_offset, n_vocab_total, n_ranks,
+                          params, params_per_row, history, history_ld, history_len, send,
+                          want_lse ? 1 : 0, stream);
+    if (s != ZS_OK) return s;
+    {
+        DeviceGuard g(h->device);
+        const int r = g_nccl.all_gather(send, recv, (size_t)bytes, /*ncclUint8*/ 1, nccl_comm,
+                                        (cudaStream_t)stream);
+        if (r != 0)
+            return fail(ZS_ERR_NCCL, std::string("ncclAllGather: ") +
+                                         (g_nccl.err_str ? g_nccl.err_str(r) : "error"));
+    }
+    return zs_shard_merge(h, recv, n_ranks, batch, n_vocab_total, params, params_per_row,
+                          rng_state, out_ids, extras, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,288 @@
+"""Python face of the B200 sampler: zeninfer's sample.h API plus a batched
+device API, both over the C ABI (include/zs_sampler.h).
+
+Reference interface (namespace zen, src/sample.h):
+    SamplingParams           src/sample.h:9-15
+    Rng (xorshift64*)        src/sample.h:18-26, src/sample.cpp:15-22
+    argmax_token             src/sample.h:28,    src/sample.cpp:24-30
+    sample_token             src/sample.h:36-37, src/sample.cpp:32-102
+
+argmax_token / sample_token take one host row, like the reference; Sampler
+takes [B, V] CUDA tensors and per-row xorshift64* states, stream-ordered.
+Torch provides device memory and streams; all compute is in libzs_sampler.so.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import threading
+from dataclasses import dataclass
+from typing import Optional, Sequence, Union
+
+import numpy as np
+
+from . import _native
+
+MASK64 = (1 << 64) - 1
+RNG_DEFAULT_SEED = 0x9E3779B97F4A7C15
+
+ROW_INFO_DTYPE = np.dtype([("max_logit", "<f4"), ("k", "<i4"), ("m", "<i4"), ("pos", "<i4"),
+                           ("r", "<f8"), ("sum", "<f8"), ("boundary", "<f8"), ("log_z", "<f8")])
+assert ROW_INFO_DTYPE.itemsize == 48
+
+
+@dataclass
+class SamplingParams:
+    """zen::SamplingParams (src/sample.h:9-15), same defaults."""
+    temp: float = 0.0            # <= 0 means greedy
+    top_k: int = 0               # 0 = disabled (256-token shortlist)
+    top_p: float = 1.0           # 1.0 = disabled
+    repeat_penalty: float = 1.0  # 1.0 = disabled
+    repeat_last_n: int = 64
+
+    def to_c(self) -> _native.ZsParams:
+        return _native.ZsParams(self.temp, int(self.top_k), self.top_p, self.repeat_penalty,
+                                int(self.repeat_last_n))
+
+
+class Rng:
+    """zen::Rng: xorshift64*, seed 0 replaced by 0x9E3779B97F4A7C15."""
+
+    def __init__(self, seed: int):
+        seed &= MASK64
+        self.state = seed if seed else RNG_DEFAULT_SEED
+
+    def next(self) -> int:
+        s = self.state
+        s ^= s >> 12
+        s ^= (s << 25) & MASK64
+        s ^= s >> 27
+        self.state = s
+        return (s * 2685821657736338717) & MASK64
+
+    def uniform(self) -> float:
+        return float(self.next() >> 11) * (1.0 / 9007199254740992.0)
+
+
+def rng_seed(seed: int) -> int:
+    """State that zen::Rng(seed) starts from."""
+    seed &= MASK64
+    return seed if seed else RNG_DEFAULT_SEED
+
+
+def states_to_tensor(states, device):
+    """uint64 states -> int64 CUDA tensor holding the same bits."""
+    import torch
+    arr = np.asarray(states, dtype=np.uint64).view(np.int64)
+    return torch.from_numpy(arr.copy()).to(device)
+
+
+def tensor_to_states(t) -> np.ndarray:
+    return t.detach().cpu().numpy().view(np.uint64)
+
+
+@dataclass
+class SampleResult:
+    ids: "object"                          # torch int32 [B]
+    row_info: Optional[np.ndarray] = None  # ROW_INFO_DTYPE [B] (host)
+    cand_ids: Optional["object"] = None    # torch int32 [B, cand_ld]
+    cand_probs: Optional["object"] = None  # torch float64 [B, cand_ld]
+
+
+def _params_array(params, batch):
+    if isinstance(params, SamplingParams):
+        return (_native.ZsParams * 1)(params.to_c()), 0
+    params = list(params)
+    if len(params) != batch:
+        raise ValueError("need one SamplingParams per row")
+    return (_native.ZsParams * batch)(*[p.to_c() for p in params]), 1
+
+
+def _stream_ptr(stream):
+    import torch
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return C.c_void_p(stream.cuda_stream)
+
+
+class Sampler:
+    """Batched device sampler bound to one CUDA device (a zs_handle)."""
+
+    def __init__(self, device: Union[int, str, None] = None):
+        import torch
+        if not torch.cuda.is_available():
+            raise RuntimeError("the B200 sampler needs a CUDA device")
+        dev = torch.device("cuda", torch.cuda.current_device() if device is None else
+                           torch.device(device).index if not isinstance(device, int) else device)
+        self.device = dev
+        self._lib = _native.lib()
+        h = C.c_void_p()
+        with torch.cuda.device(dev):
+            _native.check(self._lib.zs_create(dev.index, C.byref(h)), "zs_create")
+        self._h = h
+
+    def close(self) -> None:
+        if getattr(self, "_h", None) is not None and self._h.value:
+            self._lib.zs_destroy(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _extras(self, batch, row_info, cand_ld, want_log_z):
+        import torch
+        ex = _native.ZsExtras()
+        info_buf = cand_ids = cand_probs = None
+        if row_info or want_log_z:
+            info_buf = torch.zeros((batch, 48), dtype=torch.uint8, device=self.device)
+            ex.row_info = info_buf.data_ptr()
+        if cand_ld > 0:
+            cand_ids = torch.full((batch, cand_ld), -1, dtype=torch.int32, device=self.device)
+            cand_probs = torch.zeros((batch, cand_ld), dtype=torch.float64, device=self.device)
+            ex.cand_ids = cand_ids.data_ptr()
+            ex.cand_probs = cand_probs.data_ptr()
+            ex.cand_ld = cand_ld
+        ex.want_log_z = 1 if want_log_z else 0
+        return ex, info_buf, cand_ids, cand_probs
+
+    def sample(self, logits, params, rng_state=None, history=None, history_len=None, out=None,
+               row_info=False, cand_ld=0, want_log_z=False, stream=None,
+               sync_check=False) -> SampleResult:
+        """sample_token over every row of `logits` ([B, V] float32 CUDA, row stride
+        may exceed V).  rng_state: int64 CUDA [B] xorshift64* states, advanced in
+        place for non-greedy rows.  history: int32 CUDA [B, L] with lengths
+        history_len int32 CUDA [B]."""
+        import torch
+        if logits.dim() == 1:
+            logits = logits.unsqueeze(0)
+        if logits.dtype != torch.float32 or logits.device != self.device or logits.stride(1) != 1:
+            raise ValueError("logits must be float32, unit column stride, on the sampler's device")
+        B, V = logits.shape
+        par, per_row = _params_array(params, B)
+        if out is None:
+            out = torch.empty(B, dtype=torch.int32, device=self.device)
+        ex, info_buf, cand_ids, cand_probs = self._extras(B, row_info, cand_ld, want_log_z)
+        hist_ptr = hist_len_ptr = None
+        hist_ld = 0
+        if history is not None:
+            if history_len is None:
+                raise ValueError("history needs history_len")
+            history = history.to(torch.int32).contiguous()
+            history_len = history_len.to(torch.int32).contiguous()
+            hist_ptr, hist_len_ptr = history.data_ptr(), history_len.data_ptr()
+            hist_ld = history.shape[1] if history.dim() == 2 else 0
+        rng_ptr = rng_state.data_ptr() if rng_state is not None else None
+        st = _stream_ptr(stream)
+        _native.check(self._lib.zs_sample(self._h, logits.data_ptr(), logits.stride(0), B, V, par,
+                                          per_row, hist_ptr, hist_ld, hist_len_ptr, rng_ptr,
+                                          out.data_ptr(), C.byref(ex), st), "zs_sample")
+        if sync_check:
+            _native.check(self._lib.zs_check_device_status(self._h, st), "zs_sample (device)")
+        info = None
+        if info_buf is not None:
+            info = info_buf.cpu().numpy().view(ROW_INFO_DTYPE).reshape(B)
+        return SampleResult(out, info, cand_ids, cand_probs)
+
+    def argmax(self, logits, out=None, stream=None):
+        """argmax_token per row."""
+        import torch
+        if logits.dim() == 1:
+            logits = logits.unsqueeze(0)
+        B, V = logits.shape
+        if out is None:
+            out = torch.empty(B, dtype=torch.int32, device=self.device)
+        _native.check(self._lib.zs_argmax(self._h, logits.data_ptr(), logits.stride(0), B, V,
+                                          out.data_ptr(), _stream_ptr(stream)), "zs_argmax")
+        return out
+
+    def check_device_status(self, stream=None) -> None:
+        _native.check(self._lib.zs_check_device_status(self._h, _stream_ptr(stream)),
+                      "device status")
+
+    # ---- vocab-sharded mode ----
+    @staticmethod
+    def shard_partial_bytes(batch, n_vocab_total, n_ranks, params) -> int:
+        par, per_row = _params_array(params, batch)
+        out = C.c_int64()
+        _native.check(_native.lib().zs_shard_partial_bytes(batch, n_vocab_total, n_ranks, par,
+                                                           per_row, C.byref(out)),
+                      "zs_shard_partial_bytes")
+        return out.value
+
+    def shard_partials(self, logits_local, vocab_offset, n_vocab_total, n_ranks, params,
+                       partial_out, history=None, history_len=None, want_log_z=False,
+                       stream=None):
+        B, n_local = logits_local.shape
+        par, per_row = _params_array(params, B)
+        hist_ptr = history.data_ptr() if history is not None else None
+        hist_len_ptr = history_len.data_ptr() if history_len is not None else None
+        hist_ld = history.shape[1] if history is not None else 0
+        _native.check(self._lib.zs_shard_partials(
+            self._h, logits_local.data_ptr(), logits_local.stride(0), B, n_local, vocab_offset,
+            n_vocab_total, n_ranks, par, per_row, hist_ptr, hist_ld, hist_len_ptr,
+            partial_out.data_ptr(), 1 if want_log_z else 0, _stream_ptr(stream)),
+            "zs_shard_partials")
+
+    def shard_merge(self, gathered, n_ranks, batch, n_vocab_total, params, rng_state, out=None,
+                    row_info=False, cand_ld=0, want_log_z=False, stream=None) -> SampleResult:
+        import torch
+        par, per_row = _params_array(params, batch)
+        if out is None:
+            out = torch.empty(batch, dtype=torch.int32, device=self.device)
+        ex, info_buf, cand_ids, cand_probs = self._extras(batch, row_info, cand_ld, want_log_z)
+        _native.check(self._lib.zs_shard_merge(
+            self._h, gathered.data_ptr(), n_ranks, batch, n_vocab_total, par, per_row,
+            rng_state.data_ptr() if rng_state is not None else None, out.data_ptr(),
+            C.byref(ex), _stream_ptr(stream)), "zs_shard_merge")
+        info = None
+        if info_buf is not None:
+            info = info_buf.cpu().numpy().view(ROW_INFO_DTYPE).reshape(batch)
+        return SampleResult(out, info, cand_ids, cand_probs)
+
+
+# ---- the reference's host-row API ----
+_default = threading.local()
+
+
+def _default_sampler() -> Sampler:
+    s = getattr(_default, "sampler", None)
+    if s is None:
+        s = Sampler()
+        _default.sampler = s
+    return s
+
+
+def argmax_token(logits: Sequence[float], n: Optional[int] = None) -> int:
+    """argmax_token (src/sample.cpp:24-30) of one host row."""
+    import torch
+    x = np.ascontiguousarray(np.asarray(logits, dtype=np.float32).reshape(-1))
+    n = x.size if n is None else n
+    if n <= 0:
+        return 0
+    s = _default_sampler()
+    d = torch.from_numpy(x[:n].copy()).to(s.device)
+    return int(s.argmax(d.view(1, n)).item())
+
+
+def sample_token(logits: Sequence[float], n: Optional[int], params: SamplingParams,
+                 history: Sequence[int], rng: Rng) -> int:
+    """sample_token (src/sample.cpp:32-102) of one host row; rng advances like zen::Rng&."""
+    import torch
+    x = np.ascontiguousarray(np.asarray(logits, dtype=np.float32).reshape(-1))
+    n = x.size if n is None else n
+    if n <= 0:
+        return 0
+    s = _default_sampler()
+    d = torch.from_numpy(x[:n].copy()).to(s.device).view(1, n)
+    st = states_to_tensor([rng.state], s.device)
+    h = hl = None
+    hist = list(history)
+    if hist and params.repeat_penalty != 1.0:
+        h = torch.tensor([hist], dtype=torch.int32, device=s.device)
+        hl = torch.tensor([len(hist)], dtype=torch.int32, device=s.device)
+    res = s.sample(d, params, st, h, hl, sync_check=True)
+    rng.state = int(tensor_to_states(st)[0])
+    return int(res.ids.item())
