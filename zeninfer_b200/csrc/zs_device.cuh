@@ -121,8 +121,14 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
 }
 
 // Named barrier over the consumer warps only (the producer warp never joins).
+// bar.sync is the .aligned form: every lane of a warp must execute it together.
+// The compiler does not see inline asm as a barrier and does not reconverge a
+// warp before it, so __syncwarp() does that first; without it, lanes leaving a
+// divergent branch (or a bounded wait) at different times would arrive
+// separately and the barrier's count would go wrong.
 template <int NT>
 __device__ __forceinline__ void consumer_sync() {
+    __syncwarp();
     asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory");
 }
 

@@ -48,6 +48,22 @@ static_assert(kCandCap >= kKeffFastMax + kSlackKeep + kTileElems + kCandMargin,
 static_assert(kSortMax <= kCandCap, "sort region exceeds the candidate buffer");
 static_assert(kProbOffset + kKeffFastMax / 1 * 1 <= kCandCap, "probability region");
 
+// Bounds-checking build (-DZS_DEBUG_CHECKS): every candidate-buffer and partial
+// access is checked; the first violation (site, value, block) is recorded in
+// zs_debug_record and the access is skipped instead of faulting.
+#ifdef ZS_DEBUG_CHECKS
+__device__ unsigned long long zs_debug_record[4];
+#define ZS_CHECK(cond, site, val)                                                            \
+    ((cond) ? true                                                                           \
+            : (atomicCAS(&zs_debug_record[0], 0ull, (unsigned long long)(site)) == 0ull      \
+                   ? (zs_debug_record[1] = (unsigned long long)(val),                        \
+                      zs_debug_record[2] = (unsigned long long)blockIdx.x,                   \
+                      atomicAdd(&zs_debug_record[3], 1ull), false)                           \
+                   : (atomicAdd(&zs_debug_record[3], 1ull), false)))
+#else
+#define ZS_CHECK(cond, site, val) true
+#endif
+
 struct Params {  // zen::SamplingParams layout
     float temp;
     int32_t top_k;
@@ -109,10 +125,9 @@ struct Args {
     int32_t S;      // slices per row
     int32_t slice;  // columns per slice (multiple of 4)
     int32_t n_units;
-    int32_t mode;   // 0: draw here; 1: write partial blocks only (vocab shard)
+    int32_t mode;   // 0: draw here when S == 1; otherwise (or 1) write partial blocks
     uint8_t* part;  // partial blocks [B][S]
     int64_t part_stride;
-    unsigned* row_cnt;  // [B] arrival counters, zero between launches
     int* status;
     // large-k path workspace
     uint8_t* large_ws;
@@ -121,6 +136,10 @@ struct Args {
 
 struct MergeArgs {
     const uint8_t* gathered;
+    // history only to route rows the same way as the select kernel did
+    const int32_t* hist;
+    int64_t hist_ld;
+    const int32_t* hist_len;
     int64_t rank_stride;
     int32_t G;
     int32_t S;
@@ -214,6 +233,7 @@ struct CandState {
     int32_t win[kWinFastMax];
     uint64_t thr;
     uint64_t thr2;
+    uint4 part_hdr;
     double d_sum;
     double d_rescale;
     double lse_delta;
@@ -221,7 +241,6 @@ struct CandState {
     uint32_t removed;
     uint32_t sel_digit, sel_above, sel_cnt;
     int32_t abort;
-    int32_t is_last;
     int32_t x0_nan;
     int32_t m;
     float lse_m, lse_s;
@@ -292,7 +311,8 @@ __device__ __forceinline__ void warp_append(CandState& st, bool pred, uint64_t k
         uint32_t base = 0;
         if (lane == leader) base = atomicAdd(&st.count, (uint32_t)__popc(m));
         base = __shfl_sync(kFull, base, leader);
-        if (pred) st.cand[base + __popc(m & lanemask_lt())] = k;
+        const uint32_t at = base + __popc(m & lanemask_lt());
+        if (pred && ZS_CHECK(at < (uint32_t)kCandCap, 1, at)) st.cand[at] = k;
     }
 }
 
@@ -316,6 +336,7 @@ __device__ __forceinline__ void append4(CandState& st, bool hit, const float4& v
     if (lane == 31) base = atomicAdd(&st.count, total);
     base = __shfl_sync(kFull, base, 31);
     uint32_t pos = base + incl - c;
+    if (!ZS_CHECK(pos + c <= (uint32_t)kCandCap, 2, pos + c)) return;
     if (a0) st.cand[pos++] = k0;
     if (a1) st.cand[pos++] = k1;
     if (a2) st.cand[pos++] = k2;
@@ -326,7 +347,10 @@ __device__ __forceinline__ void append4(CandState& st, bool hit, const float4& v
 __device__ __forceinline__ void single_append(CandState& st, float x, int32_t id,
                                               uint64_t tau_key) {
     const uint64_t k = make_key(x, id);
-    if (k > tau_key) st.cand[atomicAdd(&st.count, 1u)] = k;
+    if (k > tau_key) {
+        const uint32_t at = atomicAdd(&st.count, 1u);
+        if (ZS_CHECK(at < (uint32_t)kCandCap, 3, at)) st.cand[at] = k;
+    }
 }
 
 // Online log-sum-exp in base 2: s = sum 2^((x - m) * c).
@@ -402,6 +426,7 @@ __device__ __forceinline__ float tau_value(uint64_t tau_key) {
 __device__ uint64_t compact_top(CandState& st, uint32_t n, uint32_t kk, uint32_t slack,
                                 int ctid) {
     const int lane = ctid & 31, warp = ctid >> 5;
+    if (!ZS_CHECK(n <= (uint32_t)kCandCap && n > kk, 6, ((uint64_t)n << 32) | kk)) n = min(n, (uint32_t)kCandCap);
     uint64_t lo = ~0ull, hi = 0ull;
     for (uint32_t i = ctid; i < n; i += kNC) {
         const uint64_t k = st.cand[i];
@@ -498,6 +523,7 @@ __device__ void sort_desc(CandState& st, uint32_t n, int ctid) {
     if (n <= 1) return;
     uint32_t N = 2;
     while (N < n) N <<= 1;
+    if (!ZS_CHECK(N <= (uint32_t)kCandCap, 5, N)) return;
     for (uint32_t i = n + ctid; i < N; i += kNC) st.cand[i] = 0ull;
     csync();
     for (uint32_t k = 2; k <= N; k <<= 1) {
@@ -561,7 +587,8 @@ __device__ void penalty_fixup(CandState& st, const float* row_logits, const int3
         const float raw = row_logits[gid - id_offset];
         float v = raw;
         for (int c = 0; c < mult; ++c) v = (v > 0.0f) ? v / pen : v * pen;
-        st.cand[atomicAdd(&st.count, 1u)] = make_key(v, gid);
+        const uint32_t at = atomicAdd(&st.count, 1u);
+        if (ZS_CHECK(at < (uint32_t)kCandCap, 4, at)) st.cand[at] = make_key(v, gid);
         if (gid == 0) st.x0_nan = (v != v) ? 1 : 0;
         if (have_lse && lse_m > -INFINITY) {
             const double d = exp2(((double)v - (double)lse_m) * (double)lse_c) -
@@ -605,6 +632,7 @@ __device__ void finalize_row(CandState& st, const uint64_t* cand, double* prob, 
         csync();
         return;
     }
+    ZS_CHECK(kk <= 2048u || prob != reinterpret_cast<double*>(st.cand + kProbOffset), 12, kk);
     const float inv_temp = 1.0f / p.temp;
     const float max_l = (x0_nan || kk == 0) ? __int_as_float(0x7fc00000) : key_value(cand[0]);
     for (uint32_t i = ctid; i < kk; i += kNC)
@@ -695,21 +723,31 @@ __device__ void finalize_row(CandState& st, const uint64_t* cand, double* prob, 
 
 // Streams the keys of partial blocks through the threshold filter and leaves
 // the exact top-ksel, sorted, in st.cand[0..kk).  Also merges the partials'
-// sum-exp scalars and id-0 flags.  Returns kk.
+// sum-exp scalars and id-0 flags.  Returns kk.  Runs in its own launch, after
+// every partial block is complete; each header is read once by thread 0 and
+// shared, so all threads take the same path.
 __device__ uint32_t merge_partials(CandState& st, const uint8_t* base, int64_t rank_stride,
                                    int G, int S, int64_t part_stride, int row, uint32_t ksel,
                                    float lse_c, bool& x0_nan, float& lse_m, float& lse_s,
                                    int ctid) {
     const int lane = ctid & 31;
+    const uint32_t cap = (uint32_t)((part_stride - kPartialHeaderBytes) / 8);
     if (ctid == 0) st.count = 0u;
-    csync();
     uint64_t tau = 0ull;
     float M = -INFINITY, Sx = 0.0f;
     bool nan0 = false;
     for (int g = 0; g < G; ++g) {
         for (int s = 0; s < S; ++s) {
             const uint8_t* pp = base + (int64_t)g * rank_stride + ((int64_t)row * S + s) * part_stride;
-            const uint4 hv = __ldcg(reinterpret_cast<const uint4*>(pp));
+            if (ctid == 0) {
+                uint4 hv = __ldcg(reinterpret_cast<const uint4*>(pp));
+                if (!ZS_CHECK(hv.x <= cap, 8, ((uint64_t)row << 32) | hv.x)) hv.x = 0u;
+                hv.x = hv.x < cap ? hv.x : cap;
+                st.part_hdr = hv;
+            }
+            csync();
+            const uint4 hv = st.part_hdr;
+            csync();
             const uint32_t cnt = hv.x, flags = hv.y;
             lse_merge(M, Sx, __uint_as_float(hv.z), __uint_as_float(hv.w), lse_c);
             if ((flags & kPartHasId0) && (flags & kPartX0Nan)) nan0 = true;
@@ -728,6 +766,7 @@ __device__ uint32_t merge_partials(CandState& st, const uint8_t* base, int64_t r
             }
         }
     }
+    csync();
     uint32_t n = st.count;
     if (n > ksel) {
         compact_top(st, n, ksel, kSlackKeep, ctid);
@@ -823,6 +862,7 @@ __device__ void end_unit(FastSmem& sm, const Args& a, const RowPlan& rp, const U
         compact_top(st, n, (uint32_t)rp.keff, kSlackKeep, ctid);
         n = st.count;
     }
+    ZS_CHECK(n <= (uint32_t)kCandCap, 9, n);
     const float* row_logits = a.logits + (int64_t)g.row * a.ld;
     float M = -INFINITY, Sx = 0.0f;
     if (LSE) {
@@ -850,7 +890,8 @@ __device__ void end_unit(FastSmem& sm, const Args& a, const RowPlan& rp, const U
     } else {
         uint8_t* pp = a.part + ((int64_t)g.row * a.S + g.s) * a.part_stride;
         uint64_t* keys = reinterpret_cast<uint64_t*>(pp + kPartialHeaderBytes);
-        for (uint32_t i = ctid; i < kk; i += kNC) keys[i] = st.cand[i];
+        ZS_CHECK(16 + 8 * (int64_t)kk <= a.part_stride && kk <= (uint32_t)rp.ksel, 7, kk);
+        for (uint32_t i = ctid; i < kk && 16 + 8 * (int64_t)(i + 1) <= a.part_stride; i += kNC) keys[i] = st.cand[i];
         if (ctid == 0) {
             const bool has0 = (a.id_offset + g.v0 == 0) && (g.v1 > g.v0);
             uint4 hv;
@@ -859,23 +900,6 @@ __device__ void end_unit(FastSmem& sm, const Args& a, const RowPlan& rp, const U
             hv.z = __float_as_uint(M);
             hv.w = __float_as_uint(Sx);
             *reinterpret_cast<uint4*>(pp) = hv;
-        }
-        if (a.mode == 0) {
-            __threadfence();
-            csync();
-            if (ctid == 0) st.is_last = (atomicAdd(&a.row_cnt[g.row], 1u) == (unsigned)(a.S - 1)) ? 1 : 0;
-            csync();
-            if (st.is_last) {
-                __threadfence();
-                bool x0m;
-                float mm, ss;
-                const uint32_t kf = merge_partials(st, a.part, 0, 1, a.S, a.part_stride, g.row,
-                                                   (uint32_t)rp.ksel, lc, x0m, mm, ss, ctid);
-                finalize_row(st, st.cand, reinterpret_cast<double*>(st.cand + kProbOffset), kf,
-                             rp, x0m, LSE, mm, ss, g.row, a.rng, a.out_ids, a.info, a.cand_ids,
-                             a.cand_probs, a.cand_ld, ctid);
-                if (ctid == 0) a.row_cnt[g.row] = 0u;
-            }
         }
     }
     csync();
@@ -930,6 +954,8 @@ __device__ void consumer_loop(FastSmem& sm, const Args& a, int ctid) {
             }
         }
         row_logits = a.logits + (int64_t)g.row * a.ld;
+        ZS_CHECK(md.n <= kTileElems && md.start >= 0 && md.start + md.n <= a.V, 10, ((uint64_t)md.start << 32) | (uint32_t)md.n);
+        ZS_CHECK(st.count + kTileElems + kCandMargin <= (uint32_t)kCandCap, 11, st.count);
         {
             const float4* t4 = reinterpret_cast<const float4*>(sm.ring[stage]);
             const int n4 = md.n >> 2;
@@ -1006,8 +1032,9 @@ __global__ void __launch_bounds__(kNC) zs_merge_kernel(const MergeArgs a) {
     CandState& st = *reinterpret_cast<CandState*>(smem_raw);
     const int ctid = threadIdx.x;
     for (int row = blockIdx.x; row < a.B; row += gridDim.x) {
-        const RowPlan rp = plan_row(load_params(a.row_params, a.shared, row), a.V_total, nullptr,
-                                    nullptr, 0, row);
+        const RowPlan rp = plan_row(load_params(a.row_params, a.shared, row), a.V_total, a.hist,
+                                    a.hist_len, a.hist_ld, row);
+        if (!rp.fast) continue;  // drawn by zs_large_kernel
         const float lc = (rp.greedy ? 1.0f : 1.0f / rp.p.temp) * 1.4426950408889634f;
         bool x0n;
         float mm, ss;

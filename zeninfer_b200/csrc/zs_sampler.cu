@@ -139,8 +139,6 @@ struct zs_context {
     // scratch, grown on demand (never shrinks)
     uint8_t* part = nullptr;
     size_t part_bytes = 0;
-    unsigned* row_cnt = nullptr;  // zeroed at allocation; kernels leave it zero
-    size_t row_cnt_n = 0;
     int* status = nullptr;
     zs::Params* params = nullptr;
     size_t params_n = 0;
@@ -160,18 +158,6 @@ zs_status grow(void** p, size_t* have, size_t want) {
     const size_t sz = std::max(want, (size_t)4096);
     ZS_CUDA(cudaMalloc(p, sz));
     *have = sz;
-    return ZS_OK;
-}
-
-zs_status ensure_row_cnt(zs_context* h, size_t n) {
-    if (n <= h->row_cnt_n) return ZS_OK;
-    if (h->row_cnt) cudaFree(h->row_cnt);
-    h->row_cnt = nullptr;
-    h->row_cnt_n = 0;
-    const size_t sz = std::max(n, (size_t)1024);
-    ZS_CUDA(cudaMalloc((void**)&h->row_cnt, sz * sizeof(unsigned)));
-    ZS_CUDA(cudaMemset(h->row_cnt, 0, sz * sizeof(unsigned)));
-    h->row_cnt_n = sz;
     return ZS_OK;
 }
 
@@ -220,7 +206,10 @@ zs::Params to_dev(const zs_params& p) {
     return d;
 }
 
-// Launches the select (and, when needed, large-path) kernels for one batch.
+// Launches the select kernel for one batch: rows with one slice are drawn in
+// place; rows cut into slices leave partial blocks that zs_merge_kernel merges
+// in a second launch.  Rows needing the large shortlist path follow in
+// zs_large_kernel.
 zs_status launch_select(zs_context* h, const zs::Args& base, const Plan& pl, bool want_lse,
                         cudaStream_t st) {
     zs::Args a = base;
@@ -229,13 +218,11 @@ zs_status launch_select(zs_context* h, const zs::Args& base, const Plan& pl, boo
     a.n_units = (int32_t)std::min<int64_t>((int64_t)a.B * pl.S, INT32_MAX);
     a.part_stride = pl.part_stride;
     a.status = h->status;
-    if (a.mode == 0 && pl.S > 1) {
+    const bool split = (a.mode == 0 && pl.S > 1);
+    if (split) {
         zs_status s = grow((void**)&h->part, &h->part_bytes, (size_t)a.B * pl.S * pl.part_stride);
         if (s != ZS_OK) return s;
-        s = ensure_row_cnt(h, (size_t)a.B);
-        if (s != ZS_OK) return s;
         a.part = h->part;
-        a.row_cnt = h->row_cnt;
     }
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(a.n_units, h->select_ctas));
     if (want_lse)
@@ -243,6 +230,35 @@ zs_status launch_select(zs_context* h, const zs::Args& base, const Plan& pl, boo
     else
         zs::zs_select_kernel<false><<<grid, zs::kThreads, h->select_smem, st>>>(a);
     ZS_CUDA(cudaGetLastError());
+    if (split) {
+        zs::MergeArgs m;
+        std::memset(&m, 0, sizeof(m));
+        m.gathered = a.part;
+        m.rank_stride = 0;
+        m.G = 1;
+        m.S = pl.S;
+        m.part_stride = pl.part_stride;
+        m.B = a.B;
+        m.V_total = a.V_total;
+        m.shared = a.shared;
+        m.row_params = a.row_params;
+        m.hist_len = a.hist_len;
+        m.hist_ld = a.hist_ld;
+        m.hist = a.hist;
+        m.rng = a.rng;
+        m.out_ids = a.out_ids;
+        m.info = a.info;
+        m.cand_ids = a.cand_ids;
+        m.cand_probs = a.cand_probs;
+        m.cand_ld = a.cand_ld;
+        m.status = h->status;
+        const int mgrid = std::max(1, std::min(a.B, 4 * h->num_sms));
+        if (want_lse)
+            zs::zs_merge_kernel<true><<<mgrid, zs::kNC, h->merge_smem, st>>>(m);
+        else
+            zs::zs_merge_kernel<false><<<mgrid, zs::kNC, h->merge_smem, st>>>(m);
+        ZS_CUDA(cudaGetLastError());
+    }
     if (pl.any_large) {
         if (a.mode != 0)
             return fail(ZS_ERR_INVALID_ARGUMENT,
@@ -329,7 +345,6 @@ zs_status zs_destroy(zs_handle h) {
     if (!h) return ZS_OK;
     DeviceGuard g(h->device);
     cudaFree(h->part);
-    cudaFree(h->row_cnt);
     cudaFree(h->status);
     cudaFree(h->params);
     cudaFree(h->large);
@@ -409,8 +424,6 @@ zs_status zs_check_device_status(zs_handle h, void* stream) {
     ZS_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
     if (v != 0) {
         ZS_CUDA(cudaMemset(h->status, 0, sizeof(int)));
-        // An abandoned split-row merge can leave arrival counters behind.
-        if (h->row_cnt) ZS_CUDA(cudaMemset(h->row_cnt, 0, h->row_cnt_n * sizeof(unsigned)));
         return fail(ZS_ERR_DEVICE_TIMEOUT, "a sampler kernel gave up on a bounded wait");
     }
     return ZS_OK;
@@ -562,5 +575,12 @@ zs_status zs_sample_sharded(zs_handle h, const float* logits_local, int64_t ld, 
     return zs_shard_merge(h, recv, n_ranks, batch, n_vocab_total, params, params_per_row,
                           rng_state, out_ids, extras, stream);
 }
+
+#ifdef ZS_DEBUG_CHECKS
+// Bounds-checking builds only: the first recorded violation {site, value, block, count}.
+int zs_debug_read(unsigned long long* out4) {
+    return (int)cudaMemcpyFromSymbol(out4, zs::zs_debug_record, 4 * sizeof(unsigned long long));
+}
+#endif
 
 }  // extern "C"
