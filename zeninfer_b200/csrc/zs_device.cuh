@@ -92,11 +92,26 @@ __device__ __forceinline__ uint64_t global_ns() {
 // ZS_ERR_DEVICE_TIMEOUT instead of spinning forever.
 constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s
 
-// Bounded wait for an mbarrier phase; false when the limit ran out.
+// try_wait that may suspend the thread for up to hint_ns before returning false.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity,
+                                                    uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for an mbarrier phase; false when the limit ran out.  Meant for
+// one thread per CTA (others sleep on a named barrier meanwhile).
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
-    while (!mbar_try_wait(bar, parity)) {
+    while (!mbar_try_wait_sleep(bar, parity, 20000u)) {
         if (global_ns() - t0 > kWaitLimitNs) return false;
     }
     return true;
@@ -130,6 +145,26 @@ template <int NT>
 __device__ __forceinline__ void consumer_sync() {
     __syncwarp();
     asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory");
+}
+
+// consumer_sync that also ORs a predicate over the consumer threads; every
+// thread gets the same result.  A decision taken from shared state that other
+// threads may still be changing (a counter that later appends bump) must come
+// through here, never from each thread reading the state on its own after a
+// plain barrier: fast threads would act on a value slow threads never see.
+template <int NT>
+__device__ __forceinline__ bool consumer_sync_or(bool pred) {
+    __syncwarp();
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 q, %1, 0;\n\t"
+        "bar.red.or.pred p, 1, %2, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(r)
+        : "r"((uint32_t)pred), "n"(NT)
+        : "memory");
+    return r != 0;
 }
 
 __device__ __forceinline__ unsigned lanemask_lt() {

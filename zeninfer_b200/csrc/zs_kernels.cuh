@@ -35,16 +35,23 @@ constexpr int kStages = 8;
 constexpr int kKeffFastMax = 2048;        // top-k + penalty window handled in shared memory
 constexpr int kWinFastMax = 512;          // penalty window handled in shared memory
 constexpr int kCandMargin = 16;           // head/tail elements appended outside the tile check
-constexpr int kSlackKeep = 64;            // a compaction may keep up to this many extra keys
+constexpr int kSlackMin = 64;             // a compaction may keep slack(K) extra keys: whole
+constexpr int kSlackMax = 1024;           // radix buckets (tie groups) instead of splitting them
 constexpr int kCompactMinGrowth = 512;    // compact once the buffer grew by max(K_eff, this)
-constexpr int kCandCap = 4224;            // >= kKeffFastMax + kSlackKeep + kTileElems + kCandMargin
+constexpr int kCandCap = 5136;            // >= kKeffFastMax + kSlackMax + kTileElems + kCandMargin
 constexpr int kCandRegs = (kCandCap + kNC - 1) / kNC;
 constexpr int kSortMax = 4096;            // bitonic size bound (kKeffFastMax + kWinFastMax -> 4096)
 constexpr int kProbOffset = 2048;         // f64 probabilities alias cand[2048..4096)
 constexpr int kShortlistDefault = 256;    // kTopPShortlist, src/sample.cpp:12
 
-static_assert(kCandCap >= kKeffFastMax + kSlackKeep + kTileElems + kCandMargin,
+static_assert(kCandCap >= kKeffFastMax + kSlackMax + kTileElems + kCandMargin,
               "candidate buffer too small");
+static_assert(kKeffFastMax + kSlackMax + kWinFastMax <= kSortMax, "sort bound");
+
+__host__ __device__ constexpr uint32_t slack_for(uint32_t k) {
+    return k / 2 < (uint32_t)kSlackMin ? (uint32_t)kSlackMin
+                                       : (k / 2 > (uint32_t)kSlackMax ? (uint32_t)kSlackMax : k / 2);
+}
 static_assert(kSortMax <= kCandCap, "sort region exceeds the candidate buffer");
 static_assert(kProbOffset + kKeffFastMax / 1 * 1 <= kCandCap, "probability region");
 
@@ -257,6 +264,7 @@ struct FastSmem {
 // ---- block primitives over the kNC consumer threads ----
 
 __device__ __forceinline__ void csync() { consumer_sync<kNC>(); }
+__device__ __forceinline__ bool csync_or(bool pred) { return consumer_sync_or<kNC>(pred); }
 
 // Inclusive scan across the consumer threads; ends synchronised.
 __device__ __forceinline__ uint32_t block_incl_scan(uint32_t v, uint32_t* s_scan, int ctid,
@@ -702,6 +710,7 @@ __device__ void finalize_row(CandState& st, const uint64_t* cand, double* prob, 
         } else {
             d = r - acc;
         }
+        ZS_CHECK(pos < (int)kk || kk == 0, 17, ((uint64_t)(uint32_t)pos << 32) | kk);
         if (out_ids) out_ids[row] = (kk == 0) ? 0 : key_id(cand[pos < 0 ? 0 : pos]);
         if (info) {
             RowInfo ri;
@@ -734,6 +743,7 @@ __device__ uint32_t merge_partials(CandState& st, const uint8_t* base, int64_t r
     const uint32_t cap = (uint32_t)((part_stride - kPartialHeaderBytes) / 8);
     if (ctid == 0) st.count = 0u;
     uint64_t tau = 0ull;
+    bool full = false;  // same on every thread: no room for another chunk
     float M = -INFINITY, Sx = 0.0f;
     bool nan0 = false;
     for (int g = 0; g < G; ++g) {
@@ -756,20 +766,19 @@ __device__ uint32_t merge_partials(CandState& st, const uint8_t* base, int64_t r
             for (uint32_t b = 0; b < cnt; b += kNC) {
                 // Partial keys are sorted: stop at the first chunk that cannot pass.
                 if (__ldcg(keys + b) <= tau) break;
-                if (st.count + kNC + kCandMargin > (uint32_t)kCandCap) {
-                    tau = compact_top(st, st.count, ksel, kSlackKeep, ctid);
-                }
+                if (full) tau = compact_top(st, st.count, ksel, slack_for(ksel), ctid);
                 const uint32_t i = b + ctid;
                 const uint64_t k = (i < cnt) ? __ldcg(keys + i) : 0ull;
                 warp_append(st, k > tau, k, lane);
-                csync();
+                // Each thread tests the count after its own append; the OR is exact.
+                full = csync_or(st.count + kNC + kCandMargin > (uint32_t)kCandCap);
             }
         }
     }
     csync();
     uint32_t n = st.count;
     if (n > ksel) {
-        compact_top(st, n, ksel, kSlackKeep, ctid);
+        compact_top(st, n, ksel, slack_for(ksel), ctid);
         n = st.count;
     }
     sort_desc(st, n, ctid);
@@ -859,7 +868,7 @@ __device__ void end_unit(FastSmem& sm, const Args& a, const RowPlan& rp, const U
     CandState& st = sm.st;
     uint32_t n = st.count;
     if (n > (uint32_t)rp.keff) {
-        compact_top(st, n, (uint32_t)rp.keff, kSlackKeep, ctid);
+        compact_top(st, n, (uint32_t)rp.keff, slack_for((uint32_t)rp.keff), ctid);
         n = st.count;
     }
     ZS_CHECK(n <= (uint32_t)kCandCap, 9, n);
@@ -888,6 +897,7 @@ __device__ void end_unit(FastSmem& sm, const Args& a, const RowPlan& rp, const U
                      LSE, M, Sx, g.row, a.rng, a.out_ids, a.info, a.cand_ids, a.cand_probs,
                      a.cand_ld, ctid);
     } else {
+        ZS_CHECK(g.row >= 0 && g.row < a.B && g.s >= 0 && g.s < a.S, 15, ((uint64_t)g.row << 32) | (uint32_t)g.s);
         uint8_t* pp = a.part + ((int64_t)g.row * a.S + g.s) * a.part_stride;
         uint64_t* keys = reinterpret_cast<uint64_t*>(pp + kPartialHeaderBytes);
         ZS_CHECK(16 + 8 * (int64_t)kk <= a.part_stride && kk <= (uint32_t)rp.ksel, 7, kk);
@@ -909,6 +919,47 @@ __device__ void end_unit(FastSmem& sm, const Args& a, const RowPlan& rp, const U
     }
 }
 
+// Filters the float4s at t4[j] and t4[j + kNC/...] of one ring stage.
+template <bool LSE>
+__device__ __forceinline__ void filter_tile(CandState& st, const float4* t4, int n4, int gid0,
+                                            uint64_t tau_key, float tau_f, float lc, float& lm,
+                                            float& ls, int lane, int warp) {
+    // Two float4 per thread per step: j and j + kNC.
+    for (int base = warp * 32; base < n4; base += 2 * kNC) {
+        const int j0 = base + lane, j1 = j0 + kNC;
+        const bool ok0 = j0 < n4, ok1 = j1 < n4;
+        float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
+        if (ok0) v0 = t4[j0];
+        if (ok1) v1 = t4[j1];
+        const float m0 = fmaxf(fmaxf(v0.x, v0.y), fmaxf(v0.z, v0.w));
+        const float m1 = fmaxf(fmaxf(v1.x, v1.y), fmaxf(v1.z, v1.w));
+        const bool h0 = ok0 && !(m0 < tau_f);
+        const bool h1 = ok1 && !(m1 < tau_f);
+        if (LSE) {
+            if (ok0) lse_add4(lm, ls, v0, m0, lc);
+            if (ok1) lse_add4(lm, ls, v1, m1, lc);
+        }
+        const unsigned any0 = __ballot_sync(kFull, h0), any1 = __ballot_sync(kFull, h1);
+        if (any0) append4(st, h0, v0, gid0 + 4 * j0, tau_key, lane);
+        if (any1) append4(st, h1, v1, gid0 + 4 * j1, tau_key, lane);
+    }
+}
+
+// One thread waits for the stage; everyone else sleeps on the named barrier,
+// which also ORs each thread's `want` into `any_want` (the same for everyone).
+// Returns false (for every thread) when the wait ran out.
+__device__ __forceinline__ bool stage_ready(FastSmem& sm, int stage, uint32_t parity,
+                                            const Args& a, int ctid, bool want, bool& any_want) {
+    if (ctid == 0 && !mbar_wait_bounded(&sm.full[stage], parity)) {
+        *(volatile int32_t*)&sm.st.abort = 1;
+        set_status(a.status, kStatusTimeout);
+    }
+    any_want = csync_or(want);
+    if (*(volatile int32_t*)&sm.st.abort) return false;
+    mbar_try_wait(&sm.full[stage], parity);  // completed: acquires the stage for this thread
+    return true;
+}
+
 template <bool LSE>
 __device__ void consumer_loop(FastSmem& sm, const Args& a, int ctid) {
     CandState& st = sm.st;
@@ -923,16 +974,24 @@ __device__ void consumer_loop(FastSmem& sm, const Args& a, int ctid) {
     UnitGeom g;
     rp.fast = false;
     g.row = 0;
-    if (!mbar_wait_bounded(&sm.full[stage], fparity)) *(volatile int32_t*)&st.abort = 1;
-    csync();
+    bool compact_now = false;
+    if (!stage_ready(sm, stage, fparity, a, ctid, false, compact_now)) return;
     for (;;) {
-        if (*(volatile int32_t*)&st.abort) break;
-        mbar_try_wait(&sm.full[stage], fparity);  // acquire for this thread (phase is complete)
         const StageMeta md = sm.meta[stage];
         if (md.flags & kMetaDone) break;
+#ifdef ZS_DEBUG_CHECKS
+        if (!ZS_CHECK(md.unit >= 0 && md.unit < a.n_units && md.n >= 0 && md.n <= kTileElems &&
+                          (md.flags & ~(kMetaFirst | kMetaLast)) == 0,
+                      13, ((uint64_t)(uint32_t)md.unit << 32) | (uint32_t)md.flags)) {
+            set_status(a.status, kStatusTimeout);
+            return;
+        }
+#endif
         const float* row_logits;
         if (md.flags & kMetaFirst) {
             g = unit_geom(a, md.unit);
+            ZS_CHECK(g.row >= 0 && g.row < a.B && g.v0 >= 0 && g.v0 <= g.v1 && g.v1 <= a.V && g.e0 <= g.e1,
+                     14, ((uint64_t)(uint32_t)g.row << 32) | (uint32_t)g.v0);
             rp = plan_row(load_params(a.row_params, a.shared, g.row), a.V_total, a.hist,
                           a.hist_len, a.hist_ld, g.row);
             tau_key = 0ull;
@@ -941,7 +1000,8 @@ __device__ void consumer_loop(FastSmem& sm, const Args& a, int ctid) {
             ls = 0.0f;
             lc = (rp.greedy ? 1.0f : 1.0f / rp.p.temp) * 1.4426950408889634f;
             compact_at = min((uint32_t)(kCandCap - kTileElems - kCandMargin),
-                             (uint32_t)(rp.keff + max(rp.keff, kCompactMinGrowth)));
+                             (uint32_t)rp.keff + slack_for((uint32_t)rp.keff) +
+                                 (uint32_t)max(rp.keff, kCompactMinGrowth));
             row_logits = a.logits + (int64_t)g.row * a.ld;
             for (int i = g.v0 + ctid; i < g.e0; i += kNC) {
                 const float x = row_logits[i];
@@ -954,23 +1014,10 @@ __device__ void consumer_loop(FastSmem& sm, const Args& a, int ctid) {
             }
         }
         row_logits = a.logits + (int64_t)g.row * a.ld;
-        ZS_CHECK(md.n <= kTileElems && md.start >= 0 && md.start + md.n <= a.V, 10, ((uint64_t)md.start << 32) | (uint32_t)md.n);
-        ZS_CHECK(st.count + kTileElems + kCandMargin <= (uint32_t)kCandCap, 11, st.count);
-        {
-            const float4* t4 = reinterpret_cast<const float4*>(sm.ring[stage]);
-            const int n4 = md.n >> 2;
-            const int gid0 = a.id_offset + md.start;
-            for (int base = warp * 32; base < n4; base += kNC) {
-                const int j = base + lane;
-                const bool valid = j < n4;
-                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (valid) v = t4[j];
-                const float vm = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
-                const bool hit = valid && !(vm < tau_f);
-                if (LSE && valid) lse_add4(lm, ls, v, vm, lc);
-                if (__any_sync(kFull, hit)) append4(st, hit, v, gid0 + 4 * j, tau_key, lane);
-            }
-        }
+        ZS_CHECK(md.n <= kTileElems && md.start >= 0 && md.start + md.n <= a.V, 10,
+                 ((uint64_t)md.start << 32) | (uint32_t)md.n);
+        filter_tile<LSE>(st, reinterpret_cast<const float4*>(sm.ring[stage]), md.n >> 2,
+                         a.id_offset + md.start, tau_key, tau_f, lc, lm, ls, lane, warp);
         const bool last = (md.flags & kMetaLast) != 0;
         if (last) {
             for (int i = g.e1 + ctid; i < g.v1; i += kNC) {
@@ -984,21 +1031,22 @@ __device__ void consumer_loop(FastSmem& sm, const Args& a, int ctid) {
             stage = 0;
             fparity ^= 1u;
         }
-        csync();  // every consumer is done with ring[prev]; all appends are visible
-        if (ctid == 0) mbar_arrive(&sm.empty[prev]);
+        // The next stage was issued long ago (its slot was freed kStages tiles back),
+        // so thread 0 can wait for it before the barrier that ends this tile.  Each
+        // thread tests the count after its own appends; the last appender sees the
+        // final count, so the OR over threads is exactly "count >= compact_at".
+        const bool want = !last && st.count >= compact_at;
+        if (!stage_ready(sm, stage, fparity, a, ctid, want, compact_now)) return;
+        if (ctid == 0) mbar_arrive(&sm.empty[prev]);  // everyone is done with ring[prev]
         if (last) {
             end_unit<LSE>(sm, a, rp, g, lm, ls, lc, ctid);
             tau_key = 0ull;
             tau_f = -INFINITY;
-        } else if (st.count >= compact_at) {
-            tau_key = compact_top(st, st.count, (uint32_t)rp.keff, kSlackKeep, ctid);
+            csync();
+        } else if (compact_now) {
+            tau_key = compact_top(st, st.count, (uint32_t)rp.keff, slack_for((uint32_t)rp.keff), ctid);
             tau_f = tau_value(tau_key);
         }
-        if (!mbar_wait_bounded(&sm.full[stage], fparity)) {
-            *(volatile int32_t*)&st.abort = 1;
-            set_status(a.status, kStatusTimeout);
-        }
-        csync();
     }
 }
 
@@ -1038,6 +1086,7 @@ __global__ void __launch_bounds__(kNC) zs_merge_kernel(const MergeArgs a) {
         const float lc = (rp.greedy ? 1.0f : 1.0f / rp.p.temp) * 1.4426950408889634f;
         bool x0n;
         float mm, ss;
+        ZS_CHECK(rp.ksel <= kKeffFastMax, 16, rp.ksel);
         const uint32_t kk = merge_partials(st, a.gathered, a.rank_stride, a.G, a.S, a.part_stride,
                                            row, (uint32_t)rp.ksel, lc, x0n, mm, ss, ctid);
         finalize_row(st, st.cand, reinterpret_cast<double*>(st.cand + kProbOffset), kk, rp, x0n,
