@@ -107,11 +107,16 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 }
 
 // Bounded wait for an mbarrier phase; false when the limit ran out.  Meant for
-// one thread per CTA (others sleep on a named barrier meanwhile).
+// one thread per CTA (others sleep on a named barrier meanwhile).  Backs off
+// with nanosleep so a waiting thread does not take issue slots from the warps
+// doing the work.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
-    while (!mbar_try_wait_sleep(bar, parity, 20000u)) {
+    uint32_t ns = 32;
+    while (!mbar_try_wait(bar, parity)) {
+        __nanosleep(ns);
+        if (ns < 256) ns <<= 1;
         if (global_ns() - t0 > kWaitLimitNs) return false;
     }
     return true;

@@ -1,24 +1,23 @@
 // zs_kernels.cuh -- the sampler's device code.
 //
-// One launch of zs_select_kernel streams every logits row once from HBM and
-// produces, per row, the sampled id (or a partial candidate block for the
-// vocab-sharded mode).  Semantics follow sample_token, src/sample.cpp:32-102.
+// zs_select_kernel streams every logits row once from HBM and leaves, per
+// work unit (row, vocab slice), a partial block: the unit's candidate keys
+// (a superset of its top-k after the repetition penalty), the sum-exp
+// scalars and an id-0 flag.  zs_merge_kernel then merges a row's blocks --
+// from the slices of one GPU, or from every rank after the vocab-shard
+// all-gather -- sorts the shortlist and runs the f64 tail of sample_token
+// (src/sample.cpp:52-101).  Rows whose shortlist does not fit shared memory go
+// through zs_large_kernel instead.
 //
-// Work unit = (row, vocab slice).  Large batches use one slice per row; small
-// batches cut rows into slices so every SM has work, and the CTA that finishes
-// a row's last slice merges the slices' partial blocks.
-//
-// Per CTA: one producer warp issues 1-D bulk copies (cp.async.bulk, no tensor
-// map, no multicast) of 8 KB tiles into an 8-stage shared-memory ring,
+// Per select CTA: one producer warp issues 1-D bulk copies (cp.async.bulk, no
+// tensor map, no multicast) of 16 KB stages into a 4-stage shared-memory ring,
 // completion tracked by mbarrier transaction counts.  Eight consumer warps
-// filter each tile against the current threshold key: a float4 whose max is
-// below the threshold value costs four FMNMX and one vote; survivors are
-// appended with warp ballots to a shared candidate buffer.  When the buffer
-// fills, an exact radix select (8-bit digits over the 64-bit key) keeps the
-// K_eff best and raises the threshold.  At the end of a unit the survivors are
-// sorted (bitonic), the repetition penalty is patched in, and the f64 tail of
-// the reference (softmax over the shortlist, nucleus, inverse CDF) runs in
-// the reference's summation order.
+// filter each stage against the current threshold key with plain float
+// compares; survivors are appended to a shared candidate buffer.  The first
+// stage of a unit sets the threshold from the per-thread maxima; when the
+// buffer fills, a compaction keeps a superset of the best K_eff and raises it.
+// The streaming kernel does no per-row sorting or f64 work, so nothing stalls
+// the copy engine between rows.
 #pragma once
 
 #include <math.h>
@@ -30,22 +29,26 @@ namespace zs {
 constexpr int kConsumerWarps = 8;
 constexpr int kNC = kConsumerWarps * 32;  // consumer threads
 constexpr int kThreads = kNC + 32;        // + one producer warp
-constexpr int kTileElems = 2048;          // floats per ring stage (8 KB)
-constexpr int kStages = 8;
+constexpr int kTileElems = 4096;          // floats per ring stage (16 KB)
+constexpr int kHalfElems = kTileElems / 2;
+constexpr int kStages = 4;
 constexpr int kKeffFastMax = 2048;        // top-k + penalty window handled in shared memory
 constexpr int kWinFastMax = 512;          // penalty window handled in shared memory
 constexpr int kCandMargin = 16;           // head/tail elements appended outside the tile check
 constexpr int kSlackMin = 64;             // a compaction may keep slack(K) extra keys: whole
 constexpr int kSlackMax = 1024;           // radix buckets (tie groups) instead of splitting them
 constexpr int kCompactMinGrowth = 512;    // compact once the buffer grew by max(K_eff, this)
-constexpr int kCandCap = 5136;            // >= kKeffFastMax + kSlackMax + kTileElems + kCandMargin
+constexpr int kCandCap = 5136;            // >= kKeffFastMax + kSlackMax + kHalfElems + kCandMargin
+constexpr int kOnePassMaxKeff = 256;      // shortlists up to this filter a stage in one pass
 constexpr int kCandRegs = (kCandCap + kNC - 1) / kNC;
 constexpr int kSortMax = 4096;            // bitonic size bound (kKeffFastMax + kWinFastMax -> 4096)
 constexpr int kProbOffset = 2048;         // f64 probabilities alias cand[2048..4096)
 constexpr int kShortlistDefault = 256;    // kTopPShortlist, src/sample.cpp:12
 
-static_assert(kCandCap >= kKeffFastMax + kSlackMax + kTileElems + kCandMargin,
-              "candidate buffer too small");
+static_assert(kCandCap >= kKeffFastMax + kSlackMax + kHalfElems + kCandMargin,
+              "candidate buffer too small for half-stage passes");
+static_assert(kCandCap >= kOnePassMaxKeff + 2 * 128 + 256 + kTileElems + kCandMargin,
+              "candidate buffer too small for one-pass stages");
 static_assert(kKeffFastMax + kSlackMax + kWinFastMax <= kSortMax, "sort bound");
 
 __host__ __device__ constexpr uint32_t slack_for(uint32_t k) {
@@ -68,7 +71,8 @@ __device__ unsigned long long zs_debug_record[4];
                       atomicAdd(&zs_debug_record[3], 1ull), false)                           \
                    : (atomicAdd(&zs_debug_record[3], 1ull), false)))
 #else
-#define ZS_CHECK(cond, site, val) true
+__device__ __forceinline__ bool zs_check_off() { return true; }
+#define ZS_CHECK(cond, site, val) zs_check_off()
 #endif
 
 struct Params {  // zen::SamplingParams layout
@@ -132,7 +136,7 @@ struct Args {
     int32_t S;      // slices per row
     int32_t slice;  // columns per slice (multiple of 4)
     int32_t n_units;
-    int32_t mode;   // 0: draw here when S == 1; otherwise (or 1) write partial blocks
+    int32_t mode;   // 0: zs_sample (blocks in handle scratch); 1: vocab shard (caller's blocks)
     uint8_t* part;  // partial blocks [B][S]
     int64_t part_stride;
     int* status;
@@ -237,7 +241,10 @@ struct CandState {
     uint64_t red64[kConsumerWarps];
     uint64_t red64b[kConsumerWarps];
     float redf[2 * kConsumerWarps];
-    int32_t win[kWinFastMax];
+    union {
+        int32_t win[kWinFastMax];  // penalty window (end of a unit)
+        uint64_t prop[kNC];        // per-thread threshold proposals
+    };
     uint64_t thr;
     uint64_t thr2;
     uint4 part_hdr;
@@ -426,6 +433,68 @@ __device__ __forceinline__ float tau_value(uint64_t tau_key) {
     return o == 0u ? -INFINITY : value_of_ord(o);
 }
 
+// Shortlists up to kGroupMaxK use a cheaper threshold than a radix select: every
+// consumer thread proposes the largest key of its own share of the keys, and the
+// kk-th largest of those 256 proposals is a valid threshold (the kk proposals at
+// or above it are kk distinct keys), usually only a little below the exact kk-th
+// key.  Exact order comes later from the final sort.
+constexpr uint32_t kGroupMaxK = kNC;
+
+// kk-th largest of the per-thread proposals (0 = no key); 0 when fewer than kk
+// threads proposed a key.  Ends synchronised; every thread gets the result.
+__device__ __forceinline__ uint64_t kth_of_proposals(CandState& st, uint64_t mine, uint32_t kk,
+                                                     int ctid) {
+    uint64_t* prop = st.prop;
+    prop[ctid] = mine;
+    csync();
+    uint32_t rank = 0;
+    if (mine != 0ull)
+        for (int j = 0; j < kNC; ++j) rank += prop[j] > mine ? 1u : 0u;
+    if (mine != 0ull && rank == kk - 1) st.thr = mine;
+    const unsigned have = __popc(__ballot_sync(kFull, mine != 0ull));
+    if ((ctid & 31) == 0) st.scan[ctid >> 5] = have;
+    csync();
+    uint32_t total = 0;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) total += st.scan[w];
+    const uint64_t T = total >= kk ? st.thr : 0ull;
+    csync();
+    return T;
+}
+
+// Warp 0 finds the radix bucket holding the need-th largest key: hist[] holds
+// counts per digit; scanning digits from 255 down, the bucket is where the
+// running count reaches need.  Writes sel_digit / sel_above / sel_cnt.
+__device__ __forceinline__ void select_bucket(CandState& st, uint32_t need, int lane) {
+    // lane l owns digits 255-8l .. 248-8l (descending)
+    uint32_t h[8];
+    uint32_t sum = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        h[q] = st.hist[255 - 8 * lane - q];
+        sum += h[q];
+    }
+    uint32_t incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += t;
+    }
+    const uint32_t before = incl - sum;
+    if (before < need && incl >= need) {
+        uint32_t cum = before;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            if (cum < need && cum + h[q] >= need) {
+                st.sel_digit = 255u - 8u * (uint32_t)lane - (uint32_t)q;
+                st.sel_above = cum;
+                st.sel_cnt = h[q];
+            }
+            cum += h[q];
+        }
+    }
+}
+
 // Keeps the kk largest of the n > kk keys in cand[0..) -- plus at most `slack`
 // more, when a whole radix bucket is cheaper to keep than to split -- and
 // returns the smallest kept key, the new filter threshold.  Radix select on
@@ -447,25 +516,20 @@ __device__ uint64_t compact_top(CandState& st, uint32_t n, uint32_t kk, uint32_t
         st.red64[warp] = lo;
         st.red64b[warp] = hi;
     }
+    st.hist[ctid] = 0u;
     csync();
-    if (ctid == 0) {
-        uint64_t a = st.red64[0], b = st.red64b[0];
-        for (int w = 1; w < kConsumerWarps; ++w) {
-            a = st.red64[w] < a ? st.red64[w] : a;
-            b = st.red64b[w] > b ? st.red64b[w] : b;
-        }
-        st.thr = a;
-        st.thr2 = b;
+    uint64_t a = st.red64[0], b = st.red64b[0];
+#pragma unroll
+    for (int w = 1; w < kConsumerWarps; ++w) {
+        a = st.red64[w] < a ? st.red64[w] : a;
+        b = st.red64b[w] > b ? st.red64b[w] : b;
     }
-    csync();
-    const uint64_t diff = st.thr ^ st.thr2;  // n >= 2 unique keys: nonzero
+    const uint64_t diff = a ^ b;  // n >= 2 unique keys: nonzero
     int shift = diff ? ((63 - __clzll((long long)diff)) >> 3) << 3 : 0;
     uint64_t mask = shift >= 56 ? 0ull : (~0ull << (shift + 8));
-    uint64_t prefix = st.thr & mask;
+    uint64_t prefix = a & mask;
     uint32_t need = kk;
-    for (; shift >= 0; shift -= 8) {
-        st.hist[ctid] = 0u;
-        csync();
+    for (;;) {
         for (uint32_t b0 = (uint32_t)warp * 32; b0 < n; b0 += kNC) {
             const uint32_t i = b0 + lane;
             const uint64_t k = i < n ? st.cand[i] : 0ull;
@@ -475,21 +539,17 @@ __device__ uint64_t compact_top(CandState& st, uint32_t n, uint32_t kk, uint32_t
             if (in && (__ffs(peers) - 1) == lane) atomicAdd(&st.hist[d], (uint32_t)__popc(peers));
         }
         csync();
-        const uint32_t h = st.hist[255 - ctid];
-        uint32_t tot;
-        const uint32_t cum = block_incl_scan(h, st.scan, ctid, tot);
-        if (cum >= need && cum - h < need) {
-            st.sel_digit = 255u - (uint32_t)ctid;
-            st.sel_above = cum - h;
-            st.sel_cnt = h;
-        }
+        if (warp == 0) select_bucket(st, need, lane);
         csync();
         const uint32_t digit = st.sel_digit, above = st.sel_above, cnt = st.sel_cnt;
         prefix |= (uint64_t)digit << shift;
         mask |= 0xffull << shift;
         need -= above;
+        // keeping the whole bucket is exact or close enough; else split it further
+        if (cnt <= need + slack || shift == 0) break;
+        shift -= 8;
+        st.hist[ctid] = 0u;
         csync();
-        if (cnt <= need + slack) break;  // keeping the whole bucket is exact or close enough
     }
     // Threshold = smallest key of the selected bucket (all of it is kept).
     uint64_t mn = ~0ull;
@@ -500,35 +560,99 @@ __device__ uint64_t compact_top(CandState& st, uint32_t n, uint32_t kk, uint32_t
     mn = warp_min_u64(mn);
     if (lane == 0) st.red64[warp] = mn;
     csync();
-    if (ctid == 0) {
-        uint64_t t = st.red64[0];
-        for (int w = 1; w < kConsumerWarps; ++w) t = st.red64[w] < t ? st.red64[w] : t;
-        st.thr = t;
-    }
-    csync();
-    const uint64_t T = st.thr;
+    uint64_t T = st.red64[0];
+#pragma unroll
+    for (int w = 1; w < kConsumerWarps; ++w) T = st.red64[w] < T ? st.red64[w] : T;
+    // Move the kept keys to the front: read all, then place with warp ballots.
     uint64_t loc[kCandRegs];
-    uint32_t c = 0;
 #pragma unroll
     for (int j = 0; j < kCandRegs; ++j) {
         const uint32_t i = ctid + j * kNC;
-        const uint64_t k = (i < n) ? st.cand[i] : 0ull;
-        loc[j] = k;
-        c += (k >= T) ? 1u : 0u;
+        loc[j] = (i < n) ? st.cand[i] : 0ull;
     }
-    uint32_t tot;
-    uint32_t o = block_incl_scan(c, st.scan, ctid, tot) - c;
+    if (ctid == 0) st.count = 0u;
+    csync();
+    uint32_t wk = 0;
 #pragma unroll
-    for (int j = 0; j < kCandRegs; ++j)
-        if (loc[j] >= T) st.cand[o++] = loc[j];
-    if (ctid == 0) st.count = tot;
+    for (int j = 0; j < kCandRegs; ++j) wk += __popc(__ballot_sync(kFull, loc[j] >= T));
+    uint32_t base = 0;
+    if (lane == 0 && wk) base = atomicAdd(&st.count, wk);
+    base = __shfl_sync(kFull, base, 0);
+    const unsigned below = lanemask_lt();
+#pragma unroll
+    for (int j = 0; j < kCandRegs; ++j) {
+        const unsigned m = __ballot_sync(kFull, loc[j] >= T);
+        if (loc[j] >= T) st.cand[base + __popc(m & below)] = loc[j];
+        base += __popc(m);
+    }
     csync();
     return T;
 }
 
-// Sorts cand[0..n) descending (bitonic over the next power of two, 0-padded).
+// Keeps the keys >= T of cand[0..n) at the front and returns how many.
+__device__ __forceinline__ uint32_t keep_at_least(CandState& st, uint32_t n, uint64_t T, int ctid) {
+    const int lane = ctid & 31;
+    uint64_t loc[kCandRegs];
+#pragma unroll
+    for (int j = 0; j < kCandRegs; ++j) {
+        const uint32_t i = ctid + j * kNC;
+        loc[j] = (i < n) ? st.cand[i] : 0ull;
+    }
+    if (ctid == 0) st.count = 0u;
+    csync();
+    uint32_t wk = 0;
+#pragma unroll
+    for (int j = 0; j < kCandRegs; ++j) wk += __popc(__ballot_sync(kFull, loc[j] >= T));
+    uint32_t base = 0;
+    if (lane == 0 && wk) base = atomicAdd(&st.count, wk);
+    base = __shfl_sync(kFull, base, 0);
+    const unsigned below = lanemask_lt();
+#pragma unroll
+    for (int j = 0; j < kCandRegs; ++j) {
+        const unsigned m = __ballot_sync(kFull, loc[j] >= T);
+        if (loc[j] >= T) st.cand[base + __popc(m & below)] = loc[j];
+        base += __popc(m);
+    }
+    csync();
+    return st.count;
+}
+
+// Reduces cand[0..n) (n > kk) to a set that contains its kk largest keys and
+// returns the new threshold (the smallest kept key).  Shortlists up to
+// kGroupMaxK use the per-thread-maximum proposal (a few barriers); when that
+// keeps too much, or for larger shortlists, the radix select finishes the job.
+__device__ uint64_t compact_select(CandState& st, uint32_t n, uint32_t kk, int ctid) {
+    const uint32_t slack = slack_for(kk);
+    if (kk <= kGroupMaxK) {
+        uint64_t mine = 0ull;
+        for (uint32_t i = ctid; i < n; i += kNC) {
+            const uint64_t k = st.cand[i];
+            mine = k > mine ? k : mine;
+        }
+        const uint64_t T = kth_of_proposals(st, mine, kk, ctid);
+        if (T != 0ull) {
+            const uint32_t kept = keep_at_least(st, n, T, ctid);
+            if (kept <= kk + 2 * slack + 256u) return T;
+            n = kept;
+        }
+    }
+    return compact_top(st, n, kk, slack, ctid);
+}
+
+// Sorts cand[0..n) descending.  n <= kNC: every thread ranks one key against
+// all others (keys are unique); larger n: bitonic over the next power of two.
 __device__ void sort_desc(CandState& st, uint32_t n, int ctid) {
     if (n <= 1) return;
+    if (n <= (uint32_t)kNC) {
+        const uint64_t k = (uint32_t)ctid < n ? st.cand[ctid] : 0ull;
+        uint32_t rank = 0;
+        if ((uint32_t)ctid < n)
+            for (uint32_t i = 0; i < n; ++i) rank += st.cand[i] > k ? 1u : 0u;
+        csync();
+        if ((uint32_t)ctid < n) st.cand[rank] = k;
+        csync();
+        return;
+    }
     uint32_t N = 2;
     while (N < n) N <<= 1;
     if (!ZS_CHECK(N <= (uint32_t)kCandCap, 5, N)) return;
@@ -730,11 +854,11 @@ __device__ void finalize_row(CandState& st, const uint64_t* cand, double* prob, 
     csync();
 }
 
-// Streams the keys of partial blocks through the threshold filter and leaves
-// the exact top-ksel, sorted, in st.cand[0..kk).  Also merges the partials'
-// sum-exp scalars and id-0 flags.  Returns kk.  Runs in its own launch, after
-// every partial block is complete; each header is read once by thread 0 and
-// shared, so all threads take the same path.
+// Streams the keys of partial blocks (unsorted; 0 = removed) through the
+// threshold filter and leaves the exact top-ksel, sorted, in st.cand[0..kk).
+// Also merges the partials' sum-exp scalars and id-0 flags.  Returns kk.  Runs
+// in its own launch, after every partial block is complete; each header is
+// read once by thread 0 and shared, so all threads take the same path.
 __device__ uint32_t merge_partials(CandState& st, const uint8_t* base, int64_t rank_stride,
                                    int G, int S, int64_t part_stride, int row, uint32_t ksel,
                                    float lse_c, bool& x0_nan, float& lse_m, float& lse_s,
@@ -764,9 +888,7 @@ __device__ uint32_t merge_partials(CandState& st, const uint8_t* base, int64_t r
             const unsigned long long* keys =
                 reinterpret_cast<const unsigned long long*>(pp + kPartialHeaderBytes);
             for (uint32_t b = 0; b < cnt; b += kNC) {
-                // Partial keys are sorted: stop at the first chunk that cannot pass.
-                if (__ldcg(keys + b) <= tau) break;
-                if (full) tau = compact_top(st, st.count, ksel, slack_for(ksel), ctid);
+                if (full) tau = compact_select(st, st.count, ksel, ctid);
                 const uint32_t i = b + ctid;
                 const uint64_t k = (i < cnt) ? __ldcg(keys + i) : 0ull;
                 warp_append(st, k > tau, k, lane);
@@ -778,7 +900,7 @@ __device__ uint32_t merge_partials(CandState& st, const uint8_t* base, int64_t r
     csync();
     uint32_t n = st.count;
     if (n > ksel) {
-        compact_top(st, n, ksel, slack_for(ksel), ctid);
+        compact_select(st, n, ksel, ctid);
         n = st.count;
     }
     sort_desc(st, n, ctid);
@@ -862,13 +984,16 @@ __device__ void producer_loop(FastSmem& sm, const Args& a) {
         if (pending & (1u << s)) mbar_wait_bounded(&sm.full[s], (pend_parity >> s) & 1u);
 }
 
+// End of a unit: shrink the candidates to a set holding the unit's top-keff,
+// patch in the repetition penalty, and write the partial block (unsorted).  The
+// exact selection, order and draw happen in zs_merge_kernel.
 template <bool LSE>
 __device__ void end_unit(FastSmem& sm, const Args& a, const RowPlan& rp, const UnitGeom& g,
                          float lm, float ls, float lc, int ctid) {
     CandState& st = sm.st;
     uint32_t n = st.count;
     if (n > (uint32_t)rp.keff) {
-        compact_top(st, n, (uint32_t)rp.keff, slack_for((uint32_t)rp.keff), ctid);
+        compact_select(st, n, (uint32_t)rp.keff, ctid);
         n = st.count;
     }
     ZS_CHECK(n <= (uint32_t)kCandCap, 9, n);
@@ -879,38 +1004,29 @@ __device__ void end_unit(FastSmem& sm, const Args& a, const RowPlan& rp, const U
         M = st.lse_m;
         Sx = st.lse_s;
     }
-    uint32_t removed = 0;
     if (rp.penal) {
         const int32_t* window = a.hist + (int64_t)g.row * a.hist_ld + (rp.hist_len - rp.win);
         penalty_fixup(st, row_logits, window, rp.win, rp.p.repeat_penalty, a.id_offset, g.v0,
                       g.v1, a.V_total, n, LSE, M, lc, ctid);
         n = st.count;
-        removed = st.removed;
         if (LSE) Sx = (float)((double)Sx + st.lse_delta);
     }
-    sort_desc(st, n, ctid);
-    const uint32_t valid = n - removed;
-    const uint32_t kk = valid < (uint32_t)rp.ksel ? valid : (uint32_t)rp.ksel;
     const bool x0n = st.x0_nan != 0;
-    if (a.mode == 0 && a.S == 1) {
-        finalize_row(st, st.cand, reinterpret_cast<double*>(st.cand + kProbOffset), kk, rp, x0n,
-                     LSE, M, Sx, g.row, a.rng, a.out_ids, a.info, a.cand_ids, a.cand_probs,
-                     a.cand_ld, ctid);
-    } else {
-        ZS_CHECK(g.row >= 0 && g.row < a.B && g.s >= 0 && g.s < a.S, 15, ((uint64_t)g.row << 32) | (uint32_t)g.s);
-        uint8_t* pp = a.part + ((int64_t)g.row * a.S + g.s) * a.part_stride;
-        uint64_t* keys = reinterpret_cast<uint64_t*>(pp + kPartialHeaderBytes);
-        ZS_CHECK(16 + 8 * (int64_t)kk <= a.part_stride && kk <= (uint32_t)rp.ksel, 7, kk);
-        for (uint32_t i = ctid; i < kk && 16 + 8 * (int64_t)(i + 1) <= a.part_stride; i += kNC) keys[i] = st.cand[i];
-        if (ctid == 0) {
-            const bool has0 = (a.id_offset + g.v0 == 0) && (g.v1 > g.v0);
-            uint4 hv;
-            hv.x = kk;
-            hv.y = (has0 ? kPartHasId0 : 0u) | ((has0 && x0n) ? kPartX0Nan : 0u);
-            hv.z = __float_as_uint(M);
-            hv.w = __float_as_uint(Sx);
-            *reinterpret_cast<uint4*>(pp) = hv;
-        }
+    ZS_CHECK(g.row >= 0 && g.row < a.B && g.s >= 0 && g.s < a.S, 15, ((uint64_t)g.row << 32) | (uint32_t)g.s);
+    uint8_t* pp = a.part + ((int64_t)g.row * a.S + g.s) * a.part_stride;
+    unsigned long long* keys = reinterpret_cast<unsigned long long*>(pp + kPartialHeaderBytes);
+    const uint32_t cap = (uint32_t)((a.part_stride - kPartialHeaderBytes) / 8);
+    ZS_CHECK(n <= cap, 7, n);
+    const uint32_t kk = n < cap ? n : cap;
+    for (uint32_t i = ctid; i < kk; i += kNC) __stcg(keys + i, (unsigned long long)st.cand[i]);
+    if (ctid == 0) {
+        const bool has0 = (a.id_offset + g.v0 == 0) && (g.v1 > g.v0);
+        uint4 hv;
+        hv.x = kk;
+        hv.y = (has0 ? kPartHasId0 : 0u) | ((has0 && x0n) ? kPartX0Nan : 0u);
+        hv.z = __float_as_uint(M);
+        hv.w = __float_as_uint(Sx);
+        *reinterpret_cast<uint4*>(pp) = hv;
     }
     csync();
     if (ctid == 0) {
@@ -919,29 +1035,90 @@ __device__ void end_unit(FastSmem& sm, const Args& a, const RowPlan& rp, const U
     }
 }
 
-// Filters the float4s at t4[j] and t4[j + kNC/...] of one ring stage.
-template <bool LSE>
-__device__ __forceinline__ void filter_tile(CandState& st, const float4* t4, int n4, int gid0,
-                                            uint64_t tau_key, float tau_f, float lc, float& lm,
-                                            float& ls, int lane, int warp) {
-    // Two float4 per thread per step: j and j + kNC.
+// Appends the components of v (ids id..id+3) that beat the threshold, one
+// shared atomic per survivor.  Components strictly above tau_f beat tau_key by
+// value alone; only ties with the threshold value need the id comparison.
+__device__ __forceinline__ void append_lane(CandState& st, const float4& v, int32_t id,
+                                            uint64_t tau_key, float tau_f) {
+    const float xs[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const float x = xs[q];
+        if (x > tau_f || (x == tau_f && make_key(x, id + q) > tau_key)) {
+            const uint32_t at = atomicAdd(&st.count, 1u);
+            if (ZS_CHECK(at < (uint32_t)kCandCap, 18, at)) st.cand[at] = make_key(x, id + q);
+        }
+    }
+}
+
+// Threshold for the first stage of a unit: each thread proposes its largest key
+// among the float4s it filters (the same j0/j1 split as filter_range), and the
+// keff-th largest proposal minus one is a filter key that lets at least keff keys
+// of this tile through.  Returns 0 when that is not usable (too few elements, or
+// the proposal is a NaN), which keeps exact per-element comparisons.
+__device__ __forceinline__ uint64_t tile_threshold(CandState& st, const float4* t4, int n4,
+                                                   int gid0, uint32_t keff, int lane, int warp,
+                                                   int ctid) {
+    uint64_t mine = 0ull;
     for (int base = warp * 32; base < n4; base += 2 * kNC) {
         const int j0 = base + lane, j1 = j0 + kNC;
-        const bool ok0 = j0 < n4, ok1 = j1 < n4;
-        float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
+        if (j0 < n4) {
+            const float4 v = t4[j0];
+            const int id = gid0 + 4 * j0;
+            uint64_t k = make_key(v.x, id);
+            uint64_t t = make_key(v.y, id + 1); k = t > k ? t : k;
+            t = make_key(v.z, id + 2); k = t > k ? t : k;
+            t = make_key(v.w, id + 3); k = t > k ? t : k;
+            mine = k > mine ? k : mine;
+        }
+        if (j1 < n4) {
+            const float4 v = t4[j1];
+            const int id = gid0 + 4 * j1;
+            uint64_t k = make_key(v.x, id);
+            uint64_t t = make_key(v.y, id + 1); k = t > k ? t : k;
+            t = make_key(v.z, id + 2); k = t > k ? t : k;
+            t = make_key(v.w, id + 3); k = t > k ? t : k;
+            mine = k > mine ? k : mine;
+        }
+    }
+    const uint64_t T = kth_of_proposals(st, mine, keff, ctid);
+    if (T == 0ull || (uint32_t)(T >> 32) == 0u) return 0ull;
+    return T - 1ull;  // keys are integers: "> T-1" is ">= T"
+}
+
+// Filters float4s [j_begin, j_end) of a ring stage against the threshold.
+template <bool LSE>
+__device__ __forceinline__ void filter_range(CandState& st, const float4* t4, int j_begin,
+                                             int j_end, int gid0, uint64_t tau_key, float tau_f,
+                                             float lc, float& lm, float& ls, int lane, int warp) {
+    // No usable value threshold yet (start of a unit, or the K-th best is a NaN):
+    // exact key comparisons with warp-aggregated appends.
+    if ((uint32_t)(tau_key >> 32) == 0u) {
+        for (int base = j_begin + warp * 32; base < j_end; base += kNC) {
+            const int j = base + lane;
+            const bool ok = j < j_end;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (ok) v = t4[j];
+            if (LSE && ok) lse_add4(lm, ls, v, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)), lc);
+            append4(st, ok, v, gid0 + 4 * j, tau_key, lane);
+        }
+        return;
+    }
+    // Two float4 per thread per step: j and j + kNC.
+    for (int base = j_begin + warp * 32; base < j_end; base += 2 * kNC) {
+        const int j0 = base + lane, j1 = j0 + kNC;
+        const bool ok0 = j0 < j_end, ok1 = j1 < j_end;
+        float4 v0 = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY), v1 = v0;
         if (ok0) v0 = t4[j0];
         if (ok1) v1 = t4[j1];
-        const float m0 = fmaxf(fmaxf(v0.x, v0.y), fmaxf(v0.z, v0.w));
-        const float m1 = fmaxf(fmaxf(v1.x, v1.y), fmaxf(v1.z, v1.w));
-        const bool h0 = ok0 && !(m0 < tau_f);
-        const bool h1 = ok1 && !(m1 < tau_f);
         if (LSE) {
-            if (ok0) lse_add4(lm, ls, v0, m0, lc);
-            if (ok1) lse_add4(lm, ls, v1, m1, lc);
+            if (ok0) lse_add4(lm, ls, v0, fmaxf(fmaxf(v0.x, v0.y), fmaxf(v0.z, v0.w)), lc);
+            if (ok1) lse_add4(lm, ls, v1, fmaxf(fmaxf(v1.x, v1.y), fmaxf(v1.z, v1.w)), lc);
         }
-        const unsigned any0 = __ballot_sync(kFull, h0), any1 = __ballot_sync(kFull, h1);
-        if (any0) append4(st, h0, v0, gid0 + 4 * j0, tau_key, lane);
-        if (any1) append4(st, h1, v1, gid0 + 4 * j1, tau_key, lane);
+        const bool h0 = ok0 && ((v0.x >= tau_f) | (v0.y >= tau_f) | (v0.z >= tau_f) | (v0.w >= tau_f));
+        const bool h1 = ok1 && ((v1.x >= tau_f) | (v1.y >= tau_f) | (v1.z >= tau_f) | (v1.w >= tau_f));
+        if (h0) append_lane(st, v0, gid0 + 4 * j0, tau_key, tau_f);
+        if (h1) append_lane(st, v1, gid0 + 4 * j1, tau_key, tau_f);
     }
 }
 
@@ -970,6 +1147,7 @@ __device__ void consumer_loop(FastSmem& sm, const Args& a, int ctid) {
     float tau_f = -INFINITY;
     float lm = -INFINITY, ls = 0.0f, lc = 1.4426950408889634f;
     uint32_t compact_at = (uint32_t)(kCandCap - kTileElems - kCandMargin);
+    bool two_pass = false;
     RowPlan rp;
     UnitGeom g;
     rp.fast = false;
@@ -999,7 +1177,8 @@ __device__ void consumer_loop(FastSmem& sm, const Args& a, int ctid) {
             lm = -INFINITY;
             ls = 0.0f;
             lc = (rp.greedy ? 1.0f : 1.0f / rp.p.temp) * 1.4426950408889634f;
-            compact_at = min((uint32_t)(kCandCap - kTileElems - kCandMargin),
+            two_pass = rp.keff > kOnePassMaxKeff;
+            compact_at = min((uint32_t)(kCandCap - (two_pass ? kHalfElems : kTileElems) - kCandMargin),
                              (uint32_t)rp.keff + slack_for((uint32_t)rp.keff) +
                                  (uint32_t)max(rp.keff, kCompactMinGrowth));
             row_logits = a.logits + (int64_t)g.row * a.ld;
@@ -1016,8 +1195,29 @@ __device__ void consumer_loop(FastSmem& sm, const Args& a, int ctid) {
         row_logits = a.logits + (int64_t)g.row * a.ld;
         ZS_CHECK(md.n <= kTileElems && md.start >= 0 && md.start + md.n <= a.V, 10,
                  ((uint64_t)md.start << 32) | (uint32_t)md.n);
-        filter_tile<LSE>(st, reinterpret_cast<const float4*>(sm.ring[stage]), md.n >> 2,
-                         a.id_offset + md.start, tau_key, tau_f, lc, lm, ls, lane, warp);
+        const float4* t4 = reinterpret_cast<const float4*>(sm.ring[stage]);
+        const int n4 = md.n >> 2;
+        const int gid0 = a.id_offset + md.start;
+        if (!two_pass) {
+            if (tau_key == 0ull && (uint32_t)rp.keff <= kGroupMaxK) {
+                // Threshold from this stage before filtering it: the keff-th largest
+                // of the per-thread maxima over this stage's float4s.
+                tau_key = tile_threshold(st, t4, n4, gid0, (uint32_t)rp.keff, lane, warp, ctid);
+                tau_f = tau_value(tau_key);
+            }
+            filter_range<LSE>(st, t4, 0, n4, gid0, tau_key, tau_f, lc, lm, ls, lane, warp);
+        } else {
+            // Large shortlists: two half-stage passes, with the buffer check between.
+            const int h = n4 < kHalfElems / 4 ? n4 : kHalfElems / 4;
+            filter_range<LSE>(st, t4, 0, h, gid0, tau_key, tau_f, lc, lm, ls, lane, warp);
+            if (n4 > h) {
+                if (csync_or(st.count >= compact_at)) {
+                    tau_key = compact_select(st, st.count, (uint32_t)rp.keff, ctid);
+                    tau_f = tau_value(tau_key);
+                }
+                filter_range<LSE>(st, t4, h, n4, gid0, tau_key, tau_f, lc, lm, ls, lane, warp);
+            }
+        }
         const bool last = (md.flags & kMetaLast) != 0;
         if (last) {
             for (int i = g.e1 + ctid; i < g.v1; i += kNC) {
@@ -1044,7 +1244,7 @@ __device__ void consumer_loop(FastSmem& sm, const Args& a, int ctid) {
             tau_f = -INFINITY;
             csync();
         } else if (compact_now) {
-            tau_key = compact_top(st, st.count, (uint32_t)rp.keff, slack_for((uint32_t)rp.keff), ctid);
+            tau_key = compact_select(st, st.count, (uint32_t)rp.keff, ctid);
             tau_f = tau_value(tau_key);
         }
     }

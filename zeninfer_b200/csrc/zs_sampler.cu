@@ -77,6 +77,16 @@ int win_bound_of(const zs_params& p) {
     return std::max(0, p.repeat_last_n);
 }
 
+// Keys one partial block can hold for a row: the unit epilogue keeps the top
+// keff = ksel + window plus the compaction's slack, then appends up to `window`
+// penalised values.
+int64_t partial_keys_for(int ksel, int wb) {
+    const uint32_t keff = (uint32_t)std::min<int64_t>((int64_t)ksel + wb, zs::kKeffFastMax);
+    const uint32_t slack = zs::slack_for(keff);
+    const uint32_t extra = keff <= zs::kGroupMaxK ? 2 * slack + 256u : slack;
+    return (int64_t)keff + extra + std::min(wb, zs::kWinFastMax);
+}
+
 int choose_slices(int B, int V, int ctas) {
     if (B <= 0 || V <= 0) return 1;
     const int smax = std::max(1, V / (2 * zs::kTileElems));
@@ -88,19 +98,21 @@ Plan make_plan(int B, int V_cols, int V_total, const zs_params* params, int per_
                bool have_history) {
     Plan pl;
     const int np = per_row ? B : 1;
+    int64_t max_keys = 1;
     for (int i = 0; i < np; ++i) {
         const zs_params& p = params[i];
         const int ks = ksel_of(p, V_total);
-        const int wb = have_history ? win_bound_of(p) : 0;
+        const int wb = win_bound_of(p);  // the block layout must not depend on history presence
         pl.max_ksel = std::max(pl.max_ksel, ks);
-        if (wb > 0) pl.any_penal = true;
-        if ((long)ks + wb > zs::kKeffFastMax || wb > zs::kWinFastMax) pl.any_large = true;
+        if (have_history && wb > 0) pl.any_penal = true;
+        if (have_history && ((long)ks + wb > zs::kKeffFastMax || wb > zs::kWinFastMax)) pl.any_large = true;
+        max_keys = std::max(max_keys, partial_keys_for(ks, wb));
     }
     pl.S = choose_slices(B, V_cols, ctas);
     const int per = (V_cols + pl.S - 1) / pl.S;
     pl.slice = std::max(4, (per + 3) & ~3);
     pl.S = std::max(1, (V_cols + pl.slice - 1) / pl.slice);
-    pl.part_stride = ((int64_t)zs::kPartialHeaderBytes + 8LL * std::min(pl.max_ksel, zs::kKeffFastMax) + 15) & ~15LL;
+    pl.part_stride = ((int64_t)zs::kPartialHeaderBytes + 8LL * max_keys + 15) & ~15LL;
     return pl;
 }
 
@@ -206,9 +218,9 @@ zs::Params to_dev(const zs_params& p) {
     return d;
 }
 
-// Launches the select kernel for one batch: rows with one slice are drawn in
-// place; rows cut into slices leave partial blocks that zs_merge_kernel merges
-// in a second launch.  Rows needing the large shortlist path follow in
+// Launches the select kernel for one batch, which leaves one partial block per
+// (row, slice); zs_merge_kernel then merges each row's blocks, sorts the
+// shortlist and draws.  Rows needing the large shortlist path follow in
 // zs_large_kernel.
 zs_status launch_select(zs_context* h, const zs::Args& base, const Plan& pl, bool want_lse,
                         cudaStream_t st) {
@@ -218,7 +230,7 @@ zs_status launch_select(zs_context* h, const zs::Args& base, const Plan& pl, boo
     a.n_units = (int32_t)std::min<int64_t>((int64_t)a.B * pl.S, INT32_MAX);
     a.part_stride = pl.part_stride;
     a.status = h->status;
-    const bool split = (a.mode == 0 && pl.S > 1);
+    const bool split = (a.mode == 0);  // drawn by zs_merge_kernel after the partials
     if (split) {
         zs_status s = grow((void**)&h->part, &h->part_bytes, (size_t)a.B * pl.S * pl.part_stride);
         if (s != ZS_OK) return s;
