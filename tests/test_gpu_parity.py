@@ -61,3 +61,42 @@ def test_split_rows(sampler, rows):
     compare(run_gpu(sampler, x, p, st, cand_ld=40), run_oracle(x, p, st, cand_ld=40))
     pg = SamplingParams()
     compare(run_gpu(sampler, x, pg, st), run_oracle(x, pg, st))
+
+
+@pytest.mark.parametrize("order", ["descending", "front_loaded", "ascending"])
+def test_speculation_fallback(sampler, order):
+    """Rows whose best values sit in the first stage defeat the speculative
+    threshold (too few keys above it); those units are redone exactly."""
+    rows, n = 16, W.VOCAB
+    rng = np.random.default_rng(7)
+    x = rng.normal(0, 1, size=(rows, n)).astype(np.float32)
+    if order == "descending":
+        x = -np.sort(-x, axis=1)
+    elif order == "ascending":
+        x = np.sort(x, axis=1)
+    else:  # the 2048 largest values of each row moved to its front
+        idx = np.argsort(-x, axis=1)[:, :2048]
+        for r in range(rows):
+            top = x[r, idx[r]].copy()
+            x[r, idx[r]] = x[r, :2048]
+            x[r, :2048] = top
+    x = np.ascontiguousarray(x)
+    for p in (SamplingParams(temp=0.7, top_k=50, top_p=0.9), SamplingParams(temp=1.0, top_p=0.95),
+              SamplingParams(temp=0.8, top_k=1024), SamplingParams()):
+        k = p.top_k if p.top_k > 0 else 256
+        st = _states(range(rows))
+        compare(run_gpu(sampler, x, p, st, cand_ld=k if p.temp > 0 else 0),
+                run_oracle(x, p, st, cand_ld=k if p.temp > 0 else 0))
+
+
+@pytest.mark.parametrize("params", [SamplingParams(), SamplingParams(temp=1.0, top_p=0.95),
+                                    SamplingParams(temp=0.9, top_k=1),
+                                    SamplingParams(temp=1.3, top_k=255, top_p=0.5)])
+def test_warp_merge_batch(sampler, params):
+    """Batches of at least four rows per SM merge each row in one warp."""
+    rows = 1024
+    x = W.generate(3, rows, row0=77)
+    k = params.top_k if params.top_k > 0 else 256
+    st = _states(range(rows))
+    cl = k if params.temp > 0 else 0
+    compare(run_gpu(sampler, x, params, st, cand_ld=cl), run_oracle(x, params, st, cand_ld=cl))

@@ -38,6 +38,7 @@ constexpr int kCandMargin = 16;           // head/tail elements appended outside
 constexpr int kSlackMin = 64;             // a compaction may keep slack(K) extra keys: whole
 constexpr int kSlackMax = 1024;           // radix buckets (tie groups) instead of splitting them
 constexpr int kCompactMinGrowth = 512;    // compact once the buffer grew by max(K_eff, this)
+constexpr int kCompactGrowthSmall = 128;  // ... for one-pass shortlists, whose compaction is cheap
 constexpr int kCandCap = 5136;            // >= kKeffFastMax + kSlackMax + kHalfElems + kCandMargin
 constexpr int kOnePassMaxKeff = 256;      // shortlists up to this filter a stage in one pass
 constexpr int kCandRegs = (kCandCap + kNC - 1) / kNC;
@@ -137,6 +138,12 @@ struct Args {
     int32_t slice;  // columns per slice (multiple of 4)
     int32_t n_units;
     int32_t mode;   // 0: zs_sample (blocks in handle scratch); 1: vocab shard (caller's blocks)
+    // Speculative thresholds: units whose guess was too high are listed here
+    // (fail_count, fail_units) and redone by a second launch with
+    // `redo` set, which takes its units from that list and does not speculate.
+    unsigned* fail_count;
+    int32_t* fail_units;
+    int32_t redo;
     uint8_t* part;  // partial blocks [B][S]
     int64_t part_stride;
     int* status;
@@ -440,26 +447,77 @@ __device__ __forceinline__ float tau_value(uint64_t tau_key) {
 // key.  Exact order comes later from the final sort.
 constexpr uint32_t kGroupMaxK = kNC;
 
+__device__ __forceinline__ void select_bucket(CandState& st, uint32_t need, int lane);
+
 // kk-th largest of the per-thread proposals (0 = no key); 0 when fewer than kk
-// threads proposed a key.  Ends synchronised; every thread gets the result.
-__device__ __forceinline__ uint64_t kth_of_proposals(CandState& st, uint64_t mine, uint32_t kk,
-                                                     int ctid) {
-    uint64_t* prop = st.prop;
-    prop[ctid] = mine;
+// threads proposed a key.  The proposals go to shared memory and warp 0 alone
+// runs an exact radix select over them (8 keys per lane, warp-private
+// histogram), so the block pays two barriers.  Every thread gets the result.
+__device__ uint64_t kth_of_proposals(CandState& st, uint64_t mine, uint32_t kk, int ctid) {
+    const int lane = ctid & 31, warp = ctid >> 5;
+    st.prop[ctid] = mine;
     csync();
-    uint32_t rank = 0;
-    if (mine != 0ull)
-        for (int j = 0; j < kNC; ++j) rank += prop[j] > mine ? 1u : 0u;
-    if (mine != 0ull && rank == kk - 1) st.thr = mine;
-    const unsigned have = __popc(__ballot_sync(kFull, mine != 0ull));
-    if ((ctid & 31) == 0) st.scan[ctid >> 5] = have;
-    csync();
-    uint32_t total = 0;
+    if (warp == 0) {
+        constexpr int Q = kNC / 32;
+        uint64_t k[Q];
+        uint64_t lo = ~0ull, hi = 0ull;
+        uint32_t have = 0;
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) total += st.scan[w];
-    const uint64_t T = total >= kk ? st.thr : 0ull;
+        for (int q = 0; q < Q; ++q) {
+            k[q] = st.prop[lane + 32 * q];
+            if (k[q]) {
+                lo = k[q] < lo ? k[q] : lo;
+                hi = k[q] > hi ? k[q] : hi;
+                ++have;
+            }
+        }
+        lo = warp_min_u64(lo);
+        hi = warp_max_u64(hi);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) have += __shfl_xor_sync(kFull, have, o);
+        uint64_t T = 0ull;
+        if (have >= kk) {
+            if (kk == 1) {
+                T = hi;
+            } else {
+                const uint64_t diff = lo ^ hi;
+                int shift = diff ? ((63 - __clzll((long long)diff)) >> 3) << 3 : 0;
+                uint64_t mask = shift >= 56 ? 0ull : (~0ull << (shift + 8));
+                uint64_t prefix = lo & mask;
+                uint32_t need = kk;
+                for (;;) {
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) st.hist[lane * 8 + q] = 0u;
+                    __syncwarp();
+#pragma unroll
+                    for (int q = 0; q < Q; ++q) {
+                        const bool in = k[q] != 0ull && (k[q] & mask) == prefix;
+                        const uint32_t d = in ? ((uint32_t)(k[q] >> shift) & 255u) : 256u + lane;
+                        const unsigned peers = __match_any_sync(kFull, d);
+                        if (in && (__ffs(peers) - 1) == lane) atomicAdd(&st.hist[d], (uint32_t)__popc(peers));
+                    }
+                    __syncwarp();
+                    select_bucket(st, need, lane);
+                    __syncwarp();
+                    const uint32_t digit = st.sel_digit, above = st.sel_above, cnt = st.sel_cnt;
+                    __syncwarp();
+                    prefix |= (uint64_t)digit << shift;
+                    mask |= 0xffull << shift;
+                    need -= above;
+                    if (cnt == need || shift == 0) break;  // whole bucket in: its minimum is the kk-th
+                    shift -= 8;
+                }
+                uint64_t m = ~0ull;
+#pragma unroll
+                for (int q = 0; q < Q; ++q)
+                    if (k[q] != 0ull && (k[q] & mask) == prefix && k[q] < m) m = k[q];
+                T = warp_min_u64(m);
+            }
+        }
+        if (lane == 0) st.thr = T;
+    }
     csync();
-    return T;
+    return st.thr;
 }
 
 // Warp 0 finds the radix bucket holding the need-th largest key: hist[] holds
@@ -925,7 +983,9 @@ __device__ void producer_loop(FastSmem& sm, const Args& a) {
     uint32_t pending = 0u;  // stages with a copy issued whose completion we have not seen
     uint32_t pend_parity = 0u;
     bool ok = true;
-    for (int u = blockIdx.x; u < a.n_units && ok; u += gridDim.x) {
+    const int n_work = a.redo ? (int)*(volatile unsigned*)a.fail_count : a.n_units;
+    for (int w = blockIdx.x; w < n_work && ok; w += gridDim.x) {
+        const int u = a.redo ? a.fail_units[w] : w;
         const int row = u / a.S;
         const RowPlan rp = plan_row(load_params(a.row_params, a.shared, row), a.V_total, a.hist,
                                     a.hist_len, a.hist_ld, row);
@@ -989,10 +1049,19 @@ __device__ void producer_loop(FastSmem& sm, const Args& a) {
 // exact selection, order and draw happen in zs_merge_kernel.
 template <bool LSE>
 __device__ void end_unit(FastSmem& sm, const Args& a, const RowPlan& rp, const UnitGeom& g,
-                         float lm, float ls, float lc, int ctid) {
+                         float lm, float ls, float lc, bool spec_used, int32_t unit, int ctid) {
     CandState& st = sm.st;
     uint32_t n = st.count;
-    if (n > (uint32_t)rp.keff) {
+    // Every key of the unit at or above the speculative threshold is here; with
+    // fewer than keff of them the unit's top-keff is incomplete: queue a redo.
+    if (spec_used && n < (uint32_t)rp.keff && ctid == 0) {
+        const unsigned slot = atomicAdd(a.fail_count, 1u);
+        a.fail_units[slot] = unit;
+    }
+    // Shrink only when the block could not hold the candidates plus the penalty
+    // appends; the merge kernel selects exactly anyway.
+    const uint32_t block_keys = (uint32_t)((a.part_stride - kPartialHeaderBytes) / 8);
+    if (n > (uint32_t)rp.keff && n + (uint32_t)rp.win > block_keys) {
         compact_select(st, n, (uint32_t)rp.keff, ctid);
         n = st.count;
     }
@@ -1117,8 +1186,12 @@ __device__ __forceinline__ void filter_range(CandState& st, const float4* t4, in
         }
         const bool h0 = ok0 && ((v0.x >= tau_f) | (v0.y >= tau_f) | (v0.z >= tau_f) | (v0.w >= tau_f));
         const bool h1 = ok1 && ((v1.x >= tau_f) | (v1.y >= tau_f) | (v1.z >= tau_f) | (v1.w >= tau_f));
-        if (h0) append_lane(st, v0, gid0 + 4 * j0, tau_key, tau_f);
-        if (h1) append_lane(st, v1, gid0 + 4 * j1, tau_key, tau_f);
+        // A warp-uniform branch around the rare append path: without the vote the
+        // compiler predicates it, and every warp issues it on every step.
+        if (__any_sync(kFull, h0 | h1)) {
+            if (h0) append_lane(st, v0, gid0 + 4 * j0, tau_key, tau_f);
+            if (h1) append_lane(st, v1, gid0 + 4 * j1, tau_key, tau_f);
+        }
     }
 }
 
@@ -1148,6 +1221,13 @@ __device__ void consumer_loop(FastSmem& sm, const Args& a, int ctid) {
     float lm = -INFINITY, ls = 0.0f, lc = 1.4426950408889634f;
     uint32_t compact_at = (uint32_t)(kCandCap - kTileElems - kCandMargin);
     bool two_pass = false;
+    // Speculative threshold: after the first stage, raise the threshold to the
+    // spec_k-th best key seen so far (spec_k well below keff, scaled by the share
+    // of the unit that stage covers).  If fewer than keff keys of the unit end up
+    // above it, the guess was too high and the unit is redone without it.
+    bool spec_pending = false, spec_used = false;
+    uint32_t spec_k = 0;
+    int32_t cur_unit = 0;
     RowPlan rp;
     UnitGeom g;
     rp.fast = false;
@@ -1178,9 +1258,19 @@ __device__ void consumer_loop(FastSmem& sm, const Args& a, int ctid) {
             ls = 0.0f;
             lc = (rp.greedy ? 1.0f : 1.0f / rp.p.temp) * 1.4426950408889634f;
             two_pass = rp.keff > kOnePassMaxKeff;
+            cur_unit = md.unit;
+            {
+                const uint64_t n_unit = (uint64_t)(g.v1 - g.v0);
+                const uint64_t n_first = (uint64_t)md.n + (uint64_t)(g.e0 - g.v0);
+                spec_k = n_unit ? (uint32_t)(((uint64_t)rp.keff * n_first * 8 + n_unit - 1) / n_unit) + 8u
+                                : 0u;
+                spec_pending = !a.redo && n_unit >= 4ull * (uint64_t)rp.keff &&
+                               spec_k < (uint32_t)rp.keff;
+                spec_used = false;
+            }
             compact_at = min((uint32_t)(kCandCap - (two_pass ? kHalfElems : kTileElems) - kCandMargin),
                              (uint32_t)rp.keff + slack_for((uint32_t)rp.keff) +
-                                 (uint32_t)max(rp.keff, kCompactMinGrowth));
+                                 (uint32_t)max(rp.keff, two_pass ? kCompactMinGrowth : kCompactGrowthSmall));
             row_logits = a.logits + (int64_t)g.row * a.ld;
             for (int i = g.v0 + ctid; i < g.e0; i += kNC) {
                 const float x = row_logits[i];
@@ -1239,10 +1329,18 @@ __device__ void consumer_loop(FastSmem& sm, const Args& a, int ctid) {
         if (!stage_ready(sm, stage, fparity, a, ctid, want, compact_now)) return;
         if (ctid == 0) mbar_arrive(&sm.empty[prev]);  // everyone is done with ring[prev]
         if (last) {
-            end_unit<LSE>(sm, a, rp, g, lm, ls, lc, ctid);
+            end_unit<LSE>(sm, a, rp, g, lm, ls, lc, spec_used, cur_unit, ctid);
             tau_key = 0ull;
             tau_f = -INFINITY;
             csync();
+        } else if (spec_pending) {
+            spec_pending = false;
+            const uint32_t n = st.count;  // stable: every append of the stage is in
+            if (n > spec_k) {
+                tau_key = compact_select(st, n, spec_k, ctid);
+                tau_f = tau_value(tau_key);
+                spec_used = true;
+            }
         } else if (compact_now) {
             tau_key = compact_select(st, st.count, (uint32_t)rp.keff, ctid);
             tau_f = tau_value(tau_key);
@@ -1292,6 +1390,316 @@ __global__ void __launch_bounds__(kNC) zs_merge_kernel(const MergeArgs a) {
         finalize_row(st, st.cand, reinterpret_cast<double*>(st.cand + kProbOffset), kk, rp, x0n,
                      LSE, mm, ss, row, a.rng, a.out_ids, a.info, a.cand_ids, a.cand_probs,
                      a.cand_ld, ctid);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Warp-per-row merge for shortlists up to kWarpMergeMaxK: each warp merges one
+// row's partial blocks in its own shared-memory slot with warp-synchronous
+// steps only (no block barriers), so a CTA keeps eight rows in flight.
+// ---------------------------------------------------------------------------
+constexpr int kWarpCap = 1024;              // candidate keys per warp
+constexpr uint32_t kWarpMergeMaxK = 256;
+constexpr int kWarpProbOffset = 512;        // f64 probabilities alias cand[512..768)
+
+struct WarpSlot {
+    uint64_t cand[kWarpCap];
+    uint32_t hist[256];
+};
+
+struct WarpMergeSmem {
+    WarpSlot w[kConsumerWarps];
+};
+
+// The digit bucket holding the need-th largest key, from 256 per-digit counts.
+__device__ __forceinline__ void warp_pick_bucket(const uint32_t* hist, uint32_t need, int lane,
+                                                 uint32_t& digit, uint32_t& above, uint32_t& cnt) {
+    uint32_t h[8];
+    uint32_t sum = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        h[q] = hist[255 - 8 * lane - q];
+        sum += h[q];
+    }
+    uint32_t incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += t;
+    }
+    const uint32_t before = incl - sum;
+    const bool mine = before < need && incl >= need;
+    uint32_t d = 0, ab = 0, c = 0, cum = before;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        if (mine && cum < need && cum + h[q] >= need) {
+            d = 255u - 8u * (uint32_t)lane - (uint32_t)q;
+            ab = cum;
+            c = h[q];
+        }
+        cum += h[q];
+    }
+    const int src = __ffs(__ballot_sync(kFull, mine)) - 1;
+    digit = __shfl_sync(kFull, d, src);
+    above = __shfl_sync(kFull, ab, src);
+    cnt = __shfl_sync(kFull, c, src);
+}
+
+// Exact kk-th largest of the unique keys keys[0..n), n > kk >= 1.
+__device__ uint64_t warp_kth(const uint64_t* keys, uint32_t n, uint32_t kk, uint32_t* hist,
+                             int lane) {
+    uint64_t lo = ~0ull, hi = 0ull;
+    for (uint32_t i = lane; i < n; i += 32) {
+        const uint64_t k = keys[i];
+        lo = k < lo ? k : lo;
+        hi = k > hi ? k : hi;
+    }
+    lo = warp_min_u64(lo);
+    hi = warp_max_u64(hi);
+    if (kk == 1) return hi;
+    const uint64_t diff = lo ^ hi;
+    int shift = diff ? ((63 - __clzll((long long)diff)) >> 3) << 3 : 0;
+    uint64_t mask = shift >= 56 ? 0ull : (~0ull << (shift + 8));
+    uint64_t prefix = lo & mask;
+    uint32_t need = kk;
+    for (;;) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) hist[lane * 8 + q] = 0u;
+        __syncwarp();
+        for (uint32_t b = 0; b < n; b += 32) {
+            const uint32_t i = b + lane;
+            const uint64_t k = i < n ? keys[i] : 0ull;
+            const bool in = i < n && (k & mask) == prefix;
+            const uint32_t d = in ? ((uint32_t)(k >> shift) & 255u) : 256u + lane;
+            const unsigned peers = __match_any_sync(kFull, d);
+            if (in && (__ffs(peers) - 1) == lane) atomicAdd(&hist[d], (uint32_t)__popc(peers));
+        }
+        __syncwarp();
+        uint32_t digit, above, cnt;
+        warp_pick_bucket(hist, need, lane, digit, above, cnt);
+        __syncwarp();
+        prefix |= (uint64_t)digit << shift;
+        mask |= 0xffull << shift;
+        need -= above;
+        if (cnt == need || shift == 0) break;  // the whole bucket is in: its minimum is the kk-th
+        shift -= 8;
+    }
+    uint64_t m = ~0ull;
+    for (uint32_t i = lane; i < n; i += 32) {
+        const uint64_t k = keys[i];
+        if ((k & mask) == prefix && k < m) m = k;
+    }
+    return warp_min_u64(m);
+}
+
+// Keeps the keys >= T of keys[0..n) at the front (in order); returns how many.
+__device__ uint32_t warp_keep(uint64_t* keys, uint32_t n, uint64_t T, int lane) {
+    uint32_t out = 0;
+    const unsigned below = lanemask_lt();
+    for (uint32_t b = 0; b < n; b += 32) {
+        const uint32_t i = b + lane;
+        const uint64_t k = i < n ? keys[i] : 0ull;
+        const bool keep = i < n && k >= T;
+        const unsigned m = __ballot_sync(kFull, keep);
+        __syncwarp();
+        if (keep) keys[out + __popc(m & below)] = k;
+        out += __popc(m);
+        __syncwarp();
+    }
+    return out;
+}
+
+// Sorts keys[0..n) descending, n <= kWarpMergeMaxK (unique keys: rank counting).
+__device__ void warp_sort_desc(uint64_t* keys, uint32_t n, int lane) {
+    constexpr int Q = kWarpMergeMaxK / 32;
+    uint64_t k[Q];
+    uint32_t r[Q];
+#pragma unroll
+    for (int q = 0; q < Q; ++q) {
+        const uint32_t i = lane + 32 * q;
+        k[q] = i < n ? keys[i] : 0ull;
+        r[q] = 0;
+    }
+    for (uint32_t j = 0; j < n; ++j) {
+        const uint64_t kj = keys[j];
+#pragma unroll
+        for (int q = 0; q < Q; ++q) r[q] += kj > k[q] ? 1u : 0u;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < Q; ++q)
+        if (lane + 32 * q < (int)n) keys[r[q]] = k[q];
+    __syncwarp();
+}
+
+// f64 tail of sample_token (src/sample.cpp:52-101) over the sorted shortlist
+// cand[0..kk), by one warp: the same expressions and summation order as
+// finalize_row (sequential sums on lane 0).
+__device__ void warp_finalize(const uint64_t* cand, double* prob, uint32_t kk, const RowPlan& rp,
+                              bool x0_nan, bool have_lse, float lse_m, float lse_s, int row,
+                              uint64_t* rng, int32_t* out_ids, RowInfo* info, int32_t* cand_ids,
+                              double* cand_probs, int32_t cand_ld, int lane) {
+    const Params& p = rp.p;
+    const double qnan = __longlong_as_double(0x7ff8000000000000ll);
+    if (rp.greedy) {
+        if (lane == 0) {
+            const int32_t id = (x0_nan || kk == 0) ? 0 : key_id(cand[0]);
+            if (out_ids) out_ids[row] = id;
+            if (info) {
+                RowInfo ri;
+                ri.max_logit = x0_nan ? __int_as_float(0x7fc00000) : (kk ? key_value(cand[0]) : 0.0f);
+                ri.k = 0;
+                ri.m = 0;
+                ri.pos = -1;
+                ri.r = 0.0;
+                ri.sum = 0.0;
+                ri.boundary = 0.0;
+                ri.log_z = (have_lse && !x0_nan)
+                               ? log((double)lse_s) + ((double)lse_m - (double)ri.max_logit)
+                               : qnan;
+                info[row] = ri;
+            }
+        }
+        __syncwarp();
+        return;
+    }
+    const float inv_temp = 1.0f / p.temp;
+    const float max_l = (x0_nan || kk == 0) ? __int_as_float(0x7fc00000) : key_value(cand[0]);
+    for (uint32_t i = lane; i < kk; i += 32)
+        prob[i] = exp(((double)key_value(cand[i]) - (double)max_l) * (double)inv_temp);
+    __syncwarp();
+    double sum = 0.0;
+    if (lane == 0)
+        for (uint32_t i = 0; i < kk; ++i) sum += prob[i];
+    sum = __shfl_sync(kFull, sum, 0);
+    for (uint32_t i = lane; i < kk; i += 32) {
+        const double pi = prob[i] / sum;
+        prob[i] = pi;
+        if ((int32_t)i < cand_ld) {
+            if (cand_ids) cand_ids[(int64_t)row * cand_ld + i] = key_id(cand[i]);
+            if (cand_probs) cand_probs[(int64_t)row * cand_ld + i] = pi;
+        }
+    }
+    __syncwarp();
+    const bool nucleus = p.top_p < 1.0f;
+    int m = (int)kk;
+    double rescale = 1.0;
+    if (lane == 0 && nucleus) {
+        double acc = 0.0;
+        m = 0;
+        while (m < (int)kk && acc < (double)p.top_p) {
+            acc += prob[m];
+            ++m;
+        }
+        if (m == 0) m = 1;
+        rescale = 0.0;
+        for (int i = 0; i < m; ++i) rescale += prob[i];
+    }
+    m = __shfl_sync(kFull, m, 0);
+    rescale = __shfl_sync(kFull, rescale, 0);
+    if (nucleus) {
+        for (int i = lane; i < m; i += 32) prob[i] /= rescale;
+        __syncwarp();
+    }
+    if (lane == 0) {
+        uint64_t st = rng[row];
+        const double r = rng_uniform(st);
+        rng[row] = st;
+        double acc = 0.0, prev = 0.0;
+        int pos = m - 1;
+        bool hit = false;
+        for (int i = 0; i < m; ++i) {
+            prev = acc;
+            acc += prob[i];
+            if (r < acc) {
+                pos = i;
+                hit = true;
+                break;
+            }
+        }
+        double d;
+        if (hit) {
+            const double da = r - prev, db = acc - r;
+            d = da < db ? da : db;
+        } else {
+            d = r - acc;
+        }
+        if (out_ids) out_ids[row] = (kk == 0) ? 0 : key_id(cand[pos < 0 ? 0 : pos]);
+        if (info) {
+            RowInfo ri;
+            ri.max_logit = max_l;
+            ri.k = (int32_t)kk;
+            ri.m = m;
+            ri.pos = pos;
+            ri.r = r;
+            ri.sum = sum;
+            ri.boundary = d;
+            ri.log_z = (have_lse && !x0_nan)
+                           ? log((double)lse_s) + ((double)lse_m - (double)max_l) * (double)inv_temp
+                           : qnan;
+            info[row] = ri;
+        }
+    }
+    __syncwarp();
+}
+
+template <bool LSE>
+__global__ void __launch_bounds__(kNC) zs_warp_merge_kernel(const MergeArgs a) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    WarpMergeSmem& sm = *reinterpret_cast<WarpMergeSmem*>(smem_raw);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    WarpSlot& ws = sm.w[warp];
+    const uint32_t block_cap = (uint32_t)((a.part_stride - kPartialHeaderBytes) / 8);
+    const unsigned below = lanemask_lt();
+    for (int row = blockIdx.x * kConsumerWarps + warp; row < a.B; row += gridDim.x * kConsumerWarps) {
+        const RowPlan rp = plan_row(load_params(a.row_params, a.shared, row), a.V_total, a.hist,
+                                    a.hist_len, a.hist_ld, row);
+        if (!rp.fast) continue;  // drawn by zs_large_kernel
+        const uint32_t ksel = (uint32_t)rp.ksel;
+        const float lc = (rp.greedy ? 1.0f : 1.0f / rp.p.temp) * 1.4426950408889634f;
+        uint32_t count = 0;
+        uint64_t tau = 0ull;
+        float M = -INFINITY, Sx = 0.0f;
+        bool nan0 = false;
+        for (int g = 0; g < a.G; ++g) {
+            for (int s = 0; s < a.S; ++s) {
+                const uint8_t* pp = a.gathered + (int64_t)g * a.rank_stride +
+                                    ((int64_t)row * a.S + s) * a.part_stride;
+                uint4 hv = make_uint4(0u, 0u, 0u, 0u);
+                if (lane == 0) hv = __ldcg(reinterpret_cast<const uint4*>(pp));
+                hv.x = __shfl_sync(kFull, hv.x, 0);
+                hv.y = __shfl_sync(kFull, hv.y, 0);
+                hv.z = __shfl_sync(kFull, hv.z, 0);
+                hv.w = __shfl_sync(kFull, hv.w, 0);
+                const uint32_t cnt = hv.x < block_cap ? hv.x : block_cap;
+                lse_merge(M, Sx, __uint_as_float(hv.z), __uint_as_float(hv.w), lc);
+                if ((hv.y & kPartHasId0) && (hv.y & kPartX0Nan)) nan0 = true;
+                const unsigned long long* keys =
+                    reinterpret_cast<const unsigned long long*>(pp + kPartialHeaderBytes);
+                for (uint32_t b = 0; b < cnt; b += 32) {
+                    if (count + 32 > (uint32_t)kWarpCap) {
+                        tau = warp_kth(ws.cand, count, ksel, ws.hist, lane);
+                        count = warp_keep(ws.cand, count, tau, lane);  // exactly ksel keys >= tau
+                    }
+                    const uint32_t i = b + lane;
+                    const uint64_t k = i < cnt ? __ldcg(keys + i) : 0ull;
+                    const bool pass = k > tau;
+                    const unsigned m = __ballot_sync(kFull, pass);
+                    if (pass) ws.cand[count + __popc(m & below)] = k;
+                    count += __popc(m);
+                    __syncwarp();
+                }
+            }
+        }
+        if (count > ksel) {
+            const uint64_t T = warp_kth(ws.cand, count, ksel, ws.hist, lane);
+            count = warp_keep(ws.cand, count, T, lane);
+        }
+        warp_sort_desc(ws.cand, count, lane);
+        const uint32_t kk = count < ksel ? count : ksel;
+        warp_finalize(ws.cand, reinterpret_cast<double*>(ws.cand + kWarpProbOffset), kk, rp, nan0,
+                      LSE, M, Sx, row, a.rng, a.out_ids, a.info, a.cand_ids, a.cand_probs,
+                      a.cand_ld, lane);
     }
 }
 

@@ -148,6 +148,7 @@ struct zs_context {
     int select_ctas = 0;
     size_t select_smem = 0;
     size_t merge_smem = 0;
+    size_t warp_merge_smem = 0;
     // scratch, grown on demand (never shrinks)
     uint8_t* part = nullptr;
     size_t part_bytes = 0;
@@ -158,6 +159,9 @@ struct zs_context {
     size_t large_bytes = 0;
     uint8_t* gather = nullptr;  // zs_sample_sharded send + receive blocks
     size_t gather_bytes = 0;
+    unsigned* fail_count = nullptr;  // units whose speculative threshold was too high
+    int32_t* fail_units = nullptr;
+    size_t fail_units_n = 0;
 };
 
 namespace {
@@ -222,8 +226,32 @@ zs::Params to_dev(const zs_params& p) {
 // (row, slice); zs_merge_kernel then merges each row's blocks, sorts the
 // shortlist and draws.  Rows needing the large shortlist path follow in
 // zs_large_kernel.
+// Merge launch: one warp per row when every shortlist fits a warp slot and the
+// batch gives every SM at least four such warps; otherwise one CTA per row (a
+// small batch has many slices per row and too few rows to fill the GPU by warps).
+zs_status launch_merge(zs_context* h, const zs::MergeArgs& m, int max_ksel, bool want_lse,
+                       cudaStream_t st) {
+    if ((uint32_t)max_ksel <= zs::kWarpMergeMaxK && m.B >= 4 * h->num_sms) {
+        const int rows_per_cta = zs::kConsumerWarps;
+        const int grid = std::max(1, std::min((m.B + rows_per_cta - 1) / rows_per_cta, 8 * h->num_sms));
+        if (want_lse)
+            zs::zs_warp_merge_kernel<true><<<grid, zs::kNC, h->warp_merge_smem, st>>>(m);
+        else
+            zs::zs_warp_merge_kernel<false><<<grid, zs::kNC, h->warp_merge_smem, st>>>(m);
+    } else {
+        const int grid = std::max(1, std::min(m.B, 4 * h->num_sms));
+        if (want_lse)
+            zs::zs_merge_kernel<true><<<grid, zs::kNC, h->merge_smem, st>>>(m);
+        else
+            zs::zs_merge_kernel<false><<<grid, zs::kNC, h->merge_smem, st>>>(m);
+    }
+    ZS_CUDA(cudaGetLastError());
+    return ZS_OK;
+}
+
 zs_status launch_select(zs_context* h, const zs::Args& base, const Plan& pl, bool want_lse,
                         cudaStream_t st) {
+    zs_status s_status_ = ZS_OK;
     zs::Args a = base;
     a.S = pl.S;
     a.slice = pl.slice;
@@ -236,12 +264,27 @@ zs_status launch_select(zs_context* h, const zs::Args& base, const Plan& pl, boo
         if (s != ZS_OK) return s;
         a.part = h->part;
     }
+    if ((size_t)a.n_units > h->fail_units_n) {
+        if (h->fail_units) cudaFree(h->fail_units);
+        h->fail_units = nullptr;
+        h->fail_units_n = 0;
+        const size_t n = std::max((size_t)a.n_units, (size_t)4096);
+        ZS_CUDA(cudaMalloc((void**)&h->fail_units, n * sizeof(int32_t)));
+        h->fail_units_n = n;
+    }
+    a.fail_count = h->fail_count;
+    a.fail_units = h->fail_units;
+    a.redo = 0;
+    ZS_CUDA(cudaMemsetAsync(h->fail_count, 0, sizeof(unsigned), st));
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(a.n_units, h->select_ctas));
-    if (want_lse)
-        zs::zs_select_kernel<true><<<grid, zs::kThreads, h->select_smem, st>>>(a);
-    else
-        zs::zs_select_kernel<false><<<grid, zs::kThreads, h->select_smem, st>>>(a);
-    ZS_CUDA(cudaGetLastError());
+    for (int pass = 0; pass < 2; ++pass) {
+        a.redo = pass;  // pass 1 redoes the units listed by pass 0 (usually none)
+        if (want_lse)
+            zs::zs_select_kernel<true><<<grid, zs::kThreads, h->select_smem, st>>>(a);
+        else
+            zs::zs_select_kernel<false><<<grid, zs::kThreads, h->select_smem, st>>>(a);
+        ZS_CUDA(cudaGetLastError());
+    }
     if (split) {
         zs::MergeArgs m;
         std::memset(&m, 0, sizeof(m));
@@ -264,12 +307,8 @@ zs_status launch_select(zs_context* h, const zs::Args& base, const Plan& pl, boo
         m.cand_probs = a.cand_probs;
         m.cand_ld = a.cand_ld;
         m.status = h->status;
-        const int mgrid = std::max(1, std::min(a.B, 4 * h->num_sms));
-        if (want_lse)
-            zs::zs_merge_kernel<true><<<mgrid, zs::kNC, h->merge_smem, st>>>(m);
-        else
-            zs::zs_merge_kernel<false><<<mgrid, zs::kNC, h->merge_smem, st>>>(m);
-        ZS_CUDA(cudaGetLastError());
+        s_status_ = launch_merge(h, m, pl.max_ksel, want_lse, st);
+        if (s_status_ != ZS_OK) return s_status_;
     }
     if (pl.any_large) {
         if (a.mode != 0)
@@ -330,6 +369,7 @@ zs_status zs_create(int device, zs_handle* out) {
     h->num_sms = prop.multiProcessorCount;
     h->select_smem = sizeof(zs::FastSmem);
     h->merge_smem = sizeof(zs::CandState);
+    h->warp_merge_smem = sizeof(zs::WarpMergeSmem);
     auto cleanup = [&](zs_status s) {
         delete h;
         return s;
@@ -340,7 +380,9 @@ zs_status zs_create(int device, zs_handle* out) {
         (e = cudaFuncSetAttribute(zs::zs_merge_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->merge_smem)) != cudaSuccess ||
         (e = cudaFuncSetAttribute(zs::zs_merge_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->merge_smem)) != cudaSuccess ||
         (e = cudaFuncSetAttribute(zs::zs_large_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->merge_smem)) != cudaSuccess ||
-        (e = cudaFuncSetAttribute(zs::zs_large_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->merge_smem)) != cudaSuccess)
+        (e = cudaFuncSetAttribute(zs::zs_large_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->merge_smem)) != cudaSuccess ||
+        (e = cudaFuncSetAttribute(zs::zs_warp_merge_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->warp_merge_smem)) != cudaSuccess ||
+        (e = cudaFuncSetAttribute(zs::zs_warp_merge_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->warp_merge_smem)) != cudaSuccess)
         return cleanup(cuda_fail(e, "cudaFuncSetAttribute"));
     int per_sm = 0;
     if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, zs::zs_select_kernel<false>, zs::kThreads, h->select_smem)) != cudaSuccess)
@@ -349,6 +391,8 @@ zs_status zs_create(int device, zs_handle* out) {
     h->select_ctas = h->select_ctas_per_sm * h->num_sms;
     if ((e = cudaMalloc((void**)&h->status, sizeof(int))) != cudaSuccess) return cleanup(cuda_fail(e, "cudaMalloc status"));
     if ((e = cudaMemset(h->status, 0, sizeof(int))) != cudaSuccess) return cleanup(cuda_fail(e, "cudaMemset status"));
+    if ((e = cudaMalloc((void**)&h->fail_count, sizeof(unsigned))) != cudaSuccess) return cleanup(cuda_fail(e, "cudaMalloc fail_count"));
+    if ((e = cudaMemset(h->fail_count, 0, sizeof(unsigned))) != cudaSuccess) return cleanup(cuda_fail(e, "cudaMemset fail_count"));
     *out = h;
     return ZS_OK;
 }
@@ -361,6 +405,8 @@ zs_status zs_destroy(zs_handle h) {
     cudaFree(h->params);
     cudaFree(h->large);
     cudaFree(h->gather);
+    cudaFree(h->fail_count);
+    cudaFree(h->fail_units);
     delete h;
     return ZS_OK;
 }
@@ -543,13 +589,7 @@ zs_status zs_shard_merge(zs_handle h, const void* gathered, int32_t n_ranks, int
         m.cand_ld = (extras->cand_ids || extras->cand_probs) ? extras->cand_ld : 0;
         want_lse = extras->want_log_z && extras->row_info;
     }
-    const int grid = std::max(1, std::min(batch, 4 * h->num_sms));
-    if (want_lse)
-        zs::zs_merge_kernel<true><<<grid, zs::kNC, h->merge_smem, st>>>(m);
-    else
-        zs::zs_merge_kernel<false><<<grid, zs::kNC, h->merge_smem, st>>>(m);
-    ZS_CUDA(cudaGetLastError());
-    return ZS_OK;
+    return launch_merge(h, m, pl.max_ksel, want_lse, st);
 }
 
 zs_status zs_sample_sharded(zs_handle h, const float* logits_local, int64_t ld, int32_t batch,
