@@ -167,6 +167,46 @@ zs_status zs_sample_sharded(zs_handle h, const float* logits_local, int64_t ld, 
                             const int32_t* history_len, uint64_t* rng_state, int32_t* out_ids,
                             const zs_extras* extras, void* nccl_comm, void* stream);
 
+/* ---------------------------------------------------------------------------------
+ * zs_sample_noalloc: zs_sample without any memory allocation.  No counterpart in
+ * the reference (sample_token needs no device scratch).
+ *
+ * For callers that must not allocate while they sample: a serving loop that gave
+ * nearly all device memory to its KV-cache pool at start-up has nothing left for
+ * a library's cudaMalloc in mid-run, and a cudaFree in a decode step waits for the
+ * whole device.  This call uses a fixed scratch of ZS_NOALLOC_SCRATCH_BYTES in
+ * static device memory of the library instead, and calls no allocating routine.
+ *
+ * Same kernels and results as zs_sample with one shared zs_params, on the CURRENT
+ * device (no handle).  Differences:
+ *   - a row's candidate blocks must fit the scratch: a small batch is cut into
+ *     fewer vocabulary slices than zs_sample would use when needed, and a batch
+ *     that does not fit even at one slice per row is rejected with
+ *     ZS_ERR_INVALID_ARGUMENT before anything is launched (without a repeat
+ *     penalty that is above about 9,600 rows at top_k 50, 5,400 at the default
+ *     shortlist of 256, 2,700 at top_k 1024);
+ *   - rows whose top_k + repeat window exceed 2048, or whose window exceeds 512,
+ *     are rejected (that path needs a workspace sized by the vocabulary);
+ *   - no extras (row info, candidate lists).
+ * device_status: NULL, or a device int32 the caller zeroes before first use; a
+ *   kernel that gives up on a bounded wait stores ZS_ERR_DEVICE_TIMEOUT there.
+ * Each call clears the scratch's fail counter itself (cudaMemsetAsync on `stream`);
+ *   nothing else in the scratch needs to start at zero.
+ * The first call on a device does a one-time set-up (kernel attributes, the
+ *   scratch address); when that happens lazily, make the first call before any
+ *   stream capture starts.
+ * There is ONE scratch per device: calls in flight at the same time on one device
+ *   (other streams, other threads) race on it and corrupt each other's results.
+ *   Order them, e.g. by issuing them all on one stream.
+ * --------------------------------------------------------------------------------- */
+#define ZS_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+zs_status zs_sample_noalloc(const float* logits, int64_t ld, int32_t batch, int32_t n_vocab,
+                            const zs_params* params, const int32_t* history,
+                            int64_t history_ld, const int32_t* history_len,
+                            uint64_t* rng_state, int32_t* out_ids, int32_t* device_status,
+                            void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -17,6 +17,7 @@ EXPORTS = (
     "zs_create", "zs_destroy", "zs_last_error", "zs_status_string", "zs_abi_version",
     "zs_rng_seed", "zs_sample", "zs_argmax", "zs_check_device_status",
     "zs_shard_partial_bytes", "zs_shard_partials", "zs_shard_merge", "zs_sample_sharded",
+    "zs_sample_noalloc",
 )
 
 ZS_OK = 0
@@ -74,12 +75,14 @@ def lib() -> C.CDLL:
                                  C.POINTER(ZsExtras), vp]
     L.zs_sample_sharded.argtypes = [vp, vp, i64, i32, i32, i32, i32, i32, C.POINTER(ZsParams), i32,
                                     vp, i64, vp, vp, vp, C.POINTER(ZsExtras), vp, vp]
+    L.zs_sample_noalloc.argtypes = [vp, i64, i32, i32, C.POINTER(ZsParams), vp, i64, vp, vp, vp,
+                                    vp, vp]
     for name in EXPORTS:
         f = getattr(L, name)
         if f.restype is C.c_int or name in ("zs_create", "zs_destroy", "zs_sample", "zs_argmax",
                                             "zs_check_device_status", "zs_shard_partial_bytes",
                                             "zs_shard_partials", "zs_shard_merge",
-                                            "zs_sample_sharded"):
+                                            "zs_sample_sharded", "zs_sample_noalloc"):
             f.restype = C.c_int
     _lib = L
     return L

@@ -24,7 +24,7 @@ INCLUDE = os.path.join(ROOT, "include")
 SAMPLER_SO = os.path.join(HERE, "libzs_sampler.so")
 WORKLOAD_SO = os.path.join(HERE, "libzs_workload.so")
 
-SAMPLER_SOURCES = ["zs_sampler.cu", "sample_shim.cpp"]
+SAMPLER_SOURCES = ["zs_sampler.cu", "zs_noalloc_scratch.cu", "sample_shim.cpp"]
 SAMPLER_DEPS = SAMPLER_SOURCES + ["zs_kernels.cuh", "zs_device.cuh"]
 
 NVCC_ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

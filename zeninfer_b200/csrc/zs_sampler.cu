@@ -636,3 +636,169 @@ int zs_debug_read(unsigned long long* out4) {
 #endif
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// zs_sample_noalloc: zs_sample's select and merge kernels over the fixed static
+// scratch of zs_noalloc_scratch.cu.  Nothing here allocates device or host memory.
+// ---------------------------------------------------------------------------
+cudaError_t zs_noalloc_scratch_address(void** ptr);  // zs_noalloc_scratch.cu
+
+namespace {
+
+constexpr int kNoAllocMaxDevices = 64;
+constexpr size_t kNoAllocHeadBytes = 256;  // [0] status word, [4] fail counter
+
+// Per-device launch geometry and scratch address, set up once by the first call
+// on that device.  `ctx` carries only the geometry launch_merge reads; its
+// buffer pointers stay null.
+struct NoAllocDevice {
+    bool ready = false;
+    uint8_t* scratch = nullptr;
+    zs_context ctx;
+};
+NoAllocDevice g_noalloc[kNoAllocMaxDevices];
+std::mutex g_noalloc_mu;
+
+zs_status noalloc_setup(int dev, NoAllocDevice** out) {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    NoAllocDevice& d = g_noalloc[dev];
+    if (!d.ready) {
+        cudaDeviceProp prop;
+        ZS_CUDA(cudaGetDeviceProperties(&prop, dev));
+        if (prop.major != 10) return fail(ZS_ERR_NO_DEVICE, "zs_sample_noalloc: not an sm_100 device");
+        d.ctx.device = dev;
+        d.ctx.num_sms = prop.multiProcessorCount;
+        d.ctx.select_smem = sizeof(zs::FastSmem);
+        d.ctx.merge_smem = sizeof(zs::CandState);
+        d.ctx.warp_merge_smem = sizeof(zs::WarpMergeSmem);
+        ZS_CUDA(cudaFuncSetAttribute(zs::zs_select_kernel<false>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d.ctx.select_smem));
+        ZS_CUDA(cudaFuncSetAttribute(zs::zs_merge_kernel<false>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d.ctx.merge_smem));
+        ZS_CUDA(cudaFuncSetAttribute(zs::zs_warp_merge_kernel<false>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d.ctx.warp_merge_smem));
+        int per_sm = 0;
+        ZS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, zs::zs_select_kernel<false>,
+                                                              zs::kThreads, d.ctx.select_smem));
+        d.ctx.select_ctas_per_sm = std::max(1, per_sm);
+        d.ctx.select_ctas = d.ctx.select_ctas_per_sm * d.ctx.num_sms;
+        void* p = nullptr;
+        ZS_CUDA(zs_noalloc_scratch_address(&p));  // with `dev` current
+        d.scratch = (uint8_t*)p;
+        d.ready = true;
+    }
+    *out = &d;
+    return ZS_OK;
+}
+
+// Scratch bytes for B rows cut into S slices with blocks of `stride` bytes.
+size_t noalloc_bytes(int64_t B, int64_t S, int64_t stride) {
+    const size_t units = (size_t)(B * S);
+    return kNoAllocHeadBytes + ((units * sizeof(int32_t) + 255) & ~(size_t)255) + units * (size_t)stride;
+}
+
+}  // namespace
+
+extern "C" zs_status zs_sample_noalloc(const float* logits, int64_t ld, int32_t batch,
+                                       int32_t n_vocab, const zs_params* params,
+                                       const int32_t* history, int64_t history_ld,
+                                       const int32_t* history_len, uint64_t* rng_state,
+                                       int32_t* out_ids, int32_t* device_status, void* stream) {
+    if (batch < 0) return fail(ZS_ERR_INVALID_ARGUMENT, "batch < 0");
+    if (!params) return fail(ZS_ERR_INVALID_ARGUMENT, "params is null");
+    if (batch == 0) return ZS_OK;
+    if (!out_ids) return fail(ZS_ERR_INVALID_ARGUMENT, "out_ids is null");
+    cudaStream_t st = (cudaStream_t)stream;
+    if (n_vocab <= 0) {  // sample.cpp:34 -- returns 0 before touching the Rng
+        ZS_CUDA(cudaMemsetAsync(out_ids, 0, (size_t)batch * sizeof(int32_t), st));
+        return ZS_OK;
+    }
+    if (!logits) return fail(ZS_ERR_INVALID_ARGUMENT, "logits is null");
+    if (((uintptr_t)logits & 3u) != 0) return fail(ZS_ERR_INVALID_ARGUMENT, "logits not 4-byte aligned");
+    if (ld < n_vocab) return fail(ZS_ERR_INVALID_ARGUMENT, "ld < n_vocab");
+    if (batch > 1 && ld > (int64_t)1 << 40) return fail(ZS_ERR_INVALID_ARGUMENT, "ld too large");
+    if (!rng_state && needs_rng(params, 0, batch))
+        return fail(ZS_ERR_INVALID_ARGUMENT, "rng_state is null");
+    const bool have_hist = history && history_len;
+    if (have_hist && history_ld < 0) return fail(ZS_ERR_INVALID_ARGUMENT, "history_ld < 0");
+    int dev = -1;
+    ZS_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kNoAllocMaxDevices)
+        return fail(ZS_ERR_INVALID_ARGUMENT, "zs_sample_noalloc: device ordinal above 63");
+    NoAllocDevice* d = nullptr;
+    zs_status s = noalloc_setup(dev, &d);
+    if (s != ZS_OK) return s;
+    Plan pl = make_plan(batch, n_vocab, n_vocab, params, 0, d->ctx.select_ctas, have_hist);
+    if (pl.any_large)
+        return fail(ZS_ERR_INVALID_ARGUMENT,
+                    "zs_sample_noalloc: top_k + repeat window above 2048 (or window above 512) "
+                    "needs zs_sample");
+    const size_t cap = ZS_NOALLOC_SCRATCH_BYTES;
+    if (noalloc_bytes(batch, 1, pl.part_stride) > cap) {
+        char msg[256];
+        std::snprintf(msg, sizeof(msg),
+                      "zs_sample_noalloc: %d rows need %zu bytes of scratch, the fixed scratch "
+                      "holds %zu; split the batch or use zs_sample",
+                      batch, noalloc_bytes(batch, 1, pl.part_stride), cap);
+        return fail(ZS_ERR_INVALID_ARGUMENT, msg);
+    }
+    // Fewer slices per row when the default cut does not fit (same results).
+    while (pl.S > 1 && noalloc_bytes(batch, pl.S, pl.part_stride) > cap) {
+        pl.S -= 1;
+        const int per = (n_vocab + pl.S - 1) / pl.S;
+        pl.slice = std::max(4, (per + 3) & ~3);
+        pl.S = std::max(1, (n_vocab + pl.slice - 1) / pl.slice);
+    }
+    const int64_t units = (int64_t)batch * pl.S;
+    if (units > INT32_MAX) return fail(ZS_ERR_INVALID_ARGUMENT, "zs_sample_noalloc: batch too large");
+    uint8_t* head = d->scratch;
+    int32_t* fail_units = (int32_t*)(d->scratch + kNoAllocHeadBytes);
+    uint8_t* part = d->scratch + kNoAllocHeadBytes + (((size_t)units * sizeof(int32_t) + 255) & ~(size_t)255);
+
+    zs::Args a;
+    std::memset(&a, 0, sizeof(a));
+    a.logits = logits;
+    a.ld = ld;
+    a.B = batch;
+    a.V = n_vocab;
+    a.V_total = n_vocab;
+    a.shared = to_dev(params[0]);
+    a.hist = have_hist ? history : nullptr;
+    a.hist_ld = history_ld;
+    a.hist_len = have_hist ? history_len : nullptr;
+    a.rng = rng_state;
+    a.out_ids = out_ids;
+    a.mode = 0;
+    a.S = pl.S;
+    a.slice = pl.slice;
+    a.n_units = (int32_t)units;
+    a.part_stride = pl.part_stride;
+    a.part = part;
+    a.status = device_status ? (int*)device_status : (int*)head;
+    a.fail_count = (unsigned*)(head + 4);
+    a.fail_units = fail_units;
+    // The fail counter must start every call at zero; the status word is cleared too.
+    ZS_CUDA(cudaMemsetAsync(head, 0, kNoAllocHeadBytes, st));
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(units, d->ctx.select_ctas));
+    for (int pass = 0; pass < 2; ++pass) {
+        a.redo = pass;
+        zs::zs_select_kernel<false><<<grid, zs::kThreads, d->ctx.select_smem, st>>>(a);
+        ZS_CUDA(cudaGetLastError());
+    }
+    zs::MergeArgs m;
+    std::memset(&m, 0, sizeof(m));
+    m.gathered = part;
+    m.G = 1;
+    m.S = pl.S;
+    m.part_stride = pl.part_stride;
+    m.B = batch;
+    m.V_total = n_vocab;
+    m.shared = a.shared;
+    m.hist = a.hist;
+    m.hist_ld = a.hist_ld;
+    m.hist_len = a.hist_len;
+    m.rng = rng_state;
+    m.out_ids = out_ids;
+    m.status = a.status;
+    return launch_merge(&d->ctx, m, pl.max_ksel, false, st);
+}
