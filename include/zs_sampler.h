@@ -128,6 +128,19 @@ zs_status zs_argmax(zs_handle h, const float* logits, int64_t ld, int32_t batch,
  * gave up on a bounded wait since the last check (the flag is then cleared). */
 zs_status zs_check_device_status(zs_handle h, void* stream);
 
+/* Per-kernel device time, for measurement.  While timing is on, every kernel this
+ * handle launches is bracketed by CUDA events on its stream.  zs_get_timing waits
+ * for those events, returns the sums since the previous zs_get_timing (or since
+ * timing was switched on) and starts over.  `launches` counts every kernel launch
+ * of the handle in that span, timed or not.  No counterpart in the reference. */
+typedef struct zs_timing {
+    double select_ms, merge_ms, large_ms;              /* summed event time per kernel */
+    int64_t select_launches, merge_launches, large_launches;
+    int64_t launches;
+} zs_timing;
+zs_status zs_set_timing(zs_handle h, int32_t enable);
+zs_status zs_get_timing(zs_handle h, zs_timing* out);
+
 /* ---------------------------------------------------------------------------------
  * Vocab-sharded sampling (tensor-parallel lm_head layout).  Rank g of n_ranks
  * holds columns [vocab_offset, vocab_offset + n_local) of every row.  Each rank

@@ -1,0 +1,190 @@
+"""The oracle (C restatement of src/sample.cpp) pinned against the reference.
+
+Two pins, both on CPU:
+  * tests/golden/sampler_golden.npz -- outputs of the reference's own
+    sample.cpp on seeded cases (tests/golden/make_golden.py); needs nothing at
+    run time but the restatement;
+  * the reference compiled unchanged (oracle/_ref/libzen_ref.so) on fresh
+    seeded rows, where it is built.
+
+Rule: ids equal; where the drawn value occurs more than once in the row the
+reference's shortlist order among equal values (libstdc++ introselect) may pick
+another id, and then the drawn VALUES are equal.  The restatement uses the
+reference's own f64 expressions and summation order, so no boundary tolerance.
+"""
+
+import ctypes as C
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+from zeninfer_b200 import Rng, SamplingParams, rng_seed
+from zeninfer_b200 import workloads as W
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "sampler_golden.npz")
+
+
+@pytest.fixture(scope="module")
+def golden():
+    return np.load(GOLDEN)
+
+
+def _params_of(rec):
+    return SamplingParams(float(rec["temp"]), int(rec["top_k"]), float(rec["top_p"]),
+                          float(rec["repeat_penalty"]), int(rec["repeat_last_n"]))
+
+
+def test_rng_golden(golden):
+    for seed, outs, u in zip(golden["rng_seeds"], golden["rng_next"], golden["rng_uniform"]):
+        r = Rng(int(seed))
+        assert [r.next() for _ in range(8)] == [int(v) for v in outs]
+        assert Rng(int(seed)).uniform() == u
+        st = np.array([rng_seed(int(seed))], dtype=np.uint64)
+        assert oracle.olib().zo_rng_uniform(st.ctypes.data_as(C.POINTER(C.c_uint64))) == u
+
+
+def test_golden_cases(golden):
+    L = golden
+    ties = 0
+    for i in range(len(L["ids"])):
+        n = int(L["n"][i])
+        x = L["logits"][i: i + 1, :n]
+        p = _params_of(L["params"][i])
+        hl = int(L["hist_len"][i])
+        h = L["hist"][i: i + 1] if hl else None
+        hlen = L["hist_len"][i: i + 1] if hl else None
+        st = np.array([rng_seed(int(L["seeds"][i]))], dtype=np.uint64)
+        ids, info, *_ = oracle.oracle_sample(x, p, st, h, hlen, nthreads=1)
+        ref = int(L["ids"][i])
+        if int(ids[0]) != ref:
+            assert L["tie"][i], f"case {i}: oracle {ids[0]} reference {ref} (no tie)"
+            assert x[0, ids[0]] == x[0, ref], f"case {i}: drawn values differ"
+            ties += 1
+        # the rng advanced exactly as the reference's: same next() afterwards
+        nxt = Rng(0)
+        nxt.state = int(st[0])
+        assert nxt.next() == int(L["next_after"][i]), f"case {i}: rng draws differ"
+    assert ties <= int(L["tie"].sum())
+
+
+def test_golden_workload_rows(golden):
+    L = golden
+    for cfg in (1, 2, 3, 4, 5):
+        for sign in (1, -1):
+            sel = np.nonzero(L["wl_cfg"] == sign * cfg)[0]
+            if sel.size == 0:
+                continue
+            rows = int(L["wl_row"][sel].max()) + 1
+            x = W.generate(cfg, rows)
+            wl = W.WORKLOADS[cfg]
+            p = wl.params if sign > 0 else SamplingParams()
+            st = np.array([rng_seed(int(s)) for s in wl.row_seeds(0, rows)], dtype=np.uint64)
+            ids, *_ = oracle.oracle_sample(x, p, st)
+            for j in sel:
+                r = int(L["wl_row"][j])
+                ref = int(L["wl_ids"][j])
+                if ids[r] != ref:
+                    assert L["wl_tie"][j] and x[r, ids[r]] == x[r, ref], (cfg, sign, r)
+
+
+def test_argmax_edges():
+    rng = np.random.default_rng(1)
+    rows = [np.array([np.nan, 1.0, 2.0], np.float32), np.array([1.0, np.nan, 3.0], np.float32),
+            np.array([3.0, 3.0, 1.0], np.float32), np.array([-np.inf, -np.inf], np.float32),
+            np.array([0.0, -0.0, 0.0], np.float32), np.array([np.inf, 1.0, np.inf], np.float32),
+            np.array([5.0], np.float32)]
+    rows += [(np.round(rng.normal(0, 1, 1000) * 4) / 4).astype(np.float32) for _ in range(20)]
+    expect = [0, 2, 0, 0, 0, 0, 0]
+    for i, r in enumerate(rows):
+        o = oracle.oracle_argmax(r)
+        if i < len(expect):
+            assert o == expect[i], (i, o)
+        if oracle.have_reference():
+            assert o == oracle.reference_argmax(r)
+
+
+needs_ref = pytest.mark.skipif(not oracle.have_reference(), reason="reference not built")
+
+
+@needs_ref
+@pytest.mark.parametrize("cfg", [1, 2, 3, 4, 5])
+def test_workloads_against_reference(cfg):
+    """Fresh rows of each workload (full vocabulary), restatement vs reference."""
+    wl = W.WORKLOADS[cfg]
+    rows = 1 if cfg == 1 else 24
+    x = W.generate(cfg, rows, row0=100 if cfg != 1 else 0)
+    seeds = np.arange(1, rows + 1, dtype=np.uint64) * np.uint64(7919)
+    for p in [wl.params] + ([SamplingParams()] if wl.greedy_too else []):
+        st = np.array([rng_seed(int(s)) for s in seeds], dtype=np.uint64)
+        ids, info, *_ = oracle.oracle_sample(x, p, st)
+        ref, nxt = oracle.reference_sample(x, p, seeds)
+        for r in range(rows):
+            if ids[r] != ref[r]:
+                assert np.count_nonzero(x[r] == x[r, ref[r]]) > 1, (cfg, r)
+                assert x[r, ids[r]] == x[r, ref[r]], (cfg, r)
+            s = Rng(0)
+            s.state = int(st[r])
+            assert s.next() == int(nxt[r]), (cfg, r)
+        if cfg != 4:  # continuous values: no ties at all
+            assert np.array_equal(ids, ref)
+
+
+@needs_ref
+def test_penalty_against_reference():
+    rng = np.random.default_rng(11)
+    n, rows = 4096, 64
+    x = rng.normal(0, 2, size=(rows, n)).astype(np.float32)
+    hist = rng.integers(-5, n + 5, size=(rows, 128)).astype(np.int32)
+    hist[:, 10:40] = hist[:, :1]  # one id repeated 31 times: the penalty compounds
+    hlen = rng.integers(0, 129, size=rows).astype(np.int32)
+    seeds = np.arange(rows, dtype=np.uint64) + np.uint64(3)
+    for p in (SamplingParams(temp=0.8, top_k=40, top_p=0.9, repeat_penalty=1.3, repeat_last_n=64),
+              SamplingParams(repeat_penalty=1.5, repeat_last_n=100),
+              SamplingParams(temp=1.0, repeat_penalty=0.7, repeat_last_n=7)):
+        st = np.array([rng_seed(int(s)) for s in seeds], dtype=np.uint64)
+        ids, *_ = oracle.oracle_sample(x, p, st, hist, hlen)
+        ref, _ = oracle.reference_sample(x, p, seeds, hist, hlen)
+        assert np.array_equal(ids, ref)
+
+
+@needs_ref
+def test_per_row_params_against_reference():
+    rng = np.random.default_rng(5)
+    rows, n = 40, 3000
+    x = rng.normal(0, 1.5, size=(rows, n)).astype(np.float32)
+    plist = [SamplingParams(temp=float(rng.uniform(0.0, 2.0)) if r % 5 else 0.0,
+                            top_k=int(rng.integers(0, 400)), top_p=float(rng.uniform(0.3, 1.0)))
+             for r in range(rows)]
+    seeds = np.arange(rows, dtype=np.uint64) + np.uint64(99)
+    st = np.array([rng_seed(int(s)) for s in seeds], dtype=np.uint64)
+    ids, *_ = oracle.oracle_sample(x, plist, st)
+    ref, _ = oracle.reference_sample(x, plist, seeds)
+    assert np.array_equal(ids, ref)
+
+
+def test_restatement_internal_consistency():
+    """Shortlist sorted (value desc, id asc), probabilities sum to 1, the drawn
+    position is the first CDF entry above r, and the boundary is that distance."""
+    rng = np.random.default_rng(3)
+    x = rng.normal(0, 2, size=(16, 5000)).astype(np.float32)
+    p = SamplingParams(temp=0.9, top_k=100, top_p=0.8)
+    st = np.array([rng_seed(i + 1) for i in range(16)], dtype=np.uint64)
+    ids, info, cid, cv, cp = oracle.oracle_sample(x, p, st, cand_ld=100)
+    for r in range(16):
+        order = sorted(range(5000), key=lambda i: (-x[r, i], i))[:100]
+        assert list(cid[r]) == order
+        assert abs(cp[r].sum() - 1.0) < 1e-12
+        m, pos, u = int(info["m"][r]), int(info["pos"][r]), float(info["r"][r])
+        rescale = 0.0
+        for i in range(m):  # sequential, as the reference sums
+            rescale += float(cp[r, i])
+        acc, want = 0.0, m - 1
+        for i in range(m):
+            acc += float(cp[r, i]) / rescale
+            if u < acc:
+                want = i
+                break
+        assert pos == want
+        assert ids[r] == cid[r, pos]

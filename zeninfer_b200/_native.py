@@ -17,7 +17,7 @@ EXPORTS = (
     "zs_create", "zs_destroy", "zs_last_error", "zs_status_string", "zs_abi_version",
     "zs_rng_seed", "zs_sample", "zs_argmax", "zs_check_device_status",
     "zs_shard_partial_bytes", "zs_shard_partials", "zs_shard_merge", "zs_sample_sharded",
-    "zs_sample_noalloc",
+    "zs_sample_noalloc", "zs_set_timing", "zs_get_timing",
 )
 
 ZS_OK = 0
@@ -39,6 +39,12 @@ class ZsExtras(C.Structure):
                 ("cand_ld", C.c_int32), ("want_log_z", C.c_int32)]
 
 
+class ZsTiming(C.Structure):
+    _fields_ = [("select_ms", C.c_double), ("merge_ms", C.c_double), ("large_ms", C.c_double),
+                ("select_launches", C.c_int64), ("merge_launches", C.c_int64),
+                ("large_launches", C.c_int64), ("launches", C.c_int64)]
+
+
 class SamplerError(RuntimeError):
     def __init__(self, status: int, what: str, detail: str):
         super().__init__(f"{what}: status {status} ({detail})")
@@ -55,7 +61,7 @@ def lib() -> C.CDLL:
         return _lib
     if not os.path.exists(SAMPLER_SO):
         raise RuntimeError(f"{SAMPLER_SO} is not built; run python -m zeninfer_b200.build")
-    L = C.CDLL(SAMPLER_SO, mode=C.RTLD_GLOBAL)
+    L = C.CDLL(SAMPLER_SO, mode=C.RTLD_LOCAL)
     vp, i32, i64, u64 = C.c_void_p, C.c_int32, C.c_int64, C.c_uint64
     L.zs_create.argtypes = [C.c_int, C.POINTER(vp)]
     L.zs_destroy.argtypes = [vp]
@@ -75,6 +81,8 @@ def lib() -> C.CDLL:
                                  C.POINTER(ZsExtras), vp]
     L.zs_sample_sharded.argtypes = [vp, vp, i64, i32, i32, i32, i32, i32, C.POINTER(ZsParams), i32,
                                     vp, i64, vp, vp, vp, C.POINTER(ZsExtras), vp, vp]
+    L.zs_set_timing.argtypes = [vp, i32]
+    L.zs_get_timing.argtypes = [vp, C.POINTER(ZsTiming)]
     L.zs_sample_noalloc.argtypes = [vp, i64, i32, i32, C.POINTER(ZsParams), vp, i64, vp, vp, vp,
                                     vp, vp]
     for name in EXPORTS:
@@ -82,7 +90,8 @@ def lib() -> C.CDLL:
         if f.restype is C.c_int or name in ("zs_create", "zs_destroy", "zs_sample", "zs_argmax",
                                             "zs_check_device_status", "zs_shard_partial_bytes",
                                             "zs_shard_partials", "zs_shard_merge",
-                                            "zs_sample_sharded", "zs_sample_noalloc"):
+                                            "zs_sample_sharded", "zs_sample_noalloc",
+                                            "zs_set_timing", "zs_get_timing"):
             f.restype = C.c_int
     _lib = L
     return L

@@ -62,7 +62,9 @@ def build_sampler(force: bool = False, verbose_ptxas: bool = False) -> str:
     cmd = [_nvcc(), *NVCC_FLAGS, "-shared", f"-I{INCLUDE}", "-o", tmp]
     if verbose_ptxas:
         cmd += ["-Xptxas", "-v"]
-    cmd += [os.path.join(CSRC, f) for f in SAMPLER_SOURCES] + ["-ldl"]
+    # -Bsymbolic: the library's zen:: functions call their own definitions even in
+    # a process that also loads another sample.h implementation.
+    cmd += [os.path.join(CSRC, f) for f in SAMPLER_SOURCES] + ["-ldl", "-Xlinker", "-Bsymbolic"]
     _run(cmd)
     os.replace(tmp, SAMPLER_SO)
     return SAMPLER_SO

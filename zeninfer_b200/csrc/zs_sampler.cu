@@ -105,7 +105,12 @@ Plan make_plan(int B, int V_cols, int V_total, const zs_params* params, int per_
         const int wb = win_bound_of(p);  // the block layout must not depend on history presence
         pl.max_ksel = std::max(pl.max_ksel, ks);
         if (have_history && wb > 0) pl.any_penal = true;
-        if (have_history && ((long)ks + wb > zs::kKeffFastMax || wb > zs::kWinFastMax)) pl.any_large = true;
+        // A row leaves the fast kernels when its shortlist alone is too long, or
+        // (with a history) shortlist + window or the window is; the device-side
+        // plan uses the actual window, never longer than this bound.
+        if (ks > zs::kKeffFastMax ||
+            (have_history && ((long)ks + wb > zs::kKeffFastMax || wb > zs::kWinFastMax)))
+            pl.any_large = true;
         max_keys = std::max(max_keys, partial_keys_for(ks, wb));
     }
     pl.S = choose_slices(B, V_cols, ctas);
@@ -162,6 +167,15 @@ struct zs_context {
     unsigned* fail_count = nullptr;  // units whose speculative threshold was too high
     int32_t* fail_units = nullptr;
     size_t fail_units_n = 0;
+    // optional per-kernel timing (zs_set_timing): event pairs around each launch
+    struct TimedLaunch {
+        int kind;  // 0 select, 1 merge, 2 large
+        cudaEvent_t begin, end;
+    };
+    bool timing = false;
+    std::vector<TimedLaunch> timed;      // recorded since the last zs_get_timing
+    std::vector<cudaEvent_t> spare;      // events free for reuse
+    int64_t launches = 0;                // kernel launches since the last zs_get_timing
 };
 
 namespace {
@@ -226,11 +240,42 @@ zs::Params to_dev(const zs_params& p) {
 // (row, slice); zs_merge_kernel then merges each row's blocks, sorts the
 // shortlist and draws.  Rows needing the large shortlist path follow in
 // zs_large_kernel.
+// Brackets one kernel launch with events when timing is on; counts launches.
+struct LaunchScope {
+    zs_context* h;
+    int kind;
+    cudaStream_t st;
+    cudaEvent_t b = nullptr, e = nullptr;
+    LaunchScope(zs_context* h_, int kind_, cudaStream_t st_) : h(h_), kind(kind_), st(st_) {
+        h->launches += 1;
+        if (!h->timing) return;
+        b = take();
+        e = take();
+        if (b && e) cudaEventRecord(b, st);
+    }
+    ~LaunchScope() {
+        if (!h->timing || !b || !e) return;
+        cudaEventRecord(e, st);
+        h->timed.push_back({kind, b, e});
+    }
+    cudaEvent_t take() {
+        cudaEvent_t ev = nullptr;
+        if (!h->spare.empty()) {
+            ev = h->spare.back();
+            h->spare.pop_back();
+        } else if (cudaEventCreate(&ev) != cudaSuccess) {
+            ev = nullptr;
+        }
+        return ev;
+    }
+};
+
 // Merge launch: one warp per row when every shortlist fits a warp slot and the
 // batch gives every SM at least four such warps; otherwise one CTA per row (a
 // small batch has many slices per row and too few rows to fill the GPU by warps).
 zs_status launch_merge(zs_context* h, const zs::MergeArgs& m, int max_ksel, bool want_lse,
                        cudaStream_t st) {
+    LaunchScope scope(h, 1, st);
     if ((uint32_t)max_ksel <= zs::kWarpMergeMaxK && m.B >= 4 * h->num_sms) {
         const int rows_per_cta = zs::kConsumerWarps;
         const int grid = std::max(1, std::min((m.B + rows_per_cta - 1) / rows_per_cta, 8 * h->num_sms));
@@ -279,6 +324,7 @@ zs_status launch_select(zs_context* h, const zs::Args& base, const Plan& pl, boo
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(a.n_units, h->select_ctas));
     for (int pass = 0; pass < 2; ++pass) {
         a.redo = pass;  // pass 1 redoes the units listed by pass 0 (usually none)
+        LaunchScope scope(h, 0, st);
         if (want_lse)
             zs::zs_select_kernel<true><<<grid, zs::kThreads, h->select_smem, st>>>(a);
         else
@@ -320,6 +366,7 @@ zs_status launch_select(zs_context* h, const zs::Args& base, const Plan& pl, boo
         if (s != ZS_OK) return s;
         a.large_ws = h->large;
         a.large_ws_per_cta = per_cta;
+        LaunchScope scope(h, 2, st);
         if (want_lse)
             zs::zs_large_kernel<true><<<lgrid, zs::kNC, h->merge_smem, st>>>(a);
         else
@@ -407,8 +454,42 @@ zs_status zs_destroy(zs_handle h) {
     cudaFree(h->gather);
     cudaFree(h->fail_count);
     cudaFree(h->fail_units);
+    for (auto& t : h->timed) {
+        cudaEventDestroy(t.begin);
+        cudaEventDestroy(t.end);
+    }
+    for (cudaEvent_t ev : h->spare) cudaEventDestroy(ev);
     delete h;
     return ZS_OK;
+}
+
+zs_status zs_set_timing(zs_handle h, int32_t enable) {
+    if (!h) return fail(ZS_ERR_INVALID_ARGUMENT, "null handle");
+    h->timing = enable != 0;
+    return ZS_OK;
+}
+
+zs_status zs_get_timing(zs_handle h, zs_timing* out) {
+    if (!h || !out) return fail(ZS_ERR_INVALID_ARGUMENT, "null handle or out");
+    DeviceGuard g(h->device);
+    std::memset(out, 0, sizeof(*out));
+    double* dst[3] = {&out->select_ms, &out->merge_ms, &out->large_ms};
+    int64_t* cnt[3] = {&out->select_launches, &out->merge_launches, &out->large_launches};
+    zs_status s = ZS_OK;
+    for (auto& t : h->timed) {
+        float ms = 0.0f;
+        cudaError_t e = cudaEventSynchronize(t.end);
+        if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, t.begin, t.end);
+        if (e != cudaSuccess && s == ZS_OK) s = cuda_fail(e, "timing events");
+        *dst[t.kind] += ms;
+        *cnt[t.kind] += 1;
+        h->spare.push_back(t.begin);
+        h->spare.push_back(t.end);
+    }
+    h->timed.clear();
+    out->launches = h->launches;
+    h->launches = 0;
+    return s;
 }
 
 zs_status zs_sample(zs_handle h, const float* logits, int64_t ld, int32_t batch, int32_t n_vocab,

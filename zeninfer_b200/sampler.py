@@ -198,6 +198,16 @@ class Sampler:
                                           out.data_ptr(), _stream_ptr(stream)), "zs_argmax")
         return out
 
+    def set_timing(self, enable: bool) -> None:
+        """Bracket every kernel of this sampler with CUDA events (measurement only)."""
+        _native.check(self._lib.zs_set_timing(self._h, 1 if enable else 0), "zs_set_timing")
+
+    def get_timing(self) -> dict:
+        """Per-kernel device time and launch counts since the last call."""
+        t = _native.ZsTiming()
+        _native.check(self._lib.zs_get_timing(self._h, C.byref(t)), "zs_get_timing")
+        return {f: getattr(t, f) for f, _ in t._fields_}
+
     def check_device_status(self, stream=None) -> None:
         _native.check(self._lib.zs_check_device_status(self._h, _stream_ptr(stream)),
                       "device status")
