@@ -58,16 +58,16 @@ def hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def committed_traffic():
+def committed_traffic(rows):
     """dram bytes per launch of zs_select_kernel on this workload, from the
-    committed ncu summary (profiles/), scaled to 4096 rows; None if absent."""
+    committed ncu summary (profiles/), scaled to `rows` rows; None if absent."""
     path = os.path.join(ROOT, "profiles", "zs_select_kernel_workload5.md")
     try:
         txt = open(path).read()
     except OSError:
         return None
     m = re.search(r"traffic_bytes_per_row:\s*([0-9.eE+]+)", txt)
-    return float(m.group(1)) * ROWS if m else None
+    return float(m.group(1)) * rows if m else None
 
 
 class ClockSampler:
@@ -126,21 +126,25 @@ class ClockSampler:
         return out
 
 
-def cpu_reference_rate(x_rows, params, seeds, budget_s=8.0, nthreads=None):
+def cpu_reference_rate(x_rows, params, seeds, budget_s=10.0, nthreads=None):
     """The reference's own sampler (oracle/_ref, src/sample.cpp compiled unchanged)
-    on the host cores: rows/s over a bounded sample of the workload rows."""
+    on the host cores: rows/s over a bounded sample of the workload rows (whole
+    passes over the batch, or a prefix of it, for about budget_s seconds)."""
     import oracle
     nthreads = nthreads or (os.cpu_count() or 1)
     probe = min(len(x_rows), max(64, nthreads * 4))
     t0 = time.perf_counter()
     oracle.reference_sample(x_rows[:probe], params, seeds[:probe], nthreads=nthreads)
-    dt = time.perf_counter() - t0
-    rate = probe / max(dt, 1e-9)
-    rows = int(min(len(x_rows), max(probe, rate * budget_s)))
-    t0 = time.perf_counter()
-    oracle.reference_sample(x_rows[:rows], params, seeds[:rows], nthreads=nthreads)
-    dt = time.perf_counter() - t0
-    return rows / dt, rows, dt, nthreads
+    rate = probe / max(time.perf_counter() - t0, 1e-9)
+    chunk = int(min(len(x_rows), max(probe, rate * budget_s)))
+    done, t0 = 0, time.perf_counter()
+    while True:
+        oracle.reference_sample(x_rows[:chunk], params, seeds[:chunk], nthreads=nthreads)
+        done += chunk
+        dt = time.perf_counter() - t0
+        if dt >= budget_s or chunk < len(x_rows):
+            break
+    return done / dt, done, dt, nthreads
 
 
 def run_reference_arm(args, rank, world):
@@ -158,12 +162,14 @@ def run_reference_arm(args, rank, world):
     nthreads = os.cpu_count() or 1
     x = W.generate(WORKLOAD, ROWS)
     seeds = wl.row_seeds(0, ROWS)
-    # Calibrate one step to a bounded sample (a few seconds of host work).
+    # Calibrate one step to a bounded sample: at most 3 s of host work, and the
+    # whole warm-up + timed run within about two minutes.
     t0 = time.perf_counter()
     probe = min(ROWS, max(64, 4 * nthreads))
     oracle.reference_sample(x[:probe], wl.params, seeds[:probe], nthreads=nthreads)
     rate = probe / max(time.perf_counter() - t0, 1e-9)
-    step_rows = int(min(ROWS, max(probe, rate * 3.0)))
+    step_s = min(3.0, 120.0 / max(1, args.steps + args.warmup))
+    step_rows = int(min(ROWS, max(nthreads, rate * step_s)))
     for _ in range(args.warmup):
         oracle.reference_sample(x[:step_rows], wl.params, seeds[:step_rows], nthreads=nthreads)
     times = []
@@ -208,10 +214,14 @@ def main():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--rows", type=int, default=ROWS,
+                    help="rows per GPU (default 4096, the benchmark batch; smaller only "
+                         "for profiling captures)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    rows = max(1, args.rows)
 
     world = env_int("WORLD_SIZE", 1)
     rank = env_int("RANK", 0)
@@ -249,13 +259,13 @@ def main():
     stream = torch.cuda.current_stream()
 
     # Host copy of this rank's rows (distinct rows per rank), pinned for the e2e leg.
-    row0 = rank * ROWS
-    x_host = torch.empty((ROWS, V), dtype=torch.float32).pin_memory()
-    W.generate(WORKLOAD, ROWS, row0=row0, out=x_host.numpy())
+    row0 = rank * rows
+    x_host = torch.empty((rows, V), dtype=torch.float32).pin_memory()
+    W.generate(WORKLOAD, rows, row0=row0, out=x_host.numpy())
     x_dev = x_host.to(dev)
-    states0 = wl.row_states(row0, ROWS)
+    states0 = wl.row_states(row0, rows)
     st = states_to_tensor(states0, dev)
-    out = torch.empty(ROWS, dtype=torch.int32, device=dev)
+    out = torch.empty(rows, dtype=torch.int32, device=dev)
     s = Sampler(local_rank)
 
     def step():
@@ -279,18 +289,18 @@ def main():
     barrier()
     s.check_device_status(stream)
     ms_step = max_over_ranks(ms_total / args.steps)
-    value = world * ROWS / (ms_step / 1e3)
+    value = world * rows / (ms_step / 1e3)
 
     # Roofline of the dominant kernel, zs_select_kernel (its exact-redo second
     # launch included), timed by CUDA events around its launches on the
     # sampler's stream during the timed steps.
     peak, peak_kind = hbm_peak()
-    alg_bytes = ROWS * ROW_BYTES + ROWS * 4
+    alg_bytes = rows * ROW_BYTES + rows * 4
     sel_ms = max_over_ranks(kt["select_ms"] / args.steps)
     merge_ms = max_over_ranks(kt["merge_ms"] / args.steps)
     achieved = alg_bytes / (sel_ms / 1e3) / 1e9
     step_gbs = alg_bytes / (ms_step / 1e3) / 1e9
-    traffic = committed_traffic()
+    traffic = committed_traffic(rows)
 
     # Batch 1 and 256 on the same device (latency-bound and mid-size shapes).
     by_batch = {}
@@ -311,7 +321,7 @@ def main():
                             "hbm_frac": b * ROW_BYTES / (msb / 1e3) / 1e9 / peak,
                             "params": "temp 0.7, top-k 40" + (", top-p 0.9" if b == 256 else "")}
         del xb
-    by_batch[str(ROWS)] = {"rows_per_s": ROWS / (ms_step / 1e3), "us_per_call": ms_step * 1e3,
+    by_batch[str(rows)] = {"rows_per_s": rows / (ms_step / 1e3), "us_per_call": ms_step * 1e3,
                            "logits_gbs": step_gbs, "hbm_frac": step_gbs / peak,
                            "params": "temp 0.7, top-k 50, top-p 0.9"}
 
@@ -319,7 +329,7 @@ def main():
     # logits from pinned memory, the sampler, D2H of the ids, every step.
     e2e = None
     if not args.no_e2e:
-        out_host = torch.empty(ROWS, dtype=torch.int32).pin_memory()
+        out_host = torch.empty(rows, dtype=torch.int32).pin_memory()
         x_e2e = torch.empty_like(x_dev)
 
         def e2e_step():
@@ -337,8 +347,8 @@ def main():
             torch.cuda.current_stream().synchronize()
             _ = int(out_host[0])
         e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3 / k)
-        e2e = {"value": world * ROWS / (e2e_ms / 1e3), "unit": UNIT,
-               "h2d_bytes_per_step": ROWS * ROW_BYTES, "d2h_bytes_per_step": ROWS * 4,
+        e2e = {"value": world * rows / (e2e_ms / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": rows * ROW_BYTES, "d2h_bytes_per_step": rows * 4,
                "ms_per_step": e2e_ms}
         del x_e2e
 
@@ -348,10 +358,10 @@ def main():
         from zeninfer_b200.sharding import VocabShardedSampler, vocab_range
         lo, n_loc = vocab_range(V, world, rank)
         x_loc = x_dev[:, lo:lo + n_loc]
-        nbytes = Sampler.shard_partial_bytes(ROWS, V, world, params)
+        nbytes = Sampler.shard_partial_bytes(rows, V, world, params)
         vs = VocabShardedSampler(s)
         st2 = states_to_tensor(states0, dev)
-        out2 = torch.empty(ROWS, dtype=torch.int32, device=dev)
+        out2 = torch.empty(rows, dtype=torch.int32, device=dev)
 
         def shard_step():
             vs.sample(x_loc, lo, V, params, st2, out=out2, stream=stream)
@@ -364,7 +374,7 @@ def main():
         torch.cuda.synchronize()
         barrier()
         ms_sh = max_over_ranks(ms_sh)
-        sharded = {"rows_per_s": ROWS / (ms_sh / 1e3), "ms_per_step": ms_sh,
+        sharded = {"rows_per_s": rows / (ms_sh / 1e3), "ms_per_step": ms_sh,
                    "allgather_bytes_per_rank": nbytes, "scaling": "strong"}
 
     cpu = None
@@ -372,10 +382,10 @@ def main():
         try:
             import oracle
             if oracle.have_reference():
-                rate, rows, dt, nth = cpu_reference_rate(x_host.numpy(), params,
-                                                         wl.row_seeds(row0, ROWS))
+                rate, n_cpu, dt, nth = cpu_reference_rate(x_host.numpy(), params,
+                                                          wl.row_seeds(row0, rows))
                 cpu = {"value": rate, "unit": UNIT, "cores": nth, "kind": "reference",
-                       "sample": f"{rows} of the 4096 rows ({dt:.1f} s), zen::sample_token "
+                       "sample": f"{n_cpu} rows of this batch ({dt:.1f} s), zen::sample_token "
                                  f"(src/sample.cpp compiled unchanged) on {nth} threads"}
         except Exception as e:  # reported, never fatal
             cpu = {"value": None, "unit": UNIT, "cores": None, "kind": "reference",
@@ -387,9 +397,9 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32 (f64 shortlist softmax)", "data": "synthetic",
-            "config": {"workload": "4096 x 151936 f32 logits per GPU (workload 5: N(0,2.5^2)"
+            "config": {"workload": f"{rows} x 151936 f32 logits per GPU (workload 5: N(0,2.5^2)"
                                    " + offset + 8 peaks), temp 0.7, top-k 50, top-p 0.9",
-                       "rows_per_gpu": ROWS, "vocab": V, "parallelism": f"row-split x{world}",
+                       "rows_per_gpu": rows, "vocab": V, "parallelism": f"row-split x{world}",
                        "l2": "inputs (2.49 GB per GPU) larger than L2"},
             "logits_gbs": step_gbs, "hbm_frac": step_gbs / peak,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
