@@ -133,6 +133,12 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
         : "memory");
 }
 
+// Orders this thread's earlier generic-proxy shared-memory accesses before its
+// later async-proxy ones (a bulk copy into a buffer the warp has just read).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // L2 policy for data read exactly once: evict first.
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
     uint64_t p;

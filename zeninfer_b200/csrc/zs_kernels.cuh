@@ -46,6 +46,18 @@ constexpr int kSortMax = 4096;            // bitonic size bound (kKeffFastMax + 
 constexpr int kProbOffset = 2048;         // f64 probabilities alias cand[2048..4096)
 constexpr int kShortlistDefault = 256;    // kTopPShortlist, src/sample.cpp:12
 
+// Warp-independent select (zs_wselect_kernel): rows whose shortlist + penalty
+// window is at most kWKeffMax (every default shape of the reference).
+constexpr int kWWarps = 12;                // independent warps per CTA
+constexpr int kWThreads = kWWarps * 32;
+constexpr int kWTile = 1024;               // floats per ring stage (4 KB)
+constexpr int kWStages = 3;
+constexpr int kWCap = 640;                 // candidate keys per warp
+constexpr int kWStepElems = 128;           // floats one warp step covers (32 lanes x float4)
+constexpr int kWKeffMax = 320;
+constexpr int kWWinMax = 64;
+constexpr int kWMinElems = 2048;           // smallest share of the batch per warp
+
 static_assert(kCandCap >= kKeffFastMax + kSlackMax + kHalfElems + kCandMargin,
               "candidate buffer too small for half-stage passes");
 static_assert(kCandCap >= kOnePassMaxKeff + 2 * 128 + 256 + kTileElems + kCandMargin,
@@ -150,6 +162,16 @@ struct Args {
     // large-k path workspace
     uint8_t* large_ws;
     int64_t large_ws_per_cta;
+    // Warp-piece layout (zs_wselect_kernel): the batch flattened to wl_E =
+    // B * wl_Vn columns is cut into wl_NW equal contiguous shares, one per warp;
+    // a share is cut at row ends into pieces, and piece j of warp w writes its
+    // block at wpart + (w * wl_P + j) * wl_stride.
+    uint8_t* wpart;
+    int64_t wl_E;
+    int64_t wl_stride;
+    int32_t wl_NW;
+    int32_t wl_P;
+    int32_t wl_Vn;
 };
 
 struct MergeArgs {
@@ -173,6 +195,13 @@ struct MergeArgs {
     double* cand_probs;
     int32_t cand_ld;
     int* status;
+    // warp-piece blocks (see Args), at wl_off inside each rank's area
+    int64_t wl_off;
+    int64_t wl_E;
+    int64_t wl_stride;
+    int32_t wl_NW;
+    int32_t wl_P;
+    int32_t wl_Vn;
 };
 
 struct RowPlan {
@@ -183,7 +212,9 @@ struct RowPlan {
     int32_t hist_len;
     bool greedy;
     bool penal;
-    bool fast;
+    bool wfast;  // zs_wselect_kernel: keff <= kWKeffMax, window <= kWWinMax
+    bool fast;   // zs_select_kernel: the other rows with keff <= kKeffFastMax
+    bool large;  // zs_large_kernel: the rest
 };
 
 __device__ __forceinline__ Params load_params(const Params* rp, const Params& shared, int row) {
@@ -209,8 +240,54 @@ __device__ __forceinline__ RowPlan plan_row(const Params& p, int V_total, const 
     }
     r.penal = r.win > 0;
     r.keff = r.ksel + r.win;
-    r.fast = (r.keff <= kKeffFastMax) && (r.win <= kWinFastMax);
+    r.wfast = (r.keff <= kWKeffMax) && (r.win <= kWWinMax);
+    r.fast = !r.wfast && (r.keff <= kKeffFastMax) && (r.win <= kWinFastMax);
+    r.large = !r.wfast && !r.fast;
     return r;
+}
+
+// ---- warp-piece layout ----
+__device__ __forceinline__ int64_t wl_bound(int64_t E, int32_t NW, int32_t w) {
+    return w >= NW ? E : ((int64_t)w * E) / NW;
+}
+
+// The warp whose share holds flattened column x.
+__device__ __forceinline__ int32_t wl_warp_of(int64_t E, int32_t NW, int64_t x) {
+    return (int32_t)(((x + 1) * (int64_t)NW - 1) / E);
+}
+
+struct WPiece {
+    int32_t row;
+    int32_t c0, c1;  // columns of the piece
+    int32_t e0, e1;  // 16-byte aligned sub-range moved by bulk copies
+    int32_t ntiles;
+    bool active;     // the row belongs to the warp path
+};
+
+__device__ __forceinline__ WPiece wl_piece(const Args& a, int64_t b0, int64_t b1, int32_t r0, int j) {
+    WPiece pc;
+    pc.row = r0 + j;
+    const int64_t rs = (int64_t)pc.row * a.wl_Vn;
+    int64_t c0 = b0 > rs ? b0 - rs : 0;
+    int64_t c1 = b1 - rs < (int64_t)a.wl_Vn ? b1 - rs : (int64_t)a.wl_Vn;
+    c1 = c1 < a.V ? c1 : a.V;  // a shard may hold fewer columns than the layout's row
+    c0 = c0 < c1 ? c0 : c1;
+    pc.c0 = (int32_t)c0;
+    pc.c1 = (int32_t)c1;
+    const RowPlan rp = plan_row(load_params(a.row_params, a.shared, pc.row), a.V_total, a.hist,
+                                a.hist_len, a.hist_ld, pc.row);
+    pc.active = rp.wfast;
+    const uintptr_t p0 = (uintptr_t)(a.logits + (int64_t)pc.row * a.ld + pc.c0);
+    const int pad = (int)(((16u - (unsigned)(p0 & 15u)) & 15u) >> 2);
+    const int e0 = pc.c0 + pad;
+    if (e0 >= pc.c1) {
+        pc.e0 = pc.e1 = pc.c1;
+    } else {
+        pc.e0 = e0;
+        pc.e1 = e0 + ((pc.c1 - e0) & ~3);
+    }
+    pc.ntiles = pc.active ? (pc.e1 - pc.e0 + kWTile - 1) / kWTile : 0;
+    return pc;
 }
 
 struct UnitGeom {
@@ -490,12 +567,9 @@ __device__ uint64_t kth_of_proposals(CandState& st, uint64_t mine, uint32_t kk, 
                     for (int q = 0; q < 8; ++q) st.hist[lane * 8 + q] = 0u;
                     __syncwarp();
 #pragma unroll
-                    for (int q = 0; q < Q; ++q) {
-                        const bool in = k[q] != 0ull && (k[q] & mask) == prefix;
-                        const uint32_t d = in ? ((uint32_t)(k[q] >> shift) & 255u) : 256u + lane;
-                        const unsigned peers = __match_any_sync(kFull, d);
-                        if (in && (__ffs(peers) - 1) == lane) atomicAdd(&st.hist[d], (uint32_t)__popc(peers));
-                    }
+                    for (int q = 0; q < Q; ++q)
+                        if (k[q] != 0ull && (k[q] & mask) == prefix)
+                            atomicAdd(&st.hist[(uint32_t)(k[q] >> shift) & 255u], 1u);
                     __syncwarp();
                     select_bucket(st, need, lane);
                     __syncwarp();
@@ -588,13 +662,9 @@ __device__ uint64_t compact_top(CandState& st, uint32_t n, uint32_t kk, uint32_t
     uint64_t prefix = a & mask;
     uint32_t need = kk;
     for (;;) {
-        for (uint32_t b0 = (uint32_t)warp * 32; b0 < n; b0 += kNC) {
-            const uint32_t i = b0 + lane;
-            const uint64_t k = i < n ? st.cand[i] : 0ull;
-            const bool in = i < n && (k & mask) == prefix;
-            const uint32_t d = in ? ((uint32_t)(k >> shift) & 255u) : 256u + lane;
-            const unsigned peers = __match_any_sync(kFull, d);
-            if (in && (__ffs(peers) - 1) == lane) atomicAdd(&st.hist[d], (uint32_t)__popc(peers));
+        for (uint32_t i = ctid; i < n; i += kNC) {
+            const uint64_t k = st.cand[i];
+            if ((k & mask) == prefix) atomicAdd(&st.hist[(uint32_t)(k >> shift) & 255u], 1u);
         }
         csync();
         if (warp == 0) select_bucket(st, need, lane);
@@ -912,25 +982,120 @@ __device__ void finalize_row(CandState& st, const uint64_t* cand, double* prob, 
     csync();
 }
 
+// The partial blocks of one row: S slice blocks of zs_select_kernel, or the
+// blocks of the warps whose shares cover the row (zs_wselect_kernel).
+struct BlockSet {
+    int32_t n;       // blocks per rank
+    int32_t w_lo;    // first warp (warp layout)
+    int64_t stride;  // bytes per block
+    bool warp;
+};
+
+__device__ __forceinline__ BlockSet row_blocks(const MergeArgs& a, int row, bool wfast) {
+    BlockSet bs;
+    bs.warp = wfast;
+    if (wfast) {
+        const int64_t x0 = (int64_t)row * a.wl_Vn;
+        bs.w_lo = wl_warp_of(a.wl_E, a.wl_NW, x0);
+        const int32_t w_hi = wl_warp_of(a.wl_E, a.wl_NW, x0 + a.wl_Vn - 1);
+        bs.n = w_hi - bs.w_lo + 1;
+        bs.stride = a.wl_stride;
+    } else {
+        bs.w_lo = 0;
+        bs.n = a.S;
+        bs.stride = a.part_stride;
+    }
+    return bs;
+}
+
+// Block idx of rank g for `row`; nullptr for a warp whose share is empty.
+__device__ __forceinline__ const uint8_t* block_at(const MergeArgs& a, const BlockSet& bs, int g,
+                                                   int row, int idx) {
+    const uint8_t* base = a.gathered + (int64_t)g * a.rank_stride;
+    if (!bs.warp) return base + ((int64_t)row * a.S + idx) * a.part_stride;
+    const int32_t w = bs.w_lo + idx;
+    const int64_t b0 = wl_bound(a.wl_E, a.wl_NW, w), b1 = wl_bound(a.wl_E, a.wl_NW, w + 1);
+    if (b0 >= b1) return nullptr;
+    const int32_t j = row - (int32_t)(b0 / a.wl_Vn);
+    return base + a.wl_off + ((int64_t)w * a.wl_P + j) * a.wl_stride;
+}
+
 // Streams the keys of partial blocks (unsorted; 0 = removed) through the
 // threshold filter and leaves the exact top-ksel, sorted, in st.cand[0..kk).
 // Also merges the partials' sum-exp scalars and id-0 flags.  Returns kk.  Runs
 // in its own launch, after every partial block is complete; each header is
 // read once by thread 0 and shared, so all threads take the same path.
-__device__ uint32_t merge_partials(CandState& st, const uint8_t* base, int64_t rank_stride,
-                                   int G, int S, int64_t part_stride, int row, uint32_t ksel,
-                                   float lse_c, bool& x0_nan, float& lse_m, float& lse_s,
-                                   int ctid) {
+__device__ uint32_t merge_partials(CandState& st, const MergeArgs& a, const BlockSet& bs,
+                                   int row, uint32_t ksel, float lse_c, bool& x0_nan,
+                                   float& lse_m, float& lse_s, int ctid) {
     const int lane = ctid & 31;
-    const uint32_t cap = (uint32_t)((part_stride - kPartialHeaderBytes) / 8);
+    const uint32_t cap = (uint32_t)((bs.stride - kPartialHeaderBytes) / 8);
+    const int nb = a.G * bs.n;
+    if (nb <= kNC) {
+        // Every block header at once (one thread each), offsets by a scan, then
+        // all keys gathered in parallel: one memory latency per phase instead of
+        // one per block.
+        const uint8_t* pp = nullptr;
+        uint32_t c = 0u;
+        float m = -INFINITY, sx = 0.0f;
+        bool z = false;
+        if (ctid < nb) {
+            pp = block_at(a, bs, ctid / bs.n, row, ctid % bs.n);
+            if (pp != nullptr) {
+                uint4 hv = __ldcg(reinterpret_cast<const uint4*>(pp));
+                if (!ZS_CHECK(hv.x <= cap, 8, ((uint64_t)row << 32) | hv.x)) hv.x = 0u;
+                c = hv.x < cap ? hv.x : cap;
+                m = __uint_as_float(hv.z);
+                sx = __uint_as_float(hv.w);
+                z = (hv.y & kPartHasId0) && (hv.y & kPartX0Nan);
+            }
+        }
+        uint32_t tot;
+        const uint32_t incl = block_incl_scan(c, st.scan, ctid, tot);
+        if (tot + kCandMargin <= (uint32_t)kCandCap) {  // tot is the same on every thread
+            st.hist[ctid] = incl - c;
+            st.prop[ctid] = reinterpret_cast<uint64_t>(pp);
+            csync();
+            for (uint32_t i = ctid; i < tot; i += kNC) {
+                int lo = 0, hi = nb - 1;  // the last block starting at or before i
+                while (lo < hi) {
+                    const int mid = (lo + hi + 1) >> 1;
+                    if (st.hist[mid] <= i) lo = mid;
+                    else hi = mid - 1;
+                }
+                const unsigned long long* keys = reinterpret_cast<const unsigned long long*>(
+                    st.prop[lo] + kPartialHeaderBytes);
+                st.cand[i] = __ldcg(keys + (i - st.hist[lo]));
+            }
+            block_lse(st, m, sx, lse_c, ctid);
+            x0_nan = csync_or(z);
+            lse_m = st.lse_m;
+            lse_s = st.lse_s;
+            uint32_t n = tot;
+            if (!bs.warp) {
+                n = keep_at_least(st, n, 1ull, ctid);  // zero keys mark removed candidates
+            } else {
+                if (ctid == 0) st.count = n;
+                csync();
+            }
+            if (n > ksel) {
+                compact_select(st, n, ksel, ctid);
+                n = st.count;
+            }
+            sort_desc(st, n, ctid);
+            return n < ksel ? n : ksel;
+        }
+        csync();
+    }
     if (ctid == 0) st.count = 0u;
     uint64_t tau = 0ull;
     bool full = false;  // same on every thread: no room for another chunk
     float M = -INFINITY, Sx = 0.0f;
     bool nan0 = false;
-    for (int g = 0; g < G; ++g) {
-        for (int s = 0; s < S; ++s) {
-            const uint8_t* pp = base + (int64_t)g * rank_stride + ((int64_t)row * S + s) * part_stride;
+    for (int g = 0; g < a.G; ++g) {
+        for (int s = 0; s < bs.n; ++s) {
+            const uint8_t* pp = block_at(a, bs, g, row, s);
+            if (pp == nullptr) continue;  // the same on every thread
             if (ctid == 0) {
                 uint4 hv = __ldcg(reinterpret_cast<const uint4*>(pp));
                 if (!ZS_CHECK(hv.x <= cap, 8, ((uint64_t)row << 32) | hv.x)) hv.x = 0u;
@@ -1380,13 +1545,13 @@ __global__ void __launch_bounds__(kNC) zs_merge_kernel(const MergeArgs a) {
     for (int row = blockIdx.x; row < a.B; row += gridDim.x) {
         const RowPlan rp = plan_row(load_params(a.row_params, a.shared, row), a.V_total, a.hist,
                                     a.hist_len, a.hist_ld, row);
-        if (!rp.fast) continue;  // drawn by zs_large_kernel
+        if (rp.large) continue;  // drawn by zs_large_kernel
         const float lc = (rp.greedy ? 1.0f : 1.0f / rp.p.temp) * 1.4426950408889634f;
         bool x0n;
         float mm, ss;
         ZS_CHECK(rp.ksel <= kKeffFastMax, 16, rp.ksel);
-        const uint32_t kk = merge_partials(st, a.gathered, a.rank_stride, a.G, a.S, a.part_stride,
-                                           row, (uint32_t)rp.ksel, lc, x0n, mm, ss, ctid);
+        const BlockSet bs = row_blocks(a, row, rp.wfast);
+        const uint32_t kk = merge_partials(st, a, bs, row, (uint32_t)rp.ksel, lc, x0n, mm, ss, ctid);
         finalize_row(st, st.cand, reinterpret_cast<double*>(st.cand + kProbOffset), kk, rp, x0n,
                      LSE, mm, ss, row, a.rng, a.out_ids, a.info, a.cand_ids, a.cand_probs,
                      a.cand_ld, ctid);
@@ -1466,13 +1631,9 @@ __device__ uint64_t warp_kth(const uint64_t* keys, uint32_t n, uint32_t kk, uint
 #pragma unroll
         for (int q = 0; q < 8; ++q) hist[lane * 8 + q] = 0u;
         __syncwarp();
-        for (uint32_t b = 0; b < n; b += 32) {
-            const uint32_t i = b + lane;
-            const uint64_t k = i < n ? keys[i] : 0ull;
-            const bool in = i < n && (k & mask) == prefix;
-            const uint32_t d = in ? ((uint32_t)(k >> shift) & 255u) : 256u + lane;
-            const unsigned peers = __match_any_sync(kFull, d);
-            if (in && (__ffs(peers) - 1) == lane) atomicAdd(&hist[d], (uint32_t)__popc(peers));
+        for (uint32_t i = lane; i < n; i += 32) {
+            const uint64_t k = keys[i];
+            if ((k & mask) == prefix) atomicAdd(&hist[(uint32_t)(k >> shift) & 255u], 1u);
         }
         __syncwarp();
         uint32_t digit, above, cnt;
@@ -1649,22 +1810,23 @@ __global__ void __launch_bounds__(kNC) zs_warp_merge_kernel(const MergeArgs a) {
     WarpMergeSmem& sm = *reinterpret_cast<WarpMergeSmem*>(smem_raw);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     WarpSlot& ws = sm.w[warp];
-    const uint32_t block_cap = (uint32_t)((a.part_stride - kPartialHeaderBytes) / 8);
     const unsigned below = lanemask_lt();
     for (int row = blockIdx.x * kConsumerWarps + warp; row < a.B; row += gridDim.x * kConsumerWarps) {
         const RowPlan rp = plan_row(load_params(a.row_params, a.shared, row), a.V_total, a.hist,
                                     a.hist_len, a.hist_ld, row);
-        if (!rp.fast) continue;  // drawn by zs_large_kernel
+        if (rp.large) continue;  // drawn by zs_large_kernel
         const uint32_t ksel = (uint32_t)rp.ksel;
         const float lc = (rp.greedy ? 1.0f : 1.0f / rp.p.temp) * 1.4426950408889634f;
+        const BlockSet bs = row_blocks(a, row, rp.wfast);
+        const uint32_t block_cap = (uint32_t)((bs.stride - kPartialHeaderBytes) / 8);
         uint32_t count = 0;
         uint64_t tau = 0ull;
         float M = -INFINITY, Sx = 0.0f;
         bool nan0 = false;
         for (int g = 0; g < a.G; ++g) {
-            for (int s = 0; s < a.S; ++s) {
-                const uint8_t* pp = a.gathered + (int64_t)g * a.rank_stride +
-                                    ((int64_t)row * a.S + s) * a.part_stride;
+            for (int s = 0; s < bs.n; ++s) {
+                const uint8_t* pp = block_at(a, bs, g, row, s);
+                if (pp == nullptr) continue;
                 uint4 hv = make_uint4(0u, 0u, 0u, 0u);
                 if (lane == 0) hv = __ldcg(reinterpret_cast<const uint4*>(pp));
                 hv.x = __shfl_sync(kFull, hv.x, 0);
@@ -1700,6 +1862,471 @@ __global__ void __launch_bounds__(kNC) zs_warp_merge_kernel(const MergeArgs a) {
         warp_finalize(ws.cand, reinterpret_cast<double*>(ws.cand + kWarpProbOffset), kk, rp, nan0,
                       LSE, M, Sx, row, a.rng, a.out_ids, a.info, a.cand_ids, a.cand_probs,
                       a.cand_ld, lane);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// zs_wselect_kernel: warp-independent streaming select for the rows of the warp
+// path (shortlist + penalty window <= kWKeffMax, window <= kWWinMax).
+//
+// Each warp owns an equal contiguous share of the batch flattened to
+// B * wl_Vn columns, cut at row ends into pieces.  It streams its share through
+// its own ring of kWStages 4 KB stages: lane 0 issues 1-D bulk copies (no tensor
+// map, no multicast) into the stage the warp has just finished, kWStages tiles
+// ahead, across piece boundaries.  Candidates live in the warp's own shared
+// slot; the count and the threshold are warp-uniform registers, appends are
+// ballots (no atomics), compactions exact warp radix selects.  No warp ever
+// waits for another, so there is no block barrier in the kernel.  At the end of
+// a piece the penalty is patched in, the piece's top-ksel (final values) is
+// selected exactly, and the keys go out as one unsorted block.
+// ---------------------------------------------------------------------------
+struct __align__(128) WarpSel {
+    float ring[kWStages][kWTile];
+    uint64_t cand[kWCap];
+    uint32_t hist[256];  // radix histogram; the penalty window at a piece's end
+    uint64_t full[kWStages];
+};
+
+struct WSelSmem {
+    WarpSel w[kWWarps];
+};
+
+// Issue side of a warp: the next (piece, tile) to copy.  Every lane keeps the
+// same cursor; lane 0 issues.
+struct WIssue {
+    int32_t j;
+    int32_t t;
+    WPiece pc;
+};
+
+struct WShare {
+    int64_t b0, b1;  // flattened columns of the warp's share
+    int32_t r0;      // first row
+    int32_t np;      // pieces
+};
+
+__device__ __forceinline__ bool wl_issue(const Args& a, WarpSel& ws, int stage, WIssue& is,
+                                         const WShare& sh, uint64_t pol, int lane) {
+    while (is.j < sh.np && is.t >= is.pc.ntiles) {
+        ++is.j;
+        is.t = 0;
+        if (is.j < sh.np) is.pc = wl_piece(a, sh.b0, sh.b1, sh.r0, is.j);
+    }
+    if (is.j >= sh.np) return false;
+    const int start = is.pc.e0 + is.t * kWTile;
+    const int n = min(kWTile, is.pc.e1 - start);
+    if (lane == 0) {
+        // The warp's reads of this stage (all consumed into registers before the
+        // __syncwarp that precedes this call) come before the copy's writes.
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(&ws.full[stage], (uint32_t)n * 4u);
+        bulk_load(ws.ring[stage], a.logits + (int64_t)is.pc.row * a.ld + start, (uint32_t)n * 4u,
+                  &ws.full[stage], pol);
+    }
+    ++is.t;
+    return true;
+}
+
+// Ballot append of `key` where pred; count stays warp-uniform.
+__device__ __forceinline__ void wappend(uint64_t* cand, uint32_t& count, bool pred, uint64_t key,
+                                        unsigned below) {
+    const unsigned m = __ballot_sync(kFull, pred);
+    if (pred && ZS_CHECK(count + __popc(m & below) < (uint32_t)kWCap, 20, count))
+        cand[count + __popc(m & below)] = key;
+    count += (uint32_t)__popc(m);
+}
+
+// Threshold modes of the warp filter.
+constexpr int kWAll = 0;    // no threshold yet: every element is a candidate
+constexpr int kWFast = 1;   // float threshold: x > tau_f, or x == tau_f with id < tau_id
+constexpr int kWExact = 2;  // the threshold key is a NaN: compare whole keys
+
+// Per-warp streaming state of one piece.
+struct WState {
+    uint32_t count;
+    uint64_t tau_key;
+    float tau_f;
+    int32_t tau_id;
+    int32_t mode;
+    uint64_t kb;  // greedy: this lane's best key
+    float vb;     // greedy: its value
+    float lm, ls; // online log-sum-exp (base 2) of this lane's elements
+};
+
+// Shrinks the candidates to the exact top-keff and raises the threshold to the
+// keff-th key.  For a non-NaN threshold value t, key(x, id) > key(t, tid) is
+// exactly x > t, or x == t and id < tid (-0 == +0, NaN below everything).
+__device__ __forceinline__ void wcompact(WarpSel& ws, WState& w, uint32_t keff, int lane) {
+    w.tau_key = warp_kth(ws.cand, w.count, keff, ws.hist, lane);
+    w.count = warp_keep(ws.cand, w.count, w.tau_key, lane);
+    w.tau_f = tau_value(w.tau_key);
+    w.tau_id = key_id(w.tau_key);
+    w.mode = ((uint32_t)(w.tau_key >> 32) == 0u) ? kWExact : kWFast;
+}
+
+// Appends the components of v (ids id..id+3) selected by p0..p3.  Positions
+// come from a bit-sliced warp prefix sum of the per-lane counts: one ballot per
+// possible count, so the common step (at most one hit per lane) costs two.
+__device__ __forceinline__ void wappend4(WarpSel& ws, WState& w, const float4& v, int32_t id,
+                                         bool p0, bool p1, bool p2, bool p3, unsigned below) {
+    const uint32_t c = (uint32_t)p0 + (uint32_t)p1 + (uint32_t)p2 + (uint32_t)p3;
+    const unsigned b1 = __ballot_sync(kFull, c >= 1u);
+    const unsigned b2 = __ballot_sync(kFull, c >= 2u);
+    uint32_t pos = (uint32_t)__popc(b1 & below), tot = (uint32_t)__popc(b1);
+    if (b2) {
+        const unsigned b3 = __ballot_sync(kFull, c >= 3u);
+        const unsigned b4 = __ballot_sync(kFull, c >= 4u);
+        pos += (uint32_t)(__popc(b2 & below) + __popc(b3 & below) + __popc(b4 & below));
+        tot += (uint32_t)(__popc(b2) + __popc(b3) + __popc(b4));
+    }
+    uint32_t at = w.count + pos;
+    ZS_CHECK(at + c <= (uint32_t)kWCap, 20, at + c);
+    if (p0) ws.cand[at++] = make_key(v.x, id);
+    if (p1) ws.cand[at++] = make_key(v.y, id + 1);
+    if (p2) ws.cand[at++] = make_key(v.z, id + 2);
+    if (p3) ws.cand[at] = make_key(v.w, id + 3);
+    w.count += tot;
+}
+
+// Does (x, id) beat the threshold of mode w.mode?
+__device__ __forceinline__ bool wpass(const WState& w, bool ok, float x, int32_t id) {
+    if (w.mode == kWFast) return ok && (x > w.tau_f || (x == w.tau_f && id < w.tau_id));
+    if (w.mode == kWAll) return ok;
+    return ok && make_key(x, id) > w.tau_key;
+}
+
+template <bool LSE>
+__device__ __forceinline__ void wfilter1(WarpSel& ws, WState& w, bool ok, float x, int32_t id,
+                                         bool greedy, uint32_t keff, float lc, unsigned below,
+                                         int lane) {
+    if (LSE && ok) lse_add1(w.lm, w.ls, x, lc);
+    if (greedy) {
+        if (ok && x >= w.vb) {
+            const uint64_t k = make_key(x, id);
+            if (k > w.kb) {
+                w.kb = k;
+                w.vb = x;
+            }
+        }
+        return;
+    }
+    const bool p = wpass(w, ok, x, id);
+    wappend(ws.cand, w.count, p, make_key(x, id), below);
+    if (w.count > (uint32_t)(kWCap - kWStepElems)) wcompact(ws, w, keff, lane);
+}
+
+template <bool LSE>
+__device__ __forceinline__ void wfilter_tile(WarpSel& ws, WState& w, const float4* t4, int n4,
+                                             int32_t gid0, bool greedy, uint32_t keff, float lc,
+                                             unsigned below, int lane) {
+#pragma unroll 2
+    for (int base = 0; base < n4; base += 32) {
+        const int jj = base + lane;
+        const bool ok = jj < n4;
+        const float4 v = ok ? t4[jj] : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        const int32_t id = gid0 + 4 * jj;
+        if (LSE && ok) lse_add4(w.lm, w.ls, v, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)), lc);
+        if (greedy) {
+            // running best of this lane; strict key order keeps the first index
+            const float vm = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
+            if (ok && vm >= w.vb) {
+                const float xs[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    if (xs[q] >= w.vb) {
+                        const uint64_t k = make_key(xs[q], id + q);
+                        if (k > w.kb) {
+                            w.kb = k;
+                            w.vb = xs[q];
+                        }
+                    }
+                }
+            }
+            continue;
+        }
+        // cheap pre-test: can any component reach the threshold value?
+        const float tf = w.mode == kWFast ? w.tau_f : -INFINITY;
+        const bool h = ok && (w.mode != kWFast || v.x >= tf || v.y >= tf || v.z >= tf || v.w >= tf);
+        if (__any_sync(kFull, h)) {
+            wappend4(ws, w, v, id, h && wpass(w, true, v.x, id), h && wpass(w, true, v.y, id + 1),
+                     h && wpass(w, true, v.z, id + 2), h && wpass(w, true, v.w, id + 3), below);
+            if (w.count > (uint32_t)(kWCap - kWStepElems)) wcompact(ws, w, keff, lane);
+        }
+    }
+}
+
+// Threshold mode, one whole tile at a time: a 32-bit mask per lane marks the
+// elements that reach the threshold value (float compares only); if any lane
+// has one, the marked elements are re-read from the stage, tested exactly, and
+// written at positions from one warp scan.  Returns false, having appended
+// nothing, when the tile's survivors could not fit even after a compaction; the
+// caller then filters it with the per-step path.
+template <bool LSE>
+__device__ __forceinline__ bool wfilter_tile_fast(WarpSel& ws, WState& w, const float* tile, int n4,
+                                                  int32_t gid0, uint32_t keff, float lc, int lane) {
+    const float4* t4 = reinterpret_cast<const float4*>(tile);
+    const float tf = w.tau_f;
+    uint32_t mask = 0u;
+#pragma unroll
+    for (int q = 0; q < kWTile / kWStepElems; ++q) {
+        const int jj = lane + 32 * q;
+        if (jj < n4) {
+            const float4 v = t4[jj];
+            if (LSE) lse_add4(w.lm, w.ls, v, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)), lc);
+            mask |= ((uint32_t)(v.x >= tf) | ((uint32_t)(v.y >= tf) << 1) |
+                     ((uint32_t)(v.z >= tf) << 2) | ((uint32_t)(v.w >= tf) << 3)) << (4 * q);
+        }
+    }
+    if (!__any_sync(kFull, mask != 0u)) return true;
+    uint32_t em = 0u;
+    for (uint32_t m = mask; m != 0u; m &= m - 1u) {
+        const int b = __ffs(m) - 1;
+        const int e = 4 * (lane + 32 * (b >> 2)) + (b & 3);
+        const float x = tile[e];
+        if (x > tf || (x == tf && gid0 + e < w.tau_id)) em |= 1u << b;
+    }
+    const uint32_t c = (uint32_t)__popc(em);
+    uint32_t incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += t;
+    }
+    const uint32_t tot = __shfl_sync(kFull, incl, 31);
+    if (w.count + tot > (uint32_t)kWCap) {
+        if (tot > (uint32_t)kWCap - keff) return false;
+        // The marked elements beat the old threshold; some may fall below the
+        // new one, which costs room but not exactness (the final select is exact).
+        wcompact(ws, w, keff, lane);
+    }
+    uint32_t at = w.count + incl - c;
+    for (uint32_t m = em; m != 0u; m &= m - 1u) {
+        const int b = __ffs(m) - 1;
+        const int e = 4 * (lane + 32 * (b >> 2)) + (b & 3);
+        ws.cand[at++] = make_key(tile[e], gid0 + e);
+    }
+    w.count += tot;
+    __syncwarp();
+    return true;
+}
+
+template <bool LSE>
+__device__ void wend_piece(const Args& a, WarpSel& ws, WState& w, const WPiece& pc,
+                           const RowPlan& rp, bool greedy_np, float lc, int32_t gw, int32_t j,
+                           unsigned below, int lane) {
+    const float* row_logits = a.logits + (int64_t)pc.row * a.ld;
+    if (greedy_np) {
+        const uint64_t kb = warp_max_u64(w.kb);
+        if (lane == 0 && kb != 0ull) ws.cand[0] = kb;
+        w.count = kb != 0ull ? 1u : 0u;
+        __syncwarp();
+    }
+    const bool has0 = (a.id_offset + pc.c0 == 0) && (pc.c1 > pc.c0);
+    bool x0n = false;
+    if (has0) {
+        const float x0 = row_logits[0];
+        x0n = (x0 != x0);
+    }
+    float M = -INFINITY, Sx = 0.0f;
+    if (LSE) {
+        M = w.lm;
+        Sx = w.ls;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float m2 = __shfl_xor_sync(kFull, M, o);
+            const float s2 = __shfl_xor_sync(kFull, Sx, o);
+            lse_merge(M, Sx, m2, s2, lc);
+        }
+    }
+    if (rp.penal) {
+        // src/sample.cpp:40-50 for the ids of this piece: raw keys out, penalised
+        // values in (each entry of the window applies the penalty once more).
+        int32_t* hw = reinterpret_cast<int32_t*>(ws.hist);
+        const int32_t* window = a.hist + (int64_t)pc.row * a.hist_ld + (rp.hist_len - rp.win);
+        for (int i = lane; i < rp.win; i += 32) hw[i] = window[i];
+        __syncwarp();
+        for (uint32_t i = lane; i < w.count; i += 32) {
+            const int32_t id = key_id(ws.cand[i]);
+            for (int q = 0; q < rp.win; ++q)
+                if (hw[q] == id) {
+                    ws.cand[i] = 0ull;
+                    break;
+                }
+        }
+        __syncwarp();
+        w.count = warp_keep(ws.cand, w.count, 1ull, lane);
+        const int32_t lo = a.id_offset + pc.c0, hi = a.id_offset + pc.c1;
+        const float pen = rp.p.repeat_penalty;
+        double dl = 0.0;
+        bool z_hit = false, z_nan = false;
+        for (int base = 0; base < rp.win; base += 32) {
+            const int jw = base + lane;
+            bool app = false;
+            uint64_t key = 0ull;
+            if (jw < rp.win) {
+                const int32_t gid = hw[jw];
+                if (gid >= 0 && gid < a.V_total && gid >= lo && gid < hi) {
+                    bool first = true;
+                    for (int q = 0; q < jw; ++q)
+                        if (hw[q] == gid) {
+                            first = false;
+                            break;
+                        }
+                    if (first) {
+                        int mult = 1;
+                        for (int q = jw + 1; q < rp.win; ++q) mult += (hw[q] == gid) ? 1 : 0;
+                        const float raw = row_logits[gid - a.id_offset];
+                        float v = raw;
+                        for (int c = 0; c < mult; ++c) v = (v > 0.0f) ? v / pen : v * pen;
+                        key = make_key(v, gid);
+                        app = true;
+                        if (gid == 0) {
+                            z_hit = true;
+                            z_nan = (v != v);
+                        }
+                        if (LSE && M > -INFINITY)
+                            dl += exp2(((double)v - (double)M) * (double)lc) -
+                                  exp2(((double)raw - (double)M) * (double)lc);
+                    }
+                }
+            }
+            wappend(ws.cand, w.count, app, key, below);
+        }
+        const unsigned zm = __ballot_sync(kFull, z_hit);
+        if (zm) x0n = __shfl_sync(kFull, z_nan, __ffs(zm) - 1);
+        if (LSE) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) dl += __shfl_xor_sync(kFull, dl, o);
+            Sx = (float)((double)Sx + dl);
+        }
+        __syncwarp();
+    }
+    // The row's top-ksel restricted to this piece is within the piece's own
+    // top-ksel (final values): that is all the block has to carry.
+    const uint32_t ksel = (uint32_t)rp.ksel;
+    if (w.count > ksel) {
+        const uint64_t T = warp_kth(ws.cand, w.count, ksel, ws.hist, lane);
+        w.count = warp_keep(ws.cand, w.count, T, lane);
+    }
+    uint8_t* pp = a.wpart + ((int64_t)gw * a.wl_P + j) * a.wl_stride;
+    const uint32_t cap = (uint32_t)((a.wl_stride - kPartialHeaderBytes) / 8);
+    ZS_CHECK(w.count <= cap && j < a.wl_P, 21, ((uint64_t)j << 32) | w.count);
+    const uint32_t n = w.count < cap ? w.count : cap;
+    unsigned long long* keys = reinterpret_cast<unsigned long long*>(pp + kPartialHeaderBytes);
+    for (uint32_t i = lane; i < n; i += 32) __stcg(keys + i, (unsigned long long)ws.cand[i]);
+    if (lane == 0) {
+        uint4 hv;
+        hv.x = n;
+        hv.y = (has0 ? kPartHasId0 : 0u) | ((has0 && x0n) ? kPartX0Nan : 0u);
+        hv.z = __float_as_uint(M);
+        hv.w = __float_as_uint(Sx);
+        __stcg(reinterpret_cast<uint4*>(pp), hv);
+    }
+    __syncwarp();
+}
+
+template <bool LSE>
+__global__ void __launch_bounds__(kWThreads, 1) zs_wselect_kernel(const Args a) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    WSelSmem& sm = *reinterpret_cast<WSelSmem*>(smem_raw);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    WarpSel& ws = sm.w[warp];
+    const int32_t gw = blockIdx.x * kWWarps + warp;
+    if (gw >= a.wl_NW) return;  // the whole warp; nothing in this kernel syncs the block
+    WShare sh;
+    sh.b0 = wl_bound(a.wl_E, a.wl_NW, gw);
+    sh.b1 = wl_bound(a.wl_E, a.wl_NW, gw + 1);
+    if (sh.b0 >= sh.b1) return;
+    sh.r0 = (int32_t)(sh.b0 / a.wl_Vn);
+    sh.np = (int32_t)((sh.b1 - 1) / a.wl_Vn) - sh.r0 + 1;
+    if (lane == 0) {
+        for (int s = 0; s < kWStages; ++s) mbar_init(&ws.full[s], 1);
+        mbar_fence_init();
+    }
+    __syncwarp();
+    const uint64_t pol = l2_evict_first_policy();
+    const unsigned below = lanemask_lt();
+
+    WIssue is;
+    is.j = 0;
+    is.t = 0;
+    is.pc = wl_piece(a, sh.b0, sh.b1, sh.r0, 0);
+    int32_t issued = 0, consumed = 0;
+    for (int s = 0; s < kWStages; ++s) {
+        if (!wl_issue(a, ws, s, is, sh, pol, lane)) break;
+        ++issued;
+    }
+    bool ok = true;
+    for (int32_t j = 0; j < sh.np && ok; ++j) {
+        const WPiece pc = wl_piece(a, sh.b0, sh.b1, sh.r0, j);
+        if (!pc.active) continue;
+        const RowPlan rp = plan_row(load_params(a.row_params, a.shared, pc.row), a.V_total, a.hist,
+                                    a.hist_len, a.hist_ld, pc.row);
+        const bool greedy_np = rp.greedy && !rp.penal;
+        const uint32_t keff = (uint32_t)rp.keff;
+        const uint32_t compact_at =
+            min((uint32_t)(kWCap - kWStepElems), keff + (keff > 128u ? keff : 128u));
+        const float lc = (rp.greedy ? 1.0f : 1.0f / rp.p.temp) * 1.4426950408889634f;
+        const float* row_logits = a.logits + (int64_t)pc.row * a.ld;
+        const int32_t id_col0 = a.id_offset;  // global id of local column 0
+        WState w;
+        w.count = 0u;
+        w.tau_key = 0ull;
+        w.tau_f = -INFINITY;
+        w.tau_id = 0;
+        w.mode = kWAll;
+        w.kb = 0ull;
+        w.vb = -INFINITY;
+        w.lm = -INFINITY;
+        w.ls = 0.0f;
+        // head: the columns before the first 16-byte boundary (at most 3)
+        {
+            const int nh = pc.e0 - pc.c0;
+            const bool okh = lane < nh;
+            const float x = okh ? row_logits[pc.c0 + lane] : 0.0f;
+            wfilter1<LSE>(ws, w, okh, x, id_col0 + pc.c0 + lane, greedy_np, keff, lc, below, lane);
+        }
+        for (int t = 0; t < pc.ntiles; ++t) {
+            const int stage = consumed % kWStages;
+            const uint32_t parity = (uint32_t)(consumed / kWStages) & 1u;
+            const bool got = mbar_wait_bounded(&ws.full[stage], parity);
+            if (!__all_sync(kFull, got)) {
+                ok = false;
+                break;
+            }
+            const int start = pc.e0 + t * kWTile;
+            const int n = min(kWTile, pc.e1 - start);
+            const float4* t4 = reinterpret_cast<const float4*>(ws.ring[stage]);
+            if (greedy_np || w.mode != kWFast) {
+                wfilter_tile<LSE>(ws, w, t4, n >> 2, id_col0 + start, greedy_np, keff, lc, below,
+                                  lane);
+            } else if (!wfilter_tile_fast<LSE>(ws, w, ws.ring[stage], n >> 2, id_col0 + start,
+                                               keff, lc, lane)) {
+                // too many survivors for one batch: the per-step path (log-sum-exp done)
+                wfilter_tile<false>(ws, w, t4, n >> 2, id_col0 + start, false, keff, lc, below,
+                                    lane);
+            }
+            // Raise the threshold early: fewer elements reach it afterwards.
+            if (!greedy_np && w.count > compact_at) wcompact(ws, w, keff, lane);
+            ++consumed;
+            __syncwarp();
+            if (wl_issue(a, ws, stage, is, sh, pol, lane)) ++issued;
+        }
+        if (!ok) break;
+        // tail: the columns after the last 16-byte boundary (at most 3)
+        {
+            const int nt = pc.c1 - pc.e1;
+            const bool okt = lane < nt;
+            const float x = okt ? row_logits[pc.e1 + lane] : 0.0f;
+            wfilter1<LSE>(ws, w, okt, x, id_col0 + pc.e1 + lane, greedy_np, keff, lc, below, lane);
+        }
+        wend_piece<LSE>(a, ws, w, pc, rp, greedy_np, lc, gw, j, below, lane);
+    }
+    if (!ok) {
+        if (lane == 0) set_status(a.status, kStatusTimeout);
+        // leave no copy in flight into this warp's stages
+        for (int32_t g = consumed; g < issued; ++g)
+            mbar_wait_bounded(&ws.full[g % kWStages], (uint32_t)(g / kWStages) & 1u);
     }
 }
 
@@ -1817,7 +2444,7 @@ __global__ void __launch_bounds__(kNC) zs_large_kernel(const Args a) {
     for (int row = blockIdx.x; row < a.B; row += gridDim.x) {
         const RowPlan rp = plan_row(load_params(a.row_params, a.shared, row), a.V_total, a.hist,
                                     a.hist_len, a.hist_ld, row);
-        if (rp.fast) continue;
+        if (!rp.large) continue;
         const float* x = a.logits + (int64_t)row * a.ld;
         for (int i = ctid; i < a.V; i += kNC) keys[i] = make_key(x[i], a.id_offset + i);
         __threadfence_block();

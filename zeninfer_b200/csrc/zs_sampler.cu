@@ -55,15 +55,32 @@ struct DeviceGuard {
     }
 };
 
-constexpr int kShardLayoutCtas = 296;  // fixed, so every rank derives the same block layout
+// Fixed layouts of the vocab-sharded mode, so every rank derives the same blocks.
+constexpr int kShardLayoutCtas = 296;
+constexpr int kShardLayoutWarps = 148 * zs::kWWarps;
 
+// Where the partial blocks of one call go, and which kernels run.  The block
+// areas depend only on the batch, the columns and the params (never on whether a
+// history is passed), so the ranks of a vocab shard agree on them.
 struct Plan {
-    int S = 1;
-    int slice = 0;
     int max_ksel = 1;
     bool any_large = false;
     bool any_penal = false;
+    // zs_select_kernel rows: [B][S] blocks at offset 0
+    bool cta_area = false;    // the layout holds them
+    bool launch_cta = false;  // some row of this call needs the kernel
+    int S = 1;
+    int slice = 0;
     int64_t part_stride = 0;
+    // zs_wselect_kernel rows: warp-piece blocks at wl_off
+    bool any_warp = false;
+    int64_t wl_E = 0;
+    int32_t wl_NW = 1;
+    int32_t wl_P = 1;
+    int32_t wl_Vn = 1;
+    int64_t wl_stride = 0;
+    int64_t wl_off = 0;
+    int64_t bytes = 0;  // all blocks of one rank
 };
 
 int ksel_of(const zs_params& p, int V_total) {
@@ -77,9 +94,9 @@ int win_bound_of(const zs_params& p) {
     return std::max(0, p.repeat_last_n);
 }
 
-// Keys one partial block can hold for a row: the unit epilogue keeps the top
-// keff = ksel + window plus the compaction's slack, then appends up to `window`
-// penalised values.
+// Keys one zs_select_kernel block can hold for a row: the unit epilogue keeps the
+// top keff = ksel + window plus the compaction's slack, then appends up to
+// `window` penalised values.
 int64_t partial_keys_for(int ksel, int wb) {
     const uint32_t keff = (uint32_t)std::min<int64_t>((int64_t)ksel + wb, zs::kKeffFastMax);
     const uint32_t slack = zs::slack_for(keff);
@@ -94,32 +111,64 @@ int choose_slices(int B, int V, int ctas) {
     return (int)std::max(1L, std::min((long)smax, want));
 }
 
+int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+// Cuts the [B][V_cols] batch among `layout_warps` warps (each at least
+// kWMinElems columns) and sizes the warp-piece blocks for shortlists <= max_ksel.
+void plan_warp_layout(Plan& pl, int B, int V_cols, int layout_warps, int max_ksel) {
+    pl.wl_Vn = std::max(1, V_cols);
+    pl.wl_E = (int64_t)B * pl.wl_Vn;
+    const int64_t by_size = std::max<int64_t>(1, pl.wl_E / zs::kWMinElems);
+    pl.wl_NW = (int32_t)std::max<int64_t>(1, std::min<int64_t>(layout_warps, by_size));
+    const int64_t share = (pl.wl_E + pl.wl_NW - 1) / pl.wl_NW;
+    pl.wl_P = (int32_t)((share + pl.wl_Vn - 1) / pl.wl_Vn + 1);
+    pl.wl_stride = round_up(zs::kPartialHeaderBytes + 8LL * std::max(1, max_ksel), 16);
+}
+
 Plan make_plan(int B, int V_cols, int V_total, const zs_params* params, int per_row, int ctas,
-               bool have_history) {
+               int layout_warps, bool have_history) {
     Plan pl;
     const int np = per_row ? B : 1;
     int64_t max_keys = 1;
+    int max_ksel_w = 1;
     for (int i = 0; i < np; ++i) {
         const zs_params& p = params[i];
         const int ks = ksel_of(p, V_total);
-        const int wb = win_bound_of(p);  // the block layout must not depend on history presence
+        const int wb = win_bound_of(p);
         pl.max_ksel = std::max(pl.max_ksel, ks);
         if (have_history && wb > 0) pl.any_penal = true;
-        // A row leaves the fast kernels when its shortlist alone is too long, or
-        // (with a history) shortlist + window or the window is; the device-side
-        // plan uses the actual window, never longer than this bound.
+        // The device puts a row on the warp path when ksel + its actual window
+        // fits (the window is empty without a history); on the CTA path when
+        // that is too long but fits kKeffFastMax; the rest on the large path.
+        if (ks <= zs::kWKeffMax) {
+            pl.any_warp = true;
+            max_ksel_w = std::max(max_ksel_w, ks);
+        }
+        const bool long_win = wb > 0 && (ks + wb > zs::kWKeffMax || wb > zs::kWWinMax);
+        if (ks <= zs::kKeffFastMax && (ks > zs::kWKeffMax || long_win)) {
+            pl.cta_area = true;
+            max_keys = std::max(max_keys, partial_keys_for(ks, wb));
+            if (ks > zs::kWKeffMax || have_history) pl.launch_cta = true;
+        }
         if (ks > zs::kKeffFastMax ||
             (have_history && ((long)ks + wb > zs::kKeffFastMax || wb > zs::kWinFastMax)))
             pl.any_large = true;
-        max_keys = std::max(max_keys, partial_keys_for(ks, wb));
     }
     pl.S = choose_slices(B, V_cols, ctas);
     const int per = (V_cols + pl.S - 1) / pl.S;
     pl.slice = std::max(4, (per + 3) & ~3);
     pl.S = std::max(1, (V_cols + pl.slice - 1) / pl.slice);
-    pl.part_stride = ((int64_t)zs::kPartialHeaderBytes + 8LL * max_keys + 15) & ~15LL;
+    pl.part_stride = round_up(zs::kPartialHeaderBytes + 8LL * max_keys, 16);
+    const int64_t cta_bytes = pl.cta_area ? (int64_t)B * pl.S * pl.part_stride : 0;
+    plan_warp_layout(pl, B, V_cols, layout_warps, max_ksel_w);
+    pl.wl_off = round_up(cta_bytes, 256);
+    pl.bytes = pl.wl_off + (pl.any_warp ? (int64_t)pl.wl_NW * pl.wl_P * pl.wl_stride : 0);
     return pl;
 }
+
+// Columns per rank the shard layout is cut for: equal slices, the last one also
+// taking the remainder (the largest shard that convention gives).
+int shard_cols(int V_total, int n_ranks) { return V_total / n_ranks + V_total % n_ranks; }
 
 // ---- NCCL, resolved at run time from the libnccl.so.2 this process uses ----
 struct NcclApi {
@@ -154,6 +203,8 @@ struct zs_context {
     size_t select_smem = 0;
     size_t merge_smem = 0;
     size_t warp_merge_smem = 0;
+    size_t wsel_smem = 0;
+    int wsel_warps = 0;  // warps of one full zs_wselect_kernel launch
     // scratch, grown on demand (never shrinks)
     uint8_t* part = nullptr;
     size_t part_bytes = 0;
@@ -294,75 +345,117 @@ zs_status launch_merge(zs_context* h, const zs::MergeArgs& m, int max_ksel, bool
     return ZS_OK;
 }
 
-zs_status launch_select(zs_context* h, const zs::Args& base, const Plan& pl, bool want_lse,
-                        cudaStream_t st) {
-    zs_status s_status_ = ZS_OK;
-    zs::Args a = base;
+zs::MergeArgs merge_args_for(const zs::Args& a, const Plan& pl, const uint8_t* gathered, int G,
+                             int64_t rank_stride) {
+    zs::MergeArgs m;
+    std::memset(&m, 0, sizeof(m));
+    m.gathered = gathered;
+    m.rank_stride = rank_stride;
+    m.G = G;
+    m.S = pl.S;
+    m.part_stride = pl.part_stride;
+    m.B = a.B;
+    m.V_total = a.V_total;
+    m.shared = a.shared;
+    m.row_params = a.row_params;
+    m.hist_len = a.hist_len;
+    m.hist_ld = a.hist_ld;
+    m.hist = a.hist;
+    m.rng = a.rng;
+    m.out_ids = a.out_ids;
+    m.info = a.info;
+    m.cand_ids = a.cand_ids;
+    m.cand_probs = a.cand_probs;
+    m.cand_ld = a.cand_ld;
+    m.status = a.status;
+    m.wl_off = pl.wl_off;
+    m.wl_E = pl.wl_E;
+    m.wl_stride = pl.wl_stride;
+    m.wl_NW = pl.wl_NW;
+    m.wl_P = pl.wl_P;
+    m.wl_Vn = pl.wl_Vn;
+    return m;
+}
+
+// Launches the select kernels that write one rank's partial blocks: the warp
+// kernel for warp-path rows, the CTA kernel (and its exact redo) for the rest
+// of the rows up to kKeffFastMax.  `blocks` is the rank's block area; a.status,
+// a.fail_count and a.fail_units (>= B * S entries) are set by the caller.
+zs_status launch_partials(zs_context* h, zs::Args a, const Plan& pl, uint8_t* blocks,
+                          bool want_lse, cudaStream_t st) {
     a.S = pl.S;
     a.slice = pl.slice;
     a.n_units = (int32_t)std::min<int64_t>((int64_t)a.B * pl.S, INT32_MAX);
     a.part_stride = pl.part_stride;
-    a.status = h->status;
-    const bool split = (a.mode == 0);  // drawn by zs_merge_kernel after the partials
-    if (split) {
-        zs_status s = grow((void**)&h->part, &h->part_bytes, (size_t)a.B * pl.S * pl.part_stride);
-        if (s != ZS_OK) return s;
-        a.part = h->part;
+    a.part = blocks;
+    a.wpart = blocks + pl.wl_off;
+    a.wl_E = pl.wl_E;
+    a.wl_stride = pl.wl_stride;
+    a.wl_NW = pl.wl_NW;
+    a.wl_P = pl.wl_P;
+    a.wl_Vn = pl.wl_Vn;
+    if (pl.any_warp) {
+        const int grid = (pl.wl_NW + zs::kWWarps - 1) / zs::kWWarps;
+        LaunchScope scope(h, 0, st);
+        if (want_lse)
+            zs::zs_wselect_kernel<true><<<grid, zs::kWThreads, h->wsel_smem, st>>>(a);
+        else
+            zs::zs_wselect_kernel<false><<<grid, zs::kWThreads, h->wsel_smem, st>>>(a);
+        ZS_CUDA(cudaGetLastError());
     }
-    if ((size_t)a.n_units > h->fail_units_n) {
-        if (h->fail_units) cudaFree(h->fail_units);
-        h->fail_units = nullptr;
-        h->fail_units_n = 0;
-        const size_t n = std::max((size_t)a.n_units, (size_t)4096);
-        ZS_CUDA(cudaMalloc((void**)&h->fail_units, n * sizeof(int32_t)));
-        h->fail_units_n = n;
+    if (pl.launch_cta) {
+        a.redo = 0;
+        ZS_CUDA(cudaMemsetAsync(a.fail_count, 0, sizeof(unsigned), st));
+        const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(a.n_units, h->select_ctas));
+        for (int pass = 0; pass < 2; ++pass) {
+            a.redo = pass;  // pass 1 redoes the units listed by pass 0 (usually none)
+            LaunchScope scope(h, 0, st);
+            if (want_lse)
+                zs::zs_select_kernel<true><<<grid, zs::kThreads, h->select_smem, st>>>(a);
+            else
+                zs::zs_select_kernel<false><<<grid, zs::kThreads, h->select_smem, st>>>(a);
+            ZS_CUDA(cudaGetLastError());
+        }
+    }
+    return ZS_OK;
+}
+
+zs_status ensure_fail_units(zs_context* h, int64_t units) {
+    if ((size_t)units <= h->fail_units_n) return ZS_OK;
+    if (h->fail_units) cudaFree(h->fail_units);
+    h->fail_units = nullptr;
+    h->fail_units_n = 0;
+    const size_t n = std::max((size_t)units, (size_t)4096);
+    ZS_CUDA(cudaMalloc((void**)&h->fail_units, n * sizeof(int32_t)));
+    h->fail_units_n = n;
+    return ZS_OK;
+}
+
+// zs_sample's launches: partial blocks in the handle's scratch, the merge (which
+// sorts and draws every row of the two fast paths), then the large path.
+zs_status launch_select(zs_context* h, const zs::Args& base, const Plan& pl, bool want_lse,
+                        cudaStream_t st) {
+    zs::Args a = base;
+    a.status = h->status;
+    zs_status s = grow((void**)&h->part, &h->part_bytes, (size_t)std::max<int64_t>(pl.bytes, 16));
+    if (s != ZS_OK) return s;
+    if (pl.launch_cta) {
+        s = ensure_fail_units(h, (int64_t)a.B * pl.S);
+        if (s != ZS_OK) return s;
     }
     a.fail_count = h->fail_count;
     a.fail_units = h->fail_units;
-    a.redo = 0;
-    ZS_CUDA(cudaMemsetAsync(h->fail_count, 0, sizeof(unsigned), st));
-    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(a.n_units, h->select_ctas));
-    for (int pass = 0; pass < 2; ++pass) {
-        a.redo = pass;  // pass 1 redoes the units listed by pass 0 (usually none)
-        LaunchScope scope(h, 0, st);
-        if (want_lse)
-            zs::zs_select_kernel<true><<<grid, zs::kThreads, h->select_smem, st>>>(a);
-        else
-            zs::zs_select_kernel<false><<<grid, zs::kThreads, h->select_smem, st>>>(a);
-        ZS_CUDA(cudaGetLastError());
-    }
-    if (split) {
-        zs::MergeArgs m;
-        std::memset(&m, 0, sizeof(m));
-        m.gathered = a.part;
-        m.rank_stride = 0;
-        m.G = 1;
-        m.S = pl.S;
-        m.part_stride = pl.part_stride;
-        m.B = a.B;
-        m.V_total = a.V_total;
-        m.shared = a.shared;
-        m.row_params = a.row_params;
-        m.hist_len = a.hist_len;
-        m.hist_ld = a.hist_ld;
-        m.hist = a.hist;
-        m.rng = a.rng;
-        m.out_ids = a.out_ids;
-        m.info = a.info;
-        m.cand_ids = a.cand_ids;
-        m.cand_probs = a.cand_probs;
-        m.cand_ld = a.cand_ld;
-        m.status = h->status;
-        s_status_ = launch_merge(h, m, pl.max_ksel, want_lse, st);
-        if (s_status_ != ZS_OK) return s_status_;
+    s = launch_partials(h, a, pl, h->part, want_lse, st);
+    if (s != ZS_OK) return s;
+    if (pl.any_warp || pl.cta_area) {
+        const zs::MergeArgs m = merge_args_for(a, pl, h->part, 1, 0);
+        s = launch_merge(h, m, pl.max_ksel, want_lse, st);
+        if (s != ZS_OK) return s;
     }
     if (pl.any_large) {
-        if (a.mode != 0)
-            return fail(ZS_ERR_INVALID_ARGUMENT,
-                        "vocab-sharded sampling needs top_k + repeat window <= 2048");
         const int lgrid = std::max(1, std::min(a.B, h->num_sms));
         const int64_t per_cta = ((int64_t)a.V * 24 + 255) & ~255LL;
-        zs_status s = grow((void**)&h->large, &h->large_bytes, (size_t)per_cta * lgrid);
+        s = grow((void**)&h->large, &h->large_bytes, (size_t)per_cta * lgrid);
         if (s != ZS_OK) return s;
         a.large_ws = h->large;
         a.large_ws_per_cta = per_cta;
@@ -417,6 +510,7 @@ zs_status zs_create(int device, zs_handle* out) {
     h->select_smem = sizeof(zs::FastSmem);
     h->merge_smem = sizeof(zs::CandState);
     h->warp_merge_smem = sizeof(zs::WarpMergeSmem);
+    h->wsel_smem = sizeof(zs::WSelSmem);
     auto cleanup = [&](zs_status s) {
         delete h;
         return s;
@@ -429,8 +523,15 @@ zs_status zs_create(int device, zs_handle* out) {
         (e = cudaFuncSetAttribute(zs::zs_large_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->merge_smem)) != cudaSuccess ||
         (e = cudaFuncSetAttribute(zs::zs_large_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->merge_smem)) != cudaSuccess ||
         (e = cudaFuncSetAttribute(zs::zs_warp_merge_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->warp_merge_smem)) != cudaSuccess ||
-        (e = cudaFuncSetAttribute(zs::zs_warp_merge_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->warp_merge_smem)) != cudaSuccess)
+        (e = cudaFuncSetAttribute(zs::zs_warp_merge_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->warp_merge_smem)) != cudaSuccess ||
+        (e = cudaFuncSetAttribute(zs::zs_wselect_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->wsel_smem)) != cudaSuccess ||
+        (e = cudaFuncSetAttribute(zs::zs_wselect_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->wsel_smem)) != cudaSuccess)
         return cleanup(cuda_fail(e, "cudaFuncSetAttribute"));
+    int wsel_per_sm = 0;
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&wsel_per_sm, zs::zs_wselect_kernel<false>, zs::kWThreads, h->wsel_smem)) != cudaSuccess)
+        return cleanup(cuda_fail(e, "occupancy query"));
+    if (wsel_per_sm < 1) return cleanup(fail(ZS_ERR_NO_DEVICE, "zs_wselect_kernel does not fit an SM"));
+    h->wsel_warps = wsel_per_sm * h->num_sms * zs::kWWarps;
     int per_sm = 0;
     if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, zs::zs_select_kernel<false>, zs::kThreads, h->select_smem)) != cudaSuccess)
         return cleanup(cuda_fail(e, "occupancy query"));
@@ -514,7 +615,8 @@ zs_status zs_sample(zs_handle h, const float* logits, int64_t ld, int32_t batch,
     const zs::Params* dparams = nullptr;
     s = upload_params(h, params, params_per_row, batch, st, &dparams);
     if (s != ZS_OK) return s;
-    const Plan pl = make_plan(batch, n_vocab, n_vocab, params, params_per_row, h->select_ctas, have_hist);
+    const Plan pl = make_plan(batch, n_vocab, n_vocab, params, params_per_row, h->select_ctas,
+                              h->wsel_warps, have_hist);
     zs::Args a;
     std::memset(&a, 0, sizeof(a));
     a.logits = logits;
@@ -573,10 +675,9 @@ zs_status zs_shard_partial_bytes(int32_t batch, int32_t n_vocab_total, int32_t n
                                  int64_t* out_bytes) {
     if (!out_bytes || !params || batch < 0 || n_vocab_total <= 0 || n_ranks <= 0)
         return fail(ZS_ERR_INVALID_ARGUMENT, "bad shard layout arguments");
-    const int per_rank = (n_vocab_total + n_ranks - 1) / n_ranks;
-    const Plan pl = make_plan(batch, per_rank, n_vocab_total, params, params_per_row,
-                              kShardLayoutCtas, false);
-    *out_bytes = (int64_t)batch * pl.S * pl.part_stride;
+    const Plan pl = make_plan(batch, shard_cols(n_vocab_total, n_ranks), n_vocab_total, params,
+                              params_per_row, kShardLayoutCtas, kShardLayoutWarps, false);
+    *out_bytes = pl.bytes;
     return ZS_OK;
 }
 
@@ -598,12 +699,15 @@ zs_status zs_shard_partials(zs_handle h, const float* logits_local, int64_t ld, 
     DeviceGuard g(h->device);
     if (!g.ok) return fail(ZS_ERR_CUDA, "cudaSetDevice failed");
     const bool have_hist = history && history_len;
+    const int cols = shard_cols(n_vocab_total, n_ranks);
+    if (n_local > cols)
+        return fail(ZS_ERR_INVALID_ARGUMENT,
+                    "n_local above V / n_ranks + V % n_ranks (the largest equal-slice shard)");
     const zs::Params* dparams = nullptr;
     s = upload_params(h, params, params_per_row, batch, st, &dparams);
     if (s != ZS_OK) return s;
-    const int per_rank = (n_vocab_total + n_ranks - 1) / n_ranks;
-    Plan pl = make_plan(batch, per_rank, n_vocab_total, params, params_per_row, kShardLayoutCtas,
-                        have_hist);
+    Plan pl = make_plan(batch, cols, n_vocab_total, params, params_per_row, kShardLayoutCtas,
+                        kShardLayoutWarps, have_hist);
     if (pl.any_large)
         return fail(ZS_ERR_INVALID_ARGUMENT, "vocab-sharded sampling needs top_k + repeat window <= 2048");
     // Same S on every rank; this rank's slice length covers its own columns.
@@ -623,10 +727,16 @@ zs_status zs_shard_partials(zs_handle h, const float* logits_local, int64_t ld, 
     a.hist_ld = history_ld;
     a.hist_len = have_hist ? history_len : nullptr;
     a.mode = 1;
-    a.part = (uint8_t*)partial_out;
-    // unit_geom needs a valid base address even for an empty shard
+    a.status = h->status;
+    // the geometry helpers need a valid base address even for an empty shard
     if (n_local <= 0) a.logits = (const float*)partial_out;
-    return launch_select(h, a, pl, want_log_z != 0, st);
+    if (pl.launch_cta) {
+        s = ensure_fail_units(h, (int64_t)batch * pl.S);
+        if (s != ZS_OK) return s;
+    }
+    a.fail_count = h->fail_count;
+    a.fail_units = h->fail_units;
+    return launch_partials(h, a, pl, (uint8_t*)partial_out, want_log_z != 0, st);
 }
 
 zs_status zs_shard_merge(zs_handle h, const void* gathered, int32_t n_ranks, int32_t batch,
@@ -645,31 +755,26 @@ zs_status zs_shard_merge(zs_handle h, const void* gathered, int32_t n_ranks, int
     const zs::Params* dparams = nullptr;
     zs_status s = upload_params(h, params, params_per_row, batch, st, &dparams);
     if (s != ZS_OK) return s;
-    const int per_rank = (n_vocab_total + n_ranks - 1) / n_ranks;
-    const Plan pl = make_plan(batch, per_rank, n_vocab_total, params, params_per_row,
-                              kShardLayoutCtas, false);
-    zs::MergeArgs m;
-    std::memset(&m, 0, sizeof(m));
-    m.gathered = (const uint8_t*)gathered;
-    m.rank_stride = (int64_t)batch * pl.S * pl.part_stride;
-    m.G = n_ranks;
-    m.S = pl.S;
-    m.part_stride = pl.part_stride;
-    m.B = batch;
-    m.V_total = n_vocab_total;
-    m.shared = to_dev(params[0]);
-    m.row_params = dparams;
-    m.rng = rng_state;
-    m.out_ids = out_ids;
-    m.status = h->status;
+    const Plan pl = make_plan(batch, shard_cols(n_vocab_total, n_ranks), n_vocab_total, params,
+                              params_per_row, kShardLayoutCtas, kShardLayoutWarps, false);
+    zs::Args a;
+    std::memset(&a, 0, sizeof(a));
+    a.B = batch;
+    a.V_total = n_vocab_total;
+    a.shared = to_dev(params[0]);
+    a.row_params = dparams;
+    a.rng = rng_state;
+    a.out_ids = out_ids;
+    a.status = h->status;
     bool want_lse = false;
     if (extras) {
-        m.info = reinterpret_cast<zs::RowInfo*>(extras->row_info);
-        m.cand_ids = extras->cand_ids;
-        m.cand_probs = extras->cand_probs;
-        m.cand_ld = (extras->cand_ids || extras->cand_probs) ? extras->cand_ld : 0;
+        a.info = reinterpret_cast<zs::RowInfo*>(extras->row_info);
+        a.cand_ids = extras->cand_ids;
+        a.cand_probs = extras->cand_probs;
+        a.cand_ld = (extras->cand_ids || extras->cand_probs) ? extras->cand_ld : 0;
         want_lse = extras->want_log_z && extras->row_info;
     }
+    const zs::MergeArgs m = merge_args_for(a, pl, (const uint8_t*)gathered, n_ranks, pl.bytes);
     return launch_merge(h, m, pl.max_ksel, want_lse, st);
 }
 
@@ -758,6 +863,14 @@ zs_status noalloc_setup(int dev, NoAllocDevice** out) {
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d.ctx.merge_smem));
         ZS_CUDA(cudaFuncSetAttribute(zs::zs_warp_merge_kernel<false>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d.ctx.warp_merge_smem));
+        d.ctx.wsel_smem = sizeof(zs::WSelSmem);
+        ZS_CUDA(cudaFuncSetAttribute(zs::zs_wselect_kernel<false>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d.ctx.wsel_smem));
+        int wsel_per_sm = 0;
+        ZS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&wsel_per_sm, zs::zs_wselect_kernel<false>,
+                                                              zs::kWThreads, d.ctx.wsel_smem));
+        if (wsel_per_sm < 1) return fail(ZS_ERR_NO_DEVICE, "zs_wselect_kernel does not fit an SM");
+        d.ctx.wsel_warps = wsel_per_sm * d.ctx.num_sms * zs::kWWarps;
         int per_sm = 0;
         ZS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, zs::zs_select_kernel<false>,
                                                               zs::kThreads, d.ctx.select_smem));
@@ -772,10 +885,21 @@ zs_status noalloc_setup(int dev, NoAllocDevice** out) {
     return ZS_OK;
 }
 
-// Scratch bytes for B rows cut into S slices with blocks of `stride` bytes.
-size_t noalloc_bytes(int64_t B, int64_t S, int64_t stride) {
-    const size_t units = (size_t)(B * S);
-    return kNoAllocHeadBytes + ((units * sizeof(int32_t) + 255) & ~(size_t)255) + units * (size_t)stride;
+// Scratch of one call: head, the CTA kernel's fail list, the partial blocks.
+size_t noalloc_bytes(const Plan& pl, int64_t B) {
+    const size_t units = pl.launch_cta ? (size_t)(B * pl.S) : 0;
+    return kNoAllocHeadBytes + ((units * sizeof(int32_t) + 255) & ~(size_t)255) + (size_t)pl.bytes;
+}
+
+// Re-cuts the CTA kernel's rows into S slices (the warp layout does not move).
+void replan_slices(Plan& pl, int B, int V, int S) {
+    const int per = (V + S - 1) / S;
+    pl.slice = std::max(4, (per + 3) & ~3);
+    pl.S = std::max(1, (V + pl.slice - 1) / pl.slice);
+    const int64_t warp_bytes = pl.bytes - pl.wl_off;
+    const int64_t cta_bytes = pl.cta_area ? (int64_t)B * pl.S * pl.part_stride : 0;
+    pl.wl_off = round_up(cta_bytes, 256);
+    pl.bytes = pl.wl_off + warp_bytes;
 }
 
 }  // namespace
@@ -809,28 +933,24 @@ extern "C" zs_status zs_sample_noalloc(const float* logits, int64_t ld, int32_t 
     NoAllocDevice* d = nullptr;
     zs_status s = noalloc_setup(dev, &d);
     if (s != ZS_OK) return s;
-    Plan pl = make_plan(batch, n_vocab, n_vocab, params, 0, d->ctx.select_ctas, have_hist);
+    Plan pl = make_plan(batch, n_vocab, n_vocab, params, 0, d->ctx.select_ctas, d->ctx.wsel_warps,
+                        have_hist);
     if (pl.any_large)
         return fail(ZS_ERR_INVALID_ARGUMENT,
                     "zs_sample_noalloc: top_k + repeat window above 2048 (or window above 512) "
                     "needs zs_sample");
     const size_t cap = ZS_NOALLOC_SCRATCH_BYTES;
-    if (noalloc_bytes(batch, 1, pl.part_stride) > cap) {
+    // Fewer slices per row when the default cut does not fit (same results).
+    while (pl.S > 1 && noalloc_bytes(pl, batch) > cap) replan_slices(pl, batch, n_vocab, pl.S - 1);
+    if (noalloc_bytes(pl, batch) > cap) {
         char msg[256];
         std::snprintf(msg, sizeof(msg),
                       "zs_sample_noalloc: %d rows need %zu bytes of scratch, the fixed scratch "
                       "holds %zu; split the batch or use zs_sample",
-                      batch, noalloc_bytes(batch, 1, pl.part_stride), cap);
+                      batch, noalloc_bytes(pl, batch), cap);
         return fail(ZS_ERR_INVALID_ARGUMENT, msg);
     }
-    // Fewer slices per row when the default cut does not fit (same results).
-    while (pl.S > 1 && noalloc_bytes(batch, pl.S, pl.part_stride) > cap) {
-        pl.S -= 1;
-        const int per = (n_vocab + pl.S - 1) / pl.S;
-        pl.slice = std::max(4, (per + 3) & ~3);
-        pl.S = std::max(1, (n_vocab + pl.slice - 1) / pl.slice);
-    }
-    const int64_t units = (int64_t)batch * pl.S;
+    const int64_t units = pl.launch_cta ? (int64_t)batch * pl.S : 0;
     if (units > INT32_MAX) return fail(ZS_ERR_INVALID_ARGUMENT, "zs_sample_noalloc: batch too large");
     uint8_t* head = d->scratch;
     int32_t* fail_units = (int32_t*)(d->scratch + kNoAllocHeadBytes);
@@ -850,36 +970,13 @@ extern "C" zs_status zs_sample_noalloc(const float* logits, int64_t ld, int32_t 
     a.rng = rng_state;
     a.out_ids = out_ids;
     a.mode = 0;
-    a.S = pl.S;
-    a.slice = pl.slice;
-    a.n_units = (int32_t)units;
-    a.part_stride = pl.part_stride;
-    a.part = part;
     a.status = device_status ? (int*)device_status : (int*)head;
     a.fail_count = (unsigned*)(head + 4);
     a.fail_units = fail_units;
     // The fail counter must start every call at zero; the status word is cleared too.
     ZS_CUDA(cudaMemsetAsync(head, 0, kNoAllocHeadBytes, st));
-    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(units, d->ctx.select_ctas));
-    for (int pass = 0; pass < 2; ++pass) {
-        a.redo = pass;
-        zs::zs_select_kernel<false><<<grid, zs::kThreads, d->ctx.select_smem, st>>>(a);
-        ZS_CUDA(cudaGetLastError());
-    }
-    zs::MergeArgs m;
-    std::memset(&m, 0, sizeof(m));
-    m.gathered = part;
-    m.G = 1;
-    m.S = pl.S;
-    m.part_stride = pl.part_stride;
-    m.B = batch;
-    m.V_total = n_vocab;
-    m.shared = a.shared;
-    m.hist = a.hist;
-    m.hist_ld = a.hist_ld;
-    m.hist_len = a.hist_len;
-    m.rng = rng_state;
-    m.out_ids = out_ids;
-    m.status = a.status;
+    s = launch_partials(&d->ctx, a, pl, part, false, st);
+    if (s != ZS_OK) return s;
+    const zs::MergeArgs m = merge_args_for(a, pl, part, 1, 0);
     return launch_merge(&d->ctx, m, pl.max_ksel, false, st);
 }
