@@ -1936,6 +1936,77 @@ __device__ __forceinline__ void wappend(uint64_t* cand, uint32_t& count, bool pr
     count += (uint32_t)__popc(m);
 }
 
+// Keeps exactly the kk largest of the unique keys keys[0..n) (n > kk >= 1,
+// n <= 32 * R) at keys[0..kk) and returns the kk-th largest.  The keys sit in
+// registers (R per lane); a binary radix walk from the highest bit in which the
+// keys differ narrows the bucket holding the kk-th key, one warp-wide count
+// (redux.sync) per bit, with no shared-memory atomics.
+template <int R>
+__device__ __forceinline__ uint64_t warp_topk_keep(uint64_t* keys, uint32_t n, uint32_t kk,
+                                                   int lane) {
+    uint64_t k[R];
+    uint32_t alive = 0u;
+#pragma unroll
+    for (int j = 0; j < R; ++j) {
+        const uint32_t i = (uint32_t)lane + 32u * j;
+        const bool v = i < n;
+        k[j] = v ? keys[i] : 0ull;
+        alive |= (uint32_t)v << j;
+    }
+    uint64_t lo = ~0ull, hi = 0ull;
+#pragma unroll
+    for (int j = 0; j < R; ++j) {
+        if ((alive >> j) & 1u) {
+            lo = k[j] < lo ? k[j] : lo;
+            hi = k[j] > hi ? k[j] : hi;
+        }
+    }
+    lo = warp_min_u64(lo);
+    hi = warp_max_u64(hi);
+    uint64_t T = hi;
+    if (kk > 1u) {
+        uint32_t need = kk, cnt = n;
+        for (int bit = 63 - __clzll((long long)(lo ^ hi)); bit >= 0; --bit) {
+            uint32_t ones = 0u;
+#pragma unroll
+            for (int j = 0; j < R; ++j) ones |= (uint32_t)((k[j] >> bit) & 1ull) << j;
+            ones &= alive;
+            const uint32_t c1 = __reduce_add_sync(kFull, (uint32_t)__popc(ones));
+            if (c1 >= need) {
+                alive = ones;
+                cnt = c1;
+            } else {
+                alive &= ~ones;
+                need -= c1;
+                cnt -= c1;
+            }
+            if (cnt == need) break;  // the whole bucket is in: its minimum is the kk-th
+        }
+        uint64_t m = ~0ull;
+#pragma unroll
+        for (int j = 0; j < R; ++j)
+            if ((alive >> j) & 1u) m = k[j] < m ? k[j] : m;
+        T = warp_min_u64(m);
+    }
+    uint32_t keep = 0u;
+#pragma unroll
+    for (int j = 0; j < R; ++j) keep |= (uint32_t)(k[j] >= T) << j;  // padding keys are 0 < T
+    const uint32_t c = (uint32_t)__popc(keep);
+    uint32_t incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += t;
+    }
+    __syncwarp();  // every lane has its keys in registers before any is overwritten
+    uint32_t at = incl - c;
+#pragma unroll
+    for (int j = 0; j < R; ++j)
+        if ((keep >> j) & 1u) keys[at++] = k[j];
+    __syncwarp();
+    return T;
+}
+
 // Threshold modes of the warp filter.
 constexpr int kWAll = 0;    // no threshold yet: every element is a candidate
 constexpr int kWFast = 1;   // float threshold: x > tau_f, or x == tau_f with id < tau_id
@@ -1957,8 +2028,8 @@ struct WState {
 // keff-th key.  For a non-NaN threshold value t, key(x, id) > key(t, tid) is
 // exactly x > t, or x == t and id < tid (-0 == +0, NaN below everything).
 __device__ __forceinline__ void wcompact(WarpSel& ws, WState& w, uint32_t keff, int lane) {
-    w.tau_key = warp_kth(ws.cand, w.count, keff, ws.hist, lane);
-    w.count = warp_keep(ws.cand, w.count, w.tau_key, lane);
+    w.tau_key = warp_topk_keep<kWCap / 32>(ws.cand, w.count, keff, lane);
+    w.count = keff;
     w.tau_f = tau_value(w.tau_key);
     w.tau_id = key_id(w.tau_key);
     w.mode = ((uint32_t)(w.tau_key >> 32) == 0u) ? kWExact : kWFast;
@@ -2205,8 +2276,8 @@ __device__ void wend_piece(const Args& a, WarpSel& ws, WState& w, const WPiece& 
     // top-ksel (final values): that is all the block has to carry.
     const uint32_t ksel = (uint32_t)rp.ksel;
     if (w.count > ksel) {
-        const uint64_t T = warp_kth(ws.cand, w.count, ksel, ws.hist, lane);
-        w.count = warp_keep(ws.cand, w.count, T, lane);
+        warp_topk_keep<kWCap / 32>(ws.cand, w.count, ksel, lane);
+        w.count = ksel;
     }
     uint8_t* pp = a.wpart + ((int64_t)gw * a.wl_P + j) * a.wl_stride;
     const uint32_t cap = (uint32_t)((a.wl_stride - kPartialHeaderBytes) / 8);
