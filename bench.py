@@ -6,9 +6,9 @@ Workload: 4096 rows x 151,936 f32 logits (Qwen2.5-0.5B vocab), distribution of
 workload 5 (N(0, 2.5^2) + row offset + 8 peaks), temp 0.7, top-k 50, top-p 0.9,
 one xorshift64* draw per row.  Synthetic data: no model or dataset exists here.
 
-One step = one zs_sample call over the rank's 4096 rows: the select kernel
-(plus its exact-redo launch, which finds no work on this workload) and the
-per-row merge kernel.
+One step = one zs_sample call over the rank's 4096 rows: the streaming select
+kernel (zs_wselect_kernel: every row of this workload has a top-50 shortlist)
+and the per-row merge kernel.
 With N GPUs (torchrun, one process per GPU) every rank samples its own 4096
 rows (row split, no communication): weak scaling, value = N*4096 rows / max
 over ranks of the step time.  For N > 1 the vocab-sharded mode (partials ->
@@ -61,7 +61,7 @@ def hbm_peak():
 def committed_traffic(rows):
     """dram bytes per launch of zs_select_kernel on this workload, from the
     committed ncu summary (profiles/), scaled to `rows` rows; None if absent."""
-    path = os.path.join(ROOT, "profiles", "zs_select_kernel_workload5.md")
+    path = os.path.join(ROOT, "profiles", "zs_wselect_kernel_workload5.md")
     try:
         txt = open(path).read()
     except OSError:
@@ -291,9 +291,9 @@ def main():
     ms_step = max_over_ranks(ms_total / args.steps)
     value = world * rows / (ms_step / 1e3)
 
-    # Roofline of the dominant kernel, zs_select_kernel (its exact-redo second
-    # launch included), timed by CUDA events around its launches on the
-    # sampler's stream during the timed steps.
+    # Roofline of the dominant kernel, the streaming select (zs_wselect_kernel
+    # here), timed by CUDA events around its launches on the sampler's stream
+    # during the timed steps.
     peak, peak_kind = hbm_peak()
     alg_bytes = rows * ROW_BYTES + rows * 4
     sel_ms = max_over_ranks(kt["select_ms"] / args.steps)
@@ -405,16 +405,16 @@ def main():
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
                          "peak_source": f"hbm_gbs, of {peak_kind}",
-                         "kernel": "zs_select_kernel",
+                         "kernel": "zs_wselect_kernel",
                          "kernel_ms_per_step": sel_ms, "merge_ms_per_step": merge_ms,
                          "algorithmic_bytes_per_launch": alg_bytes},
             "by_batch": by_batch,
             "clocks": clk,
             "e2e": e2e,
             "gpu_launches": kt["launches"],
-            "gpu_launches_by_kernel": {"zs_select_kernel": kt["select_launches"],
+            "gpu_launches_by_kernel": {"select": kt["select_launches"],
                                        "merge": kt["merge_launches"],
-                                       "zs_large_kernel": kt["large_launches"]},
+                                       "large": kt["large_launches"]},
             "cpu_baseline": cpu,
         }
         if sharded:
