@@ -59,7 +59,7 @@ def hbm_peak():
 
 
 def committed_traffic(rows):
-    """dram bytes per launch of zs_select_kernel on this workload, from the
+    """dram bytes per launch of the select kernel on this workload, from the
     committed ncu summary (profiles/), scaled to `rows` rows; None if absent."""
     path = os.path.join(ROOT, "profiles", "zs_wselect_kernel_workload5.md")
     try:

@@ -253,6 +253,28 @@ class Sampler:
         return SampleResult(out, info, cand_ids, cand_probs)
 
 
+    def sample_sharded(self, logits_local, vocab_offset, n_vocab_total, n_ranks, params,
+                       rng_state, nccl_comm, out=None, history=None, history_len=None,
+                       stream=None):
+        """zs_sample_sharded: partials, ncclAllGather on `nccl_comm` (an ncclComm_t
+        as an int) and merge in one call.  Every rank passes the same batch,
+        params and rng states and gets the same ids."""
+        import torch
+        B, n_local = logits_local.shape
+        par, per_row = _params_array(params, B)
+        if out is None:
+            out = torch.empty(B, dtype=torch.int32, device=self.device)
+        hist_ptr = history.data_ptr() if history is not None else None
+        hist_len_ptr = history_len.data_ptr() if history_len is not None else None
+        hist_ld = history.shape[1] if history is not None else 0
+        _native.check(self._lib.zs_sample_sharded(
+            self._h, logits_local.data_ptr(), logits_local.stride(0), B, n_local, vocab_offset,
+            n_vocab_total, n_ranks, par, per_row, hist_ptr, hist_ld, hist_len_ptr,
+            rng_state.data_ptr(), out.data_ptr(), None, C.c_void_p(nccl_comm),
+            _stream_ptr(stream)), "zs_sample_sharded")
+        return out
+
+
 # ---- the reference's host-row API ----
 _default = threading.local()
 
