@@ -71,9 +71,10 @@ def _worker(rank, port, q):
         uid = NcclUniqueId()
         if rank == 0:
             assert nccl.ncclGetUniqueId(C.byref(uid)) == 0
-        obj = [bytes(uid.internal) if rank == 0 else None]
+        # the raw 128 bytes (a c_char array's value would stop at the first NUL)
+        obj = [C.string_at(C.addressof(uid), C.sizeof(uid)) if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
-        uid.internal = obj[0]
+        C.memmove(C.addressof(uid), obj[0], C.sizeof(uid))
         comm = C.c_void_p()
         assert nccl.ncclCommInitRank(C.byref(comm), WORLD, uid, rank) == 0
         p = SamplingParams(temp=0.7, top_k=50, top_p=0.9)

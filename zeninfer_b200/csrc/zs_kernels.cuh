@@ -1558,6 +1558,77 @@ __global__ void __launch_bounds__(kNC) zs_merge_kernel(const MergeArgs a) {
     }
 }
 
+// Keeps exactly the kk largest of the unique keys keys[0..n) (n > kk >= 1,
+// n <= 32 * R) at keys[0..kk) and returns the kk-th largest.  The keys sit in
+// registers (R per lane); a binary radix walk from the highest bit in which the
+// keys differ narrows the bucket holding the kk-th key, one warp-wide count
+// (redux.sync) per bit, with no shared-memory atomics.
+template <int R>
+__device__ __forceinline__ uint64_t warp_topk_keep(uint64_t* keys, uint32_t n, uint32_t kk,
+                                                   int lane) {
+    uint64_t k[R];
+    uint32_t alive = 0u;
+#pragma unroll
+    for (int j = 0; j < R; ++j) {
+        const uint32_t i = (uint32_t)lane + 32u * j;
+        const bool v = i < n;
+        k[j] = v ? keys[i] : 0ull;
+        alive |= (uint32_t)v << j;
+    }
+    uint64_t lo = ~0ull, hi = 0ull;
+#pragma unroll
+    for (int j = 0; j < R; ++j) {
+        if ((alive >> j) & 1u) {
+            lo = k[j] < lo ? k[j] : lo;
+            hi = k[j] > hi ? k[j] : hi;
+        }
+    }
+    lo = warp_min_u64(lo);
+    hi = warp_max_u64(hi);
+    uint64_t T = hi;
+    if (kk > 1u) {
+        uint32_t need = kk, cnt = n;
+        for (int bit = 63 - __clzll((long long)(lo ^ hi)); bit >= 0; --bit) {
+            uint32_t ones = 0u;
+#pragma unroll
+            for (int j = 0; j < R; ++j) ones |= (uint32_t)((k[j] >> bit) & 1ull) << j;
+            ones &= alive;
+            const uint32_t c1 = __reduce_add_sync(kFull, (uint32_t)__popc(ones));
+            if (c1 >= need) {
+                alive = ones;
+                cnt = c1;
+            } else {
+                alive &= ~ones;
+                need -= c1;
+                cnt -= c1;
+            }
+            if (cnt == need) break;  // the whole bucket is in: its minimum is the kk-th
+        }
+        uint64_t m = ~0ull;
+#pragma unroll
+        for (int j = 0; j < R; ++j)
+            if ((alive >> j) & 1u) m = k[j] < m ? k[j] : m;
+        T = warp_min_u64(m);
+    }
+    uint32_t keep = 0u;
+#pragma unroll
+    for (int j = 0; j < R; ++j) keep |= (uint32_t)(k[j] >= T) << j;  // padding keys are 0 < T
+    const uint32_t c = (uint32_t)__popc(keep);
+    uint32_t incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += t;
+    }
+    __syncwarp();  // every lane has its keys in registers before any is overwritten
+    uint32_t at = incl - c;
+#pragma unroll
+    for (int j = 0; j < R; ++j)
+        if ((keep >> j) & 1u) keys[at++] = k[j];
+    __syncwarp();
+    return T;
+}
+
 // ---------------------------------------------------------------------------
 // Warp-per-row merge for shortlists up to kWarpMergeMaxK: each warp merges one
 // row's partial blocks in its own shared-memory slot with warp-synchronous
@@ -1569,89 +1640,11 @@ constexpr int kWarpProbOffset = 512;        // f64 probabilities alias cand[512.
 
 struct WarpSlot {
     uint64_t cand[kWarpCap];
-    uint32_t hist[256];
 };
 
 struct WarpMergeSmem {
     WarpSlot w[kConsumerWarps];
 };
-
-// The digit bucket holding the need-th largest key, from 256 per-digit counts.
-__device__ __forceinline__ void warp_pick_bucket(const uint32_t* hist, uint32_t need, int lane,
-                                                 uint32_t& digit, uint32_t& above, uint32_t& cnt) {
-    uint32_t h[8];
-    uint32_t sum = 0;
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-        h[q] = hist[255 - 8 * lane - q];
-        sum += h[q];
-    }
-    uint32_t incl = sum;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t t = __shfl_up_sync(kFull, incl, o);
-        if (lane >= o) incl += t;
-    }
-    const uint32_t before = incl - sum;
-    const bool mine = before < need && incl >= need;
-    uint32_t d = 0, ab = 0, c = 0, cum = before;
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-        if (mine && cum < need && cum + h[q] >= need) {
-            d = 255u - 8u * (uint32_t)lane - (uint32_t)q;
-            ab = cum;
-            c = h[q];
-        }
-        cum += h[q];
-    }
-    const int src = __ffs(__ballot_sync(kFull, mine)) - 1;
-    digit = __shfl_sync(kFull, d, src);
-    above = __shfl_sync(kFull, ab, src);
-    cnt = __shfl_sync(kFull, c, src);
-}
-
-// Exact kk-th largest of the unique keys keys[0..n), n > kk >= 1.
-__device__ uint64_t warp_kth(const uint64_t* keys, uint32_t n, uint32_t kk, uint32_t* hist,
-                             int lane) {
-    uint64_t lo = ~0ull, hi = 0ull;
-    for (uint32_t i = lane; i < n; i += 32) {
-        const uint64_t k = keys[i];
-        lo = k < lo ? k : lo;
-        hi = k > hi ? k : hi;
-    }
-    lo = warp_min_u64(lo);
-    hi = warp_max_u64(hi);
-    if (kk == 1) return hi;
-    const uint64_t diff = lo ^ hi;
-    int shift = diff ? ((63 - __clzll((long long)diff)) >> 3) << 3 : 0;
-    uint64_t mask = shift >= 56 ? 0ull : (~0ull << (shift + 8));
-    uint64_t prefix = lo & mask;
-    uint32_t need = kk;
-    for (;;) {
-#pragma unroll
-        for (int q = 0; q < 8; ++q) hist[lane * 8 + q] = 0u;
-        __syncwarp();
-        for (uint32_t i = lane; i < n; i += 32) {
-            const uint64_t k = keys[i];
-            if ((k & mask) == prefix) atomicAdd(&hist[(uint32_t)(k >> shift) & 255u], 1u);
-        }
-        __syncwarp();
-        uint32_t digit, above, cnt;
-        warp_pick_bucket(hist, need, lane, digit, above, cnt);
-        __syncwarp();
-        prefix |= (uint64_t)digit << shift;
-        mask |= 0xffull << shift;
-        need -= above;
-        if (cnt == need || shift == 0) break;  // the whole bucket is in: its minimum is the kk-th
-        shift -= 8;
-    }
-    uint64_t m = ~0ull;
-    for (uint32_t i = lane; i < n; i += 32) {
-        const uint64_t k = keys[i];
-        if ((k & mask) == prefix && k < m) m = k;
-    }
-    return warp_min_u64(m);
-}
 
 // Keeps the keys >= T of keys[0..n) at the front (in order); returns how many.
 __device__ uint32_t warp_keep(uint64_t* keys, uint32_t n, uint64_t T, int lane) {
@@ -1670,27 +1663,63 @@ __device__ uint32_t warp_keep(uint64_t* keys, uint32_t n, uint64_t T, int lane) 
     return out;
 }
 
-// Sorts keys[0..n) descending, n <= kWarpMergeMaxK (unique keys: rank counting).
-__device__ void warp_sort_desc(uint64_t* keys, uint32_t n, int lane) {
-    constexpr int Q = kWarpMergeMaxK / 32;
-    uint64_t k[Q];
-    uint32_t r[Q];
+// Sorts keys[0..n) descending, n <= SLOTS, in registers: a bitonic network over
+// SLOTS slots (SLOTS / 32 per lane, slot = lane * P + j; unused slots hold 0,
+// which sorts last).
+template <int SLOTS>
+__device__ __forceinline__ void warp_sort_desc_slots(uint64_t* keys, uint32_t n, int lane) {
+    constexpr int P = SLOTS / 32;
+    uint64_t k[P];
 #pragma unroll
-    for (int q = 0; q < Q; ++q) {
-        const uint32_t i = lane + 32 * q;
-        k[q] = i < n ? keys[i] : 0ull;
-        r[q] = 0;
+    for (int j = 0; j < P; ++j) {
+        const uint32_t i = (uint32_t)lane * P + j;
+        k[j] = i < n ? keys[i] : 0ull;
     }
-    for (uint32_t j = 0; j < n; ++j) {
-        const uint64_t kj = keys[j];
 #pragma unroll
-        for (int q = 0; q < Q; ++q) r[q] += kj > k[q] ? 1u : 0u;
+    for (int size = 2; size <= SLOTS; size <<= 1) {
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            if (stride >= P) {
+#pragma unroll
+                for (int j = 0; j < P; ++j) {
+                    const int i = lane * P + j;
+                    const uint64_t p = __shfl_xor_sync(kFull, k[j], stride / P);
+                    const bool desc = (i & size) == 0, lower = (i & stride) == 0;
+                    const uint64_t hi = k[j] > p ? k[j] : p, lo = k[j] > p ? p : k[j];
+                    k[j] = (lower == desc) ? hi : lo;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < P; ++j) {
+                    if ((j & stride) == 0) {
+                        const int i = lane * P + j;
+                        const bool desc = (i & size) == 0;
+                        const uint64_t a = k[j], b = k[j | stride];
+                        if (desc ? (a < b) : (a > b)) {
+                            k[j] = b;
+                            k[j | stride] = a;
+                        }
+                    }
+                }
+            }
+        }
     }
     __syncwarp();
 #pragma unroll
-    for (int q = 0; q < Q; ++q)
-        if (lane + 32 * q < (int)n) keys[r[q]] = k[q];
+    for (int j = 0; j < P; ++j) {
+        const uint32_t i = (uint32_t)lane * P + j;
+        if (i < n) keys[i] = k[j];
+    }
     __syncwarp();
+}
+
+// Sorts keys[0..n) descending, n <= 256, with the smallest network that holds n.
+__device__ __forceinline__ void warp_sort256_desc(uint64_t* keys, uint32_t n, int lane) {
+    if (n <= 1u) return;
+    if (n <= 32u) warp_sort_desc_slots<32>(keys, n, lane);
+    else if (n <= 64u) warp_sort_desc_slots<64>(keys, n, lane);
+    else if (n <= 128u) warp_sort_desc_slots<128>(keys, n, lane);
+    else warp_sort_desc_slots<256>(keys, n, lane);
 }
 
 // f64 tail of sample_token (src/sample.cpp:52-101) over the sorted shortlist
@@ -1840,8 +1869,8 @@ __global__ void __launch_bounds__(kNC) zs_warp_merge_kernel(const MergeArgs a) {
                     reinterpret_cast<const unsigned long long*>(pp + kPartialHeaderBytes);
                 for (uint32_t b = 0; b < cnt; b += 32) {
                     if (count + 32 > (uint32_t)kWarpCap) {
-                        tau = warp_kth(ws.cand, count, ksel, ws.hist, lane);
-                        count = warp_keep(ws.cand, count, tau, lane);  // exactly ksel keys >= tau
+                        tau = warp_topk_keep<kWarpCap / 32>(ws.cand, count, ksel, lane);
+                        count = ksel;  // exactly ksel keys >= tau
                     }
                     const uint32_t i = b + lane;
                     const uint64_t k = i < cnt ? __ldcg(keys + i) : 0ull;
@@ -1854,10 +1883,10 @@ __global__ void __launch_bounds__(kNC) zs_warp_merge_kernel(const MergeArgs a) {
             }
         }
         if (count > ksel) {
-            const uint64_t T = warp_kth(ws.cand, count, ksel, ws.hist, lane);
-            count = warp_keep(ws.cand, count, T, lane);
+            warp_topk_keep<kWarpCap / 32>(ws.cand, count, ksel, lane);
+            count = ksel;
         }
-        warp_sort_desc(ws.cand, count, lane);
+        warp_sort256_desc(ws.cand, count, lane);
         const uint32_t kk = count < ksel ? count : ksel;
         warp_finalize(ws.cand, reinterpret_cast<double*>(ws.cand + kWarpProbOffset), kk, rp, nan0,
                       LSE, M, Sx, row, a.rng, a.out_ids, a.info, a.cand_ids, a.cand_probs,
@@ -1934,77 +1963,6 @@ __device__ __forceinline__ void wappend(uint64_t* cand, uint32_t& count, bool pr
     if (pred && ZS_CHECK(count + __popc(m & below) < (uint32_t)kWCap, 20, count))
         cand[count + __popc(m & below)] = key;
     count += (uint32_t)__popc(m);
-}
-
-// Keeps exactly the kk largest of the unique keys keys[0..n) (n > kk >= 1,
-// n <= 32 * R) at keys[0..kk) and returns the kk-th largest.  The keys sit in
-// registers (R per lane); a binary radix walk from the highest bit in which the
-// keys differ narrows the bucket holding the kk-th key, one warp-wide count
-// (redux.sync) per bit, with no shared-memory atomics.
-template <int R>
-__device__ __forceinline__ uint64_t warp_topk_keep(uint64_t* keys, uint32_t n, uint32_t kk,
-                                                   int lane) {
-    uint64_t k[R];
-    uint32_t alive = 0u;
-#pragma unroll
-    for (int j = 0; j < R; ++j) {
-        const uint32_t i = (uint32_t)lane + 32u * j;
-        const bool v = i < n;
-        k[j] = v ? keys[i] : 0ull;
-        alive |= (uint32_t)v << j;
-    }
-    uint64_t lo = ~0ull, hi = 0ull;
-#pragma unroll
-    for (int j = 0; j < R; ++j) {
-        if ((alive >> j) & 1u) {
-            lo = k[j] < lo ? k[j] : lo;
-            hi = k[j] > hi ? k[j] : hi;
-        }
-    }
-    lo = warp_min_u64(lo);
-    hi = warp_max_u64(hi);
-    uint64_t T = hi;
-    if (kk > 1u) {
-        uint32_t need = kk, cnt = n;
-        for (int bit = 63 - __clzll((long long)(lo ^ hi)); bit >= 0; --bit) {
-            uint32_t ones = 0u;
-#pragma unroll
-            for (int j = 0; j < R; ++j) ones |= (uint32_t)((k[j] >> bit) & 1ull) << j;
-            ones &= alive;
-            const uint32_t c1 = __reduce_add_sync(kFull, (uint32_t)__popc(ones));
-            if (c1 >= need) {
-                alive = ones;
-                cnt = c1;
-            } else {
-                alive &= ~ones;
-                need -= c1;
-                cnt -= c1;
-            }
-            if (cnt == need) break;  // the whole bucket is in: its minimum is the kk-th
-        }
-        uint64_t m = ~0ull;
-#pragma unroll
-        for (int j = 0; j < R; ++j)
-            if ((alive >> j) & 1u) m = k[j] < m ? k[j] : m;
-        T = warp_min_u64(m);
-    }
-    uint32_t keep = 0u;
-#pragma unroll
-    for (int j = 0; j < R; ++j) keep |= (uint32_t)(k[j] >= T) << j;  // padding keys are 0 < T
-    const uint32_t c = (uint32_t)__popc(keep);
-    uint32_t incl = c;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t t = __shfl_up_sync(kFull, incl, o);
-        if (lane >= o) incl += t;
-    }
-    __syncwarp();  // every lane has its keys in registers before any is overwritten
-    uint32_t at = incl - c;
-#pragma unroll
-    for (int j = 0; j < R; ++j)
-        if ((keep >> j) & 1u) keys[at++] = k[j];
-    __syncwarp();
-    return T;
 }
 
 // Threshold modes of the warp filter.

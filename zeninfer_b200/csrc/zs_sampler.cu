@@ -115,18 +115,27 @@ int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 
 // Cuts the [B][V_cols] batch among `layout_warps` warps (each at least
 // kWMinElems columns) and sizes the warp-piece blocks for shortlists <= max_ksel.
-void plan_warp_layout(Plan& pl, int B, int V_cols, int layout_warps, int max_ksel) {
+// Few rows are spread over fewer warps than that when needed, so that the blocks
+// of one row, from all n_ranks ranks, hold at most kCandCap - kCandMargin keys:
+// the merge then gathers a row in one pass.
+void plan_warp_layout(Plan& pl, int B, int V_cols, int layout_warps, int max_ksel, int n_ranks) {
     pl.wl_Vn = std::max(1, V_cols);
     pl.wl_E = (int64_t)B * pl.wl_Vn;
     const int64_t by_size = std::max<int64_t>(1, pl.wl_E / zs::kWMinElems);
-    pl.wl_NW = (int32_t)std::max<int64_t>(1, std::min<int64_t>(layout_warps, by_size));
+    const int64_t blocks_per_row =
+        std::max<int64_t>(1, (zs::kCandCap - zs::kCandMargin) / ((int64_t)std::max(1, max_ksel) *
+                                                                 std::max(1, n_ranks)));
+    // a row spanning w warps' shares owns at most NW / B + 2 of them
+    const int64_t by_merge = (int64_t)B * std::max<int64_t>(1, blocks_per_row - 2);
+    pl.wl_NW = (int32_t)std::max<int64_t>(
+        1, std::min<int64_t>({(int64_t)layout_warps, by_size, by_merge}));
     const int64_t share = (pl.wl_E + pl.wl_NW - 1) / pl.wl_NW;
     pl.wl_P = (int32_t)((share + pl.wl_Vn - 1) / pl.wl_Vn + 1);
     pl.wl_stride = round_up(zs::kPartialHeaderBytes + 8LL * std::max(1, max_ksel), 16);
 }
 
 Plan make_plan(int B, int V_cols, int V_total, const zs_params* params, int per_row, int ctas,
-               int layout_warps, bool have_history) {
+               int layout_warps, bool have_history, int n_ranks = 1) {
     Plan pl;
     const int np = per_row ? B : 1;
     int64_t max_keys = 1;
@@ -160,7 +169,7 @@ Plan make_plan(int B, int V_cols, int V_total, const zs_params* params, int per_
     pl.S = std::max(1, (V_cols + pl.slice - 1) / pl.slice);
     pl.part_stride = round_up(zs::kPartialHeaderBytes + 8LL * max_keys, 16);
     const int64_t cta_bytes = pl.cta_area ? (int64_t)B * pl.S * pl.part_stride : 0;
-    plan_warp_layout(pl, B, V_cols, layout_warps, max_ksel_w);
+    plan_warp_layout(pl, B, V_cols, layout_warps, max_ksel_w, n_ranks);
     pl.wl_off = round_up(cta_bytes, 256);
     pl.bytes = pl.wl_off + (pl.any_warp ? (int64_t)pl.wl_NW * pl.wl_P * pl.wl_stride : 0);
     return pl;
@@ -676,7 +685,7 @@ zs_status zs_shard_partial_bytes(int32_t batch, int32_t n_vocab_total, int32_t n
     if (!out_bytes || !params || batch < 0 || n_vocab_total <= 0 || n_ranks <= 0)
         return fail(ZS_ERR_INVALID_ARGUMENT, "bad shard layout arguments");
     const Plan pl = make_plan(batch, shard_cols(n_vocab_total, n_ranks), n_vocab_total, params,
-                              params_per_row, kShardLayoutCtas, kShardLayoutWarps, false);
+                              params_per_row, kShardLayoutCtas, kShardLayoutWarps, false, n_ranks);
     *out_bytes = pl.bytes;
     return ZS_OK;
 }
@@ -707,7 +716,7 @@ zs_status zs_shard_partials(zs_handle h, const float* logits_local, int64_t ld, 
     s = upload_params(h, params, params_per_row, batch, st, &dparams);
     if (s != ZS_OK) return s;
     Plan pl = make_plan(batch, cols, n_vocab_total, params, params_per_row, kShardLayoutCtas,
-                        kShardLayoutWarps, have_hist);
+                        kShardLayoutWarps, have_hist, n_ranks);
     if (pl.any_large)
         return fail(ZS_ERR_INVALID_ARGUMENT, "vocab-sharded sampling needs top_k + repeat window <= 2048");
     // Same S on every rank; this rank's slice length covers its own columns.
@@ -756,7 +765,7 @@ zs_status zs_shard_merge(zs_handle h, const void* gathered, int32_t n_ranks, int
     zs_status s = upload_params(h, params, params_per_row, batch, st, &dparams);
     if (s != ZS_OK) return s;
     const Plan pl = make_plan(batch, shard_cols(n_vocab_total, n_ranks), n_vocab_total, params,
-                              params_per_row, kShardLayoutCtas, kShardLayoutWarps, false);
+                              params_per_row, kShardLayoutCtas, kShardLayoutWarps, false, n_ranks);
     zs::Args a;
     std::memset(&a, 0, sizeof(a));
     a.B = batch;
