@@ -2095,24 +2095,31 @@ __device__ __forceinline__ bool wfilter_tile_fast(WarpSel& ws, WState& w, const 
                                                   int32_t gid0, uint32_t keff, float lc, int lane) {
     const float4* t4 = reinterpret_cast<const float4*>(tile);
     const float tf = w.tau_f;
-    uint32_t mask = 0u;
+    // one bit per float4 whose largest component reaches the threshold value
+    // (fmaxf ignores NaN, which never passes)
+    uint32_t fmask = 0u;
 #pragma unroll
     for (int q = 0; q < kWTile / kWStepElems; ++q) {
         const int jj = lane + 32 * q;
         if (jj < n4) {
             const float4 v = t4[jj];
-            if (LSE) lse_add4(w.lm, w.ls, v, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)), lc);
-            mask |= ((uint32_t)(v.x >= tf) | ((uint32_t)(v.y >= tf) << 1) |
-                     ((uint32_t)(v.z >= tf) << 2) | ((uint32_t)(v.w >= tf) << 3)) << (4 * q);
+            const float vm = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
+            if (LSE) lse_add4(w.lm, w.ls, v, vm, lc);
+            fmask |= (uint32_t)(vm >= tf) << q;
         }
     }
-    if (!__any_sync(kFull, mask != 0u)) return true;
+    if (!__any_sync(kFull, fmask != 0u)) return true;
+    // exact test of the flagged float4s' components: bit 4q + r of em
     uint32_t em = 0u;
-    for (uint32_t m = mask; m != 0u; m &= m - 1u) {
-        const int b = __ffs(m) - 1;
-        const int e = 4 * (lane + 32 * (b >> 2)) + (b & 3);
-        const float x = tile[e];
-        if (x > tf || (x == tf && gid0 + e < w.tau_id)) em |= 1u << b;
+    for (uint32_t m = fmask; m != 0u; m &= m - 1u) {
+        const int q = __ffs(m) - 1;
+        const int jj = lane + 32 * q;
+        const float4 v = t4[jj];
+        const int32_t id = gid0 + 4 * jj;
+        const float xs[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+            if (xs[r] > tf || (xs[r] == tf && id + r < w.tau_id)) em |= 1u << (4 * q + r);
     }
     const uint32_t c = (uint32_t)__popc(em);
     uint32_t incl = c;
