@@ -1,11 +1,13 @@
 // zs_sampler.cu -- host side of the C ABI in include/zs_sampler.h.
 //
-// Plans a batch (slices per row, scratch sizes, which rows need the large
-// shortlist path), owns the per-device scratch, and launches:
-//   zs_select_kernel  every row whose top-k + penalty window fits the shared
-//                     candidate buffer (all the reference's default shapes)
-//   zs_large_kernel   the remaining rows (top_k > 2048, long penalty windows)
-//   zs_merge_kernel   the vocab-sharded merge after the all-gather
+// Plans a batch (which path each row can take, where the candidate blocks go),
+// owns the per-device scratch, and launches:
+//   zs_wselect_kernel  rows whose shortlist + penalty window is at most 320 (every
+//                      default of the reference)
+//   zs_select_kernel   rows with longer shortlists up to 2048
+//   zs_warp_merge_kernel / zs_merge_kernel  per row: merge the blocks, sort, draw
+//                      (also the vocab-sharded merge after the all-gather)
+//   zs_large_kernel    the remaining rows (top_k > 2048, long penalty windows)
 #include <cuda_runtime.h>
 #include <dlfcn.h>
 
