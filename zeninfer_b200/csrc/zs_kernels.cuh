@@ -1634,9 +1634,8 @@ __device__ __forceinline__ uint64_t warp_topk_keep(uint64_t* keys, uint32_t n, u
 // row's partial blocks in its own shared-memory slot with warp-synchronous
 // steps only (no block barriers), so a CTA keeps eight rows in flight.
 // ---------------------------------------------------------------------------
-constexpr int kWarpCap = 1024;              // candidate keys per warp
+constexpr int kWarpCap = 512;               // candidate keys per warp (4 KB: every CTA resident)
 constexpr uint32_t kWarpMergeMaxK = 256;
-constexpr int kWarpProbOffset = 512;        // f64 probabilities alias cand[512..768)
 
 struct WarpSlot {
     uint64_t cand[kWarpCap];
@@ -1833,8 +1832,103 @@ __device__ void warp_finalize(const uint64_t* cand, double* prob, uint32_t kk, c
     __syncwarp();
 }
 
+// One warp merges one row: reads the headers of up to 32 blocks at once (one
+// lane each), gathers their keys 256 at a time into registers (so one memory
+// latency covers them), keeps the candidates to the top-ksel whenever cand
+// (CAP keys) fills, sorts, and runs the f64 tail and draw.  The f64
+// probabilities use cand[CAP - 256 .. CAP).
+template <int CAP, bool LSE>
+__device__ void warp_merge_row(uint64_t* cand, const MergeArgs& a, int row, const RowPlan& rp,
+                               unsigned below, int lane) {
+    static_assert(CAP >= 2 * (int)kWarpMergeMaxK, "probabilities alias the top of cand");
+    constexpr int J = 8;  // keys per lane per gather round
+    const uint32_t ksel = (uint32_t)rp.ksel;
+    const float lc = (rp.greedy ? 1.0f : 1.0f / rp.p.temp) * 1.4426950408889634f;
+    const BlockSet bs = row_blocks(a, row, rp.wfast);
+    const uint32_t block_cap = (uint32_t)((bs.stride - kPartialHeaderBytes) / 8);
+    const int nb = a.G * bs.n;
+    uint32_t count = 0;
+    uint64_t tau = 0ull;
+    float M = -INFINITY, Sx = 0.0f;
+    bool nan0 = false;
+    for (int g0 = 0; g0 < nb; g0 += 32) {
+        const int b = g0 + lane;
+        unsigned long long base = 0ull;
+        uint32_t c = 0u;
+        float m = -INFINITY, sx = 0.0f;
+        bool z = false;
+        if (b < nb) {
+            const uint8_t* pp = block_at(a, bs, b / bs.n, row, b % bs.n);
+            if (pp != nullptr) {
+                const uint4 hv = __ldcg(reinterpret_cast<const uint4*>(pp));
+                c = hv.x < block_cap ? hv.x : block_cap;
+                m = __uint_as_float(hv.z);
+                sx = __uint_as_float(hv.w);
+                z = (hv.y & kPartHasId0) && (hv.y & kPartX0Nan);
+                base = reinterpret_cast<unsigned long long>(pp + kPartialHeaderBytes);
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float m2 = __shfl_xor_sync(kFull, m, o);
+            const float s2 = __shfl_xor_sync(kFull, sx, o);
+            lse_merge(m, sx, m2, s2, lc);
+        }
+        lse_merge(M, Sx, m, sx, lc);
+        nan0 = nan0 || __any_sync(kFull, z);
+        uint32_t incl = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t t = __shfl_up_sync(kFull, incl, o);
+            if (lane >= o) incl += t;
+        }
+        const uint32_t tot = __shfl_sync(kFull, incl, 31);
+        // lanes past the group never own a key index
+        const uint32_t off = (b < nb) ? incl - c : 0xffffffffu;
+        for (uint32_t i0 = 0; i0 < tot; i0 += 32u * J) {
+            uint64_t k[J];
+#pragma unroll
+            for (int jj = 0; jj < J; ++jj) {
+                const uint32_t i = i0 + 32u * jj + (uint32_t)lane;
+                int lo = 0, hi = 31;  // the last block starting at or before i
+#pragma unroll
+                for (int step = 0; step < 5; ++step) {
+                    const int mid = (lo + hi + 1) >> 1;
+                    if (__shfl_sync(kFull, off, mid) <= i) lo = mid;
+                    else hi = mid - 1;
+                }
+                const unsigned long long bq = __shfl_sync(kFull, base, lo);
+                const uint32_t oq = __shfl_sync(kFull, off, lo);
+                k[jj] = (i < tot) ? __ldcg(reinterpret_cast<const unsigned long long*>(bq) + (i - oq))
+                                  : 0ull;
+            }
+#pragma unroll
+            for (int jj = 0; jj < J; ++jj) {
+                if (count + 32 > (uint32_t)CAP) {
+                    tau = warp_topk_keep<CAP / 32>(cand, count, ksel, lane);
+                    count = ksel;  // exactly ksel keys >= tau
+                }
+                const bool pass = k[jj] > tau;
+                const unsigned mk = __ballot_sync(kFull, pass);
+                if (pass) cand[count + __popc(mk & below)] = k[jj];
+                count += __popc(mk);
+                __syncwarp();
+            }
+        }
+    }
+    if (count > ksel) {
+        warp_topk_keep<CAP / 32>(cand, count, ksel, lane);
+        count = ksel;
+    }
+    warp_sort256_desc(cand, count, lane);
+    const uint32_t kk = count < ksel ? count : ksel;
+    warp_finalize(cand, reinterpret_cast<double*>(cand + (CAP - (int)kWarpMergeMaxK)), kk, rp,
+                  nan0, LSE, M, Sx, row, a.rng, a.out_ids, a.info, a.cand_ids, a.cand_probs,
+                  a.cand_ld, lane);
+}
+
 template <bool LSE>
-__global__ void __launch_bounds__(kNC) zs_warp_merge_kernel(const MergeArgs a) {
+__global__ void __launch_bounds__(kNC, 4) zs_warp_merge_kernel(const MergeArgs a) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     WarpMergeSmem& sm = *reinterpret_cast<WarpMergeSmem*>(smem_raw);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -1844,53 +1938,7 @@ __global__ void __launch_bounds__(kNC) zs_warp_merge_kernel(const MergeArgs a) {
         const RowPlan rp = plan_row(load_params(a.row_params, a.shared, row), a.V_total, a.hist,
                                     a.hist_len, a.hist_ld, row);
         if (rp.large) continue;  // drawn by zs_large_kernel
-        const uint32_t ksel = (uint32_t)rp.ksel;
-        const float lc = (rp.greedy ? 1.0f : 1.0f / rp.p.temp) * 1.4426950408889634f;
-        const BlockSet bs = row_blocks(a, row, rp.wfast);
-        const uint32_t block_cap = (uint32_t)((bs.stride - kPartialHeaderBytes) / 8);
-        uint32_t count = 0;
-        uint64_t tau = 0ull;
-        float M = -INFINITY, Sx = 0.0f;
-        bool nan0 = false;
-        for (int g = 0; g < a.G; ++g) {
-            for (int s = 0; s < bs.n; ++s) {
-                const uint8_t* pp = block_at(a, bs, g, row, s);
-                if (pp == nullptr) continue;
-                uint4 hv = make_uint4(0u, 0u, 0u, 0u);
-                if (lane == 0) hv = __ldcg(reinterpret_cast<const uint4*>(pp));
-                hv.x = __shfl_sync(kFull, hv.x, 0);
-                hv.y = __shfl_sync(kFull, hv.y, 0);
-                hv.z = __shfl_sync(kFull, hv.z, 0);
-                hv.w = __shfl_sync(kFull, hv.w, 0);
-                const uint32_t cnt = hv.x < block_cap ? hv.x : block_cap;
-                lse_merge(M, Sx, __uint_as_float(hv.z), __uint_as_float(hv.w), lc);
-                if ((hv.y & kPartHasId0) && (hv.y & kPartX0Nan)) nan0 = true;
-                const unsigned long long* keys =
-                    reinterpret_cast<const unsigned long long*>(pp + kPartialHeaderBytes);
-                for (uint32_t b = 0; b < cnt; b += 32) {
-                    if (count + 32 > (uint32_t)kWarpCap) {
-                        tau = warp_topk_keep<kWarpCap / 32>(ws.cand, count, ksel, lane);
-                        count = ksel;  // exactly ksel keys >= tau
-                    }
-                    const uint32_t i = b + lane;
-                    const uint64_t k = i < cnt ? __ldcg(keys + i) : 0ull;
-                    const bool pass = k > tau;
-                    const unsigned m = __ballot_sync(kFull, pass);
-                    if (pass) ws.cand[count + __popc(m & below)] = k;
-                    count += __popc(m);
-                    __syncwarp();
-                }
-            }
-        }
-        if (count > ksel) {
-            warp_topk_keep<kWarpCap / 32>(ws.cand, count, ksel, lane);
-            count = ksel;
-        }
-        warp_sort256_desc(ws.cand, count, lane);
-        const uint32_t kk = count < ksel ? count : ksel;
-        warp_finalize(ws.cand, reinterpret_cast<double*>(ws.cand + kWarpProbOffset), kk, rp, nan0,
-                      LSE, M, Sx, row, a.rng, a.out_ids, a.info, a.cand_ids, a.cand_probs,
-                      a.cand_ld, lane);
+        warp_merge_row<kWarpCap, LSE>(ws.cand, a, row, rp, below, lane);
     }
 }
 
