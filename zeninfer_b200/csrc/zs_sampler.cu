@@ -333,12 +333,13 @@ struct LaunchScope {
 };
 
 // Merge launch: one warp per row when every shortlist fits a warp slot and the
-// batch gives every SM at least four such warps; otherwise one CTA per row (a
-// small batch has many slices per row and too few rows to fill the GPU by warps).
+// batch has at least two rows per SM; otherwise one CTA per row (a small batch
+// has many blocks per row and too few rows to fill the GPU by warps; measured on
+// B200, the two break even between 256 and 591 rows).
 zs_status launch_merge(zs_context* h, const zs::MergeArgs& m, int max_ksel, bool want_lse,
                        cudaStream_t st) {
     LaunchScope scope(h, 1, st);
-    if ((uint32_t)max_ksel <= zs::kWarpMergeMaxK && m.B >= 4 * h->num_sms) {
+    if ((uint32_t)max_ksel <= zs::kWarpMergeMaxK && m.B >= 2 * h->num_sms) {
         const int rows_per_cta = zs::kConsumerWarps;
         const int grid = std::max(1, std::min((m.B + rows_per_cta - 1) / rows_per_cta, 8 * h->num_sms));
         if (want_lse)
