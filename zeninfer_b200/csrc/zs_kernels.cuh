@@ -2194,6 +2194,50 @@ __device__ __forceinline__ bool wfilter_tile_fast(WarpSel& ws, WState& w, const 
     return true;
 }
 
+// Opening threshold of a piece, from its first tile: the keff-th largest of the
+// tile's float4 maxima (keff <= 256, one float4 per lane and step).  Each float4
+// maximum is a different element, so at least keff elements of the tile reach
+// it, and nothing below it can be in the piece's top-keff.  A 32-bit radix walk
+// over the maxima' ords, one redux.sync count per bit.  Returns that ord, 0 when
+// it is a NaN's (no usable threshold).
+__device__ __forceinline__ uint32_t wfirst_threshold(const float4* t4, int n4, uint32_t keff,
+                                                     int lane) {
+    constexpr int Q = kWTile / kWStepElems;
+    uint32_t o[Q];
+    uint32_t alive = 0u;
+#pragma unroll
+    for (int q = 0; q < Q; ++q) {
+        const int jj = lane + 32 * q;
+        o[q] = 0u;
+        if (jj < n4) {
+            const float4 v = t4[jj];
+            o[q] = ord_of(fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
+            alive |= 1u << q;
+        }
+    }
+    uint32_t need = keff, cnt = (uint32_t)n4;
+    for (int bit = 31; bit >= 0 && cnt != need; --bit) {
+        uint32_t ones = 0u;
+#pragma unroll
+        for (int q = 0; q < Q; ++q) ones |= ((o[q] >> bit) & 1u) << q;
+        ones &= alive;
+        const uint32_t c1 = __reduce_add_sync(kFull, (uint32_t)__popc(ones));
+        if (c1 >= need) {
+            alive = ones;
+            cnt = c1;
+        } else {
+            alive &= ~ones;
+            need -= c1;
+            cnt -= c1;
+        }
+    }
+    uint32_t m = 0xffffffffu;
+#pragma unroll
+    for (int q = 0; q < Q; ++q)
+        if ((alive >> q) & 1u) m = o[q] < m ? o[q] : m;
+    return __reduce_min_sync(kFull, m);
+}
+
 template <bool LSE>
 __device__ void wend_piece(const Args& a, WarpSel& ws, WState& w, const WPiece& pc,
                            const RowPlan& rp, bool greedy_np, float lc, int32_t gw, int32_t j,
@@ -2381,6 +2425,17 @@ __global__ void __launch_bounds__(kWThreads, 1) zs_wselect_kernel(const Args a) 
             const int start = pc.e0 + t * kWTile;
             const int n = min(kWTile, pc.e1 - start);
             const float4* t4 = reinterpret_cast<const float4*>(ws.ring[stage]);
+            if (t == 0 && !greedy_np && w.mode == kWAll && keff <= (uint32_t)(kWTile / 4) &&
+                (uint32_t)(n >> 2) >= keff) {
+                // start from a threshold instead of taking every element
+                const uint32_t T = wfirst_threshold(t4, n >> 2, keff, lane);
+                if (T != 0u) {
+                    w.mode = kWFast;
+                    w.tau_f = value_of_ord(T);
+                    w.tau_id = INT32_MAX;  // every element of that value passes
+                    w.tau_key = (uint64_t)T << 32;
+                }
+            }
             if (greedy_np || w.mode != kWFast) {
                 wfilter_tile<LSE>(ws, w, t4, n >> 2, id_col0 + start, greedy_np, keff, lc, below,
                                   lane);
