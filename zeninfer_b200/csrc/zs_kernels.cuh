@@ -1868,13 +1868,15 @@ __device__ void warp_merge_row(uint64_t* cand, const MergeArgs& a, int row, cons
                 base = reinterpret_cast<unsigned long long>(pp + kPartialHeaderBytes);
             }
         }
+        if (LSE) {
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float m2 = __shfl_xor_sync(kFull, m, o);
-            const float s2 = __shfl_xor_sync(kFull, sx, o);
-            lse_merge(m, sx, m2, s2, lc);
+            for (int o = 16; o > 0; o >>= 1) {
+                const float m2 = __shfl_xor_sync(kFull, m, o);
+                const float s2 = __shfl_xor_sync(kFull, sx, o);
+                lse_merge(m, sx, m2, s2, lc);
+            }
+            lse_merge(M, Sx, m, sx, lc);
         }
-        lse_merge(M, Sx, m, sx, lc);
         nan0 = nan0 || __any_sync(kFull, z);
         uint32_t incl = c;
 #pragma unroll
@@ -1916,7 +1918,9 @@ __device__ void warp_merge_row(uint64_t* cand, const MergeArgs& a, int row, cons
             }
         }
     }
-    if (count > ksel) {
+    // Up to 256 keys are sorted whole (the shortlist is their prefix), which is
+    // cheaper than selecting the top-ksel first; more are cut to ksel first.
+    if (count > kWarpMergeMaxK) {
         warp_topk_keep<CAP / 32>(cand, count, ksel, lane);
         count = ksel;
     }
