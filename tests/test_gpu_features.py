@@ -99,6 +99,8 @@ def _history(rows, L, n, seed, dup=True):
     SamplingParams(temp=1.0, top_p=0.95, repeat_penalty=0.8, repeat_last_n=300),
     SamplingParams(temp=0.9, top_k=100, repeat_penalty=1.2, repeat_last_n=700),  # large window
     SamplingParams(temp=0.8, top_k=2000, repeat_penalty=1.1, repeat_last_n=100),  # keff > 2048
+    SamplingParams(temp=0.9, top_k=600, repeat_penalty=1.2, repeat_last_n=200),  # long warp config
+    SamplingParams(temp=0.8, top_k=40, repeat_penalty=1.3, repeat_last_n=200),   # window > 64
 ])
 def test_penalty(sampler, params):
     rows = 64

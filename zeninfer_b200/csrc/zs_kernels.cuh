@@ -22,6 +22,8 @@
 
 #include <math.h>
 
+#include <type_traits>
+
 #include "zs_device.cuh"
 
 namespace zs {
@@ -47,16 +49,32 @@ constexpr int kProbOffset = 2048;         // f64 probabilities alias cand[2048..
 constexpr int kShortlistDefault = 256;    // kTopPShortlist, src/sample.cpp:12
 
 // Warp-independent select (zs_wselect_kernel): rows whose shortlist + penalty
-// window is at most kWKeffMax (every default shape of the reference).
-constexpr int kWWarps = 12;                // independent warps per CTA
-constexpr int kWThreads = kWWarps * 32;
+// window fits a warp's candidate slot.
 constexpr int kWTile = 1024;               // floats per ring stage (4 KB)
 constexpr int kWStages = 3;
-constexpr int kWCap = 640;                 // candidate keys per warp
 constexpr int kWStepElems = 128;           // floats one warp step covers (32 lanes x float4)
-constexpr int kWKeffMax = 320;
-constexpr int kWWinMax = 64;
 constexpr int kWMinElems = 2048;           // smallest share of the batch per warp
+
+// The two warp-kernel configurations: short shortlists (every default of the
+// reference) and longer ones.  A longer shortlist needs a bigger candidate slot
+// per warp, so fewer warps fit an SM; with fewer threads per CTA each thread may
+// use more registers, which the register-resident compaction of a bigger slot needs.
+struct WCfgS {
+    static constexpr int kCap = 640;      // candidate keys per warp
+    static constexpr int kWarps = 12;     // warps per CTA (one CTA per SM)
+    static constexpr int kKeffMax = 320;  // shortlist + penalty window
+    static constexpr int kWinMax = 64;    // penalty window
+    static constexpr int kClass = 0;
+    static constexpr uint32_t kSlackDiv = 0;  // intermediate compactions are exact
+};
+struct WCfgL {
+    static constexpr int kCap = 2048;
+    static constexpr int kWarps = 7;
+    static constexpr int kKeffMax = 1280;
+    static constexpr int kWinMax = 256;
+    static constexpr int kClass = 1;
+    static constexpr uint32_t kSlackDiv = 4;  // intermediate compactions keep <= keff + keff/4
+};
 
 static_assert(kCandCap >= kKeffFastMax + kSlackMax + kHalfElems + kCandMargin,
               "candidate buffer too small for half-stage passes");
@@ -172,6 +190,17 @@ struct Args {
     int32_t wl_NW;
     int32_t wl_P;
     int32_t wl_Vn;
+    int32_t wl_class;  // rows this warp launch serves: WCfgS::kClass or WCfgL::kClass
+};
+
+// Layout of one warp configuration's blocks (see Args).
+struct WLayout {
+    int64_t off;
+    int64_t E;
+    int64_t stride;
+    int32_t NW;
+    int32_t P;
+    int32_t Vn;
 };
 
 struct MergeArgs {
@@ -195,13 +224,9 @@ struct MergeArgs {
     double* cand_probs;
     int32_t cand_ld;
     int* status;
-    // warp-piece blocks (see Args), at wl_off inside each rank's area
-    int64_t wl_off;
-    int64_t wl_E;
-    int64_t wl_stride;
-    int32_t wl_NW;
-    int32_t wl_P;
-    int32_t wl_Vn;
+    // warp-piece blocks (see Args) of the two warp configurations, at wl[c].off
+    // inside each rank's area
+    WLayout wl[2];
 };
 
 struct RowPlan {
@@ -212,7 +237,8 @@ struct RowPlan {
     int32_t hist_len;
     bool greedy;
     bool penal;
-    bool wfast;  // zs_wselect_kernel: keff <= kWKeffMax, window <= kWWinMax
+    bool wfast;  // zs_wselect_kernel<WCfgS>: keff <= 320, window <= 64
+    bool wbig;   // zs_wselect_kernel<WCfgL>: the other rows with keff <= 1280, window <= 256
     bool fast;   // zs_select_kernel: the other rows with keff <= kKeffFastMax
     bool large;  // zs_large_kernel: the rest
 };
@@ -240,9 +266,10 @@ __device__ __forceinline__ RowPlan plan_row(const Params& p, int V_total, const 
     }
     r.penal = r.win > 0;
     r.keff = r.ksel + r.win;
-    r.wfast = (r.keff <= kWKeffMax) && (r.win <= kWWinMax);
-    r.fast = !r.wfast && (r.keff <= kKeffFastMax) && (r.win <= kWinFastMax);
-    r.large = !r.wfast && !r.fast;
+    r.wfast = (r.keff <= WCfgS::kKeffMax) && (r.win <= WCfgS::kWinMax);
+    r.wbig = !r.wfast && (r.keff <= WCfgL::kKeffMax) && (r.win <= WCfgL::kWinMax);
+    r.fast = !r.wfast && !r.wbig && (r.keff <= kKeffFastMax) && (r.win <= kWinFastMax);
+    r.large = !r.wfast && !r.wbig && !r.fast;
     return r;
 }
 
@@ -276,7 +303,7 @@ __device__ __forceinline__ WPiece wl_piece(const Args& a, int64_t b0, int64_t b1
     pc.c1 = (int32_t)c1;
     const RowPlan rp = plan_row(load_params(a.row_params, a.shared, pc.row), a.V_total, a.hist,
                                 a.hist_len, a.hist_ld, pc.row);
-    pc.active = rp.wfast;
+    pc.active = a.wl_class == WCfgS::kClass ? rp.wfast : rp.wbig;
     const uintptr_t p0 = (uintptr_t)(a.logits + (int64_t)pc.row * a.ld + pc.c0);
     const int pad = (int)(((16u - (unsigned)(p0 & 15u)) & 15u) >> 2);
     const int e0 = pc.c0 + pad;
@@ -983,23 +1010,26 @@ __device__ void finalize_row(CandState& st, const uint64_t* cand, double* prob, 
 }
 
 // The partial blocks of one row: S slice blocks of zs_select_kernel, or the
-// blocks of the warps whose shares cover the row (zs_wselect_kernel).
+// blocks of the warps whose shares cover the row (zs_wselect_kernel, in the
+// layout of the row's warp configuration).
 struct BlockSet {
     int32_t n;       // blocks per rank
     int32_t w_lo;    // first warp (warp layout)
     int64_t stride;  // bytes per block
     bool warp;
+    WLayout L;       // warp layout
 };
 
-__device__ __forceinline__ BlockSet row_blocks(const MergeArgs& a, int row, bool wfast) {
+__device__ __forceinline__ BlockSet row_blocks(const MergeArgs& a, int row, const RowPlan& rp) {
     BlockSet bs;
-    bs.warp = wfast;
-    if (wfast) {
-        const int64_t x0 = (int64_t)row * a.wl_Vn;
-        bs.w_lo = wl_warp_of(a.wl_E, a.wl_NW, x0);
-        const int32_t w_hi = wl_warp_of(a.wl_E, a.wl_NW, x0 + a.wl_Vn - 1);
+    bs.warp = rp.wfast || rp.wbig;
+    if (bs.warp) {
+        bs.L = a.wl[rp.wfast ? WCfgS::kClass : WCfgL::kClass];
+        const int64_t x0 = (int64_t)row * bs.L.Vn;
+        bs.w_lo = wl_warp_of(bs.L.E, bs.L.NW, x0);
+        const int32_t w_hi = wl_warp_of(bs.L.E, bs.L.NW, x0 + bs.L.Vn - 1);
         bs.n = w_hi - bs.w_lo + 1;
-        bs.stride = a.wl_stride;
+        bs.stride = bs.L.stride;
     } else {
         bs.w_lo = 0;
         bs.n = a.S;
@@ -1014,10 +1044,10 @@ __device__ __forceinline__ const uint8_t* block_at(const MergeArgs& a, const Blo
     const uint8_t* base = a.gathered + (int64_t)g * a.rank_stride;
     if (!bs.warp) return base + ((int64_t)row * a.S + idx) * a.part_stride;
     const int32_t w = bs.w_lo + idx;
-    const int64_t b0 = wl_bound(a.wl_E, a.wl_NW, w), b1 = wl_bound(a.wl_E, a.wl_NW, w + 1);
+    const int64_t b0 = wl_bound(bs.L.E, bs.L.NW, w), b1 = wl_bound(bs.L.E, bs.L.NW, w + 1);
     if (b0 >= b1) return nullptr;
-    const int32_t j = row - (int32_t)(b0 / a.wl_Vn);
-    return base + a.wl_off + ((int64_t)w * a.wl_P + j) * a.wl_stride;
+    const int32_t j = row - (int32_t)(b0 / bs.L.Vn);
+    return base + bs.L.off + ((int64_t)w * bs.L.P + j) * bs.L.stride;
 }
 
 // Streams the keys of partial blocks (unsorted; 0 = removed) through the
@@ -1550,7 +1580,7 @@ __global__ void __launch_bounds__(kNC) zs_merge_kernel(const MergeArgs a) {
         bool x0n;
         float mm, ss;
         ZS_CHECK(rp.ksel <= kKeffFastMax, 16, rp.ksel);
-        const BlockSet bs = row_blocks(a, row, rp.wfast);
+        const BlockSet bs = row_blocks(a, row, rp);
         const uint32_t kk = merge_partials(st, a, bs, row, (uint32_t)rp.ksel, lc, x0n, mm, ss, ctid);
         finalize_row(st, st.cand, reinterpret_cast<double*>(st.cand + kProbOffset), kk, rp, x0n,
                      LSE, mm, ss, row, a.rng, a.out_ids, a.info, a.cand_ids, a.cand_probs,
@@ -1558,22 +1588,36 @@ __global__ void __launch_bounds__(kNC) zs_merge_kernel(const MergeArgs a) {
     }
 }
 
-// Keeps exactly the kk largest of the unique keys keys[0..n) (n > kk >= 1,
-// n <= 32 * R) at keys[0..kk) and returns the kk-th largest.  The keys sit in
+// Keeps the kk largest of the unique keys keys[0..n) (n > kk >= 1, n <= 32 * R)
+// at the front of keys and returns the smallest key kept.  With slack 0 that is
+// exactly kk keys and the kk-th largest.  With slack > 0 the walk may stop once
+// its bucket holds at most `slack` keys more than still needed, and keeps the
+// whole bucket (up to kk + slack keys, *kept says how many).  The keys sit in
 // registers (R per lane); a binary radix walk from the highest bit in which the
 // keys differ narrows the bucket holding the kk-th key, one warp-wide count
 // (redux.sync) per bit, with no shared-memory atomics.
 template <int R>
+struct KeyMask {  // lane masks over R register keys: 32 or 64 bits
+    static_assert(R >= 1 && R <= 64, "at most 64 keys per lane");
+    using T = typename std::conditional<(R > 32), unsigned long long, uint32_t>::type;
+    __device__ static __forceinline__ uint32_t popc(T m) {
+        return (uint32_t)(sizeof(T) == 8 ? __popcll((unsigned long long)m) : __popc((uint32_t)m));
+    }
+};
+
+template <int R>
 __device__ __forceinline__ uint64_t warp_topk_keep(uint64_t* keys, uint32_t n, uint32_t kk,
-                                                   int lane) {
+                                                   int lane, uint32_t slack = 0u,
+                                                   uint32_t* kept = nullptr) {
+    using M = typename KeyMask<R>::T;
     uint64_t k[R];
-    uint32_t alive = 0u;
+    M alive = 0;
 #pragma unroll
     for (int j = 0; j < R; ++j) {
         const uint32_t i = (uint32_t)lane + 32u * j;
         const bool v = i < n;
         k[j] = v ? keys[i] : 0ull;
-        alive |= (uint32_t)v << j;
+        alive |= (M)v << j;
     }
     uint64_t lo = ~0ull, hi = 0ull;
 #pragma unroll
@@ -1586,14 +1630,15 @@ __device__ __forceinline__ uint64_t warp_topk_keep(uint64_t* keys, uint32_t n, u
     lo = warp_min_u64(lo);
     hi = warp_max_u64(hi);
     uint64_t T = hi;
+    uint32_t n_keep = 1u;
     if (kk > 1u) {
         uint32_t need = kk, cnt = n;
-        for (int bit = 63 - __clzll((long long)(lo ^ hi)); bit >= 0; --bit) {
-            uint32_t ones = 0u;
+        for (int bit = 63 - __clzll((long long)(lo ^ hi)); bit >= 0 && cnt - need > slack; --bit) {
+            M ones = 0;
 #pragma unroll
-            for (int j = 0; j < R; ++j) ones |= (uint32_t)((k[j] >> bit) & 1ull) << j;
+            for (int j = 0; j < R; ++j) ones |= (M)((k[j] >> bit) & 1ull) << j;
             ones &= alive;
-            const uint32_t c1 = __reduce_add_sync(kFull, (uint32_t)__popc(ones));
+            const uint32_t c1 = __reduce_add_sync(kFull, KeyMask<R>::popc(ones));
             if (c1 >= need) {
                 alive = ones;
                 cnt = c1;
@@ -1602,18 +1647,21 @@ __device__ __forceinline__ uint64_t warp_topk_keep(uint64_t* keys, uint32_t n, u
                 need -= c1;
                 cnt -= c1;
             }
-            if (cnt == need) break;  // the whole bucket is in: its minimum is the kk-th
         }
+        // The whole bucket is kept: its minimum is the kk-th key when the bucket
+        // holds exactly the keys still needed, else at most `slack` more pass.
         uint64_t m = ~0ull;
 #pragma unroll
         for (int j = 0; j < R; ++j)
             if ((alive >> j) & 1u) m = k[j] < m ? k[j] : m;
         T = warp_min_u64(m);
+        n_keep = kk - need + cnt;
     }
-    uint32_t keep = 0u;
+    if (kept) *kept = n_keep;
+    M keep = 0;
 #pragma unroll
-    for (int j = 0; j < R; ++j) keep |= (uint32_t)(k[j] >= T) << j;  // padding keys are 0 < T
-    const uint32_t c = (uint32_t)__popc(keep);
+    for (int j = 0; j < R; ++j) keep |= (M)(k[j] >= T) << j;  // padding keys are 0 < T
+    const uint32_t c = KeyMask<R>::popc(keep);
     uint32_t incl = c;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -1844,7 +1892,7 @@ __device__ void warp_merge_row(uint64_t* cand, const MergeArgs& a, int row, cons
     constexpr int J = 8;  // keys per lane per gather round
     const uint32_t ksel = (uint32_t)rp.ksel;
     const float lc = (rp.greedy ? 1.0f : 1.0f / rp.p.temp) * 1.4426950408889634f;
-    const BlockSet bs = row_blocks(a, row, rp.wfast);
+    const BlockSet bs = row_blocks(a, row, rp);
     const uint32_t block_cap = (uint32_t)((bs.stride - kPartialHeaderBytes) / 8);
     const int nb = a.G * bs.n;
     uint32_t count = 0;
@@ -1948,7 +1996,7 @@ __global__ void __launch_bounds__(kNC, 4) zs_warp_merge_kernel(const MergeArgs a
 
 // ---------------------------------------------------------------------------
 // zs_wselect_kernel: warp-independent streaming select for the rows of the warp
-// path (shortlist + penalty window <= kWKeffMax, window <= kWWinMax).
+// path (shortlist + penalty window within the configuration's limits, WCfgS or WCfgL).
 //
 // Each warp owns an equal contiguous share of the batch flattened to
 // B * wl_Vn columns, cut at row ends into pieces.  It streams its share through
@@ -1961,15 +2009,17 @@ __global__ void __launch_bounds__(kNC, 4) zs_warp_merge_kernel(const MergeArgs a
 // a piece the penalty is patched in, the piece's top-ksel (final values) is
 // selected exactly, and the keys go out as one unsorted block.
 // ---------------------------------------------------------------------------
+template <class C>
 struct __align__(128) WarpSel {
     float ring[kWStages][kWTile];
-    uint64_t cand[kWCap];
+    uint64_t cand[C::kCap];
     uint32_t hist[256];  // radix histogram; the penalty window at a piece's end
     uint64_t full[kWStages];
 };
 
+template <class C>
 struct WSelSmem {
-    WarpSel w[kWWarps];
+    WarpSel<C> w[C::kWarps];
 };
 
 // Issue side of a warp: the next (piece, tile) to copy.  Every lane keeps the
@@ -1986,7 +2036,8 @@ struct WShare {
     int32_t np;      // pieces
 };
 
-__device__ __forceinline__ bool wl_issue(const Args& a, WarpSel& ws, int stage, WIssue& is,
+template <class C>
+__device__ __forceinline__ bool wl_issue(const Args& a, WarpSel<C>& ws, int stage, WIssue& is,
                                          const WShare& sh, uint64_t pol, int lane) {
     while (is.j < sh.np && is.t >= is.pc.ntiles) {
         ++is.j;
@@ -2009,10 +2060,11 @@ __device__ __forceinline__ bool wl_issue(const Args& a, WarpSel& ws, int stage, 
 }
 
 // Ballot append of `key` where pred; count stays warp-uniform.
+template <int CAP>
 __device__ __forceinline__ void wappend(uint64_t* cand, uint32_t& count, bool pred, uint64_t key,
                                         unsigned below) {
     const unsigned m = __ballot_sync(kFull, pred);
-    if (pred && ZS_CHECK(count + __popc(m & below) < (uint32_t)kWCap, 20, count))
+    if (pred && ZS_CHECK(count + __popc(m & below) < (uint32_t)CAP, 20, count))
         cand[count + __popc(m & below)] = key;
     count += (uint32_t)__popc(m);
 }
@@ -2037,9 +2089,14 @@ struct WState {
 // Shrinks the candidates to the exact top-keff and raises the threshold to the
 // keff-th key.  For a non-NaN threshold value t, key(x, id) > key(t, tid) is
 // exactly x > t, or x == t and id < tid (-0 == +0, NaN below everything).
-__device__ __forceinline__ void wcompact(WarpSel& ws, WState& w, uint32_t keff, int lane) {
-    w.tau_key = warp_topk_keep<kWCap / 32>(ws.cand, w.count, keff, lane);
-    w.count = keff;
+template <class C>
+__device__ __forceinline__ void wcompact(WarpSel<C>& ws, WState& w, uint32_t keff, int lane) {
+    // The long configuration stops its radix walk early (keeping up to keff/4
+    // keys more): with 64 keys per lane every bit of the walk is costly, and a
+    // tie group at the keff-th key would otherwise send it through the id bits.
+    uint32_t kept = keff;
+    w.tau_key = warp_topk_keep<C::kCap / 32>(ws.cand, w.count, keff, lane, C::kSlackDiv ? keff / C::kSlackDiv : 0u, &kept);
+    w.count = kept;
     w.tau_f = tau_value(w.tau_key);
     w.tau_id = key_id(w.tau_key);
     w.mode = ((uint32_t)(w.tau_key >> 32) == 0u) ? kWExact : kWFast;
@@ -2048,7 +2105,8 @@ __device__ __forceinline__ void wcompact(WarpSel& ws, WState& w, uint32_t keff, 
 // Appends the components of v (ids id..id+3) selected by p0..p3.  Positions
 // come from a bit-sliced warp prefix sum of the per-lane counts: one ballot per
 // possible count, so the common step (at most one hit per lane) costs two.
-__device__ __forceinline__ void wappend4(WarpSel& ws, WState& w, const float4& v, int32_t id,
+template <class C>
+__device__ __forceinline__ void wappend4(WarpSel<C>& ws, WState& w, const float4& v, int32_t id,
                                          bool p0, bool p1, bool p2, bool p3, unsigned below) {
     const uint32_t c = (uint32_t)p0 + (uint32_t)p1 + (uint32_t)p2 + (uint32_t)p3;
     const unsigned b1 = __ballot_sync(kFull, c >= 1u);
@@ -2061,7 +2119,7 @@ __device__ __forceinline__ void wappend4(WarpSel& ws, WState& w, const float4& v
         tot += (uint32_t)(__popc(b2) + __popc(b3) + __popc(b4));
     }
     uint32_t at = w.count + pos;
-    ZS_CHECK(at + c <= (uint32_t)kWCap, 20, at + c);
+    ZS_CHECK(at + c <= (uint32_t)C::kCap, 20, at + c);
     if (p0) ws.cand[at++] = make_key(v.x, id);
     if (p1) ws.cand[at++] = make_key(v.y, id + 1);
     if (p2) ws.cand[at++] = make_key(v.z, id + 2);
@@ -2076,8 +2134,8 @@ __device__ __forceinline__ bool wpass(const WState& w, bool ok, float x, int32_t
     return ok && make_key(x, id) > w.tau_key;
 }
 
-template <bool LSE>
-__device__ __forceinline__ void wfilter1(WarpSel& ws, WState& w, bool ok, float x, int32_t id,
+template <class C, bool LSE>
+__device__ __forceinline__ void wfilter1(WarpSel<C>& ws, WState& w, bool ok, float x, int32_t id,
                                          bool greedy, uint32_t keff, float lc, unsigned below,
                                          int lane) {
     if (LSE && ok) lse_add1(w.lm, w.ls, x, lc);
@@ -2092,12 +2150,12 @@ __device__ __forceinline__ void wfilter1(WarpSel& ws, WState& w, bool ok, float 
         return;
     }
     const bool p = wpass(w, ok, x, id);
-    wappend(ws.cand, w.count, p, make_key(x, id), below);
-    if (w.count > (uint32_t)(kWCap - kWStepElems)) wcompact(ws, w, keff, lane);
+    wappend<C::kCap>(ws.cand, w.count, p, make_key(x, id), below);
+    if (w.count > (uint32_t)(C::kCap - kWStepElems)) wcompact(ws, w, keff, lane);
 }
 
-template <bool LSE>
-__device__ __forceinline__ void wfilter_tile(WarpSel& ws, WState& w, const float4* t4, int n4,
+template <class C, bool LSE>
+__device__ __forceinline__ void wfilter_tile(WarpSel<C>& ws, WState& w, const float4* t4, int n4,
                                              int32_t gid0, bool greedy, uint32_t keff, float lc,
                                              unsigned below, int lane) {
 #pragma unroll 2
@@ -2131,7 +2189,7 @@ __device__ __forceinline__ void wfilter_tile(WarpSel& ws, WState& w, const float
         if (__any_sync(kFull, h)) {
             wappend4(ws, w, v, id, h && wpass(w, true, v.x, id), h && wpass(w, true, v.y, id + 1),
                      h && wpass(w, true, v.z, id + 2), h && wpass(w, true, v.w, id + 3), below);
-            if (w.count > (uint32_t)(kWCap - kWStepElems)) wcompact(ws, w, keff, lane);
+            if (w.count > (uint32_t)(C::kCap - kWStepElems)) wcompact(ws, w, keff, lane);
         }
     }
 }
@@ -2142,8 +2200,8 @@ __device__ __forceinline__ void wfilter_tile(WarpSel& ws, WState& w, const float
 // written at positions from one warp scan.  Returns false, having appended
 // nothing, when the tile's survivors could not fit even after a compaction; the
 // caller then filters it with the per-step path.
-template <bool LSE>
-__device__ __forceinline__ bool wfilter_tile_fast(WarpSel& ws, WState& w, const float* tile, int n4,
+template <class C, bool LSE>
+__device__ __forceinline__ bool wfilter_tile_fast(WarpSel<C>& ws, WState& w, const float* tile, int n4,
                                                   int32_t gid0, uint32_t keff, float lc, int lane) {
     const float4* t4 = reinterpret_cast<const float4*>(tile);
     const float tf = w.tau_f;
@@ -2181,8 +2239,9 @@ __device__ __forceinline__ bool wfilter_tile_fast(WarpSel& ws, WState& w, const 
         if (lane >= o) incl += t;
     }
     const uint32_t tot = __shfl_sync(kFull, incl, 31);
-    if (w.count + tot > (uint32_t)kWCap) {
-        if (tot > (uint32_t)kWCap - keff) return false;
+    if (w.count + tot > (uint32_t)C::kCap) {
+        const uint32_t slack = C::kSlackDiv ? keff / C::kSlackDiv : 0u;
+        if (tot > (uint32_t)C::kCap - keff - slack) return false;
         // The marked elements beat the old threshold; some may fall below the
         // new one, which costs room but not exactness (the final select is exact).
         wcompact(ws, w, keff, lane);
@@ -2242,8 +2301,8 @@ __device__ __forceinline__ uint32_t wfirst_threshold(const float4* t4, int n4, u
     return __reduce_min_sync(kFull, m);
 }
 
-template <bool LSE>
-__device__ void wend_piece(const Args& a, WarpSel& ws, WState& w, const WPiece& pc,
+template <class C, bool LSE>
+__device__ void wend_piece(const Args& a, WarpSel<C>& ws, WState& w, const WPiece& pc,
                            const RowPlan& rp, bool greedy_np, float lc, int32_t gw, int32_t j,
                            unsigned below, int lane) {
     const float* row_logits = a.logits + (int64_t)pc.row * a.ld;
@@ -2269,6 +2328,10 @@ __device__ void wend_piece(const Args& a, WarpSel& ws, WState& w, const WPiece& 
             const float s2 = __shfl_xor_sync(kFull, Sx, o);
             lse_merge(M, Sx, m2, s2, lc);
         }
+    }
+    if (rp.penal && w.count + (uint32_t)rp.win > (uint32_t)C::kCap) {
+        // keep the raw top-keff (keff = ksel + window) and make room for the window
+        wcompact(ws, w, (uint32_t)rp.keff, lane);
     }
     if (rp.penal) {
         // src/sample.cpp:40-50 for the ids of this piece: raw keys out, penalised
@@ -2322,7 +2385,7 @@ __device__ void wend_piece(const Args& a, WarpSel& ws, WState& w, const WPiece& 
                     }
                 }
             }
-            wappend(ws.cand, w.count, app, key, below);
+            wappend<C::kCap>(ws.cand, w.count, app, key, below);
         }
         const unsigned zm = __ballot_sync(kFull, z_hit);
         if (zm) x0n = __shfl_sync(kFull, z_nan, __ffs(zm) - 1);
@@ -2337,7 +2400,7 @@ __device__ void wend_piece(const Args& a, WarpSel& ws, WState& w, const WPiece& 
     // top-ksel (final values): that is all the block has to carry.
     const uint32_t ksel = (uint32_t)rp.ksel;
     if (w.count > ksel) {
-        warp_topk_keep<kWCap / 32>(ws.cand, w.count, ksel, lane);
+        warp_topk_keep<C::kCap / 32>(ws.cand, w.count, ksel, lane);
         w.count = ksel;
     }
     uint8_t* pp = a.wpart + ((int64_t)gw * a.wl_P + j) * a.wl_stride;
@@ -2357,13 +2420,13 @@ __device__ void wend_piece(const Args& a, WarpSel& ws, WState& w, const WPiece& 
     __syncwarp();
 }
 
-template <bool LSE>
-__global__ void __launch_bounds__(kWThreads, 1) zs_wselect_kernel(const Args a) {
+template <class C, bool LSE>
+__global__ void __launch_bounds__(C::kWarps * 32, 1) zs_wselect_kernel(const Args a) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
-    WSelSmem& sm = *reinterpret_cast<WSelSmem*>(smem_raw);
+    WSelSmem<C>& sm = *reinterpret_cast<WSelSmem<C>*>(smem_raw);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    WarpSel& ws = sm.w[warp];
-    const int32_t gw = blockIdx.x * kWWarps + warp;
+    WarpSel<C>& ws = sm.w[warp];
+    const int32_t gw = blockIdx.x * C::kWarps + warp;
     if (gw >= a.wl_NW) return;  // the whole warp; nothing in this kernel syncs the block
     WShare sh;
     sh.b0 = wl_bound(a.wl_E, a.wl_NW, gw);
@@ -2397,7 +2460,7 @@ __global__ void __launch_bounds__(kWThreads, 1) zs_wselect_kernel(const Args a) 
         const bool greedy_np = rp.greedy && !rp.penal;
         const uint32_t keff = (uint32_t)rp.keff;
         const uint32_t compact_at =
-            min((uint32_t)(kWCap - kWStepElems), keff + (keff > 128u ? keff : 128u));
+            min((uint32_t)(C::kCap - kWStepElems), keff + (keff > 128u ? keff : 128u));
         const float lc = (rp.greedy ? 1.0f : 1.0f / rp.p.temp) * 1.4426950408889634f;
         const float* row_logits = a.logits + (int64_t)pc.row * a.ld;
         const int32_t id_col0 = a.id_offset;  // global id of local column 0
@@ -2416,7 +2479,7 @@ __global__ void __launch_bounds__(kWThreads, 1) zs_wselect_kernel(const Args a) 
             const int nh = pc.e0 - pc.c0;
             const bool okh = lane < nh;
             const float x = okh ? row_logits[pc.c0 + lane] : 0.0f;
-            wfilter1<LSE>(ws, w, okh, x, id_col0 + pc.c0 + lane, greedy_np, keff, lc, below, lane);
+            wfilter1<C, LSE>(ws, w, okh, x, id_col0 + pc.c0 + lane, greedy_np, keff, lc, below, lane);
         }
         for (int t = 0; t < pc.ntiles; ++t) {
             const int stage = consumed % kWStages;
@@ -2441,12 +2504,12 @@ __global__ void __launch_bounds__(kWThreads, 1) zs_wselect_kernel(const Args a) 
                 }
             }
             if (greedy_np || w.mode != kWFast) {
-                wfilter_tile<LSE>(ws, w, t4, n >> 2, id_col0 + start, greedy_np, keff, lc, below,
+                wfilter_tile<C, LSE>(ws, w, t4, n >> 2, id_col0 + start, greedy_np, keff, lc, below,
                                   lane);
-            } else if (!wfilter_tile_fast<LSE>(ws, w, ws.ring[stage], n >> 2, id_col0 + start,
+            } else if (!wfilter_tile_fast<C, LSE>(ws, w, ws.ring[stage], n >> 2, id_col0 + start,
                                                keff, lc, lane)) {
                 // too many survivors for one batch: the per-step path (log-sum-exp done)
-                wfilter_tile<false>(ws, w, t4, n >> 2, id_col0 + start, false, keff, lc, below,
+                wfilter_tile<C, false>(ws, w, t4, n >> 2, id_col0 + start, false, keff, lc, below,
                                     lane);
             }
             // Raise the threshold early: fewer elements reach it afterwards.
@@ -2461,9 +2524,9 @@ __global__ void __launch_bounds__(kWThreads, 1) zs_wselect_kernel(const Args a) 
             const int nt = pc.c1 - pc.e1;
             const bool okt = lane < nt;
             const float x = okt ? row_logits[pc.e1 + lane] : 0.0f;
-            wfilter1<LSE>(ws, w, okt, x, id_col0 + pc.e1 + lane, greedy_np, keff, lc, below, lane);
+            wfilter1<C, LSE>(ws, w, okt, x, id_col0 + pc.e1 + lane, greedy_np, keff, lc, below, lane);
         }
-        wend_piece<LSE>(a, ws, w, pc, rp, greedy_np, lc, gw, j, below, lane);
+        wend_piece<C, LSE>(a, ws, w, pc, rp, greedy_np, lc, gw, j, below, lane);
     }
     if (!ok) {
         if (lane == 0) set_status(a.status, kStatusTimeout);

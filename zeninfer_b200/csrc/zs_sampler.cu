@@ -59,7 +59,7 @@ struct DeviceGuard {
 
 // Fixed layouts of the vocab-sharded mode, so every rank derives the same blocks.
 constexpr int kShardLayoutCtas = 296;
-constexpr int kShardLayoutWarps = 148 * zs::kWWarps;
+constexpr int kShardLayoutWarps[2] = {148 * zs::WCfgS::kWarps, 148 * zs::WCfgL::kWarps};
 
 // Where the partial blocks of one call go, and which kernels run.  The block
 // areas depend only on the batch, the columns and the params (never on whether a
@@ -74,14 +74,20 @@ struct Plan {
     int S = 1;
     int slice = 0;
     int64_t part_stride = 0;
-    // zs_wselect_kernel rows: warp-piece blocks at wl_off
-    bool any_warp = false;
-    int64_t wl_E = 0;
-    int32_t wl_NW = 1;
-    int32_t wl_P = 1;
-    int32_t wl_Vn = 1;
-    int64_t wl_stride = 0;
-    int64_t wl_off = 0;
+    // zs_wselect_kernel rows, one layout per warp configuration (index = class):
+    // warp-piece blocks at w[c].off
+    struct Warp {
+        bool any = false;     // the layout holds blocks of this class
+        bool launch = false;  // some row of this call may be of this class
+        int max_ksel = 1;
+        int64_t E = 0;
+        int32_t NW = 1;
+        int32_t P = 1;
+        int32_t Vn = 1;
+        int64_t stride = 0;
+        int64_t off = 0;
+        int64_t bytes() const { return any ? (int64_t)NW * P * stride : 0; }
+    } w[2];
     int64_t bytes = 0;  // all blocks of one rank
 };
 
@@ -120,46 +126,64 @@ int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 // Few rows are spread over fewer warps than that when needed, so that the blocks
 // of one row, from all n_ranks ranks, hold at most kCandCap - kCandMargin keys:
 // the merge then gathers a row in one pass.
-void plan_warp_layout(Plan& pl, int B, int V_cols, int layout_warps, int max_ksel, int n_ranks) {
-    pl.wl_Vn = std::max(1, V_cols);
-    pl.wl_E = (int64_t)B * pl.wl_Vn;
-    const int64_t by_size = std::max<int64_t>(1, pl.wl_E / zs::kWMinElems);
+void plan_warp_layout(Plan::Warp& pl, int B, int V_cols, int layout_warps, int max_ksel,
+                      int n_ranks) {
+    pl.Vn = std::max(1, V_cols);
+    pl.E = (int64_t)B * pl.Vn;
+    const int64_t by_size = std::max<int64_t>(1, pl.E / zs::kWMinElems);
     const int64_t blocks_per_row =
         std::max<int64_t>(1, (zs::kCandCap - zs::kCandMargin) / ((int64_t)std::max(1, max_ksel) *
                                                                  std::max(1, n_ranks)));
     // a row spanning w warps' shares owns at most NW / B + 2 of them
     const int64_t by_merge = (int64_t)B * std::max<int64_t>(1, blocks_per_row - 2);
-    pl.wl_NW = (int32_t)std::max<int64_t>(
+    pl.NW = (int32_t)std::max<int64_t>(
         1, std::min<int64_t>({(int64_t)layout_warps, by_size, by_merge}));
-    const int64_t share = (pl.wl_E + pl.wl_NW - 1) / pl.wl_NW;
-    pl.wl_P = (int32_t)((share + pl.wl_Vn - 1) / pl.wl_Vn + 1);
-    pl.wl_stride = round_up(zs::kPartialHeaderBytes + 8LL * std::max(1, max_ksel), 16);
+    const int64_t share = (pl.E + pl.NW - 1) / pl.NW;
+    pl.P = (int32_t)((share + pl.Vn - 1) / pl.Vn + 1);
+    pl.stride = round_up(zs::kPartialHeaderBytes + 8LL * std::max(1, max_ksel), 16);
+}
+
+// Places the block areas: [B][S] CTA blocks, then each warp configuration's.
+void place_areas(Plan& pl, int B) {
+    const int64_t cta_bytes = pl.cta_area ? (int64_t)B * pl.S * pl.part_stride : 0;
+    pl.w[0].off = round_up(cta_bytes, 256);
+    pl.w[1].off = round_up(pl.w[0].off + pl.w[0].bytes(), 256);
+    pl.bytes = pl.w[1].off + pl.w[1].bytes();
 }
 
 Plan make_plan(int B, int V_cols, int V_total, const zs_params* params, int per_row, int ctas,
-               int layout_warps, bool have_history, int n_ranks = 1) {
+               const int* layout_warps, bool have_history, int n_ranks = 1) {
     Plan pl;
     const int np = per_row ? B : 1;
     int64_t max_keys = 1;
-    int max_ksel_w = 1;
     for (int i = 0; i < np; ++i) {
         const zs_params& p = params[i];
         const int ks = ksel_of(p, V_total);
         const int wb = win_bound_of(p);
         pl.max_ksel = std::max(pl.max_ksel, ks);
         if (have_history && wb > 0) pl.any_penal = true;
-        // The device puts a row on the warp path when ksel + its actual window
-        // fits (the window is empty without a history); on the CTA path when
-        // that is too long but fits kKeffFastMax; the rest on the large path.
-        if (ks <= zs::kWKeffMax) {
-            pl.any_warp = true;
-            max_ksel_w = std::max(max_ksel_w, ks);
+        // The device puts a row in the first class whose limits ksel + its
+        // actual window (empty without a history) and the window fit: the short
+        // warp configuration, the long one, the CTA path; the rest on the large
+        // path.  Any class a row may take gets a block area (whatever the
+        // history), and a launch when this call can put a row there.
+        using S = zs::WCfgS;
+        using Lc = zs::WCfgL;
+        if (ks <= S::kKeffMax) {
+            pl.w[0].any = pl.w[0].launch = true;
+            pl.w[0].max_ksel = std::max(pl.w[0].max_ksel, ks);
         }
-        const bool long_win = wb > 0 && (ks + wb > zs::kWKeffMax || wb > zs::kWWinMax);
-        if (ks <= zs::kKeffFastMax && (ks > zs::kWKeffMax || long_win)) {
+        const bool long_s = wb > 0 && (ks + wb > S::kKeffMax || wb > S::kWinMax);
+        if (ks <= Lc::kKeffMax && (ks > S::kKeffMax || long_s)) {
+            pl.w[1].any = true;
+            pl.w[1].max_ksel = std::max(pl.w[1].max_ksel, ks);
+            if (ks > S::kKeffMax || have_history) pl.w[1].launch = true;
+        }
+        const bool long_l = wb > 0 && (ks + wb > Lc::kKeffMax || wb > Lc::kWinMax);
+        if (ks <= zs::kKeffFastMax && (ks > Lc::kKeffMax || long_l)) {
             pl.cta_area = true;
             max_keys = std::max(max_keys, partial_keys_for(ks, wb));
-            if (ks > zs::kWKeffMax || have_history) pl.launch_cta = true;
+            if (ks > Lc::kKeffMax || have_history) pl.launch_cta = true;
         }
         if (ks > zs::kKeffFastMax ||
             (have_history && ((long)ks + wb > zs::kKeffFastMax || wb > zs::kWinFastMax)))
@@ -170,10 +194,9 @@ Plan make_plan(int B, int V_cols, int V_total, const zs_params* params, int per_
     pl.slice = std::max(4, (per + 3) & ~3);
     pl.S = std::max(1, (V_cols + pl.slice - 1) / pl.slice);
     pl.part_stride = round_up(zs::kPartialHeaderBytes + 8LL * max_keys, 16);
-    const int64_t cta_bytes = pl.cta_area ? (int64_t)B * pl.S * pl.part_stride : 0;
-    plan_warp_layout(pl, B, V_cols, layout_warps, max_ksel_w, n_ranks);
-    pl.wl_off = round_up(cta_bytes, 256);
-    pl.bytes = pl.wl_off + (pl.any_warp ? (int64_t)pl.wl_NW * pl.wl_P * pl.wl_stride : 0);
+    for (int c = 0; c < 2; ++c)
+        plan_warp_layout(pl.w[c], B, V_cols, layout_warps[c], pl.w[c].max_ksel, n_ranks);
+    place_areas(pl, B);
     return pl;
 }
 
@@ -214,8 +237,8 @@ struct zs_context {
     size_t select_smem = 0;
     size_t merge_smem = 0;
     size_t warp_merge_smem = 0;
-    size_t wsel_smem = 0;
-    int wsel_warps = 0;  // warps of one full zs_wselect_kernel launch
+    size_t wsel_smem[2] = {0, 0};  // per warp configuration (WCfgS, WCfgL)
+    int wsel_warps[2] = {0, 0};    // warps of one full zs_wselect_kernel launch
     // scratch, grown on demand (never shrinks)
     uint8_t* part = nullptr;
     size_t part_bytes = 0;
@@ -380,18 +403,62 @@ zs::MergeArgs merge_args_for(const zs::Args& a, const Plan& pl, const uint8_t* g
     m.cand_probs = a.cand_probs;
     m.cand_ld = a.cand_ld;
     m.status = a.status;
-    m.wl_off = pl.wl_off;
-    m.wl_E = pl.wl_E;
-    m.wl_stride = pl.wl_stride;
-    m.wl_NW = pl.wl_NW;
-    m.wl_P = pl.wl_P;
-    m.wl_Vn = pl.wl_Vn;
+    for (int c = 0; c < 2; ++c) {
+        m.wl[c].off = pl.w[c].off;
+        m.wl[c].E = pl.w[c].E;
+        m.wl[c].stride = pl.w[c].stride;
+        m.wl[c].NW = pl.w[c].NW;
+        m.wl[c].P = pl.w[c].P;
+        m.wl[c].Vn = pl.w[c].Vn;
+    }
     return m;
 }
 
+// Sets a warp configuration's kernel attributes; its warps per full launch.
+template <class C>
+zs_status setup_wselect(size_t* smem, int* warps, int num_sms) {
+    *smem = sizeof(zs::WSelSmem<C>);
+    cudaError_t e;
+    if ((e = cudaFuncSetAttribute(zs::zs_wselect_kernel<C, true>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)*smem)) != cudaSuccess ||
+        (e = cudaFuncSetAttribute(zs::zs_wselect_kernel<C, false>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)*smem)) != cudaSuccess)
+        return cuda_fail(e, "cudaFuncSetAttribute zs_wselect_kernel");
+    int per_sm = 0;
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, zs::zs_wselect_kernel<C, false>,
+                                                           C::kWarps * 32, *smem)) != cudaSuccess)
+        return cuda_fail(e, "occupancy query");
+    if (per_sm < 1) return fail(ZS_ERR_NO_DEVICE, "zs_wselect_kernel does not fit an SM");
+    *warps = per_sm * num_sms * C::kWarps;
+    return ZS_OK;
+}
+
+// One warp configuration's launch over its layout in `blocks`.
+template <class C>
+zs_status launch_wselect(zs_context* h, zs::Args a, const Plan& pl, uint8_t* blocks, bool want_lse,
+                         cudaStream_t st) {
+    const Plan::Warp& L = pl.w[C::kClass];
+    a.wpart = blocks + L.off;
+    a.wl_E = L.E;
+    a.wl_stride = L.stride;
+    a.wl_NW = L.NW;
+    a.wl_P = L.P;
+    a.wl_Vn = L.Vn;
+    a.wl_class = C::kClass;
+    const int grid = (L.NW + C::kWarps - 1) / C::kWarps;
+    const size_t smem = h->wsel_smem[C::kClass];
+    LaunchScope scope(h, 0, st);
+    if (want_lse)
+        zs::zs_wselect_kernel<C, true><<<grid, C::kWarps * 32, smem, st>>>(a);
+    else
+        zs::zs_wselect_kernel<C, false><<<grid, C::kWarps * 32, smem, st>>>(a);
+    ZS_CUDA(cudaGetLastError());
+    return ZS_OK;
+}
+
 // Launches the select kernels that write one rank's partial blocks: the warp
-// kernel for warp-path rows, the CTA kernel (and its exact redo) for the rest
-// of the rows up to kKeffFastMax.  `blocks` is the rank's block area; a.status,
+// kernel's two configurations for their rows, the CTA kernel (and its exact
+// redo) for the rest of the rows up to kKeffFastMax.  `blocks` is the rank's block area; a.status,
 // a.fail_count and a.fail_units (>= B * S entries) are set by the caller.
 zs_status launch_partials(zs_context* h, zs::Args a, const Plan& pl, uint8_t* blocks,
                           bool want_lse, cudaStream_t st) {
@@ -400,21 +467,11 @@ zs_status launch_partials(zs_context* h, zs::Args a, const Plan& pl, uint8_t* bl
     a.n_units = (int32_t)std::min<int64_t>((int64_t)a.B * pl.S, INT32_MAX);
     a.part_stride = pl.part_stride;
     a.part = blocks;
-    a.wpart = blocks + pl.wl_off;
-    a.wl_E = pl.wl_E;
-    a.wl_stride = pl.wl_stride;
-    a.wl_NW = pl.wl_NW;
-    a.wl_P = pl.wl_P;
-    a.wl_Vn = pl.wl_Vn;
-    if (pl.any_warp) {
-        const int grid = (pl.wl_NW + zs::kWWarps - 1) / zs::kWWarps;
-        LaunchScope scope(h, 0, st);
-        if (want_lse)
-            zs::zs_wselect_kernel<true><<<grid, zs::kWThreads, h->wsel_smem, st>>>(a);
-        else
-            zs::zs_wselect_kernel<false><<<grid, zs::kWThreads, h->wsel_smem, st>>>(a);
-        ZS_CUDA(cudaGetLastError());
-    }
+    zs_status s = ZS_OK;
+    if (pl.w[0].launch && (s = launch_wselect<zs::WCfgS>(h, a, pl, blocks, want_lse, st)) != ZS_OK)
+        return s;
+    if (pl.w[1].launch && (s = launch_wselect<zs::WCfgL>(h, a, pl, blocks, want_lse, st)) != ZS_OK)
+        return s;
     if (pl.launch_cta) {
         a.redo = 0;
         ZS_CUDA(cudaMemsetAsync(a.fail_count, 0, sizeof(unsigned), st));
@@ -459,7 +516,7 @@ zs_status launch_select(zs_context* h, const zs::Args& base, const Plan& pl, boo
     a.fail_units = h->fail_units;
     s = launch_partials(h, a, pl, h->part, want_lse, st);
     if (s != ZS_OK) return s;
-    if (pl.any_warp || pl.cta_area) {
+    if (pl.w[0].any || pl.w[1].any || pl.cta_area) {
         const zs::MergeArgs m = merge_args_for(a, pl, h->part, 1, 0);
         s = launch_merge(h, m, pl.max_ksel, want_lse, st);
         if (s != ZS_OK) return s;
@@ -522,7 +579,6 @@ zs_status zs_create(int device, zs_handle* out) {
     h->select_smem = sizeof(zs::FastSmem);
     h->merge_smem = sizeof(zs::CandState);
     h->warp_merge_smem = sizeof(zs::WarpMergeSmem);
-    h->wsel_smem = sizeof(zs::WSelSmem);
     auto cleanup = [&](zs_status s) {
         delete h;
         return s;
@@ -535,15 +591,11 @@ zs_status zs_create(int device, zs_handle* out) {
         (e = cudaFuncSetAttribute(zs::zs_large_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->merge_smem)) != cudaSuccess ||
         (e = cudaFuncSetAttribute(zs::zs_large_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->merge_smem)) != cudaSuccess ||
         (e = cudaFuncSetAttribute(zs::zs_warp_merge_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->warp_merge_smem)) != cudaSuccess ||
-        (e = cudaFuncSetAttribute(zs::zs_warp_merge_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->warp_merge_smem)) != cudaSuccess ||
-        (e = cudaFuncSetAttribute(zs::zs_wselect_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->wsel_smem)) != cudaSuccess ||
-        (e = cudaFuncSetAttribute(zs::zs_wselect_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->wsel_smem)) != cudaSuccess)
+        (e = cudaFuncSetAttribute(zs::zs_warp_merge_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->warp_merge_smem)) != cudaSuccess)
         return cleanup(cuda_fail(e, "cudaFuncSetAttribute"));
-    int wsel_per_sm = 0;
-    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&wsel_per_sm, zs::zs_wselect_kernel<false>, zs::kWThreads, h->wsel_smem)) != cudaSuccess)
-        return cleanup(cuda_fail(e, "occupancy query"));
-    if (wsel_per_sm < 1) return cleanup(fail(ZS_ERR_NO_DEVICE, "zs_wselect_kernel does not fit an SM"));
-    h->wsel_warps = wsel_per_sm * h->num_sms * zs::kWWarps;
+    zs_status sw = setup_wselect<zs::WCfgS>(&h->wsel_smem[0], &h->wsel_warps[0], h->num_sms);
+    if (sw == ZS_OK) sw = setup_wselect<zs::WCfgL>(&h->wsel_smem[1], &h->wsel_warps[1], h->num_sms);
+    if (sw != ZS_OK) return cleanup(sw);
     int per_sm = 0;
     if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, zs::zs_select_kernel<false>, zs::kThreads, h->select_smem)) != cudaSuccess)
         return cleanup(cuda_fail(e, "occupancy query"));
@@ -875,14 +927,11 @@ zs_status noalloc_setup(int dev, NoAllocDevice** out) {
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d.ctx.merge_smem));
         ZS_CUDA(cudaFuncSetAttribute(zs::zs_warp_merge_kernel<false>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d.ctx.warp_merge_smem));
-        d.ctx.wsel_smem = sizeof(zs::WSelSmem);
-        ZS_CUDA(cudaFuncSetAttribute(zs::zs_wselect_kernel<false>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d.ctx.wsel_smem));
-        int wsel_per_sm = 0;
-        ZS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&wsel_per_sm, zs::zs_wselect_kernel<false>,
-                                                              zs::kWThreads, d.ctx.wsel_smem));
-        if (wsel_per_sm < 1) return fail(ZS_ERR_NO_DEVICE, "zs_wselect_kernel does not fit an SM");
-        d.ctx.wsel_warps = wsel_per_sm * d.ctx.num_sms * zs::kWWarps;
+        zs_status sw = setup_wselect<zs::WCfgS>(&d.ctx.wsel_smem[0], &d.ctx.wsel_warps[0],
+                                                d.ctx.num_sms);
+        if (sw == ZS_OK)
+            sw = setup_wselect<zs::WCfgL>(&d.ctx.wsel_smem[1], &d.ctx.wsel_warps[1], d.ctx.num_sms);
+        if (sw != ZS_OK) return sw;
         int per_sm = 0;
         ZS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, zs::zs_select_kernel<false>,
                                                               zs::kThreads, d.ctx.select_smem));
@@ -903,15 +952,12 @@ size_t noalloc_bytes(const Plan& pl, int64_t B) {
     return kNoAllocHeadBytes + ((units * sizeof(int32_t) + 255) & ~(size_t)255) + (size_t)pl.bytes;
 }
 
-// Re-cuts the CTA kernel's rows into S slices (the warp layout does not move).
+// Re-cuts the CTA kernel's rows into S slices (the warp layouts do not change).
 void replan_slices(Plan& pl, int B, int V, int S) {
     const int per = (V + S - 1) / S;
     pl.slice = std::max(4, (per + 3) & ~3);
     pl.S = std::max(1, (V + pl.slice - 1) / pl.slice);
-    const int64_t warp_bytes = pl.bytes - pl.wl_off;
-    const int64_t cta_bytes = pl.cta_area ? (int64_t)B * pl.S * pl.part_stride : 0;
-    pl.wl_off = round_up(cta_bytes, 256);
-    pl.bytes = pl.wl_off + warp_bytes;
+    place_areas(pl, B);
 }
 
 }  // namespace
