@@ -55,7 +55,8 @@ def _worker(rank, port, q):
         results = {}
         for name, p in (("k50", SamplingParams(temp=0.7, top_k=50, top_p=0.9)),
                         ("greedy", SamplingParams()),
-                        ("k256", SamplingParams(temp=1.0, top_p=0.95))):
+                        ("k256", SamplingParams(temp=1.0, top_p=0.95)),
+                        ("k1024", SamplingParams(temp=0.8, top_k=1024))):
             st0 = W.WORKLOADS[5].row_states(0, rows)
             st_one = states_to_tensor(st0, dev)
             one = s.sample(x, p, st_one, sync_check=True).ids.cpu().numpy()
