@@ -141,6 +141,20 @@ typedef struct zs_timing {
 zs_status zs_set_timing(zs_handle h, int32_t enable);
 zs_status zs_get_timing(zs_handle h, zs_timing* out);
 
+/* The display numbers of zeninfer's `logits` command (src/main.cpp:473-503) for each
+ * of `batch` rows of n_vocab f32 logits (device, row r at logits + r * ld):
+ *   out_min, out_max  device double [batch]: the row's smallest and largest value,
+ *                     from starts of 1e30 and -1e30 as there (NaN ignored)
+ *   out_z             device double [batch]: sum over the row of exp(x - max), f64
+ *   top_ids           device int32 [batch][topn]: the k = clamp(topn, 1, n_vocab)
+ *                     largest ids, value descending then id ascending (the reference's
+ *                     partial_sort leaves equal values in libstdc++'s order)
+ *   top_p             device double [batch][topn]: exp(x - max) / Z of those ids
+ * Entries k..topn-1 of a row are left as they were. */
+zs_status zs_logits_stats(zs_handle h, const float* logits, int64_t ld, int32_t batch,
+                          int32_t n_vocab, int32_t topn, double* out_min, double* out_max,
+                          double* out_z, int32_t* top_ids, double* top_p, void* stream);
+
 /* ---------------------------------------------------------------------------------
  * Vocab-sharded sampling (tensor-parallel lm_head layout).  Rank g of n_ranks
  * holds columns [vocab_offset, vocab_offset + n_local) of every row.  Each rank

@@ -64,6 +64,9 @@ def olib():
         L.zo_rng_seed.restype = C.c_uint64
         L.zo_rng_uniform.argtypes = [C.POINTER(C.c_uint64)]
         L.zo_rng_uniform.restype = C.c_double
+        L.zo_logits_stats.argtypes = [vp, C.c_int64, C.c_int, C.c_int, C.c_int, vp, vp, vp, vp,
+                                      vp, C.c_int64]
+        L.zo_logits_stats.restype = C.c_int
         _olib = L
     return _olib
 
@@ -120,6 +123,23 @@ def oracle_sample(logits: np.ndarray, params, states: np.ndarray, history=None, 
                           _ptr(hl), states.ctypes.data, ids.ctypes.data, _ptr(cid), _ptr(cv),
                           _ptr(cp), cand_ld, infos.ctypes.data, 1 if full_z else 0, nthreads)
     return ids, infos, cid, cv, cp
+
+
+def oracle_logits_stats(logits: np.ndarray, topn: int):
+    """The `logits` command's display numbers (src/main.cpp:473-503) per row of
+    `logits` [B, n]: dict of min, max, z (float64 [B]), top_ids (int32 [B, k]) and
+    top_p (float64 [B, k]), k = clamp(topn, 1, n), top-N in value-desc, id-asc order."""
+    x = np.ascontiguousarray(logits, dtype=np.float32)
+    B, n = x.shape
+    k = max(1, min(topn, n))
+    out = {"min": np.zeros(B), "max": np.zeros(B), "z": np.zeros(B),
+           "top_ids": np.full((B, k), -1, dtype=np.int32), "top_p": np.zeros((B, k))}
+    rc = olib().zo_logits_stats(x.ctypes.data, n, B, n, topn, out["min"].ctypes.data,
+                                out["max"].ctypes.data, out["z"].ctypes.data,
+                                out["top_ids"].ctypes.data, out["top_p"].ctypes.data, k)
+    if rc != 0:
+        raise ValueError("zo_logits_stats failed")
+    return out
 
 
 def reference_sample(logits: np.ndarray, params, seeds: np.ndarray, history=None,

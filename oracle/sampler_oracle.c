@@ -336,3 +336,45 @@ int zo_sample_rows(const float* logits, int64_t ld, int B, int n, const zo_param
     pthread_mutex_destroy(&b.mu);
     return 0;
 }
+
+/*
+ * The display numbers of the `logits` command, src/main.cpp:473-503, one row at a
+ * time (test infrastructure, like everything here): min and max as double from
+ * starts of 1e30 / -1e30 (std::min / std::max ignore a NaN the way these compares
+ * do), Z = sum of exp((double)x - max) in index order, the top-k ids with k =
+ * clamp(topn, 1, n) in the total order (value descending, id ascending; the
+ * reference's partial_sort leaves ties in libstdc++'s order) and p = exp(x - max)/Z.
+ * top_ids / top_p rows are top_ld apart.
+ */
+int zo_logits_stats(const float* logits, int64_t ld, int B, int n, int topn, double* out_min,
+                    double* out_max, double* out_z, int32_t* top_ids, double* top_p,
+                    int64_t top_ld) {
+    if (n <= 0) return -1;
+    const int k = topn < 1 ? 1 : (topn > n ? n : topn);
+    uint64_t* keys = (uint64_t*)malloc((size_t)n * sizeof(uint64_t));
+    if (!keys) return -1;
+    for (int r = 0; r < B; ++r) {
+        const float* x = logits + (int64_t)r * ld;
+        double mx = -1e30, mn = 1e30;
+        for (int i = 0; i < n; ++i) {
+            const double v = (double)x[i];
+            mx = (mx < v) ? v : mx; /* std::max<double>(max_l, v) */
+            mn = (v < mn) ? v : mn; /* std::min<double>(min_l, v) */
+        }
+        double z = 0.0;
+        for (int i = 0; i < n; ++i) z += exp((double)x[i] - mx);
+        for (int i = 0; i < n; ++i) keys[i] = key_of(x[i], i);
+        select_largest(keys, (size_t)n, (size_t)k);
+        qsort(keys, (size_t)k, sizeof(uint64_t), cmp_desc);
+        out_min[r] = mn;
+        out_max[r] = mx;
+        out_z[r] = z;
+        for (int i = 0; i < k; ++i) {
+            const int32_t id = id_of(keys[i]);
+            top_ids[(int64_t)r * top_ld + i] = id;
+            top_p[(int64_t)r * top_ld + i] = exp((double)x[id] - mx) / z;
+        }
+    }
+    free(keys);
+    return 0;
+}

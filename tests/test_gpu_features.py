@@ -304,3 +304,34 @@ def test_cpp_api_on_device(sampler, tmp_path):
         id_, g, s = line.split()
         assert int(id_) == oids[r] and int(s) == int(st[r])
         assert int(g) == oracle.oracle_argmax(x[r])
+
+
+@pytest.mark.parametrize("topn", [1, 8, 50, 1024])
+def test_logits_stats(sampler, topn):
+    """The `logits` command's display numbers on the device against the restatement."""
+    import torch
+    rows = 6
+    x = np.concatenate([W.generate(2, 3, row0=70), W.generate(4, 3, row0=70)])  # ties in 3..5
+    x[1, 9] = np.nan
+    x[2, :] = -np.inf
+    g = sampler.logits_stats(torch.from_numpy(x).to(sampler.device), topn)
+    o = oracle.oracle_logits_stats(x, topn)
+    np.testing.assert_array_equal(g["min"].cpu().numpy(), o["min"])
+    np.testing.assert_array_equal(g["max"].cpu().numpy(), o["max"])
+    np.testing.assert_allclose(g["z"].cpu().numpy(), o["z"], rtol=1e-12, equal_nan=True)
+    ids = g["top_ids"].cpu().numpy()
+    live = [0, 1, 3, 4, 5]  # row 2 has no finite value: its top is any order of -inf ties
+    np.testing.assert_array_equal(ids[live], o["top_ids"][live])
+    np.testing.assert_allclose(g["top_p"].cpu().numpy()[live], o["top_p"][live], rtol=1e-12)
+
+
+def test_logits_stats_short_rows(sampler):
+    import torch
+    rng = np.random.default_rng(12)
+    for n, pad in ((1, 0), (5, 3), (17000, 1), (40000, 2)):
+        xf = rng.normal(0, 1, size=(3, n + pad)).astype(np.float32)
+        xd = torch.from_numpy(xf).to(sampler.device)[:, :n]
+        g = sampler.logits_stats(xd, 10)
+        o = oracle.oracle_logits_stats(np.ascontiguousarray(xf[:, :n]), 10)
+        np.testing.assert_array_equal(g["top_ids"].cpu().numpy(), o["top_ids"])
+        np.testing.assert_allclose(g["z"].cpu().numpy(), o["z"], rtol=1e-12)

@@ -70,3 +70,15 @@ def test_row_and_vocab_ranges(world):
         assert got[0][0] == 0 and got[-1][0] + got[-1][1] == V
         assert all(got[g][0] + got[g][1] == got[g + 1][0] for g in range(world - 1))
     assert sharding.vocab_range(151936, 8, 7) == (7 * 18992, 18992)
+
+
+def test_logits_file_roundtrip(tmp_path):
+    from zeninfer_b200 import logits_io
+    x = np.random.default_rng(1).normal(0, 1, size=(3, 1000)).astype(np.float32)
+    p = str(tmp_path / "l.bin")
+    logits_io.write_logits(p, x)
+    assert (tmp_path / "l.bin").stat().st_size == x.size * 4  # raw <f4, no header
+    y = logits_io.read_logits(p, n_vocab=1000)
+    assert y.shape == (3, 1000) and np.array_equal(np.asarray(y), x)
+    with pytest.raises(ValueError):
+        logits_io.read_logits(p, n_vocab=999)

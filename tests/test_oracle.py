@@ -188,3 +188,44 @@ def test_restatement_internal_consistency():
                 break
         assert pos == want
         assert ids[r] == cid[r, pos]
+
+
+def _stats_numpy(x, topn):
+    """src/main.cpp:473-503 in numpy (sequential f64 sum kept as a loop of adds)."""
+    B, n = x.shape
+    k = max(1, min(topn, n))
+    out = {"min": [], "max": [], "z": [], "top_ids": [], "top_p": []}
+    for r in range(B):
+        row = x[r].astype(np.float64)
+        mx, mn = -1e30, 1e30
+        for v in row:
+            mx = v if mx < v else mx
+            mn = v if v < mn else mn
+        z = 0.0
+        for v in np.exp(row - mx):
+            z += float(v)
+        ids = sorted(range(n), key=lambda i: (-x[r, i] if x[r, i] == x[r, i] else np.inf, i))[:k]
+        out["min"].append(mn)
+        out["max"].append(mx)
+        out["z"].append(z)
+        out["top_ids"].append(ids)
+        out["top_p"].append([np.exp(float(x[r, i]) - mx) / z if z else np.nan for i in ids])
+    return {kk: np.array(v) for kk, v in out.items()}
+
+
+@pytest.mark.parametrize("topn", [0, 1, 8, 50, 3000])
+def test_logits_stats_restatement(topn):
+    rng = np.random.default_rng(topn + 1)
+    x = rng.normal(0, 2, size=(4, 2000)).astype(np.float32)
+    x[1] = np.round(x[1] * 2) / 2     # ties
+    x[2, 5] = np.nan                   # NaN: never counted, never in the top
+    x[3, :] = -np.inf                  # nothing above the -1e30 start
+    x[3, 7] = -np.inf
+    o = oracle.oracle_logits_stats(x, topn)
+    r = _stats_numpy(x, topn)
+    np.testing.assert_array_equal(o["min"], r["min"])
+    np.testing.assert_array_equal(o["max"], r["max"])
+    np.testing.assert_allclose(o["z"], r["z"], rtol=1e-13, equal_nan=True)
+    np.testing.assert_array_equal(o["top_ids"][:3], r["top_ids"][:3])
+    np.testing.assert_allclose(o["top_p"], r["top_p"], rtol=1e-13, equal_nan=True)
+    assert o["max"][3] == -1e30 and o["min"][3] == -np.inf

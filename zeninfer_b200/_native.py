@@ -17,7 +17,7 @@ EXPORTS = (
     "zs_create", "zs_destroy", "zs_last_error", "zs_status_string", "zs_abi_version",
     "zs_rng_seed", "zs_sample", "zs_argmax", "zs_check_device_status",
     "zs_shard_partial_bytes", "zs_shard_partials", "zs_shard_merge", "zs_sample_sharded",
-    "zs_sample_noalloc", "zs_set_timing", "zs_get_timing",
+    "zs_sample_noalloc", "zs_set_timing", "zs_get_timing", "zs_logits_stats",
 )
 
 ZS_OK = 0
@@ -81,6 +81,7 @@ def lib() -> C.CDLL:
                                  C.POINTER(ZsExtras), vp]
     L.zs_sample_sharded.argtypes = [vp, vp, i64, i32, i32, i32, i32, i32, C.POINTER(ZsParams), i32,
                                     vp, i64, vp, vp, vp, C.POINTER(ZsExtras), vp, vp]
+    L.zs_logits_stats.argtypes = [vp, vp, i64, i32, i32, i32, vp, vp, vp, vp, vp, vp]
     L.zs_set_timing.argtypes = [vp, i32]
     L.zs_get_timing.argtypes = [vp, C.POINTER(ZsTiming)]
     L.zs_sample_noalloc.argtypes = [vp, i64, i32, i32, C.POINTER(ZsParams), vp, i64, vp, vp, vp,
@@ -91,7 +92,8 @@ def lib() -> C.CDLL:
                                             "zs_check_device_status", "zs_shard_partial_bytes",
                                             "zs_shard_partials", "zs_shard_merge",
                                             "zs_sample_sharded", "zs_sample_noalloc",
-                                            "zs_set_timing", "zs_get_timing"):
+                                            "zs_set_timing", "zs_get_timing",
+                                            "zs_logits_stats"):
             f.restype = C.c_int
     _lib = L
     return L

@@ -20,6 +20,7 @@
 
 #include "zs_kernels.cuh"
 #include "zs_sampler.h"
+#include "zs_stats.cuh"
 
 static_assert(sizeof(zs_params) == sizeof(zs::Params), "zs_params layout");
 static_assert(sizeof(zs_row_info) == sizeof(zs::RowInfo), "zs_row_info layout");
@@ -261,6 +262,13 @@ struct zs_context {
     std::vector<TimedLaunch> timed;      // recorded since the last zs_get_timing
     std::vector<cudaEvent_t> spare;      // events free for reuse
     int64_t launches = 0;                // kernel launches since the last zs_get_timing
+    // zs_logits_stats: where the draw of its top-N selection lands, chunk partials
+    uint64_t* stats_rng = nullptr;
+    size_t stats_rng_bytes = 0;
+    int32_t* stats_ids = nullptr;
+    size_t stats_ids_bytes = 0;
+    uint8_t* stats_part = nullptr;
+    size_t stats_part_bytes = 0;
 };
 
 namespace {
@@ -619,6 +627,9 @@ zs_status zs_destroy(zs_handle h) {
     cudaFree(h->gather);
     cudaFree(h->fail_count);
     cudaFree(h->fail_units);
+    cudaFree(h->stats_rng);
+    cudaFree(h->stats_ids);
+    cudaFree(h->stats_part);
     for (auto& t : h->timed) {
         cudaEventDestroy(t.begin);
         cudaEventDestroy(t.end);
@@ -731,6 +742,69 @@ zs_status zs_check_device_status(zs_handle h, void* stream) {
         ZS_CUDA(cudaMemset(h->status, 0, sizeof(int)));
         return fail(ZS_ERR_DEVICE_TIMEOUT, "a sampler kernel gave up on a bounded wait");
     }
+    return ZS_OK;
+}
+
+zs_status zs_logits_stats(zs_handle h, const float* logits, int64_t ld, int32_t batch,
+                          int32_t n_vocab, int32_t topn, double* out_min, double* out_max,
+                          double* out_z, int32_t* top_ids, double* top_p, void* stream) {
+    if (!h) return fail(ZS_ERR_INVALID_ARGUMENT, "null handle");
+    if (batch < 0 || topn < 0) return fail(ZS_ERR_INVALID_ARGUMENT, "batch or topn < 0");
+    if (batch == 0) return ZS_OK;
+    if (n_vocab <= 0) return fail(ZS_ERR_INVALID_ARGUMENT, "n_vocab <= 0");
+    if (!logits || !out_min || !out_max || !out_z || !top_ids || !top_p || topn < 1)
+        return fail(ZS_ERR_INVALID_ARGUMENT, "null buffer or topn < 1");
+    if (((uintptr_t)logits & 3u) != 0) return fail(ZS_ERR_INVALID_ARGUMENT, "logits not 4-byte aligned");
+    if (ld < n_vocab) return fail(ZS_ERR_INVALID_ARGUMENT, "ld < n_vocab");
+    cudaStream_t st = (cudaStream_t)stream;
+    DeviceGuard g(h->device);
+    if (!g.ok) return fail(ZS_ERR_CUDA, "cudaSetDevice failed");
+    // src/main.cpp:483: k = clamp(topk, 1, n_vocab)
+    const int k = std::max(1, std::min(topn, n_vocab));
+    zs_status s = grow((void**)&h->stats_rng, &h->stats_rng_bytes, (size_t)batch * 8);
+    if (s == ZS_OK) s = grow((void**)&h->stats_ids, &h->stats_ids_bytes, (size_t)batch * 4);
+    const int nchunk = (n_vocab + zs::kStatsChunk - 1) / zs::kStatsChunk;
+    if (s == ZS_OK)
+        s = grow((void**)&h->stats_part, &h->stats_part_bytes, (size_t)batch * nchunk * 16);
+    if (s != ZS_OK) return s;
+    // The top-k shortlist of a temp-1 call is the top-N in the display order
+    // (value descending, then id ascending); its draw goes to scratch.
+    ZS_CUDA(cudaMemsetAsync(h->stats_rng, 0, (size_t)batch * 8, st));
+    zs_params p;
+    p.temp = 1.0f;
+    p.top_k = k;
+    p.top_p = 1.0f;
+    p.repeat_penalty = 1.0f;
+    p.repeat_last_n = 0;
+    zs_extras ex;
+    std::memset(&ex, 0, sizeof(ex));
+    ex.cand_ids = top_ids;
+    ex.cand_ld = topn;
+    s = zs_sample(h, logits, ld, batch, n_vocab, &p, 0, nullptr, 0, nullptr, h->stats_rng,
+                  h->stats_ids, &ex, stream);
+    if (s != ZS_OK) return s;
+    zs::StatsArgs a;
+    a.logits = logits;
+    a.ld = ld;
+    a.B = batch;
+    a.n = n_vocab;
+    a.nchunk = nchunk;
+    a.part_mm = reinterpret_cast<float2*>(h->stats_part);
+    a.part_z = reinterpret_cast<double*>(h->stats_part + (size_t)batch * nchunk * 8);
+    a.top_ids = top_ids;
+    a.topn = k;
+    a.top_ld = topn;
+    a.out_min = out_min;
+    a.out_max = out_max;
+    a.out_z = out_z;
+    a.top_p = top_p;
+    const dim3 grid(nchunk, std::min(batch, 65535));
+    zs::zs_stats_minmax_kernel<<<grid, zs::kStatsThreads, 0, st>>>(a);
+    ZS_CUDA(cudaGetLastError());
+    zs::zs_stats_z_kernel<<<grid, zs::kStatsThreads, 0, st>>>(a);
+    ZS_CUDA(cudaGetLastError());
+    zs::zs_stats_final_kernel<<<std::min(batch, 65535), 32, 0, st>>>(a);
+    ZS_CUDA(cudaGetLastError());
     return ZS_OK;
 }
 

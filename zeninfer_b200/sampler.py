@@ -198,6 +198,29 @@ class Sampler:
                                           out.data_ptr(), _stream_ptr(stream)), "zs_argmax")
         return out
 
+    def logits_stats(self, logits, topn: int = 8, stream=None) -> dict:
+        """The `logits` command's display numbers (src/main.cpp:473-503) for every
+        row of `logits` ([B, V] float32 CUDA): min, max and Z = sum exp(x - max)
+        (float64 [B]), the top-N ids (value descending, then id ascending) and their
+        p = exp(x - max) / Z ([B, k], k = clamp(topn, 1, V)), all on the device."""
+        import torch
+        if logits.dim() == 1:
+            logits = logits.unsqueeze(0)
+        if logits.dtype != torch.float32 or logits.device != self.device or logits.stride(1) != 1:
+            raise ValueError("logits must be float32, unit column stride, on the sampler's device")
+        B, V = logits.shape
+        k = max(1, min(int(topn), V))
+        f64 = dict(dtype=torch.float64, device=self.device)
+        out = {"min": torch.empty(B, **f64), "max": torch.empty(B, **f64),
+               "z": torch.empty(B, **f64),
+               "top_ids": torch.full((B, k), -1, dtype=torch.int32, device=self.device),
+               "top_p": torch.zeros((B, k), **f64)}
+        _native.check(self._lib.zs_logits_stats(
+            self._h, logits.data_ptr(), logits.stride(0), B, V, k, out["min"].data_ptr(),
+            out["max"].data_ptr(), out["z"].data_ptr(), out["top_ids"].data_ptr(),
+            out["top_p"].data_ptr(), _stream_ptr(stream)), "zs_logits_stats")
+        return out
+
     def set_timing(self, enable: bool) -> None:
         """Bracket every kernel of this sampler with CUDA events (measurement only)."""
         _native.check(self._lib.zs_set_timing(self._h, 1 if enable else 0), "zs_set_timing")
