@@ -217,6 +217,9 @@ def main():
     ap.add_argument("--rows", type=int, default=ROWS,
                     help="rows per GPU (default 4096, the benchmark batch; smaller only "
                          "for profiling captures)")
+    ap.add_argument("--logits-file", default=None,
+                    help="raw <f4 [S][V] logits written by zeninfer's `logits --out` (its rows "
+                         "repeated to fill the batch) instead of the synthetic workload")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
@@ -261,7 +264,16 @@ def main():
     # Host copy of this rank's rows (distinct rows per rank), pinned for the e2e leg.
     row0 = rank * rows
     x_host = torch.empty((rows, V), dtype=torch.float32).pin_memory()
-    W.generate(WORKLOAD, rows, row0=row0, out=x_host.numpy())
+    data = "synthetic"
+    if args.logits_file:
+        from zeninfer_b200 import logits_io
+        src = logits_io.read_logits(args.logits_file, V)
+        xh = x_host.numpy()
+        for r in range(rows):
+            xh[r] = src[(row0 + r) % src.shape[0]]
+        data = f"file {os.path.basename(args.logits_file)} ({src.shape[0]} rows, repeated)"
+    else:
+        W.generate(WORKLOAD, rows, row0=row0, out=x_host.numpy())
     x_dev = x_host.to(dev)
     states0 = wl.row_states(row0, rows)
     st = states_to_tensor(states0, dev)
@@ -324,6 +336,30 @@ def main():
     by_batch[str(rows)] = {"rows_per_s": rows / (ms_step / 1e3), "us_per_call": ms_step * 1e3,
                            "logits_gbs": step_gbs, "hbm_frac": step_gbs / peak,
                            "params": "temp 0.7, top-k 50, top-p 0.9"}
+
+    # The `logits` command's display numbers (src/main.cpp:473-503) for one row,
+    # the last position's, as that command computes them: device-timed, beside the
+    # restatement timed on one host thread.
+    display = None
+    if rank == 0:
+        x1 = x_dev[:1]
+        for _ in range(3):
+            s.logits_stats(x1, 8, stream=stream)
+        torch.cuda.synchronize()
+        reps = 100
+        ms_disp = time_device_steps(lambda: s.logits_stats(x1, 8, stream=stream), reps,
+                                    stream) / reps
+        display = {"rows": 1, "topn": 8, "gpu_us_per_call": ms_disp * 1e3}
+        try:
+            import oracle
+            row = x_host[:1].numpy()
+            t0 = time.perf_counter()
+            for _ in range(5):
+                oracle.oracle_logits_stats(row, 8)
+            display["cpu_restatement_us_per_call"] = (time.perf_counter() - t0) / 5 * 1e6
+        except Exception as e:  # reported, never fatal
+            display["cpu_restatement_us_per_call"] = None
+            display["cpu_note"] = str(e)
 
     # End to end through the public API with host buffers: H2D of the step's
     # logits from pinned memory, the sampler, D2H of the ids, every step.
@@ -396,7 +432,7 @@ def main():
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f32 (f64 shortlist softmax)", "data": "synthetic",
+            "dtype": "f32 (f64 shortlist softmax)", "data": data,
             "config": {"workload": f"{rows} x 151936 f32 logits per GPU (workload 5: N(0,2.5^2)"
                                    " + offset + 8 peaks), temp 0.7, top-k 50, top-p 0.9",
                        "rows_per_gpu": rows, "vocab": V, "parallelism": f"row-split x{world}",
@@ -419,6 +455,8 @@ def main():
         }
         if sharded:
             line["vocab_sharded"] = sharded
+        if display:
+            line["logits_display"] = display
         print(json.dumps(line), flush=True)
 
     s.close()
