@@ -128,6 +128,13 @@ zs_status zs_argmax(zs_handle h, const float* logits, int64_t ld, int32_t batch,
  * gave up on a bounded wait since the last check (the flag is then cleared). */
 zs_status zs_check_device_status(zs_handle h, void* stream);
 
+/* Exercises the failure path of the device waits: launches one thread that waits,
+ * with the select kernels' bounded wait, on a barrier nothing ever completes; after
+ * the limit (1 s) it records ZS_ERR_DEVICE_TIMEOUT for this handle and returns, so
+ * the next zs_check_device_status reports it.  No GPU fault, nothing left running.
+ * No counterpart in the reference (its sampler has no device code). */
+zs_status zs_selftest_wait_timeout(zs_handle h, void* stream);
+
 /* Per-kernel device time, for measurement.  While timing is on, every kernel this
  * handle launches is bracketed by CUDA events on its stream.  zs_get_timing waits
  * for those events, returns the sums since the previous zs_get_timing (or since

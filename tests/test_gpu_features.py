@@ -335,3 +335,22 @@ def test_logits_stats_short_rows(sampler):
         o = oracle.oracle_logits_stats(np.ascontiguousarray(xf[:, :n]), 10)
         np.testing.assert_array_equal(g["top_ids"].cpu().numpy(), o["top_ids"])
         np.testing.assert_allclose(g["z"].cpu().numpy(), o["z"], rtol=1e-12)
+
+
+def test_device_wait_timeout_is_reported(sampler):
+    """A device wait that runs out (a barrier nothing completes) is reported as
+    ZS_ERR_DEVICE_TIMEOUT by the next status check, the flag is then cleared, and
+    the context keeps working."""
+    import ctypes as C
+    import torch
+    from zeninfer_b200 import _native
+    L = _native.lib()
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert L.zs_selftest_wait_timeout(sampler._h, stream) == 0
+    assert L.zs_check_device_status(sampler._h, stream) == 4  # ZS_ERR_DEVICE_TIMEOUT
+    assert b"bounded wait" in L.zs_last_error()
+    assert L.zs_check_device_status(sampler._h, stream) == 0  # cleared
+    x = W.generate(2, 8, row0=123)
+    p = SamplingParams(temp=0.7, top_k=40, top_p=0.9)
+    st = _states(range(8))
+    compare(run_gpu(sampler, x, p, st), run_oracle(x, p, st))

@@ -18,6 +18,7 @@ EXPORTS = (
     "zs_rng_seed", "zs_sample", "zs_argmax", "zs_check_device_status",
     "zs_shard_partial_bytes", "zs_shard_partials", "zs_shard_merge", "zs_sample_sharded",
     "zs_sample_noalloc", "zs_set_timing", "zs_get_timing", "zs_logits_stats",
+    "zs_selftest_wait_timeout",
 )
 
 ZS_OK = 0
@@ -81,6 +82,7 @@ def lib() -> C.CDLL:
                                  C.POINTER(ZsExtras), vp]
     L.zs_sample_sharded.argtypes = [vp, vp, i64, i32, i32, i32, i32, i32, C.POINTER(ZsParams), i32,
                                     vp, i64, vp, vp, vp, C.POINTER(ZsExtras), vp, vp]
+    L.zs_selftest_wait_timeout.argtypes = [vp, vp]
     L.zs_logits_stats.argtypes = [vp, vp, i64, i32, i32, i32, vp, vp, vp, vp, vp, vp]
     L.zs_set_timing.argtypes = [vp, i32]
     L.zs_get_timing.argtypes = [vp, C.POINTER(ZsTiming)]
@@ -93,7 +95,7 @@ def lib() -> C.CDLL:
                                             "zs_shard_partials", "zs_shard_merge",
                                             "zs_sample_sharded", "zs_sample_noalloc",
                                             "zs_set_timing", "zs_get_timing",
-                                            "zs_logits_stats"):
+                                            "zs_logits_stats", "zs_selftest_wait_timeout"):
             f.restype = C.c_int
     _lib = L
     return L

@@ -2536,6 +2536,19 @@ __global__ void __launch_bounds__(C::kWarps * 32, 1) zs_wselect_kernel(const Arg
     }
 }
 
+// Failure-path check: one thread waits, with the same bounded wait as the select
+// kernels, on an mbarrier phase that nothing completes (no arrival is ever made),
+// so the wait runs out after kWaitLimitNs and the kernel reports
+// ZS_ERR_DEVICE_TIMEOUT in `status` and returns.  Nothing is in flight.
+__global__ void zs_wait_selftest_kernel(int* status) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        mbar_fence_init();
+        if (!mbar_wait_bounded(&bar, 0u)) set_status(status, kStatusTimeout);
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Large-shortlist path: rows whose top-k + penalty window exceeds the shared
 // candidate buffer (top_k > 2048, or very long penalty windows).  One CTA per

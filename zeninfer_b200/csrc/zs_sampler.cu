@@ -745,6 +745,15 @@ zs_status zs_check_device_status(zs_handle h, void* stream) {
     return ZS_OK;
 }
 
+zs_status zs_selftest_wait_timeout(zs_handle h, void* stream) {
+    if (!h) return fail(ZS_ERR_INVALID_ARGUMENT, "null handle");
+    DeviceGuard g(h->device);
+    if (!g.ok) return fail(ZS_ERR_CUDA, "cudaSetDevice failed");
+    zs::zs_wait_selftest_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(h->status);
+    ZS_CUDA(cudaGetLastError());
+    return ZS_OK;
+}
+
 zs_status zs_logits_stats(zs_handle h, const float* logits, int64_t ld, int32_t batch,
                           int32_t n_vocab, int32_t topn, double* out_min, double* out_max,
                           double* out_z, int32_t* top_ids, double* top_p, void* stream) {
