@@ -237,7 +237,7 @@ def main():
     import numpy as np
     import torch
     import torch.distributed as dist
-    from zeninfer_b200 import Sampler, states_to_tensor
+    from zeninfer_b200 import Sampler, SamplingParams, states_to_tensor
     from zeninfer_b200 import workloads as W
 
     torch.cuda.set_device(local_rank)
@@ -361,6 +361,48 @@ def main():
             display["cpu_restatement_us_per_call"] = None
             display["cpu_note"] = str(e)
 
+    # The generate loop (src/main.cpp:626-632) with history, Rng states and stop
+    # flags on the device (zs_decode_step): per-step device time at 1 and 256
+    # sequences with the penalty on, beside the reference's sample_token per step on
+    # one host thread (host logits, the history as a std::vector).
+    decode = None
+    if rank == 0:
+        pdec = SamplingParams(temp=0.7, top_k=40, top_p=0.9, repeat_penalty=1.1,
+                              repeat_last_n=64)
+        decode = {"params": "temp 0.7, top-k 40, top-p 0.9, repeat_penalty 1.1, last 64",
+                  "history_ld": 128}
+        for b in (1, 256):
+            xd = x_dev[:b]
+            rngd = states_to_tensor(states0[:b], dev)
+            doned = torch.zeros(b, dtype=torch.int32, device=dev)
+            histd = torch.zeros((b, 128), dtype=torch.int32, device=dev)
+            hlend = torch.zeros(b, dtype=torch.int32, device=dev)
+            outd = torch.empty(b, dtype=torch.int32, device=dev)
+
+            def dstep(xd=xd, rngd=rngd, doned=doned, histd=histd, hlend=hlend, outd=outd):
+                s.decode_step(xd, pdec, rngd, doned, -1, histd, hlend, out=outd, stream=stream)
+
+            for _ in range(5):
+                dstep()
+            torch.cuda.synchronize()
+            reps = 200
+            msd = time_device_steps(dstep, reps, stream) / reps
+            decode[f"gpu_us_per_step_b{b}"] = msd * 1e3
+            decode[f"tokens_per_s_b{b}"] = b / (msd / 1e3)
+        try:
+            import oracle
+            if oracle.have_reference():
+                row = x_host[:1].numpy()
+                hist = np.arange(64, dtype=np.int32)[None, :] * 997 % V
+                n_ref = 10
+                t0 = time.perf_counter()
+                for i in range(n_ref):
+                    oracle.reference_sample(row, pdec, np.array([i + 1], np.uint64), hist,
+                                            np.array([64], np.int32), nthreads=1)
+                decode["reference_us_per_step_b1"] = (time.perf_counter() - t0) / n_ref * 1e6
+        except Exception as e:  # reported, never fatal
+            decode["reference_note"] = str(e)
+
     # End to end through the public API with host buffers: H2D of the step's
     # logits from pinned memory, the sampler, D2H of the ids, every step.
     e2e = None
@@ -457,6 +499,8 @@ def main():
             line["vocab_sharded"] = sharded
         if display:
             line["logits_display"] = display
+        if decode:
+            line["decode_loop"] = decode
         print(json.dumps(line), flush=True)
 
     s.close()

@@ -119,6 +119,27 @@ zs_status zs_sample(zs_handle h, const float* logits, int64_t ld, int32_t batch,
                     int64_t history_ld, const int32_t* history_len, uint64_t* rng_state,
                     int32_t* out_ids, const zs_extras* extras, void* stream);
 
+/*
+ * One step of the generate loop (src/main.cpp:626-632) with the history, the Rng
+ * states and the stop flags on the device, so a decode loop needs no host copy:
+ *   next = sample_token(logits, V, params, history, rng); if (next == eos) stop;
+ *   history.push_back(next)
+ * for every row whose done[r] is 0 on entry.  Rows with done[r] != 0 draw nothing
+ * (their rng_state is left as it was) and get out_ids[r] = -1.  A row that samples
+ * eos_id sets done[r] = 1 and does not append it (the reference breaks before the
+ * push).  Other rows append to history (device [batch][history_ld], lengths in
+ * history_len); a full row keeps its last repeat_last_n entries first, so
+ * history_ld must exceed repeat_last_n for every row with repeat_penalty != 1.
+ * history and history_len may both be NULL (no penalty, nothing appended).
+ * tokens (device [batch][tokens_ld], may be NULL) receives out_ids at column `step`.
+ * No counterpart function in the reference: cmd_generate inlines this loop.
+ */
+zs_status zs_decode_step(zs_handle h, const float* logits, int64_t ld, int32_t batch,
+                         int32_t n_vocab, const zs_params* params, int32_t params_per_row,
+                         int32_t* history, int64_t history_ld, int32_t* history_len,
+                         uint64_t* rng_state, int32_t* done, int32_t eos_id, int32_t* out_ids,
+                         int32_t* tokens, int64_t tokens_ld, int64_t step, void* stream);
+
 /* Batched argmax_token (src/sample.cpp:24-30): first index of the maximum; a NaN at
  * index 0 yields 0.  No penalty, no draw. */
 zs_status zs_argmax(zs_handle h, const float* logits, int64_t ld, int32_t batch, int32_t n_vocab,

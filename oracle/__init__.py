@@ -31,7 +31,9 @@ PARAMS_DTYPE = np.dtype([("temp", "<f4"), ("top_k", "<i4"), ("top_p", "<f4"),
 
 
 def params_array(params, batch=None) -> np.ndarray:
-    """SamplingParams-like object(s) -> PARAMS_DTYPE array."""
+    """SamplingParams-like object(s) (or a PARAMS_DTYPE array) -> PARAMS_DTYPE array."""
+    if isinstance(params, np.ndarray) and params.dtype == PARAMS_DTYPE:
+        return np.ascontiguousarray(params)
     if not isinstance(params, (list, tuple)):
         params = [params]
     arr = np.zeros(len(params), dtype=PARAMS_DTYPE)
@@ -123,6 +125,48 @@ def oracle_sample(logits: np.ndarray, params, states: np.ndarray, history=None, 
                           _ptr(hl), states.ctypes.data, ids.ctypes.data, _ptr(cid), _ptr(cv),
                           _ptr(cp), cand_ld, infos.ctypes.data, 1 if full_z else 0, nthreads)
     return ids, infos, cid, cv, cp
+
+
+def oracle_generate(step_logits, params, states: np.ndarray, eos: int):
+    """cmd_generate's loop (src/main.cpp:626-632) for B independent sequences over
+    precomputed logits, one [B, n] array per step:
+        next = sample_token(logits, n, sp, gen, rng); if next == eos: stop;
+        gen.push_back(next)
+    with gen the row's whole generated history (prompt excluded).  states (uint64
+    [B]) are advanced in place.  Returns dict: tokens int32 [B, T] (-1 once stopped),
+    gen (list of lists), done bool [B], boundary float64 [B, T] (distance of the
+    draw to the nearest CDF boundary; inf for greedy and stopped rows)."""
+    T = len(step_logits)
+    B = step_logits[0].shape[0]
+    par = params_array(params)
+    per_row = len(par) > 1
+    gen = [[] for _ in range(B)]
+    done = np.zeros(B, dtype=bool)
+    tokens = np.full((B, T), -1, dtype=np.int32)
+    boundary = np.full((B, T), np.inf)
+    for t in range(T):
+        run = np.flatnonzero(~done)
+        if run.size == 0:
+            break
+        L = max(1, max(len(gen[r]) for r in run))
+        h = np.zeros((run.size, L), dtype=np.int32)
+        hl = np.zeros(run.size, dtype=np.int32)
+        for j, r in enumerate(run):
+            h[j, :len(gen[r])] = gen[r]
+            hl[j] = len(gen[r])
+        st = np.ascontiguousarray(states[run])
+        ids, info, _, _, _ = oracle_sample(step_logits[t][run], par[run] if per_row else par, st,
+                                           h, hl)
+        states[run] = st
+        for j, r in enumerate(run):
+            tokens[r, t] = ids[j]
+            if info["k"][j] > 0:
+                boundary[r, t] = info["boundary"][j]
+            if ids[j] == eos:
+                done[r] = True
+            else:
+                gen[r].append(int(ids[j]))
+    return {"tokens": tokens, "gen": gen, "done": done, "boundary": boundary}
 
 
 def oracle_logits_stats(logits: np.ndarray, topn: int):

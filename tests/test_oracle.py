@@ -229,3 +229,55 @@ def test_logits_stats_restatement(topn):
     np.testing.assert_array_equal(o["top_ids"][:3], r["top_ids"][:3])
     np.testing.assert_allclose(o["top_p"], r["top_p"], rtol=1e-13, equal_nan=True)
     assert o["max"][3] == -1e30 and o["min"][3] == -np.inf
+
+
+def _generate_case(rows=24, n=3000, T=20, eos=7):
+    rng = np.random.default_rng(23)
+    steps = []
+    for t in range(T):
+        x = rng.normal(0, 1.5, size=(rows, n)).astype(np.float32)
+        x[:, 100:105] += 4.0  # a few ids dominate, so the penalty window matters
+        steps.append(x)
+    for r, t in ((1, 3), (5, 0), (9, 11), (13, 19), (20, 6)):
+        steps[t][r, eos] = 60.0  # these rows draw eos at that step (p ~ 1)
+    plist = []
+    for r in range(rows):
+        if r % 6 == 0:
+            plist.append(SamplingParams(temp=0.0, repeat_penalty=1.5, repeat_last_n=4))
+        elif r % 6 == 1:
+            plist.append(SamplingParams(temp=0.9, top_k=0, top_p=1.0))
+        else:
+            plist.append(SamplingParams(temp=0.8, top_k=40, top_p=0.9, repeat_penalty=1.3,
+                                        repeat_last_n=6))
+    seeds = np.arange(rows, dtype=np.uint64) + np.uint64(1000)
+    return steps, plist, seeds, eos
+
+
+@needs_ref
+def test_generate_loop_against_reference():
+    """The generate-loop restatement (history = generated ids, eos stops the row
+    without being appended, one draw per non-greedy step) against a loop over the
+    unchanged reference's sample_token carrying each row's Rng state."""
+    steps, plist, seeds, eos = _generate_case()
+    rows, T = steps[0].shape[0], len(steps)
+    st = np.array([rng_seed(int(s)) for s in seeds], dtype=np.uint64)
+    o = oracle.oracle_generate(steps, plist, st, eos)
+    for r in range(rows):
+        state, gen, toks = rng_seed(int(seeds[r])), [], []
+        for t in range(T):
+            hist = np.array([gen if gen else [0]], dtype=np.int32)
+            ids, _ = oracle.reference_sample(steps[t][r:r + 1], plist[r], np.array([state], np.uint64),
+                                             hist, np.array([len(gen)], np.int32))
+            if plist[r].temp > 0:
+                g = Rng(state)
+                g.next()
+                state = g.state
+            toks.append(int(ids[0]))
+            if ids[0] == eos:
+                break
+            gen.append(int(ids[0]))
+        assert o["tokens"][r, :len(toks)].tolist() == toks, r
+        assert (o["tokens"][r, len(toks):] == -1).all()
+        assert o["gen"][r] == gen
+        assert int(st[r]) == state
+    assert all(o["done"][r] for r in (1, 5, 9, 13, 20))  # the planted eos rows

@@ -18,7 +18,7 @@ EXPORTS = (
     "zs_rng_seed", "zs_sample", "zs_argmax", "zs_check_device_status",
     "zs_shard_partial_bytes", "zs_shard_partials", "zs_shard_merge", "zs_sample_sharded",
     "zs_sample_noalloc", "zs_set_timing", "zs_get_timing", "zs_logits_stats",
-    "zs_selftest_wait_timeout",
+    "zs_selftest_wait_timeout", "zs_decode_step",
 )
 
 ZS_OK = 0
@@ -83,6 +83,8 @@ def lib() -> C.CDLL:
     L.zs_sample_sharded.argtypes = [vp, vp, i64, i32, i32, i32, i32, i32, C.POINTER(ZsParams), i32,
                                     vp, i64, vp, vp, vp, C.POINTER(ZsExtras), vp, vp]
     L.zs_selftest_wait_timeout.argtypes = [vp, vp]
+    L.zs_decode_step.argtypes = [vp, vp, i64, i32, i32, C.POINTER(ZsParams), i32, vp, i64, vp, vp,
+                                 vp, i32, vp, vp, i64, i64, vp]
     L.zs_logits_stats.argtypes = [vp, vp, i64, i32, i32, i32, vp, vp, vp, vp, vp, vp]
     L.zs_set_timing.argtypes = [vp, i32]
     L.zs_get_timing.argtypes = [vp, C.POINTER(ZsTiming)]
@@ -95,7 +97,8 @@ def lib() -> C.CDLL:
                                             "zs_shard_partials", "zs_shard_merge",
                                             "zs_sample_sharded", "zs_sample_noalloc",
                                             "zs_set_timing", "zs_get_timing",
-                                            "zs_logits_stats", "zs_selftest_wait_timeout"):
+                                            "zs_logits_stats", "zs_selftest_wait_timeout",
+                                            "zs_decode_step"):
             f.restype = C.c_int
     _lib = L
     return L

@@ -2536,6 +2536,58 @@ __global__ void __launch_bounds__(C::kWarps * 32, 1) zs_wselect_kernel(const Arg
     }
 }
 
+// One step of zeninfer's generate loop after the sampler (src/main.cpp:626-632):
+// a row that was already stopped keeps its Rng state (the loop drew nothing for
+// it) and reports -1; a row that sampled `eos` stops without appending it; any
+// other row appends its id to its on-device history.  A full history keeps its
+// last `keep` entries (the penalty window, repeat_last_n) before the append, so
+// the window the next step reads is unchanged.  One thread per row.
+struct DecodeArgs {
+    int32_t B;
+    int32_t eos;
+    const uint64_t* rng_prev;  // [B] states before this step's draws
+    uint64_t* rng;             // [B]
+    int32_t* done;             // [B] 0 running, 1 stopped
+    int32_t* out_ids;          // [B]
+    int32_t* hist;             // [B][hist_ld] or null
+    int64_t hist_ld;
+    int32_t* hist_len;         // [B] or null
+    const Params* row_params;  // [B] or null (then `shared`)
+    Params shared;
+    int32_t* tokens;           // [B][tokens_ld] or null
+    int64_t tokens_ld;
+    int64_t step;
+};
+
+__global__ void zs_decode_append_kernel(const DecodeArgs a) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= a.B) return;
+    int32_t* tok = a.tokens ? a.tokens + (int64_t)r * a.tokens_ld + a.step : nullptr;
+    if (a.done[r]) {
+        a.rng[r] = a.rng_prev[r];
+        a.out_ids[r] = -1;
+        if (tok) *tok = -1;
+        return;
+    }
+    const int32_t id = a.out_ids[r];
+    if (tok) *tok = id;
+    if (id == a.eos) {
+        a.done[r] = 1;
+        return;
+    }
+    if (!a.hist) return;
+    int32_t* h = a.hist + (int64_t)r * a.hist_ld;
+    int64_t n = a.hist_len[r];
+    if (n >= a.hist_ld) {
+        const int32_t rln = a.row_params ? a.row_params[r].repeat_last_n : a.shared.repeat_last_n;
+        const int64_t keep = min((int64_t)max(rln, 0), a.hist_ld - 1);
+        for (int64_t i = 0; i < keep; ++i) h[i] = h[n - keep + i];
+        n = keep;
+    }
+    h[n] = id;
+    a.hist_len[r] = (int32_t)(n + 1);
+}
+
 // Failure-path check: one thread waits, with the same bounded wait as the select
 // kernels, on an mbarrier phase that nothing completes (no arrival is ever made),
 // so the wait runs out after kWaitLimitNs and the kernel reports

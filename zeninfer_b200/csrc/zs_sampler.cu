@@ -269,6 +269,9 @@ struct zs_context {
     size_t stats_ids_bytes = 0;
     uint8_t* stats_part = nullptr;
     size_t stats_part_bytes = 0;
+    // zs_decode_step: the Rng states before the step's draws
+    uint64_t* rng_prev = nullptr;
+    size_t rng_prev_bytes = 0;
 };
 
 namespace {
@@ -630,6 +633,7 @@ zs_status zs_destroy(zs_handle h) {
     cudaFree(h->stats_rng);
     cudaFree(h->stats_ids);
     cudaFree(h->stats_part);
+    cudaFree(h->rng_prev);
     for (auto& t : h->timed) {
         cudaEventDestroy(t.begin);
         cudaEventDestroy(t.end);
@@ -718,6 +722,60 @@ zs_status zs_sample(zs_handle h, const float* logits, int64_t ld, int32_t batch,
     }
     a.mode = 0;
     return launch_select(h, a, pl, want_lse, st);
+}
+
+zs_status zs_decode_step(zs_handle h, const float* logits, int64_t ld, int32_t batch,
+                         int32_t n_vocab, const zs_params* params, int32_t params_per_row,
+                         int32_t* history, int64_t history_ld, int32_t* history_len,
+                         uint64_t* rng_state, int32_t* done, int32_t eos_id, int32_t* out_ids,
+                         int32_t* tokens, int64_t tokens_ld, int64_t step, void* stream) {
+    zs_status s = validate_common(h, logits, ld, batch, n_vocab, params);
+    if (s != ZS_OK) return s;
+    if (batch == 0) return ZS_OK;
+    if (!done || !out_ids) return fail(ZS_ERR_INVALID_ARGUMENT, "done and out_ids are required");
+    if (!rng_state) return fail(ZS_ERR_INVALID_ARGUMENT, "rng_state is required");
+    if ((history == nullptr) != (history_len == nullptr))
+        return fail(ZS_ERR_INVALID_ARGUMENT, "history and history_len go together");
+    if (history) {
+        if (history_ld < 1) return fail(ZS_ERR_INVALID_ARGUMENT, "history_ld < 1");
+        const int32_t np = params_per_row ? batch : 1;
+        for (int32_t i = 0; i < np; ++i)  // a full history keeps the penalty window
+            if (params[i].repeat_penalty != 1.0f && params[i].repeat_last_n >= history_ld)
+                return fail(ZS_ERR_INVALID_ARGUMENT,
+                            "history_ld must exceed repeat_last_n of every penalised row");
+    }
+    if (tokens && (step < 0 || step >= tokens_ld))
+        return fail(ZS_ERR_INVALID_ARGUMENT, "step outside [0, tokens_ld)");
+    cudaStream_t st = (cudaStream_t)stream;
+    DeviceGuard g(h->device);
+    if (!g.ok) return fail(ZS_ERR_CUDA, "cudaSetDevice failed");
+    s = grow((void**)&h->rng_prev, &h->rng_prev_bytes, (size_t)batch * sizeof(uint64_t));
+    if (s != ZS_OK) return s;
+    ZS_CUDA(cudaMemcpyAsync(h->rng_prev, rng_state, (size_t)batch * sizeof(uint64_t),
+                            cudaMemcpyDeviceToDevice, st));
+    s = zs_sample(h, logits, ld, batch, n_vocab, params, params_per_row, history, history_ld,
+                  history_len, rng_state, out_ids, nullptr, stream);
+    if (s != ZS_OK) return s;
+    zs::DecodeArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.B = batch;
+    a.eos = eos_id;
+    a.rng_prev = h->rng_prev;
+    a.rng = rng_state;
+    a.done = done;
+    a.out_ids = out_ids;
+    a.hist = history;
+    a.hist_ld = history_ld;
+    a.hist_len = history_len;
+    a.row_params = params_per_row ? h->params : nullptr;  // uploaded by zs_sample
+    a.shared = to_dev(params[0]);
+    a.tokens = tokens;
+    a.tokens_ld = tokens_ld;
+    a.step = step;
+    zs::zs_decode_append_kernel<<<(batch + 127) / 128, 128, 0, st>>>(a);
+    ZS_CUDA(cudaGetLastError());
+    h->launches += 1;
+    return ZS_OK;
 }
 
 zs_status zs_argmax(zs_handle h, const float* logits, int64_t ld, int32_t batch, int32_t n_vocab,

@@ -186,6 +186,47 @@ class Sampler:
             info = info_buf.cpu().numpy().view(ROW_INFO_DTYPE).reshape(B)
         return SampleResult(out, info, cand_ids, cand_probs)
 
+    def decode_step(self, logits, params, rng_state, done, eos: int, history=None,
+                    history_len=None, out=None, tokens=None, step: int = 0, stream=None):
+        """One step of the generate loop (src/main.cpp:626-632) on the device: sample
+        every running row, stop rows that drew `eos` (not appended), append the
+        others' ids to `history` ([B, L] int32 CUDA, lengths `history_len`), keep
+        stopped rows' Rng states.  `done` is int32 CUDA [B]; `tokens` ([B, T] int32
+        CUDA, optional) receives the ids (-1 for stopped rows) at column `step`.
+        Returns the ids ([B] int32 CUDA)."""
+        import torch
+        if logits.dim() == 1:
+            logits = logits.unsqueeze(0)
+        if logits.dtype != torch.float32 or logits.device != self.device or logits.stride(1) != 1:
+            raise ValueError("logits must be float32, unit column stride, on the sampler's device")
+        B, V = logits.shape
+        par, per_row = _params_array(params, B)
+        if out is None:
+            out = torch.empty(B, dtype=torch.int32, device=self.device)
+        for t, name, dt in ((rng_state, "rng_state", torch.int64), (done, "done", torch.int32)):
+            if t.dtype != dt or not t.is_contiguous() or t.numel() != B:
+                raise ValueError(f"{name} must be a contiguous {dt} tensor of {B} entries")
+        hist_ptr = hist_len_ptr = None
+        hist_ld = 0
+        if history is not None:
+            if (history_len is None or history.dtype != torch.int32 or history_len.dtype != torch.int32
+                    or not history.is_contiguous() or history.dim() != 2):
+                raise ValueError("history ([B, L] int32, contiguous) needs history_len (int32)")
+            hist_ptr, hist_len_ptr, hist_ld = history.data_ptr(), history_len.data_ptr(), history.shape[1]
+        tok_ptr, tok_ld = None, 0
+        if tokens is not None:
+            if tokens.dtype != torch.int32 or tokens.dim() != 2 or tokens.stride(1) != 1:
+                raise ValueError("tokens must be [B, T] int32 with unit column stride")
+            tok_ptr, tok_ld = tokens.data_ptr(), tokens.stride(0)
+            if step >= tokens.shape[1]:
+                raise ValueError("step outside tokens")
+        _native.check(self._lib.zs_decode_step(self._h, logits.data_ptr(), logits.stride(0), B, V,
+                                               par, per_row, hist_ptr, hist_ld, hist_len_ptr,
+                                               rng_state.data_ptr(), done.data_ptr(), int(eos),
+                                               out.data_ptr(), tok_ptr, tok_ld, int(step),
+                                               _stream_ptr(stream)), "zs_decode_step")
+        return out
+
     def argmax(self, logits, out=None, stream=None):
         """argmax_token per row."""
         import torch
