@@ -39,7 +39,7 @@
 extern "C" {
 #endif
 
-#define ZS_ABI_VERSION 1
+#define ZS_ABI_VERSION 2
 
 typedef enum zs_status {
     ZS_OK = 0,
@@ -140,6 +140,36 @@ zs_status zs_decode_step(zs_handle h, const float* logits, int64_t ld, int32_t b
                          uint64_t* rng_state, int32_t* done, int32_t eos_id, int32_t* out_ids,
                          int32_t* tokens, int64_t tokens_ld, int64_t step, void* stream);
 
+/*
+ * The lm_head of Model::eval (src/model.cpp:401-403) fused with sample_token: for
+ * each of `batch` rows,
+ *   xn     = rmsnorm(hidden_r, norm_w, eps)      (src/model.cpp:31-38)
+ *   logits = matvec(xn, weight)                  (src/model.cpp:40-42, 403)
+ *   out_ids[r] = sample_token(logits, n_vocab, params, history_r, rng_r)
+ * on the tensor cores: xn is rounded to bfloat16 and `weight` is bfloat16
+ * [n_vocab][n_embd] (row-major, 16-byte aligned; the reference's output.weight
+ * after dequantisation, stored as bfloat16), products accumulate in f32.  The
+ * logits differ from the reference's f32 matvec by the bfloat16 rounding of xn and
+ * the accumulation order; the sampling on those logits is zs_sample's exactly.
+ *   hidden     device f32 [batch][hidden_ld], the last position's hidden state
+ *   norm_w     device f32 [n_embd], output_norm.weight
+ *   n_embd     a multiple of 8, >= 64
+ *   out_logits optional device f32 [batch][logits_ld] (logits_ld >= n_vocab, a
+ *              multiple of 4): the logits the sampling used
+ * Rows whose shortlist (top_k, or 256 when top_k is 0; 1 for greedy) is at most 64
+ * and that have no repeat penalty are selected inside the GEMM's epilogue and never
+ * leave the chip as logits; any other batch is written as logits (to out_logits or
+ * handle scratch) and sampled by zs_sample.  Other arguments as zs_sample.
+ * Replaces, for one step of cmd_generate, model.eval's last two lines and the
+ * sample_token call (src/main.cpp:628).
+ */
+zs_status zs_lmhead_sample(zs_handle h, const float* hidden, int64_t hidden_ld,
+                           const float* norm_w, float eps, const void* weight, int32_t batch,
+                           int32_t n_embd, int32_t n_vocab, const zs_params* params,
+                           int32_t params_per_row, const int32_t* history, int64_t history_ld,
+                           const int32_t* history_len, uint64_t* rng_state, int32_t* out_ids,
+                           float* out_logits, int64_t logits_ld, void* stream);
+
 /* Batched argmax_token (src/sample.cpp:24-30): first index of the maximum; a NaN at
  * index 0 yields 0.  No penalty, no draw. */
 zs_status zs_argmax(zs_handle h, const float* logits, int64_t ld, int32_t batch, int32_t n_vocab,
@@ -165,6 +195,8 @@ typedef struct zs_timing {
     double select_ms, merge_ms, large_ms;              /* summed event time per kernel */
     int64_t select_launches, merge_launches, large_launches;
     int64_t launches;
+    double lmhead_ms;                                  /* zs_lmhead_kernel */
+    int64_t lmhead_launches;
 } zs_timing;
 zs_status zs_set_timing(zs_handle h, int32_t enable);
 zs_status zs_get_timing(zs_handle h, zs_timing* out);

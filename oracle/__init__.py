@@ -69,6 +69,9 @@ def olib():
         L.zo_logits_stats.argtypes = [vp, C.c_int64, C.c_int, C.c_int, C.c_int, vp, vp, vp, vp,
                                       vp, C.c_int64]
         L.zo_logits_stats.restype = C.c_int
+        L.zo_lmhead_rows.argtypes = [vp, C.c_int64, C.c_int, C.c_int, vp, C.c_float, vp, C.c_int,
+                                     vp, vp, C.c_int64, C.c_int]
+        L.zo_lmhead_rows.restype = C.c_int
         _olib = L
     return _olib
 
@@ -87,6 +90,12 @@ def rlib():
         L.zref_argmax.restype = C.c_int32
         L.zref_rng_stream.argtypes = [C.c_uint64, C.c_int, vp, vp]
         L.zref_rng_stream.restype = None
+        L.zref_lmhead_rows.argtypes = [vp, C.c_int64, C.c_int, C.c_int, vp, C.c_float, vp, C.c_int,
+                                       vp, vp, C.c_int64, C.c_int, C.c_int]
+        L.zref_lmhead_rows.restype = C.c_int
+        L.zref_matvec_rows.argtypes = [vp, C.c_int, C.c_int, vp, C.c_int, vp, C.c_int64, C.c_int,
+                                       C.c_int]
+        L.zref_matvec_rows.restype = C.c_int
         _rlib = L
     return _rlib
 
@@ -167,6 +176,69 @@ def oracle_generate(step_logits, params, states: np.ndarray, eos: int):
             else:
                 gen[r].append(int(ids[j]))
     return {"tokens": tokens, "gen": gen, "done": done, "boundary": boundary}
+
+
+def oracle_lmhead(hidden: np.ndarray, norm_w: np.ndarray, eps: float, w_bf16: np.ndarray,
+                  nthreads: int | None = None):
+    """The lm_head (src/model.cpp:401-403) as the device computes it: rmsnorm, xn
+    rounded to bfloat16, then the reference's in-order double dot products over
+    the bfloat16 weights (w_bf16: uint16 [V, E] bit patterns), one float rounding.
+    Returns (xn_bf16 uint16 [B, E], logits float32 [B, V])."""
+    h = np.ascontiguousarray(hidden, dtype=np.float32)
+    B, E = h.shape
+    w = np.ascontiguousarray(w_bf16, dtype=np.uint16)
+    V = w.shape[0]
+    nw = np.ascontiguousarray(norm_w, dtype=np.float32)
+    xn = np.zeros((B, E), dtype=np.uint16)
+    logits = np.zeros((B, V), dtype=np.float32)
+    nthreads = nthreads or min(64, os.cpu_count() or 1)
+    olib().zo_lmhead_rows(h.ctypes.data, E, B, E, nw.ctypes.data, float(eps), w.ctypes.data, V,
+                          xn.ctypes.data, logits.ctypes.data, V, nthreads)
+    return xn, logits
+
+
+def reference_lmhead(hidden: np.ndarray, norm_w: np.ndarray, eps: float, w_f32: np.ndarray,
+                     impl: int = 0, nthreads: int | None = None):
+    """The unchanged reference: zen::rmsnorm then zen::matvec_f32_impl (impl 0
+    scalar, 1 AVX2) per row.  Returns (xn float32 [B, E], logits float32 [B, V])."""
+    h = np.ascontiguousarray(hidden, dtype=np.float32)
+    B, E = h.shape
+    w = np.ascontiguousarray(w_f32, dtype=np.float32)
+    V = w.shape[0]
+    nw = np.ascontiguousarray(norm_w, dtype=np.float32)
+    xn = np.zeros((B, E), dtype=np.float32)
+    logits = np.zeros((B, V), dtype=np.float32)
+    nthreads = nthreads or min(64, os.cpu_count() or 1)
+    rlib().zref_lmhead_rows(h.ctypes.data, E, B, E, nw.ctypes.data, float(eps), w.ctypes.data, V,
+                            xn.ctypes.data, logits.ctypes.data, V, impl, nthreads)
+    return xn, logits
+
+
+def reference_matvec(xn: np.ndarray, w_f32: np.ndarray, impl: int = 0,
+                     nthreads: int | None = None) -> np.ndarray:
+    """zen::matvec_f32_impl over caller-supplied rows xn [B, E]; float32 [B, V]."""
+    x = np.ascontiguousarray(xn, dtype=np.float32)
+    B, E = x.shape
+    w = np.ascontiguousarray(w_f32, dtype=np.float32)
+    V = w.shape[0]
+    out = np.zeros((B, V), dtype=np.float32)
+    nthreads = nthreads or min(64, os.cpu_count() or 1)
+    rlib().zref_matvec_rows(x.ctypes.data, B, E, w.ctypes.data, V, out.ctypes.data, V, impl,
+                            nthreads)
+    return out
+
+
+def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
+    return (np.asarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """Round to nearest even (NaN kept quiet)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    r = ((u + np.uint32(0x7fff) + ((u >> 16) & np.uint32(1))) >> 16).astype(np.uint16)
+    nan = (u & np.uint32(0x7fffffff)) > np.uint32(0x7f800000)
+    r[nan] = ((u[nan] >> 16) | np.uint32(0x40)).astype(np.uint16)
+    return r
 
 
 def oracle_logits_stats(logits: np.ndarray, topn: int):

@@ -11,6 +11,8 @@
 #include <thread>
 #include <vector>
 
+#include "kernels.h"
+#include "model.h"
 #include "sample.h"
 
 namespace {
@@ -62,6 +64,51 @@ int zref_sample_rows(const float* logits, int64_t ld, int B, int n, const RefPar
 }
 
 int32_t zref_argmax(const float* logits, int n) { return zen::argmax_token(logits, n); }
+
+// The lm_head of Model::eval (src/model.cpp:401-403) for B independent rows:
+// zen::rmsnorm of the row's hidden state with output_norm, then
+// zen::matvec_f32_impl over output_ ([V][E] f32, row-major) with the chosen
+// implementation (0 scalar, 1 AVX2), rows spread over `nthreads` host threads.
+//   out_xn   (nullable) [B][E] the normalised row
+//   logits   [B][lld]
+int zref_lmhead_rows(const float* hidden, int64_t hld, int B, int E, const float* norm_w,
+                     float eps, const float* w, int V, float* out_xn, float* logits, int64_t lld,
+                     int impl, int nthreads) {
+    if (nthreads < 1) nthreads = 1;
+    std::atomic<int> next{0};
+    auto work = [&]() {
+        std::vector<float> xn((size_t)E);
+        for (int r; (r = next.fetch_add(1)) < B;) {
+            zen::rmsnorm(xn.data(), hidden + (int64_t)r * hld, norm_w, E, eps);
+            if (out_xn)
+                for (int i = 0; i < E; ++i) out_xn[(int64_t)r * E + i] = xn[(size_t)i];
+            zen::matvec_f32_impl(logits + (int64_t)r * lld, xn.data(), w, V, E,
+                                 impl ? zen::Impl::Avx2 : zen::Impl::Scalar);
+        }
+    };
+    std::vector<std::thread> pool;
+    for (int t = 1; t < nthreads; ++t) pool.emplace_back(work);
+    work();
+    for (auto& t : pool) t.join();
+    return 0;
+}
+
+// zen::matvec_f32_impl alone over caller-supplied normalised rows xn [B][E].
+int zref_matvec_rows(const float* xn, int B, int E, const float* w, int V, float* logits,
+                     int64_t lld, int impl, int nthreads) {
+    if (nthreads < 1) nthreads = 1;
+    std::atomic<int> next{0};
+    auto work = [&]() {
+        for (int r; (r = next.fetch_add(1)) < B;)
+            zen::matvec_f32_impl(logits + (int64_t)r * lld, xn + (int64_t)r * E, w, V, E,
+                                 impl ? zen::Impl::Avx2 : zen::Impl::Scalar);
+    };
+    std::vector<std::thread> pool;
+    for (int t = 1; t < nthreads; ++t) pool.emplace_back(work);
+    work();
+    for (auto& t : pool) t.join();
+    return 0;
+}
 
 // First `count` outputs of zen::Rng(seed).next() and the first uniform().
 void zref_rng_stream(uint64_t seed, int count, uint64_t* out_next, double* out_uniform) {

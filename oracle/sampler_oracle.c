@@ -378,3 +378,93 @@ int zo_logits_stats(const float* logits, int64_t ld, int B, int n, int topn, dou
     free(keys);
     return 0;
 }
+
+/* ---- lm_head of Model::eval (src/model.cpp:401-403) as the B200 path computes it --
+ * rmsnorm (src/model.cpp:31-38): sum of x^2 in double, in order; scale =
+ * 1/sqrt(sum/n + eps); xn_i = (float)((double)x_i * scale * (double)w_i).  Every
+ * product is of two floats, so exact in double: contraction cannot change it.
+ * The device path rounds xn to bfloat16 (nearest even) for the tensor cores and
+ * takes the weights as bfloat16; the logits here are then the reference's
+ * dot_f32_scalar (src/kernels.cpp: double accumulation in order, one rounding
+ * to float at the end) over those bfloat16 values, which the tensor cores'
+ * f32 accumulation approximates. */
+static inline float bf16_to_f32(uint16_t b) {
+    uint32_t u = (uint32_t)b << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+static inline uint16_t f32_to_bf16_rne(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x0040u); /* NaN */
+    const uint32_t lsb = (u >> 16) & 1u;
+    return (uint16_t)((u + 0x7fffu + lsb) >> 16);
+}
+
+void zo_rmsnorm_bf16(const float* x, const float* w, int n, float eps, float* out_f32,
+                     uint16_t* out_bf16) {
+    double sum = 0.0;
+    for (int i = 0; i < n; ++i) sum += (double)x[i] * (double)x[i];
+    const double scale = 1.0 / sqrt(sum / (double)n + (double)eps);
+    for (int i = 0; i < n; ++i) {
+        const float v = (float)((double)x[i] * scale * (double)w[i]);
+        if (out_f32) out_f32[i] = v;
+        if (out_bf16) out_bf16[i] = f32_to_bf16_rne(v);
+    }
+}
+
+typedef struct {
+    const float* hidden;
+    int64_t hld;
+    int B, E, V;
+    const float* norm_w;
+    float eps;
+    const uint16_t* w;
+    uint16_t* out_xn;
+    float* logits;
+    int64_t lld;
+    int next;
+    pthread_mutex_t mu;
+} zo_lm_batch;
+
+static void* zo_lm_worker(void* arg) {
+    zo_lm_batch* b = (zo_lm_batch*)arg;
+    float* xf = (float*)malloc((size_t)b->E * sizeof(float));
+    uint16_t* xb = (uint16_t*)malloc((size_t)b->E * sizeof(uint16_t));
+    for (;;) {
+        pthread_mutex_lock(&b->mu);
+        const int r = b->next++;
+        pthread_mutex_unlock(&b->mu);
+        if (r >= b->B) break;
+        zo_rmsnorm_bf16(b->hidden + (int64_t)r * b->hld, b->norm_w, b->E, b->eps, xf, xb);
+        if (b->out_xn) memcpy(b->out_xn + (int64_t)r * b->E, xb, (size_t)b->E * 2);
+        for (int i = 0; i < b->E; ++i) xf[i] = bf16_to_f32(xb[i]);
+        for (int v = 0; v < b->V; ++v) {
+            const uint16_t* wr = b->w + (int64_t)v * b->E;
+            double acc = 0.0;
+            for (int i = 0; i < b->E; ++i) acc += (double)xf[i] * (double)bf16_to_f32(wr[i]);
+            b->logits[(int64_t)r * b->lld + v] = (float)acc;
+        }
+    }
+    free(xf);
+    free(xb);
+    return NULL;
+}
+
+/* hidden [B][hld] f32, norm_w [E], w [V][E] bfloat16 bits; out_xn (nullable)
+ * [B][E] bfloat16 bits; logits [B][lld]. */
+int zo_lmhead_rows(const float* hidden, int64_t hld, int B, int E, const float* norm_w, float eps,
+                   const uint16_t* w, int V, uint16_t* out_xn, float* logits, int64_t lld,
+                   int nthreads) {
+    zo_lm_batch b = {hidden, hld, B, E, V, norm_w, eps, w, out_xn, logits, lld, 0,
+                     PTHREAD_MUTEX_INITIALIZER};
+    if (nthreads < 1) nthreads = 1;
+    if (nthreads > 256) nthreads = 256;
+    pthread_t th[256];
+    for (int t = 1; t < nthreads; ++t) pthread_create(&th[t], NULL, zo_lm_worker, &b);
+    zo_lm_worker(&b);
+    for (int t = 1; t < nthreads; ++t) pthread_join(th[t], NULL);
+    return 0;
+}

@@ -1,0 +1,198 @@
+"""The lm_head fused with the sampler (zs_lmhead_sample) against the oracle.
+
+Model::eval ends with rmsnorm + matvec over output.weight (src/model.cpp:401-403)
+and cmd_generate samples the result (src/main.cpp:628).  The fused path computes
+the logits on the tensor cores (bf16 xn and weights, f32 accumulation) and selects
+the shortlist in the GEMM epilogue.  Parity, per case:
+  * logits (written by the same kernel) against the restatement on the same bf16
+    inputs within the recursive-summation bound  |d| <= (E + 2) 2^-24 sum|xn_i w_i|,
+    and against the unchanged reference's f32 lm_head within the bf16 rounding of
+    xn, |d| <= 2^-8 sum|xn_i w_i|;
+  * ids and Rng states bit-exact against zs_sample run on those logits, which is
+    itself checked against the restatement under the sampler's parity rules."""
+
+import numpy as np
+import pytest
+
+import oracle
+from tests.gpu_util import compare, run_gpu, run_oracle
+from zeninfer_b200 import SamplingParams, rng_seed, states_to_tensor, tensor_to_states
+
+pytestmark = pytest.mark.gpu
+
+EPS = 1e-6
+_MODELS = {}
+
+
+def _model(V, E, seed=7):
+    """bf16 output.weight [V, E] (as torch CPU tensor) and output_norm [E]."""
+    import torch
+    key = (V, E, seed)
+    if key not in _MODELS:
+        g = torch.Generator().manual_seed(seed)
+        w = (torch.randn(V, E, generator=g) * 0.05).to(torch.bfloat16)
+        nw = torch.rand(E, generator=g) + 0.5
+        _MODELS.clear()
+        _MODELS[key] = (w, nw)
+    return _MODELS[key]
+
+
+def _hidden(B, E, seed):
+    import torch
+    g = torch.Generator().manual_seed(1000 + seed)
+    h = torch.randn(B, E, generator=g) * 3.0
+    if B > 1:
+        h[1] *= 1e-3  # a small row: the eps term of rmsnorm matters
+    return h
+
+
+def _run(sampler, hidden, nw, w, params, seeds, with_logits=True, history=None, hlen=None):
+    import torch
+    dev = sampler.device
+    B, V = hidden.shape[0], w.shape[0]
+    st = states_to_tensor([rng_seed(int(s)) for s in seeds], dev)
+    lg = None
+    if with_logits:
+        lg = torch.full((B, (V + 3) // 4 * 4), float("nan"), dtype=torch.float32, device=dev)
+    h = hl = None
+    if history is not None:
+        h = torch.from_numpy(history).to(dev)
+        hl = torch.from_numpy(hlen).to(dev)
+    ids = sampler.lmhead_sample(hidden.to(dev), nw.to(dev), w.to(dev), params, st, eps=EPS,
+                                history=h, history_len=hl, out_logits=lg)
+    sampler.check_device_status()
+    out = {"ids": ids.cpu().numpy(), "states": tensor_to_states(st)}
+    if lg is not None:
+        out["logits"] = lg[:, :V].cpu().numpy()
+    return out
+
+
+def _w_bits(w):
+    import torch
+    return w.view(torch.int16).numpy().view(np.uint16)
+
+
+_WF = {}
+
+
+def _w_f32(w):
+    """float32 copy of the bf16 weights and its absolute values (cached)."""
+    if _WF.get("src") is not w:
+        _WF.clear()
+        wf = oracle.bf16_bits_to_f32(_w_bits(w))
+        _WF.update(src=w, wf=wf, absw=np.abs(wf))
+    return _WF["wf"], _WF["absw"]
+
+
+def _check_logits(got, hidden, nw, w, rows, against_reference=False):
+    h = hidden.numpy()[rows]
+    wb = _w_bits(w)
+    xn_b, lg = oracle.oracle_lmhead(h, nw.numpy(), EPS, wb)
+    wf, absw = _w_f32(w)
+    # sum |xn_i w_i| per logit; float32 is ample for a bound (scaled up by 1.01)
+    mag = (np.abs(oracle.bf16_bits_to_f32(xn_b)) @ absw.T).astype(np.float64) * 1.01
+    E = h.shape[1]
+    d = np.abs(got[rows].astype(np.float64) - lg.astype(np.float64))
+    assert np.all(d <= (E + 2) * 2.0 ** -24 * mag + 1e-30), float((d / (mag + 1e-30)).max())
+    if against_reference and oracle.have_reference():
+        _, ref = oracle.reference_lmhead(h, nw.numpy(), EPS, wf, impl=0)
+        d2 = np.abs(got[rows].astype(np.float64) - ref.astype(np.float64))
+        assert np.all(d2 <= 2.0 ** -8 * mag + 1e-30)
+
+
+def _check_sampling(sampler, res, params, seeds, history=None, hlen=None):
+    """ids/states bit-exact vs zs_sample on the kernel's own logits, and that
+    against the restatement."""
+    st0 = np.array([rng_seed(int(s)) for s in seeds], dtype=np.uint64)
+    g = run_gpu(sampler, res["logits"], params, st0, history, hlen)
+    assert np.array_equal(res["ids"], g["ids"])
+    assert np.array_equal(res["states"], g["states"])
+    o = run_oracle(res["logits"], params, st0, history, hlen)
+    compare(g, o)
+
+
+def _mixed_params(B):
+    out = []
+    for r in range(B):
+        out.append([SamplingParams(temp=0.0),
+                    SamplingParams(temp=0.7, top_k=40, top_p=0.9),
+                    SamplingParams(temp=1.0, top_k=1),
+                    SamplingParams(temp=0.8, top_k=64, top_p=0.95),
+                    SamplingParams(temp=1.3, top_k=7)][r % 5])
+    return out
+
+
+def test_lmhead_small_shapes(sampler):
+    """A vocabulary that is not a multiple of the 128-column tile, a hidden size of
+    two K stages, a batch smaller than one row tile, per-row params."""
+    V, E, B = 1000, 128, 5
+    w, nw = _model(V, E, seed=3)
+    hidden = _hidden(B, E, 3)
+    params = _mixed_params(B)
+    seeds = np.arange(B, dtype=np.uint64) + np.uint64(11)
+    res = _run(sampler, hidden, nw, w, params, seeds)
+    _check_logits(res["logits"], hidden, nw, w, np.arange(B), against_reference=True)
+    _check_sampling(sampler, res, params, seeds)
+
+
+def test_lmhead_full_vocab_batch(sampler):
+    """The Qwen2.5-0.5B lm_head shape (151,936 x 896) at 300 rows (warp merge),
+    temp 0.7, top-k 50, top-p 0.9; then the same rows without the logits output."""
+    V, E, B = 151936, 896, 300
+    w, nw = _model(V, E)
+    hidden = _hidden(B, E, 5)
+    p = SamplingParams(temp=0.7, top_k=50, top_p=0.9)
+    seeds = np.arange(B, dtype=np.uint64) * np.uint64(7) + np.uint64(1)
+    res = _run(sampler, hidden, nw, w, p, seeds)
+    _check_logits(res["logits"], hidden, nw, w, np.array([0, 1, 2, 150, 299]),
+                  against_reference=True)
+    _check_sampling(sampler, res, p, seeds)
+    res2 = _run(sampler, hidden, nw, w, p, seeds, with_logits=False)
+    assert np.array_equal(res2["ids"], res["ids"])
+    assert np.array_equal(res2["states"], res["states"])
+
+
+def test_lmhead_batch_one_and_mixed(sampler):
+    """Decode-sized batches: one row, and 37 rows with per-row params."""
+    V, E = 151936, 896
+    w, nw = _model(V, E)
+    for B, params in ((1, SamplingParams(temp=0.7, top_k=40)), (37, _mixed_params(37))):
+        hidden = _hidden(B, E, 9 + B)
+        seeds = np.arange(B, dtype=np.uint64) + np.uint64(5)
+        res = _run(sampler, hidden, nw, w, params, seeds)
+        _check_logits(res["logits"], hidden, nw, w, np.arange(min(B, 3)))
+        _check_sampling(sampler, res, params, seeds)
+
+
+def test_lmhead_two_pass_route(sampler):
+    """Rows the epilogue does not hold (a repeat penalty, top-k above 64, the
+    default 256-token shortlist) go through the written logits and zs_sample."""
+    V, E, B = 151936, 896, 24
+    w, nw = _model(V, E)
+    hidden = _hidden(B, E, 21)
+    params = []
+    for r in range(B):
+        params.append([SamplingParams(temp=0.7, top_k=40, top_p=0.9, repeat_penalty=1.3,
+                                      repeat_last_n=16),
+                       SamplingParams(temp=0.8, top_k=100),
+                       SamplingParams(temp=0.9)][r % 3])
+    rng = np.random.default_rng(4)
+    hist = rng.integers(0, V, size=(B, 32)).astype(np.int32)
+    hlen = rng.integers(0, 33, size=B).astype(np.int32)
+    seeds = np.arange(B, dtype=np.uint64) + np.uint64(101)
+    res = _run(sampler, hidden, nw, w, params, seeds, history=hist, hlen=hlen)
+    _check_logits(res["logits"], hidden, nw, w, np.arange(2))
+    _check_sampling(sampler, res, params, seeds, hist, hlen)
+    # without out_logits the logits live in handle scratch; same draws
+    res2 = _run(sampler, hidden, nw, w, params, seeds, with_logits=False, history=hist, hlen=hlen)
+    assert np.array_equal(res2["ids"], res["ids"])
+
+
+def test_lmhead_rejects_bad_shapes(sampler):
+    import torch
+    from zeninfer_b200._native import SamplerError
+    dev = sampler.device
+    w = torch.zeros((256, 60), dtype=torch.bfloat16, device=dev)
+    with pytest.raises(SamplerError):  # hidden size below one K stage
+        sampler.lmhead_sample(torch.zeros((1, 60), device=dev), torch.ones(60, device=dev), w,
+                              SamplingParams(), None)

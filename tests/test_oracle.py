@@ -281,3 +281,44 @@ def test_generate_loop_against_reference():
         assert o["gen"][r] == gen
         assert int(st[r]) == state
     assert all(o["done"][r] for r in (1, 5, 9, 13, 20))  # the planted eos rows
+
+
+def _lm_case(B=6, E=96, V=700, seed=3):
+    rng = np.random.default_rng(seed)
+    hidden = rng.normal(0, 3.0, size=(B, E)).astype(np.float32)
+    hidden[0, :] *= 1e-3  # a small row: the eps term matters
+    norm_w = rng.uniform(0.5, 1.5, size=E).astype(np.float32)
+    w = oracle.f32_to_bf16_bits(rng.normal(0, 0.05, size=(V, E)).astype(np.float32))
+    return hidden, norm_w, w
+
+
+@needs_ref
+def test_lmhead_restatement_against_reference():
+    """rmsnorm + matvec (src/model.cpp:401-403): the restatement's xn before the
+    bfloat16 rounding equals zen::rmsnorm's exactly (checked through the rounding
+    of the reference's xn), and on bfloat16-valued inputs its logits equal
+    zen::matvec_f32 with the scalar implementation exactly; the AVX2 one (float
+    accumulators) within its own rounding."""
+    hidden, norm_w, w = _lm_case()
+    eps = 1e-6
+    xn_b, lg = oracle.oracle_lmhead(hidden, norm_w, eps, w)
+    wf = oracle.bf16_bits_to_f32(w)
+    xn_ref, lg_ref_full = oracle.reference_lmhead(hidden, norm_w, eps, wf, impl=0)
+    assert np.array_equal(oracle.f32_to_bf16_bits(xn_ref), xn_b)
+    ref_on_bf16 = oracle.reference_matvec(oracle.bf16_bits_to_f32(xn_b), wf, impl=0)
+    assert np.array_equal(ref_on_bf16, lg)
+    avx = oracle.reference_matvec(oracle.bf16_bits_to_f32(xn_b), wf, impl=1)
+    mag = np.abs(oracle.bf16_bits_to_f32(xn_b)).astype(np.float64) @ np.abs(wf).astype(np.float64).T
+    assert np.all(np.abs(avx.astype(np.float64) - lg) <= 1e-6 * mag + 1e-30)
+    # the full-precision reference differs only by the rounding of xn to bfloat16
+    assert np.all(np.abs(lg_ref_full.astype(np.float64) - lg) <= 2.0 ** -8 * mag + 1e-30)
+
+
+def test_bf16_rounding_helpers():
+    x = np.array([1.0, 1.00390625, 1.005859375, -2.5, 3.0e38, np.inf, -0.0], dtype=np.float32)
+    b = oracle.f32_to_bf16_bits(x)
+    back = oracle.bf16_bits_to_f32(b)
+    assert back[0] == 1.0 and back[1] == 1.0  # halfway, ties to even
+    assert back[2] == np.float32(1.0078125)
+    assert back[3] == -2.5 and np.isinf(back[5]) and np.signbit(back[6])
+    assert np.isnan(oracle.bf16_bits_to_f32(oracle.f32_to_bf16_bits(np.array([np.nan], np.float32))))[0]

@@ -18,7 +18,7 @@ EXPORTS = (
     "zs_rng_seed", "zs_sample", "zs_argmax", "zs_check_device_status",
     "zs_shard_partial_bytes", "zs_shard_partials", "zs_shard_merge", "zs_sample_sharded",
     "zs_sample_noalloc", "zs_set_timing", "zs_get_timing", "zs_logits_stats",
-    "zs_selftest_wait_timeout", "zs_decode_step",
+    "zs_selftest_wait_timeout", "zs_decode_step", "zs_lmhead_sample",
 )
 
 ZS_OK = 0
@@ -43,7 +43,8 @@ class ZsExtras(C.Structure):
 class ZsTiming(C.Structure):
     _fields_ = [("select_ms", C.c_double), ("merge_ms", C.c_double), ("large_ms", C.c_double),
                 ("select_launches", C.c_int64), ("merge_launches", C.c_int64),
-                ("large_launches", C.c_int64), ("launches", C.c_int64)]
+                ("large_launches", C.c_int64), ("launches", C.c_int64),
+                ("lmhead_ms", C.c_double), ("lmhead_launches", C.c_int64)]
 
 
 class SamplerError(RuntimeError):
@@ -83,6 +84,8 @@ def lib() -> C.CDLL:
     L.zs_sample_sharded.argtypes = [vp, vp, i64, i32, i32, i32, i32, i32, C.POINTER(ZsParams), i32,
                                     vp, i64, vp, vp, vp, C.POINTER(ZsExtras), vp, vp]
     L.zs_selftest_wait_timeout.argtypes = [vp, vp]
+    L.zs_lmhead_sample.argtypes = [vp, vp, i64, vp, C.c_float, vp, i32, i32, i32,
+                                   C.POINTER(ZsParams), i32, vp, i64, vp, vp, vp, vp, i64, vp]
     L.zs_decode_step.argtypes = [vp, vp, i64, i32, i32, C.POINTER(ZsParams), i32, vp, i64, vp, vp,
                                  vp, i32, vp, vp, i64, i64, vp]
     L.zs_logits_stats.argtypes = [vp, vp, i64, i32, i32, i32, vp, vp, vp, vp, vp, vp]
@@ -98,7 +101,7 @@ def lib() -> C.CDLL:
                                             "zs_sample_sharded", "zs_sample_noalloc",
                                             "zs_set_timing", "zs_get_timing",
                                             "zs_logits_stats", "zs_selftest_wait_timeout",
-                                            "zs_decode_step"):
+                                            "zs_decode_step", "zs_lmhead_sample"):
             f.restype = C.c_int
     _lib = L
     return L

@@ -25,7 +25,7 @@ SAMPLER_SO = os.path.join(HERE, "libzs_sampler.so")
 WORKLOAD_SO = os.path.join(HERE, "libzs_workload.so")
 
 SAMPLER_SOURCES = ["zs_sampler.cu", "zs_noalloc_scratch.cu", "sample_shim.cpp"]
-SAMPLER_DEPS = SAMPLER_SOURCES + ["zs_kernels.cuh", "zs_device.cuh", "zs_stats.cuh"]
+SAMPLER_DEPS = SAMPLER_SOURCES + ["zs_kernels.cuh", "zs_device.cuh", "zs_stats.cuh", "zs_lmhead.cuh"]
 
 NVCC_ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = NVCC_ARCH + ["-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC",

@@ -227,6 +227,8 @@ struct MergeArgs {
     // warp-piece blocks (see Args) of the two warp configurations, at wl[c].off
     // inside each rank's area
     WLayout wl[2];
+    // every row's blocks are S slice blocks (zs_lmhead_kernel's output)
+    int32_t force_slices;
 };
 
 struct RowPlan {
@@ -1022,7 +1024,7 @@ struct BlockSet {
 
 __device__ __forceinline__ BlockSet row_blocks(const MergeArgs& a, int row, const RowPlan& rp) {
     BlockSet bs;
-    bs.warp = rp.wfast || rp.wbig;
+    bs.warp = !a.force_slices && (rp.wfast || rp.wbig);
     if (bs.warp) {
         bs.L = a.wl[rp.wfast ? WCfgS::kClass : WCfgL::kClass];
         const int64_t x0 = (int64_t)row * bs.L.Vn;

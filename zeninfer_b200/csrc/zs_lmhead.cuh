@@ -1,0 +1,443 @@
+// zs_lmhead.cuh -- the lm_head of Model::eval (src/model.cpp:401-403) on the
+// tensor cores, with the sampler's shortlist selection as the GEMM epilogue.
+//
+//   xn     = rmsnorm(hidden, output_norm)          zs_lm_rmsnorm_kernel, bf16 out
+//   logits = xn . W^T   (W = output.weight [V][E])  zs_lmhead_kernel
+//
+// zs_lmhead_kernel is a persistent tcgen05 GEMM: D[128 rows][128 vocab] tiles
+// accumulate in tensor memory (two accumulators, so the epilogue of one tile
+// overlaps the MMAs of the next), operands arrive by TMA (2-D tiles, 128-byte
+// swizzle, no multicast) through a 4-stage shared-memory ring.  Work units are
+// (row tile, vocabulary slice); a CTA walks its units' tiles in column order.
+// Warp 0 issues the copies, one thread of warp 1 issues the MMAs, warps 2-5 are
+// the epilogue: thread = row (its TMEM lane).  The epilogue keeps, per row, the
+// top keff keys (value desc, id asc; the sampler's key order) of the unit's
+// columns in a shared-memory buffer: a column enters when its key beats the
+// buffer's current threshold, and a full buffer is cut back to keff keys by the
+// warp together (warp_topk_keep).  At the end of a unit each row writes its keys
+// as one partial block, (row, slice), in the layout zs_merge_kernel and
+// zs_warp_merge_kernel read, so the merge, f64 softmax, nucleus and draw are the
+// sampler's own.  Optionally the epilogue also writes the f32 logits.
+//
+// Every wait is bounded (kWaitLimitNs); a wait that runs out sets the handle's
+// status to ZS_ERR_DEVICE_TIMEOUT and the kernel unwinds: the copy issuer waits
+// for its copies in flight, the MMA issuer for its MMAs, then TMEM is freed.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "zs_device.cuh"
+#include "zs_kernels.cuh"
+
+namespace zs {
+
+constexpr int kLmM = 128;       // batch rows per tile: the TMEM lanes
+constexpr int kLmN = 128;       // vocabulary columns per tile
+constexpr int kLmBK = 64;       // K per stage: one 128-byte swizzle row of bf16
+constexpr int kLmStages = 4;
+constexpr int kLmCap = 96;      // candidate keys held per row
+constexpr int kLmKeffMax = kLmCap - 32;  // room for one more 32-column chunk
+constexpr int kLmRowStride = kLmCap + 1; // odd, so rows spread over the banks
+constexpr int kLmThreads = 192; // warp 0 copies, warp 1 MMAs, warps 2-5 epilogue
+constexpr int kLmTmemCols = 2 * kLmN;
+constexpr uint32_t kLmTileABytes = kLmM * kLmBK * 2;
+constexpr uint32_t kLmTileBBytes = kLmN * kLmBK * 2;
+constexpr int64_t kLmPartStride = kPartialHeaderBytes + 8 * kLmKeffMax;
+static_assert(kLmPartStride % 16 == 0, "block headers are read as uint4");
+static_assert(kLmCap % 32 == 0 && kLmCap / 32 <= 64, "warp_topk_keep holds kLmCap keys");
+
+struct LmSmem {  // placed at a 1024-byte boundary: the swizzled tiles need it
+    uint8_t a[kLmStages][kLmTileABytes];
+    uint8_t b[kLmStages][kLmTileBBytes];
+    uint64_t cand[kLmM * kLmRowStride];
+    uint64_t full[kLmStages];
+    uint64_t empty[kLmStages];
+    uint64_t acc_full[2];
+    uint64_t acc_empty[2];
+    uint64_t drain;
+    uint32_t tmem_base;
+    int abort;
+};
+constexpr size_t kLmSmemBytes = sizeof(LmSmem) + 1024;
+
+struct LmArgs {
+    int32_t B, E, V, V_total;
+    int32_t mt, nt, S, n_units;  // row tiles, column tiles, slices per row, units
+    int32_t select;              // 1: partial blocks per (row, slice); 0: logits only
+    Params shared;
+    const Params* row_params;
+    uint8_t* part;               // [B][S] blocks of kLmPartStride bytes
+    float* out_logits;           // optional [B][logits_ld]
+    int64_t logits_ld;
+    int* status;
+};
+
+// ---- PTX wrappers: TMA tiles and the 5th-generation tensor cores ----
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x,
+                                            int32_t y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tc_alloc(uint32_t* dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_addr(dst)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tc_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// Arrives once on `bar` when every tcgen05 operation this thread issued before
+// has completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_addr(bar))
+                 : "memory");
+}
+// D[tmem] (+)= A[smem] . B[smem]^T, bf16 inputs, f32 accumulators.
+__device__ __forceinline__ void tc_mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// 32 consecutive f32 columns of this thread's TMEM lane; the wait is in the same
+// asm so no use of the registers can be scheduled before the data has arrived.
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+        "%28, %29, %30, %31}, [%32];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+          "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+// Shared-memory matrix descriptor of a K-major tile written by TMA with 128-byte
+// swizzle: rows of 128 bytes, 8-row groups 1024 bytes apart (stride byte offset),
+// leading byte offset unused for this layout (1), descriptor version 1, layout
+// type 2 (128-byte swizzle).  The tile starts at a 1024-byte boundary, so the
+// base offset is 0; a K step of 16 elements (32 bytes) adds 2 to the start field.
+__device__ __forceinline__ uint64_t sw128_desc(const void* tile) {
+    const uint32_t a = smem_addr(tile);
+    return (uint64_t)((a & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A and B bf16 (bits 7-9,
+// 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 at bit 17, M >> 4 at bit 24.
+constexpr uint32_t kLmIdesc = (1u << 4) | (1u << 7) | (1u << 10) |
+                              ((uint32_t)(kLmN >> 3) << 17) | ((uint32_t)(kLmM >> 4) << 24);
+
+// Bounded wait that also gives up when another role has aborted.
+__device__ __forceinline__ bool lm_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 15u) == 0u) {
+            if (*abort) return false;
+            if (global_ns() - t0 > kWaitLimitNs) {
+                *abort = 1;
+                return false;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void lm_unit(const LmArgs& a, int u, int& m, int& s, int& t0, int& t1) {
+    m = u / a.S;
+    s = u - m * a.S;
+    t0 = (int)(((int64_t)s * a.nt) / a.S);
+    t1 = (int)(((int64_t)(s + 1) * a.nt) / a.S);
+}
+
+// ---- rmsnorm (src/model.cpp:31-38), one thread per row, rounded to bf16 ----
+// The sum runs in order in double like the reference; every term is a product of
+// two floats and so exact in double, and 1/sqrt and the division are correctly
+// rounded, so xn equals the reference's float before the bf16 rounding.
+__global__ void zs_lm_rmsnorm_kernel(const float* hidden, int64_t hld, const float* norm_w,
+                                     float eps, int32_t B, int32_t E, __nv_bfloat16* xn) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= B) return;
+    const float* x = hidden + (int64_t)r * hld;
+    double sum = 0.0;
+    for (int i = 0; i < E; ++i) {
+        const double v = (double)x[i];
+        sum = __dadd_rn(sum, __dmul_rn(v, v));
+    }
+    const double scale = 1.0 / sqrt(sum / (double)E + (double)eps);
+    __nv_bfloat16* o = xn + (int64_t)r * E;
+    for (int i = 0; i < E; ++i) {
+        const float v = __double2float_rn(__dmul_rn(__dmul_rn((double)x[i], scale), (double)norm_w[i]));
+        o[i] = __float2bfloat16_rn(v);
+    }
+}
+
+// Cuts row L's buffer (of this warp's 32 rows) back to its top kk keys.
+__device__ __forceinline__ void lm_compact_row(uint64_t* rows, int L, uint32_t& count,
+                                               uint64_t& tau, uint32_t& tau_ord, uint32_t keff,
+                                               int lane) {
+    const uint32_t n = __shfl_sync(kFull, count, L);
+    const uint32_t kk = __shfl_sync(kFull, keff, L);
+    uint64_t* buf = rows + (int64_t)L * kLmRowStride;
+    const uint64_t T = warp_topk_keep<kLmCap / 32>(buf, n, kk, lane);
+    if (lane == L) {
+        count = kk;
+        tau = T;
+        tau_ord = (uint32_t)(T >> 32);
+    }
+}
+
+__global__ void __launch_bounds__(kLmThreads, 1)
+    zs_lmhead_kernel(const __grid_constant__ CUtensorMap tm_a,
+                     const __grid_constant__ CUtensorMap tm_b, const LmArgs a) {
+    extern __shared__ uint8_t lm_raw[];
+    const uint32_t pad = (1024u - (smem_addr(lm_raw) & 1023u)) & 1023u;
+    LmSmem& sm = *reinterpret_cast<LmSmem*>(lm_raw + pad);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nk = (a.E + kLmBK - 1) / kLmBK;
+    volatile int* abort = &sm.abort;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kLmStages; ++s) {
+            mbar_init(&sm.full[s], 1);
+            mbar_init(&sm.empty[s], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&sm.acc_full[i], 1);
+            mbar_init(&sm.acc_empty[i], 4 * 32);
+        }
+        mbar_init(&sm.drain, 1);
+        sm.abort = 0;
+        mbar_fence_init();
+        tma_prefetch_map(&tm_a);
+        tma_prefetch_map(&tm_b);
+    }
+    if (warp == 1) {
+        tc_alloc(&sm.tmem_base, kLmTmemCols);
+        tc_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = sm.tmem_base;
+
+    if (warp == 0) {
+        // ---- copy issuer ----
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0;
+            int64_t issued = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; ok && u < a.n_units; u += gridDim.x) {
+                int m, s, t0, t1;
+                lm_unit(a, u, m, s, t0, t1);
+                for (int t = t0; ok && t < t1; ++t) {
+                    for (int kb = 0; kb < nk; ++kb) {
+                        if (!lm_wait(&sm.empty[stage], phase ^ 1u, abort)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(&sm.full[stage], kLmTileABytes + kLmTileBBytes);
+                        tma_load_2d(sm.a[stage], &tm_a, kb * kLmBK, m * kLmM, &sm.full[stage]);
+                        tma_load_2d(sm.b[stage], &tm_b, kb * kLmBK, t * kLmN, &sm.full[stage]);
+                        ++issued;
+                        if (++stage == kLmStages) {
+                            stage = 0;
+                            phase ^= 1u;
+                        }
+                    }
+                }
+            }
+            if (!ok) set_status(a.status, kStatusTimeout);
+            // Every copy issued has landed before the CTA may exit (the MMA issuer
+            // has waited for all of them already unless a wait ran out).
+            for (int64_t i = issued - kLmStages; i < issued; ++i)
+                if (i >= 0) mbar_wait_bounded(&sm.full[i % kLmStages], (uint32_t)((i / kLmStages) & 1));
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---- MMA issuer ----
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; ok && u < a.n_units; u += gridDim.x) {
+                int m, s, t0, t1;
+                lm_unit(a, u, m, s, t0, t1);
+                for (int t = t0; ok && t < t1; ++t) {
+                    if (!lm_wait(&sm.acc_empty[acc], acc_phase ^ 1u, abort)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d = tmem + acc * (uint32_t)kLmN;
+                    for (int kb = 0; kb < nk; ++kb) {
+                        if (!lm_wait(&sm.full[stage], phase, abort)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint64_t ad = sw128_desc(sm.a[stage]);
+                        const uint64_t bd = sw128_desc(sm.b[stage]);
+#pragma unroll
+                        for (int k = 0; k < kLmBK / 16; ++k)
+                            tc_mma_bf16(d, ad + 2ull * k, bd + 2ull * k, kLmIdesc,
+                                        (kb | k) != 0 ? 1u : 0u);
+                        tc_commit(&sm.empty[stage]);
+                        if (++stage == kLmStages) {
+                            stage = 0;
+                            phase ^= 1u;
+                        }
+                    }
+                    if (!ok) break;
+                    tc_commit(&sm.acc_full[acc]);
+                    if (++acc == 2) {
+                        acc = 0;
+                        acc_phase ^= 1u;
+                    }
+                }
+            }
+            if (!ok) set_status(a.status, kStatusTimeout);
+            // Every MMA issued has completed before the tensor memory is freed.
+            tc_commit(&sm.drain);
+            mbar_wait_bounded(&sm.drain, 0u);
+        }
+        __syncwarp();
+    } else {
+        // ---- epilogue: thread = row of the tile (its TMEM lane) ----
+        const int q = warp & 3;  // the lane quarter this warp may access
+        const int r_in = q * 32 + lane;
+        uint64_t* rows = sm.cand + (int64_t)(q * 32) * kLmRowStride;
+        uint64_t* mine = rows + (int64_t)lane * kLmRowStride;
+        const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
+        uint32_t acc = 0, acc_phase = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; ok && u < a.n_units; u += gridDim.x) {
+            int m, s, t0, t1;
+            lm_unit(a, u, m, s, t0, t1);
+            const int row = m * kLmM + r_in;
+            const bool valid = row < a.B;
+            uint32_t keff = 1;
+            if (valid) {
+                const RowPlan rp = plan_row(load_params(a.row_params, a.shared, row), a.V_total,
+                                            nullptr, nullptr, 0, row);
+                keff = (uint32_t)rp.ksel;
+            }
+            uint32_t count = 0, tau_ord = 0;
+            uint64_t tau = 0ull;
+            bool x0nan = false;
+            float* lrow = (a.out_logits && valid) ? a.out_logits + (int64_t)row * a.logits_ld : nullptr;
+            for (int t = t0; t < t1; ++t) {
+                const bool got = lm_wait(&sm.acc_full[acc], acc_phase, abort);
+                if (!__all_sync(kFull, got)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll 1
+                for (int c = 0; c < kLmN / 32; ++c) {
+                    float v[32];
+                    __syncwarp();
+                    tc_ld32(lane_addr + acc * (uint32_t)kLmN + (uint32_t)(c * 32), v);
+                    const int col0 = t * kLmN + c * 32;
+                    if (lrow) {
+                        if (col0 + 32 <= a.V) {
+#pragma unroll
+                            for (int j = 0; j < 32; j += 4)
+                                *reinterpret_cast<float4*>(lrow + col0 + j) =
+                                    make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j)
+                                if (col0 + j < a.V) lrow[col0 + j] = v[j];
+                        }
+                    }
+                    if (a.select) {
+                        unsigned need = __ballot_sync(kFull, count > (uint32_t)(kLmCap - 32));
+                        while (need) {
+                            const int L = __ffs(need) - 1;
+                            need &= need - 1;
+                            lm_compact_row(rows, L, count, tau, tau_ord, keff, lane);
+                        }
+                        if (valid) {
+                            if (col0 == 0) x0nan = (v[0] != v[0]);
+                            // Columns arrive in id order, so a key whose value ties the
+                            // threshold's has a larger id and ranks below it: only a
+                            // greater value order can pass once a threshold is set.
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) {
+                                const uint32_t o = ord_of(v[j]);
+                                if ((o > tau_ord || tau == 0ull) && col0 + j < a.V)
+                                    mine[count++] = ((uint64_t)o << 32) | (uint64_t)(~(uint32_t)(col0 + j));
+                            }
+                        }
+                    }
+                }
+                tc_fence_before();
+                mbar_arrive(&sm.acc_empty[acc]);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            if (!ok) break;
+            if (a.select) {
+                unsigned over = __ballot_sync(kFull, count > keff);
+                while (over) {
+                    const int L = __ffs(over) - 1;
+                    over &= over - 1;
+                    lm_compact_row(rows, L, count, tau, tau_ord, keff, lane);
+                }
+                if (valid) {
+                    uint8_t* blk = a.part + ((int64_t)row * a.S + s) * kLmPartStride;
+                    const uint32_t flags = (t0 == 0) ? (kPartHasId0 | (x0nan ? kPartX0Nan : 0u)) : 0u;
+                    *reinterpret_cast<uint4*>(blk) =
+                        make_uint4(count, flags, __float_as_uint(-INFINITY), 0u);
+                    uint64_t* keys = reinterpret_cast<uint64_t*>(blk + kPartialHeaderBytes);
+                    for (uint32_t i = 0; i < count; ++i) keys[i] = mine[i];
+                }
+            }
+        }
+        if (!ok) set_status(a.status, kStatusTimeout);
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tc_dealloc(tmem, kLmTmemCols);
+    }
+}
+
+}  // namespace zs

@@ -18,7 +18,10 @@
 #include <string>
 #include <vector>
 
+#include <cudaTypedefs.h>
+
 #include "zs_kernels.cuh"
+#include "zs_lmhead.cuh"
 #include "zs_sampler.h"
 #include "zs_stats.cuh"
 
@@ -255,7 +258,7 @@ struct zs_context {
     size_t fail_units_n = 0;
     // optional per-kernel timing (zs_set_timing): event pairs around each launch
     struct TimedLaunch {
-        int kind;  // 0 select, 1 merge, 2 large
+        int kind;  // 0 select, 1 merge, 2 large, 3 lm_head
         cudaEvent_t begin, end;
     };
     bool timing = false;
@@ -272,6 +275,13 @@ struct zs_context {
     // zs_decode_step: the Rng states before the step's draws
     uint64_t* rng_prev = nullptr;
     size_t rng_prev_bytes = 0;
+    // zs_lmhead_sample: normalised rows (bf16), logits of the two-pass route, the
+    // driver's tensor-map encoder
+    uint8_t* lm_xn = nullptr;
+    size_t lm_xn_bytes = 0;
+    uint8_t* lm_logits = nullptr;
+    size_t lm_logits_bytes = 0;
+    PFN_cuTensorMapEncodeTiled_v12000 encode_tiled = nullptr;
 };
 
 namespace {
@@ -604,6 +614,10 @@ zs_status zs_create(int device, zs_handle* out) {
         (e = cudaFuncSetAttribute(zs::zs_warp_merge_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->warp_merge_smem)) != cudaSuccess ||
         (e = cudaFuncSetAttribute(zs::zs_warp_merge_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->warp_merge_smem)) != cudaSuccess)
         return cleanup(cuda_fail(e, "cudaFuncSetAttribute"));
+    if ((size_t)prop.sharedMemPerBlockOptin >= zs::kLmSmemBytes &&
+        (e = cudaFuncSetAttribute(zs::zs_lmhead_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)zs::kLmSmemBytes)) != cudaSuccess)
+        return cleanup(cuda_fail(e, "cudaFuncSetAttribute zs_lmhead_kernel"));
     zs_status sw = setup_wselect<zs::WCfgS>(&h->wsel_smem[0], &h->wsel_warps[0], h->num_sms);
     if (sw == ZS_OK) sw = setup_wselect<zs::WCfgL>(&h->wsel_smem[1], &h->wsel_warps[1], h->num_sms);
     if (sw != ZS_OK) return cleanup(sw);
@@ -634,6 +648,8 @@ zs_status zs_destroy(zs_handle h) {
     cudaFree(h->stats_ids);
     cudaFree(h->stats_part);
     cudaFree(h->rng_prev);
+    cudaFree(h->lm_xn);
+    cudaFree(h->lm_logits);
     for (auto& t : h->timed) {
         cudaEventDestroy(t.begin);
         cudaEventDestroy(t.end);
@@ -653,8 +669,9 @@ zs_status zs_get_timing(zs_handle h, zs_timing* out) {
     if (!h || !out) return fail(ZS_ERR_INVALID_ARGUMENT, "null handle or out");
     DeviceGuard g(h->device);
     std::memset(out, 0, sizeof(*out));
-    double* dst[3] = {&out->select_ms, &out->merge_ms, &out->large_ms};
-    int64_t* cnt[3] = {&out->select_launches, &out->merge_launches, &out->large_launches};
+    double* dst[4] = {&out->select_ms, &out->merge_ms, &out->large_ms, &out->lmhead_ms};
+    int64_t* cnt[4] = {&out->select_launches, &out->merge_launches, &out->large_launches,
+                       &out->lmhead_launches};
     zs_status s = ZS_OK;
     for (auto& t : h->timed) {
         float ms = 0.0f;
@@ -776,6 +793,169 @@ zs_status zs_decode_step(zs_handle h, const float* logits, int64_t ld, int32_t b
     ZS_CUDA(cudaGetLastError());
     h->launches += 1;
     return ZS_OK;
+}
+
+namespace {
+
+// A 2-D bf16 tensor map over rows x cols (row-major, cols contiguous) with boxes
+// of 128 rows x 64 columns and 128-byte swizzle, as zs_lmhead_kernel reads them.
+zs_status lm_tensor_map(zs_context* h, CUtensorMap* map, const void* base, int64_t rows,
+                        int64_t cols) {
+    if (!h->encode_tiled) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000,
+                                                         cudaEnableDefault, &q);
+        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+            return fail(ZS_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+        h->encode_tiled = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)zs::kLmBK, (cuuint32_t)zs::kLmM};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = h->encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base),
+                                       dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                       CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(ZS_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+    return ZS_OK;
+}
+
+// Slices per row for mt row tiles x nt column tiles on `ctas` CTAs: the fewest
+// slices whose busiest CTA (whole units, round robin) has at most 2% more tiles
+// than the best split.
+int lm_slices(int mt, int nt, int ctas) {
+    auto span = [&](int S) {
+        const int64_t units = (int64_t)mt * S;
+        return ((units + ctas - 1) / ctas) * (int64_t)((nt + S - 1) / S);
+    };
+    const int smax = std::min(nt, 1024);
+    int64_t best = span(1);
+    for (int S = 2; S <= smax; ++S) best = std::min(best, span(S));
+    for (int S = 1; S <= smax; ++S)
+        if (span(S) * 100 <= best * 102) return S;
+    return 1;
+}
+
+}  // namespace
+
+zs_status zs_lmhead_sample(zs_handle h, const float* hidden, int64_t hidden_ld,
+                           const float* norm_w, float eps, const void* weight, int32_t batch,
+                           int32_t n_embd, int32_t n_vocab, const zs_params* params,
+                           int32_t params_per_row, const int32_t* history, int64_t history_ld,
+                           const int32_t* history_len, uint64_t* rng_state, int32_t* out_ids,
+                           float* out_logits, int64_t logits_ld, void* stream) {
+    if (!h) return fail(ZS_ERR_INVALID_ARGUMENT, "null handle");
+    if (!params) return fail(ZS_ERR_INVALID_ARGUMENT, "params is null");
+    if (batch < 0) return fail(ZS_ERR_INVALID_ARGUMENT, "batch < 0");
+    if (batch == 0) return ZS_OK;
+    if (!hidden || !norm_w || !weight || !out_ids)
+        return fail(ZS_ERR_INVALID_ARGUMENT, "hidden, norm_w, weight and out_ids are required");
+    if (n_vocab < 1) return fail(ZS_ERR_INVALID_ARGUMENT, "n_vocab < 1");
+    if (n_embd < zs::kLmBK || n_embd % 8 != 0)
+        return fail(ZS_ERR_INVALID_ARGUMENT, "n_embd must be a multiple of 8 and at least 64");
+    if (hidden_ld < n_embd) return fail(ZS_ERR_INVALID_ARGUMENT, "hidden_ld < n_embd");
+    if (((uintptr_t)weight & 15u) != 0) return fail(ZS_ERR_INVALID_ARGUMENT, "weight not 16-byte aligned");
+    if (((uintptr_t)hidden & 3u) != 0 || ((uintptr_t)norm_w & 3u) != 0)
+        return fail(ZS_ERR_INVALID_ARGUMENT, "hidden or norm_w not 4-byte aligned");
+    if (out_logits && (logits_ld < n_vocab || ((uintptr_t)out_logits & 15u) != 0 || logits_ld % 4 != 0))
+        return fail(ZS_ERR_INVALID_ARGUMENT,
+                    "out_logits needs logits_ld >= n_vocab, a multiple of 4, 16-byte alignment");
+    if (zs::kLmSmemBytes > 232448) return fail(ZS_ERR_NO_DEVICE, "lm_head tiles do not fit");
+    if (!rng_state && needs_rng(params, params_per_row, batch))
+        return fail(ZS_ERR_INVALID_ARGUMENT, "rng_state is null");
+    const bool have_hist = history && history_len;
+    cudaStream_t st = (cudaStream_t)stream;
+    DeviceGuard g(h->device);
+    if (!g.ok) return fail(ZS_ERR_CUDA, "cudaSetDevice failed");
+
+    // Route: the fused epilogue holds up to kLmKeffMax keys per row and no penalty
+    // window; otherwise the kernel writes the logits and zs_sample takes over.
+    const int np = params_per_row ? batch : 1;
+    int max_ksel = 1;
+    bool fused = true;
+    for (int i = 0; i < np; ++i) {
+        const zs_params& p = params[i];
+        int ks = 1;
+        if (!(p.temp <= 0.0f)) ks = p.top_k > 0 ? std::min(p.top_k, n_vocab) : std::min(zs::kShortlistDefault, n_vocab);
+        max_ksel = std::max(max_ksel, ks);
+        if (ks > zs::kLmKeffMax) fused = false;
+        if (have_hist && p.repeat_penalty != 1.0f && p.repeat_last_n > 0) fused = false;
+    }
+
+    zs_status s = grow((void**)&h->lm_xn, &h->lm_xn_bytes, (size_t)batch * n_embd * 2);
+    if (s != ZS_OK) return s;
+    float* logits = out_logits;
+    int64_t lld = logits_ld;
+    if (!fused && !logits) {
+        lld = ((int64_t)n_vocab + 3) & ~(int64_t)3;
+        s = grow((void**)&h->lm_logits, &h->lm_logits_bytes, (size_t)batch * lld * sizeof(float));
+        if (s != ZS_OK) return s;
+        logits = reinterpret_cast<float*>(h->lm_logits);
+    }
+    CUtensorMap tm_a, tm_b;
+    s = lm_tensor_map(h, &tm_a, h->lm_xn, batch, n_embd);
+    if (s == ZS_OK) s = lm_tensor_map(h, &tm_b, weight, n_vocab, n_embd);
+    if (s != ZS_OK) return s;
+
+    zs::LmArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.B = batch;
+    a.E = n_embd;
+    a.V = n_vocab;
+    a.V_total = n_vocab;
+    a.mt = (batch + zs::kLmM - 1) / zs::kLmM;
+    a.nt = (n_vocab + zs::kLmN - 1) / zs::kLmN;
+    a.S = lm_slices(a.mt, a.nt, h->num_sms);
+    a.n_units = a.mt * a.S;
+    a.select = fused ? 1 : 0;
+    a.shared = to_dev(params[0]);
+    const zs::Params* dparams = nullptr;
+    s = upload_params(h, params, params_per_row, batch, st, &dparams);
+    if (s != ZS_OK) return s;
+    a.row_params = dparams;
+    a.out_logits = logits;
+    a.logits_ld = lld;
+    a.status = h->status;
+    if (fused) {
+        s = grow((void**)&h->part, &h->part_bytes, (size_t)batch * a.S * zs::kLmPartStride);
+        if (s != ZS_OK) return s;
+        a.part = h->part;
+    }
+    {
+        LaunchScope scope(h, 1, st);  // counted with the merge-side helpers
+        zs::zs_lm_rmsnorm_kernel<<<(batch + 127) / 128, 128, 0, st>>>(
+            hidden, hidden_ld, norm_w, eps, batch, n_embd,
+            reinterpret_cast<__nv_bfloat16*>(h->lm_xn));
+        ZS_CUDA(cudaGetLastError());
+    }
+    {
+        LaunchScope scope(h, 3, st);
+        const int grid = std::min(a.n_units, h->num_sms);
+        zs::zs_lmhead_kernel<<<grid, zs::kLmThreads, zs::kLmSmemBytes, st>>>(tm_a, tm_b, a);
+        ZS_CUDA(cudaGetLastError());
+    }
+    if (!fused)
+        return zs_sample(h, logits, lld, batch, n_vocab, params, params_per_row, history,
+                         history_ld, history_len, rng_state, out_ids, nullptr, stream);
+    zs::MergeArgs m;
+    std::memset(&m, 0, sizeof(m));
+    m.gathered = h->part;
+    m.rank_stride = 0;
+    m.G = 1;
+    m.S = a.S;
+    m.part_stride = zs::kLmPartStride;
+    m.B = batch;
+    m.V_total = n_vocab;
+    m.shared = a.shared;
+    m.row_params = dparams;
+    m.rng = rng_state;
+    m.out_ids = out_ids;
+    m.status = h->status;
+    m.force_slices = 1;
+    return launch_merge(h, m, max_ksel, false, st);
 }
 
 zs_status zs_argmax(zs_handle h, const float* logits, int64_t ld, int32_t batch, int32_t n_vocab,

@@ -227,6 +227,47 @@ class Sampler:
                                                _stream_ptr(stream)), "zs_decode_step")
         return out
 
+    def lmhead_sample(self, hidden, norm_w, weight, params, rng_state=None, eps: float = 1e-6,
+                      history=None, history_len=None, out=None, out_logits=None, stream=None):
+        """The lm_head (rmsnorm with `norm_w`, then hidden . weight^T; src/model.cpp:
+        401-403) fused with sample_token for every row of `hidden` ([B, E] float32
+        CUDA).  weight: bfloat16 CUDA [V, E], contiguous.  out_logits (optional,
+        float32 CUDA [B, >= V], row stride a multiple of 4) receives the logits the
+        sampling used.  Returns the ids ([B] int32 CUDA)."""
+        import torch
+        if hidden.dim() == 1:
+            hidden = hidden.unsqueeze(0)
+        if hidden.dtype != torch.float32 or hidden.stride(1) != 1 or hidden.device != self.device:
+            raise ValueError("hidden must be float32 with unit column stride on the sampler's device")
+        if weight.dtype != torch.bfloat16 or not weight.is_contiguous() or weight.dim() != 2:
+            raise ValueError("weight must be a contiguous bfloat16 [V, E] tensor")
+        B, E = hidden.shape
+        V = weight.shape[0]
+        if weight.shape[1] != E or norm_w.numel() != E or norm_w.dtype != torch.float32:
+            raise ValueError("weight [V, E] and norm_w [E] float32 must match hidden's E")
+        par, per_row = _params_array(params, B)
+        if out is None:
+            out = torch.empty(B, dtype=torch.int32, device=self.device)
+        hist_ptr = hist_len_ptr = None
+        hist_ld = 0
+        if history is not None:
+            if history_len is None:
+                raise ValueError("history needs history_len")
+            history = history.to(torch.int32).contiguous()
+            history_len = history_len.to(torch.int32).contiguous()
+            hist_ptr, hist_len_ptr, hist_ld = history.data_ptr(), history_len.data_ptr(), history.shape[1]
+        lptr, lld = None, 0
+        if out_logits is not None:
+            if out_logits.dtype != torch.float32 or out_logits.stride(1) != 1:
+                raise ValueError("out_logits must be float32 with unit column stride")
+            lptr, lld = out_logits.data_ptr(), out_logits.stride(0)
+        rng_ptr = rng_state.data_ptr() if rng_state is not None else None
+        _native.check(self._lib.zs_lmhead_sample(
+            self._h, hidden.data_ptr(), hidden.stride(0), norm_w.contiguous().data_ptr(),
+            float(eps), weight.data_ptr(), B, E, V, par, per_row, hist_ptr, hist_ld, hist_len_ptr,
+            rng_ptr, out.data_ptr(), lptr, lld, _stream_ptr(stream)), "zs_lmhead_sample")
+        return out
+
     def argmax(self, logits, out=None, stream=None):
         """argmax_token per row."""
         import torch
