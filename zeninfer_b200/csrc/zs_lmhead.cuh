@@ -10,11 +10,14 @@
 // swizzle, no multicast) through a 4-stage shared-memory ring.  Work units are
 // (row tile, vocabulary slice); a CTA walks its units' tiles in column order.
 // Warp 0 issues the copies, one thread of warp 1 issues the MMAs, warps 2-5 are
-// the epilogue: thread = row (its TMEM lane).  The epilogue keeps, per row, the
-// top keff keys (value desc, id asc; the sampler's key order) of the unit's
-// columns in a shared-memory buffer: a column enters when its key beats the
-// buffer's current threshold, and a full buffer is cut back to keff keys by the
-// warp together (warp_topk_keep).  At the end of a unit each row writes its keys
+// the epilogue: thread = row (its TMEM lane).  The epilogue keeps, per row, a
+// buffer of candidate keys (value desc, id asc is the sampler's key order) above a
+// threshold: the keff-th best key of the row's unit so far, as of the buffer's last
+// compaction.  Columns come in id order, so a column passes exactly when its value
+// order beats the threshold's; a 32-column chunk whose maximum does not is skipped
+// whole.  When a row's passing columns would overflow its buffer, the warp cuts
+// that row back to its keff best keys together (warp_topk_keep), which raises the
+// threshold.  At the end of a unit each row writes its keys
 // as one partial block, (row, slice), in the layout zs_merge_kernel and
 // zs_warp_merge_kernel read, so the merge, f64 softmax, nucleus and draw are the
 // sampler's own.  Optionally the epilogue also writes the f32 logits.
@@ -37,8 +40,8 @@ constexpr int kLmM = 128;       // batch rows per tile: the TMEM lanes
 constexpr int kLmN = 128;       // vocabulary columns per tile
 constexpr int kLmBK = 64;       // K per stage: one 128-byte swizzle row of bf16
 constexpr int kLmStages = 4;
-constexpr int kLmCap = 96;      // candidate keys held per row
-constexpr int kLmKeffMax = kLmCap - 32;  // room for one more 32-column chunk
+constexpr int kLmCap = 96;      // candidate keys buffered per row
+constexpr int kLmKeffMax = kLmCap - 32;  // a compaction leaves room for a whole chunk
 constexpr int kLmRowStride = kLmCap + 1; // odd, so rows spread over the banks
 constexpr int kLmThreads = 192; // warp 0 copies, warp 1 MMAs, warps 2-5 epilogue
 constexpr int kLmTmemCols = 2 * kLmN;
@@ -46,12 +49,11 @@ constexpr uint32_t kLmTileABytes = kLmM * kLmBK * 2;
 constexpr uint32_t kLmTileBBytes = kLmN * kLmBK * 2;
 constexpr int64_t kLmPartStride = kPartialHeaderBytes + 8 * kLmKeffMax;
 static_assert(kLmPartStride % 16 == 0, "block headers are read as uint4");
-static_assert(kLmCap % 32 == 0 && kLmCap / 32 <= 64, "warp_topk_keep holds kLmCap keys");
 
 struct LmSmem {  // placed at a 1024-byte boundary: the swizzled tiles need it
     uint8_t a[kLmStages][kLmTileABytes];
     uint8_t b[kLmStages][kLmTileBBytes];
-    uint64_t cand[kLmM * kLmRowStride];
+    uint64_t cand[kLmM * kLmRowStride];  // per row: candidate keys, unordered
     uint64_t full[kLmStages];
     uint64_t empty[kLmStages];
     uint64_t acc_full[2];
@@ -205,18 +207,66 @@ __global__ void zs_lm_rmsnorm_kernel(const float* hidden, int64_t hld, const flo
     }
 }
 
-// Cuts row L's buffer (of this warp's 32 rows) back to its top kk keys.
+// Cuts row L's buffer (of this warp's 32 rows) back to its keff best keys; lane L
+// takes the new count and threshold.
 __device__ __forceinline__ void lm_compact_row(uint64_t* rows, int L, uint32_t& count,
-                                               uint64_t& tau, uint32_t& tau_ord, uint32_t keff,
-                                               int lane) {
+                                               uint32_t& tau_ord, float& tau_f, bool& open,
+                                               uint32_t keff, int lane) {
     const uint32_t n = __shfl_sync(kFull, count, L);
     const uint32_t kk = __shfl_sync(kFull, keff, L);
-    uint64_t* buf = rows + (int64_t)L * kLmRowStride;
-    const uint64_t T = warp_topk_keep<kLmCap / 32>(buf, n, kk, lane);
+    const uint64_t T = warp_topk_keep<(kLmCap + 31) / 32>(rows + (int64_t)L * kLmRowStride, n, kk, lane);
     if (lane == L) {
         count = kk;
-        tau = T;
         tau_ord = (uint32_t)(T >> 32);
+        tau_f = value_of_ord(tau_ord);
+        open = false;
+    }
+}
+
+// Bit j set when column col0 + j (< V) passes: every column while the buffer is
+// open (no threshold yet), else a value order above tau_ord.  With tau_f the
+// threshold's value that is v > tau_f (orders are monotone in the value, -0 and
+// +0 share one), or for a NaN threshold (order 0) any non-NaN value.
+__device__ __forceinline__ uint32_t lm_pass_mask(const float (&v)[32], int col0, int V,
+                                                 uint32_t tau_ord, float tau_f, bool open) {
+    const uint32_t inside = (col0 + 32 <= V) ? 0xffffffffu
+                                             : (col0 >= V ? 0u : ((1u << (V - col0)) - 1u));
+    if (open) return inside;
+    uint32_t pm = 0;
+    if (tau_ord != 0u) {
+        float mx = v[0];
+#pragma unroll
+        for (int j = 1; j < 32; ++j) mx = fmaxf(mx, v[j]);
+        if (!(mx > tau_f)) return 0u;  // fmaxf skips NaN; an all-NaN chunk gives NaN
+#pragma unroll
+        for (int j = 0; j < 32; ++j) pm |= (v[j] > tau_f ? 1u : 0u) << j;
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) pm |= (v[j] == v[j] ? 1u : 0u) << j;
+    }
+    return pm & inside;
+}
+
+// One 32-column chunk of a tile for this warp's 32 rows: rows whose passing
+// columns would overflow their buffers are compacted first (the whole warp, one row
+// at a time), then every row appends its passing keys.
+__device__ __forceinline__ void lm_chunk(const float (&v)[32], int col0, int V, bool sel,
+                                         uint64_t* rows, uint64_t* mine, uint32_t& count,
+                                         uint32_t& tau_ord, float& tau_f, bool& open,
+                                         uint32_t keff, int lane) {
+    uint32_t pm = sel ? lm_pass_mask(v, col0, V, tau_ord, tau_f, open) : 0u;
+    unsigned over = __ballot_sync(kFull, count + __popc(pm) > (uint32_t)kLmCap);
+    while (over) {
+        const int L = __ffs(over) - 1;
+        over &= over - 1;
+        lm_compact_row(rows, L, count, tau_ord, tau_f, open, keff, lane);
+        if (lane == L) pm = lm_pass_mask(v, col0, V, tau_ord, tau_f, open);
+    }
+    if (pm) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if ((pm >> j) & 1u)
+                mine[count++] = ((uint64_t)ord_of(v[j]) << 32) | (uint64_t)(~(uint32_t)(col0 + j));
     }
 }
 
@@ -354,9 +404,12 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                                             nullptr, nullptr, 0, row);
                 keff = (uint32_t)rp.ksel;
             }
-            uint32_t count = 0, tau_ord = 0;
-            uint64_t tau = 0ull;
+            uint32_t count = 0;    // keys in the buffer
+            uint32_t tau_ord = 0;  // threshold's value order (after the first compaction)
+            float tau_f = 0.0f;    // its value
+            bool open = true;      // no threshold yet: every column enters
             bool x0nan = false;
+            const bool sel = a.select && valid;
             float* lrow = (a.out_logits && valid) ? a.out_logits + (int64_t)row * a.logits_ld : nullptr;
             for (int t = t0; t < t1; ++t) {
                 const bool got = lm_wait(&sm.acc_full[acc], acc_phase, abort);
@@ -365,12 +418,14 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                     break;
                 }
                 tc_fence_after();
+                const int tcol = t * kLmN;
 #pragma unroll 1
                 for (int c = 0; c < kLmN / 32; ++c) {
                     float v[32];
                     __syncwarp();
                     tc_ld32(lane_addr + acc * (uint32_t)kLmN + (uint32_t)(c * 32), v);
-                    const int col0 = t * kLmN + c * 32;
+                    const int col0 = tcol + c * 32;
+                    if (col0 == 0) x0nan = (v[0] != v[0]);
                     if (lrow) {
                         if (col0 + 32 <= a.V) {
 #pragma unroll
@@ -383,26 +438,8 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                                 if (col0 + j < a.V) lrow[col0 + j] = v[j];
                         }
                     }
-                    if (a.select) {
-                        unsigned need = __ballot_sync(kFull, count > (uint32_t)(kLmCap - 32));
-                        while (need) {
-                            const int L = __ffs(need) - 1;
-                            need &= need - 1;
-                            lm_compact_row(rows, L, count, tau, tau_ord, keff, lane);
-                        }
-                        if (valid) {
-                            if (col0 == 0) x0nan = (v[0] != v[0]);
-                            // Columns arrive in id order, so a key whose value ties the
-                            // threshold's has a larger id and ranks below it: only a
-                            // greater value order can pass once a threshold is set.
-#pragma unroll
-                            for (int j = 0; j < 32; ++j) {
-                                const uint32_t o = ord_of(v[j]);
-                                if ((o > tau_ord || tau == 0ull) && col0 + j < a.V)
-                                    mine[count++] = ((uint64_t)o << 32) | (uint64_t)(~(uint32_t)(col0 + j));
-                            }
-                        }
-                    }
+                    if (a.select)
+                        lm_chunk(v, col0, a.V, sel, rows, mine, count, tau_ord, tau_f, open, keff, lane);
                 }
                 tc_fence_before();
                 mbar_arrive(&sm.acc_empty[acc]);
@@ -413,20 +450,19 @@ __global__ void __launch_bounds__(kLmThreads, 1)
             }
             if (!ok) break;
             if (a.select) {
-                unsigned over = __ballot_sync(kFull, count > keff);
+                unsigned over = __ballot_sync(kFull, sel && count > keff);
                 while (over) {
                     const int L = __ffs(over) - 1;
                     over &= over - 1;
-                    lm_compact_row(rows, L, count, tau, tau_ord, keff, lane);
+                    lm_compact_row(rows, L, count, tau_ord, tau_f, open, keff, lane);
                 }
-                if (valid) {
-                    uint8_t* blk = a.part + ((int64_t)row * a.S + s) * kLmPartStride;
-                    const uint32_t flags = (t0 == 0) ? (kPartHasId0 | (x0nan ? kPartX0Nan : 0u)) : 0u;
-                    *reinterpret_cast<uint4*>(blk) =
-                        make_uint4(count, flags, __float_as_uint(-INFINITY), 0u);
-                    uint64_t* keys = reinterpret_cast<uint64_t*>(blk + kPartialHeaderBytes);
-                    for (uint32_t i = 0; i < count; ++i) keys[i] = mine[i];
-                }
+            }
+            if (sel) {
+                uint8_t* blk = a.part + ((int64_t)row * a.S + s) * kLmPartStride;
+                const uint32_t flags = (t0 == 0) ? (kPartHasId0 | (x0nan ? kPartX0Nan : 0u)) : 0u;
+                *reinterpret_cast<uint4*>(blk) = make_uint4(count, flags, __float_as_uint(-INFINITY), 0u);
+                uint64_t* keys = reinterpret_cast<uint64_t*>(blk + kPartialHeaderBytes);
+                for (uint32_t i = 0; i < count; ++i) keys[i] = mine[i];
             }
         }
         if (!ok) set_status(a.status, kStatusTimeout);

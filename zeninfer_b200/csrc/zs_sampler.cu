@@ -824,14 +824,14 @@ zs_status lm_tensor_map(zs_context* h, CUtensorMap* map, const void* base, int64
 }
 
 // Slices per row for mt row tiles x nt column tiles on `ctas` CTAs: the fewest
-// slices whose busiest CTA (whole units, round robin) has at most 2% more tiles
-// than the best split.
-int lm_slices(int mt, int nt, int ctas) {
+// slices (at most `cap`) whose busiest CTA (whole units, round robin) has at most
+// 2% more tiles than the best split.
+int lm_slices(int mt, int nt, int ctas, int cap) {
     auto span = [&](int S) {
         const int64_t units = (int64_t)mt * S;
         return ((units + ctas - 1) / ctas) * (int64_t)((nt + S - 1) / S);
     };
-    const int smax = std::min(nt, 1024);
+    const int smax = std::max(1, std::min(std::min(nt, 1024), cap));
     int64_t best = span(1);
     for (int S = 2; S <= smax; ++S) best = std::min(best, span(S));
     for (int S = 1; S <= smax; ++S)
@@ -908,7 +908,9 @@ zs_status zs_lmhead_sample(zs_handle h, const float* hidden, int64_t hidden_ld,
     a.V_total = n_vocab;
     a.mt = (batch + zs::kLmM - 1) / zs::kLmM;
     a.nt = (n_vocab + zs::kLmN - 1) / zs::kLmN;
-    a.S = lm_slices(a.mt, a.nt, h->num_sms);
+    // a row's S blocks of up to max_ksel keys stay within the merge's one-pass gather
+    const int s_cap = fused ? std::min(zs::kNC, (zs::kCandCap - zs::kCandMargin) / max_ksel) : 1024;
+    a.S = lm_slices(a.mt, a.nt, h->num_sms, s_cap);
     a.n_units = a.mt * a.S;
     a.select = fused ? 1 : 0;
     a.shared = to_dev(params[0]);
