@@ -197,6 +197,8 @@ typedef struct zs_timing {
     int64_t launches;
     double lmhead_ms;                                  /* zs_lmhead_kernel */
     int64_t lmhead_launches;
+    double lmnorm_ms;                                  /* its rmsnorm prologue */
+    int64_t lmnorm_launches;
 } zs_timing;
 zs_status zs_set_timing(zs_handle h, int32_t enable);
 zs_status zs_get_timing(zs_handle h, zs_timing* out);

@@ -44,7 +44,8 @@ class ZsTiming(C.Structure):
     _fields_ = [("select_ms", C.c_double), ("merge_ms", C.c_double), ("large_ms", C.c_double),
                 ("select_launches", C.c_int64), ("merge_launches", C.c_int64),
                 ("large_launches", C.c_int64), ("launches", C.c_int64),
-                ("lmhead_ms", C.c_double), ("lmhead_launches", C.c_int64)]
+                ("lmhead_ms", C.c_double), ("lmhead_launches", C.c_int64),
+                ("lmnorm_ms", C.c_double), ("lmnorm_launches", C.c_int64)]
 
 
 class SamplerError(RuntimeError):

@@ -125,25 +125,20 @@ __device__ __forceinline__ void tc_mma_bf16(uint32_t d_tmem, uint64_t adesc, uin
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
-// 32 consecutive f32 columns of this thread's TMEM lane; the wait is in the same
-// asm so no use of the registers can be scheduled before the data has arrived.
-__device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
-    uint32_t r[32];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
-        "%28, %29, %30, %31}, [%32];\n\t"
-        "tcgen05.wait::ld.sync.aligned;"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
-          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
-          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
-          "=r"(r[31])
-        : "r"(taddr)
-        : "memory");
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+// 32 consecutive f32 columns of this thread's TMEM lane.  tc_ld_wait names the
+// destination registers as read and written, so no use of them can be scheduled
+// before the data has arrived.
+__device__ __forceinline__ void tc_ld32_issue(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+                 : "r"(taddr)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_ld_wait(uint32_t (&r)[32]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+                 :
+                 : "memory");
 }
 
 // Shared-memory matrix descriptor of a K-major tile written by TMA with 128-byte
@@ -178,6 +173,13 @@ __device__ __forceinline__ bool lm_wait(uint64_t* bar, uint32_t parity, volatile
     }
 }
 
+// Units [u_begin, u_end) of this CTA: a contiguous share, so consecutive units of
+// one row tile (adjacent slices) meet in one CTA and share its candidate buffers.
+__device__ __forceinline__ void lm_range(const LmArgs& a, int& u_begin, int& u_end) {
+    u_begin = (int)(((int64_t)blockIdx.x * a.n_units) / gridDim.x);
+    u_end = (int)(((int64_t)(blockIdx.x + 1) * a.n_units) / gridDim.x);
+}
+
 __device__ __forceinline__ void lm_unit(const LmArgs& a, int u, int& m, int& s, int& t0, int& t1) {
     m = u / a.S;
     s = u - m * a.S;
@@ -185,26 +187,43 @@ __device__ __forceinline__ void lm_unit(const LmArgs& a, int u, int& m, int& s, 
     t1 = (int)(((int64_t)(s + 1) * a.nt) / a.S);
 }
 
-// ---- rmsnorm (src/model.cpp:31-38), one thread per row, rounded to bf16 ----
-// The sum runs in order in double like the reference; every term is a product of
-// two floats and so exact in double, and 1/sqrt and the division are correctly
-// rounded, so xn equals the reference's float before the bf16 rounding.
+// ---- rmsnorm (src/model.cpp:31-38), rounded to bf16 ----
+// One warp per row: the lanes stage the row in shared memory (coalesced), lane 0
+// sums the squares in order in double like the reference (each term is a product
+// of two floats, exact in double; 1/sqrt and the division are correctly rounded, so
+// xn equals the reference's float before the bf16 rounding), then every lane writes
+// its share.  Dynamic shared memory: E floats per warp.
 __global__ void zs_lm_rmsnorm_kernel(const float* hidden, int64_t hld, const float* norm_w,
                                      float eps, int32_t B, int32_t E, __nv_bfloat16* xn) {
-    const int r = blockIdx.x * blockDim.x + threadIdx.x;
-    if (r >= B) return;
-    const float* x = hidden + (int64_t)r * hld;
-    double sum = 0.0;
-    for (int i = 0; i < E; ++i) {
-        const double v = (double)x[i];
-        sum = __dadd_rn(sum, __dmul_rn(v, v));
+    extern __shared__ float lm_stage[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    float* xs = lm_stage + (int64_t)warp * E;
+    for (int r = blockIdx.x * nw + warp; r < B; r += gridDim.x * nw) {
+        const float* x = hidden + (int64_t)r * hld;
+        for (int i = lane; i < E; i += 32) xs[i] = x[i];
+        __syncwarp();
+        double scale = 0.0;
+        if (lane == 0) {
+            double sum = 0.0;
+#pragma unroll 8
+            for (int i = 0; i < E; ++i) {
+                const double v = (double)xs[i];
+                sum = __dadd_rn(sum, __dmul_rn(v, v));
+            }
+            scale = 1.0 / sqrt(sum / (double)E + (double)eps);
+        }
+        scale = __shfl_sync(kFull, scale, 0);
+        __nv_bfloat16* o = xn + (int64_t)r * E;
+        for (int i = lane; i < E; i += 32) {
+            const float v = __double2float_rn(__dmul_rn(__dmul_rn((double)xs[i], scale), (double)norm_w[i]));
+            o[i] = __float2bfloat16_rn(v);
+        }
+        __syncwarp();
     }
-    const double scale = 1.0 / sqrt(sum / (double)E + (double)eps);
-    __nv_bfloat16* o = xn + (int64_t)r * E;
-    for (int i = 0; i < E; ++i) {
-        const float v = __double2float_rn(__dmul_rn(__dmul_rn((double)x[i], scale), (double)norm_w[i]));
-        o[i] = __float2bfloat16_rn(v);
-    }
+}
+
+__device__ __forceinline__ uint64_t lm_keep(uint64_t* buf, uint32_t n, uint32_t kk, int lane) {
+    return warp_topk_keep<(kLmCap + 31) / 32>(buf, n, kk, lane);
 }
 
 // Cuts row L's buffer (of this warp's 32 rows) back to its keff best keys; lane L
@@ -214,7 +233,7 @@ __device__ __forceinline__ void lm_compact_row(uint64_t* rows, int L, uint32_t& 
                                                uint32_t keff, int lane) {
     const uint32_t n = __shfl_sync(kFull, count, L);
     const uint32_t kk = __shfl_sync(kFull, keff, L);
-    const uint64_t T = warp_topk_keep<(kLmCap + 31) / 32>(rows + (int64_t)L * kLmRowStride, n, kk, lane);
+    const uint64_t T = lm_keep(rows + (int64_t)L * kLmRowStride, n, kk, lane);
     if (lane == L) {
         count = kk;
         tau_ord = (uint32_t)(T >> 32);
@@ -250,10 +269,26 @@ __device__ __forceinline__ uint32_t lm_pass_mask(const float (&v)[32], int col0,
 // One 32-column chunk of a tile for this warp's 32 rows: rows whose passing
 // columns would overflow their buffers are compacted first (the whole warp, one row
 // at a time), then every row appends its passing keys.
-__device__ __forceinline__ void lm_chunk(const float (&v)[32], int col0, int V, bool sel,
-                                         uint64_t* rows, uint64_t* mine, uint32_t& count,
-                                         uint32_t& tau_ord, float& tau_f, bool& open,
-                                         uint32_t keff, int lane) {
+__device__ __forceinline__ void lm_chunk(const uint32_t (&r)[32], int col0, int V, bool sel,
+                                         float* lrow, bool& x0nan, bool select, uint64_t* rows,
+                                         uint64_t* mine, uint32_t& count, uint32_t& tau_ord,
+                                         float& tau_f, bool& open, uint32_t keff, int lane) {
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+    if (col0 == 0) x0nan = (v[0] != v[0]);
+    if (lrow) {
+        if (col0 + 32 <= V) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<float4*>(lrow + col0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (col0 + j < V) lrow[col0 + j] = v[j];
+        }
+    }
+    if (!select) return;
     uint32_t pm = sel ? lm_pass_mask(v, col0, V, tau_ord, tau_f, open) : 0u;
     unsigned over = __ballot_sync(kFull, count + __popc(pm) > (uint32_t)kLmCap);
     while (over) {
@@ -303,6 +338,8 @@ __global__ void __launch_bounds__(kLmThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = sm.tmem_base;
+    int u_begin, u_end;
+    lm_range(a, u_begin, u_end);
 
     if (warp == 0) {
         // ---- copy issuer ----
@@ -310,7 +347,7 @@ __global__ void __launch_bounds__(kLmThreads, 1)
             uint32_t stage = 0, phase = 0;
             int64_t issued = 0;
             bool ok = true;
-            for (int u = blockIdx.x; ok && u < a.n_units; u += gridDim.x) {
+            for (int u = u_begin; ok && u < u_end; ++u) {
                 int m, s, t0, t1;
                 lm_unit(a, u, m, s, t0, t1);
                 for (int t = t0; ok && t < t1; ++t) {
@@ -342,7 +379,7 @@ __global__ void __launch_bounds__(kLmThreads, 1)
         if (lane == 0) {
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool ok = true;
-            for (int u = blockIdx.x; ok && u < a.n_units; u += gridDim.x) {
+            for (int u = u_begin; ok && u < u_end; ++u) {
                 int m, s, t0, t1;
                 lm_unit(a, u, m, s, t0, t1);
                 for (int t = t0; ok && t < t1; ++t) {
@@ -393,7 +430,12 @@ __global__ void __launch_bounds__(kLmThreads, 1)
         const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
         uint32_t acc = 0, acc_phase = 0;
         bool ok = true;
-        for (int u = blockIdx.x; ok && u < a.n_units; u += gridDim.x) {
+        uint32_t count = 0;    // keys in the buffer
+        uint32_t tau_ord = 0;  // threshold's value order (after the first compaction)
+        float tau_f = 0.0f;    // its value
+        bool open = true;      // no threshold yet: every column enters
+        bool x0nan = false, has0 = false;
+        for (int u = u_begin; ok && u < u_end; ++u) {
             int m, s, t0, t1;
             lm_unit(a, u, m, s, t0, t1);
             const int row = m * kLmM + r_in;
@@ -404,11 +446,14 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                                             nullptr, nullptr, 0, row);
                 keff = (uint32_t)rp.ksel;
             }
-            uint32_t count = 0;    // keys in the buffer
-            uint32_t tau_ord = 0;  // threshold's value order (after the first compaction)
-            float tau_f = 0.0f;    // its value
-            bool open = true;      // no threshold yet: every column enters
-            bool x0nan = false;
+            if (u == u_begin || s == 0) {  // a new run of this row tile's slices
+                count = 0;
+                tau_ord = 0;
+                open = true;
+                x0nan = false;
+                has0 = false;
+            }
+            has0 = has0 || t0 == 0;
             const bool sel = a.select && valid;
             float* lrow = (a.out_logits && valid) ? a.out_logits + (int64_t)row * a.logits_ld : nullptr;
             for (int t = t0; t < t1; ++t) {
@@ -419,27 +464,15 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                 }
                 tc_fence_after();
                 const int tcol = t * kLmN;
+                const uint32_t base = lane_addr + acc * (uint32_t)kLmN;
 #pragma unroll 1
                 for (int c = 0; c < kLmN / 32; ++c) {
-                    float v[32];
+                    uint32_t ra[32];
                     __syncwarp();
-                    tc_ld32(lane_addr + acc * (uint32_t)kLmN + (uint32_t)(c * 32), v);
-                    const int col0 = tcol + c * 32;
-                    if (col0 == 0) x0nan = (v[0] != v[0]);
-                    if (lrow) {
-                        if (col0 + 32 <= a.V) {
-#pragma unroll
-                            for (int j = 0; j < 32; j += 4)
-                                *reinterpret_cast<float4*>(lrow + col0 + j) =
-                                    make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                        } else {
-#pragma unroll
-                            for (int j = 0; j < 32; ++j)
-                                if (col0 + j < a.V) lrow[col0 + j] = v[j];
-                        }
-                    }
-                    if (a.select)
-                        lm_chunk(v, col0, a.V, sel, rows, mine, count, tau_ord, tau_f, open, keff, lane);
+                    tc_ld32_issue(base + (uint32_t)(c * 32), ra);
+                    tc_ld_wait(ra);
+                    lm_chunk(ra, tcol + c * 32, a.V, sel, lrow, x0nan, a.select, rows, mine, count,
+                             tau_ord, tau_f, open, keff, lane);
                 }
                 tc_fence_before();
                 mbar_arrive(&sm.acc_empty[acc]);
@@ -449,17 +482,25 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                 }
             }
             if (!ok) break;
-            if (a.select) {
-                unsigned over = __ballot_sync(kFull, sel && count > keff);
-                while (over) {
-                    const int L = __ffs(over) - 1;
-                    over &= over - 1;
-                    lm_compact_row(rows, L, count, tau_ord, tau_f, open, keff, lane);
-                }
+            if (!a.select) continue;
+            // The run goes on into the next slice of this row tile: this slice's
+            // block stays empty and the buffer carries over.
+            const bool run_on = (u + 1 < u_end) && (s + 1 < a.S);
+            if (run_on) {
+                if (sel)
+                    *reinterpret_cast<uint4*>(a.part + ((int64_t)row * a.S + s) * kLmPartStride) =
+                        make_uint4(0u, 0u, __float_as_uint(-INFINITY), 0u);
+                continue;
+            }
+            unsigned over = __ballot_sync(kFull, sel && count > keff);
+            while (over) {
+                const int L = __ffs(over) - 1;
+                over &= over - 1;
+                lm_compact_row(rows, L, count, tau_ord, tau_f, open, keff, lane);
             }
             if (sel) {
                 uint8_t* blk = a.part + ((int64_t)row * a.S + s) * kLmPartStride;
-                const uint32_t flags = (t0 == 0) ? (kPartHasId0 | (x0nan ? kPartX0Nan : 0u)) : 0u;
+                const uint32_t flags = has0 ? (kPartHasId0 | (x0nan ? kPartX0Nan : 0u)) : 0u;
                 *reinterpret_cast<uint4*>(blk) = make_uint4(count, flags, __float_as_uint(-INFINITY), 0u);
                 uint64_t* keys = reinterpret_cast<uint64_t*>(blk + kPartialHeaderBytes);
                 for (uint32_t i = 0; i < count; ++i) keys[i] = mine[i];

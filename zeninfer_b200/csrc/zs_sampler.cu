@@ -258,7 +258,7 @@ struct zs_context {
     size_t fail_units_n = 0;
     // optional per-kernel timing (zs_set_timing): event pairs around each launch
     struct TimedLaunch {
-        int kind;  // 0 select, 1 merge, 2 large, 3 lm_head
+        int kind;  // 0 select, 1 merge, 2 large, 3 lm_head GEMM, 4 lm_head rmsnorm
         cudaEvent_t begin, end;
     };
     bool timing = false;
@@ -669,9 +669,10 @@ zs_status zs_get_timing(zs_handle h, zs_timing* out) {
     if (!h || !out) return fail(ZS_ERR_INVALID_ARGUMENT, "null handle or out");
     DeviceGuard g(h->device);
     std::memset(out, 0, sizeof(*out));
-    double* dst[4] = {&out->select_ms, &out->merge_ms, &out->large_ms, &out->lmhead_ms};
-    int64_t* cnt[4] = {&out->select_launches, &out->merge_launches, &out->large_launches,
-                       &out->lmhead_launches};
+    double* dst[5] = {&out->select_ms, &out->merge_ms, &out->large_ms, &out->lmhead_ms,
+                      &out->lmnorm_ms};
+    int64_t* cnt[5] = {&out->select_launches, &out->merge_launches, &out->large_launches,
+                       &out->lmhead_launches, &out->lmnorm_launches};
     zs_status s = ZS_OK;
     for (auto& t : h->timed) {
         float ms = 0.0f;
@@ -927,8 +928,13 @@ zs_status zs_lmhead_sample(zs_handle h, const float* hidden, int64_t hidden_ld,
         a.part = h->part;
     }
     {
-        LaunchScope scope(h, 1, st);  // counted with the merge-side helpers
-        zs::zs_lm_rmsnorm_kernel<<<(batch + 127) / 128, 128, 0, st>>>(
+        LaunchScope scope(h, 4, st);
+        // warps per CTA: as many rows as fit 48 KB of staged floats, at most 8
+        const int nw = (int)std::max<int64_t>(1, std::min<int64_t>(8, (48 << 10) / ((int64_t)n_embd * 4)));
+        const size_t smem = (size_t)nw * n_embd * sizeof(float);
+        if (smem > (48u << 10)) return fail(ZS_ERR_INVALID_ARGUMENT, "n_embd too large for rmsnorm staging");
+        const int grid = (int)std::min<int64_t>((batch + nw - 1) / nw, (int64_t)h->num_sms * 16);
+        zs::zs_lm_rmsnorm_kernel<<<grid, nw * 32, smem, st>>>(
             hidden, hidden_ld, norm_w, eps, batch, n_embd,
             reinterpret_cast<__nv_bfloat16*>(h->lm_xn));
         ZS_CUDA(cudaGetLastError());
