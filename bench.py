@@ -147,6 +147,87 @@ def cpu_reference_rate(x_rows, params, seeds, budget_s=10.0, nthreads=None):
     return done / dt, done, dt, nthreads
 
 
+def lmhead_bench(s, dev, stream, hbm_peak):
+    import numpy as np
+    import torch
+    from zeninfer_b200 import SamplingParams, states_to_tensor
+    E = 896
+    g = torch.Generator(device=dev).manual_seed(17)
+    W = (torch.randn(V, E, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+    nw = torch.rand(E, device=dev, generator=g) + 0.5
+    p = SamplingParams(temp=0.7, top_k=50, top_p=0.9)
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            tf_peak, tf_kind = float(json.load(f)["bf16_tflops"]), "measured burst"
+    except Exception:
+        tf_peak, tf_kind = 1590.0, "fallback"
+    out = {"weights": "bf16 [151936][896], seeded N(0, 0.05^2)", "hidden": "N(0, 3^2) f32",
+           "params": "temp 0.7, top-k 50, top-p 0.9"}
+    for B in (4096, 1):
+        h = torch.randn(B, E, device=dev, generator=g) * 3
+        st = states_to_tensor([i + 1 for i in range(B)], dev)
+        ids = torch.empty(B, dtype=torch.int32, device=dev)
+        fused = lambda: s.lmhead_sample(h, nw, W, p, st, out=ids, stream=stream)
+        for _ in range(3):
+            fused()
+        torch.cuda.synchronize()
+        reps = 10 if B > 1 else 100
+        s.set_timing(True)
+        s.get_timing()
+        ms = time_device_steps(fused, reps, stream) / reps
+        kt = s.get_timing()
+        s.set_timing(False)
+        k_ms = kt["lmhead_ms"] / max(1, kt["lmhead_launches"])
+        xn = torch.nn.functional.rms_norm(h, (E,), nw, 1e-6).to(torch.bfloat16)
+
+        def unfused():
+            lg = torch.mm(xn, W.t(), out_dtype=torch.float32)
+            s.sample(lg, p, st, out=ids, stream=stream)
+        for _ in range(3):
+            unfused()
+        torch.cuda.synchronize()
+        ms_u = time_device_steps(unfused, reps, stream) / reps
+        flops = 2.0 * B * E * V
+        wbytes = V * E * 2 + B * E * 2
+        r = {"us_per_call": ms * 1e3, "rows_per_s": B / (ms / 1e3),
+             "kernel_us": k_ms * 1e3,
+             "rmsnorm_us": kt["lmnorm_ms"] / max(1, kt["lmnorm_launches"]) * 1e3,
+             "merge_us": kt["merge_ms"] / max(1, kt["merge_launches"]) * 1e3,
+             "unfused_cublas_plus_zs_sample_us": ms_u * 1e3}
+        if B > 1:
+            r["roofline"] = {"bound": "tensor", "achieved": flops / (k_ms / 1e3) / 1e12,
+                             "peak": tf_peak, "unit": "TFLOP/s",
+                             "frac": flops / (k_ms / 1e3) / 1e12 / tf_peak,
+                             "peak_source": f"bf16_tflops, {tf_kind}",
+                             "algorithmic_flops_per_launch": flops}
+        else:
+            r["roofline"] = {"bound": "hbm", "achieved": wbytes / (k_ms / 1e3) / 1e9,
+                             "peak": hbm_peak, "unit": "GB/s",
+                             "frac": wbytes / (k_ms / 1e3) / 1e9 / hbm_peak,
+                             "algorithmic_bytes_per_launch": wbytes}
+        out[f"b{B}"] = r
+        del h
+    try:
+        import oracle
+        if oracle.have_reference():
+            n = 4
+            hc = (torch.randn(n, E, generator=torch.Generator().manual_seed(3)) * 3).numpy()
+            wf = W.float().cpu().numpy()
+            nth = os.cpu_count() or 1
+            t0 = time.perf_counter()
+            _, lg = oracle.reference_lmhead(hc, nw.cpu().numpy(), 1e-6, wf, impl=1, nthreads=nth)
+            oracle.reference_sample(lg, p, np.arange(1, n + 1, dtype=np.uint64), nthreads=nth)
+            dt = time.perf_counter() - t0
+            out["cpu_reference"] = {"rows_per_s": n / dt, "cores": nth, "kind": "reference",
+                                    "sample": f"{n} rows: zen::rmsnorm + zen::matvec_f32 (AVX2) "
+                                              "+ zen::sample_token, src/ compiled unchanged"}
+    except Exception as e:  # reported, never fatal
+        out["cpu_reference"] = {"note": str(e)}
+    del W
+    torch.cuda.synchronize()
+    return out
+
+
 def run_reference_arm(args, rank, world):
     """--impl reference: zeninfer's CPU sampler on the host cores, same workload."""
     if rank != 0:
@@ -221,6 +302,7 @@ def main():
                     help="raw <f4 [S][V] logits written by zeninfer's `logits --out` (its rows "
                          "repeated to fill the batch) instead of the synthetic workload")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-lmhead", action="store_true", help="skip the fused lm_head timing")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
@@ -403,6 +485,15 @@ def main():
         except Exception as e:  # reported, never fatal
             decode["reference_note"] = str(e)
 
+    # The lm_head fused with the sampler (zs_lmhead_sample): rmsnorm + the
+    # 151,936 x 896 bf16 GEMM on the tensor cores with the shortlist selection in its
+    # epilogue + merge, at 4096 and 1 rows, beside the unfused library route (cuBLAS
+    # bf16 GEMM with f32 logits, then zs_sample) and the reference's own CPU lm_head
+    # (rmsnorm + matvec_f32, AVX2, all host threads) + sample_token on a few rows.
+    lmhead = None
+    if rank == 0 and not args.no_lmhead:
+        lmhead = lmhead_bench(s, dev, stream, peak)
+
     # End to end through the public API with host buffers: H2D of the step's
     # logits from pinned memory, the sampler, D2H of the ids, every step.
     e2e = None
@@ -501,6 +592,8 @@ def main():
             line["logits_display"] = display
         if decode:
             line["decode_loop"] = decode
+        if lmhead:
+            line["lmhead_fused"] = lmhead
         print(json.dumps(line), flush=True)
 
     s.close()
