@@ -228,6 +228,45 @@ def lmhead_bench(s, dev, stream, hbm_peak):
     return out
 
 
+def full_vocab_top_p_bench(s, dev, stream):
+    import numpy as np
+    import torch
+    from zeninfer_b200 import SamplingParams, states_to_tensor
+    from zeninfer_b200 import workloads as W
+    rows = 1024
+    wl = W.WORKLOADS[3]
+    p = SamplingParams(temp=1.0, top_k=V, top_p=0.95)
+    xh = W.generate(3, rows)
+    x = torch.from_numpy(xh).to(dev)
+    st = states_to_tensor(wl.row_states(0, rows), dev)
+    ids = torch.empty(rows, dtype=torch.int32, device=dev)
+    fn = lambda: s.sample(x, p, st, out=ids, stream=stream)
+    fn()
+    torch.cuda.synchronize()
+    reps = 3
+    ms = time_device_steps(fn, reps, stream) / reps
+    res = s.sample(x[:64], p, states_to_tensor(wl.row_states(0, 64), dev), row_info=True,
+                   stream=stream)
+    m = res.row_info["m"]
+    out = {"rows": rows, "params": "temp 1.0, top-p 0.95, top_k = n_vocab (151,936)",
+           "ms_per_call": ms, "rows_per_s": rows / (ms / 1e3),
+           "nucleus_size_median": float(np.median(m))}
+    try:
+        import oracle
+        if oracle.have_reference():
+            n = 32
+            nth = os.cpu_count() or 1
+            t0 = time.perf_counter()
+            oracle.reference_sample(xh[:n], p, wl.row_seeds(0, n), nthreads=nth)
+            dt = time.perf_counter() - t0
+            out["cpu_reference"] = {"rows_per_s": n / dt, "cores": nth, "kind": "reference",
+                                    "sample": f"{n} rows, zen::sample_token with top_k = n"}
+    except Exception as e:  # reported, never fatal
+        out["cpu_reference"] = {"note": str(e)}
+    del x
+    return out
+
+
 def run_reference_arm(args, rank, world):
     """--impl reference: zeninfer's CPU sampler on the host cores, same workload."""
     if rank != 0:
@@ -303,6 +342,7 @@ def main():
                          "repeated to fill the batch) instead of the synthetic workload")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-lmhead", action="store_true", help="skip the fused lm_head timing")
+    ap.add_argument("--no-fullp", action="store_true", help="skip the full-vocabulary top-p timing")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
@@ -494,6 +534,14 @@ def main():
     if rank == 0 and not args.no_lmhead:
         lmhead = lmhead_bench(s, dev, stream, peak)
 
+    # Nucleus over the whole vocabulary (top_k = n_vocab: the shortlist is every
+    # token, sorted; softmax, nucleus and draw over all of it in f64), workload 3
+    # (1024 rows, -1.1 log(rank+1) + noise, temp 1.0, top-p 0.95), beside the
+    # reference's sample_token with the same params on a bounded sample of rows.
+    fullp = None
+    if rank == 0 and not args.no_fullp:
+        fullp = full_vocab_top_p_bench(s, dev, stream)
+
     # End to end through the public API with host buffers: H2D of the step's
     # logits from pinned memory, the sampler, D2H of the ids, every step.
     e2e = None
@@ -594,6 +642,8 @@ def main():
             line["decode_loop"] = decode
         if lmhead:
             line["lmhead_fused"] = lmhead
+        if fullp:
+            line["full_vocab_top_p"] = fullp
         print(json.dumps(line), flush=True)
 
     s.close()

@@ -354,3 +354,20 @@ def test_device_wait_timeout_is_reported(sampler):
     p = SamplingParams(temp=0.7, top_k=40, top_p=0.9)
     st = _states(range(8))
     compare(run_gpu(sampler, x, p, st), run_oracle(x, p, st))
+
+
+def test_full_vocab_top_p_against_reference(sampler):
+    """The nucleus over the whole 151,936-token vocabulary (top_k = n): device ids
+    against the unchanged reference on workload 3 rows (log-rank logits, nucleus of
+    tens of thousands of tokens), and the nucleus sizes against the restatement."""
+    rows = 6
+    x = W.generate(3, rows, row0=500)
+    p = SamplingParams(temp=1.0, top_k=2 ** 31 - 1, top_p=0.95)
+    seeds = np.arange(rows, dtype=np.uint64) + np.uint64(900)
+    g = run_gpu(sampler, x, p, _states(seeds))
+    o = run_oracle(x, p, _states(seeds))
+    compare(g, o, check_cands=False)
+    assert (o["info"]["m"] > 10000).all()
+    ref, _ = oracle.reference_sample(x, p, seeds)
+    near = o["info"]["boundary"] < BOUNDARY_EPS
+    assert np.array_equal(g["ids"][~near], ref[~near])

@@ -322,3 +322,21 @@ def test_bf16_rounding_helpers():
     assert back[2] == np.float32(1.0078125)
     assert back[3] == -2.5 and np.isinf(back[5]) and np.signbit(back[6])
     assert np.isnan(oracle.bf16_bits_to_f32(oracle.f32_to_bf16_bits(np.array([np.nan], np.float32))))[0]
+
+
+@needs_ref
+def test_full_vocab_top_p_against_reference():
+    """top_k >= n makes the shortlist the whole row (k = min(top_k, n) = n): the
+    nucleus over the full vocabulary.  Restatement and reference agree exactly."""
+    rng = np.random.default_rng(41)
+    rows, n = 24, 3000
+    ranks = np.argsort(rng.random((rows, n)), axis=1)
+    x = (-1.1 * np.log(ranks + 1.0) + rng.normal(0, 0.3, size=(rows, n))).astype(np.float32)
+    seeds = np.arange(rows, dtype=np.uint64) + np.uint64(7)
+    for top_k in (n, 2 ** 31 - 1):
+        p = SamplingParams(temp=1.0, top_k=top_k, top_p=0.95)
+        st = np.array([rng_seed(int(s)) for s in seeds], dtype=np.uint64)
+        ids, info, *_ = oracle.oracle_sample(x, p, st)
+        ref, _ = oracle.reference_sample(x, p, seeds)
+        assert np.array_equal(ids, ref)
+        assert (info["k"] == n).all() and (info["m"] > 256).all()

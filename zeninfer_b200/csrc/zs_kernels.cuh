@@ -888,6 +888,118 @@ __device__ void penalty_fixup(CandState& st, const float* row_logits, const int3
     csync();
 }
 
+// Shortlists longer than this (only the large-shortlist path has them) run the
+// f64 tail in blocked order.
+constexpr uint32_t kBlockedTail = 4096;
+
+// The f64 tail of sample_token (src/sample.cpp:69-101) for a long sorted shortlist
+// whose exps are in prob[0..kk): the same quantities, with the additions grouped by
+// chunk.  Thread c owns the contiguous chunk [c*kk/kNC, (c+1)*kk/kNC) and sums it in
+// order; thread 0 adds the chunk sums in chunk order and walks element by element
+// only inside the chunk where the nucleus prefix or the draw crosses.  Grouped
+// sums differ from the one-by-one ones in their last bits only.
+__device__ void finalize_blocked(CandState& st, const uint64_t* cand, double* prob, uint32_t kk,
+                                 const Params& p, float max_l, float inv_temp, bool have_lse,
+                                 bool x0_nan, float lse_m, float lse_s, int row, uint64_t* rng,
+                                 int32_t* out_ids, RowInfo* info, int32_t* cand_ids,
+                                 double* cand_probs, int32_t cand_ld, int ctid) {
+    double* cs = reinterpret_cast<double*>(st.prop);  // one sum per chunk
+    const uint32_t lo = (uint32_t)(((uint64_t)ctid * kk) / kNC);
+    const uint32_t hi = (uint32_t)(((uint64_t)(ctid + 1) * kk) / kNC);
+    double s = 0.0;
+    for (uint32_t i = lo; i < hi; ++i) s += prob[i];
+    cs[ctid] = s;
+    csync();
+    if (ctid == 0) {
+        double t = 0.0;
+        for (int c = 0; c < kNC; ++c) t += cs[c];
+        st.d_sum = t;
+    }
+    csync();
+    const double sum = st.d_sum;
+    s = 0.0;
+    for (uint32_t i = lo; i < hi; ++i) {
+        const double pi = prob[i] / sum;
+        prob[i] = pi;
+        s += pi;
+        if ((int32_t)i < cand_ld) {
+            if (cand_ids) cand_ids[(int64_t)row * cand_ld + i] = key_id(cand[i]);
+            if (cand_probs) cand_probs[(int64_t)row * cand_ld + i] = pi;
+        }
+    }
+    cs[ctid] = s;
+    csync();
+    const bool nucleus = p.top_p < 1.0f;
+    if (ctid == 0) {
+        int m = (int)kk;
+        double rescale = 1.0;
+        if (nucleus) {
+            const double tp = (double)p.top_p;
+            double acc = 0.0;
+            int c = 0;
+            while (c < kNC && acc + cs[c] < tp) acc += cs[c++];
+            uint32_t i = c < kNC ? (uint32_t)(((uint64_t)c * kk) / kNC) : kk;
+            while (i < kk && acc < tp) acc += prob[i++];
+            m = (int)i;
+            if (m == 0) {
+                m = 1;
+                acc = prob[0];
+            }
+            rescale = acc;
+        }
+        st.m = m;
+        st.d_rescale = rescale;
+    }
+    csync();
+    const int m = st.m;
+    const double rs = st.d_rescale;
+    s = 0.0;
+    for (uint32_t i = lo; i < hi && (int)i < m; ++i) {
+        if (nucleus) prob[i] /= rs;
+        s += prob[i];
+    }
+    csync();  // thread 0 has read every chunk sum of the nucleus pass
+    cs[ctid] = s;
+    csync();
+    if (ctid == 0) {
+        uint64_t st_rng = rng[row];
+        const double r = rng_uniform(st_rng);
+        rng[row] = st_rng;
+        double acc = 0.0, prev = 0.0;
+        int c = 0;
+        while (c < kNC && !(r < acc + cs[c])) acc += cs[c++];
+        int i = c < kNC ? (int)(((uint64_t)c * kk) / kNC) : m;
+        int pos = m - 1;
+        bool hit = false;
+        for (; i < m; ++i) {
+            prev = acc;
+            acc += prob[i];
+            if (r < acc) {
+                pos = i;
+                hit = true;
+                break;
+            }
+        }
+        const double d = hit ? fmin(r - prev, acc - r) : r - acc;
+        if (out_ids) out_ids[row] = key_id(cand[pos < 0 ? 0 : pos]);
+        if (info) {
+            RowInfo ri;
+            ri.max_logit = max_l;
+            ri.k = (int32_t)kk;
+            ri.m = m;
+            ri.pos = pos;
+            ri.r = r;
+            ri.sum = sum;
+            ri.boundary = d;
+            ri.log_z = (have_lse && !x0_nan)
+                           ? log((double)lse_s) + ((double)lse_m - (double)max_l) * (double)inv_temp
+                           : __longlong_as_double(0x7ff8000000000000ll);
+            info[row] = ri;
+        }
+    }
+    csync();
+}
+
 // f64 tail of sample_token (src/sample.cpp:52-101) over the sorted shortlist
 // cand[0..kk): softmax in shortlist order, nucleus prefix, inverse-CDF draw.
 // `prob` holds kk doubles of scratch.  Generic pointers: shared or global.
@@ -927,6 +1039,11 @@ __device__ void finalize_row(CandState& st, const uint64_t* cand, double* prob, 
     for (uint32_t i = ctid; i < kk; i += kNC)
         prob[i] = exp(((double)key_value(cand[i]) - (double)max_l) * (double)inv_temp);
     csync();
+    if (kk > kBlockedTail) {
+        finalize_blocked(st, cand, prob, kk, p, max_l, inv_temp, have_lse, x0_nan, lse_m, lse_s,
+                         row, rng, out_ids, info, cand_ids, cand_probs, cand_ld, ctid);
+        return;
+    }
     if (ctid == 0) {
         double sum = 0.0;
         for (uint32_t i = 0; i < kk; ++i) sum += prob[i];
@@ -2753,7 +2870,11 @@ __global__ void __launch_bounds__(kNC) zs_large_kernel(const Args a) {
         uint64_t T = 0ull;
         if (kk < n) T = select_threshold_global(st, keys, n, kk, ctid);
         uint32_t base = 0;
-        for (uint32_t c0 = 0; c0 < n; c0 += kNC) {
+        if (kk == n) {  // every key is kept: copy, the sort orders them
+            for (uint32_t i = ctid; i < n; i += kNC) tmp[i] = keys[i];
+            base = n;
+        }
+        for (uint32_t c0 = (kk == n) ? n : 0; c0 < n; c0 += kNC) {
             const uint32_t i = c0 + ctid;
             const uint64_t k = i < n ? keys[i] : 0ull;
             const uint32_t f = (i < n && k >= T) ? 1u : 0u;
