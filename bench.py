@@ -463,7 +463,7 @@ def main():
     # the last position's, as that command computes them: device-timed, beside the
     # restatement timed on one host thread.
     display = None
-    if rank == 0:
+    if rank == 0 and world == 1:
         x1 = x_dev[:1]
         for _ in range(3):
             s.logits_stats(x1, 8, stream=stream)
@@ -488,7 +488,7 @@ def main():
     # sequences with the penalty on, beside the reference's sample_token per step on
     # one host thread (host logits, the history as a std::vector).
     decode = None
-    if rank == 0:
+    if rank == 0 and world == 1:
         pdec = SamplingParams(temp=0.7, top_k=40, top_p=0.9, repeat_penalty=1.1,
                               repeat_last_n=64)
         decode = {"params": "temp 0.7, top-k 40, top-p 0.9, repeat_penalty 1.1, last 64",
@@ -531,7 +531,7 @@ def main():
     # bf16 GEMM with f32 logits, then zs_sample) and the reference's own CPU lm_head
     # (rmsnorm + matvec_f32, AVX2, all host threads) + sample_token on a few rows.
     lmhead = None
-    if rank == 0 and not args.no_lmhead:
+    if rank == 0 and world == 1 and not args.no_lmhead:
         lmhead = lmhead_bench(s, dev, stream, peak)
 
     # Nucleus over the whole vocabulary (top_k = n_vocab: the shortlist is every
@@ -539,7 +539,7 @@ def main():
     # (1024 rows, -1.1 log(rank+1) + noise, temp 1.0, top-p 0.95), beside the
     # reference's sample_token with the same params on a bounded sample of rows.
     fullp = None
-    if rank == 0 and not args.no_fullp:
+    if rank == 0 and world == 1 and not args.no_fullp:
         fullp = full_vocab_top_p_bench(s, dev, stream)
 
     # End to end through the public API with host buffers: H2D of the step's
