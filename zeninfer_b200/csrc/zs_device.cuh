@@ -46,6 +46,20 @@ __device__ __forceinline__ double rng_uniform(uint64_t& s) {
     return (double)(rng_next(s) >> 11) * (1.0 / 9007199254740992.0);
 }
 
+// ---- programmatic dependent launch ----
+// A kernel launched with programmatic stream serialization may start while the
+// kernel before it in the stream is still running; grid_dep_wait() returns once
+// that kernel has completed and its memory writes are visible.  Without that launch
+// attribute it returns at once.
+__device__ __forceinline__ void grid_dep_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+// Lets the next kernel in the stream (if launched as above) be scheduled now; it
+// still reads nothing of this kernel's before its grid_dep_wait().
+__device__ __forceinline__ void grid_dep_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---- shared-memory addresses, mbarriers and the bulk-copy engine ----
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
     return (uint32_t)__cvta_generic_to_shared(p);

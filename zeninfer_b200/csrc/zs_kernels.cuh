@@ -1667,6 +1667,7 @@ __global__ void __launch_bounds__(kThreads, 2) zs_select_kernel(const Args a) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     FastSmem& sm = *reinterpret_cast<FastSmem*>(smem_raw);
     const int tid = threadIdx.x;
+    grid_dep_trigger();  // the merge may be scheduled; it waits for this grid to end
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&sm.full[s], 1);
@@ -1691,6 +1692,7 @@ __global__ void __launch_bounds__(kNC) zs_merge_kernel(const MergeArgs a) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     CandState& st = *reinterpret_cast<CandState*>(smem_raw);
     const int ctid = threadIdx.x;
+    grid_dep_wait();  // the partial blocks come from the kernel before this one
     for (int row = blockIdx.x; row < a.B; row += gridDim.x) {
         const RowPlan rp = plan_row(load_params(a.row_params, a.shared, row), a.V_total, a.hist,
                                     a.hist_len, a.hist_ld, row);
@@ -2105,6 +2107,7 @@ __global__ void __launch_bounds__(kNC, 4) zs_warp_merge_kernel(const MergeArgs a
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     WarpSlot& ws = sm.w[warp];
     const unsigned below = lanemask_lt();
+    grid_dep_wait();  // the partial blocks come from the kernel before this one
     for (int row = blockIdx.x * kConsumerWarps + warp; row < a.B; row += gridDim.x * kConsumerWarps) {
         const RowPlan rp = plan_row(load_params(a.row_params, a.shared, row), a.V_total, a.hist,
                                     a.hist_len, a.hist_ld, row);
@@ -2545,6 +2548,7 @@ __global__ void __launch_bounds__(C::kWarps * 32, 1) zs_wselect_kernel(const Arg
     WSelSmem<C>& sm = *reinterpret_cast<WSelSmem<C>*>(smem_raw);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     WarpSel<C>& ws = sm.w[warp];
+    grid_dep_trigger();  // the merge may be scheduled; it waits for this grid to end
     const int32_t gw = blockIdx.x * C::kWarps + warp;
     if (gw >= a.wl_NW) return;  // the whole warp; nothing in this kernel syncs the block
     WShare sh;

@@ -383,20 +383,31 @@ struct LaunchScope {
 zs_status launch_merge(zs_context* h, const zs::MergeArgs& m, int max_ksel, bool want_lse,
                        cudaStream_t st) {
     LaunchScope scope(h, 1, st);
+    // Programmatic dependent launch: the merge may be scheduled while the kernel
+    // before it finishes; it waits (grid_dep_wait) before reading any block.
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg;
+    std::memset(&cfg, 0, sizeof(cfg));
+    cfg.blockDim = dim3(zs::kNC);
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e;
     if ((uint32_t)max_ksel <= zs::kWarpMergeMaxK && m.B >= 2 * h->num_sms) {
         const int rows_per_cta = zs::kConsumerWarps;
-        const int grid = std::max(1, std::min((m.B + rows_per_cta - 1) / rows_per_cta, 8 * h->num_sms));
-        if (want_lse)
-            zs::zs_warp_merge_kernel<true><<<grid, zs::kNC, h->warp_merge_smem, st>>>(m);
-        else
-            zs::zs_warp_merge_kernel<false><<<grid, zs::kNC, h->warp_merge_smem, st>>>(m);
+        cfg.gridDim = dim3(std::max(1, std::min((m.B + rows_per_cta - 1) / rows_per_cta, 8 * h->num_sms)));
+        cfg.dynamicSmemBytes = h->warp_merge_smem;
+        e = want_lse ? cudaLaunchKernelEx(&cfg, zs::zs_warp_merge_kernel<true>, m)
+                     : cudaLaunchKernelEx(&cfg, zs::zs_warp_merge_kernel<false>, m);
     } else {
-        const int grid = std::max(1, std::min(m.B, 4 * h->num_sms));
-        if (want_lse)
-            zs::zs_merge_kernel<true><<<grid, zs::kNC, h->merge_smem, st>>>(m);
-        else
-            zs::zs_merge_kernel<false><<<grid, zs::kNC, h->merge_smem, st>>>(m);
+        cfg.gridDim = dim3(std::max(1, std::min(m.B, 4 * h->num_sms)));
+        cfg.dynamicSmemBytes = h->merge_smem;
+        e = want_lse ? cudaLaunchKernelEx(&cfg, zs::zs_merge_kernel<true>, m)
+                     : cudaLaunchKernelEx(&cfg, zs::zs_merge_kernel<false>, m);
     }
+    if (e != cudaSuccess) return cuda_fail(e, "merge launch");
     ZS_CUDA(cudaGetLastError());
     return ZS_OK;
 }
