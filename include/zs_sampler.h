@@ -86,7 +86,9 @@ typedef struct zs_extras {
 typedef struct zs_context* zs_handle;
 
 /* One handle per device; it owns the scratch and the kernel configuration.
- * The handle is not thread-safe: use one per host thread, or serialise. */
+ * The handle is not thread-safe: use one per host thread, or serialise.  Calls on
+ * one handle share its scratch, so issue them on one stream (or order the streams):
+ * two calls of one handle running on the GPU at the same time race. */
 zs_status zs_create(int device, zs_handle* out);
 zs_status zs_destroy(zs_handle h);
 
@@ -153,7 +155,7 @@ zs_status zs_decode_step(zs_handle h, const float* logits, int64_t ld, int32_t b
  * the accumulation order; the sampling on those logits is zs_sample's exactly.
  *   hidden     device f32 [batch][hidden_ld], the last position's hidden state
  *   norm_w     device f32 [n_embd], output_norm.weight
- *   n_embd     a multiple of 8, >= 64
+ *   n_embd     a multiple of 8, from 64 to 12288
  *   out_logits optional device f32 [batch][logits_ld] (logits_ld >= n_vocab, a
  *              multiple of 4): the logits the sampling used
  * Rows whose shortlist (top_k, or 256 when top_k is 0; 1 for greedy) is at most 64
