@@ -893,41 +893,55 @@ __device__ void penalty_fixup(CandState& st, const float* row_logits, const int3
 constexpr uint32_t kBlockedTail = 4096;
 
 // The f64 tail of sample_token (src/sample.cpp:69-101) for a long sorted shortlist
-// whose exps are in prob[0..kk): the same quantities, with the additions grouped by
-// chunk.  Thread c owns the contiguous chunk [c*kk/kNC, (c+1)*kk/kNC) and sums it in
-// order; thread 0 adds the chunk sums in chunk order and walks element by element
-// only inside the chunk where the nucleus prefix or the draw crosses.  Grouped
-// sums differ from the one-by-one ones in their last bits only.
+// whose exps are in prob[0..kk): the same quantities, with the additions grouped.
+// The shortlist is cut into segments of `seg` entries (256 or more, at most 4096
+// segments); a warp sums a segment (each lane its entries in order, then a fixed
+// shuffle tree), thread 0 adds the segment sums in order and walks entry by entry
+// only inside the segment where the nucleus prefix or the draw crosses.  Grouped
+// sums differ from one-by-one ones in their last bits only.  Segment sums live in
+// st.cand, which the large-shortlist path does not otherwise use here.
+__device__ __forceinline__ double lm_seg_sum(const double* prob, uint32_t lo, uint32_t hi, int lane) {
+    double s = 0.0;
+    for (uint32_t i = lo + lane; i < hi; i += 32) s += prob[i];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(kFull, s, o);
+    return s;
+}
+
 __device__ void finalize_blocked(CandState& st, const uint64_t* cand, double* prob, uint32_t kk,
                                  const Params& p, float max_l, float inv_temp, bool have_lse,
                                  bool x0_nan, float lse_m, float lse_s, int row, uint64_t* rng,
                                  int32_t* out_ids, RowInfo* info, int32_t* cand_ids,
                                  double* cand_probs, int32_t cand_ld, int ctid) {
-    double* cs = reinterpret_cast<double*>(st.prop);  // one sum per chunk
-    const uint32_t lo = (uint32_t)(((uint64_t)ctid * kk) / kNC);
-    const uint32_t hi = (uint32_t)(((uint64_t)(ctid + 1) * kk) / kNC);
-    double s = 0.0;
-    for (uint32_t i = lo; i < hi; ++i) s += prob[i];
-    cs[ctid] = s;
+    double* ss = reinterpret_cast<double*>(st.cand);  // one sum per segment
+    const int lane = ctid & 31, warp = ctid >> 5;
+    const uint32_t seg = 256u * ((kk + 256u * 4096u - 1) / (256u * 4096u));
+    const uint32_t nseg = (kk + seg - 1) / seg;
+    for (uint32_t g = warp; g < nseg; g += kConsumerWarps) {
+        const double t = lm_seg_sum(prob, g * seg, min(kk, (g + 1) * seg), lane);
+        if (lane == 0) ss[g] = t;
+    }
     csync();
     if (ctid == 0) {
         double t = 0.0;
-        for (int c = 0; c < kNC; ++c) t += cs[c];
+        for (uint32_t g = 0; g < nseg; ++g) t += ss[g];
         st.d_sum = t;
     }
     csync();
     const double sum = st.d_sum;
-    s = 0.0;
-    for (uint32_t i = lo; i < hi; ++i) {
+    for (uint32_t i = ctid; i < kk; i += kNC) {
         const double pi = prob[i] / sum;
         prob[i] = pi;
-        s += pi;
         if ((int32_t)i < cand_ld) {
             if (cand_ids) cand_ids[(int64_t)row * cand_ld + i] = key_id(cand[i]);
             if (cand_probs) cand_probs[(int64_t)row * cand_ld + i] = pi;
         }
     }
-    cs[ctid] = s;
+    csync();
+    for (uint32_t g = warp; g < nseg; g += kConsumerWarps) {
+        const double t = lm_seg_sum(prob, g * seg, min(kk, (g + 1) * seg), lane);
+        if (lane == 0) ss[g] = t;
+    }
     csync();
     const bool nucleus = p.top_p < 1.0f;
     if (ctid == 0) {
@@ -936,9 +950,9 @@ __device__ void finalize_blocked(CandState& st, const uint64_t* cand, double* pr
         if (nucleus) {
             const double tp = (double)p.top_p;
             double acc = 0.0;
-            int c = 0;
-            while (c < kNC && acc + cs[c] < tp) acc += cs[c++];
-            uint32_t i = c < kNC ? (uint32_t)(((uint64_t)c * kk) / kNC) : kk;
+            uint32_t g = 0;
+            while (g < nseg && acc + ss[g] < tp) acc += ss[g++];
+            uint32_t i = g < nseg ? g * seg : kk;
             while (i < kk && acc < tp) acc += prob[i++];
             m = (int)i;
             if (m == 0) {
@@ -953,22 +967,24 @@ __device__ void finalize_blocked(CandState& st, const uint64_t* cand, double* pr
     csync();
     const int m = st.m;
     const double rs = st.d_rescale;
-    s = 0.0;
-    for (uint32_t i = lo; i < hi && (int)i < m; ++i) {
-        if (nucleus) prob[i] /= rs;
-        s += prob[i];
+    if (nucleus) {
+        for (int i = ctid; i < m; i += kNC) prob[i] /= rs;
+        csync();
     }
-    csync();  // thread 0 has read every chunk sum of the nucleus pass
-    cs[ctid] = s;
+    const uint32_t nseg_m = ((uint32_t)m + seg - 1) / seg;
+    for (uint32_t g = warp; g < nseg_m; g += kConsumerWarps) {
+        const double t = lm_seg_sum(prob, g * seg, min((uint32_t)m, (g + 1) * seg), lane);
+        if (lane == 0) ss[g] = t;
+    }
     csync();
     if (ctid == 0) {
         uint64_t st_rng = rng[row];
         const double r = rng_uniform(st_rng);
         rng[row] = st_rng;
         double acc = 0.0, prev = 0.0;
-        int c = 0;
-        while (c < kNC && !(r < acc + cs[c])) acc += cs[c++];
-        int i = c < kNC ? (int)(((uint64_t)c * kk) / kNC) : m;
+        uint32_t g = 0;
+        while (g < nseg_m && !(r < acc + ss[g])) acc += ss[g++];
+        int i = g < nseg_m ? (int)(g * seg) : m;
         int pos = m - 1;
         bool hit = false;
         for (; i < m; ++i) {
@@ -1036,8 +1052,15 @@ __device__ void finalize_row(CandState& st, const uint64_t* cand, double* prob, 
     ZS_CHECK(kk <= 2048u || prob != reinterpret_cast<double*>(st.cand + kProbOffset), 12, kk);
     const float inv_temp = 1.0f / p.temp;
     const float max_l = (x0_nan || kk == 0) ? __int_as_float(0x7fc00000) : key_value(cand[0]);
-    for (uint32_t i = ctid; i < kk; i += kNC)
-        prob[i] = exp(((double)key_value(cand[i]) - (double)max_l) * (double)inv_temp);
+    if (kk > kBlockedTail) {
+        // long shortlists: the exponent in double, exp itself in f32 (relative
+        // error about 1e-7, far inside the 1e-5 probability rule)
+        for (uint32_t i = ctid; i < kk; i += kNC)
+            prob[i] = (double)expf((float)(((double)key_value(cand[i]) - (double)max_l) * (double)inv_temp));
+    } else {
+        for (uint32_t i = ctid; i < kk; i += kNC)
+            prob[i] = exp(((double)key_value(cand[i]) - (double)max_l) * (double)inv_temp);
+    }
     csync();
     if (kk > kBlockedTail) {
         finalize_blocked(st, cand, prob, kk, p, max_l, inv_temp, have_lse, x0_nan, lse_m, lse_s,
@@ -2740,9 +2763,17 @@ __device__ uint64_t select_threshold_global(CandState& st, const uint64_t* src, 
     for (int shift = 56; shift >= 0; shift -= 8) {
         st.hist[ctid] = 0u;
         csync();
-        for (uint32_t i = ctid; i < n; i += kNC) {
-            const uint64_t k = src[i];
-            if ((k & mask) == prefix) atomicAdd(&st.hist[(uint32_t)(k >> shift) & 255u], 1u);
+        for (uint32_t c0 = 0; c0 < n; c0 += 4 * kNC) {  // four loads in flight per thread
+            uint64_t k[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t i = c0 + j * kNC + ctid;
+                k[j] = i < n ? src[i] : 0ull;
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (c0 + j * kNC + ctid < n && (k[j] & mask) == prefix)
+                    atomicAdd(&st.hist[(uint32_t)(k[j] >> shift) & 255u], 1u);
         }
         csync();
         const uint32_t h = st.hist[255 - ctid];
@@ -2778,8 +2809,11 @@ __device__ uint64_t select_threshold_global(CandState& st, const uint64_t* src, 
     return st.thr;
 }
 
-// Stable LSD radix sort of a[0..n) descending; b is scratch of n keys.  Eight
-// passes, so the result ends in a.  Per-warp digit counters live in wcnt.
+// Stable LSD radix sort of a[0..n) descending; b is scratch of n keys.  The keys
+// arrive in ascending id order, that is already descending in their low 32 bits
+// (~id), so a stable sort on the upper 32 bits (the value order) alone orders them
+// completely: four passes, so the result ends in a.  Per-warp digit counters live
+// in wcnt.
 __device__ void radix_sort_desc_global(CandState& st, uint32_t* wcnt, uint64_t* a, uint64_t* b,
                                        uint32_t n, int ctid) {
     const int lane = ctid & 31, warp = ctid >> 5;
@@ -2787,13 +2821,22 @@ __device__ void radix_sort_desc_global(CandState& st, uint32_t* wcnt, uint64_t* 
     const uint32_t w0 = min(n, (uint32_t)warp * seg), w1 = min(n, w0 + seg);
     uint64_t* src = a;
     uint64_t* dst = b;
-    for (int pass = 0; pass < 8; ++pass) {
+    for (int pass = 4; pass < 8; ++pass) {
         const int shift = 8 * pass;
         for (int i = ctid; i < kConsumerWarps * 256; i += kNC) wcnt[i] = 0u;
         csync();
-        for (uint32_t i = w0 + lane; i < w1; i += 32) {
-            const uint32_t d = 255u - ((uint32_t)(src[i] >> shift) & 255u);
-            atomicAdd(&wcnt[warp * 256 + d], 1u);
+        // four 32-key groups per round: their loads are in flight together
+        for (uint32_t c0 = w0; c0 < w1; c0 += 128) {
+            uint64_t k[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t i = c0 + 32 * j + lane;
+                k[j] = i < w1 ? src[i] : 0ull;
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (c0 + 32 * j + lane < w1)
+                    atomicAdd(&wcnt[warp * 256 + (255u - ((uint32_t)(k[j] >> shift) & 255u))], 1u);
         }
         csync();
         uint32_t tot_d = 0;
@@ -2806,17 +2849,32 @@ __device__ void radix_sort_desc_global(CandState& st, uint32_t* wcnt, uint64_t* 
             base += c;
         }
         csync();
-        for (uint32_t c0 = w0; c0 < w1; c0 += 32) {
-            const uint32_t i = c0 + lane;
-            const bool valid = i < w1;
-            const uint64_t k = valid ? src[i] : 0ull;
-            const uint32_t d = valid ? 255u - ((uint32_t)(k >> shift) & 255u) : 256u + lane;
-            const unsigned peers = __match_any_sync(kFull, d);
-            const uint32_t rank = __popc(peers & lanemask_lt());
-            if (valid) dst[wcnt[warp * 256 + d] + rank] = k;
-            __syncwarp();
-            if (valid && rank == 0) wcnt[warp * 256 + d] += __popc(peers);
-            __syncwarp();
+        for (uint32_t c0 = w0; c0 < w1; c0 += 128) {
+            uint64_t kb[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t i = c0 + 32 * j + lane;
+                kb[j] = i < w1 ? src[i] : 0ull;
+            }
+            // the groups in order, so equal digits keep their order (stable)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const bool valid = c0 + 32 * j + lane < w1;
+                const uint64_t k = kb[j];
+                const uint32_t d = 255u - ((uint32_t)(k >> shift) & 255u);
+                // lanes holding the same digit: one ballot per digit bit
+                unsigned peers = __ballot_sync(kFull, valid);
+#pragma unroll
+                for (int b = 0; b < 8; ++b) {
+                    const unsigned bb = __ballot_sync(kFull, (d >> b) & 1u);
+                    peers &= ((d >> b) & 1u) ? bb : ~bb;
+                }
+                const uint32_t rank = __popc(peers & lanemask_lt());
+                if (valid) dst[wcnt[warp * 256 + d] + rank] = k;
+                __syncwarp();
+                if (valid && rank == 0) wcnt[warp * 256 + d] += __popc(peers);
+                __syncwarp();
+            }
         }
         csync();
         uint64_t* t = src;
@@ -2840,7 +2898,19 @@ __global__ void __launch_bounds__(kNC) zs_large_kernel(const Args a) {
                                     a.hist_len, a.hist_ld, row);
         if (!rp.large) continue;
         const float* x = a.logits + (int64_t)row * a.ld;
-        for (int i = ctid; i < a.V; i += kNC) keys[i] = make_key(x[i], a.id_offset + i);
+        for (int c0 = 0; c0 < a.V; c0 += 4 * kNC) {  // four loads in flight, then the stores
+            float v[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int i = c0 + j * kNC + ctid;
+                v[j] = i < a.V ? x[i] : 0.0f;
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int i = c0 + j * kNC + ctid;
+                if (i < a.V) keys[i] = make_key(v[j], a.id_offset + i);
+            }
+        }
         __threadfence_block();
         csync();
         if (rp.penal && ctid == 0) {
@@ -2875,7 +2945,19 @@ __global__ void __launch_bounds__(kNC) zs_large_kernel(const Args a) {
         if (kk < n) T = select_threshold_global(st, keys, n, kk, ctid);
         uint32_t base = 0;
         if (kk == n) {  // every key is kept: copy, the sort orders them
-            for (uint32_t i = ctid; i < n; i += kNC) tmp[i] = keys[i];
+            for (uint32_t c0 = 0; c0 < n; c0 += 4 * kNC) {
+                uint64_t k4[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t i = c0 + j * kNC + ctid;
+                    k4[j] = i < n ? keys[i] : 0ull;
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t i = c0 + j * kNC + ctid;
+                    if (i < n) tmp[i] = k4[j];
+                }
+            }
             base = n;
         }
         for (uint32_t c0 = (kk == n) ? n : 0; c0 < n; c0 += kNC) {
