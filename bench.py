@@ -356,6 +356,14 @@ def main():
         run_reference_arm(args, rank, world)
         return
 
+    # With several ranks, libraries (NCCL's version banner) may write to stdout; keep
+    # stdout for the one JSON line and send everything else written there to stderr.
+    json_out = sys.stdout
+    if world > 1:
+        sys.stdout.flush()
+        json_out = os.fdopen(os.dup(1), "w")
+        os.dup2(2, 1)
+
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -644,7 +652,7 @@ def main():
             line["lmhead_fused"] = lmhead
         if fullp:
             line["full_vocab_top_p"] = fullp
-        print(json.dumps(line), flush=True)
+        print(json.dumps(line), file=json_out, flush=True)
 
     s.close()
     if world > 1:
