@@ -2883,6 +2883,54 @@ __device__ void radix_sort_desc_global(CandState& st, uint32_t* wcnt, uint64_t* 
     }
 }
 
+// Copies the keys of src[0..n) that are >= T to dst, in their order; returns how
+// many.  Each warp owns a contiguous segment: it counts its keys first, the warp
+// counts are scanned, then it writes them at its offset (ballot prefix per 32).
+__device__ uint32_t ordered_compact_ge(CandState& st, const uint64_t* src, uint32_t n, uint64_t T,
+                                       uint64_t* dst, int ctid) {
+    const int lane = ctid & 31, warp = ctid >> 5;
+    const uint32_t seg = ((n + kConsumerWarps - 1) / kConsumerWarps + 31) & ~31u;
+    const uint32_t w0 = min(n, (uint32_t)warp * seg), w1 = min(n, w0 + seg);
+    uint32_t cnt = 0;
+    for (uint32_t c0 = w0; c0 < w1; c0 += 128) {
+        uint64_t k[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t i = c0 + 32 * j + lane;
+            k[j] = i < w1 ? src[i] : 0ull;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            cnt += __popc(__ballot_sync(kFull, c0 + 32 * j + lane < w1 && k[j] >= T));
+    }
+    if (lane == 0) st.scan[warp] = cnt;
+    csync();
+    uint32_t base = 0, total = 0;
+    for (int w = 0; w < kConsumerWarps; ++w) {
+        const uint32_t c = st.scan[w];
+        if (w < warp) base += c;
+        total += c;
+    }
+    const unsigned below = lanemask_lt();
+    for (uint32_t c0 = w0; c0 < w1; c0 += 128) {
+        uint64_t k[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t i = c0 + 32 * j + lane;
+            k[j] = i < w1 ? src[i] : 0ull;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const bool f = c0 + 32 * j + lane < w1 && k[j] >= T;
+            const unsigned b = __ballot_sync(kFull, f);
+            if (f) dst[base + __popc(b & below)] = k[j];
+            base += __popc(b);
+        }
+    }
+    csync();  // st.scan is free again, dst is written
+    return total;
+}
+
 template <bool LSE>
 __global__ void __launch_bounds__(kNC) zs_large_kernel(const Args a) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -2960,15 +3008,8 @@ __global__ void __launch_bounds__(kNC) zs_large_kernel(const Args a) {
             }
             base = n;
         }
-        for (uint32_t c0 = (kk == n) ? n : 0; c0 < n; c0 += kNC) {
-            const uint32_t i = c0 + ctid;
-            const uint64_t k = i < n ? keys[i] : 0ull;
-            const uint32_t f = (i < n && k >= T) ? 1u : 0u;
-            uint32_t tot;
-            const uint32_t incl = block_incl_scan(f, st.scan, ctid, tot);
-            if (f) tmp[base + incl - 1] = k;
-            base += tot;
-        }
+        if (kk < n) base = ordered_compact_ge(st, keys, n, T, tmp, ctid);
+        ZS_CHECK(base == kk, 22, base);  // unique keys: exactly kk are >= the kk-th
         __threadfence_block();
         csync();
         radix_sort_desc_global(st, wcnt, tmp, keys, kk, ctid);
