@@ -929,12 +929,23 @@ __device__ void finalize_blocked(CandState& st, const uint64_t* cand, double* pr
     }
     csync();
     const double sum = st.d_sum;
-    for (uint32_t i = ctid; i < kk; i += kNC) {
-        const double pi = prob[i] / sum;
-        prob[i] = pi;
-        if ((int32_t)i < cand_ld) {
-            if (cand_ids) cand_ids[(int64_t)row * cand_ld + i] = key_id(cand[i]);
-            if (cand_probs) cand_probs[(int64_t)row * cand_ld + i] = pi;
+    for (uint32_t c0 = 0; c0 < kk; c0 += 4 * kNC) {  // loads ahead of the stores
+        double e4[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t i = c0 + j * kNC + ctid;
+            e4[j] = i < kk ? prob[i] : 0.0;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t i = c0 + j * kNC + ctid;
+            if (i >= kk) continue;
+            const double pi = e4[j] / sum;
+            prob[i] = pi;
+            if ((int32_t)i < cand_ld) {
+                if (cand_ids) cand_ids[(int64_t)row * cand_ld + i] = key_id(cand[i]);
+                if (cand_probs) cand_probs[(int64_t)row * cand_ld + i] = pi;
+            }
         }
     }
     csync();
@@ -1054,9 +1065,23 @@ __device__ void finalize_row(CandState& st, const uint64_t* cand, double* prob, 
     const float max_l = (x0_nan || kk == 0) ? __int_as_float(0x7fc00000) : key_value(cand[0]);
     if (kk > kBlockedTail) {
         // long shortlists: the exponent in double, exp itself in f32 (relative
-        // error about 1e-7, far inside the 1e-5 probability rule)
-        for (uint32_t i = ctid; i < kk; i += kNC)
-            prob[i] = (double)expf((float)(((double)key_value(cand[i]) - (double)max_l) * (double)inv_temp));
+        // error about 1e-7, far inside the 1e-5 probability rule); four keys loaded
+        // ahead of the stores, which may alias them as far as the compiler knows
+        for (uint32_t c0 = 0; c0 < kk; c0 += 4 * kNC) {
+            uint64_t k4[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t i = c0 + j * kNC + ctid;
+                k4[j] = i < kk ? cand[i] : 0ull;
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t i = c0 + j * kNC + ctid;
+                if (i < kk)
+                    prob[i] = (double)expf(
+                        (float)(((double)key_value(k4[j]) - (double)max_l) * (double)inv_temp));
+            }
+        }
     } else {
         for (uint32_t i = ctid; i < kk; i += kNC)
             prob[i] = exp(((double)key_value(cand[i]) - (double)max_l) * (double)inv_temp);
