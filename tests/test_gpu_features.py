@@ -371,3 +371,15 @@ def test_full_vocab_top_p_against_reference(sampler):
     ref, _ = oracle.reference_sample(x, p, seeds)
     near = o["info"]["boundary"] < BOUNDARY_EPS
     assert np.array_equal(g["ids"][~near], ref[~near])
+
+
+@pytest.mark.parametrize("k", [3000, V])
+def test_large_top_k_ties(sampler, k):
+    """The large-shortlist path on heavily tied rows (workload 4: values on a 0.125
+    grid): the shortlist order among equal values (id ascending) is the sort's
+    stability, checked entry by entry against the restatement."""
+    rows = 6
+    x = W.generate(4, rows, row0=31)
+    p = SamplingParams(temp=0.8, top_k=k, top_p=0.9)
+    st = _states(range(rows))
+    compare(run_gpu(sampler, x, p, st, cand_ld=6000), run_oracle(x, p, st, cand_ld=6000))
