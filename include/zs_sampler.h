@@ -172,6 +172,17 @@ zs_status zs_lmhead_sample(zs_handle h, const float* hidden, int64_t hidden_ld,
                            const int32_t* history_len, uint64_t* rng_state, int32_t* out_ids,
                            float* out_logits, int64_t logits_ld, void* stream);
 
+/* The lm_head alone: the last two lines of Model::eval (src/model.cpp:401-403),
+ *   out_logits[r] = matvec(rmsnorm(hidden_r, norm_w, eps), weight)
+ * for `batch` rows on the tensor cores, with the same arithmetic (bf16 xn and
+ * weight, f32 accumulation) and the same argument rules as zs_lmhead_sample;
+ * out_logits (device f32 [batch][logits_ld]) is required.  Sample the result with
+ * zs_sample when the shortlist cannot be taken in the GEMM's epilogue. */
+zs_status zs_lmhead_logits(zs_handle h, const float* hidden, int64_t hidden_ld,
+                           const float* norm_w, float eps, const void* weight, int32_t batch,
+                           int32_t n_embd, int32_t n_vocab, float* out_logits, int64_t logits_ld,
+                           void* stream);
+
 /* Batched argmax_token (src/sample.cpp:24-30): first index of the maximum; a NaN at
  * index 0 yields 0.  No penalty, no draw. */
 zs_status zs_argmax(zs_handle h, const float* logits, int64_t ld, int32_t batch, int32_t n_vocab,

@@ -196,3 +196,21 @@ def test_lmhead_rejects_bad_shapes(sampler):
     with pytest.raises(SamplerError):  # hidden size below one K stage
         sampler.lmhead_sample(torch.zeros((1, 60), device=dev), torch.ones(60, device=dev), w,
                               SamplingParams(), None)
+
+
+def test_lmhead_logits_alone(sampler):
+    """zs_lmhead_logits (the lm_head without sampling) writes the same logits as the
+    fused entry's logits output, bit for bit, and they are within the bound of the
+    restatement."""
+    V, E, B = 151936, 896, 40
+    w, nw = _model(V, E)
+    hidden = _hidden(B, E, 33)
+    p = SamplingParams(temp=0.7, top_k=50, top_p=0.9)
+    seeds = np.arange(B, dtype=np.uint64) + np.uint64(3)
+    res = _run(sampler, hidden, nw, w, p, seeds)
+    dev = sampler.device
+    lg = sampler.lmhead_logits(hidden.to(dev), nw.to(dev), w.to(dev), eps=EPS)
+    sampler.check_device_status()
+    got = lg.cpu().numpy()
+    assert np.array_equal(got, res["logits"])
+    _check_logits(got, hidden, nw, w, np.array([0, 1, B - 1]))

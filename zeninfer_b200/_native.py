@@ -18,7 +18,7 @@ EXPORTS = (
     "zs_rng_seed", "zs_sample", "zs_argmax", "zs_check_device_status",
     "zs_shard_partial_bytes", "zs_shard_partials", "zs_shard_merge", "zs_sample_sharded",
     "zs_sample_noalloc", "zs_set_timing", "zs_get_timing", "zs_logits_stats",
-    "zs_selftest_wait_timeout", "zs_decode_step", "zs_lmhead_sample",
+    "zs_selftest_wait_timeout", "zs_decode_step", "zs_lmhead_sample", "zs_lmhead_logits",
 )
 
 ZS_OK = 0
@@ -85,6 +85,7 @@ def lib() -> C.CDLL:
     L.zs_sample_sharded.argtypes = [vp, vp, i64, i32, i32, i32, i32, i32, C.POINTER(ZsParams), i32,
                                     vp, i64, vp, vp, vp, C.POINTER(ZsExtras), vp, vp]
     L.zs_selftest_wait_timeout.argtypes = [vp, vp]
+    L.zs_lmhead_logits.argtypes = [vp, vp, i64, vp, C.c_float, vp, i32, i32, i32, vp, i64, vp]
     L.zs_lmhead_sample.argtypes = [vp, vp, i64, vp, C.c_float, vp, i32, i32, i32,
                                    C.POINTER(ZsParams), i32, vp, i64, vp, vp, vp, vp, i64, vp]
     L.zs_decode_step.argtypes = [vp, vp, i64, i32, i32, C.POINTER(ZsParams), i32, vp, i64, vp, vp,
@@ -102,7 +103,8 @@ def lib() -> C.CDLL:
                                             "zs_sample_sharded", "zs_sample_noalloc",
                                             "zs_set_timing", "zs_get_timing",
                                             "zs_logits_stats", "zs_selftest_wait_timeout",
-                                            "zs_decode_step", "zs_lmhead_sample"):
+                                            "zs_decode_step", "zs_lmhead_sample",
+                                            "zs_lmhead_logits"):
             f.restype = C.c_int
     _lib = L
     return L

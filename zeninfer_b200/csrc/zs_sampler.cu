@@ -853,6 +853,89 @@ int lm_slices(int mt, int nt, int ctas, int cap) {
 
 }  // namespace
 
+namespace {
+
+// Checks shared by the lm_head entry points.
+zs_status lm_validate(zs_handle h, const float* hidden, int64_t hidden_ld, const float* norm_w,
+                      const void* weight, int32_t n_embd, int32_t n_vocab, const float* out_logits,
+                      int64_t logits_ld) {
+    if (!hidden || !norm_w || !weight)
+        return fail(ZS_ERR_INVALID_ARGUMENT, "hidden, norm_w and weight are required");
+    if (n_vocab < 1) return fail(ZS_ERR_INVALID_ARGUMENT, "n_vocab < 1");
+    if (n_embd < zs::kLmBK || n_embd % 8 != 0 || n_embd > 12288)
+        return fail(ZS_ERR_INVALID_ARGUMENT, "n_embd must be a multiple of 8 from 64 to 12288");
+    if (hidden_ld < n_embd) return fail(ZS_ERR_INVALID_ARGUMENT, "hidden_ld < n_embd");
+    if (((uintptr_t)weight & 15u) != 0) return fail(ZS_ERR_INVALID_ARGUMENT, "weight not 16-byte aligned");
+    if (((uintptr_t)hidden & 3u) != 0 || ((uintptr_t)norm_w & 3u) != 0)
+        return fail(ZS_ERR_INVALID_ARGUMENT, "hidden or norm_w not 4-byte aligned");
+    if (out_logits && (logits_ld < n_vocab || ((uintptr_t)out_logits & 15u) != 0 || logits_ld % 4 != 0))
+        return fail(ZS_ERR_INVALID_ARGUMENT,
+                    "out_logits needs logits_ld >= n_vocab, a multiple of 4, 16-byte alignment");
+    if (zs::kLmSmemBytes > 232448) return fail(ZS_ERR_NO_DEVICE, "lm_head tiles do not fit");
+    return ZS_OK;
+}
+
+// rmsnorm into the handle's bf16 rows, then zs_lmhead_kernel over `a` (whose B, E,
+// V, S, select, parameters and outputs the caller has set).
+zs_status lm_run(zs_context* h, const float* hidden, int64_t hidden_ld, const float* norm_w,
+                 float eps, const void* weight, zs::LmArgs& a, cudaStream_t st) {
+    zs_status s = grow((void**)&h->lm_xn, &h->lm_xn_bytes, (size_t)a.B * a.E * 2);
+    if (s != ZS_OK) return s;
+    CUtensorMap tm_a, tm_b;
+    s = lm_tensor_map(h, &tm_a, h->lm_xn, a.B, a.E);
+    if (s == ZS_OK) s = lm_tensor_map(h, &tm_b, weight, a.V, a.E);
+    if (s != ZS_OK) return s;
+    a.status = h->status;
+    {
+        LaunchScope scope(h, 4, st);
+        // warps per CTA: as many rows as fit 48 KB of staged floats, at most 8
+        const int nw = (int)std::max<int64_t>(1, std::min<int64_t>(8, (48 << 10) / ((int64_t)a.E * 4)));
+        const size_t smem = (size_t)nw * a.E * sizeof(float);
+        const int grid = (int)std::min<int64_t>((a.B + nw - 1) / nw, (int64_t)h->num_sms * 16);
+        zs::zs_lm_rmsnorm_kernel<<<grid, nw * 32, smem, st>>>(
+            hidden, hidden_ld, norm_w, eps, a.B, a.E, reinterpret_cast<__nv_bfloat16*>(h->lm_xn));
+        ZS_CUDA(cudaGetLastError());
+    }
+    {
+        LaunchScope scope(h, 3, st);
+        const int grid = std::min(a.n_units, h->num_sms);
+        zs::zs_lmhead_kernel<<<grid, zs::kLmThreads, zs::kLmSmemBytes, st>>>(tm_a, tm_b, a);
+        ZS_CUDA(cudaGetLastError());
+    }
+    return ZS_OK;
+}
+
+}  // namespace
+
+zs_status zs_lmhead_logits(zs_handle h, const float* hidden, int64_t hidden_ld,
+                           const float* norm_w, float eps, const void* weight, int32_t batch,
+                           int32_t n_embd, int32_t n_vocab, float* out_logits, int64_t logits_ld,
+                           void* stream) {
+    if (!h) return fail(ZS_ERR_INVALID_ARGUMENT, "null handle");
+    if (batch < 0) return fail(ZS_ERR_INVALID_ARGUMENT, "batch < 0");
+    if (batch == 0) return ZS_OK;
+    if (!out_logits) return fail(ZS_ERR_INVALID_ARGUMENT, "out_logits is required");
+    zs_status s = lm_validate(h, hidden, hidden_ld, norm_w, weight, n_embd, n_vocab, out_logits,
+                              logits_ld);
+    if (s != ZS_OK) return s;
+    DeviceGuard g(h->device);
+    if (!g.ok) return fail(ZS_ERR_CUDA, "cudaSetDevice failed");
+    zs::LmArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.B = batch;
+    a.E = n_embd;
+    a.V = n_vocab;
+    a.V_total = n_vocab;
+    a.mt = (batch + zs::kLmM - 1) / zs::kLmM;
+    a.nt = (n_vocab + zs::kLmN - 1) / zs::kLmN;
+    a.S = lm_slices(a.mt, a.nt, h->num_sms, 1024);
+    a.n_units = a.mt * a.S;
+    a.select = 0;
+    a.out_logits = out_logits;
+    a.logits_ld = logits_ld;
+    return lm_run(h, hidden, hidden_ld, norm_w, eps, weight, a, (cudaStream_t)stream);
+}
+
 zs_status zs_lmhead_sample(zs_handle h, const float* hidden, int64_t hidden_ld,
                            const float* norm_w, float eps, const void* weight, int32_t batch,
                            int32_t n_embd, int32_t n_vocab, const zs_params* params,
@@ -863,19 +946,10 @@ zs_status zs_lmhead_sample(zs_handle h, const float* hidden, int64_t hidden_ld,
     if (!params) return fail(ZS_ERR_INVALID_ARGUMENT, "params is null");
     if (batch < 0) return fail(ZS_ERR_INVALID_ARGUMENT, "batch < 0");
     if (batch == 0) return ZS_OK;
-    if (!hidden || !norm_w || !weight || !out_ids)
-        return fail(ZS_ERR_INVALID_ARGUMENT, "hidden, norm_w, weight and out_ids are required");
-    if (n_vocab < 1) return fail(ZS_ERR_INVALID_ARGUMENT, "n_vocab < 1");
-    if (n_embd < zs::kLmBK || n_embd % 8 != 0)
-        return fail(ZS_ERR_INVALID_ARGUMENT, "n_embd must be a multiple of 8 and at least 64");
-    if (hidden_ld < n_embd) return fail(ZS_ERR_INVALID_ARGUMENT, "hidden_ld < n_embd");
-    if (((uintptr_t)weight & 15u) != 0) return fail(ZS_ERR_INVALID_ARGUMENT, "weight not 16-byte aligned");
-    if (((uintptr_t)hidden & 3u) != 0 || ((uintptr_t)norm_w & 3u) != 0)
-        return fail(ZS_ERR_INVALID_ARGUMENT, "hidden or norm_w not 4-byte aligned");
-    if (out_logits && (logits_ld < n_vocab || ((uintptr_t)out_logits & 15u) != 0 || logits_ld % 4 != 0))
-        return fail(ZS_ERR_INVALID_ARGUMENT,
-                    "out_logits needs logits_ld >= n_vocab, a multiple of 4, 16-byte alignment");
-    if (zs::kLmSmemBytes > 232448) return fail(ZS_ERR_NO_DEVICE, "lm_head tiles do not fit");
+    if (!out_ids) return fail(ZS_ERR_INVALID_ARGUMENT, "out_ids is required");
+    zs_status s = lm_validate(h, hidden, hidden_ld, norm_w, weight, n_embd, n_vocab, out_logits,
+                              logits_ld);
+    if (s != ZS_OK) return s;
     if (!rng_state && needs_rng(params, params_per_row, batch))
         return fail(ZS_ERR_INVALID_ARGUMENT, "rng_state is null");
     const bool have_hist = history && history_len;
@@ -897,8 +971,6 @@ zs_status zs_lmhead_sample(zs_handle h, const float* hidden, int64_t hidden_ld,
         if (have_hist && p.repeat_penalty != 1.0f && p.repeat_last_n > 0) fused = false;
     }
 
-    zs_status s = grow((void**)&h->lm_xn, &h->lm_xn_bytes, (size_t)batch * n_embd * 2);
-    if (s != ZS_OK) return s;
     float* logits = out_logits;
     int64_t lld = logits_ld;
     if (!fused && !logits) {
@@ -907,11 +979,6 @@ zs_status zs_lmhead_sample(zs_handle h, const float* hidden, int64_t hidden_ld,
         if (s != ZS_OK) return s;
         logits = reinterpret_cast<float*>(h->lm_logits);
     }
-    CUtensorMap tm_a, tm_b;
-    s = lm_tensor_map(h, &tm_a, h->lm_xn, batch, n_embd);
-    if (s == ZS_OK) s = lm_tensor_map(h, &tm_b, weight, n_vocab, n_embd);
-    if (s != ZS_OK) return s;
-
     zs::LmArgs a;
     std::memset(&a, 0, sizeof(a));
     a.B = batch;
@@ -932,30 +999,13 @@ zs_status zs_lmhead_sample(zs_handle h, const float* hidden, int64_t hidden_ld,
     a.row_params = dparams;
     a.out_logits = logits;
     a.logits_ld = lld;
-    a.status = h->status;
     if (fused) {
         s = grow((void**)&h->part, &h->part_bytes, (size_t)batch * a.S * zs::kLmPartStride);
         if (s != ZS_OK) return s;
         a.part = h->part;
     }
-    {
-        LaunchScope scope(h, 4, st);
-        // warps per CTA: as many rows as fit 48 KB of staged floats, at most 8
-        const int nw = (int)std::max<int64_t>(1, std::min<int64_t>(8, (48 << 10) / ((int64_t)n_embd * 4)));
-        const size_t smem = (size_t)nw * n_embd * sizeof(float);
-        if (smem > (48u << 10)) return fail(ZS_ERR_INVALID_ARGUMENT, "n_embd too large for rmsnorm staging");
-        const int grid = (int)std::min<int64_t>((batch + nw - 1) / nw, (int64_t)h->num_sms * 16);
-        zs::zs_lm_rmsnorm_kernel<<<grid, nw * 32, smem, st>>>(
-            hidden, hidden_ld, norm_w, eps, batch, n_embd,
-            reinterpret_cast<__nv_bfloat16*>(h->lm_xn));
-        ZS_CUDA(cudaGetLastError());
-    }
-    {
-        LaunchScope scope(h, 3, st);
-        const int grid = std::min(a.n_units, h->num_sms);
-        zs::zs_lmhead_kernel<<<grid, zs::kLmThreads, zs::kLmSmemBytes, st>>>(tm_a, tm_b, a);
-        ZS_CUDA(cudaGetLastError());
-    }
+    s = lm_run(h, hidden, hidden_ld, norm_w, eps, weight, a, st);
+    if (s != ZS_OK) return s;
     if (!fused)
         return zs_sample(h, logits, lld, batch, n_vocab, params, params_per_row, history,
                          history_ld, history_len, rng_state, out_ids, nullptr, stream);

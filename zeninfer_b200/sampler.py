@@ -268,6 +268,32 @@ class Sampler:
             rng_ptr, out.data_ptr(), lptr, lld, _stream_ptr(stream)), "zs_lmhead_sample")
         return out
 
+    def lmhead_logits(self, hidden, norm_w, weight, eps: float = 1e-6, out=None, stream=None):
+        """The lm_head alone (rmsnorm with `norm_w`, then hidden . weight^T on the
+        tensor cores; src/model.cpp:401-403) for every row of `hidden` ([B, E] float32
+        CUDA); weight bfloat16 CUDA [V, E].  Returns float32 logits [B, V] (or fills
+        `out`, whose row stride must be a multiple of 4)."""
+        import torch
+        if hidden.dim() == 1:
+            hidden = hidden.unsqueeze(0)
+        if hidden.dtype != torch.float32 or hidden.stride(1) != 1 or hidden.device != self.device:
+            raise ValueError("hidden must be float32 with unit column stride on the sampler's device")
+        if weight.dtype != torch.bfloat16 or not weight.is_contiguous() or weight.dim() != 2:
+            raise ValueError("weight must be a contiguous bfloat16 [V, E] tensor")
+        B, E = hidden.shape
+        V = weight.shape[0]
+        if weight.shape[1] != E or norm_w.numel() != E or norm_w.dtype != torch.float32:
+            raise ValueError("weight [V, E] and norm_w [E] float32 must match hidden's E")
+        if out is None:
+            out = torch.empty((B, (V + 3) // 4 * 4), dtype=torch.float32, device=self.device)[:, :V]
+        if out.dtype != torch.float32 or out.stride(1) != 1:
+            raise ValueError("out must be float32 with unit column stride")
+        _native.check(self._lib.zs_lmhead_logits(
+            self._h, hidden.data_ptr(), hidden.stride(0), norm_w.contiguous().data_ptr(),
+            float(eps), weight.data_ptr(), B, E, V, out.data_ptr(), out.stride(0),
+            _stream_ptr(stream)), "zs_lmhead_logits")
+        return out
+
     def argmax(self, logits, out=None, stream=None):
         """argmax_token per row."""
         import torch
