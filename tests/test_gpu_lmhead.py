@@ -198,11 +198,12 @@ def test_lmhead_rejects_bad_shapes(sampler):
                               SamplingParams(), None)
 
 
-def test_lmhead_logits_alone(sampler):
+@pytest.mark.parametrize("B", [40, 300])
+def test_lmhead_logits_alone(sampler, B):
     """zs_lmhead_logits (the lm_head without sampling) writes the same logits as the
     fused entry's logits output, bit for bit, and they are within the bound of the
-    restatement."""
-    V, E, B = 151936, 896, 40
+    restatement; 40 rows store directly, 300 rows through shared memory and TMA."""
+    V, E = 151936, 896
     w, nw = _model(V, E)
     hidden = _hidden(B, E, 33)
     p = SamplingParams(temp=0.7, top_k=50, top_p=0.9)

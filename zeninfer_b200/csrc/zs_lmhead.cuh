@@ -73,6 +73,7 @@ struct LmArgs {
     uint8_t* part;               // [B][S] blocks of kLmPartStride bytes
     float* out_logits;           // optional [B][logits_ld]
     int64_t logits_ld;
+    int32_t tma_out;             // logits only: staged in shared memory, stored by TMA
     int* status;
 };
 
@@ -84,6 +85,26 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
         : "memory");
+}
+
+// Shared -> global tile store (no multicast); completion tracked by bulk groups.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int32_t x,
+                                             int32_t y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(smem_addr(src))
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Waits until at most one committed store is still reading shared memory.
+__device__ __forceinline__ void bulk_wait_read_1() {
+    asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+// Waits until every committed store has completed.
+__device__ __forceinline__ void bulk_wait_all() {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 __device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {
@@ -307,7 +328,8 @@ __device__ __forceinline__ void lm_chunk(const uint32_t (&r)[32], int col0, int 
 
 __global__ void __launch_bounds__(kLmThreads, 1)
     zs_lmhead_kernel(const __grid_constant__ CUtensorMap tm_a,
-                     const __grid_constant__ CUtensorMap tm_b, const LmArgs a) {
+                     const __grid_constant__ CUtensorMap tm_b,
+                     const __grid_constant__ CUtensorMap tm_c, const LmArgs a) {
     extern __shared__ uint8_t lm_raw[];
     const uint32_t pad = (1024u - (smem_addr(lm_raw) & 1023u)) & 1023u;
     LmSmem& sm = *reinterpret_cast<LmSmem*>(lm_raw + pad);
@@ -435,6 +457,7 @@ __global__ void __launch_bounds__(kLmThreads, 1)
         float tau_f = 0.0f;    // its value
         bool open = true;      // no threshold yet: every column enters
         bool x0nan = false, has0 = false;
+        int stg_buf = 0;  // logits-only staging buffer of this warp (two, alternating)
         for (int u = u_begin; ok && u < u_end; ++u) {
             int m, s, t0, t1;
             lm_unit(a, u, m, s, t0, t1);
@@ -471,6 +494,27 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                     __syncwarp();
                     tc_ld32_issue(base + (uint32_t)(c * 32), ra);
                     tc_ld_wait(ra);
+                    if (a.tma_out) {
+                        // logits only: this warp's 32 rows x 32 columns go to a staging
+                        // buffer in the (here unused) candidate area, in the 128-byte
+                        // swizzled layout of the output tensor map, then one TMA store
+                        uint8_t* stg = reinterpret_cast<uint8_t*>(sm.cand) + (q * 2 + stg_buf) * 4096;
+                        if (lane == 0) bulk_wait_read_1();  // the store two chunks ago read it
+                        __syncwarp();
+                        uint8_t* my = stg + lane * 128;
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            *reinterpret_cast<uint4*>(my + ((j ^ (lane & 7)) << 4)) =
+                                make_uint4(ra[4 * j], ra[4 * j + 1], ra[4 * j + 2], ra[4 * j + 3]);
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) {
+                            tma_store_2d(&tm_c, stg, tcol + c * 32, m * kLmM + q * 32);
+                            bulk_commit_group();
+                        }
+                        stg_buf ^= 1;
+                        continue;
+                    }
                     lm_chunk(ra, tcol + c * 32, a.V, sel, lrow, x0nan, a.select, rows, mine, count,
                              tau_ord, tau_f, open, keff, lane);
                 }
@@ -507,6 +551,8 @@ __global__ void __launch_bounds__(kLmThreads, 1)
             }
         }
         if (!ok) set_status(a.status, kStatusTimeout);
+        if (a.tma_out && lane == 0) bulk_wait_all();  // stores done before the CTA exits
+        __syncwarp();
     }
 
     tc_fence_before();

@@ -809,10 +809,11 @@ zs_status zs_decode_step(zs_handle h, const float* logits, int64_t ld, int32_t b
 
 namespace {
 
-// A 2-D bf16 tensor map over rows x cols (row-major, cols contiguous) with boxes
-// of 128 rows x 64 columns and 128-byte swizzle, as zs_lmhead_kernel reads them.
+// A 2-D tensor map over rows x cols (row-major, cols contiguous, rows `ld` elements
+// apart) with 128-byte swizzle: bf16 boxes of 128 rows x 64 columns, as
+// zs_lmhead_kernel reads its operands, or (f32) boxes of 32 x 32, as it stores logits.
 zs_status lm_tensor_map(zs_context* h, CUtensorMap* map, const void* base, int64_t rows,
-                        int64_t cols) {
+                        int64_t cols, bool f32 = false, int64_t ld = 0) {
     if (!h->encode_tiled) {
         void* fn = nullptr;
         cudaDriverEntryPointQueryResult q;
@@ -822,11 +823,13 @@ zs_status lm_tensor_map(zs_context* h, CUtensorMap* map, const void* base, int64
             return fail(ZS_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
         h->encode_tiled = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     }
+    const int64_t esize = f32 ? 4 : 2;
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-    const cuuint32_t box[2] = {(cuuint32_t)zs::kLmBK, (cuuint32_t)zs::kLmM};
+    const cuuint64_t strides[1] = {(cuuint64_t)(ld > 0 ? ld : cols) * esize};
+    const cuuint32_t box[2] = {f32 ? 32u : (cuuint32_t)zs::kLmBK, f32 ? 32u : (cuuint32_t)zs::kLmM};
     const cuuint32_t estr[2] = {1, 1};
-    const CUresult r = h->encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base),
+    const CUresult r = h->encode_tiled(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                                       2, const_cast<void*>(base),
                                        dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -881,10 +884,20 @@ zs_status lm_run(zs_context* h, const float* hidden, int64_t hidden_ld, const fl
                  float eps, const void* weight, zs::LmArgs& a, cudaStream_t st) {
     zs_status s = grow((void**)&h->lm_xn, &h->lm_xn_bytes, (size_t)a.B * a.E * 2);
     if (s != ZS_OK) return s;
-    CUtensorMap tm_a, tm_b;
+    CUtensorMap tm_a, tm_b, tm_c;
     s = lm_tensor_map(h, &tm_a, h->lm_xn, a.B, a.E);
     if (s == ZS_OK) s = lm_tensor_map(h, &tm_b, weight, a.V, a.E);
     if (s != ZS_OK) return s;
+    // logits only: the epilogue stores 32 x 32 tiles by TMA (its candidate buffers
+    // are free); below 64 rows most of each tile is outside the batch and direct
+    // stores of the live rows are cheaper.  Otherwise tm_c is not used.
+    a.tma_out = (!a.select && a.out_logits && a.B >= 64) ? 1 : 0;
+    if (a.tma_out) {
+        s = lm_tensor_map(h, &tm_c, a.out_logits, a.B, a.V, true, a.logits_ld);
+        if (s != ZS_OK) return s;
+    } else {
+        tm_c = tm_a;
+    }
     a.status = h->status;
     {
         LaunchScope scope(h, 4, st);
@@ -899,7 +912,7 @@ zs_status lm_run(zs_context* h, const float* hidden, int64_t hidden_ld, const fl
     {
         LaunchScope scope(h, 3, st);
         const int grid = std::min(a.n_units, h->num_sms);
-        zs::zs_lmhead_kernel<<<grid, zs::kLmThreads, zs::kLmSmemBytes, st>>>(tm_a, tm_b, a);
+        zs::zs_lmhead_kernel<<<grid, zs::kLmThreads, zs::kLmSmemBytes, st>>>(tm_a, tm_b, tm_c, a);
         ZS_CUDA(cudaGetLastError());
     }
     return ZS_OK;
