@@ -131,3 +131,45 @@ def test_decode_step_rejects_short_history(sampler):
     sampler.decode_step(x, SamplingParams(temp=0.7, repeat_last_n=6), rng, done, 999999, hist, hlen)
     torch.cuda.synchronize()
     assert hlen.cpu().tolist() == [1, 1]
+
+
+def test_decode_steps_in_a_cuda_graph(sampler):
+    """Six steps of zs_decode_step captured once in a CUDA graph (after one eager
+    call has sized the handle's scratch) and replayed give the tokens, stop flags,
+    Rng states and histories of the same steps run eagerly."""
+    import torch
+    dev = sampler.device
+    B, T, hist_ld = 16, 6, 16
+    steps, _ = _case(B, T, seed_row0=7000)
+    p = SamplingParams(temp=0.7, top_k=40, top_p=0.9, repeat_penalty=1.2, repeat_last_n=8)
+    seeds = np.arange(B, dtype=np.uint64) + np.uint64(55)
+    xs = [torch.from_numpy(x).to(dev) for x in steps]
+
+    def fresh():
+        return {"rng": states_to_tensor([rng_seed(int(s)) for s in seeds], dev),
+                "done": torch.zeros(B, dtype=torch.int32, device=dev),
+                "hist": torch.zeros((B, hist_ld), dtype=torch.int32, device=dev),
+                "hlen": torch.zeros(B, dtype=torch.int32, device=dev),
+                "tok": torch.full((B, T), -2, dtype=torch.int32, device=dev)}
+
+    def run(st):
+        for t in range(T):
+            sampler.decode_step(xs[t], p, st["rng"], st["done"], EOS, st["hist"], st["hlen"],
+                                tokens=st["tok"], step=t)
+
+    eager = fresh()
+    run(eager)
+    warm = fresh()
+    sampler.decode_step(xs[0], p, warm["rng"], warm["done"], EOS, warm["hist"], warm["hlen"],
+                        tokens=warm["tok"], step=0)
+    torch.cuda.synchronize()
+    cap = fresh()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        run(cap)
+    graph.replay()
+    torch.cuda.synchronize()
+    sampler.check_device_status()
+    for k in ("tok", "done", "hist", "hlen"):
+        assert torch.equal(cap[k], eager[k]), k
+    assert np.array_equal(tensor_to_states(cap["rng"]), tensor_to_states(eager["rng"]))
