@@ -530,6 +530,21 @@ def main():
             msd = time_device_steps(dstep, reps, stream) / reps
             decode[f"gpu_us_per_step_b{b}"] = msd * 1e3
             decode[f"tokens_per_s_b{b}"] = b / (msd / 1e3)
+            # the same steps captured once in a CUDA graph (50 per graph) and replayed:
+            # no host launch gaps between the step's stream operations
+            try:
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    for _ in range(50):
+                        s.decode_step(xd, pdec, rngd, doned, -1, histd, hlend, out=outd)
+                graph.replay()
+                torch.cuda.synchronize()
+                reps_g = 10
+                msg = time_device_steps(graph.replay, reps_g, stream) / (reps_g * 50)
+                decode[f"gpu_us_per_step_b{b}_graph"] = msg * 1e3
+                del graph
+            except Exception as e:  # reported, never fatal
+                decode["graph_note"] = str(e)
         try:
             import oracle
             if oracle.have_reference():
