@@ -2629,7 +2629,22 @@ __global__ void __launch_bounds__(C::kWarps * 32, 1) zs_wselect_kernel(const Arg
         const RowPlan rp = plan_row(load_params(a.row_params, a.shared, pc.row), a.V_total, a.hist,
                                     a.hist_len, a.hist_ld, pc.row);
         const bool greedy_np = rp.greedy && !rp.penal;
-        const uint32_t keff = (uint32_t)rp.keff;
+        // A piece keeps its top (ksel + n) raw keys, n the window entries that fall in
+        // its own columns: a key that is not penalised and has ksel + n raw keys above
+        // it has at least ksel unpenalised keys above it after the penalty, so it
+        // cannot be in the row's shortlist; penalised ids are added back at the end.
+        uint32_t keff = (uint32_t)rp.keff;
+        if (rp.penal) {
+            const int32_t* window = a.hist + (int64_t)pc.row * a.hist_ld + (rp.hist_len - rp.win);
+            const int32_t lo = a.id_offset + pc.c0, hi = a.id_offset + pc.c1;
+            uint32_t n_in = 0;
+            for (int base = 0; base < rp.win; base += 32) {
+                const int jw = base + lane;
+                const int32_t gid = jw < rp.win ? window[jw] : -1;
+                n_in += __popc(__ballot_sync(kFull, gid >= lo && gid < hi));
+            }
+            keff = min(keff, (uint32_t)rp.ksel + n_in);
+        }
         const uint32_t compact_at =
             min((uint32_t)(C::kCap - kWStepElems), keff + (keff > 128u ? keff : 128u));
         const float lc = (rp.greedy ? 1.0f : 1.0f / rp.p.temp) * 1.4426950408889634f;
