@@ -1119,9 +1119,14 @@ __device__ void finalize_row(CandState& st, const uint64_t* cand, double* prob, 
                 acc += prob[m];
                 ++m;
             }
-            if (m == 0) m = 1;
-            rescale = 0.0;
-            for (int i = 0; i < m; ++i) rescale += prob[i];
+            // The reference's rescale loop adds prob[0..m) in the same order from 0,
+            // so its sum is acc itself (prob[0] when no entry was taken).
+            if (m == 0) {
+                m = 1;
+                rescale = prob[0];
+            } else {
+                rescale = acc;
+            }
         }
         st.m = m;
         st.d_rescale = rescale;
@@ -1253,16 +1258,28 @@ __device__ uint32_t merge_partials(CandState& st, const MergeArgs& a, const Bloc
             st.hist[ctid] = incl - c;
             st.prop[ctid] = reinterpret_cast<uint64_t>(pp);
             csync();
-            for (uint32_t i = ctid; i < tot; i += kNC) {
-                int lo = 0, hi = nb - 1;  // the last block starting at or before i
-                while (lo < hi) {
-                    const int mid = (lo + hi + 1) >> 1;
-                    if (st.hist[mid] <= i) lo = mid;
-                    else hi = mid - 1;
+            // four keys per thread per round: their loads are in flight together
+            for (uint32_t i0 = ctid; i0 < tot; i0 += 4 * kNC) {
+                unsigned long long kv[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t i = i0 + j * kNC;
+                    kv[j] = 0ull;
+                    if (i < tot) {
+                        int lo = 0, hi = nb - 1;  // the last block starting at or before i
+                        while (lo < hi) {
+                            const int mid = (lo + hi + 1) >> 1;
+                            if (st.hist[mid] <= i) lo = mid;
+                            else hi = mid - 1;
+                        }
+                        const unsigned long long* keys = reinterpret_cast<const unsigned long long*>(
+                            st.prop[lo] + kPartialHeaderBytes);
+                        kv[j] = __ldcg(keys + (i - st.hist[lo]));
+                    }
                 }
-                const unsigned long long* keys = reinterpret_cast<const unsigned long long*>(
-                    st.prop[lo] + kPartialHeaderBytes);
-                st.cand[i] = __ldcg(keys + (i - st.hist[lo]));
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (i0 + j * kNC < tot) st.cand[i0 + j * kNC] = kv[j];
             }
             block_lse(st, m, sx, lse_c, ctid);
             x0_nan = csync_or(z);
@@ -1997,9 +2014,13 @@ __device__ void warp_finalize(const uint64_t* cand, double* prob, uint32_t kk, c
             acc += prob[m];
             ++m;
         }
-        if (m == 0) m = 1;
-        rescale = 0.0;
-        for (int i = 0; i < m; ++i) rescale += prob[i];
+        // the reference's rescale loop repeats these additions: its sum is acc
+        if (m == 0) {
+            m = 1;
+            rescale = prob[0];
+        } else {
+            rescale = acc;
+        }
     }
     m = __shfl_sync(kFull, m, 0);
     rescale = __shfl_sync(kFull, rescale, 0);
