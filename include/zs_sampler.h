@@ -158,7 +158,7 @@ zs_status zs_decode_step(zs_handle h, const float* logits, int64_t ld, int32_t b
  *   n_embd     a multiple of 8, from 64 to 12288
  *   out_logits optional device f32 [batch][logits_ld] (logits_ld >= n_vocab, a
  *              multiple of 4): the logits the sampling used
- * Rows whose shortlist (top_k, or 256 when top_k is 0; 1 for greedy) is at most 64
+ * Rows whose shortlist (top_k, or 256 when top_k is 0; 1 for greedy) is at most 88
  * and that have no repeat penalty are selected inside the GEMM's epilogue and never
  * leave the chip as logits; any other batch is written as logits (to out_logits or
  * handle scratch) and sampled by zs_sample.  Other arguments as zs_sample.

@@ -118,7 +118,8 @@ def _mixed_params(B):
                     SamplingParams(temp=0.7, top_k=40, top_p=0.9),
                     SamplingParams(temp=1.0, top_k=1),
                     SamplingParams(temp=0.8, top_k=64, top_p=0.95),
-                    SamplingParams(temp=1.3, top_k=7)][r % 5])
+                    SamplingParams(temp=1.3, top_k=7),
+                    SamplingParams(temp=0.9, top_k=88, top_p=0.97)][r % 6])
     return out
 
 
@@ -165,7 +166,7 @@ def test_lmhead_batch_one_and_mixed(sampler):
 
 
 def test_lmhead_two_pass_route(sampler):
-    """Rows the epilogue does not hold (a repeat penalty, top-k above 64, the
+    """Rows the epilogue does not hold (a repeat penalty, top-k above 88, the
     default 256-token shortlist) go through the written logits and zs_sample."""
     V, E, B = 151936, 896, 24
     w, nw = _model(V, E)

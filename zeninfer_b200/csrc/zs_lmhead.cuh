@@ -7,7 +7,7 @@
 // zs_lmhead_kernel is a persistent tcgen05 GEMM: D[128 rows][128 vocab] tiles
 // accumulate in tensor memory (two accumulators, so the epilogue of one tile
 // overlaps the MMAs of the next), operands arrive by TMA (2-D tiles, 128-byte
-// swizzle, no multicast) through a 4-stage shared-memory ring.  Work units are
+// swizzle, no multicast) through a 3-stage shared-memory ring.  Work units are
 // (row tile, vocabulary slice); a CTA walks its units' tiles in column order.
 // Warp 0 issues the copies, one thread of warp 1 issues the MMAs, warps 2-5 are
 // the epilogue: thread = row (its TMEM lane).  The epilogue keeps, per row, a
@@ -39,8 +39,8 @@ namespace zs {
 constexpr int kLmM = 128;       // batch rows per tile: the TMEM lanes
 constexpr int kLmN = 128;       // vocabulary columns per tile
 constexpr int kLmBK = 64;       // K per stage: one 128-byte swizzle row of bf16
-constexpr int kLmStages = 4;
-constexpr int kLmCap = 96;      // candidate keys buffered per row
+constexpr int kLmStages = 3;
+constexpr int kLmCap = 120;     // candidate keys buffered per row
 constexpr int kLmKeffMax = kLmCap - 32;  // a compaction leaves room for a whole chunk
 constexpr int kLmRowStride = kLmCap + 1; // odd, so rows spread over the banks
 constexpr int kLmThreads = 192; // warp 0 copies, warp 1 MMAs, warps 2-5 epilogue
