@@ -74,6 +74,7 @@ struct LmArgs {
     float* out_logits;           // optional [B][logits_ld]
     int64_t logits_ld;
     int32_t tma_out;             // logits only: staged in shared memory, stored by TMA
+    uint32_t* tau;               // optional [B] value orders shared by a row's slices
     int* status;
 };
 
@@ -215,7 +216,8 @@ __device__ __forceinline__ void lm_unit(const LmArgs& a, int u, int& m, int& s, 
 // xn equals the reference's float before the bf16 rounding), then every lane writes
 // its share.  Dynamic shared memory: E floats per warp.
 __global__ void zs_lm_rmsnorm_kernel(const float* hidden, int64_t hld, const float* norm_w,
-                                     float eps, int32_t B, int32_t E, __nv_bfloat16* xn) {
+                                     float eps, int32_t B, int32_t E, __nv_bfloat16* xn,
+                                     uint32_t* tau) {
     extern __shared__ float lm_stage[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     float* xs = lm_stage + (int64_t)warp * E;
@@ -234,6 +236,7 @@ __global__ void zs_lm_rmsnorm_kernel(const float* hidden, int64_t hld, const flo
             scale = 1.0 / sqrt(sum / (double)E + (double)eps);
         }
         scale = __shfl_sync(kFull, scale, 0);
+        if (tau && lane == 0) tau[r] = 0u;  // no shared bound yet for this row
         __nv_bfloat16* o = xn + (int64_t)r * E;
         for (int i = lane; i < E; i += 32) {
             const float v = __double2float_rn(__dmul_rn(__dmul_rn((double)xs[i], scale), (double)norm_w[i]));
@@ -248,17 +251,44 @@ __device__ __forceinline__ uint64_t lm_keep(uint64_t* buf, uint32_t n, uint32_t 
 }
 
 // Cuts row L's buffer (of this warp's 32 rows) back to its keff best keys; lane L
-// takes the new count and threshold.
+// takes the new count and threshold (the higher of the new one and one it holds
+// already) and publishes the new one's value order for the row's other slices.
 __device__ __forceinline__ void lm_compact_row(uint64_t* rows, int L, uint32_t& count,
                                                uint32_t& tau_ord, float& tau_f, bool& open,
-                                               uint32_t keff, int lane) {
+                                               uint32_t keff, uint32_t* gtau, int lane) {
     const uint32_t n = __shfl_sync(kFull, count, L);
     const uint32_t kk = __shfl_sync(kFull, keff, L);
     const uint64_t T = lm_keep(rows + (int64_t)L * kLmRowStride, n, kk, lane);
     if (lane == L) {
         count = kk;
-        tau_ord = (uint32_t)(T >> 32);
-        tau_f = value_of_ord(tau_ord);
+        uint32_t t = (uint32_t)(T >> 32);
+        if (gtau) atomicMax(gtau, t);
+        if (!open && tau_ord > t) t = tau_ord;
+        tau_ord = t;
+        tau_f = value_of_ord(t);
+        open = false;
+    }
+}
+
+// A row's slices share a bound: a slice whose buffer held more than keff keys
+// publishes the value order g of its keff-th best, so the row has at least keff keys
+// of value >= value(g), and no key of a smaller value is among its keff best.  Other
+// slices hold ids below or above this slice's, so an equal value may still rank in;
+// they take the bound as "value >= value(g)", that is order g - 1 under the strict
+// test of lm_pass_mask.  Orders at or below -FLT_MAX (and NaN's 0) are not taken;
+// for g = +-0, g - 1 is -0, which zeros would not pass, so -denorm_min stands in.
+__device__ __forceinline__ uint32_t lm_shared_bound(const uint32_t* gtau) {
+    uint32_t g;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(g) : "l"(gtau));
+    return g;
+}
+__device__ __forceinline__ void lm_adopt(uint32_t g, uint32_t& tau_ord, float& tau_f, bool& open) {
+    if (g <= 0x00800000u) return;
+    uint32_t c = g - 1u;
+    if (c == 0x7fffffffu) c = 0x7ffffffeu;
+    if (open || c > tau_ord) {
+        tau_ord = c;
+        tau_f = value_of_ord(c);
         open = false;
     }
 }
@@ -287,13 +317,29 @@ __device__ __forceinline__ uint32_t lm_pass_mask(const float (&v)[32], int col0,
     return pm & inside;
 }
 
+// v[j] for a j known only at run time, by five levels of selects (the array stays
+// in registers; an indexed load would put it in local memory).
+__device__ __forceinline__ float lm_pick(const float (&v)[32], int j) {
+    float x16[16], x8[8], x4[4], x2[2];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) x16[i] = (j & 16) ? v[i + 16] : v[i];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x8[i] = (j & 8) ? x16[i + 8] : x16[i];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) x4[i] = (j & 4) ? x8[i + 4] : x8[i];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) x2[i] = (j & 2) ? x4[i + 2] : x4[i];
+    return (j & 1) ? x2[1] : x2[0];
+}
+
 // One 32-column chunk of a tile for this warp's 32 rows: rows whose passing
 // columns would overflow their buffers are compacted first (the whole warp, one row
 // at a time), then every row appends its passing keys.
 __device__ __forceinline__ void lm_chunk(const uint32_t (&r)[32], int col0, int V, bool sel,
                                          float* lrow, bool& x0nan, bool select, uint64_t* rows,
                                          uint64_t* mine, uint32_t& count, uint32_t& tau_ord,
-                                         float& tau_f, bool& open, uint32_t keff, int lane) {
+                                         float& tau_f, bool& open, uint32_t keff, uint32_t* gtau,
+                                         int lane) {
     float v[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
@@ -315,14 +361,26 @@ __device__ __forceinline__ void lm_chunk(const uint32_t (&r)[32], int col0, int 
     while (over) {
         const int L = __ffs(over) - 1;
         over &= over - 1;
-        lm_compact_row(rows, L, count, tau_ord, tau_f, open, keff, lane);
+        lm_compact_row(rows, L, count, tau_ord, tau_f, open, keff, gtau, lane);
         if (lane == L) pm = lm_pass_mask(v, col0, V, tau_ord, tau_f, open);
     }
-    if (pm) {
+    // Appends: while any row of the warp passes many columns (a buffer still open)
+    // one predicated step per column; otherwise a loop over each row's passing
+    // columns, as many steps as the busiest row has, each picking its value out of
+    // the registers by a select tree.
+    if (__any_sync(kFull, __popc(pm) > 4)) {
+        if (pm) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-            if ((pm >> j) & 1u)
-                mine[count++] = ((uint64_t)ord_of(v[j]) << 32) | (uint64_t)(~(uint32_t)(col0 + j));
+            for (int j = 0; j < 32; ++j)
+                if ((pm >> j) & 1u)
+                    mine[count++] = ((uint64_t)ord_of(v[j]) << 32) | (uint64_t)(~(uint32_t)(col0 + j));
+        }
+    } else {
+        while (pm) {
+            const int j = __ffs(pm) - 1;
+            pm &= pm - 1u;
+            mine[count++] = ((uint64_t)ord_of(lm_pick(v, j)) << 32) | (uint64_t)(~(uint32_t)(col0 + j));
+        }
     }
 }
 
@@ -478,6 +536,7 @@ __global__ void __launch_bounds__(kLmThreads, 1)
             }
             has0 = has0 || t0 == 0;
             const bool sel = a.select && valid;
+            uint32_t* gtau = (sel && a.tau) ? a.tau + row : nullptr;
             float* lrow = (a.out_logits && valid) ? a.out_logits + (int64_t)row * a.logits_ld : nullptr;
             for (int t = t0; t < t1; ++t) {
                 const bool got = lm_wait(&sm.acc_full[acc], acc_phase, abort);
@@ -488,6 +547,8 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                 tc_fence_after();
                 const int tcol = t * kLmN;
                 const uint32_t base = lane_addr + acc * (uint32_t)kLmN;
+                // the other slices' bound, read now and taken after this tile
+                const uint32_t g_seen = gtau ? lm_shared_bound(gtau) : 0u;
 #pragma unroll 1
                 for (int c = 0; c < kLmN / 32; ++c) {
                     uint32_t ra[32];
@@ -516,8 +577,9 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                         continue;
                     }
                     lm_chunk(ra, tcol + c * 32, a.V, sel, lrow, x0nan, a.select, rows, mine, count,
-                             tau_ord, tau_f, open, keff, lane);
+                             tau_ord, tau_f, open, keff, gtau, lane);
                 }
+                if (gtau) lm_adopt(g_seen, tau_ord, tau_f, open);
                 tc_fence_before();
                 mbar_arrive(&sm.acc_empty[acc]);
                 if (++acc == 2) {
@@ -540,7 +602,7 @@ __global__ void __launch_bounds__(kLmThreads, 1)
             while (over) {
                 const int L = __ffs(over) - 1;
                 over &= over - 1;
-                lm_compact_row(rows, L, count, tau_ord, tau_f, open, keff, lane);
+                lm_compact_row(rows, L, count, tau_ord, tau_f, open, keff, gtau, lane);
             }
             if (sel) {
                 uint8_t* blk = a.part + ((int64_t)row * a.S + s) * kLmPartStride;

@@ -840,10 +840,7 @@ zs_status lm_tensor_map(zs_context* h, CUtensorMap* map, const void* base, int64
 
 // Slices per row for mt row tiles x nt column tiles on `ctas` CTAs: the fewest
 // slices (at most `cap`) whose busiest CTA has at most 2% more tiles than the best
-// split.  When the epilogue selects (cap below 1024) and there are at least 8 row
-// tiles, up to 15% more: every slice restarts each row's threshold, and at large
-// batches those restarts cost more than the idle SMs (measured at 4096 rows: 2.61
-// against 2.29 ms per call).
+// split.
 int lm_slices(int mt, int nt, int ctas, int cap) {
     auto span = [&](int S) {
         const int64_t units = (int64_t)mt * S;
@@ -853,7 +850,7 @@ int lm_slices(int mt, int nt, int ctas, int cap) {
     int64_t best = span(1);
     for (int S = 2; S <= smax; ++S) best = std::min(best, span(S));
     for (int S = 1; S <= smax; ++S)
-        if (span(S) * 100 <= best * ((cap < 1024 && mt >= 8) ? 115 : 102)) return S;
+        if (span(S) * 100 <= best * 102) return S;
     return 1;
 }
 
@@ -909,7 +906,8 @@ zs_status lm_run(zs_context* h, const float* hidden, int64_t hidden_ld, const fl
         const size_t smem = (size_t)nw * a.E * sizeof(float);
         const int grid = (int)std::min<int64_t>((a.B + nw - 1) / nw, (int64_t)h->num_sms * 16);
         zs::zs_lm_rmsnorm_kernel<<<grid, nw * 32, smem, st>>>(
-            hidden, hidden_ld, norm_w, eps, a.B, a.E, reinterpret_cast<__nv_bfloat16*>(h->lm_xn));
+            hidden, hidden_ld, norm_w, eps, a.B, a.E, reinterpret_cast<__nv_bfloat16*>(h->lm_xn),
+            a.tau);
         ZS_CUDA(cudaGetLastError());
     }
     {
@@ -1016,9 +1014,13 @@ zs_status zs_lmhead_sample(zs_handle h, const float* hidden, int64_t hidden_ld,
     a.out_logits = logits;
     a.logits_ld = lld;
     if (fused) {
-        s = grow((void**)&h->part, &h->part_bytes, (size_t)batch * a.S * zs::kLmPartStride);
+        // the blocks, then (more than one slice) a value order per row that the
+        // row's slices share as a lower bound for their thresholds
+        const size_t blocks = (size_t)batch * a.S * zs::kLmPartStride;
+        s = grow((void**)&h->part, &h->part_bytes, blocks + (size_t)batch * sizeof(uint32_t));
         if (s != ZS_OK) return s;
         a.part = h->part;
+        if (a.S > 1) a.tau = reinterpret_cast<uint32_t*>(h->part + blocks);
     }
     s = lm_run(h, hidden, hidden_ld, norm_w, eps, weight, a, st);
     if (s != ZS_OK) return s;
