@@ -39,7 +39,8 @@ namespace zs {
 constexpr int kLmM = 128;       // batch rows per tile: the TMEM lanes
 constexpr int kLmN = 128;       // vocabulary columns per tile
 constexpr int kLmBK = 64;       // K per stage: one 128-byte swizzle row of bf16
-constexpr int kLmStages = 3;
+constexpr int kLmStages = 3;      // ring stages when all 128 rows hold candidates
+constexpr int kLmStagesMax = 5;   // with only 32 rows' buffers the ring takes the rest
 constexpr int kLmCap = 120;     // candidate keys buffered per row
 constexpr int kLmKeffMax = kLmCap - 32;  // a compaction leaves room for a whole chunk
 constexpr int kLmRowStride = kLmCap + 1; // odd, so rows spread over the banks
@@ -49,13 +50,17 @@ constexpr uint32_t kLmTileABytes = kLmM * kLmBK * 2;
 constexpr uint32_t kLmTileBBytes = kLmN * kLmBK * 2;
 constexpr int64_t kLmPartStride = kPartialHeaderBytes + 8 * kLmKeffMax;
 static_assert(kLmPartStride % 16 == 0, "block headers are read as uint4");
+constexpr uint32_t kLmStageBytes = kLmTileABytes + kLmTileBBytes;
+constexpr uint32_t kLmRowBytes = kLmRowStride * 8;  // one row's candidate buffer
+// ns stages of A tiles, ns of B tiles, then the candidate buffers of the rows in use
+constexpr uint32_t kLmRingBytes = kLmStages * kLmStageBytes + kLmM * kLmRowBytes;
+static_assert(kLmStagesMax * kLmStageBytes + 32 * kLmRowBytes <= kLmRingBytes,
+              "the deepest ring leaves room for one warp's buffers");
 
 struct LmSmem {  // placed at a 1024-byte boundary: the swizzled tiles need it
-    uint8_t a[kLmStages][kLmTileABytes];
-    uint8_t b[kLmStages][kLmTileBBytes];
-    uint64_t cand[kLmM * kLmRowStride];  // per row: candidate keys, unordered
-    uint64_t full[kLmStages];
-    uint64_t empty[kLmStages];
+    uint8_t ring[kLmRingBytes];  // tiles (1024-byte aligned), then per row: keys, unordered
+    uint64_t full[kLmStagesMax];
+    uint64_t empty[kLmStagesMax];
     uint64_t acc_full[2];
     uint64_t acc_empty[2];
     uint64_t drain;
@@ -74,6 +79,7 @@ struct LmArgs {
     float* out_logits;           // optional [B][logits_ld]
     int64_t logits_ld;
     int32_t tma_out;             // logits only: staged in shared memory, stored by TMA
+    int32_t ns;                  // ring stages: kLmStages, or more when few rows hold keys
     uint32_t* tau;               // optional [B] value orders shared by a row's slices
     int* status;
 };
@@ -368,7 +374,7 @@ __device__ __forceinline__ void lm_chunk(const uint32_t (&r)[32], int col0, int 
     // one predicated step per column; otherwise a loop over each row's passing
     // columns, as many steps as the busiest row has, each picking its value out of
     // the registers by a select tree.
-    if (__any_sync(kFull, __popc(pm) > 4)) {
+    if (__any_sync(kFull, __popc(pm) > 16)) {
         if (pm) {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
@@ -395,8 +401,13 @@ __global__ void __launch_bounds__(kLmThreads, 1)
     const int nk = (a.E + kLmBK - 1) / kLmBK;
     volatile int* abort = &sm.abort;
 
+    const int ns = a.ns;
+    uint8_t* const tiles_a = sm.ring;
+    uint8_t* const tiles_b = sm.ring + (size_t)ns * kLmTileABytes;
+    uint64_t* const cand = reinterpret_cast<uint64_t*>(sm.ring + (size_t)ns * kLmStageBytes);
+
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kLmStages; ++s) {
+        for (int s = 0; s < ns; ++s) {
             mbar_init(&sm.full[s], 1);
             mbar_init(&sm.empty[s], 1);
         }
@@ -437,10 +448,12 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                             break;
                         }
                         mbar_arrive_expect_tx(&sm.full[stage], kLmTileABytes + kLmTileBBytes);
-                        tma_load_2d(sm.a[stage], &tm_a, kb * kLmBK, m * kLmM, &sm.full[stage]);
-                        tma_load_2d(sm.b[stage], &tm_b, kb * kLmBK, t * kLmN, &sm.full[stage]);
+                        tma_load_2d(tiles_a + stage * kLmTileABytes, &tm_a, kb * kLmBK, m * kLmM,
+                                    &sm.full[stage]);
+                        tma_load_2d(tiles_b + stage * kLmTileBBytes, &tm_b, kb * kLmBK, t * kLmN,
+                                    &sm.full[stage]);
                         ++issued;
-                        if (++stage == kLmStages) {
+                        if (++stage == (uint32_t)ns) {
                             stage = 0;
                             phase ^= 1u;
                         }
@@ -450,8 +463,8 @@ __global__ void __launch_bounds__(kLmThreads, 1)
             if (!ok) set_status(a.status, kStatusTimeout);
             // Every copy issued has landed before the CTA may exit (the MMA issuer
             // has waited for all of them already unless a wait ran out).
-            for (int64_t i = issued - kLmStages; i < issued; ++i)
-                if (i >= 0) mbar_wait_bounded(&sm.full[i % kLmStages], (uint32_t)((i / kLmStages) & 1));
+            for (int64_t i = issued - ns; i < issued; ++i)
+                if (i >= 0) mbar_wait_bounded(&sm.full[i % ns], (uint32_t)((i / ns) & 1));
         }
         __syncwarp();
     } else if (warp == 1) {
@@ -475,14 +488,14 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                             break;
                         }
                         tc_fence_after();
-                        const uint64_t ad = sw128_desc(sm.a[stage]);
-                        const uint64_t bd = sw128_desc(sm.b[stage]);
+                        const uint64_t ad = sw128_desc(tiles_a + stage * kLmTileABytes);
+                        const uint64_t bd = sw128_desc(tiles_b + stage * kLmTileBBytes);
 #pragma unroll
                         for (int k = 0; k < kLmBK / 16; ++k)
                             tc_mma_bf16(d, ad + 2ull * k, bd + 2ull * k, kLmIdesc,
                                         (kb | k) != 0 ? 1u : 0u);
                         tc_commit(&sm.empty[stage]);
-                        if (++stage == kLmStages) {
+                        if (++stage == (uint32_t)ns) {
                             stage = 0;
                             phase ^= 1u;
                         }
@@ -505,7 +518,9 @@ __global__ void __launch_bounds__(kLmThreads, 1)
         // ---- epilogue: thread = row of the tile (its TMEM lane) ----
         const int q = warp & 3;  // the lane quarter this warp may access
         const int r_in = q * 32 + lane;
-        uint64_t* rows = sm.cand + (int64_t)(q * 32) * kLmRowStride;
+        // rows at or beyond the batch never touch their buffers (the host sized
+        // the ring so that the buffers of the rows in use fit behind it)
+        uint64_t* rows = cand + (int64_t)(q * 32) * kLmRowStride;
         uint64_t* mine = rows + (int64_t)lane * kLmRowStride;
         const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
         uint32_t acc = 0, acc_phase = 0;
@@ -559,7 +574,7 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                         // logits only: this warp's 32 rows x 32 columns go to a staging
                         // buffer in the (here unused) candidate area, in the 128-byte
                         // swizzled layout of the output tensor map, then one TMA store
-                        uint8_t* stg = reinterpret_cast<uint8_t*>(sm.cand) + (q * 2 + stg_buf) * 4096;
+                        uint8_t* stg = reinterpret_cast<uint8_t*>(cand) + (q * 2 + stg_buf) * 4096;
                         if (lane == 0) bulk_wait_read_1();  // the store two chunks ago read it
                         __syncwarp();
                         uint8_t* my = stg + lane * 128;

@@ -898,6 +898,20 @@ zs_status lm_run(zs_context* h, const float* hidden, int64_t hidden_ld, const fl
     } else {
         tm_c = tm_a;
     }
+    // Ring depth: the candidate buffers (or the logits staging) of the rows in use
+    // sit behind the ring, so a batch within one warp's 32 rows (or logits stored
+    // directly) leaves room for more weight tiles in flight.
+    {
+        const int64_t rows_in_use = (a.select || a.tma_out)
+                                        ? (a.mt > 1 || a.tma_out ? zs::kLmM : ((int64_t)a.B + 31) / 32 * 32)
+                                        : 0;
+        a.ns = zs::kLmStages;
+        for (int n = zs::kLmStagesMax; n > zs::kLmStages; --n)
+            if ((int64_t)n * zs::kLmStageBytes + rows_in_use * zs::kLmRowBytes <= (int64_t)zs::kLmRingBytes) {
+                a.ns = n;
+                break;
+            }
+    }
     a.status = h->status;
     {
         LaunchScope scope(h, 4, st);
