@@ -80,6 +80,7 @@ struct LmArgs {
     int64_t logits_ld;
     int32_t tma_out;             // logits only: staged in shared memory, stored by TMA
     int32_t ns;                  // ring stages: kLmStages, or more when few rows hold keys
+    int32_t prefetch;            // weight boxes each CTA prefetches into L2 while rmsnorm runs
     uint32_t* tau;               // optional [B] value orders shared by a row's slices
     int* status;
 };
@@ -112,6 +113,14 @@ __device__ __forceinline__ void bulk_wait_read_1() {
 // Waits until every committed store has completed.
 __device__ __forceinline__ void bulk_wait_all() {
     asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// One box of a tensor into L2 only (no shared memory, no barrier).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int32_t x, int32_t y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y)
+                 : "memory");
 }
 
 __device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {
@@ -225,6 +234,7 @@ __global__ void zs_lm_rmsnorm_kernel(const float* hidden, int64_t hld, const flo
                                      float eps, int32_t B, int32_t E, __nv_bfloat16* xn,
                                      uint32_t* tau) {
     extern __shared__ float lm_stage[];
+    grid_dep_trigger();  // zs_lmhead_kernel may start its weight prefetch now
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     float* xs = lm_stage + (int64_t)warp * E;
     for (int r = blockIdx.x * nw + warp; r < B; r += gridDim.x * nw) {
@@ -431,6 +441,22 @@ __global__ void __launch_bounds__(kLmThreads, 1)
     const uint32_t tmem = sm.tmem_base;
     int u_begin, u_end;
     lm_range(a, u_begin, u_end);
+
+    // Launched behind zs_lm_rmsnorm_kernel as a programmatic dependent: the copy
+    // issuer first pulls its first weight boxes into L2 (they do not depend on the
+    // rmsnorm), then every thread waits for that grid before reading xn or the
+    // shared bounds the rmsnorm clears.
+    if (warp == 0 && lane == 0 && a.prefetch > 0) {
+        int left = a.prefetch;
+        for (int u = u_begin; left > 0 && u < u_end; ++u) {
+            int m, s, t0, t1;
+            lm_unit(a, u, m, s, t0, t1);
+            for (int t = t0; left > 0 && t < t1; ++t)
+                for (int kb = 0; left > 0 && kb < nk; ++kb, --left)
+                    tma_prefetch_l2_2d(&tm_b, kb * kLmBK, t * kLmN);
+        }
+    }
+    grid_dep_wait();
 
     if (warp == 0) {
         // ---- copy issuer ----

@@ -927,8 +927,21 @@ zs_status lm_run(zs_context* h, const float* hidden, int64_t hidden_ld, const fl
     {
         LaunchScope scope(h, 3, st);
         const int grid = std::min(a.n_units, h->num_sms);
-        zs::zs_lmhead_kernel<<<grid, zs::kLmThreads, zs::kLmSmemBytes, st>>>(tm_a, tm_b, tm_c, a);
-        ZS_CUDA(cudaGetLastError());
+        // One row tile streams the weights once: while the rmsnorm runs, each CTA
+        // prefetches its first weight boxes, about 80 MB in all (within the L2).
+        a.prefetch = a.mt == 1 ? (int)((80ll << 20) / zs::kLmTileBBytes / grid) : 0;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cudaLaunchConfig_t cfg;
+        std::memset(&cfg, 0, sizeof(cfg));
+        cfg.gridDim = dim3(grid);
+        cfg.blockDim = dim3(zs::kLmThreads);
+        cfg.dynamicSmemBytes = zs::kLmSmemBytes;
+        cfg.stream = st;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        ZS_CUDA(cudaLaunchKernelEx(&cfg, zs::zs_lmhead_kernel, tm_a, tm_b, tm_c, a));
     }
     return ZS_OK;
 }
