@@ -168,15 +168,23 @@ def lmhead_bench(s, dev, stream, hbm_peak):
         st = states_to_tensor([i + 1 for i in range(B)], dev)
         ids = torch.empty(B, dtype=torch.int32, device=dev)
         fused = lambda: s.lmhead_sample(h, nw, W, p, st, out=ids, stream=stream)
+        reps = 10 if B > 1 else 100
+        # the default route (two passes up to 1024 rows, fused above) ...
         for _ in range(3):
             fused()
         torch.cuda.synchronize()
-        reps = 10 if B > 1 else 100
+        ms_auto = time_device_steps(fused, reps, stream) / reps
+        # ... and the fused route forced, with its kernels timed one by one
+        s.set_lmhead_route("fused")
+        for _ in range(3):
+            fused()
+        torch.cuda.synchronize()
         s.set_timing(True)
         s.get_timing()
         ms = time_device_steps(fused, reps, stream) / reps
         kt = s.get_timing()
         s.set_timing(False)
+        s.set_lmhead_route("auto")
         k_ms = kt["lmhead_ms"] / max(1, kt["lmhead_launches"])
         xn = torch.nn.functional.rms_norm(h, (E,), nw, 1e-6).to(torch.bfloat16)
 
@@ -199,7 +207,9 @@ def lmhead_bench(s, dev, stream, hbm_peak):
         del lg_own
         flops = 2.0 * B * E * V
         wbytes = V * E * 2 + B * E * 2
-        r = {"us_per_call": ms * 1e3, "rows_per_s": B / (ms / 1e3),
+        r = {"default_route_us_per_call": ms_auto * 1e3,
+             "default_route": "two_pass" if B <= 1024 else "fused",
+             "us_per_call": ms * 1e3, "rows_per_s": B / (ms / 1e3),
              "kernel_us": k_ms * 1e3,
              "rmsnorm_us": kt["lmnorm_ms"] / max(1, kt["lmnorm_launches"]) * 1e3,
              "merge_us": kt["merge_ms"] / max(1, kt["merge_launches"]) * 1e3,

@@ -159,9 +159,10 @@ zs_status zs_decode_step(zs_handle h, const float* logits, int64_t ld, int32_t b
  *   out_logits optional device f32 [batch][logits_ld] (logits_ld >= n_vocab, a
  *              multiple of 4): the logits the sampling used
  * Rows whose shortlist (top_k, or 256 when top_k is 0; 1 for greedy) is at most 88
- * and that have no repeat penalty are selected inside the GEMM's epilogue and never
- * leave the chip as logits; any other batch is written as logits (to out_logits or
- * handle scratch) and sampled by zs_sample.  Other arguments as zs_sample.
+ * and that have no repeat penalty can be selected inside the GEMM's epilogue and never
+ * leave the chip as logits; zs_set_lmhead_route says when they are (by default above
+ * 1024 rows).  Any other batch is written as logits (to out_logits or handle scratch)
+ * and sampled by zs_sample.  Other arguments as zs_sample.
  * Replaces, for one step of cmd_generate, model.eval's last two lines and the
  * sample_token call (src/main.cpp:628).
  */
@@ -215,6 +216,20 @@ typedef struct zs_timing {
 } zs_timing;
 zs_status zs_set_timing(zs_handle h, int32_t enable);
 zs_status zs_get_timing(zs_handle h, zs_timing* out);
+
+/* How zs_lmhead_sample takes the shortlist, for this handle.  No counterpart in the
+ * reference (its lm_head and sampler are separate CPU calls).
+ *   ZS_LMHEAD_ROUTE_AUTO      (default) two passes up to 1024 rows, fused above, the
+ *                             faster of the two on B200 at each size
+ *   ZS_LMHEAD_ROUTE_FUSED     in the GEMM's epilogue whenever the rows allow it (no
+ *                             logits buffer: for callers that cannot spare one)
+ *   ZS_LMHEAD_ROUTE_TWO_PASS  always write logits, then zs_sample
+ * Both routes give the same ids and Rng states.  The two-pass route writes the logits
+ * to out_logits when given, else to handle scratch of batch x n_vocab floats. */
+#define ZS_LMHEAD_ROUTE_AUTO 0
+#define ZS_LMHEAD_ROUTE_FUSED 1
+#define ZS_LMHEAD_ROUTE_TWO_PASS 2
+zs_status zs_set_lmhead_route(zs_handle h, int32_t route);
 
 /* The display numbers of zeninfer's `logits` command (src/main.cpp:473-503) for each
  * of `batch` rows of n_vocab f32 logits (device, row r at logits + r * ld):

@@ -9,7 +9,10 @@ the shortlist in the GEMM epilogue.  Parity, per case:
     and against the unchanged reference's f32 lm_head within the bf16 rounding of
     xn, |d| <= 2^-8 sum|xn_i w_i|;
   * ids and Rng states bit-exact against zs_sample run on those logits, which is
-    itself checked against the restatement under the sampler's parity rules."""
+    itself checked against the restatement under the sampler's parity rules.
+The cases below force the fused route (the default takes two passes up to 1024
+rows), so the epilogue's selection is covered at every size; one test checks that
+the routes agree bit for bit."""
 
 import numpy as np
 import pytest
@@ -46,7 +49,8 @@ def _hidden(B, E, seed):
     return h
 
 
-def _run(sampler, hidden, nw, w, params, seeds, with_logits=True, history=None, hlen=None):
+def _run(sampler, hidden, nw, w, params, seeds, with_logits=True, history=None, hlen=None,
+         route="fused"):
     import torch
     dev = sampler.device
     B, V = hidden.shape[0], w.shape[0]
@@ -58,8 +62,12 @@ def _run(sampler, hidden, nw, w, params, seeds, with_logits=True, history=None, 
     if history is not None:
         h = torch.from_numpy(history).to(dev)
         hl = torch.from_numpy(hlen).to(dev)
-    ids = sampler.lmhead_sample(hidden.to(dev), nw.to(dev), w.to(dev), params, st, eps=EPS,
-                                history=h, history_len=hl, out_logits=lg)
+    sampler.set_lmhead_route(route)
+    try:
+        ids = sampler.lmhead_sample(hidden.to(dev), nw.to(dev), w.to(dev), params, st, eps=EPS,
+                                    history=h, history_len=hl, out_logits=lg)
+    finally:
+        sampler.set_lmhead_route("auto")
     sampler.check_device_status()
     out = {"ids": ids.cpu().numpy(), "states": tensor_to_states(st)}
     if lg is not None:
@@ -187,6 +195,30 @@ def test_lmhead_two_pass_route(sampler):
     # without out_logits the logits live in handle scratch; same draws
     res2 = _run(sampler, hidden, nw, w, params, seeds, with_logits=False, history=hist, hlen=hlen)
     assert np.array_equal(res2["ids"], res["ids"])
+
+
+@pytest.mark.parametrize("B", [5, 300])
+def test_lmhead_routes_agree(sampler, B):
+    """Fused, two-pass and the default route give the same ids, Rng states and
+    logits, bit for bit (5 rows: the default takes two passes)."""
+    V, E = 151936, 896
+    w, nw = _model(V, E)
+    hidden = _hidden(B, E, 41)
+    params = _mixed_params(B)
+    seeds = np.arange(B, dtype=np.uint64) + np.uint64(77)
+    got = {r: _run(sampler, hidden, nw, w, params, seeds, route=r)
+           for r in ("fused", "two_pass", "auto")}
+    for r in ("two_pass", "auto"):
+        assert np.array_equal(got[r]["ids"], got["fused"]["ids"]), r
+        assert np.array_equal(got[r]["states"], got["fused"]["states"]), r
+        assert np.array_equal(got[r]["logits"].view(np.uint32),
+                              got["fused"]["logits"].view(np.uint32)), r
+    _check_sampling(sampler, got["auto"], params, seeds)
+
+
+def test_lmhead_route_rejects_unknown(sampler):
+    with pytest.raises(ValueError):
+        sampler.set_lmhead_route("fastest")
 
 
 def test_lmhead_rejects_bad_shapes(sampler):

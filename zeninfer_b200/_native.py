@@ -19,6 +19,7 @@ EXPORTS = (
     "zs_shard_partial_bytes", "zs_shard_partials", "zs_shard_merge", "zs_sample_sharded",
     "zs_sample_noalloc", "zs_set_timing", "zs_get_timing", "zs_logits_stats",
     "zs_selftest_wait_timeout", "zs_decode_step", "zs_lmhead_sample", "zs_lmhead_logits",
+    "zs_set_lmhead_route",
 )
 
 ZS_OK = 0
@@ -92,6 +93,7 @@ def lib() -> C.CDLL:
                                  vp, i32, vp, vp, i64, i64, vp]
     L.zs_logits_stats.argtypes = [vp, vp, i64, i32, i32, i32, vp, vp, vp, vp, vp, vp]
     L.zs_set_timing.argtypes = [vp, i32]
+    L.zs_set_lmhead_route.argtypes = [vp, i32]
     L.zs_get_timing.argtypes = [vp, C.POINTER(ZsTiming)]
     L.zs_sample_noalloc.argtypes = [vp, i64, i32, i32, C.POINTER(ZsParams), vp, i64, vp, vp, vp,
                                     vp, vp]
@@ -104,7 +106,7 @@ def lib() -> C.CDLL:
                                             "zs_set_timing", "zs_get_timing",
                                             "zs_logits_stats", "zs_selftest_wait_timeout",
                                             "zs_decode_step", "zs_lmhead_sample",
-                                            "zs_lmhead_logits"):
+                                            "zs_lmhead_logits", "zs_set_lmhead_route"):
             f.restype = C.c_int
     _lib = L
     return L

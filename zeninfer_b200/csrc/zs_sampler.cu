@@ -262,6 +262,7 @@ struct zs_context {
         cudaEvent_t begin, end;
     };
     bool timing = false;
+    int32_t lm_route = ZS_LMHEAD_ROUTE_AUTO;  // zs_set_lmhead_route
     std::vector<TimedLaunch> timed;      // recorded since the last zs_get_timing
     std::vector<cudaEvent_t> spare;      // events free for reuse
     int64_t launches = 0;                // kernel launches since the last zs_get_timing
@@ -676,6 +677,15 @@ zs_status zs_set_timing(zs_handle h, int32_t enable) {
     return ZS_OK;
 }
 
+zs_status zs_set_lmhead_route(zs_handle h, int32_t route) {
+    if (!h) return fail(ZS_ERR_INVALID_ARGUMENT, "null handle");
+    if (route != ZS_LMHEAD_ROUTE_AUTO && route != ZS_LMHEAD_ROUTE_FUSED &&
+        route != ZS_LMHEAD_ROUTE_TWO_PASS)
+        return fail(ZS_ERR_INVALID_ARGUMENT, "route must be ZS_LMHEAD_ROUTE_AUTO, _FUSED or _TWO_PASS");
+    h->lm_route = route;
+    return ZS_OK;
+}
+
 zs_status zs_get_timing(zs_handle h, zs_timing* out) {
     if (!h || !out) return fail(ZS_ERR_INVALID_ARGUMENT, "null handle or out");
     DeviceGuard g(h->device);
@@ -858,6 +868,8 @@ int lm_slices(int mt, int nt, int ctas, int cap) {
 
 namespace {
 
+constexpr int32_t kLmTwoPassMaxRows = 1024;
+
 // Checks shared by the lm_head entry points.
 zs_status lm_validate(zs_handle h, const float* hidden, int64_t hidden_ld, const float* norm_w,
                       const void* weight, int32_t n_embd, int32_t n_vocab, const float* out_logits,
@@ -1011,6 +1023,13 @@ zs_status zs_lmhead_sample(zs_handle h, const float* hidden, int64_t hidden_ld,
         if (ks > zs::kLmKeffMax) fused = false;
         if (have_hist && p.repeat_penalty != 1.0f && p.repeat_last_n > 0) fused = false;
     }
+    // Up to kLmTwoPassMaxRows rows the two passes are faster (measured on B200, 151,936
+    // x 896 weights, top-k 50: 149 against 346 us at 32 rows, 631 against 679 us at
+    // 1024; fused 997 against 1111 us at 2048): with so few row tiles, each CTA's
+    // epilogue selects for its rows on too few warps to keep up with the GEMM.
+    if (h->lm_route == ZS_LMHEAD_ROUTE_TWO_PASS ||
+        (h->lm_route == ZS_LMHEAD_ROUTE_AUTO && batch <= kLmTwoPassMaxRows))
+        fused = false;
 
     float* logits = out_logits;
     int64_t lld = logits_ld;

@@ -329,6 +329,17 @@ class Sampler:
             out["top_p"].data_ptr(), _stream_ptr(stream)), "zs_logits_stats")
         return out
 
+    LMHEAD_ROUTES = {"auto": 0, "fused": 1, "two_pass": 2}
+
+    def set_lmhead_route(self, route: str) -> None:
+        """How lmhead_sample takes the shortlist: "auto" (two passes up to 1024 rows,
+        fused above), "fused" (in the GEMM epilogue whenever the rows allow it; no
+        logits buffer) or "two_pass" (logits, then sample).  Same results either way."""
+        if route not in self.LMHEAD_ROUTES:
+            raise ValueError(f"route must be one of {sorted(self.LMHEAD_ROUTES)}")
+        _native.check(self._lib.zs_set_lmhead_route(self._h, self.LMHEAD_ROUTES[route]),
+                      "zs_set_lmhead_route")
+
     def set_timing(self, enable: bool) -> None:
         """Bracket every kernel of this sampler with CUDA events (measurement only)."""
         _native.check(self._lib.zs_set_timing(self._h, 1 if enable else 0), "zs_set_timing")
