@@ -7,7 +7,8 @@
 // zs_lmhead_kernel is a persistent tcgen05 GEMM: D[128 rows][128 vocab] tiles
 // accumulate in tensor memory (two accumulators, so the epilogue of one tile
 // overlaps the MMAs of the next), operands arrive by TMA (2-D tiles, 128-byte
-// swizzle, no multicast) through a 3-stage shared-memory ring.  Work units are
+// swizzle, no multicast) through a shared-memory ring of 3 to 5 stages (deeper
+// when the batch leaves candidate buffers unused).  Work units are
 // (row tile, vocabulary slice); a CTA walks its units' tiles in column order.
 // Warp 0 issues the copies, one thread of warp 1 issues the MMAs, warps 2-5 are
 // the epilogue: thread = row (its TMEM lane).  The epilogue keeps, per row, a
@@ -17,7 +18,8 @@
 // order beats the threshold's; a 32-column chunk whose maximum does not is skipped
 // whole.  When a row's passing columns would overflow its buffer, the warp cuts
 // that row back to its keff best keys together (warp_topk_keep), which raises the
-// threshold.  At the end of a unit each row writes its keys
+// threshold.  A row's slices also share a lower bound through global memory
+// (lm_shared_bound / lm_adopt).  At the end of a unit each row writes its keys
 // as one partial block, (row, slice), in the layout zs_merge_kernel and
 // zs_warp_merge_kernel read, so the merge, f64 softmax, nucleus and draw are the
 // sampler's own.  Optionally the epilogue also writes the f32 logits.
