@@ -8,13 +8,22 @@ one xorshift64* draw per row.  Synthetic data: no model or dataset exists here.
 
 One step = one zs_sample call over the rank's 4096 rows: the streaming select
 kernel (zs_wselect_kernel: every row of this workload has a top-50 shortlist)
-and the per-row merge kernel.
+and the per-row merge kernel.  Each step is also timed on its own (per_step_ms).
 With N GPUs (torchrun, one process per GPU) every rank samples its own 4096
 rows (row split, no communication): weak scaling, value = N*4096 rows / max
-over ranks of the step time.  For N > 1 the vocab-sharded mode (partials ->
-NCCL all-gather -> merge) over the same 4096 rows is reported beside it.
+over ranks of the step time.  For N > 1 the vocab-sharded mode over the same
+4096 rows (partials -> row-owner exchange or all-gather -> merge) is reported
+beside it, with its partials / merge / exchange split.
 
-Inputs (2.49 GB per rank) are larger than L2 (126 MB), so every step reads HBM.
+With one GPU the line also carries: by_config (the five workloads at their own
+batch sizes 1, 256, 1024, 512 and 4096, each with the select / merge split and
+the parity counts of one checked call against the restatement and the unchanged
+reference), host_api_b1 (zen::sample_token on one host row, the drop-in C++
+API), the logits display numbers, the decode loop, the lm_head routes and the
+full-vocabulary nucleus.
+
+Inputs (2.49 GB per rank) are larger than L2 (126 MB), so every step reads HBM;
+smaller workloads rotate over copies of their input that together exceed L2.
 """
 
 from __future__ import annotations
@@ -71,17 +80,57 @@ def committed_traffic(rows):
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clocks and clock-event (throttle) reasons sampled during the timed region:
+    NVML read every 2 ms from a thread (the timed region of a short run lasts only
+    milliseconds), else nvidia-smi every 100 ms.  Reads only; changes nothing."""
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # nvmlClocksEventReason* bits
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap"}
 
-    def __init__(self, gpu_index):
+    def __init__(self, gpu_index, pci_bus_id=None):
         self.gpu = gpu_index
+        self.pci = pci_bus_id
         self.proc = None
         self.path = None
+        self.thread = None
+        self.stop_flag = False
+        self.sm, self.mx, self.reasons = [], [], set()
+
+    def _nvml_loop(self, nv, h):
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        while not self.stop_flag:
+            try:
+                self.sm.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+                self.mx.append(float(mx))
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                for bit, name in self.REASONS.items():
+                    if bits & bit:
+                        self.reasons.add(name)
+            except Exception:
+                break
+            time.sleep(0.002)
 
     def start(self):
+        try:
+            import threading
+            import pynvml as nv
+            nv.nvmlInit()
+            h = None
+            if self.pci:
+                try:
+                    h = nv.nvmlDeviceGetHandleByPciBusId(self.pci)
+                except Exception:
+                    h = None
+            if h is None:
+                h = nv.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.thread = threading.Thread(target=self._nvml_loop, args=(nv, h), daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.thread = None
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
@@ -94,35 +143,41 @@ class ClockSampler:
 
     def stop(self):
         out = {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        if self.proc is None:
+        if self.thread is not None:
+            self.stop_flag = True
+            self.thread.join(timeout=5)
+            src = "nvml, every 2 ms"
+        elif self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            try:
+                for line in open(self.path):
+                    parts = [p.strip() for p in line.split(",")]
+                    if len(parts) < 9:
+                        continue
+                    try:
+                        self.sm.append(float(parts[1]))
+                        self.mx.append(float(parts[2]))
+                    except ValueError:
+                        continue
+                    for n, v in zip(names, parts[5:9]):
+                        if v.lower() == "active":
+                            self.reasons.add(n)
+                os.unlink(self.path)
+            except OSError:
+                pass
+            src = "nvidia-smi, every 100 ms"
+        else:
             return out
-        time.sleep(0.25)
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        try:
-            for line in open(self.path):
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) < 9:
-                    continue
-                try:
-                    sm.append(float(parts[1]))
-                    mx.append(float(parts[2]))
-                except ValueError:
-                    continue
-                for n, v in zip(names, parts[5:9]):
-                    if v.lower() == "active":
-                        reasons.add(n)
-            os.unlink(self.path)
-        except OSError:
-            pass
-        if sm:
-            out = {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
-                   "reasons": sorted(reasons), "samples": len(sm)}
+        if self.sm:
+            out = {"sm_mhz": statistics.median(self.sm), "sm_max_mhz": max(self.mx),
+                   "sm_min_mhz": min(self.sm), "reasons": sorted(self.reasons),
+                   "samples": len(self.sm), "source": src}
         return out
 
 
@@ -335,16 +390,274 @@ def run_reference_arm(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
-def time_device_steps(fn, steps, stream):
+def time_device_steps(fn, steps, stream, per_step=None):
+    """Device time (ms) of `steps` calls of fn on `stream`, by CUDA events around the
+    whole run; with a list as per_step, each step's own time (ms) is appended to it
+    (an event after every step)."""
     import torch
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
+    marks = []
     start.record(stream)
     for _ in range(steps):
         fn()
+        if per_step is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record(stream)
+            marks.append(ev)
     end.record(stream)
     end.synchronize()
+    if per_step is not None:
+        prev = start
+        for ev in marks:
+            per_step.append(prev.elapsed_time(ev))
+            prev = ev
     return start.elapsed_time(end)
+
+
+def spread(ms_list):
+    """min / median / max of per-step times (ms)."""
+    if not ms_list:
+        return None
+    return {"min_ms": min(ms_list), "median_ms": statistics.median(ms_list),
+            "max_ms": max(ms_list), "n": len(ms_list)}
+
+
+L2_BYTES = 126 * 2**20
+
+
+def shortlist_len(p):
+    if p.temp <= 0:
+        return 0
+    return min(p.top_k, V) if p.top_k > 0 else min(256, V)
+
+
+def parity_counts(s, dev, x, p, states, seeds, stream):
+    """One checked call outside the timed region, against the restatement (oracle/)
+    and the unchanged reference (oracle/_ref, src/sample.cpp): the counts the parity
+    rules name.  Returns a dict; never raises."""
+    import numpy as np
+    import torch
+    from zeninfer_b200 import Rng, states_to_tensor, tensor_to_states
+    try:
+        import oracle
+        k = shortlist_len(p)
+        xd = torch.from_numpy(x).to(dev)
+        st = states_to_tensor(states, dev)
+        res = s.sample(xd, p, st, row_info=True, cand_ld=k, stream=stream)
+        torch.cuda.synchronize()
+        g_ids = res.ids.cpu().numpy()
+        g_st = tensor_to_states(st)
+        o_st = np.array(states, dtype=np.uint64, copy=True)
+        o_ids, o_info, o_cid, _, o_cp = oracle.oracle_sample(x, p, o_st, cand_ld=k)
+        greedy = p.temp <= 0
+        near = (o_info["boundary"] < 1e-6) if not greedy else np.zeros(len(g_ids), bool)
+        out = {"rows": int(len(g_ids)),
+               "boundary_rows": int(near.sum()),
+               "boundary_rows_id_differs": int(((g_ids != o_ids) & near).sum()),
+               "id_mismatch_vs_restatement": int(((g_ids != o_ids) & ~near).sum()),
+               "rng_state_mismatch_vs_restatement": int((g_st != o_st).sum())}
+        if k > 0:
+            gc = res.cand_ids.cpu().numpy()
+            gp = res.cand_probs.cpu().numpy()
+            kk = np.minimum(o_info["k"], k)
+            sets = 0
+            rel = 0.0
+            for r in range(len(g_ids)):
+                n = int(kk[r])
+                if not np.array_equal(gc[r, :n], o_cid[r, :n]):
+                    sets += 1
+                op = o_cp[r, :n]
+                m = op > 0
+                if m.any():
+                    rel = max(rel, float(np.max(np.abs(gp[r, :n][m] - op[m]) / op[m])))
+            out["topk_mismatch_vs_restatement"] = sets
+            out["max_rel_prob_err"] = rel
+        if oracle.have_reference():
+            ref_ids, ref_next = oracle.reference_sample(x, p, seeds)
+            diff = g_ids != ref_ids
+            rows = np.nonzero(diff)[0]
+            tie = np.zeros(len(g_ids), bool)
+            tie[rows] = x[rows, ref_ids[rows]] == x[rows, g_ids[rows]]
+            out["id_mismatch_vs_reference"] = int((diff & ~tie & ~near).sum())
+            out["tie_group_rows"] = int((diff & tie).sum())
+            nxt = []
+            for v in g_st:
+                r = Rng(0)
+                r.state = int(v)
+                nxt.append(r.next())
+            out["rng_mismatch_vs_reference"] = int((np.array(nxt, dtype=np.uint64) != ref_next).sum())
+            if greedy:
+                out["greedy_mismatch_vs_reference"] = int(diff.sum())
+        return out
+    except Exception as e:  # reported, never fatal
+        return {"error": str(e)}
+
+
+def config_bench(s, dev, stream, peak, row0=0, with_parity=True):
+    """BASELINE's five workloads at their own batch sizes (workloads 1 and 4 also
+    greedy): device time per call, the select / merge split, GB/s against the HBM
+    peak, and the parity counts of one checked call.  Small inputs rotate over
+    copies that together exceed L2 (126 MB), so every call reads HBM."""
+    import torch
+    from zeninfer_b200 import SamplingParams, states_to_tensor
+    from zeninfer_b200 import workloads as W
+    out = {}
+    for cfg, wl in W.WORKLOADS.items():
+        B = wl.batch
+        xh = W.generate(cfg, B, row0=row0)
+        copies = max(1, -(-2 * L2_BYTES // (B * ROW_BYTES))) if B * ROW_BYTES < 2 * L2_BYTES else 1
+        X = torch.empty((copies, B, V), dtype=torch.float32, device=dev)
+        X[0].copy_(torch.from_numpy(xh))
+        if copies > 1:
+            X[1:].copy_(X[0].expand(copies - 1, B, V))
+        entry = {"rows": B, "l2": (f"{copies} rotating copies of the input "
+                                   f"({copies * B * ROW_BYTES / 2**20:.0f} MiB)" if copies > 1
+                                   else "input larger than L2")}
+        runs = [("sampled", wl.params)] + ([("greedy", SamplingParams())] if wl.greedy_too else [])
+        for label, p in runs:
+            st = states_to_tensor(wl.row_states(row0, B), dev)
+            ids = torch.empty(B, dtype=torch.int32, device=dev)
+            it = [0]
+
+            def call(p=p, st=st, ids=ids):
+                s.sample(X[it[0] % copies], p, st, out=ids, stream=stream)
+                it[0] += 1
+            for _ in range(5):
+                call()
+            torch.cuda.synchronize()
+            reps = max(20, min(400, int(0.1 / max(B * ROW_BYTES / (peak * 1e9), 1e-6))))
+            steps = []
+            ms = time_device_steps(call, reps, stream, per_step=steps) / reps
+            s.get_timing()
+            s.set_timing(True)
+            time_device_steps(call, 10, stream)
+            kt = s.get_timing()
+            s.set_timing(False)
+            gbs = B * ROW_BYTES / (ms / 1e3) / 1e9
+            r = {"params": describe(p), "us_per_call": ms * 1e3, "rows_per_s": B / (ms / 1e3),
+                 "logits_gbs": gbs, "hbm_frac": gbs / peak,
+                 "per_call_us": {k2: v * 1e3 for k2, v in spread(steps).items() if k2 != "n"},
+                 "select_us": kt["select_ms"] / 10 * 1e3, "merge_us": kt["merge_ms"] / 10 * 1e3,
+                 "large_us": kt["large_ms"] / 10 * 1e3,
+                 "select_gbs": (B * ROW_BYTES / (kt["select_ms"] / 10 / 1e3) / 1e9
+                                if kt["select_ms"] > 0 else None)}
+            if with_parity:
+                r["parity"] = parity_counts(s, dev, xh, p, wl.row_states(row0, B),
+                                            wl.row_seeds(row0, B), stream)
+            entry[label] = r
+        out[str(cfg)] = entry
+        del X
+    return out
+
+
+def describe(p):
+    if p.temp <= 0:
+        parts = ["greedy"]
+    else:
+        parts = [f"temp {p.temp:g}"]
+        if p.top_k > 0:
+            parts.append(f"top-k {p.top_k}")
+        if p.top_p < 1.0:
+            parts.append(f"top-p {p.top_p:g}")
+    if p.repeat_penalty != 1.0:
+        parts.append(f"repeat_penalty {p.repeat_penalty:g}, last {p.repeat_last_n}")
+    return ", ".join(parts)
+
+
+def host_api_bench(x_row):
+    """The drop-in C++ API (include/zen/sample.h) as cmd_generate calls it: one host
+    row per call through zen::sample_token (libzs_sampler.so's sample_shim.cpp),
+    timed by the compiled driver zeninfer_b200/bench_host_api; beside it the
+    reference's own sample_token on one host thread."""
+    import numpy as np
+    exe = os.path.join(ROOT, "zeninfer_b200", "bench_host_api")
+    if not os.path.exists(exe):
+        return {"note": "zeninfer_b200/bench_host_api not built"}
+    out = {"rows_per_call": 1, "path": "host row -> pinned staging -> H2D -> zs_sample -> D2H id"}
+    fd, path = tempfile.mkstemp(suffix=".f32")
+    os.close(fd)
+    try:
+        np.ascontiguousarray(x_row, dtype=np.float32).tofile(path)
+        cases = {"temp 0.7, top-k 40": ("0.7", "40", "1.0", "1.0", "64", "0"),
+                 "temp 0.7, top-k 40, top-p 0.9, repeat_penalty 1.1, last 64, 64-id history":
+                     ("0.7", "40", "0.9", "1.1", "64", "64")}
+        for name, (t, k, tp, pen, ln, hl) in cases.items():
+            r = subprocess.run([exe, path, str(V), "500", t, k, tp, pen, ln, hl],
+                               capture_output=True, text=True, timeout=120)
+            try:
+                res = json.loads(r.stdout.strip().splitlines()[-1])
+            except Exception:
+                res = {"error": (r.stderr or r.stdout)[-300:]}
+            try:
+                import oracle
+                from zeninfer_b200 import SamplingParams
+                if oracle.have_reference():
+                    p = SamplingParams(temp=float(t), top_k=int(k), top_p=float(tp),
+                                       repeat_penalty=float(pen), repeat_last_n=int(ln))
+                    hist = (np.arange(int(hl), dtype=np.int64) * 997 % V).astype(np.int32)[None, :]
+                    row = np.ascontiguousarray(x_row[None, :], dtype=np.float32)
+                    n_ref = 10
+                    t0 = time.perf_counter()
+                    for i in range(n_ref):
+                        oracle.reference_sample(row, p, np.array([i + 1], np.uint64),
+                                                hist if int(hl) else None,
+                                                np.array([int(hl)], np.int32) if int(hl) else None,
+                                                nthreads=1)
+                    res["reference_us_per_call"] = (time.perf_counter() - t0) / n_ref * 1e6
+            except Exception as e:  # reported, never fatal
+                res["reference_note"] = str(e)
+            out[name] = res
+    finally:
+        os.unlink(path)
+    return out
+
+
+def shard_bench(s, dev, stream, x_dev, params, states0, rows, world, rank, steps, warmup,
+                max_over_ranks, barrier):
+    """Vocab-sharded mode over the same rows (N > 1), both exchanges: the whole step,
+    and the partials and the merge alone, so the exchange's share is the rest."""
+    import torch
+    from zeninfer_b200 import Sampler, states_to_tensor
+    from zeninfer_b200.sharding import VocabShardedSampler, vocab_range
+    lo, n_loc = vocab_range(V, world, rank)
+    x_loc = x_dev[:, lo:lo + n_loc]
+    nbytes = Sampler.shard_partial_bytes(rows, V, world, params)
+    res = {"rows": rows, "columns_per_rank": n_loc, "scaling": "strong",
+           "block_area_bytes_per_rank": nbytes}
+    part = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    for owner in (True, False):
+        vs = VocabShardedSampler(s, owner=owner)
+        st2 = states_to_tensor(states0, dev)
+        out2 = torch.empty(rows, dtype=torch.int32, device=dev)
+
+        def shard_step():
+            vs.sample(x_loc, lo, V, params, st2, out=out2, stream=stream)
+
+        for _ in range(warmup):
+            shard_step()
+        torch.cuda.synchronize()
+        barrier()
+        ms_sh = max_over_ranks(time_device_steps(shard_step, steps, stream) / steps)
+        torch.cuda.synchronize()
+        barrier()
+        # the rank's own kernels alone (no collective): partials, and its merge
+        ms_p = time_device_steps(lambda: s.shard_partials(x_loc, lo, V, world, params, part,
+                                                          stream=stream), steps, stream) / steps
+        r0, n = Sampler.shard_owner_rows(rows, world, rank) if owner else (0, rows)
+        gathered = vs._slots  # the blocks of the last step, as its merge read them
+        st3 = states_to_tensor(states0, dev)
+        ms_m = time_device_steps(lambda: s.shard_merge(gathered, world, rows, V, params, st3,
+                                                       out=out2, stream=stream, rows=(r0, n)),
+                                 steps, stream) / steps
+        ms_p, ms_m = max_over_ranks(ms_p), max_over_ranks(ms_m)
+        res["row_owner" if owner else "all_gather"] = {
+            "ms_per_step": ms_sh, "rows_per_s": rows / (ms_sh / 1e3),
+            "partials_ms": ms_p, "merge_ms": ms_m,
+            "exchange_and_rest_ms": max(0.0, ms_sh - ms_p - ms_m),
+            "merged_rows_per_rank": n}
+        barrier()
+    return res
 
 
 def main():
@@ -365,6 +678,10 @@ def main():
     ap.add_argument("--no-lmhead", action="store_true", help="skip the fused lm_head timing")
     ap.add_argument("--no-fullp", action="store_true", help="skip the full-vocabulary top-p timing")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the per-workload timings and parity counts")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="per-workload timings without the parity counts")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     rows = max(1, args.rows)
@@ -440,11 +757,17 @@ def main():
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
-    clocks = ClockSampler(local_rank)
+    try:
+        props = torch.cuda.get_device_properties(dev)
+        pci = (f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0")
+    except Exception:
+        pci = None
+    clocks = ClockSampler(local_rank, pci)
     clocks.start()
     s.get_timing()  # start the per-kernel event sums and launch count afresh
     s.set_timing(True)
-    ms_total = time_device_steps(step, args.steps, stream)
+    step_ms = []
+    ms_total = time_device_steps(step, args.steps, stream, per_step=step_ms)
     s.set_timing(False)
     kt = s.get_timing()
     clk = clocks.stop()
@@ -465,25 +788,17 @@ def main():
     step_gbs = alg_bytes / (ms_step / 1e3) / 1e9
     traffic = committed_traffic(rows)
 
-    # Batch 1 and 256 on the same device (latency-bound and mid-size shapes).
+    # BASELINE's five workloads at their own batch sizes (1, 256, 1024, 512, 4096 rows)
+    # with the select / merge split and the parity counts of one checked call each.
+    by_config = None
+    if rank == 0 and world == 1 and not args.no_configs:
+        by_config = config_bench(s, dev, stream, peak, with_parity=not args.no_parity)
     by_batch = {}
-    for b, cfgw in ((1, 1), (256, 2)):
-        wlb = W.WORKLOADS[cfgw]
-        xb = torch.from_numpy(W.generate(cfgw, b, row0=row0)).to(dev)
-        stb = states_to_tensor(wlb.row_states(row0, b), dev)
-        ob = torch.empty(b, dtype=torch.int32, device=dev)
-        fnb = (lambda xb=xb, stb=stb, ob=ob, p=wlb.params:
-               s.sample(xb, p, stb, out=ob, stream=stream))
-        for _ in range(5):
-            fnb()
-        torch.cuda.synchronize()
-        reps = 200 if b == 1 else 50
-        msb = time_device_steps(fnb, reps, stream) / reps
-        by_batch[str(b)] = {"rows_per_s": b / (msb / 1e3), "us_per_call": msb * 1e3,
-                            "logits_gbs": b * ROW_BYTES / (msb / 1e3) / 1e9,
-                            "hbm_frac": b * ROW_BYTES / (msb / 1e3) / 1e9 / peak,
-                            "params": "temp 0.7, top-k 40" + (", top-p 0.9" if b == 256 else "")}
-        del xb
+    if by_config:
+        for b, cfgw in ((1, "1"), (256, "2")):
+            e = by_config[cfgw]["sampled"]
+            by_batch[str(b)] = {k2: e[k2] for k2 in ("rows_per_s", "us_per_call", "logits_gbs",
+                                                      "hbm_frac", "params")}
     by_batch[str(rows)] = {"rows_per_s": rows / (ms_step / 1e3), "us_per_call": ms_step * 1e3,
                            "logits_gbs": step_gbs, "hbm_frac": step_gbs / peak,
                            "params": "temp 0.7, top-k 50, top-p 0.9"}
@@ -613,30 +928,16 @@ def main():
                "ms_per_step": e2e_ms}
         del x_e2e
 
-    # Vocab-sharded mode over the same rows (N > 1): partials -> all-gather -> merge.
+    # Vocab-sharded mode over the same rows (N > 1): partials -> exchange -> merge.
     sharded = None
     if world > 1:
-        from zeninfer_b200.sharding import VocabShardedSampler, vocab_range
-        lo, n_loc = vocab_range(V, world, rank)
-        x_loc = x_dev[:, lo:lo + n_loc]
-        nbytes = Sampler.shard_partial_bytes(rows, V, world, params)
-        vs = VocabShardedSampler(s)
-        st2 = states_to_tensor(states0, dev)
-        out2 = torch.empty(rows, dtype=torch.int32, device=dev)
+        sharded = shard_bench(s, dev, stream, x_dev, params, states0, rows, world, rank,
+                              args.steps, args.warmup, max_over_ranks, barrier)
 
-        def shard_step():
-            vs.sample(x_loc, lo, V, params, st2, out=out2, stream=stream)
-
-        for _ in range(args.warmup):
-            shard_step()
-        torch.cuda.synchronize()
-        barrier()
-        ms_sh = time_device_steps(shard_step, args.steps, stream) / args.steps
-        torch.cuda.synchronize()
-        barrier()
-        ms_sh = max_over_ranks(ms_sh)
-        sharded = {"rows_per_s": rows / (ms_sh / 1e3), "ms_per_step": ms_sh,
-                   "allgather_bytes_per_rank": nbytes, "scaling": "strong"}
+    # The drop-in C++ API with one host row per call (cmd_generate's call).
+    host_api = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        host_api = host_api_bench(W.generate(1, 1)[0])
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -669,6 +970,7 @@ def main():
                          "kernel": "zs_wselect_kernel",
                          "kernel_ms_per_step": sel_ms, "merge_ms_per_step": merge_ms,
                          "algorithmic_bytes_per_launch": alg_bytes},
+            "per_step_ms": spread(step_ms),
             "by_batch": by_batch,
             "clocks": clk,
             "e2e": e2e,
@@ -678,8 +980,12 @@ def main():
                                        "large": kt["large_launches"]},
             "cpu_baseline": cpu,
         }
+        if by_config:
+            line["by_config"] = by_config
         if sharded:
             line["vocab_sharded"] = sharded
+        if host_api:
+            line["host_api_b1"] = host_api
         if display:
             line["logits_display"] = display
         if decode:

@@ -39,7 +39,7 @@
 extern "C" {
 #endif
 
-#define ZS_ABI_VERSION 2
+#define ZS_ABI_VERSION 3
 
 typedef enum zs_status {
     ZS_OK = 0,
@@ -247,17 +247,24 @@ zs_status zs_logits_stats(zs_handle h, const float* logits, int64_t ld, int32_t 
 
 /* ---------------------------------------------------------------------------------
  * Vocab-sharded sampling (tensor-parallel lm_head layout).  Rank g of n_ranks
- * holds columns [vocab_offset, vocab_offset + n_local) of every row.  Each rank
- *   1. zs_shard_partials: selects its local candidates -> a partial block
+ * holds columns [vocab_offset, vocab_offset + n_local) of every row.  No
+ * counterpart function in the reference (its sampler sees whole rows); per row the
+ * result is sample_token's (src/sample.cpp:32-102) on the whole row.  Each rank
+ *   1. zs_shard_partials: selects its local candidates -> a partial block area
  *      (per row: local top-k keys, local max, local sum-exp, flags);
- *   2. all-gathers the partial blocks (any transport: NCCL, torch.distributed);
- *   3. zs_shard_merge: merges the n_ranks blocks per row and draws.
+ *   2. exchanges blocks (any transport: NCCL, torch.distributed), either
+ *      a. all of them to every rank (all-gather), then zs_shard_merge merges every
+ *         row on every rank; or
+ *      b. row-owner: rank o owns rows zs_shard_owner_rows(o); every rank sends the
+ *         zs_shard_row_spans of o's rows to o, o merges only its rows
+ *         (zs_shard_merge_rows), then the owners' ids and Rng states are
+ *         all-gathered.  The merge work per rank shrinks with n_ranks.
  * Every rank ends with identical ids and rng states.  zs_sample_sharded does the
- * three steps with NCCL itself.  All ranks must pass the same batch, n_vocab_total,
- * n_ranks and params.
+ * whole step with NCCL itself (route b).  All ranks must pass the same batch,
+ * n_vocab_total, n_ranks and params.
  * --------------------------------------------------------------------------------- */
 
-/* Bytes of one rank's partial block (the all-gather send size), for this batch. */
+/* Bytes of one rank's partial block area (the all-gather send size), for this batch. */
 zs_status zs_shard_partial_bytes(int32_t batch, int32_t n_vocab_total, int32_t n_ranks,
                                  const zs_params* params, int32_t params_per_row,
                                  int64_t* out_bytes);
@@ -269,20 +276,65 @@ zs_status zs_shard_partials(zs_handle h, const float* logits_local, int64_t ld, 
                             const int32_t* history_len, void* partial_out, int32_t want_log_z,
                             void* stream);
 
-/* gathered: device, n_ranks partial blocks back to back (rank order). */
+/* gathered: device, n_ranks partial block areas back to back (rank order). */
 zs_status zs_shard_merge(zs_handle h, const void* gathered, int32_t n_ranks, int32_t batch,
                          int32_t n_vocab_total, const zs_params* params, int32_t params_per_row,
                          uint64_t* rng_state, int32_t* out_ids, const zs_extras* extras,
                          void* stream);
 
-/* Steps 1-3 with an ncclComm_t (passed as void*) created by the caller against the
- * NCCL that this process has loaded (libnccl.so.2 is resolved at run time). */
+/* The rows rank `rank` owns in the row-owner exchange: [*row_begin, *row_begin +
+ * *row_count), R = ceil(batch / n_ranks) rows per rank in rank order, so the owners'
+ * shares sit back to back in an array of n_ranks * R entries (the last ranks may own
+ * fewer rows, or none). */
+zs_status zs_shard_owner_rows(int32_t batch, int32_t n_ranks, int32_t rank, int32_t* row_begin,
+                              int32_t* row_count);
+
+/* Byte ranges of one rank's partial block area that hold every block the merge of
+ * rows [row_begin, row_begin + row_count) reads: *n_spans (at most 3) pairs
+ * (offset, length) in spans[0 .. 2 * *n_spans).  The owner of those rows needs these
+ * ranges of every rank's area, each at the same offsets inside that rank's slot of
+ * its gathered buffer. */
+zs_status zs_shard_row_spans(int32_t batch, int32_t n_vocab_total, int32_t n_ranks,
+                             const zs_params* params, int32_t params_per_row, int32_t row_begin,
+                             int32_t row_count, int64_t* spans, int32_t* n_spans);
+
+/* zs_shard_merge for rows [row_begin, row_begin + row_count) only.  `gathered` has
+ * the layout of zs_shard_merge's, but only the zs_shard_row_spans of these rows need
+ * to be filled; only these rows' entries of rng_state, out_ids and extras are read
+ * or written (indexed by row, 0 .. batch - 1). */
+zs_status zs_shard_merge_rows(zs_handle h, const void* gathered, int32_t n_ranks, int32_t batch,
+                              int32_t row_begin, int32_t row_count, int32_t n_vocab_total,
+                              const zs_params* params, int32_t params_per_row,
+                              uint64_t* rng_state, int32_t* out_ids, const zs_extras* extras,
+                              void* stream);
+
+/* The whole sharded step with an ncclComm_t (passed as void*) created by the caller
+ * against the NCCL that this process has loaded (libnccl.so.2 is resolved at run
+ * time); n_ranks must equal the communicator's size.  Without extras it takes the
+ * row-owner route (grouped ncclSend/ncclRecv of the owners' block spans, the owner's
+ * merge, an in-place ncclAllGather of ids and Rng states); with extras (row info or
+ * candidate lists for every row) every rank merges every row after one all-gather.
+ *
+ * Failure handling: with a collective timeout (zs_set_collective_timeout, default
+ * 30000 ms) the call waits, before it returns, until its work on `stream` is done,
+ * polling ncclCommGetAsyncError.  If NCCL reports an error, or the deadline passes
+ * (a rank stopped taking part, so the collective cannot complete), it calls
+ * ncclCommAbort on the communicator, which ends the waiting NCCL kernels, and returns
+ * ZS_ERR_NCCL; the communicator is then freed and must not be used or destroyed
+ * again (create a new one), and out_ids / rng_state hold no valid result.  The
+ * handle stays usable.  A timeout of 0 makes the call asynchronous (no wait, no
+ * abort: the caller watches the communicator).  Non-blocking communicators
+ * (ncclInProgress) are polled within the same deadline.
+ * The reference has no failure path but exiting with "error:" (src/main.cpp:815-818). */
 zs_status zs_sample_sharded(zs_handle h, const float* logits_local, int64_t ld, int32_t batch,
                             int32_t n_local, int32_t vocab_offset, int32_t n_vocab_total,
                             int32_t n_ranks, const zs_params* params, int32_t params_per_row,
                             const int32_t* history, int64_t history_ld,
                             const int32_t* history_len, uint64_t* rng_state, int32_t* out_ids,
                             const zs_extras* extras, void* nccl_comm, void* stream);
+
+/* zs_sample_sharded's bound, per handle, in milliseconds (0 = do not wait). */
+zs_status zs_set_collective_timeout(zs_handle h, int32_t timeout_ms);
 
 /* ---------------------------------------------------------------------------------
  * zs_sample_noalloc: zs_sample without any memory allocation.  No counterpart in

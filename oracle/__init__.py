@@ -302,12 +302,12 @@ def reference_rng_stream(seed: int, count: int):
 
 
 def build(with_reference: bool | None = None) -> None:
-    """make -C oracle (the reference part only where its sources exist)."""
+    """make -C oracle: the restatement, and the reference part where its sources
+    exist (oracle/Makefile's REF_SRC); with_reference=True requires them."""
     import subprocess
-    targets = ["oracle"]
-    ref_src = os.environ.get("REF_SRC", "/root/reference/src")
-    if with_reference or (with_reference is None and os.path.exists(os.path.join(ref_src, "sample.cpp"))):
-        targets.append("ref")
+    targets = ["oracle", "ref" if with_reference else "ref-if-present"]
+    if with_reference is False:
+        targets = ["oracle"]
     r = subprocess.run(["make", "-s", "-C", HERE, *targets], capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError("oracle build failed:\n" + r.stdout + r.stderr)

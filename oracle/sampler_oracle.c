@@ -8,7 +8,7 @@
  * It restates src/sample.cpp of the reference step by step (same f32 / f64
  * expressions, same summation order) with one deliberate change: the shortlist
  * order is total -- value descending, then token id ascending -- where the
- * reference's std::nth_element / std::sort (src/sample.cpp:101-106) order equal
+ * reference's std::nth_element / std::sort (src/sample.cpp:62-67) order equal
  * values in whatever way libstdc++'s introselect leaves them.  NaN logits rank
  * below every number (the reference's comparator is not a strict weak order
  * with NaNs, so its output there is unspecified).  On rows without ties at the

@@ -222,6 +222,51 @@ def test_vocab_shards_on_one_gpu(sampler, world, params):
     np.testing.assert_allclose(res.row_info["log_z"], one.row_info["log_z"], rtol=0, atol=2e-4)
 
 
+@pytest.mark.parametrize("world,rows", [(2, 96), (3, 97), (8, 97)])
+@pytest.mark.parametrize("params", [SamplingParams(temp=0.7, top_k=50, top_p=0.9),
+                                    SamplingParams(temp=0.8, top_k=1024),
+                                    SamplingParams(temp=1.0, top_k=1500, top_p=0.9),
+                                    SamplingParams(temp=1.0, top_p=0.95, repeat_penalty=1.3,
+                                                   repeat_last_n=64)])
+def test_vocab_shard_row_owner_merge_on_one_gpu(sampler, world, rows, params):
+    """The row-owner exchange emulated on one GPU: every rank's partials computed
+    here; each owner's buffer gets only the zs_shard_row_spans of its rows from every
+    rank (everything else is filler bytes), and zs_shard_merge_rows merges only those
+    rows.  Over all owners, ids and rng states equal the unsharded call."""
+    import torch
+    from zeninfer_b200 import Sampler
+    dev = sampler.device
+    x = torch.from_numpy(W.generate(5, rows, row0=700)).to(dev)
+    h, hl = _history(rows, 96, V, 6)
+    hd, hld = torch.from_numpy(h).to(dev), torch.from_numpy(hl).to(dev)
+    nbytes = Sampler.shard_partial_bytes(rows, V, world, params)
+    full = torch.empty(world * nbytes, dtype=torch.uint8, device=dev)
+    for g in range(world):
+        lo, n = sharding.vocab_range(V, world, g)
+        sampler.shard_partials(x[:, lo:lo + n], lo, V, world, params,
+                               full[g * nbytes:(g + 1) * nbytes], hd, hld)
+    st_sh = states_to_tensor(_states(range(rows)), dev)
+    ids_sh = torch.full((rows,), -7, dtype=torch.int32, device=dev)
+    covered = np.zeros(rows, dtype=bool)
+    for o in range(world):
+        r0, n = Sampler.shard_owner_rows(rows, world, o)
+        assert not covered[r0:r0 + n].any()
+        covered[r0:r0 + n] = True
+        owner_buf = torch.full((world * nbytes,), 0xA5, dtype=torch.uint8, device=dev)
+        for off, ln in Sampler.shard_row_spans(rows, V, world, params, r0, n):
+            assert 0 <= off and off + ln <= nbytes
+            for g in range(world):
+                owner_buf[g * nbytes + off:g * nbytes + off + ln] = \
+                    full[g * nbytes + off:g * nbytes + off + ln]
+        sampler.shard_merge(owner_buf, world, rows, V, params, st_sh, out=ids_sh, rows=(r0, n))
+    assert covered.all()
+    sampler.check_device_status()
+    st_one = states_to_tensor(_states(range(rows)), dev)
+    one = sampler.sample(x, params, st_one, hd, hld, sync_check=True)
+    assert np.array_equal(ids_sh.cpu().numpy(), one.ids.cpu().numpy())
+    assert np.array_equal(tensor_to_states(st_sh), tensor_to_states(st_one))
+
+
 def test_argmax_entry(sampler):
     import torch
     rows, n = 16, 10007

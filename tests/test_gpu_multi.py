@@ -1,12 +1,25 @@
 """Two GPUs, one process each: the vocab-sharded sampler over NCCL gives every
-rank the single-GPU ids and rng states, through the package's all-gather path
-(torch.distributed) and through the C ABI's own zs_sample_sharded (an NCCL
-communicator created with the process's libnccl).  Skipped with fewer than two
+rank the single-GPU ids and rng states,
+
+  * through the package's torch.distributed path (VocabShardedSampler): the
+    row-owner exchange (grouped sends of each owner's block spans, the owner's
+    merge, an all-gather of ids and states) and the all-gather route, on a batch
+    that divides by the world size and on one that does not;
+  * through the C ABI's own zs_sample_sharded (an NCCL communicator created with
+    the process's libnccl): the row-owner route, and with row info the route that
+    merges every row on every rank.
+
+Then one rank stops taking part (it never makes its next zs_sample_sharded
+call): the other rank's call must return ZS_ERR_NCCL within its collective
+timeout, having aborted the communicator, and its handle must still sample
+correctly.  The rank that stopped leaves only between steps, with nothing of its
+own in flight; NVLS is off (NCCL_NVLS_ENABLE=0).  Skipped with fewer than two
 GPUs."""
 
 import ctypes as C
 import os
 import socket
+import time
 import traceback
 from datetime import timedelta
 
@@ -16,6 +29,7 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 WORLD = 2
+ZS_ERR_NCCL = 5
 
 
 def _gpus():
@@ -43,30 +57,42 @@ def _worker(rank, port, q):
         from zeninfer_b200 import Sampler, SamplingParams, states_to_tensor, tensor_to_states
         from zeninfer_b200 import sharding
         from zeninfer_b200 import workloads as W
+        from zeninfer_b200._native import SamplerError
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
         torch.cuda.set_device(rank)
         dev = torch.device("cuda", rank)
         dist.init_process_group("nccl", rank=rank, world_size=WORLD,
                                 timeout=timedelta(seconds=30), device_id=dev)
         s = Sampler(rank)
-        rows, V = 384, W.VOCAB
-        x = torch.from_numpy(W.generate(5, rows, row0=900)).to(dev)
+        V = W.VOCAB
+        x_all = torch.from_numpy(W.generate(5, 385, row0=900)).to(dev)
         lo, n = sharding.vocab_range(V, WORLD, rank)
         results = {}
+
+        def single(x, p):
+            st = states_to_tensor(W.WORKLOADS[5].row_states(0, x.shape[0]), dev)
+            ids = s.sample(x, p, st, sync_check=True, row_info=True)
+            return ids.ids.cpu().numpy(), tensor_to_states(st), ids.row_info
+
+        def same(a_ids, a_st, b_ids, b_st):
+            return (bool(np.array_equal(a_ids, b_ids.cpu().numpy())),
+                    bool(np.array_equal(a_st, tensor_to_states(b_st))))
+
         for name, p in (("k50", SamplingParams(temp=0.7, top_k=50, top_p=0.9)),
                         ("greedy", SamplingParams()),
                         ("k256", SamplingParams(temp=1.0, top_p=0.95)),
                         ("k1024", SamplingParams(temp=0.8, top_k=1024))):
-            st0 = W.WORKLOADS[5].row_states(0, rows)
-            st_one = states_to_tensor(st0, dev)
-            one = s.sample(x, p, st_one, sync_check=True).ids.cpu().numpy()
-            st_sh = states_to_tensor(st0, dev)
-            sh = sharding.VocabShardedSampler(s).sample(x[:, lo:lo + n].contiguous(), lo, V, p,
-                                                        st_sh)
-            torch.cuda.synchronize()
-            s.check_device_status()
-            results[name] = (bool(np.array_equal(one, sh.cpu().numpy())),
-                             bool(np.array_equal(tensor_to_states(st_one), tensor_to_states(st_sh))))
+            for rows in ((384, 385) if name == "k50" else (384,)):
+                x = x_all[:rows]
+                one_ids, one_st, _ = single(x, p)
+                for owner in (True, False):
+                    st_sh = states_to_tensor(W.WORKLOADS[5].row_states(0, rows), dev)
+                    sh = sharding.VocabShardedSampler(s, owner=owner).sample(
+                        x[:, lo:lo + n].contiguous(), lo, V, p, st_sh)
+                    torch.cuda.synchronize()
+                    s.check_device_status()
+                    results[f"torch_{name}_{rows}_{'owner' if owner else 'gather'}"] = \
+                        same(one_ids, one_st, sh, st_sh)
         # the C ABI's own NCCL path: a communicator from this process's libnccl
         nccl = C.CDLL("libnccl.so.2")
         uid = NcclUniqueId()
@@ -79,16 +105,49 @@ def _worker(rank, port, q):
         comm = C.c_void_p()
         assert nccl.ncclCommInitRank(C.byref(comm), WORLD, uid, rank) == 0
         p = SamplingParams(temp=0.7, top_k=50, top_p=0.9)
-        st0 = W.WORKLOADS[5].row_states(0, rows)
-        st_one = states_to_tensor(st0, dev)
-        one = s.sample(x, p, st_one, sync_check=True).ids.cpu().numpy()
-        st_c = states_to_tensor(st0, dev)
-        ids_c = s.sample_sharded(x[:, lo:lo + n].contiguous(), lo, V, WORLD, p, st_c, comm.value)
-        torch.cuda.synchronize()
-        s.check_device_status()
-        results["c_abi"] = (bool(np.array_equal(one, ids_c.cpu().numpy())),
-                            bool(np.array_equal(tensor_to_states(st_one), tensor_to_states(st_c))))
-        nccl.ncclCommDestroy(comm)
+        for rows in (384, 385):
+            x = x_all[:rows]
+            one_ids, one_st, one_info = single(x, p)
+            xl = x[:, lo:lo + n].contiguous()
+            st_c = states_to_tensor(W.WORKLOADS[5].row_states(0, rows), dev)
+            ids_c = s.sample_sharded(xl, lo, V, WORLD, p, st_c, comm.value)
+            torch.cuda.synchronize()
+            s.check_device_status()
+            results[f"c_abi_owner_{rows}"] = same(one_ids, one_st, ids_c, st_c)
+            st_c = states_to_tensor(W.WORKLOADS[5].row_states(0, rows), dev)
+            ids_c, info = s.sample_sharded(xl, lo, V, WORLD, p, st_c, comm.value, row_info=True)
+            torch.cuda.synchronize()
+            ok_ids, ok_st = same(one_ids, one_st, ids_c, st_c)
+            results[f"c_abi_full_{rows}"] = (ok_ids and bool(np.array_equal(info["m"],
+                                                                              one_info["m"])),
+                                             ok_st)
+        # A rank stops taking part: rank 1 skips the next step.  Rank 0's call must
+        # come back with ZS_ERR_NCCL inside its timeout, not wait for good.
+        x = x_all[:384]
+        one_ids, one_st, _ = single(x, p)
+        xl = x[:, lo:lo + n].contiguous()
+        if rank == 0:
+            s.set_collective_timeout(2000)
+            st_c = states_to_tensor(W.WORKLOADS[5].row_states(0, 384), dev)
+            t0 = time.monotonic()
+            status = 0
+            try:
+                s.sample_sharded(xl, lo, V, WORLD, p, st_c, comm.value)
+            except SamplerError as e:
+                status = e.status
+            dt = time.monotonic() - t0
+            torch.cuda.synchronize()
+            # the handle still samples correctly after the abort
+            after_ids, after_st, _ = single(x, p)
+            results["dropout"] = (status == ZS_ERR_NCCL and dt < 20.0,
+                                  bool(np.array_equal(after_ids, one_ids) and
+                                       np.array_equal(after_st, one_st)))
+            results["dropout_seconds"] = dt
+        dist.barrier()  # rank 1 waits here until rank 0's call has returned
+        if rank == 1:
+            nccl.ncclCommAbort(comm)  # local: its peer has already aborted
+        else:
+            pass  # rank 0's communicator was aborted (and freed) by zs_sample_sharded
         s.close()
         dist.destroy_process_group()
         q.put((rank, results))
@@ -112,5 +171,9 @@ def test_vocab_shard_two_gpus():
             p.kill()
     for r in range(WORLD):
         assert not isinstance(res[r], str), res[r]
-        for name, (ids_ok, st_ok) in res[r].items():
-            assert ids_ok and st_ok, (r, name, ids_ok, st_ok)
+        for name, val in res[r].items():
+            if name.endswith("_seconds"):
+                continue
+            ids_ok, st_ok = val
+            assert ids_ok and st_ok, (r, name, ids_ok, st_ok, res[r].get("dropout_seconds"))
+    assert "dropout" in res[0]

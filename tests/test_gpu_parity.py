@@ -18,8 +18,12 @@ def _states(seeds):
     return np.asarray([rng_seed(int(s)) for s in seeds], dtype=np.uint64)
 
 
-@pytest.mark.parametrize("cfg,rows", [(1, 1), (2, 256), (3, 256), (4, 256), (5, 512)])
+@pytest.mark.parametrize("cfg,rows", [(1, 1), (2, 256), (3, 1024), (4, 512), (5, 4096)])
 def test_workload_parity(sampler, cfg, rows):
+    """Each workload at its own batch size, every row against the restatement (ids,
+    rng states, shortlist sizes, nucleus sizes, draws, candidate ids and
+    probabilities) and against the unchanged reference (ids; on the tie-heavy
+    workload 4, equal drawn values where libstdc++ orders a tie group its own way)."""
     wl = W.WORKLOADS[cfg]
     x = W.generate(cfg, rows)
     seeds = wl.row_seeds(0, rows)
@@ -33,16 +37,6 @@ def test_workload_parity(sampler, cfg, rows):
         ties = compare_reference(x, g["ids"], p, seeds, tie_ok=(cfg == 4))
         if cfg != 4:
             assert ties == 0
-
-
-def test_workload5_full_batch(sampler):
-    """The benchmark batch, every row against the restatement."""
-    wl = W.WORKLOADS[5]
-    x = W.generate(5, wl.batch)
-    seeds = wl.row_seeds()
-    g = run_gpu(sampler, x, wl.params, _states(seeds), cand_ld=50)
-    o = run_oracle(x, wl.params, _states(seeds), cand_ld=50)
-    compare(g, o)
 
 
 def test_greedy_matches_reference(sampler):

@@ -7,6 +7,11 @@ sharding.all_gather_blocks -- the collective the GPU path uses.  Merging the
 gathered blocks must give the global shortlist of the restatement on every
 rank.  A second test drops one rank before the collective: the survivor gets
 an error from the short process-group timeout instead of waiting forever.
+
+The row-owner exchange (sharding.exchange_owner_blocks and the ids/states
+all-gather) runs on world sizes 2 and 3 with the library's own block spans
+(zs_shard_row_spans, host arithmetic only): every owner must end up with each
+rank's bytes at exactly the spans of its rows.
 """
 
 import os
@@ -113,3 +118,66 @@ def test_dropped_rank_fails_the_collective():
     res = _run("drop")
     assert res[1] == "left"
     assert isinstance(res[0], str) and res[0].startswith("error:"), res[0]
+
+
+def _owner_worker(rank, world, port, batch, q):
+    try:
+        import torch
+        import torch.distributed as dist
+        from zeninfer_b200 import Sampler, SamplingParams, sharding
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=timedelta(seconds=20))
+        out = {}
+        for name, p in (("k50", SamplingParams(temp=0.7, top_k=50, top_p=0.9)),
+                        ("k1500", SamplingParams(temp=1.0, top_k=1500))):
+            nbytes = Sampler.shard_partial_bytes(batch, 151936, world, p)
+            spans = [Sampler.shard_row_spans(batch, 151936, world, p,
+                                             *Sampler.shard_owner_rows(batch, world, o))
+                     for o in range(world)]
+            pattern = lambda g: ((torch.arange(nbytes, dtype=torch.int64) * 7 + g * 31) % 251
+                                 ).to(torch.uint8)
+            slots = torch.zeros(world * nbytes, dtype=torch.uint8)
+            slots[rank * nbytes:(rank + 1) * nbytes] = pattern(rank)
+            sharding.exchange_owner_blocks(slots, nbytes, spans)
+            ok = True
+            for g in range(world):
+                want = pattern(g)
+                for off, ln in spans[rank]:
+                    got = slots[g * nbytes + off:g * nbytes + off + ln]
+                    ok = ok and bool(torch.equal(got, want[off:off + ln]))
+            # the owners' results to every rank: rows r0..r0+n written by their owner only
+            R = (batch + world - 1) // world
+            ids = torch.full((world * R,), -1, dtype=torch.int32)
+            r0, n = Sampler.shard_owner_rows(batch, world, rank)
+            assert r0 == rank * R or n == 0
+            ids[r0:r0 + n] = torch.arange(r0, r0 + n, dtype=torch.int32) * 10 + rank
+            sharding._all_gather_own(ids, R, rank)
+            want_ids = [r * 10 + min(r // R, world - 1) for r in range(batch)]
+            out[name] = (ok, ids[:batch].tolist() == want_ids, len(spans[rank]))
+        q.put((rank, out))
+        dist.destroy_process_group()
+    except Exception:
+        q.put((rank, "exception:" + traceback.format_exc()))
+
+
+@pytest.mark.parametrize("world,batch", [(2, 4096), (2, 5), (3, 7)])
+def test_row_owner_exchange(world, batch):
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_owner_worker, args=(r, world, port, batch, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    for r in range(world):
+        assert not isinstance(res[r], str), res[r]
+        for name, (spans_ok, ids_ok, nspans) in res[r].items():
+            assert spans_ok and ids_ok, (r, name, spans_ok, ids_ok, nspans)

@@ -19,7 +19,8 @@ EXPORTS = (
     "zs_shard_partial_bytes", "zs_shard_partials", "zs_shard_merge", "zs_sample_sharded",
     "zs_sample_noalloc", "zs_set_timing", "zs_get_timing", "zs_logits_stats",
     "zs_selftest_wait_timeout", "zs_decode_step", "zs_lmhead_sample", "zs_lmhead_logits",
-    "zs_set_lmhead_route",
+    "zs_set_lmhead_route", "zs_shard_owner_rows", "zs_shard_row_spans", "zs_shard_merge_rows",
+    "zs_set_collective_timeout",
 )
 
 ZS_OK = 0
@@ -85,6 +86,12 @@ def lib() -> C.CDLL:
                                  C.POINTER(ZsExtras), vp]
     L.zs_sample_sharded.argtypes = [vp, vp, i64, i32, i32, i32, i32, i32, C.POINTER(ZsParams), i32,
                                     vp, i64, vp, vp, vp, C.POINTER(ZsExtras), vp, vp]
+    L.zs_shard_owner_rows.argtypes = [i32, i32, i32, C.POINTER(i32), C.POINTER(i32)]
+    L.zs_shard_row_spans.argtypes = [i32, i32, i32, C.POINTER(ZsParams), i32, i32, i32,
+                                     C.POINTER(i64), C.POINTER(i32)]
+    L.zs_shard_merge_rows.argtypes = [vp, vp, i32, i32, i32, i32, i32, C.POINTER(ZsParams), i32,
+                                      vp, vp, C.POINTER(ZsExtras), vp]
+    L.zs_set_collective_timeout.argtypes = [vp, i32]
     L.zs_selftest_wait_timeout.argtypes = [vp, vp]
     L.zs_lmhead_logits.argtypes = [vp, vp, i64, vp, C.c_float, vp, i32, i32, i32, vp, i64, vp]
     L.zs_lmhead_sample.argtypes = [vp, vp, i64, vp, C.c_float, vp, i32, i32, i32,
@@ -106,7 +113,9 @@ def lib() -> C.CDLL:
                                             "zs_set_timing", "zs_get_timing",
                                             "zs_logits_stats", "zs_selftest_wait_timeout",
                                             "zs_decode_step", "zs_lmhead_sample",
-                                            "zs_lmhead_logits", "zs_set_lmhead_route"):
+                                            "zs_lmhead_logits", "zs_set_lmhead_route",
+                                            "zs_shard_owner_rows", "zs_shard_row_spans",
+                                            "zs_shard_merge_rows", "zs_set_collective_timeout"):
             f.restype = C.c_int
     _lib = L
     return L

@@ -2,6 +2,7 @@
 
     libzs_sampler.so   CUDA kernels (sm_100a) + C ABI + zen:: C++ API
     libzs_workload.so  synthetic logits generator (host C)
+    bench_host_api     timing driver of the drop-in C++ API (zen::sample_token)
 
 Both land next to this file, so they travel with the source tree.  Rebuilds
 only when a source is newer than its library (or force=True).
@@ -23,6 +24,7 @@ INCLUDE = os.path.join(ROOT, "include")
 
 SAMPLER_SO = os.path.join(HERE, "libzs_sampler.so")
 WORKLOAD_SO = os.path.join(HERE, "libzs_workload.so")
+HOST_API_BENCH = os.path.join(HERE, "bench_host_api")
 
 SAMPLER_SOURCES = ["zs_sampler.cu", "zs_noalloc_scratch.cu", "sample_shim.cpp"]
 SAMPLER_DEPS = SAMPLER_SOURCES + ["zs_kernels.cuh", "zs_device.cuh", "zs_stats.cuh", "zs_lmhead.cuh"]
@@ -81,9 +83,23 @@ def build_workload(force: bool = False) -> str:
     return WORKLOAD_SO
 
 
+def build_host_api_bench(force: bool = False) -> str:
+    """The C++ program bench.py runs to time zen::sample_token through the library."""
+    src = os.path.join(CSRC, "bench_host_api.cpp")
+    deps = [src, SAMPLER_SO, os.path.join(INCLUDE, "zen", "sample.h")]
+    if not force and not _stale(HOST_API_BENCH, deps):
+        return HOST_API_BENCH
+    tmp = HOST_API_BENCH + ".tmp"
+    _run(["g++", "-std=c++17", "-O2", HOST_ARCH, f"-I{INCLUDE}", "-o", tmp, src,
+          f"-L{HERE}", "-l:libzs_sampler.so", "-Wl,-rpath,$ORIGIN"])
+    os.replace(tmp, HOST_API_BENCH)
+    return HOST_API_BENCH
+
+
 def build_all(force: bool = False) -> None:
     build_workload(force)
     build_sampler(force)
+    build_host_api_bench(force)
 
 
 if __name__ == "__main__":

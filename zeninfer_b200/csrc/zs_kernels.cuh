@@ -229,6 +229,9 @@ struct MergeArgs {
     WLayout wl[2];
     // every row's blocks are S slice blocks (zs_lmhead_kernel's output)
     int32_t force_slices;
+    // rows merged by this launch: [row0, row1) of the B rows the blocks describe
+    // (the row-owner merge of the vocab-sharded mode takes a share of them)
+    int32_t row0, row1;
 };
 
 struct RowPlan {
@@ -276,12 +279,12 @@ __device__ __forceinline__ RowPlan plan_row(const Params& p, int V_total, const 
 }
 
 // ---- warp-piece layout ----
-__device__ __forceinline__ int64_t wl_bound(int64_t E, int32_t NW, int32_t w) {
+__host__ __device__ __forceinline__ int64_t wl_bound(int64_t E, int32_t NW, int32_t w) {
     return w >= NW ? E : ((int64_t)w * E) / NW;
 }
 
 // The warp whose share holds flattened column x.
-__device__ __forceinline__ int32_t wl_warp_of(int64_t E, int32_t NW, int64_t x) {
+__host__ __device__ __forceinline__ int32_t wl_warp_of(int64_t E, int32_t NW, int64_t x) {
     return (int32_t)(((x + 1) * (int64_t)NW - 1) / E);
 }
 
@@ -1758,7 +1761,7 @@ __global__ void __launch_bounds__(kNC) zs_merge_kernel(const MergeArgs a) {
     CandState& st = *reinterpret_cast<CandState*>(smem_raw);
     const int ctid = threadIdx.x;
     grid_dep_wait();  // the partial blocks come from the kernel before this one
-    for (int row = blockIdx.x; row < a.B; row += gridDim.x) {
+    for (int row = a.row0 + blockIdx.x; row < a.row1; row += gridDim.x) {
         const RowPlan rp = plan_row(load_params(a.row_params, a.shared, row), a.V_total, a.hist,
                                     a.hist_len, a.hist_ld, row);
         if (rp.large) continue;  // drawn by zs_large_kernel
@@ -2177,7 +2180,8 @@ __global__ void __launch_bounds__(kNC, 4) zs_warp_merge_kernel(const MergeArgs a
     WarpSlot& ws = sm.w[warp];
     const unsigned below = lanemask_lt();
     grid_dep_wait();  // the partial blocks come from the kernel before this one
-    for (int row = blockIdx.x * kConsumerWarps + warp; row < a.B; row += gridDim.x * kConsumerWarps) {
+    for (int row = a.row0 + blockIdx.x * kConsumerWarps + warp; row < a.row1;
+         row += gridDim.x * kConsumerWarps) {
         const RowPlan rp = plan_row(load_params(a.row_params, a.shared, row), a.V_total, a.hist,
                                     a.hist_len, a.hist_ld, row);
         if (rp.large) continue;  // drawn by zs_large_kernel

@@ -12,10 +12,12 @@
 #include <dlfcn.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include <cudaTypedefs.h>
@@ -208,27 +210,98 @@ Plan make_plan(int B, int V_cols, int V_total, const zs_params* params, int per_
 // taking the remainder (the largest shard that convention gives).
 int shard_cols(int V_total, int n_ranks) { return V_total / n_ranks + V_total % n_ranks; }
 
+// Byte ranges of one rank's block area that hold every block the merge of rows
+// [r0, r0 + n) reads: the rows' CTA blocks, and in each warp layout all pieces of
+// the warps whose shares touch those rows (block_at's arithmetic).  At most three
+// (offset, length) pairs, in area order; returns how many.
+int row_spans(const Plan& pl, int B, int r0, int n, int64_t spans[3][2]) {
+    int k = 0;
+    if (n <= 0 || r0 < 0 || r0 + n > B) return 0;
+    if (pl.cta_area) {
+        spans[k][0] = (int64_t)r0 * pl.S * pl.part_stride;
+        spans[k][1] = (int64_t)n * pl.S * pl.part_stride;
+        ++k;
+    }
+    for (int c = 0; c < 2; ++c) {
+        const Plan::Warp& w = pl.w[c];
+        if (!w.any) continue;
+        const int32_t w_lo = zs::wl_warp_of(w.E, w.NW, (int64_t)r0 * w.Vn);
+        const int32_t w_hi = zs::wl_warp_of(w.E, w.NW, (int64_t)(r0 + n) * w.Vn - 1);
+        spans[k][0] = w.off + (int64_t)w_lo * w.P * w.stride;
+        spans[k][1] = (int64_t)(w_hi - w_lo + 1) * w.P * w.stride;
+        ++k;
+    }
+    return k;
+}
+
 // ---- NCCL, resolved at run time from the libnccl.so.2 this process uses ----
+// ncclResult_t values used here (nccl.h): ncclSuccess 0, ncclInProgress 7.
+constexpr int kNcclSuccess = 0;
+constexpr int kNcclInProgress = 7;
+// ncclDataType_t: ncclUint8 1, ncclInt32 2, ncclUint64 5.
+constexpr int kNcclUint8 = 1;
+constexpr int kNcclInt32 = 2;
+constexpr int kNcclUint64 = 5;
+
 struct NcclApi {
     typedef int (*AllGatherFn)(const void*, void*, size_t, int, void*, cudaStream_t);
+    typedef int (*SendFn)(const void*, size_t, int, int, void*, cudaStream_t);
+    typedef int (*RecvFn)(void*, size_t, int, int, void*, cudaStream_t);
+    typedef int (*VoidFn)();
+    typedef int (*CommIntFn)(void*, int*);
+    typedef int (*CommFn)(void*);
     typedef const char* (*ErrStrFn)(int);
     AllGatherFn all_gather = nullptr;
+    SendFn send = nullptr;
+    RecvFn recv = nullptr;
+    VoidFn group_start = nullptr;
+    VoidFn group_end = nullptr;
+    CommIntFn user_rank = nullptr;
+    CommIntFn count = nullptr;
+    CommIntFn async_error = nullptr;  // ncclCommGetAsyncError(comm, ncclResult_t*)
+    CommFn abort = nullptr;
     ErrStrFn err_str = nullptr;
     bool tried = false;
+    bool ok = false;
 };
 NcclApi g_nccl;
 std::mutex g_nccl_mu;
 
 bool load_nccl() {
     std::lock_guard<std::mutex> lk(g_nccl_mu);
-    if (g_nccl.tried) return g_nccl.all_gather != nullptr;
+    if (g_nccl.tried) return g_nccl.ok;
     g_nccl.tried = true;
     void* lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
     if (!lib) lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
     if (!lib) return false;
     g_nccl.all_gather = (NcclApi::AllGatherFn)dlsym(lib, "ncclAllGather");
+    g_nccl.send = (NcclApi::SendFn)dlsym(lib, "ncclSend");
+    g_nccl.recv = (NcclApi::RecvFn)dlsym(lib, "ncclRecv");
+    g_nccl.group_start = (NcclApi::VoidFn)dlsym(lib, "ncclGroupStart");
+    g_nccl.group_end = (NcclApi::VoidFn)dlsym(lib, "ncclGroupEnd");
+    g_nccl.user_rank = (NcclApi::CommIntFn)dlsym(lib, "ncclCommUserRank");
+    g_nccl.count = (NcclApi::CommIntFn)dlsym(lib, "ncclCommCount");
+    g_nccl.async_error = (NcclApi::CommIntFn)dlsym(lib, "ncclCommGetAsyncError");
+    g_nccl.abort = (NcclApi::CommFn)dlsym(lib, "ncclCommAbort");
     g_nccl.err_str = (NcclApi::ErrStrFn)dlsym(lib, "ncclGetErrorString");
-    return g_nccl.all_gather != nullptr;
+    g_nccl.ok = g_nccl.all_gather && g_nccl.send && g_nccl.recv && g_nccl.group_start &&
+                g_nccl.group_end && g_nccl.user_rank && g_nccl.count && g_nccl.async_error &&
+                g_nccl.abort;
+    return g_nccl.ok;
+}
+
+std::string nccl_msg(const char* what, int r) {
+    return std::string(what) + ": " + (g_nccl.err_str ? g_nccl.err_str(r) : "error") + " (" +
+           std::to_string(r) + ")";
+}
+
+// Rows the row-owner merge gives rank `rank`: [*r0, *r0 + *n), R = ceil(B / G)
+// rows per rank, so the ranks' shares sit back to back in a [G][R] padded array.
+void owner_rows(int B, int G, int rank, int* r0, int* n) {
+    const int R = (B + G - 1) / G;
+    const int lo = std::min(B, rank * R);
+    *r0 = lo;
+    *n = std::min(B, lo + R) - lo;
 }
 
 }  // namespace
@@ -251,8 +324,10 @@ struct zs_context {
     size_t params_n = 0;
     uint8_t* large = nullptr;
     size_t large_bytes = 0;
-    uint8_t* gather = nullptr;  // zs_sample_sharded send + receive blocks
+    uint8_t* gather = nullptr;  // zs_sample_sharded: every rank's blocks, padded ids/states
     size_t gather_bytes = 0;
+    int32_t coll_timeout_ms = 30000;     // zs_set_collective_timeout
+    cudaEvent_t coll_event = nullptr;    // marks the end of zs_sample_sharded's work
     unsigned* fail_count = nullptr;  // units whose speculative threshold was too high
     int32_t* fail_units = nullptr;
     size_t fail_units_n = 0;
@@ -383,6 +458,8 @@ struct LaunchScope {
 // B200, the two break even between 256 and 591 rows).
 zs_status launch_merge(zs_context* h, const zs::MergeArgs& m, int max_ksel, bool want_lse,
                        cudaStream_t st) {
+    const int rows = m.row1 - m.row0;
+    if (rows <= 0) return ZS_OK;
     LaunchScope scope(h, 1, st);
     // Programmatic dependent launch: the merge may be scheduled while the kernel
     // before it finishes; it waits (grid_dep_wait) before reading any block.
@@ -396,14 +473,14 @@ zs_status launch_merge(zs_context* h, const zs::MergeArgs& m, int max_ksel, bool
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaError_t e;
-    if ((uint32_t)max_ksel <= zs::kWarpMergeMaxK && m.B >= 2 * h->num_sms) {
+    if ((uint32_t)max_ksel <= zs::kWarpMergeMaxK && rows >= 2 * h->num_sms) {
         const int rows_per_cta = zs::kConsumerWarps;
-        cfg.gridDim = dim3(std::max(1, std::min((m.B + rows_per_cta - 1) / rows_per_cta, 8 * h->num_sms)));
+        cfg.gridDim = dim3(std::max(1, std::min((rows + rows_per_cta - 1) / rows_per_cta, 8 * h->num_sms)));
         cfg.dynamicSmemBytes = h->warp_merge_smem;
         e = want_lse ? cudaLaunchKernelEx(&cfg, zs::zs_warp_merge_kernel<true>, m)
                      : cudaLaunchKernelEx(&cfg, zs::zs_warp_merge_kernel<false>, m);
     } else {
-        cfg.gridDim = dim3(std::max(1, std::min(m.B, 4 * h->num_sms)));
+        cfg.gridDim = dim3(std::max(1, std::min(rows, 4 * h->num_sms)));
         cfg.dynamicSmemBytes = h->merge_smem;
         e = want_lse ? cudaLaunchKernelEx(&cfg, zs::zs_merge_kernel<true>, m)
                      : cudaLaunchKernelEx(&cfg, zs::zs_merge_kernel<false>, m);
@@ -423,6 +500,8 @@ zs::MergeArgs merge_args_for(const zs::Args& a, const Plan& pl, const uint8_t* g
     m.S = pl.S;
     m.part_stride = pl.part_stride;
     m.B = a.B;
+    m.row0 = 0;
+    m.row1 = a.B;
     m.V_total = a.V_total;
     m.shared = a.shared;
     m.row_params = a.row_params;
@@ -573,6 +652,59 @@ zs_status launch_select(zs_context* h, const zs::Args& base, const Plan& pl, boo
 
 }  // namespace
 
+namespace {
+
+using Clock = std::chrono::steady_clock;
+
+// A NCCL call's result on a communicator that may be non-blocking: ncclInProgress
+// is polled through ncclCommGetAsyncError until it resolves or the deadline passes.
+int nccl_settle(int r, void* comm, Clock::time_point deadline) {
+    while (r == kNcclInProgress) {
+        if (Clock::now() > deadline) return kNcclInProgress;
+        std::this_thread::sleep_for(std::chrono::microseconds(20));
+        int ae = kNcclInProgress;
+        if (g_nccl.async_error(comm, &ae) != kNcclSuccess) return kNcclInProgress;
+        r = ae;
+    }
+    return r;
+}
+
+// Waits (bounded by the handle's collective timeout) until every operation this
+// call queued on `st` has finished, watching the communicator's asynchronous
+// error.  A peer that stopped taking part leaves the NCCL kernels waiting; at
+// the deadline the communicator is aborted (ncclCommAbort ends its kernels) and
+// ZS_ERR_NCCL returned, so the caller never blocks for good.
+zs_status wait_collectives(zs_context* h, void* comm, cudaStream_t st, Clock::time_point t0) {
+    if (h->coll_timeout_ms <= 0) return ZS_OK;
+    if (!h->coll_event) ZS_CUDA(cudaEventCreateWithFlags(&h->coll_event, cudaEventDisableTiming));
+    ZS_CUDA(cudaEventRecord(h->coll_event, st));
+    const Clock::time_point deadline = t0 + std::chrono::milliseconds(h->coll_timeout_ms);
+    for (;;) {
+        const cudaError_t q = cudaEventQuery(h->coll_event);
+        if (q == cudaSuccess) return ZS_OK;
+        if (q != cudaErrorNotReady) return cuda_fail(q, "waiting for the sharded step");
+        int ae = kNcclSuccess;
+        const int qr = g_nccl.async_error(comm, &ae);
+        const bool failed = qr != kNcclSuccess || (ae != kNcclSuccess && ae != kNcclInProgress);
+        const bool late = Clock::now() > deadline;
+        if (failed || late) {
+            g_nccl.abort(comm);
+            // the aborted kernels return; give the stream a bounded time to drain
+            const Clock::time_point drain = Clock::now() + std::chrono::seconds(10);
+            while (cudaEventQuery(h->coll_event) == cudaErrorNotReady && Clock::now() < drain)
+                std::this_thread::sleep_for(std::chrono::microseconds(200));
+            const std::string why =
+                failed ? nccl_msg("NCCL reported an asynchronous error", qr != kNcclSuccess ? qr : ae)
+                       : "the sharded step did not finish within " +
+                             std::to_string(h->coll_timeout_ms) + " ms (a rank stopped taking part?)";
+            return fail(ZS_ERR_NCCL, why + "; the communicator was aborted and must not be used again");
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+}
+
+}  // namespace
+
 extern "C" {
 
 int zs_abi_version(void) { return ZS_ABI_VERSION; }
@@ -667,7 +799,15 @@ zs_status zs_destroy(zs_handle h) {
         cudaEventDestroy(t.end);
     }
     for (cudaEvent_t ev : h->spare) cudaEventDestroy(ev);
+    if (h->coll_event) cudaEventDestroy(h->coll_event);
     delete h;
+    return ZS_OK;
+}
+
+zs_status zs_set_collective_timeout(zs_handle h, int32_t timeout_ms) {
+    if (!h) return fail(ZS_ERR_INVALID_ARGUMENT, "null handle");
+    if (timeout_ms < 0) return fail(ZS_ERR_INVALID_ARGUMENT, "timeout_ms < 0");
+    h->coll_timeout_ms = timeout_ms;
     return ZS_OK;
 }
 
@@ -1081,6 +1221,8 @@ zs_status zs_lmhead_sample(zs_handle h, const float* hidden, int64_t hidden_ld,
     m.S = a.S;
     m.part_stride = zs::kLmPartStride;
     m.B = batch;
+    m.row0 = 0;
+    m.row1 = batch;
     m.V_total = n_vocab;
     m.shared = a.shared;
     m.row_params = dparams;
@@ -1257,13 +1399,44 @@ zs_status zs_shard_partials(zs_handle h, const float* logits_local, int64_t ld, 
     return launch_partials(h, a, pl, (uint8_t*)partial_out, want_log_z != 0, st);
 }
 
-zs_status zs_shard_merge(zs_handle h, const void* gathered, int32_t n_ranks, int32_t batch,
-                         int32_t n_vocab_total, const zs_params* params, int32_t params_per_row,
-                         uint64_t* rng_state, int32_t* out_ids, const zs_extras* extras,
-                         void* stream) {
-    if (!h || !params || n_ranks <= 0 || batch < 0 || n_vocab_total <= 0)
+zs_status zs_shard_owner_rows(int32_t batch, int32_t n_ranks, int32_t rank, int32_t* row_begin,
+                              int32_t* row_count) {
+    if (!row_begin || !row_count || batch < 0 || n_ranks <= 0 || rank < 0 || rank >= n_ranks)
+        return fail(ZS_ERR_INVALID_ARGUMENT, "bad owner-row arguments");
+    int r0 = 0, n = 0;
+    owner_rows(batch, n_ranks, rank, &r0, &n);
+    *row_begin = r0;
+    *row_count = n;
+    return ZS_OK;
+}
+
+zs_status zs_shard_row_spans(int32_t batch, int32_t n_vocab_total, int32_t n_ranks,
+                             const zs_params* params, int32_t params_per_row, int32_t row_begin,
+                             int32_t row_count, int64_t* spans, int32_t* n_spans) {
+    if (!spans || !n_spans || !params || batch < 0 || n_vocab_total <= 0 || n_ranks <= 0 ||
+        row_begin < 0 || row_count < 0 || (int64_t)row_begin + row_count > batch)
+        return fail(ZS_ERR_INVALID_ARGUMENT, "bad row-span arguments");
+    const Plan pl = make_plan(batch, shard_cols(n_vocab_total, n_ranks), n_vocab_total, params,
+                              params_per_row, kShardLayoutCtas, kShardLayoutWarps, false, n_ranks);
+    int64_t sp[3][2];
+    const int k = row_spans(pl, batch, row_begin, row_count, sp);
+    for (int i = 0; i < 3; ++i) {
+        spans[2 * i] = i < k ? sp[i][0] : 0;
+        spans[2 * i + 1] = i < k ? sp[i][1] : 0;
+    }
+    *n_spans = k;
+    return ZS_OK;
+}
+
+zs_status zs_shard_merge_rows(zs_handle h, const void* gathered, int32_t n_ranks, int32_t batch,
+                              int32_t row_begin, int32_t row_count, int32_t n_vocab_total,
+                              const zs_params* params, int32_t params_per_row,
+                              uint64_t* rng_state, int32_t* out_ids, const zs_extras* extras,
+                              void* stream) {
+    if (!h || !params || n_ranks <= 0 || batch < 0 || n_vocab_total <= 0 || row_begin < 0 ||
+        row_count < 0 || (int64_t)row_begin + row_count > batch)
         return fail(ZS_ERR_INVALID_ARGUMENT, "bad merge arguments");
-    if (batch == 0) return ZS_OK;
+    if (batch == 0 || row_count == 0) return ZS_OK;
     if (!gathered || !out_ids) return fail(ZS_ERR_INVALID_ARGUMENT, "null buffer");
     if (!rng_state && needs_rng(params, params_per_row, batch))
         return fail(ZS_ERR_INVALID_ARGUMENT, "rng_state is null");
@@ -1292,8 +1465,18 @@ zs_status zs_shard_merge(zs_handle h, const void* gathered, int32_t n_ranks, int
         a.cand_ld = (extras->cand_ids || extras->cand_probs) ? extras->cand_ld : 0;
         want_lse = extras->want_log_z && extras->row_info;
     }
-    const zs::MergeArgs m = merge_args_for(a, pl, (const uint8_t*)gathered, n_ranks, pl.bytes);
+    zs::MergeArgs m = merge_args_for(a, pl, (const uint8_t*)gathered, n_ranks, pl.bytes);
+    m.row0 = row_begin;
+    m.row1 = row_begin + row_count;
     return launch_merge(h, m, pl.max_ksel, want_lse, st);
+}
+
+zs_status zs_shard_merge(zs_handle h, const void* gathered, int32_t n_ranks, int32_t batch,
+                         int32_t n_vocab_total, const zs_params* params, int32_t params_per_row,
+                         uint64_t* rng_state, int32_t* out_ids, const zs_extras* extras,
+                         void* stream) {
+    return zs_shard_merge_rows(h, gathered, n_ranks, batch, 0, batch, n_vocab_total, params,
+                               params_per_row, rng_state, out_ids, extras, stream);
 }
 
 zs_status zs_sample_sharded(zs_handle h, const float* logits_local, int64_t ld, int32_t batch,
@@ -1303,33 +1486,111 @@ zs_status zs_sample_sharded(zs_handle h, const float* logits_local, int64_t ld, 
                             const int32_t* history_len, uint64_t* rng_state, int32_t* out_ids,
                             const zs_extras* extras, void* nccl_comm, void* stream) {
     if (!h || !nccl_comm) return fail(ZS_ERR_INVALID_ARGUMENT, "null handle or communicator");
-    if (!load_nccl()) return fail(ZS_ERR_NCCL, "libnccl.so.2 not loadable");
+    if (!load_nccl()) return fail(ZS_ERR_NCCL, "libnccl.so.2 not loadable (or too old)");
+    const Clock::time_point t0 = Clock::now();
     int64_t bytes = 0;
     zs_status s = zs_shard_partial_bytes(batch, n_vocab_total, n_ranks, params, params_per_row, &bytes);
     if (s != ZS_OK) return s;
     if (batch == 0) return ZS_OK;
+    if (!out_ids) return fail(ZS_ERR_INVALID_ARGUMENT, "out_ids is null");
+    const bool with_rng = needs_rng(params, params_per_row, batch);
+    if (!rng_state && with_rng) return fail(ZS_ERR_INVALID_ARGUMENT, "rng_state is null");
+    int G = 0, rank = -1;
+    int r = g_nccl.count(nccl_comm, &G);
+    if (r == kNcclSuccess) r = g_nccl.user_rank(nccl_comm, &rank);
+    if (r != kNcclSuccess) return fail(ZS_ERR_NCCL, nccl_msg("communicator size/rank", r));
+    if (G != n_ranks || rank < 0 || rank >= G)
+        return fail(ZS_ERR_INVALID_ARGUMENT, "n_ranks differs from the communicator's size");
+    cudaStream_t st = (cudaStream_t)stream;
+    // With extras every rank merges every row (row_info and candidate lists for the
+    // whole batch); otherwise each rank merges only the rows it owns.
+    const bool full = extras && (extras->row_info || extras->cand_ids || extras->cand_probs);
+    const int R = (batch + G - 1) / G;
+    const bool padded = !full && (int64_t)R * G != batch;
+    const size_t slots_bytes = (size_t)bytes * G;
+    const size_t ids_off = (slots_bytes + 255) & ~(size_t)255;
+    const size_t st_off = ids_off + (((size_t)R * G * sizeof(int32_t) + 255) & ~(size_t)255);
+    const size_t need = padded ? st_off + (size_t)R * G * sizeof(uint64_t) : slots_bytes;
     {
         DeviceGuard g(h->device);
-        s = grow((void**)&h->gather, &h->gather_bytes, (size_t)bytes * (n_ranks + 1));
+        if (!g.ok) return fail(ZS_ERR_CUDA, "cudaSetDevice failed");
+        s = grow((void**)&h->gather, &h->gather_bytes, need);
         if (s != ZS_OK) return s;
     }
-    uint8_t* send = h->gather;
-    uint8_t* recv = h->gather + bytes;
+    uint8_t* slots = h->gather;  // rank g's blocks at slots + g * bytes
+    uint8_t* mine = slots + (size_t)rank * bytes;
     const bool want_lse = extras && extras->want_log_z && extras->row_info;
     s = zs_shard_partials(h, logits_local, ld, batch, n_local, vocab_offset, n_vocab_total, n_ranks,
-                          params, params_per_row, history, history_ld, history_len, send,
+                          params, params_per_row, history, history_ld, history_len, mine,
                           want_lse ? 1 : 0, stream);
     if (s != ZS_OK) return s;
-    {
-        DeviceGuard g(h->device);
-        const int r = g_nccl.all_gather(send, recv, (size_t)bytes, /*ncclUint8*/ 1, nccl_comm,
-                                        (cudaStream_t)stream);
-        if (r != 0)
-            return fail(ZS_ERR_NCCL, std::string("ncclAllGather: ") +
-                                         (g_nccl.err_str ? g_nccl.err_str(r) : "error"));
+    const Clock::time_point deadline =
+        t0 + std::chrono::milliseconds(h->coll_timeout_ms > 0 ? h->coll_timeout_ms : 3600000);
+    DeviceGuard g(h->device);
+    if (full) {
+        // in place: rank g's blocks already sit at slots + g * bytes
+        r = nccl_settle(g_nccl.all_gather(mine, slots, (size_t)bytes, kNcclUint8, nccl_comm, st),
+                        nccl_comm, deadline);
+        if (r != kNcclSuccess) return fail(ZS_ERR_NCCL, nccl_msg("ncclAllGather", r));
+        s = zs_shard_merge(h, slots, n_ranks, batch, n_vocab_total, params, params_per_row,
+                           rng_state, out_ids, extras, stream);
+        if (s != ZS_OK) return s;
+        return wait_collectives(h, nccl_comm, st, t0);
     }
-    return zs_shard_merge(h, recv, n_ranks, batch, n_vocab_total, params, params_per_row,
-                          rng_state, out_ids, extras, stream);
+    // 1. every rank sends each owner the blocks of the owner's rows
+    const Plan pl = make_plan(batch, shard_cols(n_vocab_total, n_ranks), n_vocab_total, params,
+                              params_per_row, kShardLayoutCtas, kShardLayoutWarps, false, n_ranks);
+    int my_r0 = 0, my_n = 0;
+    owner_rows(batch, G, rank, &my_r0, &my_n);
+    r = g_nccl.group_start();
+    for (int peer = 0; peer < G && r == kNcclSuccess; ++peer) {
+        if (peer == rank) continue;
+        int o_r0 = 0, o_n = 0;
+        owner_rows(batch, G, peer, &o_r0, &o_n);
+        int64_t sp[3][2];
+        const int ks = row_spans(pl, batch, o_r0, o_n, sp);
+        for (int i = 0; i < ks && r == kNcclSuccess; ++i)
+            r = g_nccl.send(mine + sp[i][0], (size_t)sp[i][1], kNcclUint8, peer, nccl_comm, st);
+        const int kr = row_spans(pl, batch, my_r0, my_n, sp);
+        uint8_t* from = slots + (size_t)peer * bytes;
+        for (int i = 0; i < kr && r == kNcclSuccess; ++i)
+            r = g_nccl.recv(from + sp[i][0], (size_t)sp[i][1], kNcclUint8, peer, nccl_comm, st);
+    }
+    {
+        const int re = g_nccl.group_end();
+        if (r == kNcclSuccess) r = re;
+    }
+    r = nccl_settle(r, nccl_comm, deadline);
+    if (r != kNcclSuccess) return fail(ZS_ERR_NCCL, nccl_msg("block exchange (ncclSend/ncclRecv)", r));
+    // 2. the owner merges its rows into [G][R] arrays (the caller's when B = G * R)
+    int32_t* ids_buf = padded ? (int32_t*)(h->gather + ids_off) : out_ids;
+    uint64_t* st_buf = padded ? (uint64_t*)(h->gather + st_off) : rng_state;
+    if (padded && with_rng)
+        ZS_CUDA(cudaMemcpyAsync(st_buf, rng_state, (size_t)batch * sizeof(uint64_t),
+                                cudaMemcpyDeviceToDevice, st));
+    s = zs_shard_merge_rows(h, slots, n_ranks, batch, my_r0, my_n, n_vocab_total, params,
+                            params_per_row, with_rng ? st_buf : nullptr, ids_buf, nullptr, stream);
+    if (s != ZS_OK) return s;
+    // 3. every rank gets every owner's ids and Rng states (in place)
+    r = g_nccl.group_start();
+    if (r == kNcclSuccess)
+        r = g_nccl.all_gather(ids_buf + (size_t)rank * R, ids_buf, (size_t)R, kNcclInt32, nccl_comm, st);
+    if (r == kNcclSuccess && with_rng)
+        r = g_nccl.all_gather(st_buf + (size_t)rank * R, st_buf, (size_t)R, kNcclUint64, nccl_comm, st);
+    {
+        const int re = g_nccl.group_end();
+        if (r == kNcclSuccess) r = re;
+    }
+    r = nccl_settle(r, nccl_comm, deadline);
+    if (r != kNcclSuccess) return fail(ZS_ERR_NCCL, nccl_msg("ids/states all-gather", r));
+    if (padded) {
+        ZS_CUDA(cudaMemcpyAsync(out_ids, ids_buf, (size_t)batch * sizeof(int32_t),
+                                cudaMemcpyDeviceToDevice, st));
+        if (with_rng)
+            ZS_CUDA(cudaMemcpyAsync(rng_state, st_buf, (size_t)batch * sizeof(uint64_t),
+                                    cudaMemcpyDeviceToDevice, st));
+    }
+    return wait_collectives(h, nccl_comm, st, t0);
 }
 
 #ifdef ZS_DEBUG_CHECKS

@@ -379,28 +379,60 @@ class Sampler:
             "zs_shard_partials")
 
     def shard_merge(self, gathered, n_ranks, batch, n_vocab_total, params, rng_state, out=None,
-                    row_info=False, cand_ld=0, want_log_z=False, stream=None) -> SampleResult:
+                    row_info=False, cand_ld=0, want_log_z=False, stream=None,
+                    rows=None) -> SampleResult:
+        """Merges the gathered blocks of every row, or of rows = (row_begin, row_count)
+        only (zs_shard_merge_rows: only those rows' entries of out and rng_state are
+        written)."""
         import torch
         par, per_row = _params_array(params, batch)
         if out is None:
             out = torch.empty(batch, dtype=torch.int32, device=self.device)
+        r0, n = (0, batch) if rows is None else rows
         ex, info_buf, cand_ids, cand_probs = self._extras(batch, row_info, cand_ld, want_log_z)
-        _native.check(self._lib.zs_shard_merge(
-            self._h, gathered.data_ptr(), n_ranks, batch, n_vocab_total, par, per_row,
+        _native.check(self._lib.zs_shard_merge_rows(
+            self._h, gathered.data_ptr(), n_ranks, batch, r0, n, n_vocab_total, par, per_row,
             rng_state.data_ptr() if rng_state is not None else None, out.data_ptr(),
-            C.byref(ex), _stream_ptr(stream)), "zs_shard_merge")
+            C.byref(ex), _stream_ptr(stream)), "zs_shard_merge_rows")
         info = None
         if info_buf is not None:
             info = info_buf.cpu().numpy().view(ROW_INFO_DTYPE).reshape(batch)
         return SampleResult(out, info, cand_ids, cand_probs)
 
+    @staticmethod
+    def shard_owner_rows(batch, n_ranks, rank):
+        """(row_begin, row_count) that `rank` merges in the row-owner exchange."""
+        r0, n = C.c_int32(), C.c_int32()
+        _native.check(_native.lib().zs_shard_owner_rows(batch, n_ranks, rank, C.byref(r0),
+                                                        C.byref(n)), "zs_shard_owner_rows")
+        return r0.value, n.value
+
+    @staticmethod
+    def shard_row_spans(batch, n_vocab_total, n_ranks, params, row_begin, row_count):
+        """[(offset, length), ...]: the byte ranges of a rank's block area that the merge
+        of rows [row_begin, row_begin + row_count) reads."""
+        par, per_row = _params_array(params, batch)
+        sp = (C.c_int64 * 6)()
+        k = C.c_int32()
+        _native.check(_native.lib().zs_shard_row_spans(batch, n_vocab_total, n_ranks, par,
+                                                       per_row, row_begin, row_count, sp,
+                                                       C.byref(k)), "zs_shard_row_spans")
+        return [(sp[2 * i], sp[2 * i + 1]) for i in range(k.value)]
+
+    def set_collective_timeout(self, timeout_ms: int) -> None:
+        """zs_sample_sharded's bound on its collectives (0: asynchronous, no bound)."""
+        _native.check(self._lib.zs_set_collective_timeout(self._h, int(timeout_ms)),
+                      "zs_set_collective_timeout")
+
 
     def sample_sharded(self, logits_local, vocab_offset, n_vocab_total, n_ranks, params,
                        rng_state, nccl_comm, out=None, history=None, history_len=None,
-                       stream=None):
-        """zs_sample_sharded: partials, ncclAllGather on `nccl_comm` (an ncclComm_t
-        as an int) and merge in one call.  Every rank passes the same batch,
-        params and rng states and gets the same ids."""
+                       row_info=False, stream=None):
+        """zs_sample_sharded: the whole vocab-sharded step over `nccl_comm` (an
+        ncclComm_t as an int) in one call: the row-owner exchange, or with
+        row_info=True one all-gather and a merge of every row on every rank.
+        Every rank passes the same batch, params and rng states and gets the same
+        ids.  Returns the ids, or (ids, row info) with row_info=True."""
         import torch
         B, n_local = logits_local.shape
         par, per_row = _params_array(params, B)
@@ -409,11 +441,15 @@ class Sampler:
         hist_ptr = history.data_ptr() if history is not None else None
         hist_len_ptr = history_len.data_ptr() if history_len is not None else None
         hist_ld = history.shape[1] if history is not None else 0
+        ex, info_buf, _, _ = self._extras(B, row_info, 0, False)
         _native.check(self._lib.zs_sample_sharded(
             self._h, logits_local.data_ptr(), logits_local.stride(0), B, n_local, vocab_offset,
             n_vocab_total, n_ranks, par, per_row, hist_ptr, hist_ld, hist_len_ptr,
-            rng_state.data_ptr(), out.data_ptr(), None, C.c_void_p(nccl_comm),
+            rng_state.data_ptr() if rng_state is not None else None, out.data_ptr(),
+            C.byref(ex) if row_info else None, C.c_void_p(nccl_comm),
             _stream_ptr(stream)), "zs_sample_sharded")
+        if row_info:
+            return out, info_buf.cpu().numpy().view(ROW_INFO_DTYPE).reshape(B)
         return out
 
 
