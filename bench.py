@@ -297,6 +297,28 @@ def lmhead_bench(s, dev, stream, hbm_peak):
             out["cpu_reference"] = {"rows_per_s": n / dt, "cores": nth, "kind": "reference",
                                     "sample": f"{n} rows: zen::rmsnorm + zen::matvec_f32 (AVX2) "
                                               "+ zen::sample_token, src/ compiled unchanged"}
+            # Ids of the fused route (bf16 xn and weights, f32 accumulation) against the
+            # reference's own f32 lm_head + sample_token on the same rows and seeds.
+            n = 64
+            hc = (torch.randn(n, E, generator=torch.Generator().manual_seed(4)) * 3)
+            cmp = {"rows": n, "precision": "fused route: xn rounded to bf16, bf16 weights, f32 "
+                                           "accumulation; reference: f32 xn and f32 matvec over "
+                                           "the same (bf16-valued) weights"}
+            s.set_lmhead_route("fused")
+            try:
+                for label, pp in (("sampled", p), ("greedy", SamplingParams())):
+                    st_n = states_to_tensor([i + 1 for i in range(n)], dev)
+                    got = s.lmhead_sample(hc.to(dev), nw, W, pp, st_n, stream=stream)
+                    torch.cuda.synchronize()
+                    got = got.cpu().numpy()
+                    _, lg = oracle.reference_lmhead(hc.numpy(), nw.cpu().numpy(), 1e-6, wf,
+                                                    impl=1, nthreads=nth)
+                    ref, _ = oracle.reference_sample(lg, pp, np.arange(1, n + 1, dtype=np.uint64),
+                                                     nthreads=nth)
+                    cmp[f"{label}_id_mismatch_vs_reference_f32"] = int((got != ref).sum())
+            finally:
+                s.set_lmhead_route("auto")
+            out["parity_vs_reference_f32"] = cmp
     except Exception as e:  # reported, never fatal
         out["cpu_reference"] = {"note": str(e)}
     del W

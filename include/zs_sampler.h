@@ -351,9 +351,11 @@ zs_status zs_set_collective_timeout(zs_handle h, int32_t timeout_ms);
  *   - a row's candidate blocks must fit the scratch: a small batch is cut into
  *     fewer vocabulary slices than zs_sample would use when needed, and a batch
  *     that does not fit even at one slice per row is rejected with
- *     ZS_ERR_INVALID_ARGUMENT before anything is launched (without a repeat
- *     penalty that is above about 9,600 rows at top_k 50, 5,400 at the default
- *     shortlist of 256, 2,700 at top_k 1024);
+ *     ZS_ERR_INVALID_ARGUMENT before anything is launched.  Without a repeat
+ *     penalty, over 151,936 columns, the most rows one call takes are 2,072 at
+ *     top_k 321 to 1280 (e.g. 1024), 14,208 at the default shortlist of 256 and
+ *     about 78,000 at top_k 50: the blocks take about (batch + 2 w) x (16 + 8 k)
+ *     bytes, w = 1,776 warps for k <= 320 and 1,036 above;
  *   - rows whose top_k + repeat window exceed 2048, or whose window exceeds 512,
  *     are rejected (that path needs a workspace sized by the vocabulary);
  *   - no extras (row info, candidate lists).

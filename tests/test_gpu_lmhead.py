@@ -11,8 +11,11 @@ the shortlist in the GEMM epilogue.  Parity, per case:
   * ids and Rng states bit-exact against zs_sample run on those logits, which is
     itself checked against the restatement under the sampler's parity rules.
 The cases below force the fused route (the default takes two passes up to 1024
-rows), so the epilogue's selection is covered at every size; one test checks that
-the routes agree bit for bit."""
+rows), so the epilogue's selection is covered at every size, up to the 2048 and
+4096 rows the default route sends to it; one test checks that the routes agree bit
+for bit, and two build logits that tie exactly across vocabulary slices
+(duplicated weight rows) and at zero (all-zero weight rows, +0 and -0), where the
+slices' shared threshold bound decides which keys may enter a row's buffer."""
 
 import numpy as np
 import pytest
@@ -248,3 +251,98 @@ def test_lmhead_logits_alone(sampler, B):
     got = lg.cpu().numpy()
     assert np.array_equal(got, res["logits"])
     _check_logits(got, hidden, nw, w, np.array([0, 1, B - 1]))
+
+
+@pytest.mark.parametrize("B", [2048, 4096])
+def test_lmhead_fused_at_routed_batches(sampler, B):
+    """The batch sizes the default route sends to the fused kernel, with the
+    benchmark's parameters: ids and Rng states against zs_sample on the kernel's own
+    logits and the restatement on every row; the same ids without the logits
+    output; logits within the bounds on a few rows."""
+    V, E = 151936, 896
+    w, nw = _model(V, E)
+    hidden = _hidden(B, E, 60 + B)
+    p = SamplingParams(temp=0.7, top_k=50, top_p=0.9)
+    seeds = np.arange(B, dtype=np.uint64) + np.uint64(9)
+    res = _run(sampler, hidden, nw, w, p, seeds)
+    _check_logits(res["logits"], hidden, nw, w, np.array([0, 1, B // 2, B - 1]),
+                  against_reference=True)
+    _check_sampling(sampler, res, p, seeds)
+    res2 = _run(sampler, hidden, nw, w, p, seeds, with_logits=False)
+    assert np.array_equal(res2["ids"], res["ids"])
+    assert np.array_equal(res2["states"], res["states"])
+    auto = _run(sampler, hidden, nw, w, p, seeds, with_logits=False, route="auto")
+    assert np.array_equal(auto["ids"], res["ids"])
+
+
+def _tied_model(V, E, seed, zero_rows):
+    """Weights whose second half repeats the first (every logit occurs twice, the
+    copies V/2 columns apart, so in different vocabulary slices) with all-zero rows
+    (and their copies) at `zero_rows`."""
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    half = V // 2
+    base = (torch.randn(half, E, generator=g) * 0.05).to(torch.bfloat16)
+    base[zero_rows] = 0
+    w = torch.cat([base, base], 0)
+    nw = torch.rand(E, generator=g) + 0.5
+    return w, nw
+
+
+@pytest.mark.parametrize("B", [300, 2048])
+def test_lmhead_ties_across_slices(sampler, B):
+    """Random weights, every logit doubled across slices, zero rows: ids and Rng
+    states of the fused route equal zs_sample's on the same logits, bit for bit."""
+    V, E = 151936, 896
+    zero = np.arange(0, V // 2, 1777)
+    w, nw = _tied_model(V, E, 5, zero)
+    hidden = _hidden(B, E, 70)
+    params = _mixed_params(B)
+    seeds = np.arange(B, dtype=np.uint64) + np.uint64(31)
+    res = _run(sampler, hidden, nw, w, params, seeds)
+    lg = res["logits"]
+    assert np.array_equal(lg[:, :V // 2].view(np.uint32), lg[:, V // 2:].view(np.uint32))
+    _check_sampling(sampler, res, params, seeds)
+    two = _run(sampler, hidden, nw, w, params, seeds, route="two_pass")
+    assert np.array_equal(two["ids"], res["ids"])
+    assert np.array_equal(two["states"], res["states"])
+
+
+@pytest.mark.parametrize("B", [300, 2048])
+def test_lmhead_ties_at_zero(sampler, B):
+    """Every row's best logits are exact zeros, tied across slices: all weight rows
+    point against one hidden direction (their logits negative) except zero rows.
+    Hidden rows along that direction (all entries negative) make every product at a
+    zero row -0; rows with a few positive entries add +0 products (the sign the
+    tensor cores give the sums is theirs to choose: either way the ids must match
+    zs_sample's on the same logits).  Shortlists of 20 (inside the
+    tie group of 2 x 19 zeros), 38 (exactly the group) and 50 and 88 (past it)."""
+    import torch
+    V, E = 151936, 896
+    half = V // 2
+    g = torch.Generator().manual_seed(12)
+    d = -(0.5 + torch.rand(E, generator=g))          # all entries negative
+    scale = 0.5 + torch.rand(half, 1, generator=g)
+    base = (scale * (-d)[None, :] * 0.02).to(torch.bfloat16)  # logits < 0 along d
+    zero = np.arange(7, half, 4001)[:19]
+    base[zero] = 0
+    w = torch.cat([base, base], 0)
+    nw = torch.rand(E, generator=g) + 0.5
+    c = 0.5 + torch.rand(B, 1, generator=g)
+    hidden = c * d[None, :]
+    noisy = torch.arange(B) % 2 == 1
+    hidden[noisy] += torch.randn(int(noisy.sum()), E, generator=g) * 0.05
+    hidden[noisy, :8] = hidden[noisy, :8].abs()  # a few positive entries: +0 at zero rows
+    params = [[SamplingParams(temp=0.7, top_k=20), SamplingParams(temp=0.7, top_k=38, top_p=0.9),
+               SamplingParams(temp=1.0, top_k=50), SamplingParams(temp=0.9, top_k=88),
+               SamplingParams()][r % 5] for r in range(B)]
+    seeds = np.arange(B, dtype=np.uint64) + np.uint64(57)
+    res = _run(sampler, hidden, nw, w, params, seeds)
+    lg = res["logits"]
+    zs = np.concatenate([zero, zero + half])
+    assert np.all(lg[:, zs] == 0)
+    assert lg[:, np.setdiff1d(np.arange(V), zs)].max() < 0
+    _check_sampling(sampler, res, params, seeds)
+    two = _run(sampler, hidden, nw, w, params, seeds, route="two_pass")
+    assert np.array_equal(two["ids"], res["ids"])
+    assert np.array_equal(two["states"], res["states"])

@@ -99,3 +99,28 @@ def test_noalloc_rejects_oversized_batch(sampler):
                             torch.cuda.current_stream().cuda_stream)
     assert s == 1  # ZS_ERR_INVALID_ARGUMENT, before any launch
     assert b"fixed scratch" in L.zs_last_error()
+
+
+@pytest.mark.parametrize("top_k,limit", [(1024, 2072), (256, 14208)])
+def test_noalloc_stated_limits(sampler, top_k, limit):
+    """The largest batches include/zs_sampler.h states for the fixed scratch (no
+    penalty, 151,936 columns): `limit` rows run, `limit + 1` are rejected before any
+    launch."""
+    import torch
+    dev = sampler.device
+    x = torch.randn((limit + 1, W.VOCAB), dtype=torch.float32, device=dev)
+    st = states_to_tensor(np.array([rng_seed(i) for i in range(limit + 1)], dtype=np.uint64), dev)
+    out = torch.empty(limit + 1, dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    L = _native.lib()
+    prm = SamplingParams(temp=0.8, top_k=top_k).to_c()
+    stream = torch.cuda.current_stream().cuda_stream
+    s = L.zs_sample_noalloc(x.data_ptr(), x.stride(0), limit, W.VOCAB, C.byref(prm), None, 0,
+                            None, st.data_ptr(), out.data_ptr(), status.data_ptr(), stream)
+    assert s == 0, L.zs_last_error()
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    s = L.zs_sample_noalloc(x.data_ptr(), x.stride(0), limit + 1, W.VOCAB, C.byref(prm), None,
+                            0, None, st.data_ptr(), out.data_ptr(), status.data_ptr(), stream)
+    assert s == 1 and b"fixed scratch" in L.zs_last_error()
+    del x

@@ -252,6 +252,81 @@ __device__ __forceinline__ Params load_params(const Params* rp, const Params& sh
     return rp ? rp[row] : shared;
 }
 
+// The sequential f64 loops of sample_token's tail (src/sample.cpp:69-101) for one
+// thread: the same additions in the same order as the plain loops, with the
+// operands loaded eight at a time ahead of the dependent additions.
+
+// sum of p[0..n), in index order
+__device__ __forceinline__ double seq_sum(const double* p, uint32_t n) {
+    double s = 0.0;
+    uint32_t i = 0;
+    if (n >= 8u) {
+        double v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = p[j];
+        for (i = 8; i + 8u <= n; i += 8u) {
+            double u[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) u[j] = p[i + j];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) s += v[j];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = u[j];
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s += v[j];
+    }
+    for (; i < n; ++i) s += p[i];
+    return s;
+}
+
+// The nucleus loop `while (m < n && acc < top_p) acc += p[m++]`; returns m, acc.
+__device__ __forceinline__ int seq_nucleus(const double* p, int n, double top_p, double& acc_out) {
+    double acc = 0.0;
+    int m = 0;
+    while (m < n && acc < top_p) {
+        double v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = (m + j < n) ? p[m + j] : 0.0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (m < n && acc < top_p) {
+                acc += v[j];
+                ++m;
+            }
+        }
+    }
+    acc_out = acc;
+    return m;
+}
+
+// The inverse-CDF walk: the first i < m with r < acc_i (acc_i the running sum of
+// p[0..i]); returns it, or -1 when none, with acc_i and acc_{i-1} (or the total).
+__device__ __forceinline__ int seq_cdf(const double* p, int m, double r, double& acc_out,
+                                       double& prev_out) {
+    double acc = 0.0, prev = 0.0;
+    for (int i0 = 0; i0 < m; i0 += 8) {
+        double v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = (i0 + j < m) ? p[i0 + j] : 0.0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (i0 + j < m) {
+                prev = acc;
+                acc += v[j];
+                if (r < acc) {
+                    acc_out = acc;
+                    prev_out = prev;
+                    return i0 + j;
+                }
+            }
+        }
+    }
+    acc_out = acc;
+    prev_out = prev;
+    return -1;
+}
+
 __device__ __forceinline__ RowPlan plan_row(const Params& p, int V_total, const int32_t* hist,
                                             const int32_t* hist_len, int64_t hist_ld, int row) {
     RowPlan r;
@@ -1096,9 +1171,7 @@ __device__ void finalize_row(CandState& st, const uint64_t* cand, double* prob, 
         return;
     }
     if (ctid == 0) {
-        double sum = 0.0;
-        for (uint32_t i = 0; i < kk; ++i) sum += prob[i];
-        st.d_sum = sum;
+        st.d_sum = seq_sum(prob, kk);
     }
     csync();
     const double sum = st.d_sum;
@@ -1117,11 +1190,7 @@ __device__ void finalize_row(CandState& st, const uint64_t* cand, double* prob, 
         double rescale = 1.0;
         if (nucleus) {
             double acc = 0.0;
-            m = 0;
-            while (m < (int)kk && acc < (double)p.top_p) {
-                acc += prob[m];
-                ++m;
-            }
+            m = seq_nucleus(prob, (int)kk, (double)p.top_p, acc);
             // The reference's rescale loop adds prob[0..m) in the same order from 0,
             // so its sum is acc itself (prob[0] when no entry was taken).
             if (m == 0) {
@@ -1146,17 +1215,9 @@ __device__ void finalize_row(CandState& st, const uint64_t* cand, double* prob, 
         const double r = rng_uniform(s);
         rng[row] = s;
         double acc = 0.0, prev = 0.0;
-        int pos = m - 1;
-        bool hit = false;
-        for (int i = 0; i < m; ++i) {
-            prev = acc;
-            acc += prob[i];
-            if (r < acc) {
-                pos = i;
-                hit = true;
-                break;
-            }
-        }
+        const int hit_at = seq_cdf(prob, m, r, acc, prev);
+        const bool hit = hit_at >= 0;
+        const int pos = hit ? hit_at : m - 1;
         double d;
         if (hit) {
             const double da = r - prev, db = acc - r;
@@ -1995,8 +2056,7 @@ __device__ void warp_finalize(const uint64_t* cand, double* prob, uint32_t kk, c
         prob[i] = exp(((double)key_value(cand[i]) - (double)max_l) * (double)inv_temp);
     __syncwarp();
     double sum = 0.0;
-    if (lane == 0)
-        for (uint32_t i = 0; i < kk; ++i) sum += prob[i];
+    if (lane == 0) sum = seq_sum(prob, kk);
     sum = __shfl_sync(kFull, sum, 0);
     for (uint32_t i = lane; i < kk; i += 32) {
         const double pi = prob[i] / sum;
@@ -2012,11 +2072,7 @@ __device__ void warp_finalize(const uint64_t* cand, double* prob, uint32_t kk, c
     double rescale = 1.0;
     if (lane == 0 && nucleus) {
         double acc = 0.0;
-        m = 0;
-        while (m < (int)kk && acc < (double)p.top_p) {
-            acc += prob[m];
-            ++m;
-        }
+        m = seq_nucleus(prob, (int)kk, (double)p.top_p, acc);
         // the reference's rescale loop repeats these additions: its sum is acc
         if (m == 0) {
             m = 1;
@@ -2036,17 +2092,9 @@ __device__ void warp_finalize(const uint64_t* cand, double* prob, uint32_t kk, c
         const double r = rng_uniform(st);
         rng[row] = st;
         double acc = 0.0, prev = 0.0;
-        int pos = m - 1;
-        bool hit = false;
-        for (int i = 0; i < m; ++i) {
-            prev = acc;
-            acc += prob[i];
-            if (r < acc) {
-                pos = i;
-                hit = true;
-                break;
-            }
-        }
+        const int hit_at = seq_cdf(prob, m, r, acc, prev);
+        const bool hit = hit_at >= 0;
+        const int pos = hit ? hit_at : m - 1;
         double d;
         if (hit) {
             const double da = r - prev, db = acc - r;
