@@ -231,6 +231,23 @@ zs_status zs_get_timing(zs_handle h, zs_timing* out);
 #define ZS_LMHEAD_ROUTE_TWO_PASS 2
 zs_status zs_set_lmhead_route(zs_handle h, int32_t route);
 
+/* Speculative opening thresholds of zs_sample (and zs_decode_step), per handle.  No
+ * counterpart in the reference.  A long row slice of a long shortlist (top_k or the
+ * default 256 at least 128, no repeat penalty, no log Z) can start its streaming
+ * filter from a threshold sampled from about 3% of its columns instead of ramping up
+ * from its first tile; the merge certifies every such row (its shortlist's last key
+ * is at or above every threshold its slices used, so nothing dropped could rank) and
+ * redoes the rest exactly with the large-shortlist kernel before drawing.  Results
+ * are identical in every mode; only the time differs.
+ *   ZS_SPECULATION_ON        (default)
+ *   ZS_SPECULATION_OFF       every slice ramps up from its first tile
+ *   ZS_SPECULATION_REDO_ALL  speculate, then redo every speculated row (a test of
+ *                            the redo path; slow) */
+#define ZS_SPECULATION_OFF 0
+#define ZS_SPECULATION_ON 1
+#define ZS_SPECULATION_REDO_ALL 2
+zs_status zs_set_speculation(zs_handle h, int32_t mode);
+
 /* The display numbers of zeninfer's `logits` command (src/main.cpp:473-503) for each
  * of `batch` rows of n_vocab f32 logits (device, row r at logits + r * ld):
  *   out_min, out_max  device double [batch]: the row's smallest and largest value,

@@ -192,6 +192,11 @@ __device__ __forceinline__ bool consumer_sync_or(bool pred) {
     return r != 0;
 }
 
+// Asks L2 for the 128-byte line holding p (no register, no wait).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 __device__ __forceinline__ unsigned lanemask_lt() {
     unsigned m;
     asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));

@@ -134,6 +134,13 @@ struct PartialHeader {
 };
 constexpr uint32_t kPartHasId0 = 1u;
 constexpr uint32_t kPartX0Nan = 2u;
+// The block's piece was filtered from a speculative opening threshold whose value
+// order is in the header's third word (that word holds no log-sum-exp then).
+constexpr uint32_t kPartSpec = 4u;
+// Speculative opening thresholds (zs_wselect_kernel): pieces of at least
+// kSpecMinCols columns whose row has a shortlist of at least kSpecMinKeff keys.
+constexpr uint32_t kSpecMinKeff = 128;
+constexpr int kSpecMinCols = 32768;
 constexpr int kPartialHeaderBytes = 16;
 
 struct StageMeta {
@@ -191,6 +198,12 @@ struct Args {
     int32_t wl_P;
     int32_t wl_Vn;
     int32_t wl_class;  // rows this warp launch serves: WCfgS::kClass or WCfgL::kClass
+    // Speculative opening thresholds allowed (zs_wselect_kernel; the merge checks
+    // each row and lists the rows it cannot certify for an exact redo).
+    int32_t spec;
+    // zs_large_kernel: when set, the rows to redo are spec_rows[0 .. *spec_count)
+    const unsigned* spec_count;
+    const int32_t* spec_rows;
 };
 
 // Layout of one warp configuration's blocks (see Args).
@@ -232,6 +245,11 @@ struct MergeArgs {
     // rows merged by this launch: [row0, row1) of the B rows the blocks describe
     // (the row-owner merge of the vocab-sharded mode takes a share of them)
     int32_t row0, row1;
+    // rows whose speculative thresholds the merge cannot certify go to this list
+    // (drawn afterwards by zs_large_kernel); null when no block can be speculative
+    unsigned* spec_count;
+    int32_t* spec_rows;
+    int32_t spec_redo_all;  // list every speculative row (tests of the redo path)
 };
 
 struct RowPlan {
@@ -445,6 +463,7 @@ struct CandState {
     uint32_t count;
     uint32_t removed;
     uint32_t sel_digit, sel_above, sel_cnt;
+    uint32_t spec_ord;  // merge: largest speculative threshold order among the row's blocks
     int32_t abort;
     int32_t x0_nan;
     int32_t m;
@@ -1297,6 +1316,8 @@ __device__ uint32_t merge_partials(CandState& st, const MergeArgs& a, const Bloc
     const int lane = ctid & 31;
     const uint32_t cap = (uint32_t)((bs.stride - kPartialHeaderBytes) / 8);
     const int nb = a.G * bs.n;
+    if (ctid == 0) st.spec_ord = 0u;
+    csync();
     if (nb <= kNC) {
         // Every block header at once (one thread each), offsets by a scan, then
         // all keys gathered in parallel: one memory latency per phase instead of
@@ -1314,6 +1335,11 @@ __device__ uint32_t merge_partials(CandState& st, const MergeArgs& a, const Bloc
                 m = __uint_as_float(hv.z);
                 sx = __uint_as_float(hv.w);
                 z = (hv.y & kPartHasId0) && (hv.y & kPartX0Nan);
+                if (hv.y & kPartSpec) {
+                    atomicMax(&st.spec_ord, hv.z);
+                    m = -INFINITY;  // that word is the threshold, not a log-sum-exp
+                    sx = 0.0f;
+                }
             }
         }
         uint32_t tot;
@@ -1384,7 +1410,11 @@ __device__ uint32_t merge_partials(CandState& st, const MergeArgs& a, const Bloc
             const uint4 hv = st.part_hdr;
             csync();
             const uint32_t cnt = hv.x, flags = hv.y;
-            lse_merge(M, Sx, __uint_as_float(hv.z), __uint_as_float(hv.w), lse_c);
+            if (flags & kPartSpec) {
+                if (ctid == 0 && hv.z > st.spec_ord) st.spec_ord = hv.z;
+            } else {
+                lse_merge(M, Sx, __uint_as_float(hv.z), __uint_as_float(hv.w), lse_c);
+            }
             if ((flags & kPartHasId0) && (flags & kPartX0Nan)) nan0 = true;
             const unsigned long long* keys =
                 reinterpret_cast<const unsigned long long*>(pp + kPartialHeaderBytes);
@@ -1832,6 +1862,18 @@ __global__ void __launch_bounds__(kNC) zs_merge_kernel(const MergeArgs a) {
         ZS_CHECK(rp.ksel <= kKeffFastMax, 16, rp.ksel);
         const BlockSet bs = row_blocks(a, row, rp);
         const uint32_t kk = merge_partials(st, a, bs, row, (uint32_t)rp.ksel, lc, x0n, mm, ss, ctid);
+        csync();
+        if (st.spec_ord != 0u) {  // the same on every thread
+            // Exact only if the row's ksel-th key is at or above every block's
+            // speculative threshold (all keys dropped there were below it).
+            const bool fail = a.spec_redo_all || kk < (uint32_t)rp.ksel ||
+                              ((uint64_t)st.spec_ord << 32) > st.cand[kk - 1];
+            if (fail) {
+                if (ctid == 0 && a.spec_count) a.spec_rows[atomicAdd(a.spec_count, 1u)] = row;
+                csync();
+                continue;
+            }
+        }
         finalize_row(st, st.cand, reinterpret_cast<double*>(st.cand + kProbOffset), kk, rp, x0n,
                      LSE, mm, ss, row, a.rng, a.out_ids, a.info, a.cand_ids, a.cand_probs,
                      a.cand_ld, ctid);
@@ -2140,6 +2182,7 @@ __device__ void warp_merge_row(uint64_t* cand, const MergeArgs& a, int row, cons
     uint64_t tau = 0ull;
     float M = -INFINITY, Sx = 0.0f;
     bool nan0 = false;
+    uint32_t spec_ord = 0u;
     for (int g0 = 0; g0 < nb; g0 += 32) {
         const int b = g0 + lane;
         unsigned long long base = 0ull;
@@ -2154,6 +2197,11 @@ __device__ void warp_merge_row(uint64_t* cand, const MergeArgs& a, int row, cons
                 m = __uint_as_float(hv.z);
                 sx = __uint_as_float(hv.w);
                 z = (hv.y & kPartHasId0) && (hv.y & kPartX0Nan);
+                if (hv.y & kPartSpec) {
+                    spec_ord = hv.z > spec_ord ? hv.z : spec_ord;
+                    m = -INFINITY;  // that word is the threshold, not a log-sum-exp
+                    sx = 0.0f;
+                }
                 base = reinterpret_cast<unsigned long long>(pp + kPartialHeaderBytes);
             }
         }
@@ -2215,6 +2263,16 @@ __device__ void warp_merge_row(uint64_t* cand, const MergeArgs& a, int row, cons
     }
     warp_sort256_desc(cand, count, lane);
     const uint32_t kk = count < ksel ? count : ksel;
+    spec_ord = __reduce_max_sync(kFull, spec_ord);
+    if (spec_ord != 0u) {
+        // Exact only if the row's ksel-th key is at or above every block's
+        // speculative threshold (all keys dropped there were below it).
+        if (a.spec_redo_all || kk < ksel || ((uint64_t)spec_ord << 32) > cand[kk - 1]) {
+            if (lane == 0 && a.spec_count) a.spec_rows[atomicAdd(a.spec_count, 1u)] = row;
+            __syncwarp();
+            return;
+        }
+    }
     warp_finalize(cand, reinterpret_cast<double*>(cand + (CAP - (int)kWarpMergeMaxK)), kk, rp,
                   nan0, LSE, M, Sx, row, a.rng, a.out_ids, a.info, a.cand_ids, a.cand_probs,
                   a.cand_ld, lane);
@@ -2544,10 +2602,99 @@ __device__ __forceinline__ uint32_t wfirst_threshold(const float4* t4, int n4, u
     return __reduce_min_sync(kFull, m);
 }
 
+// The need-th largest of the value orders o[q] (bit q of `alive`) over the warp,
+// or with slack > 0 a value order at or below it with at most need + slack orders
+// at or above it: a radix walk from the highest bit in which the orders differ,
+// one redux.sync count per bit, stopping once its bucket is that small.
+template <int Q>
+__device__ __forceinline__ uint32_t warp_kth_ord(const uint32_t (&o)[Q], uint32_t alive,
+                                                 uint32_t need, uint32_t cnt, uint32_t slack = 0u) {
+    uint32_t lo = 0xffffffffu, hi = 0u;
+#pragma unroll
+    for (int q = 0; q < Q; ++q)
+        if ((alive >> q) & 1u) {
+            lo = o[q] < lo ? o[q] : lo;
+            hi = o[q] > hi ? o[q] : hi;
+        }
+    lo = __reduce_min_sync(kFull, lo);
+    hi = __reduce_max_sync(kFull, hi);
+    for (int bit = (lo == hi) ? -1 : 31 - __clz(lo ^ hi); bit >= 0 && cnt - need > slack; --bit) {
+        uint32_t ones = 0u;
+#pragma unroll
+        for (int q = 0; q < Q; ++q) ones |= ((o[q] >> bit) & 1u) << q;
+        ones &= alive;
+        const uint32_t c1 = __reduce_add_sync(kFull, (uint32_t)__popc(ones));
+        if (c1 >= need) {
+            alive = ones;
+            cnt = c1;
+        } else {
+            alive &= ~ones;
+            need -= c1;
+            cnt -= c1;
+        }
+    }
+    uint32_t m = 0xffffffffu;
+#pragma unroll
+    for (int q = 0; q < Q; ++q)
+        if ((alive >> q) & 1u) m = o[q] < m ? o[q] : m;
+    return __reduce_min_sync(kFull, m);
+}
+
+// Speculative opening threshold of a long piece: a sample of 32 x Q float4s in
+// 128-byte chunks spread evenly over the piece's aligned columns, read with plain
+// loads (the piece's stream reads those lines again soon, mostly from L2).  The
+// threshold is the value order of the need-th largest sample float4 maximum, need
+// four standard deviations (plus 4) above the expected number of sample elements
+// at or above the piece's keff-th value: the piece then keeps about 2 to 4 x keff
+// keys instead of ramping up from its first tile.  Nothing makes this exact: the
+// merge checks each row against the thresholds its blocks carry.  Returns 0 when
+// such a sample cannot cut the piece usefully.
+template <int Q>
+__device__ __forceinline__ uint32_t wspec_threshold(const float* row_logits, const WPiece& pc,
+                                                    uint32_t keff, int lane) {
+    static_assert(Q % 8 == 0 && Q <= 32, "sample float4s per lane");
+    constexpr int S4 = 32 * Q;  // sample float4s
+    constexpr int NC = S4 / 8;  // 128-byte chunks, eight lanes each
+    const int64_t n4 = (pc.e1 - pc.e0) >> 2;
+    if (n4 < 8 * NC || n4 > (1 << 25)) return 0u;
+    const float j = (4.0f * S4) * (float)keff / (float)(pc.c1 - pc.c0);
+    const uint32_t need = (uint32_t)ceilf(j + 4.0f * sqrtf(j) + 4.0f);
+    if (need > (uint32_t)S4 / 4u) return 0u;  // a quarter of the sample passes: no gain
+    const float4* base = reinterpret_cast<const float4*>(row_logits + pc.e0);
+    // chunk c starts at float4 (n4 - 8) * c / (NC - 1): 32-bit arithmetic (a row
+    // has at most 2^31 / 4 float4s; the product stays below 2^32 for NC <= 128)
+    const uint32_t span = (uint32_t)(n4 - 8);
+    // every chunk requested from L2 first, so the batches below wait about one
+    // memory latency in all, not one each
+    if ((lane & 7) == 0) {
+#pragma unroll
+        for (int q = 0; q < Q; ++q) {
+            const uint32_t c = 4u * q + (uint32_t)(lane >> 3);
+            prefetch_l2(base + span * c / (uint32_t)(NC - 1));
+        }
+    }
+    uint32_t o[Q];
+#pragma unroll
+    for (int q0 = 0; q0 < Q; q0 += 8) {
+        float4 v[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const uint32_t c = 4u * (q0 + q) + (uint32_t)(lane >> 3);  // this lane group's chunk
+            v[q] = base[span * c / (uint32_t)(NC - 1) + (uint32_t)(lane & 7)];
+        }
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+            o[q0 + q] = ord_of(fmaxf(fmaxf(v[q].x, v[q].y), fmaxf(v[q].z, v[q].w)));
+    }
+    // any order with need to 1.5 x need sample maxima at or above it will do
+    return warp_kth_ord<Q>(o, Q == 32 ? 0xffffffffu : ((1u << Q) - 1u), need, (uint32_t)S4,
+                           need / 2u);
+}
+
 template <class C, bool LSE>
 __device__ void wend_piece(const Args& a, WarpSel<C>& ws, WState& w, const WPiece& pc,
                            const RowPlan& rp, bool greedy_np, float lc, int32_t gw, int32_t j,
-                           unsigned below, int lane) {
+                           uint32_t spec_ord, unsigned below, int lane) {
     const float* row_logits = a.logits + (int64_t)pc.row * a.ld;
     if (greedy_np) {
         const uint64_t kb = warp_max_u64(w.kb);
@@ -2655,16 +2802,20 @@ __device__ void wend_piece(const Args& a, WarpSel<C>& ws, WState& w, const WPiec
     if (lane == 0) {
         uint4 hv;
         hv.x = n;
-        hv.y = (has0 ? kPartHasId0 : 0u) | ((has0 && x0n) ? kPartX0Nan : 0u);
-        hv.z = __float_as_uint(M);
+        hv.y = (has0 ? kPartHasId0 : 0u) | ((has0 && x0n) ? kPartX0Nan : 0u) |
+               (spec_ord ? kPartSpec : 0u);
+        hv.z = spec_ord ? spec_ord : __float_as_uint(M);  // no log-sum-exp with a speculation
         hv.w = __float_as_uint(Sx);
         __stcg(reinterpret_cast<uint4*>(pp), hv);
     }
     __syncwarp();
 }
 
-template <class C, bool LSE>
+// SPEC: the instantiation that may start long pieces from a sampled threshold
+// (kept apart so the others carry none of its code).
+template <class C, bool LSE, bool SPEC>
 __global__ void __launch_bounds__(C::kWarps * 32, 1) zs_wselect_kernel(const Args a) {
+    static_assert(!(LSE && SPEC), "no speculation with the log-sum-exp");
     extern __shared__ __align__(128) uint8_t smem_raw[];
     WSelSmem<C>& sm = *reinterpret_cast<WSelSmem<C>*>(smem_raw);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -2733,6 +2884,21 @@ __global__ void __launch_bounds__(C::kWarps * 32, 1) zs_wselect_kernel(const Arg
         w.vb = -INFINITY;
         w.lm = -INFINITY;
         w.ls = 0.0f;
+        // A long piece of a long shortlist starts from a sampled threshold instead of
+        // ramping up from its first tile (see wspec_threshold; the merge certifies it).
+        uint32_t spec_ord = 0u;
+        if (SPEC && a.spec && !rp.greedy && !rp.penal && keff >= kSpecMinKeff &&
+            pc.c1 - pc.c0 >= kSpecMinCols) {
+            spec_ord = (pc.c1 - pc.c0 >= 2 * kSpecMinCols)
+                           ? wspec_threshold<32>(row_logits, pc, keff, lane)
+                           : wspec_threshold<16>(row_logits, pc, keff, lane);
+            if (spec_ord != 0u) {
+                w.mode = kWFast;
+                w.tau_f = value_of_ord(spec_ord);
+                w.tau_id = INT32_MAX;  // every element of that value passes
+                w.tau_key = (uint64_t)spec_ord << 32;
+            }
+        }
         // head: the columns before the first 16-byte boundary (at most 3)
         {
             const int nh = pc.e0 - pc.c0;
@@ -2785,7 +2951,7 @@ __global__ void __launch_bounds__(C::kWarps * 32, 1) zs_wselect_kernel(const Arg
             const float x = okt ? row_logits[pc.e1 + lane] : 0.0f;
             wfilter1<C, LSE>(ws, w, okt, x, id_col0 + pc.e1 + lane, greedy_np, keff, lc, below, lane);
         }
-        wend_piece<C, LSE>(a, ws, w, pc, rp, greedy_np, lc, gw, j, below, lane);
+        wend_piece<C, LSE>(a, ws, w, pc, rp, greedy_np, lc, gw, j, spec_ord, below, lane);
     }
     if (!ok) {
         if (lane == 0) set_status(a.status, kStatusTimeout);
@@ -3054,10 +3220,14 @@ __global__ void __launch_bounds__(kNC) zs_large_kernel(const Args a) {
     uint64_t* keys = reinterpret_cast<uint64_t*>(ws);
     uint64_t* tmp = keys + a.V;
     double* prob = reinterpret_cast<double*>(tmp + a.V);
-    for (int row = blockIdx.x; row < a.B; row += gridDim.x) {
+    // Either the large-path rows of the batch, or (spec_count set) the rows a merge
+    // could not certify after speculative thresholds, whatever their path.
+    const int n_work = a.spec_count ? (int)*(volatile const unsigned*)a.spec_count : a.B;
+    for (int wi = blockIdx.x; wi < n_work; wi += gridDim.x) {
+        const int row = a.spec_count ? a.spec_rows[wi] : wi;
         const RowPlan rp = plan_row(load_params(a.row_params, a.shared, row), a.V_total, a.hist,
                                     a.hist_len, a.hist_ld, row);
-        if (!rp.large) continue;
+        if (!rp.large && !a.spec_count) continue;
         const float* x = a.logits + (int64_t)row * a.ld;
         for (int c0 = 0; c0 < a.V; c0 += 4 * kNC) {  // four loads in flight, then the stores
             float v[4];

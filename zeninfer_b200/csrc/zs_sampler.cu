@@ -324,6 +324,8 @@ struct zs_context {
     size_t params_n = 0;
     uint8_t* large = nullptr;
     size_t large_bytes = 0;
+    uint8_t* spec = nullptr;  // speculative thresholds: [0] failed-row count, then the rows
+    size_t spec_bytes = 0;
     uint8_t* gather = nullptr;  // zs_sample_sharded: every rank's blocks, padded ids/states
     size_t gather_bytes = 0;
     int32_t coll_timeout_ms = 30000;     // zs_set_collective_timeout
@@ -338,6 +340,7 @@ struct zs_context {
     };
     bool timing = false;
     int32_t lm_route = ZS_LMHEAD_ROUTE_AUTO;  // zs_set_lmhead_route
+    int32_t spec_mode = ZS_SPECULATION_ON;    // zs_set_speculation
     std::vector<TimedLaunch> timed;      // recorded since the last zs_get_timing
     std::vector<cudaEvent_t> spare;      // events free for reuse
     int64_t launches = 0;                // kernel launches since the last zs_get_timing
@@ -531,13 +534,15 @@ template <class C>
 zs_status setup_wselect(size_t* smem, int* warps, int num_sms) {
     *smem = sizeof(zs::WSelSmem<C>);
     cudaError_t e;
-    if ((e = cudaFuncSetAttribute(zs::zs_wselect_kernel<C, true>,
+    if ((e = cudaFuncSetAttribute(zs::zs_wselect_kernel<C, true, false>,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)*smem)) != cudaSuccess ||
-        (e = cudaFuncSetAttribute(zs::zs_wselect_kernel<C, false>,
+        (e = cudaFuncSetAttribute(zs::zs_wselect_kernel<C, false, false>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)*smem)) != cudaSuccess ||
+        (e = cudaFuncSetAttribute(zs::zs_wselect_kernel<C, false, true>,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)*smem)) != cudaSuccess)
         return cuda_fail(e, "cudaFuncSetAttribute zs_wselect_kernel");
     int per_sm = 0;
-    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, zs::zs_wselect_kernel<C, false>,
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, zs::zs_wselect_kernel<C, false, false>,
                                                            C::kWarps * 32, *smem)) != cudaSuccess)
         return cuda_fail(e, "occupancy query");
     if (per_sm < 1) return fail(ZS_ERR_NO_DEVICE, "zs_wselect_kernel does not fit an SM");
@@ -561,9 +566,11 @@ zs_status launch_wselect(zs_context* h, zs::Args a, const Plan& pl, uint8_t* blo
     const size_t smem = h->wsel_smem[C::kClass];
     LaunchScope scope(h, 0, st);
     if (want_lse)
-        zs::zs_wselect_kernel<C, true><<<grid, C::kWarps * 32, smem, st>>>(a);
+        zs::zs_wselect_kernel<C, true, false><<<grid, C::kWarps * 32, smem, st>>>(a);
+    else if (a.spec && L.max_ksel >= (int)zs::kSpecMinKeff)
+        zs::zs_wselect_kernel<C, false, true><<<grid, C::kWarps * 32, smem, st>>>(a);
     else
-        zs::zs_wselect_kernel<C, false><<<grid, C::kWarps * 32, smem, st>>>(a);
+        zs::zs_wselect_kernel<C, false, false><<<grid, C::kWarps * 32, smem, st>>>(a);
     ZS_CUDA(cudaGetLastError());
     return ZS_OK;
 }
@@ -614,6 +621,25 @@ zs_status ensure_fail_units(zs_context* h, int64_t units) {
 
 // zs_sample's launches: partial blocks in the handle's scratch, the merge (which
 // sorts and draws every row of the two fast paths), then the large path.
+// Blocks per CTA of the exact redo of rows whose speculative thresholds their
+// merge could not certify (zs_large_kernel over a device list; normally empty).
+constexpr int kSpecRedoCtas = 8;
+
+zs_status launch_large(zs_context* h, zs::Args a, int grid, bool want_lse, cudaStream_t st) {
+    const int64_t per_cta = ((int64_t)a.V * 24 + 255) & ~255LL;
+    zs_status s = grow((void**)&h->large, &h->large_bytes, (size_t)per_cta * grid);
+    if (s != ZS_OK) return s;
+    a.large_ws = h->large;
+    a.large_ws_per_cta = per_cta;
+    LaunchScope scope(h, 2, st);
+    if (want_lse)
+        zs::zs_large_kernel<true><<<grid, zs::kNC, h->merge_smem, st>>>(a);
+    else
+        zs::zs_large_kernel<false><<<grid, zs::kNC, h->merge_smem, st>>>(a);
+    ZS_CUDA(cudaGetLastError());
+    return ZS_OK;
+}
+
 zs_status launch_select(zs_context* h, const zs::Args& base, const Plan& pl, bool want_lse,
                         cudaStream_t st) {
     zs::Args a = base;
@@ -626,26 +652,42 @@ zs_status launch_select(zs_context* h, const zs::Args& base, const Plan& pl, boo
     }
     a.fail_count = h->fail_count;
     a.fail_units = h->fail_units;
+    // Speculative opening thresholds for the warp paths' long shortlists: the
+    // merge lists the rows it cannot certify and zs_large_kernel redoes them.
+    const bool spec = h->spec_mode != ZS_SPECULATION_OFF && !want_lse && a.mode == 0 &&
+                      a.V >= zs::kSpecMinCols &&
+                      ((pl.w[0].launch && pl.w[0].max_ksel >= (int)zs::kSpecMinKeff) ||
+                       (pl.w[1].launch && pl.w[1].max_ksel >= (int)zs::kSpecMinKeff));
+    unsigned* spec_count = nullptr;
+    int32_t* spec_rows = nullptr;
+    if (spec) {
+        s = grow((void**)&h->spec, &h->spec_bytes, 256 + (size_t)a.B * sizeof(int32_t));
+        if (s != ZS_OK) return s;
+        spec_count = reinterpret_cast<unsigned*>(h->spec);
+        spec_rows = reinterpret_cast<int32_t*>(h->spec + 256);
+        ZS_CUDA(cudaMemsetAsync(spec_count, 0, sizeof(unsigned), st));
+        a.spec = 1;
+    }
     s = launch_partials(h, a, pl, h->part, want_lse, st);
     if (s != ZS_OK) return s;
     if (pl.w[0].any || pl.w[1].any || pl.cta_area) {
-        const zs::MergeArgs m = merge_args_for(a, pl, h->part, 1, 0);
+        zs::MergeArgs m = merge_args_for(a, pl, h->part, 1, 0);
+        m.spec_count = spec_count;
+        m.spec_rows = spec_rows;
+        m.spec_redo_all = h->spec_mode == ZS_SPECULATION_REDO_ALL ? 1 : 0;
         s = launch_merge(h, m, pl.max_ksel, want_lse, st);
         if (s != ZS_OK) return s;
     }
     if (pl.any_large) {
-        const int lgrid = std::max(1, std::min(a.B, h->num_sms));
-        const int64_t per_cta = ((int64_t)a.V * 24 + 255) & ~255LL;
-        s = grow((void**)&h->large, &h->large_bytes, (size_t)per_cta * lgrid);
+        s = launch_large(h, a, std::max(1, std::min(a.B, h->num_sms)), want_lse, st);
         if (s != ZS_OK) return s;
-        a.large_ws = h->large;
-        a.large_ws_per_cta = per_cta;
-        LaunchScope scope(h, 2, st);
-        if (want_lse)
-            zs::zs_large_kernel<true><<<lgrid, zs::kNC, h->merge_smem, st>>>(a);
-        else
-            zs::zs_large_kernel<false><<<lgrid, zs::kNC, h->merge_smem, st>>>(a);
-        ZS_CUDA(cudaGetLastError());
+    }
+    if (spec) {
+        zs::Args r = a;
+        r.spec_count = spec_count;
+        r.spec_rows = spec_rows;
+        s = launch_large(h, r, std::max(1, std::min(a.B, kSpecRedoCtas)), want_lse, st);
+        if (s != ZS_OK) return s;
     }
     return ZS_OK;
 }
@@ -785,6 +827,7 @@ zs_status zs_destroy(zs_handle h) {
     cudaFree(h->status);
     cudaFree(h->params);
     cudaFree(h->large);
+    cudaFree(h->spec);
     cudaFree(h->gather);
     cudaFree(h->fail_count);
     cudaFree(h->fail_units);
@@ -814,6 +857,14 @@ zs_status zs_set_collective_timeout(zs_handle h, int32_t timeout_ms) {
 zs_status zs_set_timing(zs_handle h, int32_t enable) {
     if (!h) return fail(ZS_ERR_INVALID_ARGUMENT, "null handle");
     h->timing = enable != 0;
+    return ZS_OK;
+}
+
+zs_status zs_set_speculation(zs_handle h, int32_t mode) {
+    if (!h) return fail(ZS_ERR_INVALID_ARGUMENT, "null handle");
+    if (mode != ZS_SPECULATION_OFF && mode != ZS_SPECULATION_ON && mode != ZS_SPECULATION_REDO_ALL)
+        return fail(ZS_ERR_INVALID_ARGUMENT, "unknown speculation mode");
+    h->spec_mode = mode;
     return ZS_OK;
 }
 

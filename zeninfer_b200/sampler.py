@@ -419,6 +419,16 @@ class Sampler:
                                                        C.byref(k)), "zs_shard_row_spans")
         return [(sp[2 * i], sp[2 * i + 1]) for i in range(k.value)]
 
+    _SPEC_MODES = {"off": 0, "on": 1, "redo_all": 2}
+
+    def set_speculation(self, mode: str) -> None:
+        """zs_set_speculation: "on" (default), "off", or "redo_all" (every speculated
+        row redone exactly: a test of the redo path)."""
+        if mode not in self._SPEC_MODES:
+            raise ValueError(f"speculation mode must be one of {sorted(self._SPEC_MODES)}")
+        _native.check(self._lib.zs_set_speculation(self._h, self._SPEC_MODES[mode]),
+                      "zs_set_speculation")
+
     def set_collective_timeout(self, timeout_ms: int) -> None:
         """zs_sample_sharded's bound on its collectives (0: asynchronous, no bound)."""
         _native.check(self._lib.zs_set_collective_timeout(self._h, int(timeout_ms)),
