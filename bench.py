@@ -551,6 +551,22 @@ def config_bench(s, dev, stream, peak, row0=0, with_parity=True):
             reps = max(20, min(400, int(0.1 / max(B * ROW_BYTES / (peak * 1e9), 1e-6))))
             steps = []
             ms = time_device_steps(call, reps, stream, per_step=steps) / reps
+            # the same calls captured in a CUDA graph and replayed: device time without
+            # the host's per-call work (bindings, planning, launches)
+            graph_us = None
+            try:
+                n_cap = 16
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    for q in range(n_cap):
+                        s.sample(X[q % copies], p, st, out=ids)
+                graph.replay()
+                torch.cuda.synchronize()
+                reps_g = max(2, reps // n_cap)
+                graph_us = time_device_steps(graph.replay, reps_g, stream) / (reps_g * n_cap) * 1e3
+                del graph
+            except Exception as e:  # reported, never fatal
+                graph_us = f"capture failed: {e}"
             s.get_timing()
             s.set_timing(True)
             time_device_steps(call, 10, stream)
@@ -558,6 +574,7 @@ def config_bench(s, dev, stream, peak, row0=0, with_parity=True):
             s.set_timing(False)
             gbs = B * ROW_BYTES / (ms / 1e3) / 1e9
             r = {"params": describe(p), "us_per_call": ms * 1e3, "rows_per_s": B / (ms / 1e3),
+                 "us_per_call_graph": graph_us,
                  "logits_gbs": gbs, "hbm_frac": gbs / peak,
                  "per_call_us": {k2: v * 1e3 for k2, v in spread(steps).items() if k2 != "n"},
                  "select_us": kt["select_ms"] / 10 * 1e3, "merge_us": kt["merge_ms"] / 10 * 1e3,
@@ -677,8 +694,47 @@ def shard_bench(s, dev, stream, x_dev, params, states0, rows, world, rank, steps
             "ms_per_step": ms_sh, "rows_per_s": rows / (ms_sh / 1e3),
             "partials_ms": ms_p, "merge_ms": ms_m,
             "exchange_and_rest_ms": max(0.0, ms_sh - ms_p - ms_m),
-            "merged_rows_per_rank": n}
+            "merged_rows_per_rank": n, "path": "torch.distributed (NCCL) around the C ABI"}
         barrier()
+    # The C ABI's own zs_sample_sharded over an NCCL communicator of this process's
+    # libnccl (asynchronous: collective timeout 0), the path a C++ caller takes.
+    try:
+        import ctypes as C
+        import torch.distributed as dist
+
+        class NcclUniqueId(C.Structure):
+            _fields_ = [("internal", C.c_char * 128)]
+        nccl = C.CDLL("libnccl.so.2")
+        uid = NcclUniqueId()
+        if rank == 0 and nccl.ncclGetUniqueId(C.byref(uid)) != 0:
+            raise RuntimeError("ncclGetUniqueId failed")
+        obj = [C.string_at(C.addressof(uid), C.sizeof(uid)) if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        C.memmove(C.addressof(uid), obj[0], C.sizeof(uid))
+        comm = C.c_void_p()
+        if nccl.ncclCommInitRank(C.byref(comm), world, uid, rank) != 0:
+            raise RuntimeError("ncclCommInitRank failed")
+        st4 = states_to_tensor(states0, dev)
+        out4 = torch.empty(rows, dtype=torch.int32, device=dev)
+        xl = x_loc.contiguous() if x_loc.stride(1) != 1 else x_loc
+
+        def c_step():
+            s.sample_sharded(xl, lo, V, world, params, st4, comm.value, out=out4, stream=stream)
+        s.set_collective_timeout(60000)  # warm-up calls wait, bounded
+        for _ in range(warmup):
+            c_step()
+        s.set_collective_timeout(0)  # timed calls are stream-ordered only
+        torch.cuda.synchronize()
+        barrier()
+        ms_c = max_over_ranks(time_device_steps(c_step, steps, stream) / steps)
+        torch.cuda.synchronize()
+        barrier()
+        res["c_abi_row_owner"] = {"ms_per_step": ms_c, "rows_per_s": rows / (ms_c / 1e3),
+                                  "path": "zs_sample_sharded (NCCL send/recv + all-gather inside)"}
+        s.set_collective_timeout(30000)
+        nccl.ncclCommDestroy(comm)
+    except Exception as e:  # reported, never fatal
+        res["c_abi_note"] = str(e)
     return res
 
 

@@ -161,14 +161,16 @@ def test_vocab_shard_two_gpus():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, port, q)) for r in range(WORLD)]
+    procs = [ctx.Process(target=_worker, args=(r, port, q), daemon=True) for r in range(WORLD)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=240) for _ in procs)
-    for p in procs:
-        p.join(timeout=60)
-        if p.is_alive():
-            p.kill()
+    try:
+        res = dict(q.get(timeout=240) for _ in procs)
+    finally:  # never leave a rank behind, whatever happened
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
     for r in range(WORLD):
         assert not isinstance(res[r], str), res[r]
         for name, val in res[r].items():

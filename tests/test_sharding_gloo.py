@@ -90,14 +90,16 @@ def _run(mode):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, q), daemon=True) for r in range(2)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=120) for _ in procs)
-    for p in procs:
-        p.join(timeout=60)
-        if p.is_alive():
-            p.kill()
+    try:
+        res = dict(q.get(timeout=120) for _ in procs)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
     return res
 
 
@@ -168,15 +170,17 @@ def test_row_owner_exchange(world, batch):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_owner_worker, args=(r, world, port, batch, q))
+    procs = [ctx.Process(target=_owner_worker, args=(r, world, port, batch, q), daemon=True)
              for r in range(world)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=120) for _ in procs)
-    for p in procs:
-        p.join(timeout=60)
-        if p.is_alive():
-            p.kill()
+    try:
+        res = dict(q.get(timeout=120) for _ in procs)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
     for r in range(world):
         assert not isinstance(res[r], str), res[r]
         for name, (spans_ok, ids_ok, nspans) in res[r].items():

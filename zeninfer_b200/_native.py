@@ -20,7 +20,7 @@ EXPORTS = (
     "zs_sample_noalloc", "zs_set_timing", "zs_get_timing", "zs_logits_stats",
     "zs_selftest_wait_timeout", "zs_decode_step", "zs_lmhead_sample", "zs_lmhead_logits",
     "zs_set_lmhead_route", "zs_shard_owner_rows", "zs_shard_row_spans", "zs_shard_merge_rows",
-    "zs_set_collective_timeout", "zs_set_speculation",
+    "zs_set_collective_timeout", "zs_set_speculation", "zs_set_small_batch",
 )
 
 ZS_OK = 0
@@ -93,6 +93,7 @@ def lib() -> C.CDLL:
                                       vp, vp, C.POINTER(ZsExtras), vp]
     L.zs_set_collective_timeout.argtypes = [vp, i32]
     L.zs_set_speculation.argtypes = [vp, i32]
+    L.zs_set_small_batch.argtypes = [vp, i32]
     L.zs_selftest_wait_timeout.argtypes = [vp, vp]
     L.zs_lmhead_logits.argtypes = [vp, vp, i64, vp, C.c_float, vp, i32, i32, i32, vp, i64, vp]
     L.zs_lmhead_sample.argtypes = [vp, vp, i64, vp, C.c_float, vp, i32, i32, i32,
@@ -117,7 +118,7 @@ def lib() -> C.CDLL:
                                             "zs_lmhead_logits", "zs_set_lmhead_route",
                                             "zs_shard_owner_rows", "zs_shard_row_spans",
                                             "zs_shard_merge_rows", "zs_set_collective_timeout",
-                                            "zs_set_speculation"):
+                                            "zs_set_speculation", "zs_set_small_batch"):
             f.restype = C.c_int
     _lib = L
     return L

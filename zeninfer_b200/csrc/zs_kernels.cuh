@@ -24,6 +24,8 @@
 
 #include <type_traits>
 
+#include <cooperative_groups.h>
+
 #include "zs_device.cuh"
 
 namespace zs {
@@ -3305,4 +3307,277 @@ __global__ void __launch_bounds__(kNC) zs_large_kernel(const Args a) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// zs_small_kernel: a small batch (decode-sized, a few rows) in ONE launch.
+// One thread block cluster of kSmallCl CTAs per row.  CTA r of a cluster holds
+// the r-th slice of the row's columns in registers (coalesced float4 loads, all
+// of a thread's loads in flight at once).  Each CTA keeps its slice's keys at or
+// above the ksel-th largest of its threads' maximum keys (kth_of_proposals: ksel
+// different keys of the slice reach it, so nothing below it can be in the row's
+// shortlist), cuts them to at most ksel + slack (compact_select) and publishes
+// them in its own shared memory with that threshold.  After a cluster barrier,
+// CTA 0 reads every CTA's keys through distributed shared memory, keeping those
+// at or above the largest published threshold (every CTA has ksel keys above
+// its own), selects and sorts the exact top-ksel, and after a second cluster
+// barrier (which keeps the other CTAs' shared memory alive until CTA 0 has read
+// it) runs the f64 tail of sample_token (finalize_row).  No spin-waits: the
+// cluster barriers are hardware barriers every CTA reaches exactly twice.
+// Serves rows without a repeat penalty, shortlists up to kGroupMaxK, no log Z,
+// 16-byte aligned rows of at most kSmallMaxCols columns (the host checks).
+// ---------------------------------------------------------------------------
+constexpr int kSmallCl = 16;  // CTAs per row (a non-portable cluster size)
+constexpr int kSmallNJ = 12;  // float4s per thread
+constexpr int kSmallMaxCols = kSmallCl * kNC * 4 * kSmallNJ;  // 196,608
+constexpr int kSmallMinCols = kSmallCl * kNC * 4;             // every thread holds a float4
+
+struct SmallSmem {
+    CandState st;             // this CTA's candidates; on CTA 0 also the row's merge
+    uint64_t pub[kCandCap];   // this CTA's published keys
+    uint64_t pub_tau;         // at least ksel of this slice's keys are >= pub_tau
+    uint32_t pub_n;
+    int32_t x0_nan;
+    uint32_t g_off[kSmallCl];  // CTA 0: first key of each CTA in the concatenated list
+    uint32_t g_all;            // CTA 0: keys published in all
+};
+
+__global__ void __launch_bounds__(kNC, 1) zs_small_kernel(const Args a) {
+    namespace cg = cooperative_groups;
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    SmallSmem& sm = *reinterpret_cast<SmallSmem*>(smem_raw);
+    CandState& st = sm.st;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int crank = (int)cluster.block_rank();
+    const int row = (int)blockIdx.x / kSmallCl;
+    const int ctid = (int)threadIdx.x, lane = ctid & 31;
+    const RowPlan rp = plan_row(load_params(a.row_params, a.shared, row), a.V_total, nullptr,
+                                nullptr, 0, row);
+    const uint32_t ksel = (uint32_t)rp.ksel;
+    const int per = ((a.V + kSmallCl - 1) / kSmallCl + 3) & ~3;
+    const int c0 = min(a.V, crank * per), c1 = min(a.V, c0 + per);
+    const float* x = a.logits + (int64_t)row * a.ld;
+    const int n4 = (c1 - c0) >> 2;
+    const float4* x4 = reinterpret_cast<const float4*>(x + c0);
+    float4 v[kSmallNJ];
+#pragma unroll
+    for (int j = 0; j < kSmallNJ; ++j) {
+        const int i = j * kNC + ctid;
+        if (i < n4) v[j] = x4[i];
+    }
+    const int tail0 = c0 + 4 * n4;  // at most 3 columns after the last float4
+    const bool has_t = ctid < c1 - tail0;
+    const float xt = has_t ? x[tail0 + ctid] : 0.0f;
+    if (crank == 0 && ctid == 0) sm.x0_nan = (a.V > 0 && x[0] != x[0]) ? 1 : 0;
+    // This thread's largest key (short shortlists) or its four largest keys
+    // (descending; longer ones): its proposals.
+    uint64_t t0 = 0ull, t1 = 0ull, t2 = 0ull, t3 = 0ull;
+    const bool four = ksel > 64u;  // the same on every thread of the row
+    auto propose = [&](uint64_t k) {
+        if (!four) {
+            t0 = k > t0 ? k : t0;
+        } else if (k > t3) {
+            t3 = k;
+            if (t3 > t2) { const uint64_t u = t2; t2 = t3; t3 = u; }
+            if (t2 > t1) { const uint64_t u = t1; t1 = t2; t2 = u; }
+            if (t1 > t0) { const uint64_t u = t0; t0 = t1; t1 = u; }
+        }
+    };
+#pragma unroll
+    for (int j = 0; j < kSmallNJ; ++j) {
+        const int i = j * kNC + ctid;
+        if (i < n4) {
+            const int32_t id = a.id_offset + c0 + 4 * i;
+            propose(make_key(v[j].x, id));
+            propose(make_key(v[j].y, id + 1));
+            propose(make_key(v[j].z, id + 2));
+            propose(make_key(v[j].w, id + 3));
+        }
+    }
+    if (has_t) propose(make_key(xt, a.id_offset + tail0 + ctid));
+    if (ksel == 1u) {
+        // greedy: the slice's largest key is all it publishes
+        const uint64_t wm = warp_max_u64(t0);
+        if (lane == 0) st.red64[ctid >> 5] = wm;
+        csync();
+        if (ctid == 0) {
+            uint64_t m = 0ull;
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) m = st.red64[w] > m ? st.red64[w] : m;
+            sm.pub[0] = m;
+            sm.pub_n = 1u;
+            sm.pub_tau = m;
+        }
+    } else {
+        // T: the ksel-th largest proposal (each is a different key of the slice, and
+        // every thread holds at least four elements): ksel keys of the slice reach it.
+        // Short shortlists rank the threads' maxima directly (each thread against all
+        // 256); longer ones sort all four proposals of every thread.
+        uint64_t T;
+        if (ksel <= 64u) {
+            st.cand[ctid] = t0;
+            csync();
+            uint32_t rank = 0;
+            for (int i = 0; i < kNC; ++i) rank += st.cand[i] > t0 ? 1u : 0u;
+            csync();
+            st.cand[rank] = t0;
+            csync();
+            T = st.cand[ksel - 1];
+        } else {
+            st.cand[4 * ctid] = t0;
+            st.cand[4 * ctid + 1] = t1;
+            st.cand[4 * ctid + 2] = t2;
+            st.cand[4 * ctid + 3] = t3;
+            csync();
+            sort_desc(st, 4 * kNC, ctid);
+            T = st.cand[ksel - 1];
+        }
+        uint32_t c = 0u;
+    #pragma unroll
+        for (int j = 0; j < kSmallNJ; ++j) {
+            const int i = j * kNC + ctid;
+            if (i < n4) {
+                const int32_t id = a.id_offset + c0 + 4 * i;
+                c += (uint32_t)(make_key(v[j].x, id) >= T) + (uint32_t)(make_key(v[j].y, id + 1) >= T) +
+                     (uint32_t)(make_key(v[j].z, id + 2) >= T) + (uint32_t)(make_key(v[j].w, id + 3) >= T);
+            }
+        }
+        if (has_t) c += (uint32_t)(make_key(xt, a.id_offset + tail0 + ctid) >= T);
+        uint32_t total;
+        const uint32_t incl = block_incl_scan(c, st.scan, ctid, total);
+        if (total + kCandMargin <= (uint32_t)kCandCap) {  // the same on every thread
+            // published as they are: CTA 0 filters them against every CTA's threshold
+            uint32_t at = incl - c;
+    #pragma unroll
+            for (int j = 0; j < kSmallNJ; ++j) {
+                const int i = j * kNC + ctid;
+                if (i < n4) {
+                    const int32_t id = a.id_offset + c0 + 4 * i;
+                    const uint64_t ks[4] = {make_key(v[j].x, id), make_key(v[j].y, id + 1),
+                                            make_key(v[j].z, id + 2), make_key(v[j].w, id + 3)};
+    #pragma unroll
+                    for (int r = 0; r < 4; ++r)
+                        if (ks[r] >= T) sm.pub[at++] = ks[r];
+                }
+            }
+            if (has_t) {
+                const uint64_t k = make_key(xt, a.id_offset + tail0 + ctid);
+                if (k >= T) sm.pub[at] = k;
+            }
+            if (ctid == 0) {
+                sm.pub_n = total;
+                sm.pub_tau = T;
+            }
+        } else {
+            // More keys reach T than the buffer holds (heavy ties across threads'
+            // maxima): append in rounds, compacting to the top ksel when full.
+            if (ctid == 0) st.count = 0u;
+            csync();
+            uint64_t tau = T - 1ull;  // keys > tau are the keys >= T
+            bool full = false;
+            for (int j = 0; j <= kSmallNJ; ++j) {  // rounds kSmallNJ - 1 and the tail
+                const int i = j * kNC + ctid;
+                uint64_t ks[4] = {0ull, 0ull, 0ull, 0ull};
+                if (j < kSmallNJ && i < n4) {
+                    const float4 w = x4[i];  // read again (from L2): no register indexing
+                    const int32_t id = a.id_offset + c0 + 4 * i;
+                    ks[0] = make_key(w.x, id);
+                    ks[1] = make_key(w.y, id + 1);
+                    ks[2] = make_key(w.z, id + 2);
+                    ks[3] = make_key(w.w, id + 3);
+                } else if (j == kSmallNJ && has_t) {
+                    ks[0] = make_key(xt, a.id_offset + tail0 + ctid);
+                }
+    #pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    if (full) tau = compact_select(st, st.count, ksel, ctid);
+                    warp_append(st, ks[r] > tau, ks[r], lane);
+                    full = csync_or(st.count + kNC + kCandMargin > (uint32_t)kCandCap);
+                }
+            }
+            uint32_t n = st.count;
+            uint64_t tau_c = tau + 1ull;
+            if (n > ksel) {
+                tau_c = compact_select(st, n, ksel, ctid);
+                n = st.count;
+            }
+            for (uint32_t i = ctid; i < n; i += kNC) sm.pub[i] = st.cand[i];
+            if (ctid == 0) {
+                sm.pub_n = n;
+                sm.pub_tau = tau_c;
+            }
+        }
+    }
+    cluster.sync();  // every CTA's keys are published
+    uint32_t kk = 0u;
+    if (crank == 0) {
+        // Every CTA has ksel keys at or above its own threshold, so the row's
+        // shortlist is at or above the largest one: only those keys are gathered.
+        // Counts, thresholds and offsets of all CTAs first (one remote read each).
+        if (ctid < 32) {
+            uint32_t nr = 0u;
+            uint64_t t = 0ull;
+            if (ctid < kSmallCl) {
+                const SmallSmem* rs = cluster.map_shared_rank(&sm, ctid);
+                nr = rs->pub_n;
+                t = rs->pub_tau;
+            }
+            const uint64_t tmax = warp_max_u64(t);
+            uint32_t inc = nr;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t u = __shfl_up_sync(kFull, inc, o);
+                if (lane >= o) inc += u;
+            }
+            if (ctid < kSmallCl) sm.g_off[ctid] = inc - nr;  // first key of CTA ctid
+            if (ctid == 31) sm.g_all = inc;                  // all published keys
+            if (ctid == 0) {
+                st.thr = tmax;
+                st.count = 0u;
+            }
+        }
+        csync();
+        uint64_t tau = st.thr - 1ull;  // keys > tau: at or above the largest threshold
+        const uint32_t all = sm.g_all;
+        // Every published key is read in parallel, four loads in flight a thread,
+        // in rounds of 4 x kNC keys; before a round that might not fit, the
+        // candidates are cut to the top ksel (which raises tau).  The loop bound
+        // is the same on every thread (warp_append needs all lanes).
+        bool full = false;
+        for (uint32_t b = 0; b < all; b += 4 * kNC) {
+            if (full) tau = compact_select(st, st.count, ksel, ctid);
+            const uint32_t i0 = b + (uint32_t)ctid;
+            uint64_t kv[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t i = i0 + j * kNC;
+                kv[j] = 0ull;
+                if (i < all) {
+                    int lo = 0, hi = kSmallCl - 1;  // the last CTA starting at or before i
+                    while (lo < hi) {
+                        const int mid = (lo + hi + 1) >> 1;
+                        if (sm.g_off[mid] <= i) lo = mid;
+                        else hi = mid - 1;
+                    }
+                    kv[j] = cluster.map_shared_rank(&sm, lo)->pub[i - sm.g_off[lo]];
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) warp_append(st, kv[j] > tau, kv[j], lane);
+            full = csync_or(st.count + 4 * kNC + kCandMargin > (uint32_t)kCandCap);
+        }
+        uint32_t m = st.count;
+        if (m > (uint32_t)kNC && m > ksel) {  // up to kNC keys are sorted whole
+            compact_select(st, m, ksel, ctid);
+            m = st.count;
+        }
+        sort_desc(st, m, ctid);
+        kk = m < ksel ? m : ksel;
+    }
+    cluster.sync();  // CTA 0 has read every CTA's keys
+    if (crank == 0)
+        finalize_row(st, st.cand, reinterpret_cast<double*>(st.cand + kProbOffset), kk, rp,
+                     sm.x0_nan != 0, false, -INFINITY, 0.0f, row, a.rng, a.out_ids, a.info,
+                     a.cand_ids, a.cand_probs, a.cand_ld, ctid);
+}
+
 }  // namespace zs
+

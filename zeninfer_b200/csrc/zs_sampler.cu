@@ -341,6 +341,8 @@ struct zs_context {
     bool timing = false;
     int32_t lm_route = ZS_LMHEAD_ROUTE_AUTO;  // zs_set_lmhead_route
     int32_t spec_mode = ZS_SPECULATION_ON;    // zs_set_speculation
+    int small_clusters = 0;                   // zs_small_kernel clusters resident at once (0: none)
+    int32_t small_max_rows = 8;               // zs_set_small_batch
     std::vector<TimedLaunch> timed;      // recorded since the last zs_get_timing
     std::vector<cudaEvent_t> spare;      // events free for reuse
     int64_t launches = 0;                // kernel launches since the last zs_get_timing
@@ -640,10 +642,41 @@ zs_status launch_large(zs_context* h, zs::Args a, int grid, bool want_lse, cudaS
     return ZS_OK;
 }
 
+// One launch for a small batch: a cluster of zs::kSmallCl CTAs per row
+// (zs_small_kernel), when every row fits that kernel's limits.
+bool small_path_ok(const zs_context* h, const zs::Args& a, const Plan& pl, bool want_lse) {
+    return !want_lse && a.mode == 0 && a.B >= 1 && a.B <= h->small_max_rows &&
+           a.B <= h->small_clusters && !pl.any_large && !pl.any_penal &&
+           pl.max_ksel <= (int)zs::kGroupMaxK && a.V >= zs::kSmallMinCols &&
+           a.V <= zs::kSmallMaxCols && ((uintptr_t)a.logits & 15u) == 0 && (a.ld & 3) == 0;
+}
+
+zs_status launch_small(zs_context* h, const zs::Args& a, cudaStream_t st) {
+    LaunchScope scope(h, 0, st);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = zs::kSmallCl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg;
+    std::memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(a.B * zs::kSmallCl);
+    cfg.blockDim = dim3(zs::kNC);
+    cfg.dynamicSmemBytes = sizeof(zs::SmallSmem);
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, zs::zs_small_kernel, a);
+    if (e != cudaSuccess) return cuda_fail(e, "small-batch launch");
+    ZS_CUDA(cudaGetLastError());
+    return ZS_OK;
+}
+
 zs_status launch_select(zs_context* h, const zs::Args& base, const Plan& pl, bool want_lse,
                         cudaStream_t st) {
     zs::Args a = base;
     a.status = h->status;
+    if (small_path_ok(h, a, pl, want_lse)) return launch_small(h, a, st);
     zs_status s = grow((void**)&h->part, &h->part_bytes, (size_t)std::max<int64_t>(pl.bytes, 16));
     if (s != ZS_OK) return s;
     if (pl.launch_cta) {
@@ -807,6 +840,30 @@ zs_status zs_create(int device, zs_handle* out) {
     zs_status sw = setup_wselect<zs::WCfgS>(&h->wsel_smem[0], &h->wsel_warps[0], h->num_sms);
     if (sw == ZS_OK) sw = setup_wselect<zs::WCfgL>(&h->wsel_smem[1], &h->wsel_warps[1], h->num_sms);
     if (sw != ZS_OK) return cleanup(sw);
+    // The one-launch small-batch path needs clusters of zs::kSmallCl CTAs (a
+    // non-portable size); where they cannot be resident the path stays off.
+    h->small_clusters = 0;
+    if (cudaFuncSetAttribute(zs::zs_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)sizeof(zs::SmallSmem)) == cudaSuccess &&
+        cudaFuncSetAttribute(zs::zs_small_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed,
+                             1) == cudaSuccess) {
+        cudaLaunchAttribute cattr[1];
+        cattr[0].id = cudaLaunchAttributeClusterDimension;
+        cattr[0].val.clusterDim.x = zs::kSmallCl;
+        cattr[0].val.clusterDim.y = 1;
+        cattr[0].val.clusterDim.z = 1;
+        cudaLaunchConfig_t ccfg;
+        std::memset(&ccfg, 0, sizeof(ccfg));
+        ccfg.gridDim = dim3(zs::kSmallCl);
+        ccfg.blockDim = dim3(zs::kNC);
+        ccfg.dynamicSmemBytes = sizeof(zs::SmallSmem);
+        ccfg.attrs = cattr;
+        ccfg.numAttrs = 1;
+        int nc = 0;
+        if (cudaOccupancyMaxActiveClusters(&nc, zs::zs_small_kernel, &ccfg) == cudaSuccess)
+            h->small_clusters = nc;
+    }
+    (void)cudaGetLastError();  // a refused cluster size only turns the path off
     int per_sm = 0;
     if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, zs::zs_select_kernel<false>, zs::kThreads, h->select_smem)) != cudaSuccess)
         return cleanup(cuda_fail(e, "occupancy query"));
@@ -857,6 +914,13 @@ zs_status zs_set_collective_timeout(zs_handle h, int32_t timeout_ms) {
 zs_status zs_set_timing(zs_handle h, int32_t enable) {
     if (!h) return fail(ZS_ERR_INVALID_ARGUMENT, "null handle");
     h->timing = enable != 0;
+    return ZS_OK;
+}
+
+zs_status zs_set_small_batch(zs_handle h, int32_t max_rows) {
+    if (!h) return fail(ZS_ERR_INVALID_ARGUMENT, "null handle");
+    if (max_rows < 0) return fail(ZS_ERR_INVALID_ARGUMENT, "max_rows < 0");
+    h->small_max_rows = max_rows;
     return ZS_OK;
 }
 

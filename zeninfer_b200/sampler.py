@@ -429,6 +429,10 @@ class Sampler:
         _native.check(self._lib.zs_set_speculation(self._h, self._SPEC_MODES[mode]),
                       "zs_set_speculation")
 
+    def set_small_batch(self, max_rows: int) -> None:
+        """zs_set_small_batch: batches up to max_rows rows in one cluster launch (0: off)."""
+        _native.check(self._lib.zs_set_small_batch(self._h, int(max_rows)), "zs_set_small_batch")
+
     def set_collective_timeout(self, timeout_ms: int) -> None:
         """zs_sample_sharded's bound on its collectives (0: asynchronous, no bound)."""
         _native.check(self._lib.zs_set_collective_timeout(self._h, int(timeout_ms)),
