@@ -3430,37 +3430,37 @@ __global__ void __launch_bounds__(kNC, 1) zs_small_kernel(const Args a) {
             sort_desc(st, 4 * kNC, ctid);
             T = st.cand[ksel - 1];
         }
+        auto passes = [&](float x, int32_t id) { return make_key(x, id) >= T; };
         uint32_t c = 0u;
-    #pragma unroll
+#pragma unroll
         for (int j = 0; j < kSmallNJ; ++j) {
             const int i = j * kNC + ctid;
             if (i < n4) {
                 const int32_t id = a.id_offset + c0 + 4 * i;
-                c += (uint32_t)(make_key(v[j].x, id) >= T) + (uint32_t)(make_key(v[j].y, id + 1) >= T) +
-                     (uint32_t)(make_key(v[j].z, id + 2) >= T) + (uint32_t)(make_key(v[j].w, id + 3) >= T);
+                c += (uint32_t)passes(v[j].x, id) + (uint32_t)passes(v[j].y, id + 1) +
+                     (uint32_t)passes(v[j].z, id + 2) + (uint32_t)passes(v[j].w, id + 3);
             }
         }
-        if (has_t) c += (uint32_t)(make_key(xt, a.id_offset + tail0 + ctid) >= T);
+        if (has_t) c += (uint32_t)passes(xt, a.id_offset + tail0 + ctid);
         uint32_t total;
         const uint32_t incl = block_incl_scan(c, st.scan, ctid, total);
         if (total + kCandMargin <= (uint32_t)kCandCap) {  // the same on every thread
             // published as they are: CTA 0 filters them against every CTA's threshold
             uint32_t at = incl - c;
-    #pragma unroll
-            for (int j = 0; j < kSmallNJ; ++j) {
-                const int i = j * kNC + ctid;
-                if (i < n4) {
-                    const int32_t id = a.id_offset + c0 + 4 * i;
-                    const uint64_t ks[4] = {make_key(v[j].x, id), make_key(v[j].y, id + 1),
-                                            make_key(v[j].z, id + 2), make_key(v[j].w, id + 3)};
-    #pragma unroll
-                    for (int r = 0; r < 4; ++r)
-                        if (ks[r] >= T) sm.pub[at++] = ks[r];
+            if (c) {
+#pragma unroll
+                for (int j = 0; j < kSmallNJ; ++j) {
+                    const int i = j * kNC + ctid;
+                    if (i < n4) {
+                        const int32_t id = a.id_offset + c0 + 4 * i;
+                        if (passes(v[j].x, id)) sm.pub[at++] = make_key(v[j].x, id);
+                        if (passes(v[j].y, id + 1)) sm.pub[at++] = make_key(v[j].y, id + 1);
+                        if (passes(v[j].z, id + 2)) sm.pub[at++] = make_key(v[j].z, id + 2);
+                        if (passes(v[j].w, id + 3)) sm.pub[at++] = make_key(v[j].w, id + 3);
+                    }
                 }
-            }
-            if (has_t) {
-                const uint64_t k = make_key(xt, a.id_offset + tail0 + ctid);
-                if (k >= T) sm.pub[at] = k;
+                if (has_t && passes(xt, a.id_offset + tail0 + ctid))
+                    sm.pub[at] = make_key(xt, a.id_offset + tail0 + ctid);
             }
             if (ctid == 0) {
                 sm.pub_n = total;
@@ -3486,7 +3486,7 @@ __global__ void __launch_bounds__(kNC, 1) zs_small_kernel(const Args a) {
                 } else if (j == kSmallNJ && has_t) {
                     ks[0] = make_key(xt, a.id_offset + tail0 + ctid);
                 }
-    #pragma unroll
+#pragma unroll
                 for (int r = 0; r < 4; ++r) {
                     if (full) tau = compact_select(st, st.count, ksel, ctid);
                     warp_append(st, ks[r] > tau, ks[r], lane);

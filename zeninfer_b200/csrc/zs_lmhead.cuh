@@ -5,8 +5,8 @@
 //   logits = xn . W^T   (W = output.weight [V][E])  zs_lmhead_kernel
 //
 // zs_lmhead_kernel is a persistent tcgen05 GEMM: D[128 rows][128 vocab] tiles
-// accumulate in tensor memory (two accumulators, so the epilogue of one tile
-// overlaps the MMAs of the next), operands arrive by TMA (2-D tiles, 128-byte
+// accumulate in tensor memory (four accumulators, all 512 columns, so the MMAs
+// run up to three tiles ahead of the epilogue, whose time per tile varies), operands arrive by TMA (2-D tiles, 128-byte
 // swizzle, no multicast) through a shared-memory ring of 3 to 5 stages (deeper
 // when the batch leaves candidate buffers unused).  Work units are
 // (row tile, vocabulary slice); a CTA walks its units' tiles in column order.
@@ -47,7 +47,8 @@ constexpr int kLmCap = 120;     // candidate keys buffered per row
 constexpr int kLmKeffMax = kLmCap - 32;  // a compaction leaves room for a whole chunk
 constexpr int kLmRowStride = kLmCap + 1; // odd, so rows spread over the banks
 constexpr int kLmThreads = 192; // warp 0 copies, warp 1 MMAs, warps 2-5 epilogue
-constexpr int kLmTmemCols = 2 * kLmN;
+constexpr int kLmAccs = 4;  // accumulators in tensor memory (all 512 columns)
+constexpr int kLmTmemCols = kLmAccs * kLmN;
 constexpr uint32_t kLmTileABytes = kLmM * kLmBK * 2;
 constexpr uint32_t kLmTileBBytes = kLmN * kLmBK * 2;
 constexpr int64_t kLmPartStride = kPartialHeaderBytes + 8 * kLmKeffMax;
@@ -63,8 +64,8 @@ struct LmSmem {  // placed at a 1024-byte boundary: the swizzled tiles need it
     uint8_t ring[kLmRingBytes];  // tiles (1024-byte aligned), then per row: keys, unordered
     uint64_t full[kLmStagesMax];
     uint64_t empty[kLmStagesMax];
-    uint64_t acc_full[2];
-    uint64_t acc_empty[2];
+    uint64_t acc_full[kLmAccs];
+    uint64_t acc_empty[kLmAccs];
     uint64_t drain;
     uint32_t tmem_base;
     int abort;
@@ -423,7 +424,7 @@ __global__ void __launch_bounds__(kLmThreads, 1)
             mbar_init(&sm.full[s], 1);
             mbar_init(&sm.empty[s], 1);
         }
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < kLmAccs; ++i) {
             mbar_init(&sm.acc_full[i], 1);
             mbar_init(&sm.acc_empty[i], 4 * 32);
         }
@@ -530,7 +531,7 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                     }
                     if (!ok) break;
                     tc_commit(&sm.acc_full[acc]);
-                    if (++acc == 2) {
+                    if (++acc == kLmAccs) {
                         acc = 0;
                         acc_phase ^= 1u;
                     }
@@ -625,7 +626,7 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                 if (gtau) lm_adopt(g_seen, tau_ord, tau_f, open);
                 tc_fence_before();
                 mbar_arrive(&sm.acc_empty[acc]);
-                if (++acc == 2) {
+                if (++acc == kLmAccs) {
                     acc = 0;
                     acc_phase ^= 1u;
                 }
