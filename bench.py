@@ -516,7 +516,7 @@ def parity_counts(s, dev, x, p, states, seeds, stream):
         return {"error": str(e)}
 
 
-def config_bench(s, dev, stream, peak, row0=0, with_parity=True):
+def config_bench(s, dev, stream, peak, row0=0, with_parity=True, only=None):
     """BASELINE's five workloads at their own batch sizes (workloads 1 and 4 also
     greedy): device time per call, the select / merge split, GB/s against the HBM
     peak, and the parity counts of one checked call.  Small inputs rotate over
@@ -526,6 +526,8 @@ def config_bench(s, dev, stream, peak, row0=0, with_parity=True):
     from zeninfer_b200 import workloads as W
     out = {}
     for cfg, wl in W.WORKLOADS.items():
+        if only is not None and cfg not in only:
+            continue
         B = wl.batch
         xh = W.generate(cfg, B, row0=row0)
         copies = max(1, -(-2 * L2_BYTES // (B * ROW_BYTES))) if B * ROW_BYTES < 2 * L2_BYTES else 1
@@ -760,6 +762,8 @@ def main():
                     help="skip the per-workload timings and parity counts")
     ap.add_argument("--no-parity", action="store_true",
                     help="per-workload timings without the parity counts")
+    ap.add_argument("--configs", default="1,2,3,4,5",
+                    help="workloads of the per-workload section (comma list, default all)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     rows = max(1, args.rows)
@@ -870,10 +874,13 @@ def main():
     # with the select / merge split and the parity counts of one checked call each.
     by_config = None
     if rank == 0 and world == 1 and not args.no_configs:
-        by_config = config_bench(s, dev, stream, peak, with_parity=not args.no_parity)
+        only = {int(c) for c in args.configs.split(",") if c.strip()}
+        by_config = config_bench(s, dev, stream, peak, with_parity=not args.no_parity, only=only)
     by_batch = {}
     if by_config:
         for b, cfgw in ((1, "1"), (256, "2")):
+            if cfgw not in by_config:
+                continue
             e = by_config[cfgw]["sampled"]
             by_batch[str(b)] = {k2: e[k2] for k2 in ("rows_per_s", "us_per_call", "logits_gbs",
                                                       "hbm_frac", "params")}
