@@ -1849,7 +1849,7 @@ __global__ void __launch_bounds__(kThreads, 2) zs_select_kernel(const Args a) {
 
 // Merge of gathered partial blocks (vocab shard): one CTA per row at a time.
 template <bool LSE>
-__global__ void __launch_bounds__(kNC) zs_merge_kernel(const MergeArgs a) {
+__global__ void __launch_bounds__(kNC, 3) zs_merge_kernel(const MergeArgs a) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     CandState& st = *reinterpret_cast<CandState*>(smem_raw);
     const int ctid = threadIdx.x;
