@@ -250,8 +250,8 @@ zs_status zs_set_speculation(zs_handle h, int32_t mode);
 
 /* Batches of at most max_rows rows (default 8; 0 turns it off) run as ONE launch:
  * a cluster of 16 CTAs per row holds the row in registers, and the row's shortlist
- * is merged through distributed shared memory, for rows without a repeat penalty,
- * shortlists up to 256, no log Z, 16-byte aligned rows (logits and ld * 4) of 16,384
+ * is merged through distributed shared memory, for penalty windows (repeat_last_n)
+ * up to 256, shortlists up to 256, no log Z, 16-byte aligned rows (logits and ld * 4) of 16,384
  * to 196,608 columns, where the GPU can keep that many 16-CTA clusters resident.
  * Other batches take the select and merge launches.  Results are identical either
  * way.  No counterpart in the reference. */

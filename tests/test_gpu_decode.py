@@ -105,6 +105,20 @@ def test_decode_loop_matches_generate_loop(sampler):
             assert (dev["tokens"][r, t + 1:] == -1).all()
 
 
+@pytest.mark.parametrize("B", [1, 4, 8])
+def test_decode_loop_small_batches(sampler, B):
+    """Decode-sized batches (the one-launch cluster path, penalised rows included)
+    against the generate loop's restatement."""
+    T, hist_ld = 12, 8
+    steps, planted = _case(B, T, seed_row0=900)
+    params = _params(B)
+    seeds = np.arange(B, dtype=np.uint64) + np.uint64(5)
+    dev = _run_device(sampler, steps, params, seeds, hist_ld)
+    st = np.array([rng_seed(int(s)) for s in seeds], dtype=np.uint64)
+    o = oracle.oracle_generate(steps, params, st, EOS)
+    _check(dev, o, st, hist_ld)
+
+
 def test_decode_loop_shared_params_no_history(sampler):
     B, T = 48, 6
     steps, _ = _case(B, T, seed_row0=5000)

@@ -3,7 +3,9 @@ merged through distributed shared memory) against the select + merge launches on
 the same rows, and against the restatement: ids, Rng states, shortlists and
 probabilities bit for bit, for batches of 1 to 8 rows, greedy and sampled rows,
 per-row parameters, ties, a NaN at index 0, row lengths that leave a ragged tail,
-and the shapes the path declines (penalty, unaligned rows, log Z)."""
+repeat penalties (repeated ids, ids at slice edges and in the tail, out-of-range
+ids, windows up to the kernel's 256), and the shapes the path declines (longer
+windows, unaligned rows, log Z)."""
 
 import numpy as np
 import pytest
@@ -100,15 +102,69 @@ def test_small_batch_special_values(sampler):
     compare(got["small"], run_oracle(x[1:], p, _states(rows - 1), cand_ld=40))
 
 
+def _penalty_history(x, rows, hist_ld, seed):
+    """Windows that hit the rows' top ids (so the penalty changes the shortlist),
+    repeat ids (the penalty compounds), and reach the edges of the 16 slices, the
+    scalar tail, id 0 and ids outside the vocabulary."""
+    rng = np.random.default_rng(seed)
+    n = x.shape[1]
+    per = ((n + 15) // 16 + 3) & ~3
+    hist = rng.integers(0, n, size=(rows, hist_ld)).astype(np.int32)
+    for r in range(rows):
+        top = np.argsort(-x[r], kind="stable")[:24]
+        k = min(hist_ld, 48)
+        hist[r, -k:] = rng.choice(np.concatenate([top, top[:6]]), size=k)
+        edges = [0, n - 1, per - 1, per, 5 * per - 1, 5 * per, -3, n + 7]
+        hist[r, -len(edges) - 1:-1] = np.asarray(edges, dtype=np.int64).astype(np.int32)
+    return hist
+
+
+@pytest.mark.parametrize("rows,win,n", [(1, 64, V), (4, 64, V), (8, 256, V), (3, 64, 20001)])
+def test_small_batch_penalty(sampler, rows, win, n):
+    """Penalised rows run in the small-batch kernel: the same ids, states,
+    shortlists and probabilities as the launches and the restatement."""
+    xf = W.generate(2, rows, row0=41)[:, :n].copy()
+    xf[0, 0] = -np.inf if rows > 1 else xf[0, 0]  # id 0 penalised from -inf
+    hist = _penalty_history(xf, rows, win + 8, 7 + rows)
+    hl = np.full(rows, win + 8, dtype=np.int32)
+    if rows > 1:
+        hl[-1] = win // 2  # a history shorter than repeat_last_n
+    for p in (SamplingParams(temp=0.7, top_k=40, top_p=0.9, repeat_penalty=1.3,
+                             repeat_last_n=win),
+              SamplingParams(temp=0.0, repeat_penalty=2.0, repeat_last_n=win),
+              SamplingParams(temp=1.0, top_p=0.95, repeat_penalty=0.8, repeat_last_n=win)):
+        k = p.top_k if p.top_k > 0 else 256
+        cl = k if p.temp > 0 else 0
+        got = _both(sampler, xf, p, cl, history=hist, history_len=hl)
+        _same(got["small"], got["launches"])
+        compare(got["small"], run_oracle(xf, p, _states(rows), history=hist, history_len=hl,
+                                         cand_ld=cl))
+
+
+def test_small_batch_penalty_nan_at_zero(sampler):
+    """logits[0] NaN stays NaN under the penalty: greedy returns 0 either way."""
+    rows = 2
+    x = W.generate(1, rows, row0=5)
+    x[:, 0] = np.nan
+    hist = np.zeros((rows, 16), dtype=np.int32)  # id 0, sixteen times
+    hl = np.full(rows, 16, dtype=np.int32)
+    p = SamplingParams(temp=0.0, repeat_penalty=1.5, repeat_last_n=16)
+    got = _both(sampler, x, p, 0, history=hist, history_len=hl)
+    _same(got["small"], got["launches"])
+    assert (got["small"]["ids"] == 0).all()
+
+
 def test_small_batch_declined_shapes(sampler):
-    """Penalised rows, log Z and unaligned rows take the launches; same results."""
+    """Windows longer than 256, log Z and unaligned rows take the launches; same
+    results."""
     x = W.generate(2, 4, row0=11)
     rng = np.random.default_rng(1)
-    hist = rng.integers(0, V, size=(4, 64)).astype(np.int32)
-    hl = np.full(4, 64, dtype=np.int32)
-    p = SamplingParams(temp=0.7, top_k=40, top_p=0.9, repeat_penalty=1.2, repeat_last_n=64)
+    hist = rng.integers(0, V, size=(4, 300)).astype(np.int32)
+    hl = np.full(4, 300, dtype=np.int32)
+    p = SamplingParams(temp=0.7, top_k=40, top_p=0.9, repeat_penalty=1.2, repeat_last_n=257)
     got = _both(sampler, x, p, 40, history=hist, history_len=hl)
     _same(got["small"], got["launches"])
+    compare(got["small"], run_oracle(x, p, _states(4), history=hist, history_len=hl, cand_ld=40))
     got = _both(sampler, x, SamplingParams(temp=0.7, top_k=40), 40, want_log_z=True)
     _same(got["small"], got["launches"])
     import torch

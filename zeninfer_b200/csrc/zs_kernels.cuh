@@ -3322,13 +3322,20 @@ __global__ void __launch_bounds__(kNC) zs_large_kernel(const Args a) {
 // barrier (which keeps the other CTAs' shared memory alive until CTA 0 has read
 // it) runs the f64 tail of sample_token (finalize_row).  No spin-waits: the
 // cluster barriers are hardware barriers every CTA reaches exactly twice.
-// Serves rows without a repeat penalty, shortlists up to kGroupMaxK, no log Z,
-// 16-byte aligned rows of at most kSmallMaxCols columns (the host checks).
+// A repeat penalty (window up to kSmallWinMax) is applied to the values in
+// registers before any key is made: each CTA stages the window in shared memory,
+// one thread per window entry computes the compounded value of each distinct id
+// in its slice from the raw logit and marks the register slot that holds it, and
+// the owning thread swaps the value in.  Serves shortlists up to kGroupMaxK, no
+// log Z, 16-byte aligned rows of at most kSmallMaxCols columns (the host checks).
 // ---------------------------------------------------------------------------
 constexpr int kSmallCl = 16;  // CTAs per row (a non-portable cluster size)
 constexpr int kSmallNJ = 12;  // float4s per thread
 constexpr int kSmallMaxCols = kSmallCl * kNC * 4 * kSmallNJ;  // 196,608
 constexpr int kSmallMinCols = kSmallCl * kNC * 4;             // every thread holds a float4
+constexpr int kSmallWinMax = kNC;                             // one thread per window entry
+constexpr int kSmallTailBit = 4 * kSmallNJ;                   // pen_mask bit of the tail column
+static_assert(kSmallTailBit < 64, "a thread's register slots fit one 64-bit mask");
 
 struct SmallSmem {
     CandState st;             // this CTA's candidates; on CTA 0 also the row's merge
@@ -3338,6 +3345,12 @@ struct SmallSmem {
     int32_t x0_nan;
     uint32_t g_off[kSmallCl];  // CTA 0: first key of each CTA in the concatenated list
     uint32_t g_all;            // CTA 0: keys published in all
+    // repeat penalty: the window, the penalised ids of this slice (-1 elsewhere)
+    // with their values, and per thread the register slots that hold one
+    int32_t win[kSmallWinMax];
+    int32_t pen_id[kSmallWinMax];
+    float pen_v[kSmallWinMax];
+    uint64_t pen_mask[kNC];
 };
 
 __global__ void __launch_bounds__(kNC, 1) zs_small_kernel(const Args a) {
@@ -3349,8 +3362,8 @@ __global__ void __launch_bounds__(kNC, 1) zs_small_kernel(const Args a) {
     const int crank = (int)cluster.block_rank();
     const int row = (int)blockIdx.x / kSmallCl;
     const int ctid = (int)threadIdx.x, lane = ctid & 31;
-    const RowPlan rp = plan_row(load_params(a.row_params, a.shared, row), a.V_total, nullptr,
-                                nullptr, 0, row);
+    const RowPlan rp = plan_row(load_params(a.row_params, a.shared, row), a.V_total, a.hist,
+                                a.hist_len, a.hist_ld, row);
     const uint32_t ksel = (uint32_t)rp.ksel;
     const int per = ((a.V + kSmallCl - 1) / kSmallCl + 3) & ~3;
     const int c0 = min(a.V, crank * per), c1 = min(a.V, c0 + per);
@@ -3365,8 +3378,78 @@ __global__ void __launch_bounds__(kNC, 1) zs_small_kernel(const Args a) {
     }
     const int tail0 = c0 + 4 * n4;  // at most 3 columns after the last float4
     const bool has_t = ctid < c1 - tail0;
-    const float xt = has_t ? x[tail0 + ctid] : 0.0f;
-    if (crank == 0 && ctid == 0) sm.x0_nan = (a.V > 0 && x[0] != x[0]) ? 1 : 0;
+    float xt = has_t ? x[tail0 + ctid] : 0.0f;
+    // Repetition penalty (src/sample.cpp:40-50) on this slice's values.  Bit
+    // 4 j + c of a thread's mask: component c of its float4 v[j]; kSmallTailBit:
+    // its tail column.  rp.penal is the same on every thread of the cluster.
+    uint64_t pmask = 0ull;
+    auto pen_value = [&](int32_t id, float raw) {
+        for (int q = 0; q < rp.win; ++q)
+            if (sm.pen_id[q] == id) return sm.pen_v[q];
+        return raw;
+    };
+    if (rp.penal) {
+        const int32_t* window = a.hist + (int64_t)row * a.hist_ld + (rp.hist_len - rp.win);
+        sm.pen_mask[ctid] = 0ull;
+        if (ctid < rp.win) sm.win[ctid] = window[ctid];
+        csync();
+        if (ctid < rp.win) {
+            const int32_t gid = sm.win[ctid];
+            const int32_t lo = a.id_offset + c0, hi = a.id_offset + c1;
+            int32_t pid = -1;
+            float pv = 0.0f;
+            if (gid >= 0 && gid < a.V_total && gid >= lo && gid < hi) {
+                bool first = true;
+                for (int q = 0; q < ctid; ++q)
+                    if (sm.win[q] == gid) {
+                        first = false;
+                        break;
+                    }
+                if (first) {
+                    // each entry of the window applies the penalty once more
+                    int mult = 1;
+                    for (int q = ctid + 1; q < rp.win; ++q) mult += sm.win[q] == gid ? 1 : 0;
+                    const float pen = rp.p.repeat_penalty;
+                    float val = x[gid - a.id_offset];
+                    for (int c = 0; c < mult; ++c) val = (val > 0.0f) ? val / pen : val * pen;
+                    pid = gid;
+                    pv = val;
+                    const int l = gid - lo;  // column within the slice
+                    int t, bit;
+                    if (l < 4 * n4) {
+                        const int i = l >> 2;
+                        t = i % kNC;
+                        bit = 4 * (i / kNC) + (l & 3);
+                    } else {
+                        t = l - 4 * n4;
+                        bit = kSmallTailBit;
+                    }
+                    atomicOr(reinterpret_cast<unsigned long long*>(&sm.pen_mask[t]),
+                             1ull << bit);
+                }
+            }
+            sm.pen_id[ctid] = pid;
+            sm.pen_v[ctid] = pv;
+        }
+        csync();
+        pmask = sm.pen_mask[ctid];
+        if (pmask) {
+#pragma unroll
+            for (int j = 0; j < kSmallNJ; ++j) {
+                if ((pmask >> (4 * j)) & 15ull) {
+                    const int32_t id = a.id_offset + c0 + 4 * (j * kNC + ctid);
+                    if ((pmask >> (4 * j)) & 1ull) v[j].x = pen_value(id, v[j].x);
+                    if ((pmask >> (4 * j + 1)) & 1ull) v[j].y = pen_value(id + 1, v[j].y);
+                    if ((pmask >> (4 * j + 2)) & 1ull) v[j].z = pen_value(id + 2, v[j].z);
+                    if ((pmask >> (4 * j + 3)) & 1ull) v[j].w = pen_value(id + 3, v[j].w);
+                }
+            }
+            if ((pmask >> kSmallTailBit) & 1ull) xt = pen_value(a.id_offset + tail0 + ctid, xt);
+        }
+    }
+    // the NaN test of logits[0] sees its penalised value (column 0 is v[0].x of
+    // CTA 0's thread 0: every thread holds at least one float4)
+    if (crank == 0 && ctid == 0) sm.x0_nan = (a.V > 0 && v[0].x != v[0].x) ? 1 : 0;
     // This thread's largest key (short shortlists) or its four largest keys
     // (descending; longer ones): its proposals.
     uint64_t t0 = 0ull, t1 = 0ull, t2 = 0ull, t3 = 0ull;
@@ -3477,8 +3560,14 @@ __global__ void __launch_bounds__(kNC, 1) zs_small_kernel(const Args a) {
                 const int i = j * kNC + ctid;
                 uint64_t ks[4] = {0ull, 0ull, 0ull, 0ull};
                 if (j < kSmallNJ && i < n4) {
-                    const float4 w = x4[i];  // read again (from L2): no register indexing
+                    float4 w = x4[i];  // read again (from L2): no register indexing
                     const int32_t id = a.id_offset + c0 + 4 * i;
+                    if ((pmask >> (4 * j)) & 15ull) {  // penalised again, as above
+                        if ((pmask >> (4 * j)) & 1ull) w.x = pen_value(id, w.x);
+                        if ((pmask >> (4 * j + 1)) & 1ull) w.y = pen_value(id + 1, w.y);
+                        if ((pmask >> (4 * j + 2)) & 1ull) w.z = pen_value(id + 2, w.z);
+                        if ((pmask >> (4 * j + 3)) & 1ull) w.w = pen_value(id + 3, w.w);
+                    }
                     ks[0] = make_key(w.x, id);
                     ks[1] = make_key(w.y, id + 1);
                     ks[2] = make_key(w.z, id + 2);

@@ -74,6 +74,7 @@ struct Plan {
     int max_ksel = 1;
     bool any_large = false;
     bool any_penal = false;
+    int max_win = 0;  // longest penalty window a row of this call may have
     // zs_select_kernel rows: [B][S] blocks at offset 0
     bool cta_area = false;    // the layout holds them
     bool launch_cta = false;  // some row of this call needs the kernel
@@ -167,7 +168,10 @@ Plan make_plan(int B, int V_cols, int V_total, const zs_params* params, int per_
         const int ks = ksel_of(p, V_total);
         const int wb = win_bound_of(p);
         pl.max_ksel = std::max(pl.max_ksel, ks);
-        if (have_history && wb > 0) pl.any_penal = true;
+        if (have_history && wb > 0) {
+            pl.any_penal = true;
+            pl.max_win = std::max(pl.max_win, wb);
+        }
         // The device puts a row in the first class whose limits ksel + its
         // actual window (empty without a history) and the window fit: the short
         // warp configuration, the long one, the CTA path; the rest on the large
@@ -646,7 +650,7 @@ zs_status launch_large(zs_context* h, zs::Args a, int grid, bool want_lse, cudaS
 // (zs_small_kernel), when every row fits that kernel's limits.
 bool small_path_ok(const zs_context* h, const zs::Args& a, const Plan& pl, bool want_lse) {
     return !want_lse && a.mode == 0 && a.B >= 1 && a.B <= h->small_max_rows &&
-           a.B <= h->small_clusters && !pl.any_large && !pl.any_penal &&
+           a.B <= h->small_clusters && !pl.any_large && pl.max_win <= zs::kSmallWinMax &&
            pl.max_ksel <= (int)zs::kGroupMaxK && a.V >= zs::kSmallMinCols &&
            a.V <= zs::kSmallMaxCols && ((uintptr_t)a.logits & 15u) == 0 && (a.ld & 3) == 0;
 }
