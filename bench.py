@@ -98,18 +98,26 @@ class ClockSampler:
         self.thread = None
         self.stop_flag = False
         self.sm, self.mx, self.reasons = [], [], set()
+        self.err = None
 
-    def _nvml_loop(self, nv, h):
-        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+    def _nvml_sample(self, nv, h, mx):
+        self.sm.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+        self.mx.append(float(mx))
+        try:
+            bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+        except Exception as e:  # clocks are still recorded; say why reasons are not
+            self.err = f"clock event reasons: {e}"
+            return
+        for bit, name in self.REASONS.items():
+            if bits & bit:
+                self.reasons.add(name)
+
+    def _nvml_loop(self, nv, h, mx):
         while not self.stop_flag:
             try:
-                self.sm.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
-                self.mx.append(float(mx))
-                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
-                for bit, name in self.REASONS.items():
-                    if bits & bit:
-                        self.reasons.add(name)
-            except Exception:
+                self._nvml_sample(nv, h, mx)
+            except Exception as e:
+                self.err = f"nvml: {e}"
                 break
             time.sleep(0.002)
 
@@ -126,11 +134,16 @@ class ClockSampler:
                     h = None
             if h is None:
                 h = nv.nvmlDeviceGetHandleByIndex(self.gpu)
-            self.thread = threading.Thread(target=self._nvml_loop, args=(nv, h), daemon=True)
+            mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            self._nvml_sample(nv, h, mx)  # one sample before the timed region starts
+            self.nv, self.h, self.mx_clock = nv, h, mx
+            self.thread = threading.Thread(target=self._nvml_loop, args=(nv, h, mx), daemon=True)
             self.thread.start()
             return
-        except Exception:
+        except Exception as e:
+            self.err = f"nvml unavailable: {e}"
             self.thread = None
+            self.sm, self.mx, self.reasons = [], [], set()
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
@@ -144,10 +157,23 @@ class ClockSampler:
     def stop(self):
         out = {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
         if self.thread is not None:
+            try:  # one sample as the timed region ends, whatever the thread managed
+                self._nvml_sample(self.nv, self.h, self.mx_clock)
+            except Exception as e:
+                self.err = f"nvml: {e}"
             self.stop_flag = True
             self.thread.join(timeout=5)
             src = "nvml, every 2 ms"
         elif self.proc is not None:
+            # nvidia-smi needs a moment to start: wait (up to 3 s) for its first line
+            t_end = time.monotonic() + 3.0
+            while time.monotonic() < t_end:
+                try:
+                    if os.path.getsize(self.path) > 0:
+                        break
+                except OSError:
+                    break
+                time.sleep(0.05)
             time.sleep(0.25)
             self.proc.terminate()
             try:
@@ -173,11 +199,15 @@ class ClockSampler:
                 pass
             src = "nvidia-smi, every 100 ms"
         else:
+            if self.err:
+                out["note"] = self.err
             return out
         if self.sm:
             out = {"sm_mhz": statistics.median(self.sm), "sm_max_mhz": max(self.mx),
                    "sm_min_mhz": min(self.sm), "reasons": sorted(self.reasons),
                    "samples": len(self.sm), "source": src}
+        if self.err:
+            out["note"] = self.err
         return out
 
 

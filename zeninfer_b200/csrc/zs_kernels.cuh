@@ -2288,7 +2288,8 @@ __global__ void __launch_bounds__(kNC, 4) zs_warp_merge_kernel(const MergeArgs a
     WarpSlot& ws = sm.w[warp];
     const unsigned below = lanemask_lt();
     grid_dep_wait();  // the partial blocks come from the kernel before this one
-    for (int row = a.row0 + blockIdx.x * kConsumerWarps + warp; row < a.row1;
+    // row r goes to CTA r mod grid: spread over the SMs before doubling up in a CTA
+    for (int row = a.row0 + warp * gridDim.x + blockIdx.x; row < a.row1;
          row += gridDim.x * kConsumerWarps) {
         const RowPlan rp = plan_row(load_params(a.row_params, a.shared, row), a.V_total, a.hist,
                                     a.hist_len, a.hist_ld, row);
