@@ -1978,18 +1978,14 @@ __device__ __forceinline__ uint64_t warp_topk_keep(uint64_t* keys, uint32_t n, u
 // ---------------------------------------------------------------------------
 constexpr int kWarpCap = 512;               // candidate keys per warp (4 KB: every CTA resident)
 constexpr uint32_t kWarpMergeMaxK = 256;
-// Long shortlists (up to 1024) get 16 KB per warp (128 KB a CTA, one CTA per SM):
-// eight rows per SM at once instead of the CTA merge's three, and a batch of 512
-// rows in one wave instead of two.
-constexpr int kBigWarpCap = 2048;
-constexpr uint32_t kBigWarpMergeMaxK = 1024;
 
-template <int CAP>
-struct WarpMergeSmemT {
-    uint64_t cand[kConsumerWarps][CAP];
+struct WarpSlot {
+    uint64_t cand[kWarpCap];
 };
-using WarpMergeSmem = WarpMergeSmemT<kWarpCap>;
-using BigWarpMergeSmem = WarpMergeSmemT<kBigWarpCap>;
+
+struct WarpMergeSmem {
+    WarpSlot w[kConsumerWarps];
+};
 
 // Keeps the keys >= T of keys[0..n) at the front (in order); returns how many.
 __device__ uint32_t warp_keep(uint64_t* keys, uint32_t n, uint64_t T, int lane) {
@@ -2058,18 +2054,13 @@ __device__ __forceinline__ void warp_sort_desc_slots(uint64_t* keys, uint32_t n,
     __syncwarp();
 }
 
-// Sorts keys[0..n) descending, n <= MAXN (256 or 1024), with the smallest network
-// that holds n.
-template <int MAXN>
-__device__ __forceinline__ void warp_sort_desc(uint64_t* keys, uint32_t n, int lane) {
-    static_assert(MAXN == 256 || MAXN == 1024, "network sizes");
+// Sorts keys[0..n) descending, n <= 256, with the smallest network that holds n.
+__device__ __forceinline__ void warp_sort256_desc(uint64_t* keys, uint32_t n, int lane) {
     if (n <= 1u) return;
     if (n <= 32u) warp_sort_desc_slots<32>(keys, n, lane);
     else if (n <= 64u) warp_sort_desc_slots<64>(keys, n, lane);
     else if (n <= 128u) warp_sort_desc_slots<128>(keys, n, lane);
-    else if (MAXN == 256 || n <= 256u) warp_sort_desc_slots<256>(keys, n, lane);
-    else if (n <= 512u) warp_sort_desc_slots<(MAXN > 256 ? 512 : 256)>(keys, n, lane);
-    else warp_sort_desc_slots<MAXN>(keys, n, lane);
+    else warp_sort_desc_slots<256>(keys, n, lane);
 }
 
 // f64 tail of sample_token (src/sample.cpp:52-101) over the sorted shortlist
@@ -2177,13 +2168,12 @@ __device__ void warp_finalize(const uint64_t* cand, double* prob, uint32_t kk, c
 // One warp merges one row: reads the headers of up to 32 blocks at once (one
 // lane each), gathers their keys 256 at a time into registers (so one memory
 // latency covers them), keeps the candidates to the top-ksel whenever cand
-// (CAP keys) fills, sorts, and runs the f64 tail and draw.  Shortlists up to
-// MAXK = CAP / 2; the f64 probabilities use cand[CAP - MAXK .. CAP).
+// (CAP keys) fills, sorts, and runs the f64 tail and draw.  The f64
+// probabilities use cand[CAP - 256 .. CAP).
 template <int CAP, bool LSE>
 __device__ void warp_merge_row(uint64_t* cand, const MergeArgs& a, int row, const RowPlan& rp,
                                unsigned below, int lane) {
-    constexpr uint32_t MAXK = (uint32_t)CAP / 2u;
-    static_assert(MAXK == kWarpMergeMaxK || MAXK == kBigWarpMergeMaxK, "merge sizes");
+    static_assert(CAP >= 2 * (int)kWarpMergeMaxK, "probabilities alias the top of cand");
     constexpr int J = 8;  // keys per lane per gather round
     const uint32_t ksel = (uint32_t)rp.ksel;
     const float lc = (rp.greedy ? 1.0f : 1.0f / rp.p.temp) * 1.4426950408889634f;
@@ -2269,11 +2259,11 @@ __device__ void warp_merge_row(uint64_t* cand, const MergeArgs& a, int row, cons
     }
     // Up to 256 keys are sorted whole (the shortlist is their prefix), which is
     // cheaper than selecting the top-ksel first; more are cut to ksel first.
-    if (count > kWarpMergeMaxK && count > ksel) {
+    if (count > kWarpMergeMaxK) {
         warp_topk_keep<CAP / 32>(cand, count, ksel, lane);
         count = ksel;
     }
-    warp_sort_desc<(int)MAXK>(cand, count, lane);
+    warp_sort256_desc(cand, count, lane);
     const uint32_t kk = count < ksel ? count : ksel;
     spec_ord = __reduce_max_sync(kFull, spec_ord);
     if (spec_ord != 0u) {
@@ -2285,17 +2275,17 @@ __device__ void warp_merge_row(uint64_t* cand, const MergeArgs& a, int row, cons
             return;
         }
     }
-    warp_finalize(cand, reinterpret_cast<double*>(cand + (CAP - (int)MAXK)), kk, rp,
+    warp_finalize(cand, reinterpret_cast<double*>(cand + (CAP - (int)kWarpMergeMaxK)), kk, rp,
                   nan0, LSE, M, Sx, row, a.rng, a.out_ids, a.info, a.cand_ids, a.cand_probs,
                   a.cand_ld, lane);
 }
 
-template <bool LSE, int CAP>
-__global__ void __launch_bounds__(kNC, CAP == kWarpCap ? 4 : 1) zs_warp_merge_kernel(const MergeArgs a) {
+template <bool LSE>
+__global__ void __launch_bounds__(kNC, 4) zs_warp_merge_kernel(const MergeArgs a) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
-    WarpMergeSmemT<CAP>& sm = *reinterpret_cast<WarpMergeSmemT<CAP>*>(smem_raw);
+    WarpMergeSmem& sm = *reinterpret_cast<WarpMergeSmem*>(smem_raw);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    uint64_t* cand = sm.cand[warp];
+    WarpSlot& ws = sm.w[warp];
     const unsigned below = lanemask_lt();
     grid_dep_wait();  // the partial blocks come from the kernel before this one
     // row r goes to CTA r mod grid: spread over the SMs before doubling up in a CTA
@@ -2304,7 +2294,7 @@ __global__ void __launch_bounds__(kNC, CAP == kWarpCap ? 4 : 1) zs_warp_merge_ke
         const RowPlan rp = plan_row(load_params(a.row_params, a.shared, row), a.V_total, a.hist,
                                     a.hist_len, a.hist_ld, row);
         if (rp.large) continue;  // drawn by zs_large_kernel
-        warp_merge_row<CAP, LSE>(cand, a, row, rp, below, lane);
+        warp_merge_row<kWarpCap, LSE>(ws.cand, a, row, rp, below, lane);
     }
 }
 

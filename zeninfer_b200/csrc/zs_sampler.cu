@@ -325,10 +325,6 @@ struct zs_context {
     size_t select_smem = 0;
     size_t merge_smem = 0;
     size_t warp_merge_smem = 0;
-    size_t big_warp_merge_smem = 0;
-    // shortlists of 257-1024: warp-per-row merge from this many rows (below it, the
-    // CTA merge's lower per-row latency wins)
-    int big_warp_merge_min_rows = 256;
     size_t wsel_smem[2] = {0, 0};  // per warp configuration (WCfgS, WCfgL)
     int wsel_warps[2] = {0, 0};    // warps of one full zs_wselect_kernel launch
     // scratch, grown on demand (never shrinks)
@@ -493,23 +489,15 @@ zs_status launch_merge(zs_context* h, const zs::MergeArgs& m, int max_ksel, bool
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaError_t e;
-    const bool small_k = (uint32_t)max_ksel <= zs::kWarpMergeMaxK;
-    const bool big_k = !small_k && (uint32_t)max_ksel <= zs::kBigWarpMergeMaxK;
-    if ((small_k && rows >= 2 * h->num_sms) || (big_k && rows >= h->big_warp_merge_min_rows)) {
+    if ((uint32_t)max_ksel <= zs::kWarpMergeMaxK && rows >= 2 * h->num_sms) {
         // at least one CTA per SM: rows are dealt to CTAs first, then to their warps
         const int rows_per_cta = zs::kConsumerWarps;
         const int by_rows = (rows + rows_per_cta - 1) / rows_per_cta;
         cfg.gridDim = dim3(std::max(1, std::min(std::max(by_rows, std::min(rows, h->num_sms)),
                                                 8 * h->num_sms)));
-        if (small_k) {
-            cfg.dynamicSmemBytes = h->warp_merge_smem;
-            e = want_lse ? cudaLaunchKernelEx(&cfg, zs::zs_warp_merge_kernel<true, zs::kWarpCap>, m)
-                         : cudaLaunchKernelEx(&cfg, zs::zs_warp_merge_kernel<false, zs::kWarpCap>, m);
-        } else {
-            cfg.dynamicSmemBytes = h->big_warp_merge_smem;
-            e = want_lse ? cudaLaunchKernelEx(&cfg, zs::zs_warp_merge_kernel<true, zs::kBigWarpCap>, m)
-                         : cudaLaunchKernelEx(&cfg, zs::zs_warp_merge_kernel<false, zs::kBigWarpCap>, m);
-        }
+        cfg.dynamicSmemBytes = h->warp_merge_smem;
+        e = want_lse ? cudaLaunchKernelEx(&cfg, zs::zs_warp_merge_kernel<true>, m)
+                     : cudaLaunchKernelEx(&cfg, zs::zs_warp_merge_kernel<false>, m);
     } else {
         cfg.gridDim = dim3(std::max(1, std::min(rows, 4 * h->num_sms)));
         cfg.dynamicSmemBytes = h->merge_smem;
@@ -845,7 +833,6 @@ zs_status zs_create(int device, zs_handle* out) {
     h->select_smem = sizeof(zs::FastSmem);
     h->merge_smem = sizeof(zs::CandState);
     h->warp_merge_smem = sizeof(zs::WarpMergeSmem);
-    h->big_warp_merge_smem = sizeof(zs::BigWarpMergeSmem);
     auto cleanup = [&](zs_status s) {
         delete h;
         return s;
@@ -857,10 +844,8 @@ zs_status zs_create(int device, zs_handle* out) {
         (e = cudaFuncSetAttribute(zs::zs_merge_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->merge_smem)) != cudaSuccess ||
         (e = cudaFuncSetAttribute(zs::zs_large_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->merge_smem)) != cudaSuccess ||
         (e = cudaFuncSetAttribute(zs::zs_large_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->merge_smem)) != cudaSuccess ||
-        (e = cudaFuncSetAttribute(zs::zs_warp_merge_kernel<true, zs::kWarpCap>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->warp_merge_smem)) != cudaSuccess ||
-        (e = cudaFuncSetAttribute(zs::zs_warp_merge_kernel<false, zs::kWarpCap>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->warp_merge_smem)) != cudaSuccess ||
-        (e = cudaFuncSetAttribute(zs::zs_warp_merge_kernel<true, zs::kBigWarpCap>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->big_warp_merge_smem)) != cudaSuccess ||
-        (e = cudaFuncSetAttribute(zs::zs_warp_merge_kernel<false, zs::kBigWarpCap>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->big_warp_merge_smem)) != cudaSuccess)
+        (e = cudaFuncSetAttribute(zs::zs_warp_merge_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->warp_merge_smem)) != cudaSuccess ||
+        (e = cudaFuncSetAttribute(zs::zs_warp_merge_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->warp_merge_smem)) != cudaSuccess)
         return cleanup(cuda_fail(e, "cudaFuncSetAttribute"));
     if ((size_t)prop.sharedMemPerBlockOptin >= zs::kLmSmemBytes &&
         (e = cudaFuncSetAttribute(zs::zs_lmhead_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1780,16 +1765,12 @@ zs_status noalloc_setup(int dev, NoAllocDevice** out) {
         d.ctx.select_smem = sizeof(zs::FastSmem);
         d.ctx.merge_smem = sizeof(zs::CandState);
         d.ctx.warp_merge_smem = sizeof(zs::WarpMergeSmem);
-        d.ctx.big_warp_merge_smem = sizeof(zs::BigWarpMergeSmem);
         ZS_CUDA(cudaFuncSetAttribute(zs::zs_select_kernel<false>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d.ctx.select_smem));
         ZS_CUDA(cudaFuncSetAttribute(zs::zs_merge_kernel<false>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d.ctx.merge_smem));
-        ZS_CUDA(cudaFuncSetAttribute(zs::zs_warp_merge_kernel<false, zs::kWarpCap>,
+        ZS_CUDA(cudaFuncSetAttribute(zs::zs_warp_merge_kernel<false>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d.ctx.warp_merge_smem));
-        ZS_CUDA(cudaFuncSetAttribute(zs::zs_warp_merge_kernel<false, zs::kBigWarpCap>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)d.ctx.big_warp_merge_smem));
         zs_status sw = setup_wselect<zs::WCfgS>(&d.ctx.wsel_smem[0], &d.ctx.wsel_warps[0],
                                                 d.ctx.num_sms);
         if (sw == ZS_OK)
