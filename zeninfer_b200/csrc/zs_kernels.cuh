@@ -895,17 +895,133 @@ __device__ uint64_t compact_select(CandState& st, uint32_t n, uint32_t kk, int c
     return compact_top(st, n, kk, slack, ctid);
 }
 
+// Sorts keys[0..n) descending, n <= SLOTS, in registers: a bitonic network over
+// SLOTS slots (SLOTS / 32 per lane, slot = lane * P + j; unused slots hold 0,
+// which sorts last).
+template <int SLOTS>
+__device__ __forceinline__ void warp_sort_desc_slots(uint64_t* keys, uint32_t n, int lane) {
+    constexpr int P = SLOTS / 32;
+    uint64_t k[P];
+#pragma unroll
+    for (int j = 0; j < P; ++j) {
+        const uint32_t i = (uint32_t)lane * P + j;
+        k[j] = i < n ? keys[i] : 0ull;
+    }
+#pragma unroll
+    for (int size = 2; size <= SLOTS; size <<= 1) {
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            if (stride >= P) {
+#pragma unroll
+                for (int j = 0; j < P; ++j) {
+                    const int i = lane * P + j;
+                    const uint64_t p = __shfl_xor_sync(kFull, k[j], stride / P);
+                    const bool desc = (i & size) == 0, lower = (i & stride) == 0;
+                    const uint64_t hi = k[j] > p ? k[j] : p, lo = k[j] > p ? p : k[j];
+                    k[j] = (lower == desc) ? hi : lo;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < P; ++j) {
+                    if ((j & stride) == 0) {
+                        const int i = lane * P + j;
+                        const bool desc = (i & size) == 0;
+                        const uint64_t a = k[j], b = k[j | stride];
+                        if (desc ? (a < b) : (a > b)) {
+                            k[j] = b;
+                            k[j | stride] = a;
+                        }
+                    }
+                }
+            }
+        }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < P; ++j) {
+        const uint32_t i = (uint32_t)lane * P + j;
+        if (i < n) keys[i] = k[j];
+    }
+    __syncwarp();
+}
+
 // Sorts cand[0..n) descending.  n <= kNC: every thread ranks one key against
-// all others (keys are unique); larger n: bitonic over the next power of two.
+// all others (keys are unique).  n <= kNC * 8: each warp sorts one of eight
+// chunks in registers (a bitonic network of up to 256 slots), then three levels
+// of pairwise merges (merge path) through cand[kSortScratch ..) join them.
+// Larger n: bitonic over the next power of two in shared memory.
+constexpr uint32_t kChunkSortMax = (uint32_t)kNC * 8u;  // 2048: chunks of <= 256
+constexpr int kSortScratch = 2048;                       // cand[2048 .. 2048 + n) is free
+static_assert(kSortScratch + (int)kChunkSortMax <= kCandCap, "sort scratch");
+
 __device__ void sort_desc(CandState& st, uint32_t n, int ctid) {
     if (n <= 1) return;
     if (n <= (uint32_t)kNC) {
         const uint64_t k = (uint32_t)ctid < n ? st.cand[ctid] : 0ull;
         uint32_t rank = 0;
-        if ((uint32_t)ctid < n)
-            for (uint32_t i = 0; i < n; ++i) rank += st.cand[i] > k ? 1u : 0u;
+        if ((uint32_t)ctid < n) {
+            uint32_t i = 0;
+            for (; i + 8u <= n; i += 8u) {  // eight broadcast loads in flight
+                uint64_t y[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) y[j] = st.cand[i + j];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) rank += y[j] > k ? 1u : 0u;
+            }
+            for (; i < n; ++i) rank += st.cand[i] > k ? 1u : 0u;
+        }
         csync();
         if ((uint32_t)ctid < n) st.cand[rank] = k;
+        csync();
+        return;
+    }
+    if (n <= kChunkSortMax) {
+        constexpr uint32_t NW = (uint32_t)kConsumerWarps;
+        const int lane = ctid & 31;
+        const uint32_t w = (uint32_t)ctid >> 5;
+        const uint32_t c = (n + NW - 1) / NW;  // 33..256; every chunk holds at least one key
+        const uint32_t b0 = min(n, w * c), nc = min(n, b0 + c) - b0;
+        if (c <= 64u) warp_sort_desc_slots<64>(st.cand + b0, nc, lane);
+        else if (c <= 128u) warp_sort_desc_slots<128>(st.cand + b0, nc, lane);
+        else warp_sort_desc_slots<256>(st.cand + b0, nc, lane);
+        csync();
+        // Three merge levels (8 runs -> 4 -> 2 -> 1), ping-ponging between cand and
+        // cand + kSortScratch.  At each level a pair's threads split its output into
+        // equal spans; a thread finds where its span starts in the two runs by a
+        // binary search on that diagonal (merge path) and merges the span.
+        uint64_t* src = st.cand;
+        uint64_t* dst = st.cand + kSortScratch;
+        for (uint32_t lvl = 0; lvl < 3u; ++lvl) {
+            const uint32_t run = c << lvl;                  // input run length
+            const uint32_t tpp = (uint32_t)kNC >> (2u - lvl);  // threads per pair: 64, 128, 256
+            const uint32_t pair = (uint32_t)ctid / tpp, t = (uint32_t)ctid % tpp;
+            const uint32_t a0 = min(n, 2u * pair * run), a1 = min(n, a0 + run);
+            const uint32_t b1 = min(n, a1 + run);
+            const uint32_t la = a1 - a0, lb = b1 - a1, tot = la + lb;
+            const uint32_t per = (tot + tpp - 1) / tpp;
+            const uint32_t d0 = min(tot, t * per), d1 = min(tot, d0 + per);
+            if (d0 < d1) {
+                const uint64_t* A = src + a0;
+                const uint64_t* B = src + a1;
+                // a = how many of the first d0 outputs come from A (A first on ties)
+                uint32_t lo = d0 > lb ? d0 - lb : 0u, hi = d0 < la ? d0 : la;
+                while (lo < hi) {
+                    const uint32_t mid = (lo + hi) >> 1;
+                    if (A[mid] >= B[d0 - 1u - mid]) lo = mid + 1u;
+                    else hi = mid;
+                }
+                uint32_t ia = lo, ib = d0 - lo;
+                for (uint32_t k = d0; k < d1; ++k) {
+                    const bool take_a = ib >= lb || (ia < la && A[ia] >= B[ib]);
+                    dst[a0 + k] = take_a ? A[ia++] : B[ib++];
+                }
+            }
+            csync();
+            uint64_t* tmp = src;
+            src = dst;
+            dst = tmp;
+        }
+        for (uint32_t i = ctid; i < n; i += kNC) st.cand[i] = src[i];  // src: the last output
         csync();
         return;
     }
@@ -1384,7 +1500,9 @@ __device__ uint32_t merge_partials(CandState& st, const MergeArgs& a, const Bloc
                 if (ctid == 0) st.count = n;
                 csync();
             }
-            if (n > ksel) {
+            // up to kNC keys are ranked whole (the shortlist is their prefix), which
+            // is cheaper than selecting the top-ksel first
+            if (n > ksel && n > (uint32_t)kNC) {
                 compact_select(st, n, ksel, ctid);
                 n = st.count;
             }
@@ -2002,56 +2120,6 @@ __device__ uint32_t warp_keep(uint64_t* keys, uint32_t n, uint64_t T, int lane) 
         __syncwarp();
     }
     return out;
-}
-
-// Sorts keys[0..n) descending, n <= SLOTS, in registers: a bitonic network over
-// SLOTS slots (SLOTS / 32 per lane, slot = lane * P + j; unused slots hold 0,
-// which sorts last).
-template <int SLOTS>
-__device__ __forceinline__ void warp_sort_desc_slots(uint64_t* keys, uint32_t n, int lane) {
-    constexpr int P = SLOTS / 32;
-    uint64_t k[P];
-#pragma unroll
-    for (int j = 0; j < P; ++j) {
-        const uint32_t i = (uint32_t)lane * P + j;
-        k[j] = i < n ? keys[i] : 0ull;
-    }
-#pragma unroll
-    for (int size = 2; size <= SLOTS; size <<= 1) {
-#pragma unroll
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-            if (stride >= P) {
-#pragma unroll
-                for (int j = 0; j < P; ++j) {
-                    const int i = lane * P + j;
-                    const uint64_t p = __shfl_xor_sync(kFull, k[j], stride / P);
-                    const bool desc = (i & size) == 0, lower = (i & stride) == 0;
-                    const uint64_t hi = k[j] > p ? k[j] : p, lo = k[j] > p ? p : k[j];
-                    k[j] = (lower == desc) ? hi : lo;
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < P; ++j) {
-                    if ((j & stride) == 0) {
-                        const int i = lane * P + j;
-                        const bool desc = (i & size) == 0;
-                        const uint64_t a = k[j], b = k[j | stride];
-                        if (desc ? (a < b) : (a > b)) {
-                            k[j] = b;
-                            k[j | stride] = a;
-                        }
-                    }
-                }
-            }
-        }
-    }
-    __syncwarp();
-#pragma unroll
-    for (int j = 0; j < P; ++j) {
-        const uint32_t i = (uint32_t)lane * P + j;
-        if (i < n) keys[i] = k[j];
-    }
-    __syncwarp();
 }
 
 // Sorts keys[0..n) descending, n <= 256, with the smallest network that holds n.
