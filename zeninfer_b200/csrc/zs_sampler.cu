@@ -21,11 +21,22 @@
 #include <vector>
 
 #include <cudaTypedefs.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include "zs_kernels.cuh"
 #include "zs_lmhead.cuh"
 #include "zs_sampler.h"
 #include "zs_stats.cuh"
+
+// Named NVTX ranges around the entry points that launch work, so a timeline
+// (Nsight Systems, or any NVTX client) shows each call with its kernels.  Without
+// a tool attached a push/pop is a check of one function pointer.
+struct NvtxRange {
+    explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+    NvtxRange(const NvtxRange&) = delete;
+    NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 static_assert(sizeof(zs_params) == sizeof(zs::Params), "zs_params layout");
 static_assert(sizeof(zs_row_info) == sizeof(zs::RowInfo), "zs_row_info layout");
@@ -984,6 +995,7 @@ zs_status zs_sample(zs_handle h, const float* logits, int64_t ld, int32_t batch,
                     const zs_params* params, int32_t params_per_row, const int32_t* history,
                     int64_t history_ld, const int32_t* history_len, uint64_t* rng_state,
                     int32_t* out_ids, const zs_extras* extras, void* stream) {
+    NvtxRange nvtx_range("zs_sample");
     zs_status s = validate_common(h, logits, ld, batch, n_vocab, params);
     if (s != ZS_OK) return s;
     if (batch == 0) return ZS_OK;
@@ -1037,6 +1049,7 @@ zs_status zs_decode_step(zs_handle h, const float* logits, int64_t ld, int32_t b
                          int32_t* history, int64_t history_ld, int32_t* history_len,
                          uint64_t* rng_state, int32_t* done, int32_t eos_id, int32_t* out_ids,
                          int32_t* tokens, int64_t tokens_ld, int64_t step, void* stream) {
+    NvtxRange nvtx_range("zs_decode_step");
     zs_status s = validate_common(h, logits, ld, batch, n_vocab, params);
     if (s != ZS_OK) return s;
     if (batch == 0) return ZS_OK;
@@ -1233,6 +1246,7 @@ zs_status zs_lmhead_logits(zs_handle h, const float* hidden, int64_t hidden_ld,
                            const float* norm_w, float eps, const void* weight, int32_t batch,
                            int32_t n_embd, int32_t n_vocab, float* out_logits, int64_t logits_ld,
                            void* stream) {
+    NvtxRange nvtx_range("zs_lmhead_logits");
     if (!h) return fail(ZS_ERR_INVALID_ARGUMENT, "null handle");
     if (batch < 0) return fail(ZS_ERR_INVALID_ARGUMENT, "batch < 0");
     if (batch == 0) return ZS_OK;
@@ -1264,6 +1278,7 @@ zs_status zs_lmhead_sample(zs_handle h, const float* hidden, int64_t hidden_ld,
                            int32_t params_per_row, const int32_t* history, int64_t history_ld,
                            const int32_t* history_len, uint64_t* rng_state, int32_t* out_ids,
                            float* out_logits, int64_t logits_ld, void* stream) {
+    NvtxRange nvtx_range("zs_lmhead_sample");
     if (!h) return fail(ZS_ERR_INVALID_ARGUMENT, "null handle");
     if (!params) return fail(ZS_ERR_INVALID_ARGUMENT, "params is null");
     if (batch < 0) return fail(ZS_ERR_INVALID_ARGUMENT, "batch < 0");
@@ -1364,6 +1379,7 @@ zs_status zs_lmhead_sample(zs_handle h, const float* hidden, int64_t hidden_ld,
 
 zs_status zs_argmax(zs_handle h, const float* logits, int64_t ld, int32_t batch, int32_t n_vocab,
                     int32_t* out_ids, void* stream) {
+    NvtxRange nvtx_range("zs_argmax");
     zs_params p;
     p.temp = 0.0f;
     p.top_k = 0;
@@ -1399,6 +1415,7 @@ zs_status zs_selftest_wait_timeout(zs_handle h, void* stream) {
 zs_status zs_logits_stats(zs_handle h, const float* logits, int64_t ld, int32_t batch,
                           int32_t n_vocab, int32_t topn, double* out_min, double* out_max,
                           double* out_z, int32_t* top_ids, double* top_p, void* stream) {
+    NvtxRange nvtx_range("zs_logits_stats");
     if (!h) return fail(ZS_ERR_INVALID_ARGUMENT, "null handle");
     if (batch < 0 || topn < 0) return fail(ZS_ERR_INVALID_ARGUMENT, "batch or topn < 0");
     if (batch == 0) return ZS_OK;
@@ -1476,6 +1493,7 @@ zs_status zs_shard_partials(zs_handle h, const float* logits_local, int64_t ld, 
                             const int32_t* history, int64_t history_ld,
                             const int32_t* history_len, void* partial_out, int32_t want_log_z,
                             void* stream) {
+    NvtxRange nvtx_range("zs_shard_partials");
     zs_status s = validate_common(h, logits_local, ld, batch, n_local, params);
     if (s != ZS_OK) return s;
     if (n_vocab_total <= 0 || n_ranks <= 0 || n_local < 0 || vocab_offset < 0 ||
@@ -1562,6 +1580,7 @@ zs_status zs_shard_merge_rows(zs_handle h, const void* gathered, int32_t n_ranks
                               const zs_params* params, int32_t params_per_row,
                               uint64_t* rng_state, int32_t* out_ids, const zs_extras* extras,
                               void* stream) {
+    NvtxRange nvtx_range("zs_shard_merge_rows");
     if (!h || !params || n_ranks <= 0 || batch < 0 || n_vocab_total <= 0 || row_begin < 0 ||
         row_count < 0 || (int64_t)row_begin + row_count > batch)
         return fail(ZS_ERR_INVALID_ARGUMENT, "bad merge arguments");
@@ -1614,6 +1633,7 @@ zs_status zs_sample_sharded(zs_handle h, const float* logits_local, int64_t ld, 
                             const int32_t* history, int64_t history_ld,
                             const int32_t* history_len, uint64_t* rng_state, int32_t* out_ids,
                             const zs_extras* extras, void* nccl_comm, void* stream) {
+    NvtxRange nvtx_range("zs_sample_sharded");
     if (!h || !nccl_comm) return fail(ZS_ERR_INVALID_ARGUMENT, "null handle or communicator");
     if (!load_nccl()) return fail(ZS_ERR_NCCL, "libnccl.so.2 not loadable (or too old)");
     const Clock::time_point t0 = Clock::now();
@@ -1811,6 +1831,7 @@ extern "C" zs_status zs_sample_noalloc(const float* logits, int64_t ld, int32_t 
                                        const int32_t* history, int64_t history_ld,
                                        const int32_t* history_len, uint64_t* rng_state,
                                        int32_t* out_ids, int32_t* device_status, void* stream) {
+    NvtxRange nvtx_range("zs_sample_noalloc");
     if (batch < 0) return fail(ZS_ERR_INVALID_ARGUMENT, "batch < 0");
     if (!params) return fail(ZS_ERR_INVALID_ARGUMENT, "params is null");
     if (batch == 0) return ZS_OK;
