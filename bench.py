@@ -500,6 +500,13 @@ def parity_counts(s, dev, x, p, states, seeds, stream):
         torch.cuda.synchronize()
         g_ids = res.ids.cpu().numpy()
         g_st = tensor_to_states(st)
+        # the timed call wants ids only, which takes the certified parallel tail:
+        # it must give the same ids and states as this checked call
+        st2 = states_to_tensor(states, dev)
+        t_ids = s.sample(xd, p, st2, stream=stream).ids
+        torch.cuda.synchronize()
+        t_ids = t_ids.cpu().numpy()
+        t_st = tensor_to_states(st2)
         o_st = np.array(states, dtype=np.uint64, copy=True)
         o_ids, o_info, o_cid, _, o_cp = oracle.oracle_sample(x, p, o_st, cand_ld=k)
         greedy = p.temp <= 0
@@ -508,7 +515,9 @@ def parity_counts(s, dev, x, p, states, seeds, stream):
                "boundary_rows": int(near.sum()),
                "boundary_rows_id_differs": int(((g_ids != o_ids) & near).sum()),
                "id_mismatch_vs_restatement": int(((g_ids != o_ids) & ~near).sum()),
-               "rng_state_mismatch_vs_restatement": int((g_st != o_st).sum())}
+               "rng_state_mismatch_vs_restatement": int((g_st != o_st).sum()),
+               "timed_call_id_mismatch": int((t_ids != g_ids).sum()),
+               "timed_call_rng_mismatch": int((t_st != g_st).sum())}
         if k > 0:
             gc = res.cand_ids.cpu().numpy()
             gp = res.cand_probs.cpu().numpy()

@@ -1242,6 +1242,112 @@ __device__ void finalize_blocked(CandState& st, const uint64_t* cand, double* pr
     csync();
 }
 
+// Certified parallel tail for calls that want only the drawn id (no row info, no
+// candidate lists).  sample_token's tail (src/sample.cpp:69-101) makes two
+// decisions from sequential f64 sums: where the nucleus ends (the first m with
+// acc_m >= top_p) and where the draw lands (the first i with r < acc'_i).  Here
+// the same sums are parallel prefix sums E_k of e = exp((x - max) / temp) in
+// another order, so they differ from the sequential ones, but by little: every
+// sum of at most 4096 terms in [0, 1] is off by at most (4 kk + 80) 2^-53 < 2e-12
+// relative to its exact value, in either order, divisions included.  So a
+// decision whose compared quantities lie further than kTailMargin (1e-10) apart
+// on the parallel sums is the sequential decision too; when one does not, the
+// caller runs the sequential loops instead (a draw within 1e-10 of a CDF
+// boundary: about one row in 10^9).  Nothing is written until the result is
+// certified; then the id and the advanced Rng state are stored.  Returns whether
+// it drew (the same on every thread).
+constexpr uint32_t kFastTailMin = 128;  // shorter shortlists: the sequential loops are short
+constexpr double kTailMargin = 1e-10;
+
+__device__ bool fast_tail(CandState& st, const uint64_t* cand, const double* e, uint32_t kk,
+                          const Params& p, int row, uint64_t* rng, int32_t* out_ids, int ctid) {
+    const int lane = ctid & 31, warp = ctid >> 5;
+    // contiguous segments, at most 16 terms a thread (kk <= kBlockedTail)
+    const uint32_t per = (kk + kNC - 1) / kNC;
+    const uint32_t s0 = min(kk, (uint32_t)ctid * per), s1 = min(kk, s0 + per);
+    double seg = 0.0;
+    for (uint32_t i = s0; i < s1; ++i) seg += e[i];
+    // block exclusive scan of the segment sums
+    double inc = seg;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const double t = __shfl_up_sync(kFull, inc, o);
+        if (lane >= o) inc += t;
+    }
+    if (lane == 31) st.red64[warp] = (uint64_t)__double_as_longlong(inc);
+    if (ctid == 0) {
+        uint64_t sr = rng[row];
+        st.lse_delta = rng_uniform(sr);  // the draw (not stored unless certified)
+        st.thr2 = sr;
+        st.sel_above = 0u;               // 1: a decision is too close to call
+        st.m = (int)kk;
+        st.sel_cnt = 0xffffffffu;        // the drawn position
+    }
+    csync();
+    double pre = inc - seg, T = 0.0;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) {
+        const double t = __longlong_as_double((long long)st.red64[w]);
+        if (w < warp) pre += t;
+        T += t;
+    }
+    const double r = st.lse_delta;
+    if (!(T > 0.0) || !(T < INFINITY)) {  // NaN or inf terms: the same on every thread
+        csync();
+        return false;
+    }
+    // nucleus end: the first m (1..kk) with E_m / T >= top_p
+    const bool nucleus = p.top_p < 1.0f;
+    const double top_p = (double)p.top_p;
+    if (nucleus) {
+        if (!(top_p > 0.0)) {  // the loop takes no term: left to the sequential code
+            csync();
+            return false;
+        }
+        double E = pre;
+        for (uint32_t i = s0; i < s1; ++i) {
+            const double Ep = E;
+            E += e[i];
+            const double a = Ep / T, b = E / T;
+            if (a < top_p && b >= top_p) {  // the crossing (E is nondecreasing)
+                if (!(a < top_p - kTailMargin && b >= top_p + kTailMargin)) st.sel_above = 1u;
+                st.m = (int)(i + 1);
+                st.d_rescale = E;
+            }
+        }
+        if (ctid == (int)((kk - 1) / per)) {  // the thread holding the last term
+            if (E / T < top_p && !(E / T < top_p - kTailMargin)) st.sel_above = 1u;
+        }
+    }
+    csync();
+    const uint32_t m = (uint32_t)st.m;
+    const double Em = (nucleus && m < kk) ? st.d_rescale : T;
+    // the draw: the first i < m with r < E_{i+1} / E_m
+    {
+        double E = pre;
+        for (uint32_t i = s0; i < s1 && i < m; ++i) {
+            const double Ep = E;
+            E += e[i];
+            const double a = Ep / Em, b = E / Em;
+            if (a <= r && r < b) {
+                if (!(a < r - kTailMargin && b > r + kTailMargin)) st.sel_above = 1u;
+                st.sel_cnt = i;
+            }
+        }
+    }
+    csync();
+    if (st.sel_above != 0u || st.sel_cnt == 0xffffffffu) {  // read by every thread alike
+        csync();
+        return false;
+    }
+    if (ctid == 0) {
+        rng[row] = st.thr2;
+        if (out_ids) out_ids[row] = key_id(cand[st.sel_cnt]);
+    }
+    csync();
+    return true;
+}
+
 // f64 tail of sample_token (src/sample.cpp:52-101) over the sorted shortlist
 // cand[0..kk): softmax in shortlist order, nucleus prefix, inverse-CDF draw.
 // `prob` holds kk doubles of scratch.  Generic pointers: shared or global.
@@ -1307,6 +1413,9 @@ __device__ void finalize_row(CandState& st, const uint64_t* cand, double* prob, 
                          row, rng, out_ids, info, cand_ids, cand_probs, cand_ld, ctid);
         return;
     }
+    if (info == nullptr && !(cand_ld > 0 && (cand_ids != nullptr || cand_probs != nullptr)) &&
+        kk >= kFastTailMin && fast_tail(st, cand, prob, kk, p, row, rng, out_ids, ctid))
+        return;
     if (ctid == 0) {
         st.d_sum = seq_sum(prob, kk);
     }
@@ -2131,6 +2240,83 @@ __device__ __forceinline__ void warp_sort256_desc(uint64_t* keys, uint32_t n, in
     else warp_sort_desc_slots<256>(keys, n, lane);
 }
 
+// fast_tail for one warp (kk <= 256: at most 8 terms a lane): the same parallel
+// prefix sums and the same certification, with shuffles and votes in place of
+// shared memory.  Returns whether it drew (the same on every lane).
+__device__ bool warp_fast_tail(const uint64_t* cand, const double* e, uint32_t kk, const Params& p,
+                               int row, uint64_t* rng, int32_t* out_ids, int lane) {
+    const uint32_t per = (kk + 31u) / 32u;
+    const uint32_t s0 = min(kk, (uint32_t)lane * per), s1 = min(kk, s0 + per);
+    double seg = 0.0;
+    for (uint32_t i = s0; i < s1; ++i) seg += e[i];
+    double inc = seg;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const double t = __shfl_up_sync(kFull, inc, o);
+        if (lane >= o) inc += t;
+    }
+    const double T = __shfl_sync(kFull, inc, 31);
+    const double pre = inc - seg;
+    if (!(T > 0.0) || !(T < INFINITY)) return false;  // NaN or inf terms (uniform)
+    uint64_t sr = 0ull;
+    double r = 0.0;
+    if (lane == 0) {
+        sr = rng[row];
+        r = rng_uniform(sr);  // not stored unless certified
+    }
+    r = __shfl_sync(kFull, r, 0);
+    bool bad = false;
+    uint32_t m = kk;
+    double Em = T;
+    if (p.top_p < 1.0f) {
+        const double top_p = (double)p.top_p;
+        if (!(top_p > 0.0)) return false;  // the loop takes no term: sequential code
+        double E = pre;
+        int mloc = -1;
+        double eloc = 0.0;
+        for (uint32_t i = s0; i < s1; ++i) {
+            const double Ep = E;
+            E += e[i];
+            const double a = Ep / T, b = E / T;
+            if (a < top_p && b >= top_p) {
+                if (!(a < top_p - kTailMargin && b >= top_p + kTailMargin)) bad = true;
+                mloc = (int)(i + 1);
+                eloc = E;
+            }
+        }
+        if (s1 == kk && s0 < s1 && E / T < top_p && !(E / T < top_p - kTailMargin)) bad = true;
+        const unsigned hit = __ballot_sync(kFull, mloc >= 0);
+        if (hit) {
+            const int src = __ffs(hit) - 1;
+            m = (uint32_t)__shfl_sync(kFull, mloc, src);
+            const double em = __shfl_sync(kFull, eloc, src);
+            if (m < kk) Em = em;
+        }
+    }
+    int pos = -1;
+    {
+        double E = pre;
+        for (uint32_t i = s0; i < s1 && i < m; ++i) {
+            const double Ep = E;
+            E += e[i];
+            const double a = Ep / Em, b = E / Em;
+            if (a <= r && r < b) {
+                if (!(a < r - kTailMargin && b > r + kTailMargin)) bad = true;
+                pos = (int)i;
+            }
+        }
+    }
+    const unsigned found = __ballot_sync(kFull, pos >= 0);
+    if (__any_sync(kFull, bad) || found == 0u) return false;
+    pos = __shfl_sync(kFull, pos, __ffs(found) - 1);
+    if (lane == 0) {
+        rng[row] = sr;
+        if (out_ids) out_ids[row] = key_id(cand[pos]);
+    }
+    __syncwarp();
+    return true;
+}
+
 // f64 tail of sample_token (src/sample.cpp:52-101) over the sorted shortlist
 // cand[0..kk), by one warp: the same expressions and summation order as
 // finalize_row (sequential sums on lane 0).
@@ -2167,6 +2353,9 @@ __device__ void warp_finalize(const uint64_t* cand, double* prob, uint32_t kk, c
     for (uint32_t i = lane; i < kk; i += 32)
         prob[i] = exp(((double)key_value(cand[i]) - (double)max_l) * (double)inv_temp);
     __syncwarp();
+    if (info == nullptr && !(cand_ld > 0 && (cand_ids != nullptr || cand_probs != nullptr)) &&
+        kk >= kFastTailMin && warp_fast_tail(cand, prob, kk, p, row, rng, out_ids, lane))
+        return;
     double sum = 0.0;
     if (lane == 0) sum = seq_sum(prob, kk);
     sum = __shfl_sync(kFull, sum, 0);
