@@ -3567,48 +3567,51 @@ __global__ void __launch_bounds__(kNC) zs_large_kernel(const Args a) {
 
 // ---------------------------------------------------------------------------
 // zs_small_kernel: a small batch (decode-sized, a few rows) in ONE launch.
-// One thread block cluster of kSmallCl CTAs per row.  CTA r of a cluster holds
-// the r-th slice of the row's columns in registers (coalesced float4 loads, all
-// of a thread's loads in flight at once).  Each CTA keeps its slice's keys at or
-// above the ksel-th largest of its threads' maximum keys (kth_of_proposals: ksel
-// different keys of the slice reach it, so nothing below it can be in the row's
-// shortlist), cuts them to at most ksel + slack (compact_select) and publishes
-// them in its own shared memory with that threshold.  After a cluster barrier,
-// CTA 0 reads every CTA's keys through distributed shared memory, keeping those
-// at or above the largest published threshold (every CTA has ksel keys above
-// its own), selects and sorts the exact top-ksel, and after a second cluster
-// barrier (which keeps the other CTAs' shared memory alive until CTA 0 has read
-// it) runs the f64 tail of sample_token (finalize_row).  No spin-waits: the
-// cluster barriers are hardware barriers every CTA reaches exactly twice.
-// A repeat penalty (window up to kSmallWinMax) is applied to the values in
-// registers before any key is made: each CTA stages the window in shared memory,
-// one thread per window entry computes the compounded value of each distinct id
-// in its slice from the raw logit and marks the register slot that holds it, and
-// the owning thread swaps the value in.  Serves shortlists up to kGroupMaxK, no
-// log Z, 16-byte aligned rows of at most kSmallMaxCols columns (the host checks).
+// One thread block cluster of kSmallCl CTAs per row.  CTA r copies the r-th slice
+// of the row's columns into its shared memory with 1-D bulk copies (the at most
+// three columns after the last 16-byte boundary by plain loads), so every later
+// step is a short loop over shared memory: a one-row call is latency-bound, and
+// much of that latency was fetching the long unrolled code of a register-resident
+// slice.  A repeat penalty (window up to kSmallWinMax) is written over the
+// slice's values in place (src/sample.cpp:40-50: one thread per distinct window
+// id, compounding once per occurrence).  Each thread proposes its largest key (or
+// its four largest, for shortlists above 64), and warp 0 finds the ksel-th
+// largest proposal with a register radix walk: ksel different keys of the slice
+// reach it.  After a cluster barrier every CTA reads the 16 thresholds through
+// distributed shared memory and takes the largest, T: its CTA has ksel keys at
+// or above T, so the row's shortlist is at or above T.  Each CTA publishes its
+// keys at or above T (a float4 whose largest component is below T's value is
+// skipped without making keys); after a second barrier CTA 0 reads every CTA's
+// keys, selects and sorts the exact top-ksel, and after a third (which keeps the
+// other CTAs' shared memory alive until CTA 0 has read it) runs the f64 tail of
+// sample_token (finalize_row).  Greedy rows publish each slice's largest key and
+// need no threshold.  The cluster barriers are hardware barriers every CTA of the
+// cluster reaches alike; the bulk copies' wait is bounded (it reports
+// ZS_ERR_DEVICE_TIMEOUT and the CTA goes on with an empty slice, so the cluster
+// still meets at every barrier).  Serves shortlists up to kGroupMaxK, no log Z,
+// 16-byte aligned rows of kSmallMinCols to kSmallMaxCols columns (the host
+// checks).
 // ---------------------------------------------------------------------------
 constexpr int kSmallCl = 16;  // CTAs per row (a non-portable cluster size)
 constexpr int kSmallNJ = 12;  // float4s per thread
 constexpr int kSmallMaxCols = kSmallCl * kNC * 4 * kSmallNJ;  // 196,608
 constexpr int kSmallMinCols = kSmallCl * kNC * 4;             // every thread holds a float4
 constexpr int kSmallWinMax = kNC;                             // one thread per window entry
-constexpr int kSmallTailBit = 4 * kSmallNJ;                   // pen_mask bit of the tail column
-static_assert(kSmallTailBit < 64, "a thread's register slots fit one 64-bit mask");
+constexpr int kSmallChunk = 4096;                             // bytes per bulk copy
 
 struct SmallSmem {
     CandState st;             // this CTA's candidates; on CTA 0 also the row's merge
     uint64_t pub[kCandCap];   // this CTA's published keys
+    float4 vals[kSmallNJ * kNC];  // the slice (penalised in place)
+    float tail[4];            // its columns after the last 16-byte boundary
+    uint64_t bar;             // the bulk copies' completion
     uint64_t pub_tau;         // at least ksel of this slice's keys are >= pub_tau
     uint32_t pub_n;
     int32_t x0_nan;
+    int32_t lost;              // the bulk copies' wait ran out: the slice is not there
     uint32_t g_off[kSmallCl];  // CTA 0: first key of each CTA in the concatenated list
     uint32_t g_all;            // CTA 0: keys published in all
-    // repeat penalty: the window, the penalised ids of this slice (-1 elsewhere)
-    // with their values, and per thread the register slots that hold one
-    int32_t win[kSmallWinMax];
-    int32_t pen_id[kSmallWinMax];
-    float pen_v[kSmallWinMax];
-    uint64_t pen_mask[kNC];
+    int32_t win[kSmallWinMax];  // the penalty window
 };
 
 __global__ void __launch_bounds__(kNC, 1) zs_small_kernel(const Args a) {
@@ -3626,36 +3629,39 @@ __global__ void __launch_bounds__(kNC, 1) zs_small_kernel(const Args a) {
     const int per = ((a.V + kSmallCl - 1) / kSmallCl + 3) & ~3;
     const int c0 = min(a.V, crank * per), c1 = min(a.V, c0 + per);
     const float* x = a.logits + (int64_t)row * a.ld;
-    const int n4 = (c1 - c0) >> 2;
-    const float4* x4 = reinterpret_cast<const float4*>(x + c0);
-    float4 v[kSmallNJ];
-#pragma unroll
-    for (int j = 0; j < kSmallNJ; ++j) {
-        const int i = j * kNC + ctid;
-        if (i < n4) v[j] = x4[i];
-    }
+    int n4 = (c1 - c0) >> 2;
     const int tail0 = c0 + 4 * n4;  // at most 3 columns after the last float4
-    const bool has_t = ctid < c1 - tail0;
-    float xt = has_t ? x[tail0 + ctid] : 0.0f;
-    // Repetition penalty (src/sample.cpp:40-50) on this slice's values.  Bit
-    // 4 j + c of a thread's mask: component c of its float4 v[j]; kSmallTailBit:
-    // its tail column.  rp.penal is the same on every thread of the cluster.
-    uint64_t pmask = 0ull;
-    auto pen_value = [&](int32_t id, float raw) {
-        for (int q = 0; q < rp.win; ++q)
-            if (sm.pen_id[q] == id) return sm.pen_v[q];
-        return raw;
-    };
-    if (rp.penal) {
-        const int32_t* window = a.hist + (int64_t)row * a.hist_ld + (rp.hist_len - rp.win);
-        sm.pen_mask[ctid] = 0ull;
-        if (ctid < rp.win) sm.win[ctid] = window[ctid];
-        csync();
+    const int nt = c1 - tail0;
+    const uint32_t bytes = (uint32_t)n4 * 16u;
+    if (ctid == 0) {
+        mbar_init(&sm.bar, 1);
+        mbar_fence_init();
+        mbar_arrive_expect_tx(&sm.bar, bytes);
+        const uint64_t pol = l2_evict_first_policy();
+        for (uint32_t off = 0; off < bytes; off += kSmallChunk)
+            bulk_load(reinterpret_cast<uint8_t*>(sm.vals) + off,
+                      reinterpret_cast<const uint8_t*>(x + c0) + off,
+                      min((uint32_t)kSmallChunk, bytes - off), &sm.bar, pol);
+    }
+    if (ctid < nt) sm.tail[ctid] = x[tail0 + ctid];
+    if (rp.penal && ctid < rp.win)
+        sm.win[ctid] = a.hist[(int64_t)row * a.hist_ld + (rp.hist_len - rp.win) + ctid];
+    if (ctid == 0) {
+        sm.pub_n = 0u;
+        sm.lost = mbar_wait_bounded(&sm.bar, 0u) ? 0 : 1;
+        if (sm.lost) set_status(a.status, kStatusTimeout);
+    }
+    csync();
+    const bool lost = sm.lost != 0;
+    if (lost) n4 = 0;  // go on with an empty slice, so every barrier is still met
+    float* sv = reinterpret_cast<float*>(sm.vals);
+    // Repetition penalty (src/sample.cpp:40-50) on this slice's values, in place:
+    // the thread of a window id's first occurrence compounds the penalty once per
+    // occurrence on the raw logit.  rp.penal is the same on every thread of the row.
+    if (rp.penal && !lost) {
         if (ctid < rp.win) {
             const int32_t gid = sm.win[ctid];
             const int32_t lo = a.id_offset + c0, hi = a.id_offset + c1;
-            int32_t pid = -1;
-            float pv = 0.0f;
             if (gid >= 0 && gid < a.V_total && gid >= lo && gid < hi) {
                 bool first = true;
                 for (int q = 0; q < ctid; ++q)
@@ -3664,76 +3670,71 @@ __global__ void __launch_bounds__(kNC, 1) zs_small_kernel(const Args a) {
                         break;
                     }
                 if (first) {
-                    // each entry of the window applies the penalty once more
                     int mult = 1;
                     for (int q = ctid + 1; q < rp.win; ++q) mult += sm.win[q] == gid ? 1 : 0;
                     const float pen = rp.p.repeat_penalty;
                     float val = x[gid - a.id_offset];
                     for (int c = 0; c < mult; ++c) val = (val > 0.0f) ? val / pen : val * pen;
-                    pid = gid;
-                    pv = val;
                     const int l = gid - lo;  // column within the slice
-                    int t, bit;
-                    if (l < 4 * n4) {
-                        const int i = l >> 2;
-                        t = i % kNC;
-                        bit = 4 * (i / kNC) + (l & 3);
-                    } else {
-                        t = l - 4 * n4;
-                        bit = kSmallTailBit;
-                    }
-                    atomicOr(reinterpret_cast<unsigned long long*>(&sm.pen_mask[t]),
-                             1ull << bit);
+                    if (l < 4 * n4) sv[l] = val;
+                    else sm.tail[l - 4 * n4] = val;
                 }
             }
-            sm.pen_id[ctid] = pid;
-            sm.pen_v[ctid] = pv;
         }
         csync();
-        pmask = sm.pen_mask[ctid];
-        if (pmask) {
-#pragma unroll
-            for (int j = 0; j < kSmallNJ; ++j) {
-                if ((pmask >> (4 * j)) & 15ull) {
-                    const int32_t id = a.id_offset + c0 + 4 * (j * kNC + ctid);
-                    if ((pmask >> (4 * j)) & 1ull) v[j].x = pen_value(id, v[j].x);
-                    if ((pmask >> (4 * j + 1)) & 1ull) v[j].y = pen_value(id + 1, v[j].y);
-                    if ((pmask >> (4 * j + 2)) & 1ull) v[j].z = pen_value(id + 2, v[j].z);
-                    if ((pmask >> (4 * j + 3)) & 1ull) v[j].w = pen_value(id + 3, v[j].w);
-                }
-            }
-            if ((pmask >> kSmallTailBit) & 1ull) xt = pen_value(a.id_offset + tail0 + ctid, xt);
-        }
     }
-    // the NaN test of logits[0] sees its penalised value (column 0 is v[0].x of
-    // CTA 0's thread 0: every thread holds at least one float4)
-    if (crank == 0 && ctid == 0) sm.x0_nan = (a.V > 0 && v[0].x != v[0].x) ? 1 : 0;
+    // the NaN test of logits[0] sees its penalised value (column 0 of CTA 0)
+    if (crank == 0 && ctid == 0) sm.x0_nan = (a.V > 0 && !lost && sv[0] != sv[0]) ? 1 : 0;
+    const bool has_t = !lost && ctid < nt;
+    const float xt = has_t ? sm.tail[ctid] : 0.0f;
+    const int32_t tid_t = a.id_offset + tail0 + ctid;  // the tail column's id
     // This thread's largest key (short shortlists) or its four largest keys
     // (descending; longer ones): its proposals.
     uint64_t t0 = 0ull, t1 = 0ull, t2 = 0ull, t3 = 0ull;
     const bool four = ksel > 64u;  // the same on every thread of the row
-    auto propose = [&](uint64_t k) {
-        if (!four) {
+    if (!four) {
+        // the largest value first (fmaxf skips NaN), then the smallest id holding it
+        float M = has_t ? xt : __int_as_float(0x7fc00000);
+        for (int i = ctid; i < n4; i += kNC) {
+            const float4 w = sm.vals[i];
+            M = fmaxf(M, fmaxf(fmaxf(w.x, w.y), fmaxf(w.z, w.w)));
+        }
+        const bool all_nan = M != M;
+        for (int i = ctid; i < n4; i += kNC) {
+            const float4 w = sm.vals[i];
+            if (all_nan || w.x == M || w.y == M || w.z == M || w.w == M) {
+                const int32_t id = a.id_offset + c0 + 4 * i;
+                uint64_t k = make_key(w.x, id);
+                k = max(k, make_key(w.y, id + 1));
+                k = max(k, make_key(w.z, id + 2));
+                k = max(k, make_key(w.w, id + 3));
+                t0 = k > t0 ? k : t0;
+            }
+        }
+        if (has_t) {
+            const uint64_t k = make_key(xt, tid_t);
             t0 = k > t0 ? k : t0;
-        } else if (k > t3) {
-            t3 = k;
-            if (t3 > t2) { const uint64_t u = t2; t2 = t3; t3 = u; }
-            if (t2 > t1) { const uint64_t u = t1; t1 = t2; t2 = u; }
-            if (t1 > t0) { const uint64_t u = t0; t0 = t1; t1 = u; }
         }
-    };
-#pragma unroll
-    for (int j = 0; j < kSmallNJ; ++j) {
-        const int i = j * kNC + ctid;
-        if (i < n4) {
+    } else {
+        auto propose = [&](uint64_t k) {
+            if (k > t3) {
+                t3 = k;
+                if (t3 > t2) { const uint64_t u = t2; t2 = t3; t3 = u; }
+                if (t2 > t1) { const uint64_t u = t1; t1 = t2; t2 = u; }
+                if (t1 > t0) { const uint64_t u = t0; t0 = t1; t1 = u; }
+            }
+        };
+        for (int i = ctid; i < n4; i += kNC) {
+            const float4 w = sm.vals[i];
             const int32_t id = a.id_offset + c0 + 4 * i;
-            propose(make_key(v[j].x, id));
-            propose(make_key(v[j].y, id + 1));
-            propose(make_key(v[j].z, id + 2));
-            propose(make_key(v[j].w, id + 3));
+            propose(make_key(w.x, id));
+            propose(make_key(w.y, id + 1));
+            propose(make_key(w.z, id + 2));
+            propose(make_key(w.w, id + 3));
         }
+        if (has_t) propose(make_key(xt, tid_t));
     }
-    if (has_t) propose(make_key(xt, a.id_offset + tail0 + ctid));
+    uint64_t T = 0ull;  // sampled rows: every published key is at or above it
     if (ksel == 1u) {
         // greedy: the slice's largest key is all it publishes
         const uint64_t wm = warp_max_u64(t0);
@@ -3744,96 +3745,96 @@ __global__ void __launch_bounds__(kNC, 1) zs_small_kernel(const Args a) {
 #pragma unroll
             for (int w = 0; w < kConsumerWarps; ++w) m = st.red64[w] > m ? st.red64[w] : m;
             sm.pub[0] = m;
-            sm.pub_n = 1u;
-            sm.pub_tau = m;
+            sm.pub_n = m != 0ull ? 1u : 0u;
         }
     } else {
-        // T: the ksel-th largest proposal (each is a different key of the slice, and
-        // every thread holds at least four elements): ksel keys of the slice reach it.
-        // Short shortlists rank the threads' maxima directly (each thread against all
-        // 256); longer ones sort all four proposals of every thread.
-        uint64_t T;
-        if (ksel <= 64u) {
+        // This CTA's threshold: the ksel-th largest proposal (each is a different key
+        // of the slice, and every thread holds at least four elements, so ksel keys
+        // of the slice reach it), by warp 0's register radix walk.  An empty slice
+        // (a lost copy) proposes nothing and publishes threshold 0.
+        if (!four) {
             st.cand[ctid] = t0;
-            csync();
-            uint32_t rank = 0;
-            for (int i = 0; i < kNC; ++i) rank += st.cand[i] > t0 ? 1u : 0u;
-            csync();
-            st.cand[rank] = t0;
-            csync();
-            T = st.cand[ksel - 1];
         } else {
             st.cand[4 * ctid] = t0;
             st.cand[4 * ctid + 1] = t1;
             st.cand[4 * ctid + 2] = t2;
             st.cand[4 * ctid + 3] = t3;
-            csync();
-            sort_desc(st, 4 * kNC, ctid);
-            T = st.cand[ksel - 1];
         }
-        auto passes = [&](float x, int32_t id) { return make_key(x, id) >= T; };
+        csync();
+        if (ctid < 32) {
+            uint64_t t = 0ull;
+            if (!lost)
+                t = four ? warp_topk_keep<4 * kNC / 32>(st.cand, 4 * kNC, ksel, lane)
+                         : warp_topk_keep<kNC / 32>(st.cand, kNC, ksel, lane);
+            if (lane == 0) sm.pub_tau = t;
+        }
+        cluster.sync();  // every CTA's threshold is published
+        // The largest of them: its CTA has ksel keys at or above it, so the row's
+        // shortlist is at or above it, and each CTA publishes only its keys there.
+        if (ctid < 32) {
+            const uint64_t t = ctid < kSmallCl ? cluster.map_shared_rank(&sm, ctid)->pub_tau : 0ull;
+            const uint64_t tm = warp_max_u64(t);
+            if (ctid == 0) st.thr = tm;
+        }
+        csync();
+        T = st.thr;
+        // A float4 whose largest component is below T's value has no key at or
+        // above T (fmaxf skips NaN, whose keys are below any T of a non-NaN value);
+        // T of a NaN value compares whole keys.
+        const uint32_t To = (uint32_t)(T >> 32);
+        const float Tv = value_of_ord(To);
+        auto reaches = [&](const float4& w) {
+            return To == 0u || fmaxf(fmaxf(w.x, w.y), fmaxf(w.z, w.w)) >= Tv;
+        };
         uint32_t c = 0u;
-#pragma unroll
-        for (int j = 0; j < kSmallNJ; ++j) {
-            const int i = j * kNC + ctid;
-            if (i < n4) {
+        for (int i = ctid; i < n4; i += kNC) {
+            const float4 w = sm.vals[i];
+            if (reaches(w)) {
                 const int32_t id = a.id_offset + c0 + 4 * i;
-                c += (uint32_t)passes(v[j].x, id) + (uint32_t)passes(v[j].y, id + 1) +
-                     (uint32_t)passes(v[j].z, id + 2) + (uint32_t)passes(v[j].w, id + 3);
+                c += (uint32_t)(make_key(w.x, id) >= T) + (uint32_t)(make_key(w.y, id + 1) >= T) +
+                     (uint32_t)(make_key(w.z, id + 2) >= T) + (uint32_t)(make_key(w.w, id + 3) >= T);
             }
         }
-        if (has_t) c += (uint32_t)passes(xt, a.id_offset + tail0 + ctid);
+        if (has_t && make_key(xt, tid_t) >= T) ++c;
         uint32_t total;
-        const uint32_t incl = block_incl_scan(c, st.scan, ctid, total);
+        block_incl_scan(c, st.scan, ctid, total);
         if (total + kCandMargin <= (uint32_t)kCandCap) {  // the same on every thread
-            // published as they are: CTA 0 filters them against every CTA's threshold
-            uint32_t at = incl - c;
+            // published in any order (CTA 0 sorts): a slot per key from a counter
             if (c) {
-#pragma unroll
-                for (int j = 0; j < kSmallNJ; ++j) {
-                    const int i = j * kNC + ctid;
-                    if (i < n4) {
+                for (int i = ctid; i < n4; i += kNC) {
+                    const float4 w = sm.vals[i];
+                    if (reaches(w)) {
                         const int32_t id = a.id_offset + c0 + 4 * i;
-                        if (passes(v[j].x, id)) sm.pub[at++] = make_key(v[j].x, id);
-                        if (passes(v[j].y, id + 1)) sm.pub[at++] = make_key(v[j].y, id + 1);
-                        if (passes(v[j].z, id + 2)) sm.pub[at++] = make_key(v[j].z, id + 2);
-                        if (passes(v[j].w, id + 3)) sm.pub[at++] = make_key(v[j].w, id + 3);
+                        const float xs[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                        for (int r = 0; r < 4; ++r) {
+                            const uint64_t k = make_key(xs[r], id + r);
+                            if (k >= T) sm.pub[atomicAdd(&sm.pub_n, 1u)] = k;
+                        }
                     }
                 }
-                if (has_t && passes(xt, a.id_offset + tail0 + ctid))
-                    sm.pub[at] = make_key(xt, a.id_offset + tail0 + ctid);
-            }
-            if (ctid == 0) {
-                sm.pub_n = total;
-                sm.pub_tau = T;
+                if (has_t && make_key(xt, tid_t) >= T) sm.pub[atomicAdd(&sm.pub_n, 1u)] = make_key(xt, tid_t);
             }
         } else {
-            // More keys reach T than the buffer holds (heavy ties across threads'
-            // maxima): append in rounds, compacting to the top ksel when full.
+            // More keys reach T than the buffer holds (heavy ties at T): append in
+            // rounds, compacting to the top ksel when full.
             if (ctid == 0) st.count = 0u;
             csync();
             uint64_t tau = T - 1ull;  // keys > tau are the keys >= T
             bool full = false;
-            for (int j = 0; j <= kSmallNJ; ++j) {  // rounds kSmallNJ - 1 and the tail
+            for (int j = 0; j <= kSmallNJ; ++j) {  // rounds of one float4 a thread, then the tail
                 const int i = j * kNC + ctid;
                 uint64_t ks[4] = {0ull, 0ull, 0ull, 0ull};
                 if (j < kSmallNJ && i < n4) {
-                    float4 w = x4[i];  // read again (from L2): no register indexing
+                    const float4 w = sm.vals[i];
                     const int32_t id = a.id_offset + c0 + 4 * i;
-                    if ((pmask >> (4 * j)) & 15ull) {  // penalised again, as above
-                        if ((pmask >> (4 * j)) & 1ull) w.x = pen_value(id, w.x);
-                        if ((pmask >> (4 * j + 1)) & 1ull) w.y = pen_value(id + 1, w.y);
-                        if ((pmask >> (4 * j + 2)) & 1ull) w.z = pen_value(id + 2, w.z);
-                        if ((pmask >> (4 * j + 3)) & 1ull) w.w = pen_value(id + 3, w.w);
-                    }
                     ks[0] = make_key(w.x, id);
                     ks[1] = make_key(w.y, id + 1);
                     ks[2] = make_key(w.z, id + 2);
                     ks[3] = make_key(w.w, id + 3);
                 } else if (j == kSmallNJ && has_t) {
-                    ks[0] = make_key(xt, a.id_offset + tail0 + ctid);
+                    ks[0] = make_key(xt, tid_t);
                 }
-#pragma unroll
                 for (int r = 0; r < 4; ++r) {
                     if (full) tau = compact_select(st, st.count, ksel, ctid);
                     warp_append(st, ks[r] > tau, ks[r], lane);
@@ -3841,33 +3842,24 @@ __global__ void __launch_bounds__(kNC, 1) zs_small_kernel(const Args a) {
                 }
             }
             uint32_t n = st.count;
-            uint64_t tau_c = tau + 1ull;
             if (n > ksel) {
-                tau_c = compact_select(st, n, ksel, ctid);
+                compact_select(st, n, ksel, ctid);
                 n = st.count;
             }
             for (uint32_t i = ctid; i < n; i += kNC) sm.pub[i] = st.cand[i];
-            if (ctid == 0) {
-                sm.pub_n = n;
-                sm.pub_tau = tau_c;
-            }
+            if (ctid == 0) sm.pub_n = n;
         }
     }
     cluster.sync();  // every CTA's keys are published
     uint32_t kk = 0u;
     if (crank == 0) {
-        // Every CTA has ksel keys at or above its own threshold, so the row's
-        // shortlist is at or above the largest one: only those keys are gathered.
-        // Counts, thresholds and offsets of all CTAs first (one remote read each).
+        // Counts and offsets of all CTAs first (one remote read each), then every
+        // published key in parallel, four loads in flight a thread, in rounds of
+        // 4 x kNC keys; before a round that might not fit, the candidates are cut to
+        // the top ksel.  The loop bound is the same on every thread (warp_append
+        // needs all lanes).
         if (ctid < 32) {
-            uint32_t nr = 0u;
-            uint64_t t = 0ull;
-            if (ctid < kSmallCl) {
-                const SmallSmem* rs = cluster.map_shared_rank(&sm, ctid);
-                nr = rs->pub_n;
-                t = rs->pub_tau;
-            }
-            const uint64_t tmax = warp_max_u64(t);
+            const uint32_t nr = ctid < kSmallCl ? cluster.map_shared_rank(&sm, ctid)->pub_n : 0u;
             uint32_t inc = nr;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
@@ -3876,18 +3868,11 @@ __global__ void __launch_bounds__(kNC, 1) zs_small_kernel(const Args a) {
             }
             if (ctid < kSmallCl) sm.g_off[ctid] = inc - nr;  // first key of CTA ctid
             if (ctid == 31) sm.g_all = inc;                  // all published keys
-            if (ctid == 0) {
-                st.thr = tmax;
-                st.count = 0u;
-            }
+            if (ctid == 0) st.count = 0u;
         }
         csync();
-        uint64_t tau = st.thr - 1ull;  // keys > tau: at or above the largest threshold
+        uint64_t tau = T ? T - 1ull : 0ull;  // every published key passes
         const uint32_t all = sm.g_all;
-        // Every published key is read in parallel, four loads in flight a thread,
-        // in rounds of 4 x kNC keys; before a round that might not fit, the
-        // candidates are cut to the top ksel (which raises tau).  The loop bound
-        // is the same on every thread (warp_append needs all lanes).
         bool full = false;
         for (uint32_t b = 0; b < all; b += 4 * kNC) {
             if (full) tau = compact_select(st, st.count, ksel, ctid);
