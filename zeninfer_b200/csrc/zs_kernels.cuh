@@ -2198,6 +2198,17 @@ __device__ __forceinline__ uint64_t warp_topk_keep(uint64_t* keys, uint32_t n, u
     return T;
 }
 
+// warp_topk_keep at the smallest register width that holds n keys: the walk's
+// cost per bit grows with the width, and most compactions see a few hundred keys
+// in a buffer sized for thousands.
+template <int RMAX>
+__device__ __forceinline__ uint64_t warp_topk_keep_fit(uint64_t* keys, uint32_t n, uint32_t kk,
+                                                       int lane, uint32_t slack = 0u,
+                                                       uint32_t* kept = nullptr) {
+    if (RMAX > 8 && n <= 256u) return warp_topk_keep<8>(keys, n, kk, lane, slack, kept);
+    return warp_topk_keep<RMAX>(keys, n, kk, lane, slack, kept);
+}
+
 // ---------------------------------------------------------------------------
 // Warp-per-row merge for shortlists up to kWarpMergeMaxK: each warp merges one
 // row's partial blocks in its own shared-memory slot with warp-synchronous
@@ -2503,7 +2514,7 @@ __device__ void warp_merge_row(uint64_t* cand, const MergeArgs& a, int row, cons
 #pragma unroll
             for (int jj = 0; jj < J; ++jj) {
                 if (count + 32 > (uint32_t)CAP) {
-                    tau = warp_topk_keep<CAP / 32>(cand, count, ksel, lane);
+                    tau = warp_topk_keep_fit<CAP / 32>(cand, count, ksel, lane);
                     count = ksel;  // exactly ksel keys >= tau
                 }
                 const bool pass = k[jj] > tau;
@@ -2517,7 +2528,7 @@ __device__ void warp_merge_row(uint64_t* cand, const MergeArgs& a, int row, cons
     // Up to 256 keys are sorted whole (the shortlist is their prefix), which is
     // cheaper than selecting the top-ksel first; more are cut to ksel first.
     if (count > kWarpMergeMaxK) {
-        warp_topk_keep<CAP / 32>(cand, count, ksel, lane);
+        warp_topk_keep_fit<CAP / 32>(cand, count, ksel, lane);
         count = ksel;
     }
     warp_sort256_desc(cand, count, lane);
@@ -2656,7 +2667,7 @@ __device__ __forceinline__ void wcompact(WarpSel<C>& ws, WState& w, uint32_t kef
     // keys more): with 64 keys per lane every bit of the walk is costly, and a
     // tie group at the keff-th key would otherwise send it through the id bits.
     uint32_t kept = keff;
-    w.tau_key = warp_topk_keep<C::kCap / 32>(ws.cand, w.count, keff, lane, C::kSlackDiv ? keff / C::kSlackDiv : 0u, &kept);
+    w.tau_key = warp_topk_keep_fit<C::kCap / 32>(ws.cand, w.count, keff, lane, C::kSlackDiv ? keff / C::kSlackDiv : 0u, &kept);
     w.count = kept;
     w.tau_f = tau_value(w.tau_key);
     w.tau_id = key_id(w.tau_key);
@@ -3050,7 +3061,7 @@ __device__ void wend_piece(const Args& a, WarpSel<C>& ws, WState& w, const WPiec
     // top-ksel (final values): that is all the block has to carry.
     const uint32_t ksel = (uint32_t)rp.ksel;
     if (w.count > ksel) {
-        warp_topk_keep<C::kCap / 32>(ws.cand, w.count, ksel, lane);
+        warp_topk_keep_fit<C::kCap / 32>(ws.cand, w.count, ksel, lane);
         w.count = ksel;
     }
     uint8_t* pp = a.wpart + ((int64_t)gw * a.wl_P + j) * a.wl_stride;
