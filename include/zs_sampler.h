@@ -231,6 +231,19 @@ zs_status zs_get_timing(zs_handle h, zs_timing* out);
 #define ZS_LMHEAD_ROUTE_TWO_PASS 2
 zs_status zs_set_lmhead_route(zs_handle h, int32_t route);
 
+/* The tiles of the lm_head GEMM (zs_lmhead_sample, zs_lmhead_logits), for this
+ * handle.  No counterpart in the reference.
+ *   ZS_LMHEAD_TILES_AUTO    (default) CTA pairs from 256 rows up, one CTA below
+ *   ZS_LMHEAD_TILES_SINGLE  one CTA per 128-row x 128-column tile
+ *   ZS_LMHEAD_TILES_PAIR    two CTAs (a cluster of two SMs) per 256 x 256 tile
+ *                           whenever the device can hold them
+ * A pair's MMAs read half the operand bytes per product of one CTA's.  Logits, ids
+ * and Rng states are the same either way. */
+#define ZS_LMHEAD_TILES_AUTO 0
+#define ZS_LMHEAD_TILES_SINGLE 1
+#define ZS_LMHEAD_TILES_PAIR 2
+zs_status zs_set_lmhead_tiles(zs_handle h, int32_t mode);
+
 /* Speculative opening thresholds of zs_sample (and zs_decode_step), per handle.  No
  * counterpart in the reference.  A long row slice of a long shortlist (top_k or the
  * default 256 at least 128, no repeat penalty, no log Z) can start its streaming

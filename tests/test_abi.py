@@ -71,6 +71,7 @@ def test_argument_errors_need_no_device(lib):
     out = C.c_int64()
     assert lib.zs_shard_partial_bytes(4, 0, 2, C.byref(p), 0, C.byref(out)) == 1
     assert lib.zs_set_lmhead_route(None, 0) == 1
+    assert lib.zs_set_lmhead_tiles(None, 0) == 1
 
 
 def test_create_without_device(lib):

@@ -53,7 +53,7 @@ def _hidden(B, E, seed):
 
 
 def _run(sampler, hidden, nw, w, params, seeds, with_logits=True, history=None, hlen=None,
-         route="fused"):
+         route="fused", tiles="auto"):
     import torch
     dev = sampler.device
     B, V = hidden.shape[0], w.shape[0]
@@ -66,11 +66,13 @@ def _run(sampler, hidden, nw, w, params, seeds, with_logits=True, history=None, 
         h = torch.from_numpy(history).to(dev)
         hl = torch.from_numpy(hlen).to(dev)
     sampler.set_lmhead_route(route)
+    sampler.set_lmhead_tiles(tiles)
     try:
         ids = sampler.lmhead_sample(hidden.to(dev), nw.to(dev), w.to(dev), params, st, eps=EPS,
                                     history=h, history_len=hl, out_logits=lg)
     finally:
         sampler.set_lmhead_route("auto")
+        sampler.set_lmhead_tiles("auto")
     sampler.check_device_status()
     out = {"ids": ids.cpu().numpy(), "states": tensor_to_states(st)}
     if lg is not None:
@@ -217,6 +219,40 @@ def test_lmhead_routes_agree(sampler, B):
         assert np.array_equal(got[r]["logits"].view(np.uint32),
                               got["fused"]["logits"].view(np.uint32)), r
     _check_sampling(sampler, got["auto"], params, seeds)
+
+
+@pytest.mark.parametrize("B,tiles", [(5, "pair"), (37, "pair"), (300, "single"),
+                                     (300, "pair"), (2048, "single")])
+def test_lmhead_tiles(sampler, B, tiles):
+    """One-CTA tiles and CTA-pair tiles (tcgen05 cta_group::2, 256 x 256), each
+    forced where the default would take the other: pairs at 5 and 37 rows (the
+    second CTA's rows all lie outside the batch), single CTAs at 300 and 2048 rows.
+    Logits within the bounds, ids and Rng states against zs_sample on those logits
+    and the restatement, both routes, and the same draws as the other tiling."""
+    V, E = 151936, 896
+    w, nw = _model(V, E)
+    hidden = _hidden(B, E, 90 + B)
+    params = _mixed_params(B)
+    seeds = np.arange(B, dtype=np.uint64) + np.uint64(13)
+    other = "single" if tiles == "pair" else "pair"
+    res = _run(sampler, hidden, nw, w, params, seeds, tiles=tiles)
+    _check_logits(res["logits"], hidden, nw, w, np.array([0, 1, B // 2, B - 1]),
+                  against_reference=True)
+    _check_sampling(sampler, res, params, seeds)
+    two = _run(sampler, hidden, nw, w, params, seeds, route="two_pass", tiles=tiles)
+    _check_logits(two["logits"], hidden, nw, w, np.array([0, B - 1]))
+    _check_sampling(sampler, two, params, seeds)
+    alt = _run(sampler, hidden, nw, w, params, seeds, tiles=other)
+    _check_sampling(sampler, alt, params, seeds)
+    same = np.array_equal(alt["logits"].view(np.uint32), res["logits"].view(np.uint32))
+    if same:  # equal logits must give equal draws
+        assert np.array_equal(alt["ids"], res["ids"])
+        assert np.array_equal(alt["states"], res["states"])
+
+
+def test_lmhead_tiles_rejects_unknown(sampler):
+    with pytest.raises(ValueError):
+        sampler.set_lmhead_tiles("quad")
 
 
 def test_lmhead_route_rejects_unknown(sampler):

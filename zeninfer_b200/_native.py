@@ -21,6 +21,7 @@ EXPORTS = (
     "zs_selftest_wait_timeout", "zs_decode_step", "zs_lmhead_sample", "zs_lmhead_logits",
     "zs_set_lmhead_route", "zs_shard_owner_rows", "zs_shard_row_spans", "zs_shard_merge_rows",
     "zs_set_collective_timeout", "zs_set_speculation", "zs_set_small_batch",
+    "zs_set_lmhead_tiles",
 )
 
 ZS_OK = 0
@@ -103,6 +104,7 @@ def lib() -> C.CDLL:
     L.zs_logits_stats.argtypes = [vp, vp, i64, i32, i32, i32, vp, vp, vp, vp, vp, vp]
     L.zs_set_timing.argtypes = [vp, i32]
     L.zs_set_lmhead_route.argtypes = [vp, i32]
+    L.zs_set_lmhead_tiles.argtypes = [vp, i32]
     L.zs_get_timing.argtypes = [vp, C.POINTER(ZsTiming)]
     L.zs_sample_noalloc.argtypes = [vp, i64, i32, i32, C.POINTER(ZsParams), vp, i64, vp, vp, vp,
                                     vp, vp]
@@ -118,7 +120,8 @@ def lib() -> C.CDLL:
                                             "zs_lmhead_logits", "zs_set_lmhead_route",
                                             "zs_shard_owner_rows", "zs_shard_row_spans",
                                             "zs_shard_merge_rows", "zs_set_collective_timeout",
-                                            "zs_set_speculation", "zs_set_small_batch"):
+                                            "zs_set_speculation", "zs_set_small_batch",
+                                            "zs_set_lmhead_tiles"):
             f.restype = C.c_int
     _lib = L
     return L

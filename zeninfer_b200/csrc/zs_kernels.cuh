@@ -3092,7 +3092,10 @@ __global__ void __launch_bounds__(C::kWarps * 32, 1) zs_wselect_kernel(const Arg
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     WarpSel<C>& ws = sm.w[warp];
     grid_dep_trigger();  // the merge may be scheduled; it waits for this grid to end
-    const int32_t gw = blockIdx.x * C::kWarps + warp;
+    // Warp slots are dealt across the CTAs first (slot `warp` of CTA b takes share
+    // warp * gridDim.x + b), so a layout with fewer warps than the grid's slots still
+    // has warps on every SM of the grid instead of filling the first CTAs.
+    const int32_t gw = warp * (int32_t)gridDim.x + (int32_t)blockIdx.x;
     if (gw >= a.wl_NW) return;  // the whole warp; nothing in this kernel syncs the block
     WShare sh;
     sh.b0 = wl_bound(a.wl_E, a.wl_NW, gw);

@@ -86,6 +86,7 @@ struct LmArgs {
     int32_t prefetch;            // weight boxes each CTA prefetches into L2 while rmsnorm runs
     uint32_t* tau;               // optional [B] value orders shared by a row's slices
     int* status;
+    int32_t pair;                // 2: zs_lmhead_kernel<2> (CTA pairs), else <1>; host only
 };
 
 // ---- PTX wrappers: TMA tiles and the 5th-generation tensor cores ----
@@ -194,8 +195,96 @@ __device__ __forceinline__ uint64_t sw128_desc(const void* tile) {
 
 // Instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A and B bf16 (bits 7-9,
 // 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 at bit 17, M >> 4 at bit 24.
-constexpr uint32_t kLmIdesc = (1u << 4) | (1u << 7) | (1u << 10) |
-                              ((uint32_t)(kLmN >> 3) << 17) | ((uint32_t)(kLmM >> 4) << 24);
+constexpr uint32_t lm_idesc(int M, int N) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// Tile geometry of zs_lmhead_kernel<P>.  P = 1: one CTA computes 128 rows x 128
+// vocabulary columns per tile.  P = 2: a CTA pair (a cluster of two) computes 256 x
+// 256 with tcgen05.mma.cta_group::2: each CTA stages its own 128 rows of xn and its
+// own 128 of the tile's 256 weight rows, and holds its 128 rows x all 256 columns in
+// its tensor memory.  Per MMA an SM then reads 8 KB of operands from shared memory
+// for 128 x 256 x 16 products, where the one-CTA tile reads 8 KB for 128 x 128 x 16:
+// half the shared-memory and L2 traffic per product.
+template <int P>
+struct LmGeom {
+    static_assert(P == 1 || P == 2, "one CTA or a CTA pair");
+    static constexpr int kRows = kLmM * P;        // batch rows per tile (the pair's)
+    static constexpr int kCols = kLmN * P;        // vocabulary columns per tile
+    static constexpr int kAccs = 512 / kCols;     // accumulators: all 512 TMEM columns
+    static constexpr uint32_t kIdesc = lm_idesc(kRows, kCols);
+    // epilogue arrivals that free an accumulator: every thread of the four epilogue
+    // warps (P = 1), or one lane per epilogue warp of both CTAs, on the leader (P = 2)
+    static constexpr uint32_t kAccEmptyCount = P == 1 ? 4 * 32 : 2 * 4;
+};
+static_assert(LmGeom<1>::kAccs <= kLmAccs && LmGeom<2>::kAccs <= kLmAccs, "barrier arrays");
+
+// ---- CTA-pair (cluster of two) primitives ----
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// The shared::cluster address of `local` (this CTA's shared memory) in CTA `rank`.
+__device__ __forceinline__ uint32_t smem_in_cta(const void* local, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(local)), "r"(rank));
+    return r;
+}
+// Every thread of both CTAs: orders this CTA's earlier shared-memory writes (barrier
+// initialisation included) before the other CTA's later accesses.
+__device__ __forceinline__ void cluster_sync_all() {
+    __syncwarp();  // the .aligned forms want the whole warp at the same instruction
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                     : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster)
+                 : "memory");
+}
+// A 2-D tile into this CTA's shared memory whose bytes count on the barrier of the
+// pair's leader (bar_cluster: a shared::cluster address), no multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int32_t x,
+                                                 int32_t y, uint32_t bar_cluster) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster)
+        : "memory");
+}
+__device__ __forceinline__ void tc_alloc_pair(uint32_t* dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_addr(dst)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tc_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+// D (both CTAs' tensor memory) (+)= A (both CTAs' rows) . B (both CTAs' halves)^T;
+// the descriptors and the TMEM address name the leader's copies, the peer's are at
+// the same offsets.
+__device__ __forceinline__ void tc_mma_bf16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrives once on `bar` (same offset) in every CTA of `mask` when this thread's
+// earlier tcgen05 operations of the pair have completed.
+__device__ __forceinline__ void tc_commit_pair(uint64_t* bar, uint16_t mask) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
+        "[%0], %1;" ::"r"(smem_addr(bar)),
+        "h"(mask)
+        : "memory");
+}
 
 // Bounded wait that also gives up when another role has aborted.
 __device__ __forceinline__ bool lm_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
@@ -213,11 +302,14 @@ __device__ __forceinline__ bool lm_wait(uint64_t* bar, uint32_t parity, volatile
     }
 }
 
-// Units [u_begin, u_end) of this CTA: a contiguous share, so consecutive units of
-// one row tile (adjacent slices) meet in one CTA and share its candidate buffers.
+// Units [u_begin, u_end) of this CTA (of this CTA pair for P = 2, whose CTAs are
+// consecutive blocks): a contiguous share, so consecutive units of one row tile
+// (adjacent slices) meet in one CTA and share its candidate buffers.
+template <int P>
 __device__ __forceinline__ void lm_range(const LmArgs& a, int& u_begin, int& u_end) {
-    u_begin = (int)(((int64_t)blockIdx.x * a.n_units) / gridDim.x);
-    u_end = (int)(((int64_t)(blockIdx.x + 1) * a.n_units) / gridDim.x);
+    const int64_t c = blockIdx.x / P, n = gridDim.x / P;
+    u_begin = (int)((c * a.n_units) / n);
+    u_end = (int)(((c + 1) * a.n_units) / n);
 }
 
 __device__ __forceinline__ void lm_unit(const LmArgs& a, int u, int& m, int& s, int& t0, int& t1) {
@@ -403,16 +495,25 @@ __device__ __forceinline__ void lm_chunk(const uint32_t (&r)[32], int col0, int 
     }
 }
 
+// P = 1: one CTA per tile.  P = 2: launched in clusters of two CTAs, each pair one
+// 256 x 256 tile at a time (LmGeom); the leader (cluster rank 0) issues the MMAs for
+// both, the copies of both CTAs count on the leader's barriers, the MMA commits
+// arrive on both CTAs' barriers, and both epilogues free an accumulator on the
+// leader's barrier.
+template <int P>
 __global__ void __launch_bounds__(kLmThreads, 1)
     zs_lmhead_kernel(const __grid_constant__ CUtensorMap tm_a,
                      const __grid_constant__ CUtensorMap tm_b,
                      const __grid_constant__ CUtensorMap tm_c, const LmArgs a) {
+    using G = LmGeom<P>;
     extern __shared__ uint8_t lm_raw[];
     const uint32_t pad = (1024u - (smem_addr(lm_raw) & 1023u)) & 1023u;
     LmSmem& sm = *reinterpret_cast<LmSmem*>(lm_raw + pad);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nk = (a.E + kLmBK - 1) / kLmBK;
     volatile int* abort = &sm.abort;
+    const uint32_t rank = P == 2 ? cluster_rank() : 0u;  // this CTA's half of the pair
+    const bool leader = rank == 0u;
 
     const int ns = a.ns;
     uint8_t* const tiles_a = sm.ring;
@@ -424,9 +525,9 @@ __global__ void __launch_bounds__(kLmThreads, 1)
             mbar_init(&sm.full[s], 1);
             mbar_init(&sm.empty[s], 1);
         }
-        for (int i = 0; i < kLmAccs; ++i) {
+        for (int i = 0; i < G::kAccs; ++i) {
             mbar_init(&sm.acc_full[i], 1);
-            mbar_init(&sm.acc_empty[i], 4 * 32);
+            mbar_init(&sm.acc_empty[i], G::kAccEmptyCount);
         }
         mbar_init(&sm.drain, 1);
         sm.abort = 0;
@@ -435,15 +536,23 @@ __global__ void __launch_bounds__(kLmThreads, 1)
         tma_prefetch_map(&tm_b);
     }
     if (warp == 1) {
-        tc_alloc(&sm.tmem_base, kLmTmemCols);
-        tc_relinquish();
+        if (P == 1) {
+            tc_alloc(&sm.tmem_base, kLmTmemCols);
+            tc_relinquish();
+        } else {
+            tc_alloc_pair(&sm.tmem_base, kLmTmemCols);
+            tc_relinquish_pair();
+        }
     }
     tc_fence_before();
-    __syncthreads();
+    if (P == 1)
+        __syncthreads();
+    else
+        cluster_sync_all();  // both CTAs' barriers exist before either signals the other's
     tc_fence_after();
     const uint32_t tmem = sm.tmem_base;
     int u_begin, u_end;
-    lm_range(a, u_begin, u_end);
+    lm_range<P>(a, u_begin, u_end);
 
     // Launched behind zs_lm_rmsnorm_kernel as a programmatic dependent: the copy
     // issuer first pulls its first weight boxes into L2 (they do not depend on the
@@ -456,7 +565,7 @@ __global__ void __launch_bounds__(kLmThreads, 1)
             lm_unit(a, u, m, s, t0, t1);
             for (int t = t0; left > 0 && t < t1; ++t)
                 for (int kb = 0; left > 0 && kb < nk; ++kb, --left)
-                    tma_prefetch_l2_2d(&tm_b, kb * kLmBK, t * kLmN);
+                    tma_prefetch_l2_2d(&tm_b, kb * kLmBK, t * G::kCols + (int)rank * kLmN);
         }
     }
     grid_dep_wait();
@@ -476,11 +585,24 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                             ok = false;
                             break;
                         }
-                        mbar_arrive_expect_tx(&sm.full[stage], kLmTileABytes + kLmTileBBytes);
-                        tma_load_2d(tiles_a + stage * kLmTileABytes, &tm_a, kb * kLmBK, m * kLmM,
-                                    &sm.full[stage]);
-                        tma_load_2d(tiles_b + stage * kLmTileBBytes, &tm_b, kb * kLmBK, t * kLmN,
-                                    &sm.full[stage]);
+                        if (P == 1) {
+                            mbar_arrive_expect_tx(&sm.full[stage], kLmTileABytes + kLmTileBBytes);
+                            tma_load_2d(tiles_a + stage * kLmTileABytes, &tm_a, kb * kLmBK,
+                                        m * kLmM, &sm.full[stage]);
+                            tma_load_2d(tiles_b + stage * kLmTileBBytes, &tm_b, kb * kLmBK,
+                                        t * kLmN, &sm.full[stage]);
+                        } else {
+                            // both CTAs' bytes count on the leader's barrier, which the
+                            // leader alone arms; the peer's copies may land first
+                            if (leader)
+                                mbar_arrive_expect_tx(&sm.full[stage],
+                                                      2u * (kLmTileABytes + kLmTileBBytes));
+                            const uint32_t bar = smem_in_cta(&sm.full[stage], 0u);
+                            tma_load_2d_pair(tiles_a + stage * kLmTileABytes, &tm_a, kb * kLmBK,
+                                             m * G::kRows + (int)rank * kLmM, bar);
+                            tma_load_2d_pair(tiles_b + stage * kLmTileBBytes, &tm_b, kb * kLmBK,
+                                             t * G::kCols + (int)rank * kLmN, bar);
+                        }
                         ++issued;
                         if (++stage == (uint32_t)ns) {
                             stage = 0;
@@ -491,14 +613,21 @@ __global__ void __launch_bounds__(kLmThreads, 1)
             }
             if (!ok) set_status(a.status, kStatusTimeout);
             // Every copy issued has landed before the CTA may exit (the MMA issuer
-            // has waited for all of them already unless a wait ran out).
-            for (int64_t i = issued - ns; i < issued; ++i)
-                if (i >= 0) mbar_wait_bounded(&sm.full[i % ns], (uint32_t)((i / ns) & 1));
+            // has waited for all of them already unless a wait ran out).  The peer
+            // of a pair cannot see its copies complete (they count on the leader's
+            // barriers, which the leader waits for): after a wait ran out it gives
+            // them time to land instead.
+            if (P == 1 || leader) {
+                for (int64_t i = issued - ns; i < issued; ++i)
+                    if (i >= 0) mbar_wait_bounded(&sm.full[i % ns], (uint32_t)((i / ns) & 1));
+            } else if (!ok) {
+                for (int i = 0; i < 100; ++i) __nanosleep(1000);
+            }
         }
         __syncwarp();
     } else if (warp == 1) {
-        // ---- MMA issuer ----
-        if (lane == 0) {
+        // ---- MMA issuer (the leader's, for a pair) ----
+        if (lane == 0 && (P == 1 || leader)) {
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool ok = true;
             for (int u = u_begin; ok && u < u_end; ++u) {
@@ -510,7 +639,7 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t d = tmem + acc * (uint32_t)kLmN;
+                    const uint32_t d = tmem + acc * (uint32_t)G::kCols;
                     for (int kb = 0; kb < nk; ++kb) {
                         if (!lm_wait(&sm.full[stage], phase, abort)) {
                             ok = false;
@@ -520,18 +649,29 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                         const uint64_t ad = sw128_desc(tiles_a + stage * kLmTileABytes);
                         const uint64_t bd = sw128_desc(tiles_b + stage * kLmTileBBytes);
 #pragma unroll
-                        for (int k = 0; k < kLmBK / 16; ++k)
-                            tc_mma_bf16(d, ad + 2ull * k, bd + 2ull * k, kLmIdesc,
-                                        (kb | k) != 0 ? 1u : 0u);
-                        tc_commit(&sm.empty[stage]);
+                        for (int k = 0; k < kLmBK / 16; ++k) {
+                            if (P == 1)
+                                tc_mma_bf16(d, ad + 2ull * k, bd + 2ull * k, G::kIdesc,
+                                            (kb | k) != 0 ? 1u : 0u);
+                            else
+                                tc_mma_bf16_pair(d, ad + 2ull * k, bd + 2ull * k, G::kIdesc,
+                                                 (kb | k) != 0 ? 1u : 0u);
+                        }
+                        if (P == 1)
+                            tc_commit(&sm.empty[stage]);
+                        else
+                            tc_commit_pair(&sm.empty[stage], (uint16_t)3u);  // both CTAs' stage
                         if (++stage == (uint32_t)ns) {
                             stage = 0;
                             phase ^= 1u;
                         }
                     }
                     if (!ok) break;
-                    tc_commit(&sm.acc_full[acc]);
-                    if (++acc == kLmAccs) {
+                    if (P == 1)
+                        tc_commit(&sm.acc_full[acc]);
+                    else
+                        tc_commit_pair(&sm.acc_full[acc], (uint16_t)3u);
+                    if (++acc == G::kAccs) {
                         acc = 0;
                         acc_phase ^= 1u;
                     }
@@ -539,7 +679,10 @@ __global__ void __launch_bounds__(kLmThreads, 1)
             }
             if (!ok) set_status(a.status, kStatusTimeout);
             // Every MMA issued has completed before the tensor memory is freed.
-            tc_commit(&sm.drain);
+            if (P == 1)
+                tc_commit(&sm.drain);
+            else
+                tc_commit_pair(&sm.drain, (uint16_t)1u);  // the leader's own barrier
             mbar_wait_bounded(&sm.drain, 0u);
         }
         __syncwarp();
@@ -563,7 +706,7 @@ __global__ void __launch_bounds__(kLmThreads, 1)
         for (int u = u_begin; ok && u < u_end; ++u) {
             int m, s, t0, t1;
             lm_unit(a, u, m, s, t0, t1);
-            const int row = m * kLmM + r_in;
+            const int row = m * G::kRows + (int)rank * kLmM + r_in;
             const bool valid = row < a.B;
             uint32_t keff = 1;
             if (valid) {
@@ -589,12 +732,12 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                const int tcol = t * kLmN;
-                const uint32_t base = lane_addr + acc * (uint32_t)kLmN;
+                const int tcol = t * G::kCols;
+                const uint32_t base = lane_addr + acc * (uint32_t)G::kCols;
                 // the other slices' bound, read now and taken after this tile
                 const uint32_t g_seen = gtau ? lm_shared_bound(gtau) : 0u;
 #pragma unroll 1
-                for (int c = 0; c < kLmN / 32; ++c) {
+                for (int c = 0; c < G::kCols / 32; ++c) {
                     uint32_t ra[32];
                     __syncwarp();
                     tc_ld32_issue(base + (uint32_t)(c * 32), ra);
@@ -614,7 +757,8 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                         fence_proxy_async_smem();
                         __syncwarp();
                         if (lane == 0) {
-                            tma_store_2d(&tm_c, stg, tcol + c * 32, m * kLmM + q * 32);
+                            tma_store_2d(&tm_c, stg, tcol + c * 32,
+                                         m * G::kRows + (int)rank * kLmM + q * 32);
                             bulk_commit_group();
                         }
                         stg_buf ^= 1;
@@ -625,8 +769,13 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                 }
                 if (gtau) lm_adopt(g_seen, tau_ord, tau_f, open);
                 tc_fence_before();
-                mbar_arrive(&sm.acc_empty[acc]);
-                if (++acc == kLmAccs) {
+                if (P == 1) {
+                    mbar_arrive(&sm.acc_empty[acc]);
+                } else {
+                    __syncwarp();  // the warp's TMEM loads have all completed
+                    if (lane == 0) mbar_arrive_cluster(smem_in_cta(&sm.acc_empty[acc], 0u));
+                }
+                if (++acc == G::kAccs) {
                     acc = 0;
                     acc_phase ^= 1u;
                 }
@@ -662,10 +811,16 @@ __global__ void __launch_bounds__(kLmThreads, 1)
     }
 
     tc_fence_before();
-    __syncthreads();
+    if (P == 1)
+        __syncthreads();
+    else
+        cluster_sync_all();  // the leader's MMAs (into both CTAs) have drained
     if (warp == 1) {
         tc_fence_after();
-        tc_dealloc(tmem, kLmTmemCols);
+        if (P == 1)
+            tc_dealloc(tmem, kLmTmemCols);
+        else
+            tc_dealloc_pair(tmem, kLmTmemCols);
     }
 }
 

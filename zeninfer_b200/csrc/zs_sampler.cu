@@ -362,6 +362,8 @@ struct zs_context {
     };
     bool timing = false;
     int32_t lm_route = ZS_LMHEAD_ROUTE_AUTO;  // zs_set_lmhead_route
+    int32_t lm_tiles = ZS_LMHEAD_TILES_AUTO;  // zs_set_lmhead_tiles
+    int lm_pairs = 0;                         // resident CTA pairs of zs_lmhead_kernel<2>
     int32_t spec_mode = ZS_SPECULATION_ON;    // zs_set_speculation
     int small_clusters = 0;                   // zs_small_kernel clusters resident at once (0: none)
     int32_t small_max_rows = 8;               // zs_set_small_batch
@@ -589,7 +591,10 @@ zs_status launch_wselect(zs_context* h, zs::Args a, const Plan& pl, uint8_t* blo
     a.wl_P = L.P;
     a.wl_Vn = L.Vn;
     a.wl_class = C::kClass;
-    const int grid = (L.NW + C::kWarps - 1) / C::kWarps;
+    // At least one CTA per SM (up to one per warp): the kernel deals warp slots across
+    // CTAs, so a row-aligned layout of, say, 1024 warps runs on all SMs rather than on
+    // 86 full CTAs.
+    const int grid = std::max((L.NW + C::kWarps - 1) / C::kWarps, std::min(L.NW, h->num_sms));
     const size_t smem = h->wsel_smem[C::kClass];
     LaunchScope scope(h, 0, st);
     if (want_lse)
@@ -859,9 +864,32 @@ zs_status zs_create(int device, zs_handle* out) {
         (e = cudaFuncSetAttribute(zs::zs_warp_merge_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)h->warp_merge_smem)) != cudaSuccess)
         return cleanup(cuda_fail(e, "cudaFuncSetAttribute"));
     if ((size_t)prop.sharedMemPerBlockOptin >= zs::kLmSmemBytes &&
-        (e = cudaFuncSetAttribute(zs::zs_lmhead_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)zs::kLmSmemBytes)) != cudaSuccess)
+        ((e = cudaFuncSetAttribute(zs::zs_lmhead_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)zs::kLmSmemBytes)) != cudaSuccess ||
+         (e = cudaFuncSetAttribute(zs::zs_lmhead_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)zs::kLmSmemBytes)) != cudaSuccess))
         return cleanup(cuda_fail(e, "cudaFuncSetAttribute zs_lmhead_kernel"));
+    // CTA pairs of the lm_head kernel that can be resident at once (0: none; the
+    // one-CTA tiles are used then).
+    h->lm_pairs = 0;
+    if ((size_t)prop.sharedMemPerBlockOptin >= zs::kLmSmemBytes) {
+        cudaLaunchConfig_t cfg;
+        std::memset(&cfg, 0, sizeof(cfg));
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.gridDim = dim3(2 * (h->num_sms / 2));
+        cfg.blockDim = dim3(zs::kLmThreads);
+        cfg.dynamicSmemBytes = zs::kLmSmemBytes;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, zs::zs_lmhead_kernel<2>, &cfg) == cudaSuccess)
+            h->lm_pairs = std::min(n, h->num_sms / 2);
+        (void)cudaGetLastError();
+    }
     zs_status sw = setup_wselect<zs::WCfgS>(&h->wsel_smem[0], &h->wsel_warps[0], h->num_sms);
     if (sw == ZS_OK) sw = setup_wselect<zs::WCfgL>(&h->wsel_smem[1], &h->wsel_warps[1], h->num_sms);
     if (sw != ZS_OK) return cleanup(sw);
@@ -963,6 +991,16 @@ zs_status zs_set_lmhead_route(zs_handle h, int32_t route) {
         route != ZS_LMHEAD_ROUTE_TWO_PASS)
         return fail(ZS_ERR_INVALID_ARGUMENT, "route must be ZS_LMHEAD_ROUTE_AUTO, _FUSED or _TWO_PASS");
     h->lm_route = route;
+    return ZS_OK;
+}
+
+zs_status zs_set_lmhead_tiles(zs_handle h, int32_t mode) {
+    if (!h) return fail(ZS_ERR_INVALID_ARGUMENT, "null handle");
+    if (mode != ZS_LMHEAD_TILES_AUTO && mode != ZS_LMHEAD_TILES_SINGLE &&
+        mode != ZS_LMHEAD_TILES_PAIR)
+        return fail(ZS_ERR_INVALID_ARGUMENT,
+                    "mode must be ZS_LMHEAD_TILES_AUTO, _SINGLE or _PAIR");
+    h->lm_tiles = mode;
     return ZS_OK;
 }
 
@@ -1133,6 +1171,28 @@ zs_status lm_tensor_map(zs_context* h, CUtensorMap* map, const void* base, int64
 // Slices per row for mt row tiles x nt column tiles on `ctas` CTAs: the fewest
 // slices (at most `cap`) whose busiest CTA has at most 2% more tiles than the best
 // split.
+// Tiles of one CTA (128 rows x 128 columns) or of a CTA pair (256 x 256): pairs
+// halve the operand traffic per product, so they are the default from 256 rows up,
+// where both halves of a pair's rows are in use (zs_set_lmhead_tiles overrides).
+int lm_pair_for(const zs_context* h, int batch) {
+    if (h->lm_pairs <= 0 || h->lm_tiles == ZS_LMHEAD_TILES_SINGLE) return 1;
+    if (h->lm_tiles == ZS_LMHEAD_TILES_PAIR) return 2;
+    return batch >= 2 * zs::kLmM ? 2 : 1;
+}
+
+int lm_slices(int mt, int nt, int ctas, int cap);
+
+// Sets a.pair, the row and column tile counts, the slices per row tile (at most
+// `cap`) and the units of a batch.
+void lm_geometry(const zs_context* h, zs::LmArgs& a, int batch, int n_vocab, int cap) {
+    a.pair = lm_pair_for(h, batch);
+    const int rows = zs::kLmM * a.pair, cols = zs::kLmN * a.pair;
+    a.mt = (batch + rows - 1) / rows;
+    a.nt = (n_vocab + cols - 1) / cols;
+    a.S = lm_slices(a.mt, a.nt, a.pair == 2 ? h->lm_pairs : h->num_sms, cap);
+    a.n_units = a.mt * a.S;
+}
+
 int lm_slices(int mt, int nt, int ctas, int cap) {
     auto span = [&](int S) {
         const int64_t units = (int64_t)mt * S;
@@ -1196,9 +1256,11 @@ zs_status lm_run(zs_context* h, const float* hidden, int64_t hidden_ld, const fl
     // sit behind the ring, so a batch within one warp's 32 rows (or logits stored
     // directly) leaves room for more weight tiles in flight.
     {
-        const int64_t rows_in_use = (a.select || a.tma_out)
-                                        ? (a.mt > 1 || a.tma_out ? zs::kLmM : ((int64_t)a.B + 31) / 32 * 32)
-                                        : 0;
+        const int64_t rows_in_use =
+            (a.select || a.tma_out)
+                ? (a.mt > 1 || a.tma_out ? zs::kLmM
+                                         : std::min<int64_t>(zs::kLmM, ((int64_t)a.B + 31) / 32 * 32))
+                : 0;
         a.ns = zs::kLmStages;
         for (int n = zs::kLmStagesMax; n > zs::kLmStages; --n)
             if ((int64_t)n * zs::kLmStageBytes + rows_in_use * zs::kLmRowBytes <= (int64_t)zs::kLmRingBytes) {
@@ -1220,13 +1282,19 @@ zs_status lm_run(zs_context* h, const float* hidden, int64_t hidden_ld, const fl
     }
     {
         LaunchScope scope(h, 3, st);
-        const int grid = std::min(a.n_units, h->num_sms);
+        // one CTA per SM, or one CTA pair per two SMs (clusters of two)
+        const int grid = a.pair == 2 ? 2 * std::min(a.n_units, h->lm_pairs)
+                                     : std::min(a.n_units, h->num_sms);
         // One row tile streams the weights once: while the rmsnorm runs, each CTA
         // prefetches its first weight boxes, about 80 MB in all (within the L2).
         a.prefetch = a.mt == 1 ? (int)((80ll << 20) / zs::kLmTileBBytes / grid) : 0;
-        cudaLaunchAttribute attr[1];
+        cudaLaunchAttribute attr[2];
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
         attr[0].val.programmaticStreamSerializationAllowed = 1;
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = 2;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
         cudaLaunchConfig_t cfg;
         std::memset(&cfg, 0, sizeof(cfg));
         cfg.gridDim = dim3(grid);
@@ -1234,8 +1302,11 @@ zs_status lm_run(zs_context* h, const float* hidden, int64_t hidden_ld, const fl
         cfg.dynamicSmemBytes = zs::kLmSmemBytes;
         cfg.stream = st;
         cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        ZS_CUDA(cudaLaunchKernelEx(&cfg, zs::zs_lmhead_kernel, tm_a, tm_b, tm_c, a));
+        cfg.numAttrs = a.pair == 2 ? 2 : 1;
+        if (a.pair == 2)
+            ZS_CUDA(cudaLaunchKernelEx(&cfg, zs::zs_lmhead_kernel<2>, tm_a, tm_b, tm_c, a));
+        else
+            ZS_CUDA(cudaLaunchKernelEx(&cfg, zs::zs_lmhead_kernel<1>, tm_a, tm_b, tm_c, a));
     }
     return ZS_OK;
 }
@@ -1262,10 +1333,7 @@ zs_status zs_lmhead_logits(zs_handle h, const float* hidden, int64_t hidden_ld,
     a.E = n_embd;
     a.V = n_vocab;
     a.V_total = n_vocab;
-    a.mt = (batch + zs::kLmM - 1) / zs::kLmM;
-    a.nt = (n_vocab + zs::kLmN - 1) / zs::kLmN;
-    a.S = lm_slices(a.mt, a.nt, h->num_sms, 1024);
-    a.n_units = a.mt * a.S;
+    lm_geometry(h, a, batch, n_vocab, 1024);
     a.select = 0;
     a.out_logits = out_logits;
     a.logits_ld = logits_ld;
@@ -1329,12 +1397,10 @@ zs_status zs_lmhead_sample(zs_handle h, const float* hidden, int64_t hidden_ld,
     a.E = n_embd;
     a.V = n_vocab;
     a.V_total = n_vocab;
-    a.mt = (batch + zs::kLmM - 1) / zs::kLmM;
-    a.nt = (n_vocab + zs::kLmN - 1) / zs::kLmN;
+
     // a row's S blocks of up to max_ksel keys stay within the merge's one-pass gather
     const int s_cap = fused ? std::min(zs::kNC, (zs::kCandCap - zs::kCandMargin) / max_ksel) : 1024;
-    a.S = lm_slices(a.mt, a.nt, h->num_sms, s_cap);
-    a.n_units = a.mt * a.S;
+    lm_geometry(h, a, batch, n_vocab, s_cap);
     a.select = fused ? 1 : 0;
     a.shared = to_dev(params[0]);
     const zs::Params* dparams = nullptr;

@@ -340,6 +340,17 @@ class Sampler:
         _native.check(self._lib.zs_set_lmhead_route(self._h, self.LMHEAD_ROUTES[route]),
                       "zs_set_lmhead_route")
 
+    LMHEAD_TILES = {"auto": 0, "single": 1, "pair": 2}
+
+    def set_lmhead_tiles(self, mode: str) -> None:
+        """Tiles of the lm_head GEMM: "auto" (CTA pairs from 256 rows up), "single"
+        (one CTA per 128 x 128 tile) or "pair" (two CTAs of a cluster per 256 x 256
+        tile).  Same logits, ids and Rng states either way."""
+        if mode not in self.LMHEAD_TILES:
+            raise ValueError(f"mode must be one of {sorted(self.LMHEAD_TILES)}")
+        _native.check(self._lib.zs_set_lmhead_tiles(self._h, self.LMHEAD_TILES[mode]),
+                      "zs_set_lmhead_tiles")
+
     def set_timing(self, enable: bool) -> None:
         """Bracket every kernel of this sampler with CUDA events (measurement only)."""
         _native.check(self._lib.zs_set_timing(self._h, 1 if enable else 0), "zs_set_timing")
