@@ -110,11 +110,19 @@ def _keys(vals, ids):
         ~ids.astype(np.uint32)).astype(np.uint64)
 
 
-def _run_slices(vals, S, keff, cap, order_rng, reverse=False):
+def _slack(keff):
+    """lm_slack: keys an intermediate compaction may keep beyond keff."""
+    return min(keff // 4, max(0, 88 - keff))
+
+
+def _run_slices(vals, S, keff, cap, order_rng, reverse=False, slack=False):
     """Slices of one row processed in an interleaving drawn from order_rng (or, with
     `reverse`, each slice whole from the last to the first), chunk by chunk (32
     columns), with the buffer, compaction and shared bound of the epilogue; returns
-    the union of the slices' final blocks (keys)."""
+    the union of the slices' final blocks (keys).  With `slack` an intermediate
+    compaction keeps, like the radix walk that stops early, every key at or above
+    some key T whose rank lies anywhere in [keff, keff + lm_slack(keff)] (drawn from
+    order_rng) and takes T as its threshold; the final block is exact."""
     n = len(vals)
     bounds = [(s * n) // S for s in range(S + 1)]
     state = []
@@ -135,8 +143,11 @@ def _run_slices(vals, S, keff, cap, order_rng, reverse=False):
         else:
             pm = passes(v, st["tau"])
         if len(st["buf"]) + int(pm.sum()) > cap:
-            # lm_compact_row: keep the keff best, publish, take the higher threshold
-            buf = sorted(st["buf"], reverse=True)[:keff]
+            # lm_compact_row: keep the keff best (or the slack bucket), publish, take
+            # the higher threshold
+            r = int(order_rng.integers(0, _slack(keff) + 1)) if slack else 0
+            buf = sorted(st["buf"], reverse=True)
+            buf = buf[:min(len(buf), keff + r)]
             t = int(buf[-1] >> np.uint64(32))
             shared = max(shared, t)
             if not (not st["open"] and st["tau"] > t):
@@ -159,8 +170,9 @@ def _run_slices(vals, S, keff, cap, order_rng, reverse=False):
     return np.array(out, dtype=np.uint64)
 
 
+@pytest.mark.parametrize("slack", [False, True])
 @pytest.mark.parametrize("case", range(12))
-def test_shared_bound_keeps_the_top_keff(case):
+def test_shared_bound_keeps_the_top_keff(case, slack):
     """Rows with heavy ties (values from a few levels, so equal values sit in every
     slice), signed zeros, -inf and NaN; random interleavings of the slices."""
     rng = np.random.default_rng(100 + case)
@@ -176,16 +188,17 @@ def test_shared_bound_keeps_the_top_keff(case):
         vals[rng.integers(0, n, size=5)] = np.nan
     keff = int(rng.integers(1, 89))
     S = int(rng.integers(2, 10))
-    got = _run_slices(vals, S, keff, 120, rng)
+    got = _run_slices(vals, S, keff, 120, rng, slack=slack)
     allk = np.sort(_keys(vals, np.arange(n)))[::-1]
     want = allk[:keff]
     top = np.sort(got)[::-1][:keff]
     assert np.array_equal(top, want)
 
 
+@pytest.mark.parametrize("slack", [False, True])
 @pytest.mark.parametrize("keff", [1, 7, 50, 88])
 @pytest.mark.parametrize("top", [2.5, 0.0, -0.0, -np.inf])
-def test_shared_bound_ties_across_slices(keff, top):
+def test_shared_bound_ties_across_slices(keff, top, slack):
     """More than keff copies of the row's best value in every slice, the slices run
     from the last to the first: each publishes the tied value, and the earlier slices,
     whose copies have the smaller ids and so are the row's keff best, must still keep
@@ -198,6 +211,6 @@ def test_shared_bound_ties_across_slices(keff, top):
     for s in range(S):
         idx = s * per + rng.choice(per, size=keff + 40, replace=False)
         vals[idx] = np.float32(top)
-    got = _run_slices(vals, S, keff, 120, rng, reverse=True)
+    got = _run_slices(vals, S, keff, 120, rng, reverse=True, slack=slack)
     want = np.sort(_keys(vals, np.arange(n)))[::-1][:keff]
     assert np.array_equal(np.sort(got)[::-1][:keff], want)

@@ -357,8 +357,17 @@ __global__ void zs_lm_rmsnorm_kernel(const float* hidden, int64_t hld, const flo
     }
 }
 
-__device__ __forceinline__ uint64_t lm_keep(uint64_t* buf, uint32_t n, uint32_t kk, int lane) {
-    return warp_topk_keep<(kLmCap + 31) / 32>(buf, n, kk, lane);
+__device__ __forceinline__ uint64_t lm_keep(uint64_t* buf, uint32_t n, uint32_t kk, int lane,
+                                            uint32_t slack, uint32_t* kept) {
+    return warp_topk_keep<(kLmCap + 31) / 32>(buf, n, kk, lane, slack, kept);
+}
+
+// Keys an intermediate compaction may keep beyond keff: the radix walk stops once
+// its bucket is within this many keys of keff (a quarter of keff), which saves most
+// of its bits, while the kept keys still leave room for a whole 32-column chunk.
+__device__ __forceinline__ uint32_t lm_slack(uint32_t keff) {
+    const uint32_t room = keff < (uint32_t)kLmKeffMax ? (uint32_t)kLmKeffMax - keff : 0u;
+    return min(keff / 4u, room);
 }
 
 // Cuts row L's buffer (of this warp's 32 rows) back to its keff best keys; lane L
@@ -366,12 +375,15 @@ __device__ __forceinline__ uint64_t lm_keep(uint64_t* buf, uint32_t n, uint32_t 
 // already) and publishes the new one's value order for the row's other slices.
 __device__ __forceinline__ void lm_compact_row(uint64_t* rows, int L, uint32_t& count,
                                                uint32_t& tau_ord, float& tau_f, bool& open,
-                                               uint32_t keff, uint32_t* gtau, int lane) {
+                                               uint32_t keff, uint32_t* gtau, int lane,
+                                               bool exact) {
     const uint32_t n = __shfl_sync(kFull, count, L);
     const uint32_t kk = __shfl_sync(kFull, keff, L);
-    const uint64_t T = lm_keep(rows + (int64_t)L * kLmRowStride, n, kk, lane);
+    uint32_t kept = kk;
+    const uint64_t T = lm_keep(rows + (int64_t)L * kLmRowStride, n, kk, lane,
+                               exact ? 0u : lm_slack(kk), &kept);
     if (lane == L) {
-        count = kk;
+        count = kept;  // keff keys, or (not exact) the bucket of at most keff + slack
         uint32_t t = (uint32_t)(T >> 32);
         if (gtau) atomicMax(gtau, t);
         if (!open && tau_ord > t) t = tau_ord;
@@ -413,19 +425,26 @@ __device__ __forceinline__ uint32_t lm_pass_mask(const float (&v)[32], int col0,
     const uint32_t inside = (col0 + 32 <= V) ? 0xffffffffu
                                              : (col0 >= V ? 0u : ((1u << (V - col0)) - 1u));
     if (open) return inside;
-    uint32_t pm = 0;
+    // The mask is an OR tree (depth 4) over all 32 tests: the epilogue warps are one
+    // per scheduler, so nothing hides a dependent chain's latency.  No early test of
+    // the chunk's maximum: some row of the warp passes in most chunks (about k ln(n/k)
+    // appends per row are spread over the whole row), and then the warp runs the
+    // tests anyway.
+    uint32_t b[16];
     if (tau_ord != 0u) {
-        float mx = v[0];
 #pragma unroll
-        for (int j = 1; j < 32; ++j) mx = fmaxf(mx, v[j]);
-        if (!(mx > tau_f)) return 0u;  // fmaxf skips NaN; an all-NaN chunk gives NaN
-#pragma unroll
-        for (int j = 0; j < 32; ++j) pm |= (v[j] > tau_f ? 1u : 0u) << j;
+        for (int j = 0; j < 16; ++j)
+            b[j] = (v[j] > tau_f ? 1u << j : 0u) | (v[j + 16] > tau_f ? 1u << (j + 16) : 0u);
     } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) pm |= (v[j] == v[j] ? 1u : 0u) << j;
+        for (int j = 0; j < 16; ++j)
+            b[j] = (v[j] == v[j] ? 1u << j : 0u) | (v[j + 16] == v[j + 16] ? 1u << (j + 16) : 0u);
     }
-    return pm & inside;
+#pragma unroll
+    for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+        for (int j = 0; j < w; ++j) b[j] |= b[j + w];
+    return b[0] & inside;
 }
 
 // v[j] for a j known only at run time, by five levels of selects (the array stays
@@ -472,7 +491,7 @@ __device__ __forceinline__ void lm_chunk(const uint32_t (&r)[32], int col0, int 
     while (over) {
         const int L = __ffs(over) - 1;
         over &= over - 1;
-        lm_compact_row(rows, L, count, tau_ord, tau_f, open, keff, gtau, lane);
+        lm_compact_row(rows, L, count, tau_ord, tau_f, open, keff, gtau, lane, false);
         if (lane == L) pm = lm_pass_mask(v, col0, V, tau_ord, tau_f, open);
     }
     // Appends: while any row of the warp passes many columns (a buffer still open)
@@ -487,10 +506,19 @@ __device__ __forceinline__ void lm_chunk(const uint32_t (&r)[32], int col0, int 
                     mine[count++] = ((uint64_t)ord_of(v[j]) << 32) | (uint64_t)(~(uint32_t)(col0 + j));
         }
     } else {
+        // two columns per step: the two picks are independent, so their latencies
+        // overlap (the busiest row of the warp sets the number of steps)
         while (pm) {
-            const int j = __ffs(pm) - 1;
+            const int j1 = __ffs(pm) - 1;
             pm &= pm - 1u;
-            mine[count++] = ((uint64_t)ord_of(lm_pick(v, j)) << 32) | (uint64_t)(~(uint32_t)(col0 + j));
+            const bool two = pm != 0u;
+            const int j2 = two ? __ffs(pm) - 1 : j1;
+            pm &= pm - 1u;
+            const float x1 = lm_pick(v, j1), x2 = lm_pick(v, j2);
+            mine[count] = ((uint64_t)ord_of(x1) << 32) | (uint64_t)(~(uint32_t)(col0 + j1));
+            if (two)
+                mine[count + 1] = ((uint64_t)ord_of(x2) << 32) | (uint64_t)(~(uint32_t)(col0 + j2));
+            count += two ? 2u : 1u;
         }
     }
 }
@@ -736,12 +764,20 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                 const uint32_t base = lane_addr + acc * (uint32_t)G::kCols;
                 // the other slices' bound, read now and taken after this tile
                 const uint32_t g_seen = gtau ? lm_shared_bound(gtau) : 0u;
+                // The next chunk's TMEM load is in flight while this chunk is
+                // processed (rb is written asynchronously between its issue and the
+                // wait; nothing reads it there).
+                uint32_t rb[32];
+                __syncwarp();
+                tc_ld32_issue(base, rb);
 #pragma unroll 1
                 for (int c = 0; c < G::kCols / 32; ++c) {
                     uint32_t ra[32];
+                    tc_ld_wait(rb);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) ra[j] = rb[j];
                     __syncwarp();
-                    tc_ld32_issue(base + (uint32_t)(c * 32), ra);
-                    tc_ld_wait(ra);
+                    if (c + 1 < G::kCols / 32) tc_ld32_issue(base + (uint32_t)((c + 1) * 32), rb);
                     if (a.tma_out) {
                         // logits only: this warp's 32 rows x 32 columns go to a staging
                         // buffer in the (here unused) candidate area, in the 128-byte
@@ -795,7 +831,7 @@ __global__ void __launch_bounds__(kLmThreads, 1)
             while (over) {
                 const int L = __ffs(over) - 1;
                 over &= over - 1;
-                lm_compact_row(rows, L, count, tau_ord, tau_f, open, keff, gtau, lane);
+                lm_compact_row(rows, L, count, tau_ord, tau_f, open, keff, gtau, lane, true);
             }
             if (sel) {
                 uint8_t* blk = a.part + ((int64_t)row * a.S + s) * kLmPartStride;
