@@ -4,23 +4,25 @@
 //   xn     = rmsnorm(hidden, output_norm)          zs_lm_rmsnorm_kernel, bf16 out
 //   logits = xn . W^T   (W = output.weight [V][E])  zs_lmhead_kernel
 //
-// zs_lmhead_kernel is a persistent tcgen05 GEMM: D[128 rows][128 vocab] tiles
-// accumulate in tensor memory (four accumulators, all 512 columns, so the MMAs
-// run up to three tiles ahead of the epilogue, whose time per tile varies), operands arrive by TMA (2-D tiles, 128-byte
-// swizzle, no multicast) through a shared-memory ring of 3 to 5 stages (deeper
-// when the batch leaves candidate buffers unused).  Work units are
-// (row tile, vocabulary slice); a CTA walks its units' tiles in column order.
-// Warp 0 issues the copies, one thread of warp 1 issues the MMAs, warps 2-5 are
-// the epilogue: thread = row (its TMEM lane).  The epilogue keeps, per row, a
-// buffer of candidate keys (value desc, id asc is the sampler's key order) above a
-// threshold: the keff-th best key of the row's unit so far, as of the buffer's last
-// compaction.  Columns come in id order, so a column passes exactly when its value
-// order beats the threshold's; a 32-column chunk whose maximum does not is skipped
-// whole.  When a row's passing columns would overflow its buffer, the warp cuts
-// that row back to its keff best keys together (warp_topk_keep), which raises the
+// zs_lmhead_kernel is a persistent tcgen05 GEMM: D[128 rows][128 vocab] tiles per
+// CTA, or D[256][256] per CTA pair (cta_group::2, LmGeom), accumulate in tensor
+// memory (all 512 columns: four or two accumulators, so the MMAs run ahead of the
+// epilogue, whose time per tile varies); operands arrive by TMA (2-D tiles, 128-byte
+// swizzle, no multicast) through a shared-memory ring of 3 to 5 stages (deeper when
+// the batch leaves candidate buffers unused).  Work units are (row tile, vocabulary
+// slice); a CTA walks its units' tiles in column order.  Warp 0 issues the copies,
+// one thread of warp 1 issues the MMAs, warps 2-9 are the epilogue: two warps per
+// TMEM lane quarter, 16 rows (lanes) each, a row's 32-column chunk split over a lane
+// pair (16x64b TMEM loads), so each scheduler has two epilogue warps to switch
+// between.  The epilogue keeps, per row, a buffer of candidate keys (value desc, id
+// asc is the sampler's key order) above a threshold: about the keff-th best key of
+// the row's unit so far, as of the buffer's last compaction.  Columns come in id
+// order, so a column passes exactly when its value order beats the threshold's.
+// When a row's passing columns would overflow its buffer, the warp cuts that row
+// back to (about) its keff best keys together (warp_topk_keep), which raises the
 // threshold.  A row's slices also share a lower bound through global memory
-// (lm_shared_bound / lm_adopt).  At the end of a unit each row writes its keys
-// as one partial block, (row, slice), in the layout zs_merge_kernel and
+// (lm_shared_bound / lm_adopt).  At the end of a unit each row writes its exact top
+// keff as one partial block, (row, slice), in the layout zs_merge_kernel and
 // zs_warp_merge_kernel read, so the merge, f64 softmax, nucleus and draw are the
 // sampler's own.  Optionally the epilogue also writes the f32 logits.
 //
@@ -46,7 +48,11 @@ constexpr int kLmStagesMax = 5;   // with only 32 rows' buffers the ring takes t
 constexpr int kLmCap = 120;     // candidate keys buffered per row
 constexpr int kLmKeffMax = kLmCap - 32;  // a compaction leaves room for a whole chunk
 constexpr int kLmRowStride = kLmCap + 1; // odd, so rows spread over the banks
-constexpr int kLmThreads = 192; // warp 0 copies, warp 1 MMAs, warps 2-5 epilogue
+constexpr int kLmThreads = 320; // warp 0 copies, warp 1 MMAs, warps 2-9 epilogue
+constexpr int kLmEpiWarps = 8;  // two per TMEM lane quarter, 16 rows (lanes) each
+// Lanes of an epilogue warp that own a row (the other lane of each pair, lane ^ 2,
+// holds the row's other 16 columns of a chunk): lanes whose bit 1 is clear.
+constexpr unsigned kLmOwnerLanes = 0x33333333u;
 constexpr int kLmAccs = 4;  // accumulators in tensor memory (all 512 columns)
 constexpr int kLmTmemCols = kLmAccs * kLmN;
 constexpr uint32_t kLmTileABytes = kLmM * kLmBK * 2;
@@ -182,6 +188,23 @@ __device__ __forceinline__ void tc_ld_wait(uint32_t (&r)[32]) {
                  : "memory");
 }
 
+// 32 columns of 16 TMEM lanes (shape 16x64b, 16 repeats): lane t of the warp gets
+// lane 8 (t & 1) + (t >> 2) of the 16, columns ((t >> 1) & 1) + 2 j, j = 0..15.
+__device__ __forceinline__ void tc_ld16_issue(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile("tcgen05.ld.sync.aligned.16x64b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+                 : "r"(taddr)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_ld16_wait(uint32_t (&r)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+                 :
+                 : "memory");
+}
+__device__ __forceinline__ int lm_dp(int lane) { return 8 * (lane & 1) + (lane >> 2); }
+__device__ __forceinline__ int lm_par(int lane) { return (lane >> 1) & 1; }
+
 // Shared-memory matrix descriptor of a K-major tile written by TMA with 128-byte
 // swizzle: rows of 128 bytes, 8-row groups 1024 bytes apart (stride byte offset),
 // leading byte offset unused for this layout (1), descriptor version 1, layout
@@ -213,9 +236,10 @@ struct LmGeom {
     static constexpr int kCols = kLmN * P;        // vocabulary columns per tile
     static constexpr int kAccs = 512 / kCols;     // accumulators: all 512 TMEM columns
     static constexpr uint32_t kIdesc = lm_idesc(kRows, kCols);
-    // epilogue arrivals that free an accumulator: every thread of the four epilogue
-    // warps (P = 1), or one lane per epilogue warp of both CTAs, on the leader (P = 2)
-    static constexpr uint32_t kAccEmptyCount = P == 1 ? 4 * 32 : 2 * 4;
+    // epilogue arrivals that free an accumulator: every thread of the epilogue warps
+    // (P = 1), or one lane per epilogue warp of both CTAs, on the leader (P = 2)
+    static constexpr uint32_t kAccEmptyCount =
+        P == 1 ? kLmEpiWarps * 32 : 2 * kLmEpiWarps;
 };
 static_assert(LmGeom<1>::kAccs <= kLmAccs && LmGeom<2>::kAccs <= kLmAccs, "barrier arrays");
 
@@ -370,9 +394,11 @@ __device__ __forceinline__ uint32_t lm_slack(uint32_t keff) {
     return min(keff / 4u, room);
 }
 
-// Cuts row L's buffer (of this warp's 32 rows) back to its keff best keys; lane L
-// takes the new count and threshold (the higher of the new one and one it holds
-// already) and publishes the new one's value order for the row's other slices.
+// Cuts one row's buffer (row lm_dp(L) of this warp's 16, L an owner lane) back to
+// its keff best keys (exact) or to the radix walk's bucket of at most keff +
+// lm_slack(keff) keys; lanes L and L ^ 2 take the new count and threshold (the
+// higher of the new one and one they hold already), and L publishes its value order
+// for the row's other slices.
 __device__ __forceinline__ void lm_compact_row(uint64_t* rows, int L, uint32_t& count,
                                                uint32_t& tau_ord, float& tau_f, bool& open,
                                                uint32_t keff, uint32_t* gtau, int lane,
@@ -380,12 +406,12 @@ __device__ __forceinline__ void lm_compact_row(uint64_t* rows, int L, uint32_t& 
     const uint32_t n = __shfl_sync(kFull, count, L);
     const uint32_t kk = __shfl_sync(kFull, keff, L);
     uint32_t kept = kk;
-    const uint64_t T = lm_keep(rows + (int64_t)L * kLmRowStride, n, kk, lane,
+    const uint64_t T = lm_keep(rows + (int64_t)lm_dp(L) * kLmRowStride, n, kk, lane,
                                exact ? 0u : lm_slack(kk), &kept);
-    if (lane == L) {
+    if ((lane & ~2) == L) {
         count = kept;  // keff keys, or (not exact) the bucket of at most keff + slack
         uint32_t t = (uint32_t)(T >> 32);
-        if (gtau) atomicMax(gtau, t);
+        if (gtau && lane == L) atomicMax(gtau, t);
         if (!open && tau_ord > t) t = tau_ord;
         tau_ord = t;
         tau_f = value_of_ord(t);
@@ -416,45 +442,41 @@ __device__ __forceinline__ void lm_adopt(uint32_t g, uint32_t& tau_ord, float& t
     }
 }
 
-// Bit j set when column col0 + j (< V) passes: every column while the buffer is
-// open (no threshold yet), else a value order above tau_ord.  With tau_f the
-// threshold's value that is v > tau_f (orders are monotone in the value, -0 and
-// +0 share one), or for a NaN threshold (order 0) any non-NaN value.
-__device__ __forceinline__ uint32_t lm_pass_mask(const float (&v)[32], int col0, int V,
+// Bit j set when this lane's column col0 + par + 2 j (< V) passes: every column
+// while the buffer is open (no threshold yet), else a value order above tau_ord.
+// With tau_f the threshold's value that is v > tau_f (orders are monotone in the
+// value, -0 and +0 share one), or for a NaN threshold (order 0) any non-NaN value.
+__device__ __forceinline__ uint32_t lm_pass_mask(const float (&v)[16], int col0, int par, int V,
                                                  uint32_t tau_ord, float tau_f, bool open) {
-    const uint32_t inside = (col0 + 32 <= V) ? 0xffffffffu
-                                             : (col0 >= V ? 0u : ((1u << (V - col0)) - 1u));
+    const int lim = V - col0 - par;  // column j of this lane lies in the row while 2 j < lim
+    const uint32_t inside = lim >= 32 ? 0xffffu : (lim <= 0 ? 0u : (1u << ((lim + 1) >> 1)) - 1u);
     if (open) return inside;
-    // The mask is an OR tree (depth 4) over all 32 tests: the epilogue warps are one
-    // per scheduler, so nothing hides a dependent chain's latency.  No early test of
-    // the chunk's maximum: some row of the warp passes in most chunks (about k ln(n/k)
-    // appends per row are spread over the whole row), and then the warp runs the
-    // tests anyway.
-    uint32_t b[16];
+    // an OR tree (depth 3) over all 16 tests: nothing hides a dependent chain's
+    // latency, and some row of the warp passes in most chunks, so there is no early
+    // test of the chunk's maximum
+    uint32_t b[8];
     if (tau_ord != 0u) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-            b[j] = (v[j] > tau_f ? 1u << j : 0u) | (v[j + 16] > tau_f ? 1u << (j + 16) : 0u);
+        for (int j = 0; j < 8; ++j)
+            b[j] = (v[j] > tau_f ? 1u << j : 0u) | (v[j + 8] > tau_f ? 1u << (j + 8) : 0u);
     } else {
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-            b[j] = (v[j] == v[j] ? 1u << j : 0u) | (v[j + 16] == v[j + 16] ? 1u << (j + 16) : 0u);
+        for (int j = 0; j < 8; ++j)
+            b[j] = (v[j] == v[j] ? 1u << j : 0u) | (v[j + 8] == v[j + 8] ? 1u << (j + 8) : 0u);
     }
 #pragma unroll
-    for (int w = 8; w >= 1; w >>= 1)
+    for (int w = 4; w >= 1; w >>= 1)
 #pragma unroll
         for (int j = 0; j < w; ++j) b[j] |= b[j + w];
     return b[0] & inside;
 }
 
-// v[j] for a j known only at run time, by five levels of selects (the array stays
+// v[j] for a j known only at run time, by four levels of selects (the array stays
 // in registers; an indexed load would put it in local memory).
-__device__ __forceinline__ float lm_pick(const float (&v)[32], int j) {
-    float x16[16], x8[8], x4[4], x2[2];
+__device__ __forceinline__ float lm_pick(const float (&v)[16], int j) {
+    float x8[8], x4[4], x2[2];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) x16[i] = (j & 16) ? v[i + 16] : v[i];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) x8[i] = (j & 8) ? x16[i + 8] : x16[i];
+    for (int i = 0; i < 8; ++i) x8[i] = (j & 8) ? v[i + 8] : v[i];
 #pragma unroll
     for (int i = 0; i < 4; ++i) x4[i] = (j & 4) ? x8[i + 4] : x8[i];
 #pragma unroll
@@ -462,52 +484,57 @@ __device__ __forceinline__ float lm_pick(const float (&v)[32], int j) {
     return (j & 1) ? x2[1] : x2[0];
 }
 
-// One 32-column chunk of a tile for this warp's 32 rows: rows whose passing
-// columns would overflow their buffers are compacted first (the whole warp, one row
-// at a time), then every row appends its passing keys.
-__device__ __forceinline__ void lm_chunk(const uint32_t (&r)[32], int col0, int V, bool sel,
-                                         float* lrow, bool& x0nan, bool select, uint64_t* rows,
-                                         uint64_t* mine, uint32_t& count, uint32_t& tau_ord,
-                                         float& tau_f, bool& open, uint32_t keff, uint32_t* gtau,
-                                         int lane) {
-    float v[32];
+__device__ __forceinline__ uint64_t lm_key(float x, int col) {
+    return ((uint64_t)ord_of(x) << 32) | (uint64_t)(~(uint32_t)col);
+}
+
+// One 32-column chunk of a tile for this warp's 16 rows, each row split over a lane
+// pair (L, L ^ 2: 16 columns each, interleaved).  Rows whose passing columns would
+// overflow their buffers are compacted first (the whole warp, one row at a time),
+// then both lanes of every row append their passing keys, the lane with the odd
+// columns behind the other's; both keep the row's count.
+__device__ __forceinline__ void lm_chunk(const uint32_t (&r)[16], int col0, int par, int V,
+                                         bool sel, float* lrow, bool& x0nan, bool select,
+                                         uint64_t* rows, uint64_t* mine, uint32_t& count,
+                                         uint32_t& tau_ord, float& tau_f, bool& open,
+                                         uint32_t keff, uint32_t* gtau, int lane) {
+    float v[16];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-    if (col0 == 0) x0nan = (v[0] != v[0]);
+    for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+    if (col0 == 0 && par == 0) x0nan = (v[0] != v[0]);
     if (lrow) {
-        if (col0 + 32 <= V) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<float4*>(lrow + col0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-        } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-                if (col0 + j < V) lrow[col0 + j] = v[j];
-        }
+        for (int j = 0; j < 16; ++j)
+            if (col0 + par + 2 * j < V) lrow[col0 + par + 2 * j] = v[j];
     }
     if (!select) return;
-    uint32_t pm = sel ? lm_pass_mask(v, col0, V, tau_ord, tau_f, open) : 0u;
-    unsigned over = __ballot_sync(kFull, count + __popc(pm) > (uint32_t)kLmCap);
-    while (over) {
-        const int L = __ffs(over) - 1;
-        over &= over - 1;
-        lm_compact_row(rows, L, count, tau_ord, tau_f, open, keff, gtau, lane, false);
-        if (lane == L) pm = lm_pass_mask(v, col0, V, tau_ord, tau_f, open);
+    uint32_t pm = sel ? lm_pass_mask(v, col0, par, V, tau_ord, tau_f, open) : 0u;
+    {
+        const uint32_t pc = __popc(pm);
+        const uint32_t tot = pc + __shfl_xor_sync(kFull, pc, 2);
+        unsigned over = __ballot_sync(kFull, count + tot > (uint32_t)kLmCap) & kLmOwnerLanes;
+        while (over) {
+            const int L = __ffs(over) - 1;
+            over &= over - 1;
+            lm_compact_row(rows, L, count, tau_ord, tau_f, open, keff, gtau, lane, false);
+            if ((lane & ~2) == L) pm = lm_pass_mask(v, col0, par, V, tau_ord, tau_f, open);
+        }
     }
-    // Appends: while any row of the warp passes many columns (a buffer still open)
-    // one predicated step per column; otherwise a loop over each row's passing
-    // columns, as many steps as the busiest row has, each picking its value out of
-    // the registers by a select tree.
-    if (__any_sync(kFull, __popc(pm) > 16)) {
+    const uint32_t pc = __popc(pm);
+    const uint32_t pp = __shfl_xor_sync(kFull, pc, 2);
+    uint32_t at = count + (par ? pp : 0u);
+    count += pc + pp;
+    const int cb = col0 + par;  // column of v[j]: cb + 2 j
+    // Appends: while any lane passes many columns (a buffer still open) one
+    // predicated step per column; otherwise a loop over each lane's passing columns,
+    // two per step (the two picks are independent, so their latencies overlap).
+    if (__any_sync(kFull, pc > 8u)) {
         if (pm) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-                if ((pm >> j) & 1u)
-                    mine[count++] = ((uint64_t)ord_of(v[j]) << 32) | (uint64_t)(~(uint32_t)(col0 + j));
+            for (int j = 0; j < 16; ++j)
+                if ((pm >> j) & 1u) mine[at++] = lm_key(v[j], cb + 2 * j);
         }
     } else {
-        // two columns per step: the two picks are independent, so their latencies
-        // overlap (the busiest row of the warp sets the number of steps)
         while (pm) {
             const int j1 = __ffs(pm) - 1;
             pm &= pm - 1u;
@@ -515,10 +542,9 @@ __device__ __forceinline__ void lm_chunk(const uint32_t (&r)[32], int col0, int 
             const int j2 = two ? __ffs(pm) - 1 : j1;
             pm &= pm - 1u;
             const float x1 = lm_pick(v, j1), x2 = lm_pick(v, j2);
-            mine[count] = ((uint64_t)ord_of(x1) << 32) | (uint64_t)(~(uint32_t)(col0 + j1));
-            if (two)
-                mine[count + 1] = ((uint64_t)ord_of(x2) << 32) | (uint64_t)(~(uint32_t)(col0 + j2));
-            count += two ? 2u : 1u;
+            mine[at] = lm_key(x1, cb + 2 * j1);
+            if (two) mine[at + 1] = lm_key(x2, cb + 2 * j2);
+            at += two ? 2u : 1u;
         }
     }
 }
@@ -715,17 +741,21 @@ __global__ void __launch_bounds__(kLmThreads, 1)
         }
         __syncwarp();
     } else {
-        // ---- epilogue: thread = row of the tile (its TMEM lane) ----
-        const int q = warp & 3;  // the lane quarter this warp may access
-        const int r_in = q * 32 + lane;
+        // ---- epilogue: 8 warps, two per TMEM lane quarter, each 16 rows of the
+        // tile (TMEM lanes); a row's 32-column chunk is split over a lane pair ----
+        const int ew = warp - 2;
+        const int g16 = (warp & 3) * 32 + (ew >> 2) * 16;  // first row (lane) of this warp
+        const int dp = lm_dp(lane), par = lm_par(lane);
+        const bool owner = par == 0;
+        const int r_in = g16 + dp;
         // rows at or beyond the batch never touch their buffers (the host sized
         // the ring so that the buffers of the rows in use fit behind it)
-        uint64_t* rows = cand + (int64_t)(q * 32) * kLmRowStride;
-        uint64_t* mine = rows + (int64_t)lane * kLmRowStride;
-        const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
+        uint64_t* rows = cand + (int64_t)g16 * kLmRowStride;
+        uint64_t* mine = rows + (int64_t)dp * kLmRowStride;
+        const uint32_t lane_addr = tmem + ((uint32_t)g16 << 16);
         uint32_t acc = 0, acc_phase = 0;
         bool ok = true;
-        uint32_t count = 0;    // keys in the buffer
+        uint32_t count = 0;    // keys in the row's buffer (both lanes of the pair)
         uint32_t tau_ord = 0;  // threshold's value order (after the first compaction)
         float tau_f = 0.0f;    // its value
         bool open = true;      // no threshold yet: every column enters
@@ -762,46 +792,51 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                 tc_fence_after();
                 const int tcol = t * G::kCols;
                 const uint32_t base = lane_addr + acc * (uint32_t)G::kCols;
-                // the other slices' bound, read now and taken after this tile
-                const uint32_t g_seen = gtau ? lm_shared_bound(gtau) : 0u;
+                // the other slices' bound, read now and taken after this tile (the
+                // owner's reading, so both lanes of a row keep one threshold)
+                uint32_t g_seen = (gtau && owner) ? lm_shared_bound(gtau) : 0u;
+                g_seen = __shfl_sync(kFull, g_seen, lane & ~2);
                 // The next chunk's TMEM load is in flight while this chunk is
                 // processed (rb is written asynchronously between its issue and the
                 // wait; nothing reads it there).
-                uint32_t rb[32];
+                uint32_t rb[16];
                 __syncwarp();
-                tc_ld32_issue(base, rb);
+                tc_ld16_issue(base, rb);
 #pragma unroll 1
                 for (int c = 0; c < G::kCols / 32; ++c) {
-                    uint32_t ra[32];
-                    tc_ld_wait(rb);
+                    uint32_t ra[16];
+                    tc_ld16_wait(rb);
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) ra[j] = rb[j];
+                    for (int j = 0; j < 16; ++j) ra[j] = rb[j];
                     __syncwarp();
-                    if (c + 1 < G::kCols / 32) tc_ld32_issue(base + (uint32_t)((c + 1) * 32), rb);
+                    if (c + 1 < G::kCols / 32) tc_ld16_issue(base + (uint32_t)((c + 1) * 32), rb);
                     if (a.tma_out) {
-                        // logits only: this warp's 32 rows x 32 columns go to a staging
+                        // logits only: this warp's 16 rows x 32 columns go to a staging
                         // buffer in the (here unused) candidate area, in the 128-byte
-                        // swizzled layout of the output tensor map, then one TMA store
-                        uint8_t* stg = reinterpret_cast<uint8_t*>(cand) + (q * 2 + stg_buf) * 4096;
+                        // swizzled layout of the output tensor map (rows of 128 bytes,
+                        // 16-byte unit u of row i at u ^ (i & 7)), then one TMA store
+                        uint8_t* stg = reinterpret_cast<uint8_t*>(cand) + (ew * 2 + stg_buf) * 2048;
                         if (lane == 0) bulk_wait_read_1();  // the store two chunks ago read it
                         __syncwarp();
-                        uint8_t* my = stg + lane * 128;
+                        uint8_t* my = stg + dp * 128;
 #pragma unroll
-                        for (int j = 0; j < 8; ++j)
-                            *reinterpret_cast<uint4*>(my + ((j ^ (lane & 7)) << 4)) =
-                                make_uint4(ra[4 * j], ra[4 * j + 1], ra[4 * j + 2], ra[4 * j + 3]);
+                        for (int j = 0; j < 16; ++j) {
+                            const int col = par + 2 * j;
+                            *reinterpret_cast<uint32_t*>(my + ((((col >> 2) ^ (dp & 7)) << 4) |
+                                                               ((col & 3) << 2))) = ra[j];
+                        }
                         fence_proxy_async_smem();
                         __syncwarp();
                         if (lane == 0) {
                             tma_store_2d(&tm_c, stg, tcol + c * 32,
-                                         m * G::kRows + (int)rank * kLmM + q * 32);
+                                         m * G::kRows + (int)rank * kLmM + g16);
                             bulk_commit_group();
                         }
                         stg_buf ^= 1;
                         continue;
                     }
-                    lm_chunk(ra, tcol + c * 32, a.V, sel, lrow, x0nan, a.select, rows, mine, count,
-                             tau_ord, tau_f, open, keff, gtau, lane);
+                    lm_chunk(ra, tcol + c * 32, par, a.V, sel, lrow, x0nan, a.select, rows, mine,
+                             count, tau_ord, tau_f, open, keff, gtau, lane);
                 }
                 if (gtau) lm_adopt(g_seen, tau_ord, tau_f, open);
                 tc_fence_before();
@@ -822,18 +857,18 @@ __global__ void __launch_bounds__(kLmThreads, 1)
             // block stays empty and the buffer carries over.
             const bool run_on = (u + 1 < u_end) && (s + 1 < a.S);
             if (run_on) {
-                if (sel)
+                if (sel && owner)
                     *reinterpret_cast<uint4*>(a.part + ((int64_t)row * a.S + s) * kLmPartStride) =
                         make_uint4(0u, 0u, __float_as_uint(-INFINITY), 0u);
                 continue;
             }
-            unsigned over = __ballot_sync(kFull, sel && count > keff);
+            unsigned over = __ballot_sync(kFull, sel && count > keff) & kLmOwnerLanes;
             while (over) {
                 const int L = __ffs(over) - 1;
                 over &= over - 1;
                 lm_compact_row(rows, L, count, tau_ord, tau_f, open, keff, gtau, lane, true);
             }
-            if (sel) {
+            if (sel && owner) {  // the owner lane holds column 0's NaN flag
                 uint8_t* blk = a.part + ((int64_t)row * a.S + s) * kLmPartStride;
                 const uint32_t flags = has0 ? (kPartHasId0 | (x0nan ? kPartX0Nan : 0u)) : 0u;
                 *reinterpret_cast<uint4*>(blk) = make_uint4(count, flags, __float_as_uint(-INFINITY), 0u);

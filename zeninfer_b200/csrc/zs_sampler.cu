@@ -1156,7 +1156,7 @@ zs_status lm_tensor_map(zs_context* h, CUtensorMap* map, const void* base, int64
     const int64_t esize = f32 ? 4 : 2;
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)(ld > 0 ? ld : cols) * esize};
-    const cuuint32_t box[2] = {f32 ? 32u : (cuuint32_t)zs::kLmBK, f32 ? 32u : (cuuint32_t)zs::kLmM};
+    const cuuint32_t box[2] = {f32 ? 32u : (cuuint32_t)zs::kLmBK, f32 ? 16u : (cuuint32_t)zs::kLmM};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = h->encode_tiled(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                                        2, const_cast<void*>(base),
