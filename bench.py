@@ -248,7 +248,7 @@ def lmhead_bench(s, dev, stream, hbm_peak):
         tf_peak, tf_kind = 1590.0, "fallback"
     out = {"weights": "bf16 [151936][896], seeded N(0, 0.05^2)", "hidden": "N(0, 3^2) f32",
            "params": "temp 0.7, top-k 50, top-p 0.9"}
-    for B in (4096, 1024, 1):
+    for B in (4096, 2048, 1024, 512, 256, 1):
         h = torch.randn(B, E, device=dev, generator=g) * 3
         st = states_to_tensor([i + 1 for i in range(B)], dev)
         ids = torch.empty(B, dtype=torch.int32, device=dev)
@@ -270,7 +270,7 @@ def lmhead_bench(s, dev, stream, hbm_peak):
         kt = s.get_timing()
         s.set_timing(False)
         # the other tiling (one-CTA tiles where the default pairs CTAs, and back)
-        other = "single" if B >= 256 else "pair"
+        other = "single" if B >= 512 else "pair"
         s.set_lmhead_tiles(other)
         for _ in range(3):
             fused()
@@ -306,7 +306,7 @@ def lmhead_bench(s, dev, stream, hbm_peak):
         wbytes = V * E * 2 + B * E * 2
         r = {"default_route_us_per_call": ms_auto * 1e3,
              "default_route": "two_pass" if B <= 1024 else "fused",
-             "tiles": "cta_pair_256x256" if B >= 256 else "cta_128x128",
+             "tiles": "cta_pair_256x256" if B >= 512 else "cta_128x128",
              "us_per_call": ms * 1e3, "rows_per_s": B / (ms / 1e3),
              "kernel_us": k_ms * 1e3,
              "other_tiles": {"tiles": other, "us_per_call": ms_other * 1e3,

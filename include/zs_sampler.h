@@ -233,7 +233,7 @@ zs_status zs_set_lmhead_route(zs_handle h, int32_t route);
 
 /* The tiles of the lm_head GEMM (zs_lmhead_sample, zs_lmhead_logits), for this
  * handle.  No counterpart in the reference.
- *   ZS_LMHEAD_TILES_AUTO    (default) CTA pairs from 256 rows up, one CTA below
+ *   ZS_LMHEAD_TILES_AUTO    (default) CTA pairs from 512 rows up, one CTA below
  *   ZS_LMHEAD_TILES_SINGLE  one CTA per 128-row x 128-column tile
  *   ZS_LMHEAD_TILES_PAIR    two CTAs (a cluster of two SMs) per 256 x 256 tile
  *                           whenever the device can hold them

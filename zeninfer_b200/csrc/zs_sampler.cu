@@ -1172,12 +1172,14 @@ zs_status lm_tensor_map(zs_context* h, CUtensorMap* map, const void* base, int64
 // slices (at most `cap`) whose busiest CTA has at most 2% more tiles than the best
 // split.
 // Tiles of one CTA (128 rows x 128 columns) or of a CTA pair (256 x 256): pairs
-// halve the operand traffic per product, so they are the default from 256 rows up,
-// where both halves of a pair's rows are in use (zs_set_lmhead_tiles overrides).
+// halve the operand traffic per product, so they are the default from 512 rows up
+// (measured on B200, fused route, 151,936 x 896: 289 against 292 us at 512 rows,
+// 226 against 208 us at 256, where one pair tile holds all rows and the epilogue
+// sets the pace); zs_set_lmhead_tiles overrides.
 int lm_pair_for(const zs_context* h, int batch) {
     if (h->lm_pairs <= 0 || h->lm_tiles == ZS_LMHEAD_TILES_SINGLE) return 1;
     if (h->lm_tiles == ZS_LMHEAD_TILES_PAIR) return 2;
-    return batch >= 2 * zs::kLmM ? 2 : 1;
+    return batch >= 4 * zs::kLmM ? 2 : 1;
 }
 
 int lm_slices(int mt, int nt, int ctas, int cap);

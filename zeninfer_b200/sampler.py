@@ -343,7 +343,7 @@ class Sampler:
     LMHEAD_TILES = {"auto": 0, "single": 1, "pair": 2}
 
     def set_lmhead_tiles(self, mode: str) -> None:
-        """Tiles of the lm_head GEMM: "auto" (CTA pairs from 256 rows up), "single"
+        """Tiles of the lm_head GEMM: "auto" (CTA pairs from 512 rows up), "single"
         (one CTA per 128 x 128 tile) or "pair" (two CTAs of a cluster per 256 x 256
         tile).  Same logits, ids and Rng states either way."""
         if mode not in self.LMHEAD_TILES:
