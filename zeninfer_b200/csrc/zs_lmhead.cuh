@@ -236,10 +236,9 @@ struct LmGeom {
     static constexpr int kCols = kLmN * P;        // vocabulary columns per tile
     static constexpr int kAccs = 512 / kCols;     // accumulators: all 512 TMEM columns
     static constexpr uint32_t kIdesc = lm_idesc(kRows, kCols);
-    // epilogue arrivals that free an accumulator: every thread of the epilogue warps
-    // (P = 1), or one lane per epilogue warp of both CTAs, on the leader (P = 2)
-    static constexpr uint32_t kAccEmptyCount =
-        P == 1 ? kLmEpiWarps * 32 : 2 * kLmEpiWarps;
+    // epilogue arrivals that free an accumulator: one lane per epilogue warp (P = 1),
+    // of both CTAs on the leader's barrier (P = 2)
+    static constexpr uint32_t kAccEmptyCount = P * kLmEpiWarps;
 };
 static_assert(LmGeom<1>::kAccs <= kLmAccs && LmGeom<2>::kAccs <= kLmAccs, "barrier arrays");
 
@@ -262,9 +261,11 @@ __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
                      : "memory");
 }
+// Arrives on a barrier of either CTA of the pair (default release at CTA scope: the
+// accumulator it frees is ordered by tcgen05.wait::ld and the before_thread_sync
+// fence, not by memory ordering).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster)
-                 : "memory");
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
 }
 // A 2-D tile into this CTA's shared memory whose bytes count on the barrier of the
 // pair's leader (bar_cluster: a shared::cluster address), no multicast.
@@ -840,11 +841,12 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                 }
                 if (gtau) lm_adopt(g_seen, tau_ord, tau_f, open);
                 tc_fence_before();
-                if (P == 1) {
-                    mbar_arrive(&sm.acc_empty[acc]);
-                } else {
-                    __syncwarp();  // the warp's TMEM loads have all completed
-                    if (lane == 0) mbar_arrive_cluster(smem_in_cta(&sm.acc_empty[acc], 0u));
+                __syncwarp();  // the warp's TMEM loads have all completed
+                if (lane == 0) {
+                    if (P == 1)
+                        mbar_arrive(&sm.acc_empty[acc]);
+                    else
+                        mbar_arrive_cluster(smem_in_cta(&sm.acc_empty[acc], 0u));
                 }
                 if (++acc == G::kAccs) {
                     acc = 0;
