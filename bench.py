@@ -305,7 +305,7 @@ def lmhead_bench(s, dev, stream, hbm_peak):
         flops = 2.0 * B * E * V
         wbytes = V * E * 2 + B * E * 2
         r = {"default_route_us_per_call": ms_auto * 1e3,
-             "default_route": "two_pass" if B <= 1024 else "fused",
+             "default_route": "exact" if B <= 4 else ("two_pass" if B <= 1024 else "fused"),
              "tiles": "cta_pair_256x256" if B >= 512 else "cta_128x128",
              "us_per_call": ms * 1e3, "rows_per_s": B / (ms / 1e3),
              "kernel_us": k_ms * 1e3,
@@ -365,6 +365,28 @@ def lmhead_bench(s, dev, stream, hbm_peak):
             finally:
                 s.set_lmhead_route("auto")
             out["parity_vs_reference_f32"] = cmp
+            # The exact route (the default up to 4 rows): logits against the
+            # reference's f32 lm_head bit for bit, ids against its sample_token.
+            ne = 4
+            he = hc[:ne]
+            ex = {"rows": ne, "precision": "exact route: f32 xn, f32 fused multiply-adds in "
+                                           "the reference's AVX2 summation order"}
+            s.set_lmhead_route("exact")
+            try:
+                lg_dev = s.lmhead_logits(he.to(dev), nw, W, eps=1e-6, stream=stream)
+                st_e = states_to_tensor([i + 1 for i in range(ne)], dev)
+                got = s.lmhead_sample(he.to(dev), nw, W, p, st_e, stream=stream)
+                torch.cuda.synchronize()
+                _, lg = oracle.reference_lmhead(he.numpy(), nw.cpu().numpy(), 1e-6, wf, impl=1,
+                                                nthreads=nth)
+                ref, _ = oracle.reference_sample(lg, p, np.arange(1, ne + 1, dtype=np.uint64),
+                                                 nthreads=nth)
+                mism = lg_dev.cpu().numpy().view(np.uint32) != lg.view(np.uint32)
+                ex["logit_bit_mismatch_vs_reference_f32"] = int(mism.sum())
+                ex["sampled_id_mismatch_vs_reference_f32"] = int((got.cpu().numpy() != ref).sum())
+            finally:
+                s.set_lmhead_route("auto")
+            out["exact_route_vs_reference_f32"] = ex
     except Exception as e:  # reported, never fatal
         out["cpu_reference"] = {"note": str(e)}
     del W

@@ -217,18 +217,26 @@ typedef struct zs_timing {
 zs_status zs_set_timing(zs_handle h, int32_t enable);
 zs_status zs_get_timing(zs_handle h, zs_timing* out);
 
-/* How zs_lmhead_sample takes the shortlist, for this handle.  No counterpart in the
- * reference (its lm_head and sampler are separate CPU calls).
- *   ZS_LMHEAD_ROUTE_AUTO      (default) two passes up to 1024 rows, fused above, the
- *                             faster of the two on B200 at each size
+/* How zs_lmhead_sample takes the shortlist (and zs_lmhead_logits computes its
+ * logits), for this handle.  No counterpart in the reference (its lm_head and sampler
+ * are separate CPU calls).
+ *   ZS_LMHEAD_ROUTE_AUTO      (default) exact up to 4 rows (hidden size up to 2048),
+ *                             two passes up to 1024 rows, fused above
  *   ZS_LMHEAD_ROUTE_FUSED     in the GEMM's epilogue whenever the rows allow it (no
  *                             logits buffer: for callers that cannot spare one)
- *   ZS_LMHEAD_ROUTE_TWO_PASS  always write logits, then zs_sample
- * Both routes give the same ids and Rng states.  The two-pass route writes the logits
- * to out_logits when given, else to handle scratch of batch x n_vocab floats. */
+ *   ZS_LMHEAD_ROUTE_TWO_PASS  always write tensor-core logits, then zs_sample
+ *   ZS_LMHEAD_ROUTE_EXACT     f32 logits bit-exact with the reference's default lm_head
+ *                             (src/model.cpp:401-403 with src/kernels.cpp:52-78: f32
+ *                             xn, its AVX2 summation order), then zs_sample; up to 4
+ *                             rows and hidden sizes up to 2048, else
+ *                             ZS_ERR_INVALID_ARGUMENT
+ * The tensor-core routes (fused, two passes) round xn to bf16 and give the same ids
+ * and Rng states as each other.  The routes that write logits write them to out_logits
+ * when given, else to handle scratch of batch x n_vocab floats. */
 #define ZS_LMHEAD_ROUTE_AUTO 0
 #define ZS_LMHEAD_ROUTE_FUSED 1
 #define ZS_LMHEAD_ROUTE_TWO_PASS 2
+#define ZS_LMHEAD_ROUTE_EXACT 3
 zs_status zs_set_lmhead_route(zs_handle h, int32_t route);
 
 /* The tiles of the lm_head GEMM (zs_lmhead_sample, zs_lmhead_logits), for this

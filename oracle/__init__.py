@@ -72,6 +72,9 @@ def olib():
         L.zo_lmhead_rows.argtypes = [vp, C.c_int64, C.c_int, C.c_int, vp, C.c_float, vp, C.c_int,
                                      vp, vp, C.c_int64, C.c_int]
         L.zo_lmhead_rows.restype = C.c_int
+        L.zo_lmhead_f32_rows.argtypes = [vp, C.c_int64, C.c_int, C.c_int, vp, C.c_float, vp,
+                                         C.c_int, vp, vp, C.c_int64]
+        L.zo_lmhead_f32_rows.restype = C.c_int
         _olib = L
     return _olib
 
@@ -194,6 +197,24 @@ def oracle_lmhead(hidden: np.ndarray, norm_w: np.ndarray, eps: float, w_bf16: np
     nthreads = nthreads or min(64, os.cpu_count() or 1)
     olib().zo_lmhead_rows(h.ctypes.data, E, B, E, nw.ctypes.data, float(eps), w.ctypes.data, V,
                           xn.ctypes.data, logits.ctypes.data, V, nthreads)
+    return xn, logits
+
+
+def oracle_lmhead_f32(hidden: np.ndarray, norm_w: np.ndarray, eps: float, w_bf16: np.ndarray):
+    """The lm_head as the reference computes it by default (src/model.cpp:401-403 with
+    src/kernels.cpp:52-78): rmsnorm to f32, then the AVX2 dot product's summation
+    order (32 fused multiply-add accumulators, its reduction tree, the tail in
+    double) over the bfloat16 weights (w_bf16: uint16 [V, E] bit patterns).  Returns
+    (xn float32 [B, E], logits float32 [B, V])."""
+    h = np.ascontiguousarray(hidden, dtype=np.float32)
+    B, E = h.shape
+    w = np.ascontiguousarray(w_bf16, dtype=np.uint16)
+    V = w.shape[0]
+    nw = np.ascontiguousarray(norm_w, dtype=np.float32)
+    xn = np.zeros((B, E), dtype=np.float32)
+    logits = np.zeros((B, V), dtype=np.float32)
+    olib().zo_lmhead_f32_rows(h.ctypes.data, E, B, E, nw.ctypes.data, float(eps), w.ctypes.data,
+                              V, xn.ctypes.data, logits.ctypes.data, V)
     return xn, logits
 
 

@@ -468,3 +468,47 @@ int zo_lmhead_rows(const float* hidden, int64_t hld, int B, int E, const float* 
     for (int t = 1; t < nthreads; ++t) pthread_join(th[t], NULL);
     return 0;
 }
+
+/* ---- the lm_head as the reference computes it by default (f32 throughout) ----
+ * src/kernels.cpp:52-78 dot_f32_avx2: 32 float accumulators (four vectors of 8),
+ * accumulator l takes a[i] * b[i] for i = l, l + 32, ... by fused multiply-add in
+ * order; then (acc0 + acc1) + (acc2 + acc3) per vector lane, the upper half of the
+ * 8 added to the lower, [0] + [2] and [1] + [3], and those two; the result in double
+ * plus the terms past the last multiple of 32 in double, in order; one float
+ * rounding.  a is the weight row, b the normalised row (src/kernels.cpp:85). */
+float zo_dot_avx2_order(const float* a, const float* b, int64_t n) {
+    float acc[32];
+    for (int l = 0; l < 32; ++l) acc[l] = 0.0f;
+    int64_t i = 0;
+    for (; i + 32 <= n; i += 32)
+        for (int l = 0; l < 32; ++l) acc[l] = fmaf(a[i + l], b[i + l], acc[l]);
+    float s[8], t[4];
+    for (int e = 0; e < 8; ++e) s[e] = (acc[e] + acc[8 + e]) + (acc[16 + e] + acc[24 + e]);
+    for (int m = 0; m < 4; ++m) t[m] = s[m] + s[m + 4];
+    const float t20 = t[0] + t[2], t21 = t[1] + t[3];
+    const float t3 = t20 + t21;
+    double total = (double)t3;
+    for (; i < n; ++i) total += (double)a[i] * (double)b[i];
+    return (float)total;
+}
+
+/* hidden [B][hld] f32, norm_w [E], w [V][E] bfloat16 bits; out_xn (nullable) [B][E]
+ * f32; logits [B][lld]: src/model.cpp:31-38 rmsnorm (f32 out) then the dot above. */
+int zo_lmhead_f32_rows(const float* hidden, int64_t hld, int B, int E, const float* norm_w,
+                       float eps, const uint16_t* w, int V, float* out_xn, float* logits,
+                       int64_t lld) {
+    float* xf = (float*)malloc((size_t)E * sizeof(float));
+    float* wf = (float*)malloc((size_t)E * sizeof(float));
+    for (int r = 0; r < B; ++r) {
+        zo_rmsnorm_bf16(hidden + (int64_t)r * hld, norm_w, E, eps, xf, NULL);
+        if (out_xn) memcpy(out_xn + (int64_t)r * E, xf, (size_t)E * sizeof(float));
+        for (int v = 0; v < V; ++v) {
+            const uint16_t* wr = w + (int64_t)v * E;
+            for (int i = 0; i < E; ++i) wf[i] = bf16_to_f32(wr[i]);
+            logits[(int64_t)r * lld + v] = zo_dot_avx2_order(wf, xf, E);
+        }
+    }
+    free(xf);
+    free(wf);
+    return 0;
+}

@@ -252,6 +252,51 @@ def test_lmhead_tiles(sampler, B, tiles):
     assert np.array_equal(alt["states"], res["states"])
 
 
+@pytest.mark.parametrize("B,E,V", [(1, 896, 151936), (4, 896, 151936), (2, 200, 1000),
+                                   (3, 2048, 3000), (4, 64, 777)])
+def test_lmhead_exact_route(sampler, B, E, V):
+    """The exact route: f32 xn and the reference's AVX2 summation order
+    (src/kernels.cpp:52-78).  Logits bit-exact against the restatement (itself
+    pinned to the reference) and, where the reference is built, against
+    zen::rmsnorm + zen::matvec_f32_impl(Avx2) directly; a hidden size with a tail of
+    8 past the last multiple of 32, the largest hidden size, and the smallest.  Ids
+    and Rng states against zs_sample on those logits and the restatement; the default
+    route takes it up to 4 rows."""
+    w, nw = _model(V, E, seed=11)
+    hidden = _hidden(B, E, 120 + B)
+    params = _mixed_params(B)
+    seeds = np.arange(B, dtype=np.uint64) + np.uint64(21)
+    res = _run(sampler, hidden, nw, w, params, seeds, route="exact")
+    _, lg = oracle.oracle_lmhead_f32(hidden.numpy(), nw.numpy(), EPS, _w_bits(w))
+    assert np.array_equal(res["logits"].view(np.uint32), lg.view(np.uint32))
+    if oracle.have_reference():
+        _, ref = oracle.reference_lmhead(hidden.numpy(), nw.numpy(), EPS, _w_f32(w)[0], impl=1)
+        assert np.array_equal(res["logits"].view(np.uint32), ref.view(np.uint32))
+    _check_sampling(sampler, res, params, seeds)
+    auto = _run(sampler, hidden, nw, w, params, seeds, route="auto")
+    assert np.array_equal(auto["logits"].view(np.uint32), res["logits"].view(np.uint32))
+    assert np.array_equal(auto["ids"], res["ids"])
+    assert np.array_equal(auto["states"], res["states"])
+    # without out_logits (handle scratch), and through zs_lmhead_logits
+    res2 = _run(sampler, hidden, nw, w, params, seeds, with_logits=False, route="exact")
+    assert np.array_equal(res2["ids"], res["ids"])
+    dev = sampler.device
+    lg2 = sampler.lmhead_logits(hidden.to(dev), nw.to(dev), w.to(dev), eps=EPS)
+    sampler.check_device_status()
+    assert np.array_equal(lg2.cpu().numpy().view(np.uint32), lg.view(np.uint32))
+
+
+def test_lmhead_exact_route_limits(sampler):
+    """The exact route holds up to 4 rows: 5 rows are refused, not run another way."""
+    from zeninfer_b200._native import SamplerError
+    V, E, B = 1000, 128, 5
+    w, nw = _model(V, E, seed=3)
+    hidden = _hidden(B, E, 3)
+    with pytest.raises(SamplerError):
+        _run(sampler, hidden, nw, w, SamplingParams(temp=0.7, top_k=40),
+             np.arange(B, dtype=np.uint64), route="exact")
+
+
 def test_lmhead_tiles_rejects_unknown(sampler):
     with pytest.raises(ValueError):
         sampler.set_lmhead_tiles("quad")

@@ -314,6 +314,26 @@ def test_lmhead_restatement_against_reference():
     assert np.all(np.abs(lg_ref_full.astype(np.float64) - lg) <= 2.0 ** -8 * mag + 1e-30)
 
 
+@needs_ref
+@pytest.mark.parametrize("E", [896, 200, 20])
+def test_lmhead_f32_restatement_against_reference(E):
+    """The f32 lm_head in the reference's default (AVX2) summation order
+    (src/kernels.cpp:52-78): xn and logits bit-exact against zen::rmsnorm and
+    zen::matvec_f32_impl(Avx2) on bfloat16-valued weights, with a hidden size that
+    is a multiple of 32, one with a tail of 8 summed in double, and one below 32."""
+    rng = np.random.default_rng(E)
+    B, V = 3, 257
+    hidden = rng.normal(0, 3, size=(B, E)).astype(np.float32)
+    hidden[1] *= np.float32(1e-3)
+    norm_w = rng.uniform(0.5, 1.5, size=E).astype(np.float32)
+    w = oracle.f32_to_bf16_bits(rng.normal(0, 0.05, size=(V, E)).astype(np.float32))
+    xn, lg = oracle.oracle_lmhead_f32(hidden, norm_w, 1e-6, w)
+    xn_ref, lg_ref = oracle.reference_lmhead(hidden, norm_w, 1e-6, oracle.bf16_bits_to_f32(w),
+                                             impl=1)
+    assert np.array_equal(xn.view(np.uint32), xn_ref.view(np.uint32))
+    assert np.array_equal(lg.view(np.uint32), lg_ref.view(np.uint32))
+
+
 def test_bf16_rounding_helpers():
     x = np.array([1.0, 1.00390625, 1.005859375, -2.5, 3.0e38, np.inf, -0.0], dtype=np.float32)
     b = oracle.f32_to_bf16_bits(x)

@@ -382,6 +382,215 @@ __global__ void zs_lm_rmsnorm_kernel(const float* hidden, int64_t hld, const flo
     }
 }
 
+// ---- the lm_head in f32, in the reference's own summation order (small batches) ----
+// zs_lm_exact_kernel computes the logits as the reference does by default
+// (src/model.cpp:401-403 with src/kernels.cpp:52-78 dot_f32_avx2): xn in f32
+// (rmsnorm as above, without the bf16 rounding), and per logit 32 f32 accumulators,
+// accumulator l taking w[i] * xn[i] for i = l, l + 32, ... by fused multiply-add in
+// order (lane l of a warp holds accumulator l), then the AVX2 code's reduction tree
+// (lanes e, 8 + e, 16 + e, 24 + e as (a0 + a1) + (a2 + a3), then + 4, + 2, + 1 apart)
+// by shuffles, the terms past the last multiple of 32 in double, one float rounding:
+// bit-exact with the reference's logits.  No tensor cores: up to kExMaxRows rows the
+// lm_head is a stream of the weights, which the copy warp moves through a ring of
+// bulk copies (and, while the rows' f64 sums of squares run, prefetches into L2).
+constexpr int kExMaxRows = 4;
+constexpr int kExMaxE = 2048;
+constexpr int kExWarps = 8;                      // consumer warps
+constexpr int kExThreads = 32 * (kExWarps + 1);  // + the copy warp
+constexpr int kExStages = 3;
+constexpr uint32_t kExStageBytes = 58u << 10;  // 32 padded rows of 896
+constexpr int kExMaxStageRows = 64;
+constexpr int kExRowsPerWarp = 4;  // a warp's rows at once: 8 lanes per row
+// Weight rows sit in the ring padded by 64 bytes: with 8 lanes per row each reading 8
+// bytes, the 4 rows of a warp then fall on two bank halves (two wavefronts).
+__host__ __device__ constexpr uint32_t ex_row_stride(int E) { return (uint32_t)E * 2u + 64u; }
+
+struct ExArgs {
+    const float* hidden;
+    int64_t hld;
+    const float* norm_w;
+    float eps;
+    int32_t B, E, V;
+    const uint16_t* w;  // bf16 bits [V][E]
+    float* out;         // [B][lld]
+    int64_t lld;
+    int32_t rows_per_stage;
+    int64_t prefetch_bytes;  // per CTA, after the ring's first stages
+    int* status;
+};
+
+// ring, xn [B][E], the B scales, 2 x kExStages barriers, the abort flag
+__host__ __device__ constexpr size_t ex_smem_bytes(int B, int E) {
+    return (size_t)kExStages * kExStageBytes + (size_t)B * E * 4 + (size_t)kExMaxRows * 8 +
+           (size_t)2 * kExStages * 8 + 16;
+}
+
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+__global__ void __launch_bounds__(kExThreads, 1) zs_lm_exact_kernel(const ExArgs a) {
+    extern __shared__ __align__(128) uint8_t ex_raw[];
+    uint8_t* ring = ex_raw;
+    float* xn = reinterpret_cast<float*>(ring + (size_t)kExStages * kExStageBytes);
+    double* scale_s = reinterpret_cast<double*>(xn + (size_t)a.B * a.E);  // E % 8 == 0
+    uint64_t* full = reinterpret_cast<uint64_t*>(scale_s + kExMaxRows);
+    uint64_t* empty = full + kExStages;
+    volatile int* abort = reinterpret_cast<volatile int*>(empty + kExStages);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kExStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kExWarps);
+        }
+        *abort = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+    const int64_t v_lo = (int64_t)blockIdx.x * a.V / gridDim.x;
+    const int64_t v_hi = (int64_t)(blockIdx.x + 1) * a.V / gridDim.x;
+    const int R = a.rows_per_stage;
+    const int nst = (int)((v_hi - v_lo + R - 1) / R);
+    if (warp == 0) {
+        // ---- copy issuer ----
+        if (lane == 0) {
+            const uint64_t pol = l2_evict_first_policy();
+            bool ok = true;
+            int issued = 0;
+            for (int st = 0; st < nst; ++st) {
+                const int slot = st % kExStages;
+                if (!lm_wait(&empty[slot], (uint32_t)((st / kExStages) & 1) ^ 1u, abort)) {
+                    ok = false;
+                    break;
+                }
+                const int64_t v0 = v_lo + (int64_t)st * R;
+                const int nrow = (int)min((int64_t)R, v_hi - v0);
+                const uint32_t rb = (uint32_t)a.E * 2u;
+                mbar_arrive_expect_tx(&full[slot], (uint32_t)nrow * rb);
+                for (int r = 0; r < nrow; ++r)  // one copy per row, into its padded slot
+                    bulk_load(ring + (size_t)slot * kExStageBytes + (size_t)r * ex_row_stride(a.E),
+                              a.w + (v0 + r) * a.E, rb, &full[slot], pol);
+                ++issued;
+                if (st == kExStages - 1 || (st == nst - 1 && nst < kExStages)) {
+                    // the rest of this CTA's weights (up to prefetch_bytes) into L2
+                    // while the consumers' row sums run
+                    const uint8_t* p0 = reinterpret_cast<const uint8_t*>(a.w + (v0 + R) * a.E);
+                    const uint8_t* pend = reinterpret_cast<const uint8_t*>(a.w + v_hi * a.E);
+                    int64_t left = min((int64_t)a.prefetch_bytes, pend - p0);
+                    for (const uint8_t* p = p0; left > 0; p += 65536, left -= 65536)
+                        prefetch_l2_bulk(p, (uint32_t)min((int64_t)65536, left));
+                }
+            }
+            if (!ok) set_status(a.status, kStatusTimeout);
+            for (int i = issued - kExStages; i < issued; ++i)  // copies landed before exit
+                if (i >= 0) mbar_wait_bounded(&full[i % kExStages], (uint32_t)((i / kExStages) & 1));
+        }
+        __syncwarp();
+        return;
+    }
+    // ---- consumers: rmsnorm (src/model.cpp:31-38) to f32, then the dot products ----
+    const int cw = warp - 1;
+    // the rows, staged in xn's place (coalesced), then row lane's sum of squares in
+    // order in double, then xn over them in place
+    for (int idx = threadIdx.x - 32; idx < a.B * a.E; idx += kExWarps * 32) {
+        const int b = idx / a.E, i = idx - b * a.E;
+        xn[idx] = a.hidden[(int64_t)b * a.hld + i];
+    }
+    consumer_sync<kExWarps * 32>();
+    if (cw == 0 && lane < a.B) {
+        const float* x = xn + lane * a.E;
+        double sum = 0.0;
+#pragma unroll 8
+        for (int i = 0; i < a.E; ++i) {
+            const double v = (double)x[i];
+            sum = __fma_rn(v, v, sum);  // v * v is exact in double
+        }
+        scale_s[lane] = 1.0 / sqrt(sum / (double)a.E + (double)a.eps);
+    }
+    consumer_sync<kExWarps * 32>();
+    for (int idx = threadIdx.x - 32; idx < a.B * a.E; idx += kExWarps * 32) {
+        const int b = idx / a.E, i = idx - b * a.E;
+        xn[idx] = __double2float_rn(__dmul_rn(__dmul_rn((double)xn[idx], scale_s[b]),
+                                              (double)a.norm_w[i]));
+    }
+    consumer_sync<kExWarps * 32>();
+    const int n32 = a.E & ~31;
+    bool ok = true;
+    for (int st = 0; st < nst && ok; ++st) {
+        const int slot = st % kExStages;
+        const bool got = lm_wait(&full[slot], (uint32_t)((st / kExStages) & 1), abort);
+        if (!__all_sync(kFull, got)) {
+            ok = false;
+            break;
+        }
+        const int64_t v0 = v_lo + (int64_t)st * R;
+        const int rows = (int)min((int64_t)R, v_hi - v0);
+        const uint16_t* wt = reinterpret_cast<const uint16_t*>(ring + (size_t)slot * kExStageBytes);
+        // A warp takes kExRowsPerWarp rows at once, 8 lanes per row: lane p of a row
+        // holds accumulators 4p .. 4p + 3 (the reference's accumulator l takes the
+        // columns l, l + 32, ...), so its four chains are independent and each
+        // 32-column block is one 8-byte load of weights per lane.
+        const int rq = lane >> 3, p = lane & 7;
+        const uint32_t rs = ex_row_stride(a.E);
+        for (int r0 = cw * kExRowsPerWarp; r0 < rows; r0 += kExWarps * kExRowsPerWarp) {
+            const int r = r0 + rq;
+            const bool live = r < rows;
+            const uint8_t* wrow = ring + (size_t)slot * kExStageBytes + (size_t)(live ? r : 0) * rs;
+            float acc[kExMaxRows][4];
+#pragma unroll
+            for (int b = 0; b < kExMaxRows; ++b)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) acc[b][c] = 0.0f;
+#pragma unroll 4
+            for (int blk = 0; blk < n32; blk += 32) {
+                const uint2 wq = *reinterpret_cast<const uint2*>(wrow + (size_t)(blk + 4 * p) * 2);
+                const float w0 = __uint_as_float(wq.x << 16), w1 = __uint_as_float(wq.x & 0xffff0000u);
+                const float w2 = __uint_as_float(wq.y << 16), w3 = __uint_as_float(wq.y & 0xffff0000u);
+#pragma unroll
+                for (int b = 0; b < kExMaxRows; ++b) {
+                    if (b < a.B) {
+                        const float4 x = *reinterpret_cast<const float4*>(xn + b * a.E + blk + 4 * p);
+                        acc[b][0] = __fmaf_rn(w0, x.x, acc[b][0]);
+                        acc[b][1] = __fmaf_rn(w1, x.y, acc[b][1]);
+                        acc[b][2] = __fmaf_rn(w2, x.z, acc[b][2]);
+                        acc[b][3] = __fmaf_rn(w3, x.w, acc[b][3]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int b = 0; b < kExMaxRows; ++b) {
+                if (b >= a.B) break;
+                // The AVX2 reduction.  Accumulator l = 8 k + e is vector k's lane e;
+                // lane p holds l = 4p .. 4p + 3, so vector k sits on lanes 2k, 2k + 1.
+                // (a0 + a1) + (a2 + a3) per vector lane e: lanes 0, 1 and 4, 5 add the
+                // lanes two above them, then lanes 0, 1 add lanes 4, 5: lane 0 holds
+                // s[0..3], lane 1 s[4..7]; then s[m] + s[m + 4], [0] + [2], [1] + [3],
+                // and those two.
+                float v[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    v[c] = __fadd_rn(acc[b][c], __shfl_down_sync(kFull, acc[b][c], 2));
+                    v[c] = __fadd_rn(v[c], __shfl_down_sync(kFull, v[c], 4));
+                    v[c] = __fadd_rn(v[c], __shfl_down_sync(kFull, v[c], 1));
+                }
+                const float t20 = __fadd_rn(v[0], v[2]), t21 = __fadd_rn(v[1], v[3]);
+                const float t3 = __fadd_rn(t20, t21);
+                if (p == 0 && live) {
+                    double total = (double)t3;
+                    const uint16_t* wr = reinterpret_cast<const uint16_t*>(wrow);
+                    for (int i = n32; i < a.E; ++i)
+                        total = __fma_rn((double)__uint_as_float((uint32_t)wr[i] << 16),
+                                         (double)xn[b * a.E + i], total);
+                    a.out[(int64_t)b * a.lld + v0 + r] = __double2float_rn(total);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+    if (!ok) set_status(a.status, kStatusTimeout);
+}
+
 __device__ __forceinline__ uint64_t lm_keep(uint64_t* buf, uint32_t n, uint32_t kk, int lane,
                                             uint32_t slack, uint32_t* kept) {
     return warp_topk_keep<(kLmCap + 31) / 32>(buf, n, kk, lane, slack, kept);

@@ -869,6 +869,10 @@ zs_status zs_create(int device, zs_handle* out) {
          (e = cudaFuncSetAttribute(zs::zs_lmhead_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)zs::kLmSmemBytes)) != cudaSuccess))
         return cleanup(cuda_fail(e, "cudaFuncSetAttribute zs_lmhead_kernel"));
+    if ((size_t)prop.sharedMemPerBlockOptin >= zs::ex_smem_bytes(zs::kExMaxRows, zs::kExMaxE) &&
+        (e = cudaFuncSetAttribute(zs::zs_lm_exact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)zs::ex_smem_bytes(zs::kExMaxRows, zs::kExMaxE))) != cudaSuccess)
+        return cleanup(cuda_fail(e, "cudaFuncSetAttribute zs_lm_exact_kernel"));
     // CTA pairs of the lm_head kernel that can be resident at once (0: none; the
     // one-CTA tiles are used then).
     h->lm_pairs = 0;
@@ -988,8 +992,9 @@ zs_status zs_set_speculation(zs_handle h, int32_t mode) {
 zs_status zs_set_lmhead_route(zs_handle h, int32_t route) {
     if (!h) return fail(ZS_ERR_INVALID_ARGUMENT, "null handle");
     if (route != ZS_LMHEAD_ROUTE_AUTO && route != ZS_LMHEAD_ROUTE_FUSED &&
-        route != ZS_LMHEAD_ROUTE_TWO_PASS)
-        return fail(ZS_ERR_INVALID_ARGUMENT, "route must be ZS_LMHEAD_ROUTE_AUTO, _FUSED or _TWO_PASS");
+        route != ZS_LMHEAD_ROUTE_TWO_PASS && route != ZS_LMHEAD_ROUTE_EXACT)
+        return fail(ZS_ERR_INVALID_ARGUMENT,
+                    "route must be ZS_LMHEAD_ROUTE_AUTO, _FUSED, _TWO_PASS or _EXACT");
     h->lm_route = route;
     return ZS_OK;
 }
@@ -1313,6 +1318,46 @@ zs_status lm_run(zs_context* h, const float* hidden, int64_t hidden_ld, const fl
     return ZS_OK;
 }
 
+// The exact route: zs_lm_exact_kernel writes f32 logits [batch][lld] computed in the
+// reference's own summation order; one CTA per SM streams its share of the vocabulary.
+bool lm_exact_fits(int batch, int n_embd) {
+    return batch <= zs::kExMaxRows && n_embd <= zs::kExMaxE;
+}
+
+bool lm_take_exact(const zs_context* h, int batch, int n_embd) {
+    return h->lm_route == ZS_LMHEAD_ROUTE_EXACT ||
+           (h->lm_route == ZS_LMHEAD_ROUTE_AUTO && lm_exact_fits(batch, n_embd));
+}
+
+zs_status lm_exact_run(zs_context* h, const float* hidden, int64_t hidden_ld, const float* norm_w,
+                       float eps, const void* weight, int batch, int n_embd, int n_vocab,
+                       float* logits, int64_t lld, cudaStream_t st) {
+    if (!lm_exact_fits(batch, n_embd))
+        return fail(ZS_ERR_INVALID_ARGUMENT,
+                    "the exact lm_head route holds up to 4 rows and hidden sizes up to 2048");
+    zs::ExArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.hidden = hidden;
+    a.hld = hidden_ld;
+    a.norm_w = norm_w;
+    a.eps = eps;
+    a.B = batch;
+    a.E = n_embd;
+    a.V = n_vocab;
+    a.w = reinterpret_cast<const uint16_t*>(weight);
+    a.out = logits;
+    a.lld = lld;
+    a.rows_per_stage = std::max(1, std::min<int>(zs::kExMaxStageRows,
+                                                 (int)(zs::kExStageBytes / zs::ex_row_stride(n_embd))));
+    // about 96 MB of the weights (within the L2) prefetched while the rows' sums run
+    a.prefetch_bytes = (96ll << 20) / h->num_sms;
+    a.status = h->status;
+    LaunchScope scope(h, 3, st);
+    zs::zs_lm_exact_kernel<<<h->num_sms, zs::kExThreads, zs::ex_smem_bytes(batch, n_embd), st>>>(a);
+    ZS_CUDA(cudaGetLastError());
+    return ZS_OK;
+}
+
 }  // namespace
 
 zs_status zs_lmhead_logits(zs_handle h, const float* hidden, int64_t hidden_ld,
@@ -1329,6 +1374,9 @@ zs_status zs_lmhead_logits(zs_handle h, const float* hidden, int64_t hidden_ld,
     if (s != ZS_OK) return s;
     DeviceGuard g(h->device);
     if (!g.ok) return fail(ZS_ERR_CUDA, "cudaSetDevice failed");
+    if (lm_take_exact(h, batch, n_embd))
+        return lm_exact_run(h, hidden, hidden_ld, norm_w, eps, weight, batch, n_embd, n_vocab,
+                            out_logits, logits_ld, (cudaStream_t)stream);
     zs::LmArgs a;
     std::memset(&a, 0, sizeof(a));
     a.B = batch;
@@ -1364,6 +1412,23 @@ zs_status zs_lmhead_sample(zs_handle h, const float* hidden, int64_t hidden_ld,
     DeviceGuard g(h->device);
     if (!g.ok) return fail(ZS_ERR_CUDA, "cudaSetDevice failed");
 
+    // Up to kExMaxRows rows (and by choice): the logits in f32, exactly as the
+    // reference computes them, then zs_sample on them.
+    if (lm_take_exact(h, batch, n_embd)) {
+        float* lg = out_logits;
+        int64_t ld = logits_ld;
+        if (!lg) {
+            ld = ((int64_t)n_vocab + 3) & ~(int64_t)3;
+            s = grow((void**)&h->lm_logits, &h->lm_logits_bytes, (size_t)batch * ld * sizeof(float));
+            if (s != ZS_OK) return s;
+            lg = reinterpret_cast<float*>(h->lm_logits);
+        }
+        s = lm_exact_run(h, hidden, hidden_ld, norm_w, eps, weight, batch, n_embd, n_vocab, lg, ld,
+                         st);
+        if (s != ZS_OK) return s;
+        return zs_sample(h, lg, ld, batch, n_vocab, params, params_per_row, history, history_ld,
+                         history_len, rng_state, out_ids, nullptr, stream);
+    }
     // Route: the fused epilogue holds up to kLmKeffMax keys per row and no penalty
     // window; otherwise the kernel writes the logits and zs_sample takes over.
     const int np = params_per_row ? batch : 1;
