@@ -305,7 +305,7 @@ def lmhead_bench(s, dev, stream, hbm_peak):
         flops = 2.0 * B * E * V
         wbytes = V * E * 2 + B * E * 2
         r = {"default_route_us_per_call": ms_auto * 1e3,
-             "default_route": "exact" if B <= 4 else ("two_pass" if B <= 1024 else "fused"),
+             "default_route": "exact" if B <= 4 else ("two_pass" if B < 1024 else "fused"),
              "tiles": "cta_pair_256x256" if B >= 512 else "cta_128x128",
              "us_per_call": ms * 1e3, "rows_per_s": B / (ms / 1e3),
              "kernel_us": k_ms * 1e3,

@@ -221,7 +221,7 @@ zs_status zs_get_timing(zs_handle h, zs_timing* out);
  * logits), for this handle.  No counterpart in the reference (its lm_head and sampler
  * are separate CPU calls).
  *   ZS_LMHEAD_ROUTE_AUTO      (default) exact up to 4 rows (hidden size up to 2048),
- *                             two passes up to 1024 rows, fused above
+ *                             two passes below 1024 rows, fused from 1024
  *   ZS_LMHEAD_ROUTE_FUSED     in the GEMM's epilogue whenever the rows allow it (no
  *                             logits buffer: for callers that cannot spare one)
  *   ZS_LMHEAD_ROUTE_TWO_PASS  always write tensor-core logits, then zs_sample

@@ -1217,7 +1217,7 @@ int lm_slices(int mt, int nt, int ctas, int cap) {
 
 namespace {
 
-constexpr int32_t kLmTwoPassMaxRows = 1024;
+constexpr int32_t kLmTwoPassMaxRows = 1023;
 
 // Checks shared by the lm_head entry points.
 zs_status lm_validate(zs_handle h, const float* hidden, int64_t hidden_ld, const float* norm_w,
@@ -1443,9 +1443,9 @@ zs_status zs_lmhead_sample(zs_handle h, const float* hidden, int64_t hidden_ld,
         if (have_hist && p.repeat_penalty != 1.0f && p.repeat_last_n > 0) fused = false;
     }
     // Up to kLmTwoPassMaxRows rows the two passes are faster (measured on B200, 151,936
-    // x 896 weights, top-k 50: 149 against 346 us at 32 rows, 631 against 679 us at
-    // 1024; fused 997 against 1111 us at 2048): with so few row tiles, each CTA's
-    // epilogue selects for its rows on too few warps to keep up with the GEMM.
+    // x 896 weights, top-k 50: 298 against 379 us at 512 rows, 229 against 280 at 256;
+    // fused 479 against 493 us at 1024): with few row tiles each row's selection sees
+    // short runs of columns, over which its threshold ramps up from nothing.
     if (h->lm_route == ZS_LMHEAD_ROUTE_TWO_PASS ||
         (h->lm_route == ZS_LMHEAD_ROUTE_AUTO && batch <= kLmTwoPassMaxRows))
         fused = false;

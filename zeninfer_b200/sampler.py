@@ -335,7 +335,7 @@ class Sampler:
 
     def set_lmhead_route(self, route: str) -> None:
         """How lmhead_sample takes the shortlist: "auto" (exact up to 4 rows, two
-        passes up to 1024 rows, fused above), "fused" (in the GEMM epilogue whenever
+        passes below 1024 rows, fused from 1024), "fused" (in the GEMM epilogue whenever
         the rows allow it; no logits buffer), "two_pass" (tensor-core logits, then
         sample; the same results as "fused") or "exact" (f32 logits bit-exact with
         the reference's lm_head, then sample; up to 4 rows)."""
