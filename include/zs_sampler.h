@@ -227,7 +227,9 @@ zs_status zs_get_timing(zs_handle h, zs_timing* out);
  *   ZS_LMHEAD_ROUTE_TWO_PASS  always write tensor-core logits, then zs_sample
  *   ZS_LMHEAD_ROUTE_EXACT     f32 logits bit-exact with the reference's default lm_head
  *                             (src/model.cpp:401-403 with src/kernels.cpp:52-78: f32
- *                             xn, its AVX2 summation order), then zs_sample; up to 4
+ *                             xn, its AVX2 summation order) on the same weights (the
+ *                             weight argument is bf16, so a reference whose f32
+ *                             weights are bf16 values), then zs_sample; up to 4
  *                             rows and hidden sizes up to 2048, else
  *                             ZS_ERR_INVALID_ARGUMENT
  * The tensor-core routes (fused, two passes) round xn to bf16 and give the same ids
