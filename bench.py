@@ -248,13 +248,13 @@ def lmhead_bench(s, dev, stream, hbm_peak):
         tf_peak, tf_kind = 1590.0, "fallback"
     out = {"weights": "bf16 [151936][896], seeded N(0, 0.05^2)", "hidden": "N(0, 3^2) f32",
            "params": "temp 0.7, top-k 50, top-p 0.9"}
-    for B in (4096, 2048, 1024, 512, 256, 1):
+    for B in (4096, 2048, 1024, 512, 256, 8, 1):
         h = torch.randn(B, E, device=dev, generator=g) * 3
         st = states_to_tensor([i + 1 for i in range(B)], dev)
         ids = torch.empty(B, dtype=torch.int32, device=dev)
         fused = lambda: s.lmhead_sample(h, nw, W, p, st, out=ids, stream=stream)
         reps = 10 if B > 1 else 100
-        # the default route (two passes up to 1024 rows, fused above) ...
+        # the default route (exact up to 8 rows, two passes below 1024, fused from 1024) ...
         for _ in range(3):
             fused()
         torch.cuda.synchronize()
@@ -297,15 +297,17 @@ def lmhead_bench(s, dev, stream, hbm_peak):
         def two_pass():  # this library's tcgen05 GEMM writing logits, then zs_sample
             s.lmhead_logits(h, nw, W, out=lg_own, stream=stream)
             s.sample(lg_own, p, st, out=ids, stream=stream)
+        s.set_lmhead_route("two_pass")  # tensor-core logits (not the exact route)
         for _ in range(3):
             two_pass()
         torch.cuda.synchronize()
         ms_t = time_device_steps(two_pass, reps, stream) / reps
+        s.set_lmhead_route("auto")
         del lg_own
         flops = 2.0 * B * E * V
         wbytes = V * E * 2 + B * E * 2
         r = {"default_route_us_per_call": ms_auto * 1e3,
-             "default_route": "exact" if B <= 4 else ("two_pass" if B < 1024 else "fused"),
+             "default_route": "exact" if B <= 8 else ("two_pass" if B < 1024 else "fused"),
              "tiles": "cta_pair_256x256" if B >= 512 else "cta_128x128",
              "us_per_call": ms * 1e3, "rows_per_s": B / (ms / 1e3),
              "kernel_us": k_ms * 1e3,

@@ -220,7 +220,7 @@ zs_status zs_get_timing(zs_handle h, zs_timing* out);
 /* How zs_lmhead_sample takes the shortlist (and zs_lmhead_logits computes its
  * logits), for this handle.  No counterpart in the reference (its lm_head and sampler
  * are separate CPU calls).
- *   ZS_LMHEAD_ROUTE_AUTO      (default) exact up to 4 rows (hidden size up to 2048),
+ *   ZS_LMHEAD_ROUTE_AUTO      (default) exact up to 8 rows (while it fits: below),
  *                             two passes below 1024 rows, fused from 1024
  *   ZS_LMHEAD_ROUTE_FUSED     in the GEMM's epilogue whenever the rows allow it (no
  *                             logits buffer: for callers that cannot spare one)
@@ -229,9 +229,9 @@ zs_status zs_get_timing(zs_handle h, zs_timing* out);
  *                             (src/model.cpp:401-403 with src/kernels.cpp:52-78: f32
  *                             xn, its AVX2 summation order) on the same weights (the
  *                             weight argument is bf16, so a reference whose f32
- *                             weights are bf16 values), then zs_sample; up to 4
- *                             rows and hidden sizes up to 2048, else
- *                             ZS_ERR_INVALID_ARGUMENT
+ *                             weights are bf16 values), then zs_sample; up to 8
+ *                             rows, hidden sizes up to 2048 and rows x hidden size
+ *                             up to 8192, else ZS_ERR_INVALID_ARGUMENT
  * The tensor-core routes (fused, two passes) round xn to bf16 and give the same ids
  * and Rng states as each other.  The routes that write logits write them to out_logits
  * when given, else to handle scratch of batch x n_vocab floats. */

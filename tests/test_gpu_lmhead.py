@@ -202,10 +202,11 @@ def test_lmhead_two_pass_route(sampler):
     assert np.array_equal(res2["ids"], res["ids"])
 
 
-@pytest.mark.parametrize("B", [5, 300])
+@pytest.mark.parametrize("B", [16, 300])
 def test_lmhead_routes_agree(sampler, B):
     """Fused, two-pass and the default route give the same ids, Rng states and
-    logits, bit for bit (5 rows: the default takes two passes)."""
+    logits, bit for bit (16 rows: the default takes two passes; up to 8 rows it takes
+    the exact route, tested below)."""
     V, E = 151936, 896
     w, nw = _model(V, E)
     hidden = _hidden(B, E, 41)
@@ -252,8 +253,8 @@ def test_lmhead_tiles(sampler, B, tiles):
     assert np.array_equal(alt["states"], res["states"])
 
 
-@pytest.mark.parametrize("B,E,V", [(1, 896, 151936), (4, 896, 151936), (2, 200, 1000),
-                                   (3, 2048, 3000), (4, 64, 777)])
+@pytest.mark.parametrize("B,E,V", [(1, 896, 151936), (4, 896, 151936), (8, 896, 151936),
+                                   (2, 200, 1000), (4, 2048, 3000), (8, 64, 777)])
 def test_lmhead_exact_route(sampler, B, E, V):
     """The exact route: f32 xn and the reference's AVX2 summation order
     (src/kernels.cpp:52-78).  Logits bit-exact against the restatement (itself
@@ -261,7 +262,7 @@ def test_lmhead_exact_route(sampler, B, E, V):
     zen::rmsnorm + zen::matvec_f32_impl(Avx2) directly; a hidden size with a tail of
     8 past the last multiple of 32, the largest hidden size, and the smallest.  Ids
     and Rng states against zs_sample on those logits and the restatement; the default
-    route takes it up to 4 rows."""
+    route takes it up to 8 rows."""
     w, nw = _model(V, E, seed=11)
     hidden = _hidden(B, E, 120 + B)
     params = _mixed_params(B)
@@ -286,10 +287,12 @@ def test_lmhead_exact_route(sampler, B, E, V):
     assert np.array_equal(lg2.cpu().numpy().view(np.uint32), lg.view(np.uint32))
 
 
-def test_lmhead_exact_route_limits(sampler):
-    """The exact route holds up to 4 rows: 5 rows are refused, not run another way."""
+@pytest.mark.parametrize("B,E", [(9, 128), (5, 2048)])
+def test_lmhead_exact_route_limits(sampler, B, E):
+    """The exact route holds up to 8 rows and 8192 values of rows x hidden size: 9
+    rows, or 5 rows of 2048, are refused, not run another way."""
     from zeninfer_b200._native import SamplerError
-    V, E, B = 1000, 128, 5
+    V = 1000
     w, nw = _model(V, E, seed=3)
     hidden = _hidden(B, E, 3)
     with pytest.raises(SamplerError):

@@ -393,8 +393,9 @@ __global__ void zs_lm_rmsnorm_kernel(const float* hidden, int64_t hld, const flo
 // bit-exact with the reference's logits.  No tensor cores: up to kExMaxRows rows the
 // lm_head is a stream of the weights, which the copy warp moves through a ring of
 // bulk copies (and, while the rows' f64 sums of squares run, prefetches into L2).
-constexpr int kExMaxRows = 4;
+constexpr int kExMaxRows = 8;
 constexpr int kExMaxE = 2048;
+constexpr int kExMaxElems = 8192;  // rows x hidden size: xn in shared memory, 32 KB
 constexpr int kExWarps = 8;                      // consumer warps
 constexpr int kExThreads = 32 * (kExWarps + 1);  // + the copy warp
 constexpr int kExStages = 3;

@@ -869,9 +869,9 @@ zs_status zs_create(int device, zs_handle* out) {
          (e = cudaFuncSetAttribute(zs::zs_lmhead_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)zs::kLmSmemBytes)) != cudaSuccess))
         return cleanup(cuda_fail(e, "cudaFuncSetAttribute zs_lmhead_kernel"));
-    if ((size_t)prop.sharedMemPerBlockOptin >= zs::ex_smem_bytes(zs::kExMaxRows, zs::kExMaxE) &&
+    if ((size_t)prop.sharedMemPerBlockOptin >= zs::ex_smem_bytes(1, zs::kExMaxElems) &&
         (e = cudaFuncSetAttribute(zs::zs_lm_exact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)zs::ex_smem_bytes(zs::kExMaxRows, zs::kExMaxE))) != cudaSuccess)
+                                  (int)zs::ex_smem_bytes(1, zs::kExMaxElems))) != cudaSuccess)
         return cleanup(cuda_fail(e, "cudaFuncSetAttribute zs_lm_exact_kernel"));
     // CTA pairs of the lm_head kernel that can be resident at once (0: none; the
     // one-CTA tiles are used then).
@@ -1321,7 +1321,8 @@ zs_status lm_run(zs_context* h, const float* hidden, int64_t hidden_ld, const fl
 // The exact route: zs_lm_exact_kernel writes f32 logits [batch][lld] computed in the
 // reference's own summation order; one CTA per SM streams its share of the vocabulary.
 bool lm_exact_fits(int batch, int n_embd) {
-    return batch <= zs::kExMaxRows && n_embd <= zs::kExMaxE;
+    return batch <= zs::kExMaxRows && n_embd <= zs::kExMaxE &&
+           (int64_t)batch * n_embd <= zs::kExMaxElems;
 }
 
 bool lm_take_exact(const zs_context* h, int batch, int n_embd) {
@@ -1334,7 +1335,8 @@ zs_status lm_exact_run(zs_context* h, const float* hidden, int64_t hidden_ld, co
                        float* logits, int64_t lld, cudaStream_t st) {
     if (!lm_exact_fits(batch, n_embd))
         return fail(ZS_ERR_INVALID_ARGUMENT,
-                    "the exact lm_head route holds up to 4 rows and hidden sizes up to 2048");
+                    "the exact lm_head route holds up to 8 rows, hidden sizes up to 2048 and "
+                    "rows x hidden size up to 8192");
     zs::ExArgs a;
     std::memset(&a, 0, sizeof(a));
     a.hidden = hidden;

@@ -271,7 +271,7 @@ class Sampler:
     def lmhead_logits(self, hidden, norm_w, weight, eps: float = 1e-6, out=None, stream=None):
         """The lm_head alone (rmsnorm with `norm_w`, then hidden . weight^T;
         src/model.cpp:401-403) for every row of `hidden` ([B, E] float32 CUDA); weight
-        bfloat16 CUDA [V, E].  Up to 4 rows (or with the "exact" route) in f32 exactly
+        bfloat16 CUDA [V, E].  Up to 8 rows (or with the "exact" route) in f32 exactly
         as the reference computes it, else on the tensor cores with xn rounded to
         bf16.  Returns float32 logits [B, V] (or fills `out`, whose row stride must be
         a multiple of 4)."""
@@ -334,11 +334,12 @@ class Sampler:
     LMHEAD_ROUTES = {"auto": 0, "fused": 1, "two_pass": 2, "exact": 3}
 
     def set_lmhead_route(self, route: str) -> None:
-        """How lmhead_sample takes the shortlist: "auto" (exact up to 4 rows, two
+        """How lmhead_sample takes the shortlist: "auto" (exact up to 8 rows, two
         passes below 1024 rows, fused from 1024), "fused" (in the GEMM epilogue whenever
         the rows allow it; no logits buffer), "two_pass" (tensor-core logits, then
         sample; the same results as "fused") or "exact" (f32 logits bit-exact with
-        the reference's lm_head, then sample; up to 4 rows)."""
+        the reference's lm_head, then sample; up to 8 rows, rows x hidden size
+        up to 8192)."""
         if route not in self.LMHEAD_ROUTES:
             raise ValueError(f"route must be one of {sorted(self.LMHEAD_ROUTES)}")
         _native.check(self._lib.zs_set_lmhead_route(self._h, self.LMHEAD_ROUTES[route]),
