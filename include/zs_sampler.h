@@ -39,7 +39,7 @@
 extern "C" {
 #endif
 
-#define ZS_ABI_VERSION 3
+#define ZS_ABI_VERSION 4
 
 typedef enum zs_status {
     ZS_OK = 0,
